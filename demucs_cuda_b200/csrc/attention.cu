@@ -1,0 +1,393 @@
+// Fused multi-head attention for sm_100a: softmax(Q K^T / sqrt(hd)) V per (batch, head)
+// without the score matrix in memory.  Replaces dc_attention's split-heads +
+// [GEMM S = Q K^T -> dk_softmax_to_half -> GEMM O = P V] loop (ops.c:390-443,
+// attn.cu:26-89).
+//
+// CTA = 128 query rows of one head, 192 threads:
+//   warps 0-3  one query row per thread: read the S row from TMEM, online softmax in fp32
+//              (running max / sum, rescale of the output accumulator kept in registers),
+//              write P as fp16 into shared memory in the UMMA A-operand layout, then fold
+//              the P V block product (read back from TMEM) into the accumulator;
+//   warp 4     TMA producer: Q once, then K and V^T tiles of 128 keys into a 2-stage ring;
+//   warp 5     TMEM owner; lane 0 issues S = Q K^T (M=128, N=128, K=64) and
+//              O_blk = P V (M=128, N=64, K=128).
+// Head dims up to 64 are zero-extended to 64 by TMA out-of-bounds fill; keys past Tk read
+// as zero and are masked out of the softmax.
+//
+// Inputs are fp16 exactly as the reference rounds them (split_heads of the fp32
+// projections): Q [BH][Tq][hd], K [BH][Tk][hd], V^T [BH][hd][Tkp].  The reference rounds
+// the normalised probabilities to fp16; here the unnormalised exp(s - m_running) is
+// rounded and the division by the row sum happens at the end (same fp16 operand width).
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include "umma.cuh"
+
+namespace dcb {
+
+constexpr int kAttnThreads = 192;
+constexpr int kQ = 128, kKV = 128, kHD = 64;
+constexpr uint32_t kQBytes = kQ * kHD * 2;      // 16 KB
+constexpr uint32_t kKBytes = kKV * kHD * 2;     // 16 KB
+constexpr uint32_t kVBytes = kHD * kKV * 2;     // 16 KB (two 64-key halves)
+constexpr uint32_t kPBytes = kQ * kKV * 2;      // 32 KB (two 64-key halves)
+constexpr int kAttnStages = 2;
+
+struct AttnArgs {
+  int Tq, Tk, H, hd, BH;
+  float scale;
+  uint16_t *o16;  // [B][Tq][H*hd] fp16 (may be null)
+  float *o32;     // [B][Tq][H*hd] fp32 (may be null)
+};
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    k_flash_attn(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                 const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t *sQ = smem;
+  uint8_t *sK = sQ + kQBytes;
+  uint8_t *sV = sK + kAttnStages * kKBytes;
+  uint8_t *sP = sV + kAttnStages * kVBytes;
+  uint64_t *bar = (uint64_t *)(sP + kPBytes);
+  uint64_t *q_full = bar;
+  uint64_t *kv_full = bar + 1;                 // [stages]
+  uint64_t *kv_empty = kv_full + kAttnStages;  // [stages]
+  uint64_t *s_full = kv_empty + kAttnStages;
+  uint64_t *p_full = s_full + 1;
+  uint64_t *o_full = p_full + 1;
+  uint64_t *o_free = o_full + 1;
+  uint32_t *tslot = (uint32_t *)(o_free + 1);
+
+  // a fault recorded by an earlier kernel: end this grid at once (uniform CTA decision)
+  __shared__ uint32_t s_abort;
+  if (threadIdx.x == 0) s_abort = fault_pending() ? 1u : 0u;
+  __syncthreads();
+  if (s_abort) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, bh = blockIdx.y;
+  const int q0 = qt * kQ;
+  const int nkv = (a.Tk + kKV - 1) / kKV;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kAttnStages; i++) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(o_full, 1);
+    mbar_init(o_free, 4);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tslot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tS = tmem, tO = tmem + 128;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_expect_tx(q_full, kQBytes);
+      tma_load_3d(sQ, &tmQ, q_full, 0, q0, bh);
+      for (int j = 0; j < nkv; j++) {
+        const int st = j % kAttnStages;
+        const uint32_t ph = (uint32_t)(j / kAttnStages) & 1u;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1u, kFaultAttn)) break;
+        mbar_expect_tx(&kv_full[st], kKBytes + kVBytes);
+        tma_load_3d(sK + st * kKBytes, &tmK, &kv_full[st], 0, j * kKV, bh);
+        tma_load_3d(sV + st * kVBytes, &tmV, &kv_full[st], j * kKV, 0, bh);
+        tma_load_3d(sV + st * kVBytes + kVBytes / 2, &tmV, &kv_full[st], j * kKV + 64, 0, bh);
+      }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint32_t id_s = idesc_f16_f32(kQ, kKV);
+      const uint32_t id_o = idesc_f16_f32(kQ, kHD);
+      bool ok = mbar_wait(q_full, 0, kFaultAttn);
+      const uint64_t qd = sw128_desc(smem_u32(sQ));
+      for (int j = 0; j < nkv && ok; j++) {
+        const int st = j % kAttnStages;
+        const uint32_t ph = (uint32_t)(j / kAttnStages) & 1u;
+        if (!mbar_wait(&kv_full[st], ph, kFaultAttn)) break;
+        if (j > 0 && !mbar_wait(o_free, (uint32_t)(j - 1) & 1u, kFaultAttn)) break;
+        tc_fence_after();
+        const uint64_t kd = sw128_desc(smem_u32(sK + st * kKBytes));
+#pragma unroll
+        for (int k = 0; k < kHD / 16; k++) umma_f16(tS, qd + 2u * k, kd + 2u * k, id_s, k > 0);
+        umma_commit(s_full);
+        if (!mbar_wait(p_full, (uint32_t)j & 1u, kFaultAttn)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < kKV / 16; k++) {
+          const uint32_t half = (uint32_t)(k >> 2) * (kPBytes / 2);
+          const uint32_t vhalf = (uint32_t)(k >> 2) * (kVBytes / 2);
+          const uint64_t pd = sw128_desc(smem_u32(sP) + half) + 2u * (k & 3);
+          const uint64_t vd = sw128_desc(smem_u32(sV + st * kVBytes) + vhalf) + 2u * (k & 3);
+          umma_f16(tO, pd, vd, id_o, k > 0);
+        }
+        umma_commit(o_full);
+        umma_commit(&kv_empty[st]);
+      }
+    }
+  } else {
+    // softmax / accumulate warps: one query row per thread
+    const int r = threadIdx.x;
+    const uint32_t lrow = (uint32_t)(warp * 32) << 16;
+    float o[kHD];
+#pragma unroll
+    for (int d = 0; d < kHD; d++) o[d] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+    const uint32_t p_base = smem_u32(sP);
+    bool ok = true;
+    for (int j = 0; j < nkv && ok; j++) {
+      if (!mbar_wait(s_full, (uint32_t)j & 1u, kFaultAttn)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int kbase = j * kKV;
+      // pass 1: block max of scale * s (S is re-read from TMEM in pass 2 rather than
+      // held in registers)
+      float mx = m_run;
+#pragma unroll
+      for (int c = 0; c < kKV; c += 16) {
+        float v[16];
+        tmem_ld16(tS + lrow + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          if (kbase + c + i < a.Tk) mx = fmaxf(mx, v[i] * a.scale);
+        }
+      }
+      const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - mx);
+      m_run = mx;
+      float psum = 0.f;
+      // pass 2: p = exp(scale * s - m) as fp16 into the P tile (row r, keys along K, SW128)
+#pragma unroll
+      for (int c = 0; c < kKV; c += 16) {
+        float v[16];
+        tmem_ld16(tS + lrow + c, v);
+        tmem_wait_ld();
+        uint32_t w[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float p0 = kbase + c + i < a.Tk ? expf(v[i] * a.scale - mx) : 0.f;
+          const float p1 = kbase + c + i + 1 < a.Tk ? expf(v[i + 1] * a.scale - mx) : 0.f;
+          w[i >> 1] = pack_h2(p0, p1);
+          // the row sum uses the rounded values the MMA multiplies
+          psum += h2f_bits((uint16_t)(w[i >> 1] & 0xffffu)) + h2f_bits((uint16_t)(w[i >> 1] >> 16));
+        }
+        const int half = c >> 6, chunk = (c & 63) >> 3;
+        const uint32_t rowp = p_base + half * (kPBytes / 2);
+        st_shared_v4(rowp + sw128_off(r, chunk), w[0], w[1], w[2], w[3]);
+        st_shared_v4(rowp + sw128_off(r, chunk + 1), w[4], w[5], w[6], w[7]);
+      }
+      l_run = l_run * alpha + psum;
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (!mbar_wait(o_full, (uint32_t)j & 1u, kFaultAttn)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < kHD; c += 16) {
+        float v[16];
+        tmem_ld16(tO + lrow + c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; i++) o[c + i] = o[c + i] * alpha + v[i];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(o_free);
+    }
+    // normalise and store
+    const int t = q0 + r;
+    if (t < a.Tq && ok) {
+      const float inv = 1.0f / l_run;
+      const int b = bh / a.H, h = bh - b * a.H;
+      const int64_t D = (int64_t)a.H * a.hd;
+      const int64_t off = ((int64_t)b * a.Tq + t) * D + (int64_t)h * a.hd;
+#pragma unroll
+      for (int d = 0; d < kHD; d++) {
+        if (d < a.hd) {
+          const float val = o[d] * inv;
+          if (a.o16) a.o16[off + d] = f2h_bits(val);
+          if (a.o32) a.o32[off + d] = val;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ------------------------------------------------------------ CUDA-core reference kernel
+// One warp per (query, head); exact reference numerics: max over scaled scores, sum of
+// exps in double, P = fp16(exp(v - max) * (1/sum)), O = sum P V in fp32.
+__global__ void k_attn_simt(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
+                            const uint16_t *__restrict__ vt, AttnArgs a, int64_t Tkp) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= (int64_t)a.BH * a.Tq) return;
+  const int bh = (int)(gw / a.Tq), t = (int)(gw - (int64_t)bh * a.Tq);
+  const uint16_t *qr = q + ((int64_t)bh * a.Tq + t) * a.hd;
+  float qv[64];
+  for (int d = 0; d < a.hd; d++) qv[d] = h2f_bits(qr[d]);
+  auto score = [&](int j) {
+    const uint16_t *kr = k + ((int64_t)bh * a.Tk + j) * a.hd;
+    float s = 0.f;
+    for (int d = 0; d < a.hd; d++) s += qv[d] * h2f_bits(kr[d]);
+    return s * a.scale;
+  };
+  float mx = -INFINITY;
+  for (int j = lane; j < a.Tk; j += 32) mx = fmaxf(mx, score(j));
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  double sum = 0.0;
+  for (int j = lane; j < a.Tk; j += 32) sum += (double)expf(score(j) - mx);
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float inv = (float)(1.0 / sum);
+  float acc[64];
+  for (int d = 0; d < a.hd; d++) acc[d] = 0.f;
+  for (int j = lane; j < a.Tk; j += 32) {
+    const float p = h2f_bits(f2h_bits(expf(score(j) - mx) * inv));
+    for (int d = 0; d < a.hd; d++) acc[d] += p * h2f_bits(vt[((int64_t)bh * a.hd + d) * Tkp + j]);
+  }
+  const int b = bh / a.H, h = bh - b * a.H;
+  const int64_t D = (int64_t)a.H * a.hd;
+  const int64_t off = ((int64_t)b * a.Tq + t) * D + (int64_t)h * a.hd;
+  for (int d = 0; d < a.hd; d++) {
+    float v = acc[d];
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) {
+      if (a.o16) a.o16[off + d] = f2h_bits(v);
+      if (a.o32) a.o32[off + d] = v;
+    }
+  }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_enc_attn = nullptr;
+
+static bool map3(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
+                 uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1) {
+  if (!g_enc_attn) {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return false;
+    g_enc_attn = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+  }
+  if (((uintptr_t)base & 15) || (s1 * 2) % 16 || (s2 * 2) % 16) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1 * 2, s2 * 2};
+  cuuint32_t box[3] = {b0, b1, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  return g_enc_attn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims,
+                    strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// q [BH][Tq][hd], k [BH][Tk][hd], vt [BH][hd][Tkp] fp16 -> o16 / o32 [B][Tq][H*hd]
+void flash_attention(const uint16_t *q, const uint16_t *k, const uint16_t *vt, int B, int H,
+                     int Tq, int Tk, int hd, int64_t Tkp, uint16_t *o16, float *o32) {
+  DCB_REQUIRE(hd <= kHD && hd % 8 == 0, "attention: head dim %d must be a multiple of 8 <= 64",
+              hd);
+  DCB_REQUIRE(Tkp % 8 == 0 && Tkp >= Tk, "attention: padded key length %lld", (long long)Tkp);
+  AttnArgs a;
+  a.Tq = Tq;
+  a.Tk = Tk;
+  a.H = H;
+  a.hd = hd;
+  a.BH = B * H;
+  a.scale = 1.0f / sqrtf((float)hd);
+  a.o16 = o16;
+  a.o32 = o32;
+  if (!g_opt_simt) {
+    CUtensorMap mq, mk, mv;
+    bool ok = map3(&mq, q, hd, Tq, (uint64_t)B * H, hd, (uint64_t)Tq * hd, 64, kQ) &&
+              map3(&mk, k, hd, Tk, (uint64_t)B * H, hd, (uint64_t)Tk * hd, 64, kKV) &&
+              map3(&mv, vt, Tk, hd, (uint64_t)B * H, Tkp, (uint64_t)hd * Tkp, 64, 64);
+    if (ok) {
+      const size_t smem = 1024 + kQBytes + kAttnStages * (kKBytes + kVBytes) + kPBytes + 256;
+      static bool attr = false;
+      if (!attr) {
+        DCB_CUDA(cudaFuncSetAttribute(k_flash_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)smem));
+        attr = true;
+      }
+      DCB_REQUIRE(B * H <= 65535, "attention: too many heads");
+      dim3 grid((unsigned)((Tq + kQ - 1) / kQ), (unsigned)(B * H));
+      k_flash_attn<<<grid, kAttnThreads, smem, stream()>>>(mq, mk, mv, a);
+      DCB_LAUNCHED();
+      return;
+    }
+  }
+  const int64_t warps = (int64_t)B * H * Tq;
+  k_attn_simt<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, stream()>>>(q, k, vt, a, Tkp);
+  DCB_LAUNCHED();
+}
+
+// fp32 [B][T][H*hd] -> fp16 [B][H][T][hd] (transpose=0) or [B][H][hd][Tp] (transpose=1)
+__global__ void k_heads16(const float *__restrict__ x, uint16_t *__restrict__ y, int B, int T,
+                          int H, int hd, int64_t Tp, int transpose) {
+  int64_t D = (int64_t)H * hd, n = (int64_t)B * T * D;
+  DCB_GRID_STRIDE(i, n) {
+    int64_t c = i % D, bt = i / D, t = bt % T, b = bt / T;
+    int64_t h = c / hd, d = c % hd;
+    uint16_t v = f2h_bits(x[i]);
+    if (transpose) {
+      y[((b * H + h) * hd + d) * Tp + t] = v;
+    } else {
+      y[((b * H + h) * T + t) * hd + d] = v;
+    }
+  }
+}
+
+}  // namespace dcb
+
+using namespace dcb;
+
+extern "C" void dkx_attention(const float *q, const float *k, const float *v, int B, int Tq,
+                              int Tk, int H, int hd, float *y) {
+  if (B <= 0 || Tq <= 0 || Tk <= 0) return;
+  const int64_t Tkp = (Tk + 7) / 8 * 8;
+  uint16_t *qh = nullptr, *kh = nullptr, *vt = nullptr;
+  const size_t nq = (size_t)B * H * Tq * hd, nk = (size_t)B * H * Tk * hd;
+  const size_t nv = (size_t)B * H * hd * Tkp;
+  DCB_CUDA(cudaMallocAsync(&qh, nq * 2, stream()));
+  DCB_CUDA(cudaMallocAsync(&kh, nk * 2, stream()));
+  DCB_CUDA(cudaMallocAsync(&vt, nv * 2, stream()));
+  DCB_CUDA(cudaMemsetAsync(vt, 0, nv * 2, stream()));
+  k_heads16<<<grid_for((int64_t)B * Tq * H * hd, 256), 256, 0, stream()>>>(q, qh, B, Tq, H, hd,
+                                                                          0, 0);
+  DCB_LAUNCHED();
+  k_heads16<<<grid_for((int64_t)B * Tk * H * hd, 256), 256, 0, stream()>>>(k, kh, B, Tk, H, hd,
+                                                                          0, 0);
+  DCB_LAUNCHED();
+  k_heads16<<<grid_for((int64_t)B * Tk * H * hd, 256), 256, 0, stream()>>>(v, vt, B, Tk, H, hd,
+                                                                          Tkp, 1);
+  DCB_LAUNCHED();
+  flash_attention(qh, kh, vt, B, H, Tq, Tk, hd, Tkp, nullptr, y);
+  DCB_CUDA(cudaFreeAsync(qh, stream()));
+  DCB_CUDA(cudaFreeAsync(kh, stream()));
+  DCB_CUDA(cudaFreeAsync(vt, stream()));
+}

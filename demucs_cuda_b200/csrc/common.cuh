@@ -1,0 +1,86 @@
+// Shared helpers of the sm_100a backend: error handling, the backend stream, launch
+// accounting and fp16 conversion.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include "../../include/dc_b200.h"
+
+namespace dcb {
+
+// ------------------------------------------------------------------ errors
+// The reference aborts through dc_die on any failure (cuda_common.cuh:17-26).  The same
+// is the default here; a host may instead ask for the error to be recorded and the call to
+// return (dcb_set_error_mode).
+void fail(const char *fmt, ...);
+bool failed();  // an error is pending in return mode
+cudaStream_t stream();
+void count_launch();
+
+#define DCB_CUDA(call)                                                                   \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess) {                                                             \
+      ::dcb::fail("CUDA error %s at %s:%d: %s", cudaGetErrorName(e_), __FILE__, __LINE__, \
+                  cudaGetErrorString(e_));                                               \
+    }                                                                                    \
+  } while (0)
+
+#define DCB_LAUNCHED()                  \
+  do {                                  \
+    ::dcb::count_launch();              \
+    DCB_CUDA(cudaGetLastError());       \
+  } while (0)
+
+#define DCB_REQUIRE(cond, ...)  \
+  do {                          \
+    if (!(cond)) {              \
+      ::dcb::fail(__VA_ARGS__); \
+      return;                   \
+    }                           \
+  } while (0)
+
+// option values (dcb_set_option)
+extern int g_opt_simt;
+extern int g_opt_graphs;
+
+// device fault word written by bounded waits (see umma.cuh); the library is one
+// translation unit (all.cu), so the definition lives here
+__device__ uint32_t g_dev_fault = 0;
+
+static inline unsigned grid_for(int64_t n, int threads, int64_t cap = 148 * 32) {
+  int64_t b = (n + threads - 1) / threads;
+  if (b > cap) b = cap;
+  return (unsigned)(b < 1 ? 1 : b);
+}
+
+#define DCB_GRID_STRIDE(i, n) \
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (n); \
+       i += (int64_t)blockDim.x * gridDim.x)
+
+// ------------------------------------------------------------------ numerics
+// GELU in the erf form the reference uses (backend_cpu.c:144, cuda_common.cuh:42-44).
+static __device__ __forceinline__ float gelu_f(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+}
+static __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
+// fp32 -> fp16 bits, round to nearest even (the reference's dc_f32_to_f16 rule).
+static __device__ __forceinline__ uint16_t f2h_bits(float v) {
+  return __half_as_ushort(__float2half_rn(v));
+}
+static __device__ __forceinline__ float h2f_bits(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+// two floats -> packed fp16x2 (low = a)
+static __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  return (uint32_t)f2h_bits(a) | ((uint32_t)f2h_bits(b) << 16);
+}
+
+// host side RNE conversion (IEEE 754 binary32 -> binary16)
+uint16_t host_f2h(float f);
+float host_h2f(uint16_t h);
+
+}  // namespace dcb

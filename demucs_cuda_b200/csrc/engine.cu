@@ -1,0 +1,761 @@
+// htdemucs_6s model engine on the sm_100a kernels: weight loading and packing, the forward
+// pass and the segment scheduler.
+//
+// Mirrors the reference's model layer (htdemucs.c, layers.c, transformer.c, stft.c,
+// apply.c) operation by operation, but every GEMM-shaped step is one fused tensor-core
+// kernel:
+//   encoder conv      implicit-GEMM conv + bias + GELU                    (layers.c:96-121)
+//   DConv             k3 conv -> GN+GELU -> 1x1 conv -> GN+GLU+LayerScale residual,
+//                     run directly on [B, C, Fr, T] (no transposes)       (layers.c:24-68)
+//   rewrite           1x1 / 3x3 conv + bias + GLU (decoder: + skip add in the gather)
+//   conv_tr           stride-phase GEMM + bias + crop + GELU              (layers.c:192-216)
+//   attention block   LN -> fused QKV GEMM (head-split fp16 epilogue) -> flash attention
+//                     -> out-proj GEMM + LayerScale residual -> LN -> linear1 + GELU (fp16)
+//                     -> linear2 + LayerScale residual -> GroupNorm(1)   (transformer.c)
+// Activations stay fp32 between layers exactly like the reference; every GEMM operand is
+// rounded to fp16 (RNE) where the reference rounds it.
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace dcb {
+
+// defined in the other translation-unit parts of the library
+void row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var);
+void layernorm(const float *x, void *y, const float *w, const float *b, int64_t rows, int C,
+               float eps, bool half_out, int ld_out);
+void flash_attention(const uint16_t *q, const uint16_t *k, const uint16_t *vt, int B, int H,
+                     int Tq, int Tk, int hd, int64_t Tkp, uint16_t *o16, float *o32);
+
+// ------------------------------------------------------------------ config (config.c:11-264)
+struct Cfg {
+  int n_sources = 6, samplerate = 44100, nfft = 4096, hop = 1024, audio_channels = 2;
+  float segment = 7.8f;
+  int channels = 48, channels_time = 0, growth = 2, depth = 4, kernel_size = 8, stride = 4;
+  int time_stride = 2, context = 1, context_enc = 0, norm_groups = 4, norm_starts = 4;
+  int dconv_mode = 1, dconv_depth = 2, dconv_comp = 8;
+  float dconv_init = 1e-3f;
+  int rewrite = 1, cac = 1;
+  float freq_emb = 0.2f, emb_scale = 10.0f;
+  int t_layers = 5, t_heads = 8;
+  float t_hidden_scale = 4.0f, t_max_period = 10000.0f, t_weight_pos_embed = 1.0f;
+  int t_gelu = 1, t_cross_first = 0, bottom_channels = 0, use_train_segment = 1;
+  int wiener_iters = 0, valid_length = 0;
+};
+
+// The reference's tolerant key scanner: first occurrence of "key" anywhere, value after
+// the colon; "kwargs" entries override (config.c:11-104, 157-264).
+static const char *find_key(const char *js, const char *key) {
+  char pat[128];
+  snprintf(pat, sizeof(pat), "\"%s\"", key);
+  const char *p = strstr(js, pat);
+  if (!p) return nullptr;
+  p = strchr(p + strlen(pat), ':');
+  if (!p) return nullptr;
+  p++;
+  while (*p == ' ' || *p == '\n' || *p == '\t' || *p == '\r') p++;
+  return p;
+}
+static int key_int(const char *js, const char *key, int fb) {
+  const char *p = find_key(js, key);
+  if (!p) return fb;
+  if (!strncmp(p, "true", 4)) return 1;
+  if (!strncmp(p, "false", 5)) return 0;
+  if (!strncmp(p, "null", 4)) return fb;
+  return (int)strtol(p, nullptr, 10);
+}
+static float key_float(const char *js, const char *key, float fb) {
+  const char *p = find_key(js, key);
+  if (!p || !strncmp(p, "null", 4)) return fb;
+  return strtof(p, nullptr);
+}
+static int key_str_array_len(const char *js, const char *key) {
+  const char *p = find_key(js, key);
+  if (!p || *p != '[') return 0;
+  int n = 0;
+  p++;
+  while (*p && *p != ']') {
+    while (*p == ' ' || *p == '\n' || *p == '\t' || *p == ',' || *p == '\r') p++;
+    if (*p != '"') break;
+    p++;
+    while (*p && *p != '"') p++;
+    if (*p == '"') p++;
+    n++;
+  }
+  return n;
+}
+
+static void apply_keys(Cfg &c, const char *js, bool kw) {
+#define KI(name) c.name = key_int(js, #name, c.name)
+#define KF(name) c.name = key_float(js, #name, c.name)
+  if (!kw) {
+    int ns = key_str_array_len(js, "sources");
+    if (ns > 0) c.n_sources = ns;
+    KI(samplerate);
+    KF(segment);
+    KI(nfft);
+    c.hop = key_int(js, "hop_length", c.hop);
+    KI(audio_channels);
+    KI(valid_length);
+  }
+  KI(channels);
+  KI(channels_time);
+  KI(growth);
+  KI(depth);
+  KI(kernel_size);
+  KI(stride);
+  KI(time_stride);
+  KI(context);
+  KI(context_enc);
+  KI(norm_groups);
+  KI(norm_starts);
+  KI(dconv_mode);
+  KI(dconv_depth);
+  KI(dconv_comp);
+  KF(dconv_init);
+  KI(rewrite);
+  KI(cac);
+  KF(freq_emb);
+  KF(emb_scale);
+  KI(t_layers);
+  KI(t_heads);
+  KF(t_hidden_scale);
+  KF(t_max_period);
+  KF(t_weight_pos_embed);
+  KI(t_gelu);
+  KI(t_cross_first);
+  KI(bottom_channels);
+  KI(use_train_segment);
+  KI(wiener_iters);
+  if (kw) {
+    KI(nfft);
+    KI(samplerate);
+  }
+#undef KI
+#undef KF
+}
+
+static bool load_config(const char *path, Cfg &c) {
+  c = Cfg();
+  c.valid_length = (int)(c.segment * (float)c.samplerate);
+  FILE *f = path && path[0] ? fopen(path, "rb") : nullptr;
+  if (f) {
+    std::string js;
+    char buf[4096];
+    size_t n;
+    while ((n = fread(buf, 1, sizeof(buf), f)) > 0) js.append(buf, n);
+    fclose(f);
+    apply_keys(c, js.c_str(), false);
+    const char *kw = find_key(js.c_str(), "kwargs");
+    if (kw) apply_keys(c, kw, true);
+  } else if (path && path[0]) {
+    fail("cannot read config %s", path);
+    return false;
+  }
+  c.hop = c.nfft / 4;
+  if (c.valid_length <= 0) c.valid_length = (int)(c.segment * (float)c.samplerate);
+  // this engine implements the htdemucs_6s layer structure
+  const char *why = nullptr;
+  if (c.wiener_iters != 0) why = "wiener_iters != 0";
+  else if (!c.use_train_segment) why = "use_train_segment = 0";
+  else if (c.norm_starts < c.depth) why = "outer GroupNorm layers (norm_starts < depth)";
+  else if (c.dconv_mode != 1) why = "dconv_mode other than encoder-only";
+  else if (!c.cac || !c.rewrite || !c.t_gelu) why = "cac/rewrite/t_gelu disabled";
+  else if (c.channels_time && c.channels_time != c.channels) why = "channels_time";
+  else if (c.bottom_channels) why = "bottom_channels";
+  else if (c.kernel_size != 2 * c.stride) why = "kernel_size != 2 * stride";
+  else if (c.depth > 8) why = "depth > 8";
+  if (why) {
+    fail("unsupported model configuration: %s", why);
+    return false;
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ safetensors
+struct StEntry {
+  std::string dtype;
+  std::vector<int> shape;
+  size_t begin = 0, end = 0;
+};
+
+static void skip_ws(const char *&p, const char *e) {
+  while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) p++;
+}
+static bool parse_str(const char *&p, const char *e, std::string &out) {
+  skip_ws(p, e);
+  if (p >= e || *p != '"') return false;
+  p++;
+  out.clear();
+  while (p < e && *p != '"') {
+    char ch = *p++;
+    if (ch == '\\' && p < e) ch = *p++;
+    out.push_back(ch);
+  }
+  if (p >= e) return false;
+  p++;
+  return true;
+}
+static bool parse_u64(const char *&p, const char *e, uint64_t &v) {
+  skip_ws(p, e);
+  v = 0;
+  bool any = false;
+  while (p < e && *p >= '0' && *p <= '9') {
+    v = v * 10 + (uint64_t)(*p++ - '0');
+    any = true;
+  }
+  return any;
+}
+static void skip_value(const char *&p, const char *e) {
+  skip_ws(p, e);
+  int depth = 0;
+  bool in_str = false;
+  for (; p < e; p++) {
+    char ch = *p;
+    if (in_str) {
+      if (ch == '\\') p++;
+      else if (ch == '"') {
+        in_str = false;
+        if (depth == 0) {
+          p++;
+          return;
+        }
+      }
+      continue;
+    }
+    if (ch == '"') in_str = true;
+    else if (ch == '{' || ch == '[') depth++;
+    else if (ch == '}' || ch == ']') {
+      if (--depth <= 0) {
+        p++;
+        return;
+      }
+    } else if (depth == 0 && (ch == ',')) return;
+  }
+}
+static bool expect(const char *&p, const char *e, char ch) {
+  skip_ws(p, e);
+  if (p < e && *p == ch) {
+    p++;
+    return true;
+  }
+  return false;
+}
+
+static bool parse_st_header(const char *js, size_t len, std::unordered_map<std::string, StEntry> &out) {
+  const char *p = js, *e = js + len;
+  if (!expect(p, e, '{')) return false;
+  while (true) {
+    if (expect(p, e, '}')) break;
+    std::string key;
+    if (!parse_str(p, e, key) || !expect(p, e, ':')) return false;
+    if (key == "__metadata__") {
+      skip_value(p, e);
+    } else {
+      StEntry en;
+      if (!expect(p, e, '{')) return false;
+      while (!expect(p, e, '}')) {
+        std::string field;
+        if (!parse_str(p, e, field)) return false;
+        expect(p, e, ':');
+        if (field == "dtype") {
+          if (!parse_str(p, e, en.dtype)) return false;
+        } else if (field == "shape") {
+          expect(p, e, '[');
+          while (!expect(p, e, ']')) {
+            uint64_t v;
+            if (!parse_u64(p, e, v)) return false;
+            en.shape.push_back((int)v);
+            expect(p, e, ',');
+          }
+        } else if (field == "data_offsets") {
+          uint64_t a, b;
+          expect(p, e, '[');
+          if (!parse_u64(p, e, a)) return false;
+          expect(p, e, ',');
+          if (!parse_u64(p, e, b)) return false;
+          expect(p, e, ']');
+          en.begin = a;
+          en.end = b;
+        } else {
+          skip_value(p, e);
+        }
+        expect(p, e, ',');
+      }
+      out[key] = en;
+    }
+    expect(p, e, ',');
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ packed layers
+struct ConvW {             // B operand of a conv GEMM plus its epilogue constants
+  uint16_t *w = nullptr;   // [rows][ld] fp16
+  int64_t ld = 0;
+  int rows = 0;            // B rows (columns of the GEMM)
+  int O = 0, C = 0, KH = 1, KW = 1, K = 0;
+  float *bias = nullptr;
+  int glu_bn = 0;          // N tile of the GLU interleave (0 = plain)
+};
+struct LinW {
+  uint16_t *w = nullptr;   // [out][ld]
+  int64_t ld = 0;
+  int out = 0, in = 0;
+  float *bias = nullptr;
+};
+struct NormW {
+  float *w = nullptr, *b = nullptr;
+};
+struct DConvW {
+  ConvW c0, c3;
+  NormW gn1, gn4;
+  float *scale = nullptr;
+};
+struct EncW {
+  ConvW conv, rewrite;
+  DConvW dconv[4];
+  int ndconv = 0;
+  int Cin = 0, Cout = 0;
+};
+struct DecW {
+  ConvW rewrite, convtr;  // convtr in the stride-phase layout
+  int Cin = 0, Cout = 0;
+};
+struct TLayerW {
+  bool cross = false;
+  NormW norm1, norm2, norm3, norm_out;
+  LinW qkv;  // self: [3D][D]; cross: q only [D][D]
+  LinW kv;   // cross: [2D][D]
+  LinW out, lin1, lin2;
+  float *gamma1 = nullptr, *gamma2 = nullptr;
+};
+
+}  // namespace dcb
+
+struct DcbModel {
+  dcb::Cfg cfg;
+  void *block = nullptr;
+  size_t block_bytes = 0;
+  int depth = 0;
+  dcb::EncW enc[8], tenc[8];
+  dcb::DecW dec[8], tdec[8];
+  float *freq_emb = nullptr;
+  int fe_rows = 0, fe_cols = 0;
+  dcb::NormW norm_in, norm_in_t;
+  dcb::TLayerW layers[2][16];
+  float *window = nullptr;
+  int D = 0, hidden = 0;
+  // cached positional embeddings, keyed by token-grid shape
+  std::unordered_map<long long, float *> pos_cache;
+};
+
+namespace dcb {
+
+// staging of the single device block (weights.c:316-360 keeps one 256-aligned block too)
+struct Staging {
+  std::vector<uint8_t> bytes;
+  std::vector<std::pair<size_t, void **>> fix;  // offset -> pointer slot to patch
+  size_t add(const void *src, size_t n, void **slot) {
+    size_t off = (bytes.size() + 255) & ~(size_t)255;
+    bytes.resize(off + n);
+    if (src) memcpy(bytes.data() + off, src, n);
+    fix.push_back({off, slot});
+    return off;
+  }
+};
+
+struct Loader {
+  std::unordered_map<std::string, StEntry> ents;
+  const uint8_t *data = nullptr;
+  size_t data_len = 0;
+  std::string missing;
+
+  bool has(const std::string &n) const { return ents.count(n) != 0; }
+  // element i as float (F32 / F16 / BF16, weights.c:216-236)
+  float at(const StEntry &e, size_t i) const {
+    const uint8_t *p = data + e.begin;
+    if (e.dtype == "F32") {
+      float v;
+      memcpy(&v, p + i * 4, 4);
+      return v;
+    }
+    uint16_t h;
+    memcpy(&h, p + i * 2, 2);
+    if (e.dtype == "F16") return host_h2f(h);
+    uint32_t x = (uint32_t)h << 16;
+    float v;
+    memcpy(&v, &x, 4);
+    return v;
+  }
+  const StEntry *get(const std::string &n) {
+    auto it = ents.find(n);
+    if (it == ents.end()) {
+      if (missing.empty()) missing = n;
+      return nullptr;
+    }
+    return &it->second;
+  }
+  std::vector<float> f32(const std::string &n, size_t expect_numel = 0) {
+    const StEntry *e = get(n);
+    std::vector<float> v;
+    if (!e) return v;
+    size_t numel = 1;
+    for (int s : e->shape) numel *= (size_t)s;
+    if (expect_numel && numel != expect_numel) {
+      if (missing.empty()) missing = n + " (shape)";
+      return v;
+    }
+    v.resize(numel);
+    for (size_t i = 0; i < numel; i++) v[i] = at(*e, i);
+    return v;
+  }
+};
+
+static size_t dtype_size(const std::string &d) { return d == "F32" ? 4 : 2; }
+
+static void stage_f32(Staging &st, const std::vector<float> &v, float **slot) {
+  st.add(v.data(), v.size() * sizeof(float), (void **)slot);
+}
+
+// GEMM weight in the loader layout: rows o, reduction over the flattened rest, fp16 RNE,
+// K padded to 8 (weights.c:306-310, 338-347)
+static std::vector<uint16_t> pack_rows(const std::vector<float> &w, int rows, int K, int64_t kp) {
+  std::vector<uint16_t> out((size_t)rows * kp, 0);
+  for (int r = 0; r < rows; r++)
+    for (int k = 0; k < K; k++) out[(size_t)r * kp + k] = host_f2h(w[(size_t)r * K + k]);
+  return out;
+}
+
+static bool load_conv(Loader &L, Staging &st, const std::string &prefix, ConvW &cw,
+                      bool glu, int glu_bn_hint) {
+  const StEntry *e = L.get(prefix + ".conv.weight");
+  if (!e) return false;
+  const int nd = (int)e->shape.size();
+  cw.O = e->shape[0];
+  cw.C = e->shape[nd - 1];
+  cw.KH = nd == 4 ? e->shape[1] : 1;
+  cw.KW = nd == 4 ? e->shape[2] : e->shape[1];
+  cw.K = cw.KH * cw.KW * cw.C;
+  std::vector<float> w = L.f32(prefix + ".conv.weight");
+  std::vector<float> b = L.f32(prefix + ".conv.bias", (size_t)cw.O);
+  if (w.empty() || b.empty()) return false;
+  const int64_t kp = (cw.K + 7) / 8 * 8;
+  std::vector<uint16_t> packed = pack_rows(w, cw.O, cw.K, kp);
+  cw.ld = kp;
+  if (glu) {
+    // interleave [a | b] halves per N tile so each tile holds matching GLU pairs
+    const int O2 = cw.O / 2, bn = glu_bn_hint, hb = bn / 2, ntiles = (O2 + hb - 1) / hb;
+    std::vector<uint16_t> il((size_t)ntiles * bn * kp, 0);
+    for (int t = 0; t < ntiles; t++)
+      for (int j = 0; j < bn; j++) {
+        const int o = t * hb + (j < hb ? j : j - hb);
+        if (o >= O2) continue;
+        const int src = j < hb ? o : O2 + o;
+        memcpy(&il[((size_t)t * bn + j) * kp], &packed[(size_t)src * kp], kp * 2);
+      }
+    packed.swap(il);
+    cw.rows = ntiles * bn;
+    cw.glu_bn = bn;
+  } else {
+    cw.rows = cw.O;
+  }
+  st.add(packed.data(), packed.size() * 2, (void **)&cw.w);
+  stage_f32(st, b, &cw.bias);
+  return true;
+}
+
+// transposed conv weight [O][Ktaps][(1)][C] -> phase matrix B[(o, r)][(j', c)] =
+// W[o][r + S (1 - j')][c] (tap j' = 0 reads input q-1, j' = 1 reads input q)
+static bool load_convtr(Loader &L, Staging &st, const std::string &prefix, ConvW &cw, int S) {
+  const StEntry *e = L.get(prefix + ".conv.weight");
+  if (!e) return false;
+  const int nd = (int)e->shape.size();
+  const int O = e->shape[0], C = e->shape[nd - 1];
+  const int Kt = nd == 4 ? e->shape[1] * e->shape[2] : e->shape[1];
+  if (Kt != 2 * S) {
+    fail("%s: transposed-conv kernel %d is not 2 * stride", prefix.c_str(), Kt);
+    return false;
+  }
+  std::vector<float> w = L.f32(prefix + ".conv.weight");
+  std::vector<float> b = L.f32(prefix + ".conv.bias", (size_t)O);
+  if (w.empty() || b.empty()) return false;
+  const int64_t ld = (2 * C + 7) / 8 * 8;
+  std::vector<uint16_t> ph((size_t)O * S * ld, 0);
+  for (int o = 0; o < O; o++)
+    for (int r = 0; r < S; r++)
+      for (int jp = 0; jp < 2; jp++) {
+        const int tap = r + S * (1 - jp);
+        for (int c = 0; c < C; c++)
+          ph[((size_t)o * S + r) * ld + jp * C + c] = host_f2h(w[((size_t)o * Kt + tap) * C + c]);
+      }
+  cw.O = O;
+  cw.C = C;
+  cw.K = 2 * C;
+  cw.ld = ld;
+  cw.rows = O * S;
+  st.add(ph.data(), ph.size() * 2, (void **)&cw.w);
+  stage_f32(st, b, &cw.bias);
+  return true;
+}
+
+static bool load_linear_cat(Loader &L, Staging &st, const std::vector<std::string> &prefixes,
+                            LinW &lw) {
+  std::vector<float> W, B;
+  int in = 0, out = 0;
+  for (const auto &p : prefixes) {
+    const StEntry *e = L.get(p + ".weight");
+    if (!e || e->shape.size() != 2) return false;
+    if (in && e->shape[1] != in) return false;
+    in = e->shape[1];
+    std::vector<float> w = L.f32(p + ".weight");
+    std::vector<float> b = L.has(p + ".bias") ? L.f32(p + ".bias", (size_t)e->shape[0])
+                                               : std::vector<float>((size_t)e->shape[0], 0.f);
+    W.insert(W.end(), w.begin(), w.end());
+    B.insert(B.end(), b.begin(), b.end());
+    out += e->shape[0];
+  }
+  const int64_t kp = (in + 7) / 8 * 8;
+  std::vector<uint16_t> packed = pack_rows(W, out, in, kp);
+  lw.out = out;
+  lw.in = in;
+  lw.ld = kp;
+  st.add(packed.data(), packed.size() * 2, (void **)&lw.w);
+  stage_f32(st, B, &lw.bias);
+  return true;
+}
+
+static bool load_norm(Loader &L, Staging &st, const std::string &p, NormW &nw, int C) {
+  std::vector<float> w = L.f32(p + ".weight", (size_t)C), b = L.f32(p + ".bias", (size_t)C);
+  if (w.empty() || b.empty()) return false;
+  stage_f32(st, w, &nw.w);
+  stage_f32(st, b, &nw.b);
+  return true;
+}
+
+static int glu_bn_for(int O2) {
+  // fixed N tile for GLU convs: 2*O2 columns rounded up to a power of two, at most 256
+  int bn = 32;
+  while (bn < 256 && bn < 2 * O2) bn *= 2;
+  return bn;
+}
+
+}  // namespace dcb
+
+using namespace dcb;
+
+extern "C" {
+
+DcbModel *dcb_model_load(const char *st_path, const char *cfg_path) {
+  DcbModel *m = new DcbModel();
+  if (!load_config(cfg_path, m->cfg)) {
+    delete m;
+    return nullptr;
+  }
+  const Cfg &c = m->cfg;
+  FILE *f = fopen(st_path, "rb");
+  if (!f) {
+    fail("cannot read weights %s", st_path);
+    delete m;
+    return nullptr;
+  }
+  std::vector<uint8_t> file;
+  {
+    uint8_t buf[1 << 16];
+    size_t n;
+    while ((n = fread(buf, 1, sizeof(buf), f)) > 0) file.insert(file.end(), buf, buf + n);
+    fclose(f);
+  }
+  if (file.size() < 8) {
+    fail("weights file too small: %s", st_path);
+    delete m;
+    return nullptr;
+  }
+  uint64_t hlen = 0;
+  for (int i = 7; i >= 0; i--) hlen = (hlen << 8) | file[i];
+  Loader L;
+  if (8 + hlen > file.size() ||
+      !parse_st_header((const char *)file.data() + 8, (size_t)hlen, L.ents)) {
+    fail("corrupt safetensors header in %s", st_path);
+    delete m;
+    return nullptr;
+  }
+  L.data = file.data() + 8 + hlen;
+  L.data_len = file.size() - 8 - hlen;
+  for (auto &kv : L.ents) {
+    size_t numel = 1;
+    for (int s : kv.second.shape) numel *= (size_t)s;
+    const StEntry &e = kv.second;
+    if ((e.dtype != "F32" && e.dtype != "F16" && e.dtype != "BF16") || e.end < e.begin ||
+        e.end > L.data_len || e.end - e.begin != numel * dtype_size(e.dtype)) {
+      fail("bad tensor entry %s (%s)", kv.first.c_str(), e.dtype.c_str());
+      delete m;
+      return nullptr;
+    }
+  }
+
+  Staging st;
+  bool ok = true;
+  m->depth = c.depth;
+  char p[160];
+  for (int i = 0; i < c.depth && ok; i++) {
+    EncW &e = m->enc[i];
+    snprintf(p, sizeof(p), "encoder.%d.conv", i);
+    ok &= load_conv(L, st, p, e.conv, false, 0);
+    snprintf(p, sizeof(p), "encoder.%d.rewrite", i);
+    if (ok) ok &= load_conv(L, st, p, e.rewrite, true, glu_bn_for(e.conv.O));
+    e.Cin = e.conv.C;
+    e.Cout = e.conv.O;
+    EncW &t = m->tenc[i];
+    snprintf(p, sizeof(p), "tencoder.%d.conv", i);
+    if (ok) ok &= load_conv(L, st, p, t.conv, false, 0);
+    snprintf(p, sizeof(p), "tencoder.%d.rewrite", i);
+    if (ok) ok &= load_conv(L, st, p, t.rewrite, true, glu_bn_for(t.conv.O));
+    t.Cin = t.conv.C;
+    t.Cout = t.conv.O;
+    for (int br = 0; br < 2 && ok; br++) {
+      EncW &E = br ? t : e;
+      E.ndconv = c.dconv_depth;
+      for (int d = 0; d < c.dconv_depth && ok; d++) {
+        DConvW &dw = E.dconv[d];
+        snprintf(p, sizeof(p), "%s.%d.dconv.layers.%d.layers", br ? "tencoder" : "encoder", i, d);
+        std::string base(p);
+        ok &= load_conv(L, st, base + ".0", dw.c0, false, 0);
+        if (ok) ok &= load_conv(L, st, base + ".3", dw.c3, false, 0);
+        if (ok) ok &= load_norm(L, st, base + ".1", dw.gn1, dw.c0.O);
+        if (ok) ok &= load_norm(L, st, base + ".4", dw.gn4, dw.c3.O);
+        if (ok) {
+          std::vector<float> sc = L.f32(base + ".6.scale", (size_t)E.Cout);
+          ok &= !sc.empty();
+          if (ok) stage_f32(st, sc, &dw.scale);
+        }
+      }
+    }
+  }
+  for (int i = 0; i < c.depth && ok; i++) {
+    DecW &d = m->dec[i];
+    snprintf(p, sizeof(p), "decoder.%d.rewrite", i);
+    const StEntry *rw = L.get(std::string(p) + ".conv.weight");
+    ok &= rw != nullptr;
+    if (ok) ok &= load_conv(L, st, p, d.rewrite, true, glu_bn_for(rw->shape[0] / 2));
+    snprintf(p, sizeof(p), "decoder.%d.conv_tr", i);
+    if (ok) ok &= load_convtr(L, st, p, d.convtr, c.stride);
+    d.Cin = d.rewrite.C;
+    d.Cout = d.convtr.O;
+    DecW &t = m->tdec[i];
+    snprintf(p, sizeof(p), "tdecoder.%d.rewrite", i);
+    const StEntry *rt = ok ? L.get(std::string(p) + ".conv.weight") : nullptr;
+    ok &= rt != nullptr;
+    if (ok) ok &= load_conv(L, st, p, t.rewrite, true, glu_bn_for(rt->shape[0] / 2));
+    snprintf(p, sizeof(p), "tdecoder.%d.conv_tr", i);
+    if (ok) ok &= load_convtr(L, st, p, t.convtr, c.stride);
+    t.Cin = t.rewrite.C;
+    t.Cout = t.convtr.O;
+  }
+  if (ok && c.freq_emb != 0.0f && L.has("freq_emb.embedding.weight")) {
+    const StEntry *e = L.get("freq_emb.embedding.weight");
+    m->fe_rows = e->shape[0];
+    m->fe_cols = e->shape[1];
+    stage_f32(st, L.f32("freq_emb.embedding.weight"), &m->freq_emb);
+  }
+  m->D = m->enc[c.depth - 1].Cout;
+  if (ok && c.t_layers > 0) {
+    const int D = m->D;
+    ok &= load_norm(L, st, "crosstransformer.norm_in", m->norm_in, D);
+    if (ok) ok &= load_norm(L, st, "crosstransformer.norm_in_t", m->norm_in_t, D);
+    for (int br = 0; br < 2 && ok; br++) {
+      for (int l = 0; l < c.t_layers && ok; l++) {
+        TLayerW &tl = m->layers[br][l];
+        snprintf(p, sizeof(p), "crosstransformer.%s.%d", br ? "layers_t" : "layers", l);
+        std::string b(p);
+        tl.cross = (l % 2) != (c.t_cross_first ? 1 : 0);
+        const std::string a = b + (tl.cross ? ".cross_attn" : ".attn");
+        if (tl.cross) {
+          ok &= load_linear_cat(L, st, {a + ".query_proj"}, tl.qkv);
+          if (ok) ok &= load_linear_cat(L, st, {a + ".key_proj", a + ".value_proj"}, tl.kv);
+        } else {
+          ok &= load_linear_cat(L, st, {a + ".query_proj", a + ".key_proj", a + ".value_proj"},
+                                tl.qkv);
+        }
+        if (ok) ok &= load_linear_cat(L, st, {a + ".out_proj"}, tl.out);
+        if (ok) ok &= load_linear_cat(L, st, {b + ".linear1"}, tl.lin1);
+        if (ok) ok &= load_linear_cat(L, st, {b + ".linear2"}, tl.lin2);
+        if (ok) ok &= load_norm(L, st, b + ".norm1", tl.norm1, D);
+        if (ok) ok &= load_norm(L, st, b + ".norm2", tl.norm2, D);
+        if (ok && tl.cross) ok &= load_norm(L, st, b + ".norm3", tl.norm3, D);
+        if (ok) ok &= load_norm(L, st, b + ".norm_out.gn", tl.norm_out, D);
+        if (ok) {
+          std::vector<float> g1 = L.f32(b + ".gamma_1.scale", (size_t)D);
+          std::vector<float> g2 = L.f32(b + ".gamma_2.scale", (size_t)D);
+          ok &= !g1.empty() && !g2.empty();
+          if (ok) {
+            stage_f32(st, g1, &tl.gamma1);
+            stage_f32(st, g2, &tl.gamma2);
+          }
+        }
+      }
+    }
+    m->hidden = m->layers[0][0].lin1.out;
+  }
+  if (!ok) {
+    fail("weights %s: missing or malformed tensor '%s'", st_path, L.missing.c_str());
+    delete m;
+    return nullptr;
+  }
+  // periodic Hann window in double, stored as float (stft.c:5-20)
+  std::vector<float> win(c.nfft);
+  for (int i = 0; i < c.nfft; i++)
+    win[i] = (float)(0.5 - 0.5 * cos(2.0 * 3.14159265358979323846 * (double)i / (double)c.nfft));
+  stage_f32(st, win, &m->window);
+
+  m->block_bytes = st.bytes.size();
+  if (cudaMalloc(&m->block, m->block_bytes ? m->block_bytes : 1) != cudaSuccess) {
+    (void)cudaGetLastError();
+    fail("out of device memory uploading weights (%.1f MB)", (double)m->block_bytes / 1048576.0);
+    delete m;
+    return nullptr;
+  }
+  DCB_CUDA(cudaMemcpy(m->block, st.bytes.data(), m->block_bytes, cudaMemcpyHostToDevice));
+  for (auto &fx : st.fix) *fx.second = (uint8_t *)m->block + fx.first;
+  // the stream-ordered pool keeps freed activation memory for reuse
+  cudaMemPool_t pool;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+    uint64_t thr = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+  }
+  return m;
+}
+
+void dcb_model_free(DcbModel *m) {
+  if (!m) return;
+  cudaStreamSynchronize(stream());
+  for (auto &kv : m->pos_cache) cudaFree(kv.second);
+  if (m->block) cudaFree(m->block);
+  delete m;
+}
+
+int dcb_model_info(const DcbModel *m, int *n_sources, int *audio_channels, int *valid_length,
+                   int *samplerate, float *segment) {
+  if (!m) return -1;
+  if (n_sources) *n_sources = m->cfg.n_sources;
+  if (audio_channels) *audio_channels = m->cfg.audio_channels;
+  if (valid_length) *valid_length = m->cfg.valid_length;
+  if (samplerate) *samplerate = m->cfg.samplerate;
+  if (segment) *segment = m->cfg.segment;
+  return 0;
+}
+
+size_t dcb_model_weight_bytes(const DcbModel *m) { return m ? m->block_bytes : 0; }
+void *dcb_model_weight_block(DcbModel *m) { return m ? m->block : nullptr; }
+
+}  // extern "C"

@@ -1,0 +1,992 @@
+// Forward pass of the htdemucs_6s engine (htdemucs.c:136-280 order), the teacher-forced
+// single-stage entry points used by the parity tests (test_compare.c:139-216 order) and
+// the segment scheduler (apply.c:179-306).
+#include <math.h>
+
+#include <algorithm>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+
+namespace dcb {
+
+
+// ------------------------------------------------------------------ device memory
+static float *dalloc(size_t n) {
+  void *p = nullptr;
+  DCB_CUDA(cudaMallocAsync(&p, (n ? n : 1) * sizeof(float), stream()));
+  return (float *)p;
+}
+static uint16_t *halloc(size_t n) {
+  void *p = nullptr;
+  DCB_CUDA(cudaMallocAsync(&p, (n ? n : 1) * sizeof(uint16_t), stream()));
+  return (uint16_t *)p;
+}
+static void dfree(void *p) {
+  if (p) DCB_CUDA(cudaFreeAsync(p, stream()));
+}
+
+struct Stage {
+  DcbStageFn fn = nullptr;
+  void *user = nullptr;
+  void emit(const char *name, const float *p, std::initializer_list<int> shape) {
+    if (!fn) return;
+    DCB_CUDA(cudaStreamSynchronize(stream()));
+    int s[8];
+    int n = 0;
+    for (int v : shape) s[n++] = v;
+    fn(name, p, n, s, user);
+  }
+};
+
+// ------------------------------------------------------------------ conv helpers
+// conv over images of x viewed as [n1][n2] -> (c, h, w) with the given strides, output
+// written through the same kind of view; act: 0 none, 1 gelu, 2 glu (weights interleaved)
+struct Img {
+  int N1 = 1, N2 = 1;
+  int64_t sN1 = 0, sN2 = 0, sC = 0, sH = 0;
+  int C = 0, H = 1, W = 1;
+};
+
+static Img contiguous(int N, int C, int H, int W) {
+  Img v;
+  v.N1 = N;
+  v.N2 = 1;
+  v.sN1 = (int64_t)C * H * W;
+  v.sC = (int64_t)H * W;
+  v.sH = W;
+  v.C = C;
+  v.H = H;
+  v.W = W;
+  return v;
+}
+// [B, C, Fr, T] seen as B*Fr images [C][1][T] (the DConv view of layers.c:3-20)
+static Img freq_rows(int B, int C, int Fr, int T) {
+  Img v;
+  v.N1 = B;
+  v.N2 = Fr;
+  v.sN1 = (int64_t)C * Fr * T;
+  v.sN2 = T;
+  v.sC = (int64_t)Fr * T;
+  v.sH = 0;
+  v.C = C;
+  v.H = 1;
+  v.W = T;
+  return v;
+}
+
+static void conv(const ConvW &cw, const float *x, const float *x2, const Img &in, int SH, int SW,
+                 int PH, int PW, int DH, int DW, int Ho, int Wo, float *y, const Img &out,
+                 int act, const float *res = nullptr, const float *scale = nullptr) {
+  Gather g{};
+  g.x = x;
+  g.x2 = x2;
+  g.N2 = in.N2;
+  g.sN1 = in.sN1;
+  g.sN2 = in.sN2;
+  g.sC = in.sC;
+  g.sH = in.sH;
+  g.C = in.C;
+  g.H = in.H;
+  g.W = in.W;
+  g.KH = cw.KH;
+  g.KW = cw.KW;
+  g.SH = SH;
+  g.SW = SW;
+  g.PH = PH;
+  g.PW = PW;
+  g.DH = DH;
+  g.DW = DW;
+  g.Ho = Ho;
+  g.Wo = Wo;
+  g.K = cw.K;
+  Epi e;
+  e.mode = EPI_CONV;
+  e.bias = cw.bias;
+  e.act = act;
+  e.y = y;
+  e.oN2 = out.N2;
+  e.oN1 = out.sN1;
+  e.oN2s = out.sN2;
+  e.oC = out.sC;
+  e.oH = out.sH;
+  e.O = act == 2 ? cw.O / 2 : cw.O;
+  e.Ho = Ho;
+  e.Wo = Wo;
+  e.res = res;
+  e.scale = scale;
+  const int64_t M = (int64_t)in.N1 * in.N2 * Ho * Wo;
+  gemm_gather(g, M, cw.w, cw.rows, cw.ld, e, act == 2 ? cw.glu_bn : 0);
+}
+
+// stride-phase transposed conv along H (freq) or W (time), crop + optional GELU
+static void conv_tr(const ConvW &cw, const float *x, const Img &in, bool axis_h, int S,
+                    int crop, int out_len, bool gelu, float *y, const Img &out) {
+  Gather g{};
+  g.x = x;
+  g.N2 = in.N2;
+  g.sN1 = in.sN1;
+  g.sN2 = in.sN2;
+  g.sC = in.sC;
+  g.sH = in.sH;
+  g.C = in.C;
+  g.H = in.H;
+  g.W = in.W;
+  g.KH = axis_h ? 2 : 1;
+  g.KW = axis_h ? 1 : 2;
+  g.SH = g.SW = 1;
+  g.PH = axis_h ? 1 : 0;
+  g.PW = axis_h ? 0 : 1;
+  g.DH = g.DW = 1;
+  g.Ho = axis_h ? in.H + 1 : in.H;
+  g.Wo = axis_h ? in.W : in.W + 1;
+  g.K = 2 * in.C;
+  Epi e;
+  e.mode = EPI_CONVTR;
+  e.bias = cw.bias;
+  e.act = gelu ? 1 : 0;
+  e.y = y;
+  e.oN2 = out.N2;
+  e.oN1 = out.sN1;
+  e.oN2s = out.sN2;
+  e.oC = out.sC;
+  e.oH = out.sH;
+  e.O = cw.O;
+  e.Ho = g.Ho;
+  e.Wo = g.Wo;
+  e.stride = S;
+  e.crop = crop;
+  e.out_len = out_len;
+  e.axis_h = axis_h ? 1 : 0;
+  gemm_gather(g, (int64_t)in.N1 * in.N2 * g.Ho * g.Wo, cw.w, cw.rows, cw.ld, e);
+}
+
+// ------------------------------------------------------------------ layers
+// DConv residual branch (layers.c:24-53) applied in place on y [B, C, Fr, T] (Fr = 1 for
+// the time branch).
+static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
+  const Img v = freq_rows(B, C, Fr, T);
+  float *stat = dalloc((size_t)B * Fr * 2);
+  for (int d = 0; d < E.ndconv; d++) {
+    const DConvW &dw = E.dconv[d];
+    const int dil = 1 << d;
+    const int hid = dw.c0.O, C2 = dw.c3.O;
+    // conv k3, dilation 2^d, padding 2^d -> h [B, hid, Fr, T]
+    float *h = dalloc((size_t)B * hid * Fr * T);
+    const Img hv = freq_rows(B, hid, Fr, T);
+    conv(dw.c0, y, nullptr, v, 1, 1, 0, dil, 1, dil, 1, T, h, hv, 0);
+    // GroupNorm(1) + GELU
+    RowView rh{h, Fr, (int64_t)hid * Fr * T, T, (int64_t)Fr * T, hid, T};
+    rowview_stats(rh, B, 1e-5f, stat, stat + (size_t)B * Fr, nullptr);
+    {
+      const int64_t n = (int64_t)B * hid * Fr * T;
+      k_gn_gelu<<<grid_for(n, 256), 256, 0, stream()>>>(rh, h, stat, stat + (size_t)B * Fr,
+                                                       dw.gn1.w, dw.gn1.b, B);
+      DCB_LAUNCHED();
+    }
+    // conv 1x1 -> z [B, 2C, Fr, T]
+    float *z = dalloc((size_t)B * C2 * Fr * T);
+    const Img zv = freq_rows(B, C2, Fr, T);
+    conv(dw.c3, h, nullptr, hv, 1, 1, 0, 0, 1, 1, 1, T, z, zv, 0);
+    dfree(h);
+    // GroupNorm(1) + GLU, LayerScale residual into y
+    RowView rz{z, Fr, (int64_t)C2 * Fr * T, T, (int64_t)Fr * T, C2, T};
+    rowview_stats(rz, B, 1e-5f, stat, stat + (size_t)B * Fr, nullptr);
+    {
+      const int64_t n = (int64_t)B * (C2 / 2) * Fr * T;
+      k_gn_glu_res<<<grid_for(n, 256), 256, 0, stream()>>>(
+          rz, stat, stat + (size_t)B * Fr, dw.gn4.w, dw.gn4.b, dw.scale, y,
+          (int64_t)C * Fr * T, T, (int64_t)Fr * T, B);
+      DCB_LAUNCHED();
+    }
+    dfree(z);
+  }
+  dfree(stat);
+}
+
+// freq encoder (dc_henc with freq = 1): x [B, Cin, H, W] -> [B, Cout, H/S, W]
+static float *enc_freq(DcbModel *m, int idx, const float *x, int B, int H, int W, int *Ho_out) {
+  const EncW &E = m->enc[idx];
+  const int S = m->cfg.stride, K = m->cfg.kernel_size, pad = K / 4;
+  const int Ho = (H + 2 * pad - K) / S + 1;
+  const int C = E.Cout;
+  float *y = dalloc((size_t)B * C * Ho * W);
+  conv(E.conv, x, nullptr, contiguous(B, E.Cin, H, W), S, 1, pad, 0, 1, 1, Ho, W, y,
+       contiguous(B, C, Ho, W), 1);
+  dconv(E, y, B, C, Ho, W);
+  float *z = dalloc((size_t)B * C * Ho * W);
+  const int ce = m->cfg.context_enc;
+  conv(E.rewrite, y, nullptr, contiguous(B, C, Ho, W), 1, 1, ce, ce, 1, 1, Ho, W, z,
+       contiguous(B, C, Ho, W), 2);
+  dfree(y);
+  if (idx == 0 && m->freq_emb) {
+    const int64_t n = (int64_t)B * C * Ho * W;
+    k_add_freq_emb<<<grid_for(n, 256), 256, 0, stream()>>>(
+        z, m->freq_emb, m->cfg.freq_emb * m->cfg.emb_scale, B, C, Ho, W, m->fe_cols);
+    DCB_LAUNCHED();
+  }
+  *Ho_out = Ho;
+  return z;
+}
+
+// time encoder: x [B, Cin, L] -> [B, Cout, ceil(L/S)]
+static float *enc_time(DcbModel *m, int idx, const float *x, int B, int L, int *Lo_out) {
+  const EncW &E = m->tenc[idx];
+  const int S = m->cfg.stride, K = m->cfg.kernel_size, pad = K / 4;
+  const int Lp = (L + S - 1) / S * S;  // zero pad to a multiple of the stride (layers.c:88-94)
+  const int Lo = (Lp + 2 * pad - K) / S + 1;
+  const int C = E.Cout;
+  float *y = dalloc((size_t)B * C * Lo);
+  conv(E.conv, x, nullptr, contiguous(B, E.Cin, 1, L), 1, S, 0, pad, 1, 1, 1, Lo, y,
+       contiguous(B, C, 1, Lo), 1);
+  dconv(E, y, B, C, 1, Lo);
+  float *z = dalloc((size_t)B * C * Lo);
+  const int ce = m->cfg.context_enc;
+  conv(E.rewrite, y, nullptr, contiguous(B, C, 1, Lo), 1, 1, 0, ce, 1, 1, 1, Lo, z,
+       contiguous(B, C, 1, Lo), 2);
+  dfree(y);
+  *Lo_out = Lo;
+  return z;
+}
+
+// freq decoder: x, skip [B, Cin, H, W] -> [B, Cout, S*H, W]  (dc_hdec, layers.c:143-220)
+static float *dec_freq(DcbModel *m, int idx, const float *x, const float *skip, int B, int H,
+                       int W, bool last) {
+  const DecW &D = m->dec[idx];
+  const int C = D.Cin, S = m->cfg.stride, c = m->cfg.context, pad = m->cfg.kernel_size / 4;
+  float *z = dalloc((size_t)B * C * H * W);
+  conv(D.rewrite, x, skip, contiguous(B, C, H, W), 1, 1, c, c, 1, 1, H, W, z,
+       contiguous(B, C, H, W), 2);
+  const int out_len = (H - 1) * S + m->cfg.kernel_size - 2 * pad;
+  float *y = dalloc((size_t)B * D.Cout * out_len * W);
+  conv_tr(D.convtr, z, contiguous(B, C, H, W), true, S, pad, out_len, !last, y,
+          contiguous(B, D.Cout, out_len, W));
+  dfree(z);
+  return y;
+}
+
+// time decoder: x, skip [B, Cin, L] -> [B, Cout, length]
+static float *dec_time(DcbModel *m, int idx, const float *x, const float *skip, int B, int L,
+                       int length, bool last) {
+  const DecW &D = m->tdec[idx];
+  const int C = D.Cin, S = m->cfg.stride, c = m->cfg.context, pad = m->cfg.kernel_size / 4;
+  float *z = dalloc((size_t)B * C * L);
+  conv(D.rewrite, x, skip, contiguous(B, C, 1, L), 1, 1, 0, c, 1, 1, 1, L, z,
+       contiguous(B, C, 1, L), 2);
+  float *y = dalloc((size_t)B * D.Cout * length);
+  conv_tr(D.convtr, z, contiguous(B, C, 1, L), false, S, pad, length, !last, y,
+          contiguous(B, D.Cout, 1, length));
+  dfree(z);
+  return y;
+}
+
+// ------------------------------------------------------------------ transformer
+// positional embeddings (transformer.c:107-158), computed once per token grid on the host
+// with the reference's float32 formulas and cached on the device
+static const float *pos_2d(DcbModel *m, int C, int Fr, int T1) {
+  const long long key = ((long long)1 << 62) | ((long long)C << 40) | ((long long)Fr << 24) | T1;
+  auto it = m->pos_cache.find(key);
+  if (it != m->pos_cache.end()) return it->second;
+  const int half = C / 2, nterm = half / 2;
+  std::vector<float> div(nterm), pe((size_t)T1 * Fr * C);
+  const float sc = -logf(m->cfg.t_max_period) / (float)half;
+  for (int j = 0; j < nterm; j++) div[j] = expf((float)(2 * j) * sc);
+  const float wgt = m->cfg.t_weight_pos_embed;
+  for (int t = 0; t < T1; t++)
+    for (int f = 0; f < Fr; f++) {
+      float *row = &pe[((size_t)t * Fr + f) * C];
+      for (int c = 0; c < C; c++) {
+        const int cc = c < half ? c : c - half;
+        const float pos = c < half ? (float)t : (float)f;
+        const float ang = pos * div[cc / 2];
+        row[c] = ((cc % 2) == 0 ? sinf(ang) : cosf(ang)) * wgt;
+      }
+    }
+  float *d = nullptr;
+  DCB_CUDA(cudaMalloc(&d, pe.size() * sizeof(float)));
+  DCB_CUDA(cudaMemcpy(d, pe.data(), pe.size() * sizeof(float), cudaMemcpyHostToDevice));
+  m->pos_cache[key] = d;
+  return d;
+}
+
+static const float *pos_1d(DcbModel *m, int C, int T) {
+  const long long key = ((long long)C << 40) | T;
+  auto it = m->pos_cache.find(key);
+  if (it != m->pos_cache.end()) return it->second;
+  const int half = C / 2;
+  std::vector<float> pe((size_t)T * C);
+  const float wgt = m->cfg.t_weight_pos_embed;
+  for (int t = 0; t < T; t++)
+    for (int j = 0; j < half; j++) {
+      const float den = powf(m->cfg.t_max_period, (float)j / (float)(half - 1));
+      const float ph = (float)t / den;
+      pe[(size_t)t * C + j] = cosf(ph) * wgt;
+      pe[(size_t)t * C + half + j] = sinf(ph) * wgt;
+    }
+  float *d = nullptr;
+  DCB_CUDA(cudaMalloc(&d, pe.size() * sizeof(float)));
+  DCB_CUDA(cudaMemcpy(d, pe.data(), pe.size() * sizeof(float), cudaMemcpyHostToDevice));
+  m->pos_cache[key] = d;
+  return d;
+}
+
+static void linear_rows(const LinW &lw, const uint16_t *x16, int64_t R, Epi e) {
+  RowsA a{x16, (int64_t)lw.ld, 0};
+  RowsA b{lw.w, lw.ld, 0};
+  e.bias = lw.bias;
+  gemm_rows(R, lw.out, lw.in, a, b, 1, e);
+}
+
+// Per-branch work buffers of one transformer layer
+struct TBuf {
+  uint16_t *ln = nullptr;   // [R][ld] fp16 LN output (query side)
+  uint16_t *lnk = nullptr;  // [R][ld] fp16 LN output of the key/value side (cross)
+  uint16_t *q = nullptr, *k = nullptr, *vt = nullptr;
+  uint16_t *att = nullptr;  // [R][D] fp16 attention output
+  uint16_t *hid = nullptr;  // [R][hidden] fp16 FFN hidden
+};
+
+// one branch of layer l: x [B, Tq, D] (updated in place); kv side tokens Tk, its LN output
+// already in b.lnk for cross layers
+static void tlayer_branch(DcbModel *m, const TLayerW &tl, float *x, int B, int Tq, int Tk,
+                          TBuf &b) {
+  const int D = m->D, H = m->cfg.t_heads, hd = D / H;
+  const int64_t R = (int64_t)B * Tq;
+  const int64_t Tkp = (Tk + 7) / 8 * 8;
+  // attention projections with the head split fused in the epilogue
+  Epi eh;
+  eh.mode = EPI_HEADS;
+  eh.heads = H;
+  eh.hd = hd;
+  eh.sec_cols = D;
+  if (!tl.cross) {
+    eh.T = Tq;
+    eh.Tp = Tkp;
+    eh.sec_ptr[0] = b.q;
+    eh.sec_ptr[1] = b.k;
+    eh.sec_ptr[2] = b.vt;
+    eh.sec_layout[2] = 1;
+    linear_rows(tl.qkv, b.ln, R, eh);
+  } else {
+    eh.T = Tq;
+    eh.sec_ptr[0] = b.q;
+    linear_rows(tl.qkv, b.ln, R, eh);
+    Epi ek = eh;
+    ek.T = Tk;
+    ek.Tp = Tkp;
+    ek.sec_ptr[0] = b.k;
+    ek.sec_ptr[1] = b.vt;
+    ek.sec_layout[0] = 0;
+    ek.sec_layout[1] = 1;
+    linear_rows(tl.kv, b.lnk, (int64_t)B * Tk, ek);
+  }
+  flash_attention(b.q, b.k, b.vt, B, H, Tq, Tk, hd, Tkp, b.att, nullptr);
+  // x = x + gamma_1 * (att W_o^T + b_o)
+  Epi er;
+  er.mode = EPI_ROWS_F32;
+  er.out = x;
+  er.ldo = D;
+  er.res = x;
+  er.ldr = D;
+  er.gamma = tl.gamma1;
+  RowsA a{b.att, D, 0};
+  {
+    Epi e2 = er;
+    e2.bias = tl.out.bias;
+    gemm_rows(R, tl.out.out, tl.out.in, a, RowsA{tl.out.w, tl.out.ld, 0}, 1, e2);
+  }
+  // feed forward: LN -> linear1 + GELU (fp16) -> linear2 + LayerScale residual
+  const NormW &nf = tl.cross ? tl.norm3 : tl.norm2;
+  layernorm(x, b.ln, nf.w, nf.b, R, D, 1e-5f, true, (int)tl.lin1.ld);
+  Epi eg;
+  eg.mode = EPI_ROWS_F16;
+  eg.act = 1;
+  eg.out = b.hid;
+  eg.ldo = tl.lin2.ld;
+  linear_rows(tl.lin1, b.ln, R, eg);
+  Epi e3 = er;
+  e3.gamma = tl.gamma2;
+  linear_rows(tl.lin2, b.hid, R, e3);
+  // GroupNorm(1) over [Tq, D] per batch, affine on D (norm_out)
+  float *st = dalloc((size_t)B * 2);
+  row_stats(x, B, (int64_t)Tq * D, st, st + B);
+  dk_norm_apply_last(x, x, st, st + B, tl.norm_out.w, tl.norm_out.b, B, (int64_t)Tq * D, D,
+                     1e-5f);
+  dfree(st);
+}
+
+// dc_crosstransformer (transformer.c:160-216): x [B, C, Fr, T1], xt [B, C, T2] in place
+static void crosstransformer(DcbModel *m, float *x, float *xt, int B, int Fr, int T1, int T2) {
+  const int D = m->D, H = m->cfg.t_heads, hd = D / H;
+  const int N1 = Fr * T1, N2 = T2;
+  float *tx = dalloc((size_t)B * N1 * D), *tt = dalloc((size_t)B * N2 * D);
+  {
+    const int64_t warps = (int64_t)B * N1;
+    k_tokens_ln_pos<<<(unsigned)((warps + 3) / 4), 128, 0, stream()>>>(
+        x, tx, m->norm_in.w, m->norm_in.b, pos_2d(m, D, Fr, T1), B, D, Fr, T1, 1e-5f);
+    DCB_LAUNCHED();
+    const int64_t warps2 = (int64_t)B * N2;
+    k_tokens_ln_pos<<<(unsigned)((warps2 + 3) / 4), 128, 0, stream()>>>(
+        xt, tt, m->norm_in_t.w, m->norm_in_t.b, pos_1d(m, D, T2), B, D, 1, T2, 1e-5f);
+    DCB_LAUNCHED();
+  }
+  const int ldl = (D + 7) / 8 * 8;
+  const int hidden = m->hidden, ldh = (hidden + 7) / 8 * 8;
+  TBuf bx, bt;
+  const int64_t R1 = (int64_t)B * N1, R2 = (int64_t)B * N2;
+  const int64_t Np1 = (N1 + 7) / 8 * 8, Np2 = (N2 + 7) / 8 * 8;
+  const int64_t Nmax = N1 > N2 ? N1 : N2, Npmax = Np1 > Np2 ? Np1 : Np2;
+  for (TBuf *b : {&bx, &bt}) {
+    const int64_t R = b == &bx ? R1 : R2;
+    b->ln = halloc((size_t)R * ldl);
+    b->lnk = halloc((size_t)(R1 > R2 ? R1 : R2) * ldl);
+    b->q = halloc((size_t)B * H * Nmax * hd);
+    b->k = halloc((size_t)B * H * Nmax * hd);
+    b->vt = halloc((size_t)B * H * hd * Npmax);
+    b->att = halloc((size_t)R * D);
+    b->hid = halloc((size_t)R * ldh);
+  }
+  for (int l = 0; l < m->cfg.t_layers; l++) {
+    const TLayerW &lx = m->layers[0][l], &lt = m->layers[1][l];
+    if (!lx.cross) {
+      layernorm(tx, bx.ln, lx.norm1.w, lx.norm1.b, R1, D, 1e-5f, true, ldl);
+      tlayer_branch(m, lx, tx, B, N1, N1, bx);
+      layernorm(tt, bt.ln, lt.norm1.w, lt.norm1.b, R2, D, 1e-5f, true, ldl);
+      tlayer_branch(m, lt, tt, B, N2, N2, bt);
+    } else {
+      // both branches read the previous layer's tokens: take every LN first
+      layernorm(tx, bx.ln, lx.norm1.w, lx.norm1.b, R1, D, 1e-5f, true, ldl);
+      layernorm(tt, bx.lnk, lx.norm2.w, lx.norm2.b, R2, D, 1e-5f, true, ldl);
+      layernorm(tt, bt.ln, lt.norm1.w, lt.norm1.b, R2, D, 1e-5f, true, ldl);
+      layernorm(tx, bt.lnk, lt.norm2.w, lt.norm2.b, R1, D, 1e-5f, true, ldl);
+      tlayer_branch(m, lx, tx, B, N1, N2, bx);
+      tlayer_branch(m, lt, tt, B, N2, N1, bt);
+    }
+  }
+  {
+    const int64_t n1 = (int64_t)B * D * N1, n2 = (int64_t)B * D * N2;
+    k_tokens_to_chw<<<grid_for(n1, 256), 256, 0, stream()>>>(tx, x, B, D, Fr, T1);
+    DCB_LAUNCHED();
+    k_tokens_to_chw<<<grid_for(n2, 256), 256, 0, stream()>>>(tt, xt, B, D, 1, T2);
+    DCB_LAUNCHED();
+  }
+  for (TBuf *b : {&bx, &bt}) {
+    dfree(b->ln);
+    dfree(b->lnk);
+    dfree(b->q);
+    dfree(b->k);
+    dfree(b->vt);
+    dfree(b->att);
+    dfree(b->hid);
+  }
+  dfree(tx);
+  dfree(tt);
+}
+
+// ------------------------------------------------------------------ forward
+static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, Stage &sg) {
+  const Cfg &c = m->cfg;
+  const int C = c.audio_channels, L = c.valid_length, nfft = c.nfft, hop = c.hop;
+  const int depth = m->depth;
+  if (T > L) {
+    fail("forward: input length %d exceeds the training length %d", T, L);
+    return -1;
+  }
+  // mix padded to the training length (htdemucs.c:141-147)
+  const float *mix = mix_in;
+  float *mixp = nullptr;
+  if (T < L) {
+    mixp = dalloc((size_t)B * C * L);
+    k_chunk<<<grid_for((int64_t)B * C * L, 256), 256, 0, stream()>>>(mix_in, mixp, B, C, T, 0, L,
+                                                                     (int64_t)C * L);
+    DCB_LAUNCHED();
+    mix = mixp;
+  }
+  // spectrogram (stft.c:29-47): two reflect pads then the STFT
+  const int le = (L + hop - 1) / hop;
+  const int pad = (hop / 2) * 3, extra = pad + le * hop - L;
+  const int L1 = L + pad + extra, L2 = L1 + nfft;
+  const int nb = nfft / 2;
+  float *xp = dalloc((size_t)B * C * L1), *xc = dalloc((size_t)B * C * L2);
+  dk_reflect_pad(mix, xp, (int64_t)B * C, L, pad, extra);
+  dk_reflect_pad(xp, xc, (int64_t)B * C, L1, nfft / 2, nfft / 2);
+  dfree(xp);
+  float *mag = dalloc((size_t)B * 2 * C * nb * le);
+  dk_stft(xc, mag, (int64_t)B * C, L2, nfft, hop, 2, le, nb, m->window);
+  dfree(xc);
+  sg.emit("mag", mag, {B, 2 * C, nb, le});
+  // per-segment normalisation (htdemucs.c:152-159)
+  float *stats = dalloc((size_t)B * 4);
+  float *mean = stats, *var = stats + B, *meant = stats + 2 * B, *vart = stats + 3 * B;
+  const int64_t per_mag = (int64_t)2 * C * nb * le;
+  row_stats(mag, B, per_mag, mean, var);
+  float *x = dalloc((size_t)B * per_mag);
+  dk_affine_rows(mag, x, mean, var, B, per_mag, 1e-5f, 0);
+  dfree(mag);
+  sg.emit("x_norm", x, {B, 2 * C, nb, le});
+  row_stats(mix, B, (int64_t)C * L, meant, vart);
+  float *xt = dalloc((size_t)B * C * L);
+  dk_affine_rows(mix, xt, meant, vart, B, (int64_t)C * L, 1e-5f, 0);
+  sg.emit("xt_norm", xt, {B, C, L});
+
+  // encoders
+  std::vector<float *> saved, saved_t;
+  std::vector<int> fr_len, t_len;  // H of the freq input, length of the time input
+  int H = nb, W = le, Lt = L;
+  char name[32];
+  for (int i = 0; i < depth; i++) {
+    t_len.push_back(Lt);
+    int Lo;
+    float *xt2 = enc_time(m, i, xt, B, Lt, &Lo);
+    dfree(xt);
+    xt = xt2;
+    Lt = Lo;
+    saved_t.push_back(xt);
+    snprintf(name, sizeof(name), "tenc_%d", i);
+    sg.emit(name, xt, {B, m->tenc[i].Cout, Lt});
+    fr_len.push_back(H);
+    int Ho;
+    float *x2 = enc_freq(m, i, x, B, H, W, &Ho);
+    dfree(x);
+    x = x2;
+    H = Ho;
+    saved.push_back(x);
+    snprintf(name, sizeof(name), "enc_%d", i);
+    sg.emit(name, x, {B, m->enc[i].Cout, H, W});
+  }
+  // the encoder outputs are kept as skips; the transformer works on copies
+  const int D = m->D;
+  float *tx = dalloc((size_t)B * D * H * W), *txt = dalloc((size_t)B * D * Lt);
+  DCB_CUDA(cudaMemcpyAsync(tx, x, (size_t)B * D * H * W * 4, cudaMemcpyDeviceToDevice, stream()));
+  DCB_CUDA(cudaMemcpyAsync(txt, xt, (size_t)B * D * Lt * 4, cudaMemcpyDeviceToDevice, stream()));
+  if (c.t_layers > 0) crosstransformer(m, tx, txt, B, H, W, Lt);
+  sg.emit("transformer_x", tx, {B, D, H, W});
+  sg.emit("transformer_xt", txt, {B, D, Lt});
+  x = tx;
+  xt = txt;
+  // decoders (htdemucs.c:198-237)
+  for (int i = 0; i < depth; i++) {
+    const bool last = i == depth - 1;
+    float *skip = saved.back();
+    saved.pop_back();
+    const int Hin = H;
+    H = fr_len.back();
+    fr_len.pop_back();
+    float *x2 = dec_freq(m, i, x, skip, B, Hin, W, last);
+    dfree(x);
+    dfree(skip);
+    x = x2;
+    if (H != (Hin - 1) * c.stride + c.kernel_size - 2 * (c.kernel_size / 4)) {
+      fail("decoder %d: frequency length mismatch", i);
+    }
+    snprintf(name, sizeof(name), "dec_%d", i);
+    sg.emit(name, x, {B, m->dec[i].Cout, H, W});
+    float *skip_t = saved_t.back();
+    saved_t.pop_back();
+    const int Lin = Lt;
+    Lt = t_len.back();
+    t_len.pop_back();
+    float *xt2 = dec_time(m, i, xt, skip_t, B, Lin, Lt, last);
+    dfree(xt);
+    dfree(skip_t);
+    xt = xt2;
+    snprintf(name, sizeof(name), "tdec_%d", i);
+    sg.emit(name, xt, {B, m->tdec[i].Cout, Lt});
+  }
+  // output (htdemucs.c:242-279)
+  const int S = c.n_sources;
+  const int Ctot = m->dec[depth - 1].Cout;  // S * 2C
+  const int64_t per_x = (int64_t)Ctot * H * W;
+  dk_affine_rows(x, x, mean, var, B, per_x, 1e-5f, 1);
+  const int NF = W + 4;
+  const int64_t R = (int64_t)B * S * (Ctot / S / 2);
+  float *frames = dalloc((size_t)R * NF * nfft);
+  dk_istft_frames(x, frames, R, H, W, 2, nfft, m->window);
+  dfree(x);
+  float *xi = dalloc((size_t)R * L);
+  dk_ola(frames, xi, R, NF, nfft, hop, m->window, (int64_t)nfft / 2 + pad, L);
+  dfree(frames);
+  sg.emit("ispec", xi, {B, S, (int)(Ctot / S / 2), L});
+  const int keep = T < L ? T : L;
+  {
+    const int64_t per = (int64_t)m->tdec[depth - 1].Cout * Lt;
+    const int64_t n = (int64_t)B * (per / Lt) * keep;
+    k_final_combine<<<grid_for(n, 256), 256, 0, stream()>>>(xt, xi, out, meant, vart, B, per, Lt,
+                                                           L, keep, 1e-5f);
+    DCB_LAUNCHED();
+  }
+  sg.emit("stems", out, {B, S, C, keep});
+  dfree(xi);
+  dfree(xt);
+  dfree(stats);
+  dfree(mixp);
+  return keep;
+}
+
+// ------------------------------------------------------------------ segment scheduler
+// CPython's random.Random(seed).randint (MT19937, Matsumoto & Nishimura 1998; seeding by
+// init_by_array over the seed's 32-bit words; randbelow by rejection on getrandbits(k)),
+// which apply.c:5-107 restates so that shifts match the Python original.
+struct Mt {
+  uint32_t s[624];
+  int i = 625;
+  void init(uint32_t v) {
+    s[0] = v;
+    for (int k = 1; k < 624; k++) s[k] = 1812433253u * (s[k - 1] ^ (s[k - 1] >> 30)) + (uint32_t)k;
+    i = 624;
+  }
+  void seed(uint64_t n) {
+    uint32_t key[2];
+    int nk = 0;
+    if (n == 0) key[nk++] = 0;
+    while (n && nk < 2) {
+      key[nk++] = (uint32_t)(n & 0xffffffffu);
+      n >>= 32;
+    }
+    init(19650218u);
+    int a = 1, b = 0;
+    for (int k = 624 > nk ? 624 : nk; k; k--) {
+      s[a] = (s[a] ^ ((s[a - 1] ^ (s[a - 1] >> 30)) * 1664525u)) + key[b] + (uint32_t)b;
+      a++;
+      b++;
+      if (a >= 624) {
+        s[0] = s[623];
+        a = 1;
+      }
+      if (b >= nk) b = 0;
+    }
+    for (int k = 623; k; k--) {
+      s[a] = (s[a] ^ ((s[a - 1] ^ (s[a - 1] >> 30)) * 1566083941u)) - (uint32_t)a;
+      a++;
+      if (a >= 624) {
+        s[0] = s[623];
+        a = 1;
+      }
+    }
+    s[0] = 0x80000000u;
+  }
+  uint32_t next() {
+    if (i >= 624) {
+      for (int k = 0; k < 624; k++) {
+        const uint32_t y = (s[k] & 0x80000000u) | (s[(k + 1) % 624] & 0x7fffffffu);
+        s[k] = s[(k + 397) % 624] ^ (y >> 1) ^ ((y & 1u) ? 0x9908b0dfu : 0u);
+      }
+      i = 0;
+    }
+    uint32_t y = s[i++];
+    y ^= y >> 11;
+    y ^= (y << 7) & 0x9d2c5680u;
+    y ^= (y << 15) & 0xefc60000u;
+    y ^= y >> 18;
+    return y;
+  }
+  int randint(int lo, int hi) {
+    const uint32_t n = (uint32_t)(hi - lo + 1);
+    int k = 0;
+    for (uint32_t t = n; t; t >>= 1) k++;
+    uint32_t v;
+    do {
+      v = k == 0 ? 0 : next() >> (32 - k);
+    } while (v >= n);
+    return lo + (int)v;
+  }
+};
+
+struct Plan {
+  int seg = 0, stride = 0;
+  std::vector<int> offsets;
+  // forwards of this shard: indices into offsets; full segments batched, tails alone
+  std::vector<std::vector<int>> full_batches;
+  std::vector<int> tails;
+};
+
+static Plan make_plan(const Cfg &c, int length, const DcbApplyOpts &o) {
+  Plan p;
+  p.seg = (int)((float)c.samplerate * c.segment);
+  p.stride = (int)((1.0f - o.overlap) * (float)p.seg);
+  if (p.stride <= 0) return p;
+  for (int off = 0; off < length; off += p.stride) p.offsets.push_back(off);
+  const int bs = o.batch_size < 1 ? 1 : (o.batch_size > 32 ? 32 : o.batch_size);
+  const int cnt = o.shard_count > 1 ? o.shard_count : 1;
+  std::vector<int> cur;
+  for (int i = 0; i < (int)p.offsets.size(); i++) {
+    if (i % cnt != (cnt > 1 ? o.shard_index : 0)) continue;
+    if (length - p.offsets[i] >= p.seg) {
+      cur.push_back(i);
+      if ((int)cur.size() >= bs) {
+        p.full_batches.push_back(cur);
+        cur.clear();
+      }
+    } else {
+      p.tails.push_back(i);
+    }
+  }
+  if (!cur.empty()) p.full_batches.push_back(cur);
+  return p;
+}
+
+// triangular transition weights (apply.c:116-133), float32 math
+static std::vector<float> ola_weight(int n, float power) {
+  std::vector<float> w(n);
+  const int half = n / 2;
+  float mx = 0.f;
+  for (int i = 0; i < half; i++) w[i] = (float)(i + 1);
+  for (int i = half; i < n; i++) w[i] = (float)(n - i);
+  for (float v : w) mx = v > mx ? v : mx;
+  for (float &v : w) v = powf(v / mx, power);
+  return w;
+}
+
+// split pass of dc_apply_model (apply.c:223-306) on mix [B, C, length]; accumulates this
+// shard's weighted segments into out [B, S, C, length] (zeroed here) and multiplies by the
+// inverse of the full weight sum, so the shards' outputs sum to the complete result.
+static int apply_split(DcbModel *m, const float *mix, int B, int length, float *out,
+                       const DcbApplyOpts &o) {
+  const Cfg &c = m->cfg;
+  const int C = c.audio_channels, S = c.n_sources, Lv = c.valid_length;
+  Plan p = make_plan(c, length, o);
+  if (p.stride <= 0) {
+    fail("apply: invalid overlap %f", (double)o.overlap);
+    return -1;
+  }
+  std::vector<float> w = ola_weight(p.seg, o.transition_power);
+  std::vector<double> sumw((size_t)length, 0.0);
+  for (size_t i = 0; i < p.offsets.size(); i++) {
+    const int off = p.offsets[i];
+    const int n = length - off < p.seg ? length - off : p.seg;
+    for (int t = 0; t < n; t++) sumw[off + t] += w[t];
+  }
+  float *wdev = dalloc(p.seg);
+  DCB_CUDA(cudaMemcpyAsync(wdev, w.data(), p.seg * 4, cudaMemcpyHostToDevice, stream()));
+  const int64_t rows = (int64_t)B * S * C;
+  DCB_CUDA(cudaMemsetAsync(out, 0, (size_t)rows * length * 4, stream()));
+  Stage none;
+  for (const auto &bt : p.full_batches) {
+    const int nbt = (int)bt.size();
+    float *flat = dalloc((size_t)nbt * B * C * Lv);
+    for (int k = 0; k < nbt; k++) {
+      const int off = p.offsets[bt[k]];
+      const int64_t start = off - (Lv - p.seg) / 2;
+      k_chunk<<<grid_for((int64_t)B * C * Lv, 256), 256, 0, stream()>>>(
+          mix, flat + (size_t)k * B * C * Lv, B, C, length, start, Lv, (int64_t)C * Lv);
+      DCB_LAUNCHED();
+    }
+    float *y = dalloc((size_t)nbt * B * S * C * Lv);
+    if (forward(m, flat, nbt * B, Lv, y, none) < 0) return -1;
+    dfree(flat);
+    const int y0 = (Lv - p.seg) / 2;  // center_trim(y, seg)
+    for (int k = 0; k < nbt; k++) {
+      const int off = p.offsets[bt[k]];
+      k_accumulate<<<grid_for(rows * p.seg, 256), 256, 0, stream()>>>(
+          out, y + (size_t)k * rows * Lv, wdev, (int)rows, length, Lv, off, y0, p.seg);
+      DCB_LAUNCHED();
+    }
+    dfree(y);
+  }
+  for (int i : p.tails) {
+    const int off = p.offsets[i];
+    const int this_len = length - off;
+    const int valid = this_len < Lv ? Lv : this_len;
+    if (valid > Lv) {
+      fail("apply: tail segment longer than the training length");
+      return -1;
+    }
+    float *ch = dalloc((size_t)B * C * valid);
+    const int64_t start = off - (valid - this_len) / 2;
+    k_chunk<<<grid_for((int64_t)B * C * valid, 256), 256, 0, stream()>>>(
+        mix, ch, B, C, length, start, valid, (int64_t)C * valid);
+    DCB_LAUNCHED();
+    float *y = dalloc((size_t)B * S * C * valid);
+    if (forward(m, ch, B, valid, y, none) < 0) return -1;
+    dfree(ch);
+    const int y0 = (valid - this_len) / 2;
+    k_accumulate<<<grid_for(rows * this_len, 256), 256, 0, stream()>>>(
+        out, y, wdev, (int)rows, length, valid, off, y0, this_len);
+    DCB_LAUNCHED();
+    dfree(y);
+  }
+  std::vector<float> inv((size_t)length);
+  for (int t = 0; t < length; t++) inv[t] = sumw[t] > 0.0 ? (float)(1.0 / sumw[t]) : 0.0f;
+  float *invd = dalloc(length);
+  DCB_CUDA(cudaMemcpyAsync(invd, inv.data(), (size_t)length * 4, cudaMemcpyHostToDevice, stream()));
+  k_scale_time<<<grid_for(rows * length, 256), 256, 0, stream()>>>(out, invd, rows, length);
+  DCB_LAUNCHED();
+  // host vectors must outlive the async copies
+  DCB_CUDA(cudaStreamSynchronize(stream()));
+  dfree(invd);
+  dfree(wdev);
+  return 0;
+}
+
+}  // namespace dcb
+
+using namespace dcb;
+
+extern "C" {
+
+int dcb_forward(DcbModel *m, const float *mix, int B, int T, float *out, DcbStageFn fn,
+                void *user) {
+  if (!m || B <= 0 || T <= 0) return -1;
+  Stage sg;
+  sg.fn = fn;
+  sg.user = user;
+  const int r = forward(m, mix, B, T, out, sg);
+  return failed() ? -1 : r;
+}
+
+int dcb_stage_encoder(DcbModel *m, int branch, int idx, const float *x, int B, int C, int H,
+                      int W, float *y, int *out_shape) {
+  if (!m || idx < 0 || idx >= m->depth) return -1;
+  if (branch == 0) {
+    const EncW &E = m->enc[idx];
+    if (C != E.Cin) return -1;
+    const int S = m->cfg.stride, K = m->cfg.kernel_size;
+    const int Ho = (H + 2 * (K / 4) - K) / S + 1;
+    out_shape[0] = B;
+    out_shape[1] = E.Cout;
+    out_shape[2] = Ho;
+    out_shape[3] = W;
+    if (!y) return 0;
+    int ho;
+    float *z = enc_freq(m, idx, x, B, H, W, &ho);
+    DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * E.Cout * Ho * W * 4, cudaMemcpyDeviceToDevice,
+                             stream()));
+    dfree(z);
+  } else {
+    const EncW &E = m->tenc[idx];
+    if (C != E.Cin) return -1;
+    const int S = m->cfg.stride, L = W;
+    const int Lo = (L + S - 1) / S;
+    out_shape[0] = B;
+    out_shape[1] = E.Cout;
+    out_shape[2] = Lo;
+    out_shape[3] = 0;
+    if (!y) return 0;
+    int lo;
+    float *z = enc_time(m, idx, x, B, L, &lo);
+    DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * E.Cout * Lo * 4, cudaMemcpyDeviceToDevice,
+                             stream()));
+    dfree(z);
+  }
+  DCB_CUDA(cudaStreamSynchronize(stream()));
+  return failed() ? -1 : 0;
+}
+
+int dcb_stage_decoder(DcbModel *m, int branch, int idx, const float *x, const float *skip,
+                      int B, int C, int H, int W, int length, float *y, int *out_shape) {
+  if (!m || idx < 0 || idx >= m->depth) return -1;
+  const bool last = idx == m->depth - 1;
+  const int S = m->cfg.stride, K = m->cfg.kernel_size;
+  if (branch == 0) {
+    const DecW &D = m->dec[idx];
+    if (C != D.Cin) return -1;
+    const int Ho = (H - 1) * S + K - 2 * (K / 4);
+    out_shape[0] = B;
+    out_shape[1] = D.Cout;
+    out_shape[2] = Ho;
+    out_shape[3] = W;
+    if (!y) return 0;
+    float *z = dec_freq(m, idx, x, skip, B, H, W, last);
+    DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * D.Cout * Ho * W * 4, cudaMemcpyDeviceToDevice,
+                             stream()));
+    dfree(z);
+  } else {
+    const DecW &D = m->tdec[idx];
+    if (C != D.Cin) return -1;
+    out_shape[0] = B;
+    out_shape[1] = D.Cout;
+    out_shape[2] = length;
+    out_shape[3] = 0;
+    if (!y) return 0;
+    float *z = dec_time(m, idx, x, skip, B, W, length, last);
+    DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * D.Cout * length * 4, cudaMemcpyDeviceToDevice,
+                             stream()));
+    dfree(z);
+  }
+  DCB_CUDA(cudaStreamSynchronize(stream()));
+  return failed() ? -1 : 0;
+}
+
+int dcb_stage_transformer(DcbModel *m, float *x, float *xt, int B, int C, int Fr, int T1,
+                          int T2) {
+  if (!m || C != m->D) return -1;
+  crosstransformer(m, x, xt, B, Fr, T1, T2);
+  DCB_CUDA(cudaStreamSynchronize(stream()));
+  return failed() ? -1 : 0;
+}
+
+void dcb_apply_defaults(DcbApplyOpts *o) {
+  o->shifts = 1;
+  o->split = 1;
+  o->overlap = 0.25f;
+  o->transition_power = 1.0f;
+  o->batch_size = 8;
+  o->seed = 1;
+  o->use_seed = 0;
+  o->shard_index = 0;
+  o->shard_count = 1;
+}
+
+int dcb_apply_plan(DcbModel *m, int T, const DcbApplyOpts *o, int *n_forwards, int *n_batched) {
+  if (!m || !o) return -1;
+  int len = T;
+  if (o->shifts > 0) len = T + (int)(0.5f * (float)m->cfg.samplerate);  // upper bound
+  Plan p = make_plan(m->cfg, len, *o);
+  int fw = 0;
+  for (auto &b : p.full_batches) fw += (int)b.size();
+  if (n_forwards) *n_forwards = (fw + (int)p.tails.size()) * (o->shifts > 0 ? o->shifts : 1);
+  if (n_batched) *n_batched = ((int)p.full_batches.size() + (int)p.tails.size()) *
+                              (o->shifts > 0 ? o->shifts : 1);
+  return 0;
+}
+
+// dc_apply_model (apply.c:179-306): shifts wrap the split pass
+int dcb_apply(DcbModel *m, const float *mix, int B, int T, float *out, const DcbApplyOpts *o) {
+  if (!m || !o || B <= 0 || T <= 0) return -1;
+  const Cfg &c = m->cfg;
+  const int C = c.audio_channels, S = c.n_sources;
+  const int64_t rows = (int64_t)B * S * C;
+  if (!o->split) {
+    fail("apply: split=0 is not supported by this engine");
+    return -1;
+  }
+  if (o->shifts <= 0) return apply_split(m, mix, B, T, out, *o);
+  const int max_shift = (int)(0.5f * (float)c.samplerate);
+  const int Lp = T + 2 * max_shift;
+  float *padded = dalloc((size_t)B * C * Lp);
+  k_chunk<<<grid_for((int64_t)B * C * Lp, 256), 256, 0, stream()>>>(mix, padded, B, C, T,
+                                                                    -max_shift, Lp, (int64_t)C * Lp);
+  DCB_LAUNCHED();
+  Mt rng;
+  rng.seed(o->use_seed ? (uint64_t)o->seed : 1u);
+  DCB_CUDA(cudaMemsetAsync(out, 0, (size_t)rows * T * 4, stream()));
+  for (int i = 0; i < o->shifts; i++) {
+    const int off = rng.randint(0, max_shift);
+    const int Ls = T + max_shift - off;
+    float *shifted = dalloc((size_t)B * C * Ls);
+    k_chunk<<<grid_for((int64_t)B * C * Ls, 256), 256, 0, stream()>>>(padded, shifted, B, C, Lp,
+                                                                      off, Ls, (int64_t)C * Ls);
+    DCB_LAUNCHED();
+    float *part = dalloc((size_t)rows * Ls);
+    DcbApplyOpts inner = *o;
+    inner.shifts = 0;
+    if (apply_split(m, shifted, B, Ls, part, inner) < 0) return -1;
+    dfree(shifted);
+    // out += part[..., max_shift - off :] / shifts
+    float *wone = dalloc(T);
+    k_fill<<<grid_for(T, 256), 256, 0, stream()>>>(wone, T, 1.0f / (float)o->shifts);
+    DCB_LAUNCHED();
+    k_accumulate<<<grid_for(rows * T, 256), 256, 0, stream()>>>(out, part, wone, (int)rows, T, Ls,
+                                                               0, max_shift - off, T);
+    DCB_LAUNCHED();
+    dfree(wone);
+    dfree(part);
+  }
+  dfree(padded);
+  DCB_CUDA(cudaStreamSynchronize(stream()));
+  return failed() ? -1 : 0;
+}
+
+}  // extern "C"

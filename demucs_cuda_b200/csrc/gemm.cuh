@@ -1,0 +1,80 @@
+// Tensor-core GEMM family (tcgen05 / TMEM / TMA) shared by dk_gemm_half, the
+// implicit-GEMM convolutions, the stride-phase transposed convolutions and the transformer
+// linears.  Internal C++ interface; the C ABI wrappers are in gemm.cu.
+#pragma once
+
+#include "common.cuh"
+
+namespace dcb {
+
+// Implicit im2col over x viewed as images [n][c][h][w] (w contiguous).  Image n is
+// n1 * N2 + n2 with element offset n1 * sN1 + n2 * sN2, so a [B, C, Fr, T] tensor can be
+// read as B*Fr images [C][T] without the transposes of layers.c:3-20.  The GEMM row is
+// the output position p = (n, ho, wo) and the reduction index k = (kh*KW + kw)*C + c,
+// matching the packed weight layout (weights.c:298-311, backend.h:108-109).
+struct Gather {
+  const float *x;
+  const float *x2;  // optional second input added element-wise before rounding (decoder skip)
+  int N2;
+  int64_t sN1, sN2, sC, sH;
+  int C, H, W;
+  int KH, KW, SH, SW, PH, PW, DH, DW;
+  int Ho, Wo;
+  int K;  // KH*KW*C
+};
+
+enum EpiMode : int {
+  EPI_GEMM = 0,    // C = alpha acc + beta C (dk_gemm_half); swapped -> transposed store
+  EPI_CONV = 1,    // y[n][o][ho][wo] = act(acc + bias); GLU pairs interleaved columns
+  EPI_CONVTR = 2,  // stride-phase scatter: column (o, r) -> output t = S q + r - crop
+  EPI_ROWS_F32 = 3,  // out[m][n] = acc + bias (+ res[m][n] + gamma[n] * (...))
+  EPI_ROWS_F16 = 4,  // out16[m][n] = fp16(act(acc + bias))
+  EPI_HEADS = 5,     // fp16 head-split sections [B][H][T][hd] / [B][H][hd][Tp]
+};
+
+struct Epi {
+  int mode = EPI_GEMM;
+  const float *bias = nullptr;
+  int act = 0;  // 0 none, 1 gelu, 2 glu
+  // EPI_GEMM
+  float *C = nullptr;
+  int64_t ldc = 0, strideC = 0;
+  float alpha = 1.f, beta = 0.f;
+  int swapped = 0;
+  // EPI_CONV / EPI_CONVTR output view: (n, o, h, w) -> n1*oN1 + n2*oN2 + o*oC + h*oH + w
+  float *y = nullptr;
+  int oN2 = 1;
+  int64_t oN1 = 0, oN2s = 0, oC = 0, oH = 0;
+  int O = 0;          // output channels (after GLU halving)
+  int Ho = 1, Wo = 1;  // GEMM row -> (n, ho, wo)
+  int glu_half = 0;    // columns per half inside one N tile (GLU)
+  const float *res = nullptr;  // EPI_CONV: y = res + scale[o] * value (DConv residual)
+  const float *scale = nullptr;
+  // EPI_CONVTR
+  int stride = 4, crop = 0, out_len = 0, axis_h = 1;
+  // EPI_ROWS_*
+  void *out = nullptr;
+  int64_t ldo = 0, ldr = 0;
+  const float *gamma = nullptr;
+  // EPI_HEADS
+  int T = 0, heads = 0, hd = 0, sec_cols = 0;
+  int64_t Tp = 0;
+  uint16_t *sec_ptr[3] = {nullptr, nullptr, nullptr};
+  int sec_layout[3] = {0, 0, 0};
+};
+
+// A operand source for the row-major (TMA) path
+struct RowsA {
+  const uint16_t *p;
+  int64_t ld, stride;  // elements; stride 0 = shared across the batch
+};
+
+// C = A . B^T with A [M][K] fp16 rows (TMA), B [N][K] fp16 rows (TMA)
+void gemm_rows(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch, const Epi &e);
+// C = gather(x) . B^T with B [N][K] fp16 rows (TMA); M = images * Ho * Wo
+void gemm_gather(const Gather &g, int64_t M, const uint16_t *w, int64_t N, int64_t ldw,
+                 const Epi &e, int bn_hint = 0);
+// N tile used by gemm_gather for a given column count (the GLU interleave depends on it)
+int gather_bn(int64_t M, int64_t N, bool glu);
+
+}  // namespace dcb

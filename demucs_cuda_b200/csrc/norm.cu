@@ -1,0 +1,289 @@
+// Normalisation part of the backend.h ABI (backend.h:72-89).
+//
+// Row statistics follow the reference's two-pass definition (mean, then the mean squared
+// deviation, backend_cpu.c:227-243) with the row split into chunks: each CTA computes its
+// chunk's mean and centred sum of squares from registers, and a second kernel merges the
+// chunks with Chan's parallel formula in double (norm.cu:42-107 does the same merge).
+#include "common.cuh"
+
+namespace dcb {
+
+constexpr int kStatChunk = 8192;  // elements per CTA
+constexpr int kStatThreads = 256;
+
+template <typename T>
+static __device__ __forceinline__ T block_sum(T v, T *sh) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  T r = 0;
+  int nw = blockDim.x >> 5;
+  for (int i = 0; i < nw; i++) r += sh[i];
+  return r;
+}
+
+// partial[row][chunk] = {count, mean, M2}
+__global__ void __launch_bounds__(kStatThreads)
+    k_chunk_stats(const float *__restrict__ x, int64_t L, int nchunks, double *partial) {
+  __shared__ double sh[kStatThreads / 32];
+  int64_t row = blockIdx.y;
+  int chunk = blockIdx.x;
+  int64_t c0 = (int64_t)chunk * kStatChunk;
+  int64_t n = L - c0 < kStatChunk ? L - c0 : kStatChunk;
+  const float *p = x + row * L + c0;
+  constexpr int PER = kStatChunk / kStatThreads;
+  float v[PER];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    int64_t j = (int64_t)i * kStatThreads + threadIdx.x;
+    v[i] = j < n ? p[j] : 0.f;
+    s += v[i];
+  }
+  double tot = block_sum<double>((double)s, sh);
+  double mean = tot / (double)n;
+  float mf = (float)mean;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; i++) {
+    int64_t j = (int64_t)i * kStatThreads + threadIdx.x;
+    if (j < n) {
+      float d = v[i] - mf;
+      q += d * d;
+    }
+  }
+  double m2 = block_sum<double>((double)q, sh);
+  // correct the centring for the float rounding of the mean: sum (x - mf)^2 =
+  // M2 + n (mean - mf)^2
+  double dm = mean - (double)mf;
+  m2 -= (double)n * dm * dm;
+  if (threadIdx.x == 0) {
+    double *o = partial + (row * nchunks + chunk) * 3;
+    o[0] = (double)n;
+    o[1] = mean;
+    o[2] = m2 > 0 ? m2 : 0.0;
+  }
+}
+
+__global__ void k_combine_stats(const double *partial, int64_t rows, int nchunks, float *mean,
+                                float *var) {
+  int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  const double *p = partial + r * nchunks * 3;
+  double n = p[0], m = p[1], m2 = p[2];
+  for (int c = 1; c < nchunks; c++) {
+    double nb = p[c * 3], mb = p[c * 3 + 1], m2b = p[c * 3 + 2];
+    double nt = n + nb, d = mb - m;
+    m += d * nb / nt;
+    m2 += m2b + d * d * n * nb / nt;
+    n = nt;
+  }
+  mean[r] = (float)m;
+  var[r] = (float)(m2 / n);
+}
+
+static double *g_stat_scratch = nullptr;
+static size_t g_stat_cap = 0;
+
+void row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var) {
+  if (rows <= 0 || L <= 0) return;
+  int nchunks = (int)((L + kStatChunk - 1) / kStatChunk);
+  size_t need = (size_t)rows * nchunks * 3 * sizeof(double);
+  if (need > g_stat_cap) {
+    if (g_stat_scratch) {
+      DCB_CUDA(cudaStreamSynchronize(stream()));
+      DCB_CUDA(cudaFree(g_stat_scratch));
+    }
+    size_t cap = need < ((size_t)1 << 20) ? ((size_t)1 << 20) : need * 2;
+    DCB_CUDA(cudaMalloc(&g_stat_scratch, cap));
+    g_stat_cap = cap;
+  }
+  dim3 grid(nchunks, (unsigned)rows);
+  k_chunk_stats<<<grid, kStatThreads, 0, stream()>>>(x, L, nchunks, g_stat_scratch);
+  DCB_LAUNCHED();
+  k_combine_stats<<<grid_for(rows, 128, 1 << 30), 128, 0, stream()>>>(g_stat_scratch, rows,
+                                                                     nchunks, mean, var);
+  DCB_LAUNCHED();
+}
+
+__global__ void k_groupnorm(const float *__restrict__ x, float *__restrict__ y,
+                            const float *__restrict__ mean, const float *__restrict__ var,
+                            const float *__restrict__ w, const float *__restrict__ b, int64_t B,
+                            int64_t C, int64_t S, int64_t G, float eps, int act) {
+  int64_t cpg = C / G;
+  if (act == 2) {
+    int64_t H = C / 2, n = B * H * S;
+    DCB_GRID_STRIDE(i, n) {
+      int64_t s = i % S, t = i / S, c = t % H, bi = t / H;
+      int64_t ga = c / cpg, gb = (c + H) / cpg;
+      float ra = 1.0f / sqrtf(var[bi * G + ga] + eps);
+      float rb = 1.0f / sqrtf(var[bi * G + gb] + eps);
+      float xa = x[(bi * C + c) * S + s], xb = x[(bi * C + c + H) * S + s];
+      float na = (xa - mean[bi * G + ga]) * ra * w[c] + b[c];
+      float nb = (xb - mean[bi * G + gb]) * rb * w[c + H] + b[c + H];
+      y[i] = na * sigmoid_f(nb);
+    }
+    return;
+  }
+  int64_t n = B * C * S;
+  DCB_GRID_STRIDE(i, n) {
+    int64_t t = i / S, c = t % C, bi = t / C, g = c / cpg;
+    float rs = 1.0f / sqrtf(var[bi * G + g] + eps);
+    float v = (x[i] - mean[bi * G + g]) * rs * w[c] + b[c];
+    y[i] = act == 1 ? gelu_f(v) : v;
+  }
+}
+
+__global__ void k_norm_last(const float *__restrict__ x, float *__restrict__ y,
+                            const float *__restrict__ mean, const float *__restrict__ var,
+                            const float *__restrict__ w, const float *__restrict__ b,
+                            int64_t rows, int64_t L, int64_t C, float eps) {
+  int64_t n = rows * L;
+  DCB_GRID_STRIDE(i, n) {
+    int64_t r = i / L, c = (i - r * L) % C;
+    float v = (x[i] - mean[r]) * (1.0f / sqrtf(var[r] + eps));
+    if (w) v *= w[c];
+    if (b) v += b[c];
+    y[i] = v;
+  }
+}
+
+__global__ void k_affine_rows(const float *__restrict__ x, float *__restrict__ y,
+                              const float *__restrict__ mean, const float *__restrict__ var,
+                              int64_t rows, int64_t L, float eps, int denorm) {
+  int64_t n = rows * L;
+  DCB_GRID_STRIDE(i, n) {
+    int64_t r = i / L;
+    float sd = sqrtf(var[r]) + eps, m = mean[r], v = x[i];
+    y[i] = denorm ? v * sd + m : (v - m) / sd;
+  }
+}
+
+// LayerNorm, one warp per row, row kept in registers (C <= 32 * 32 * 4 = 4096 floats per
+// warp in float4 chunks; larger rows fall back to row_stats + apply).  Output either fp32
+// or fp16 (the latter is the GEMM A operand of the next linear, rounded exactly as
+// dk_to_half_rows would round the fp32 result).
+template <bool HALF_OUT>
+__global__ void k_layernorm(const float *__restrict__ x, void *__restrict__ yv,
+                            const float *__restrict__ w, const float *__restrict__ b,
+                            int64_t rows, int C, float eps, int ld_out) {
+  int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float *p = x + row * C;
+  constexpr int MAXV = 32;
+  float v[MAXV];
+  int nv = 0;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; i++) {
+    int c = i * 32 + lane;
+    v[i] = c < C ? p[c] : 0.f;
+    s += v[i];
+    nv = i;
+  }
+  (void)nv;
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  double mean_d = (double)s / (double)C;
+  float m = (float)mean_d;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; i++) {
+    int c = i * 32 + lane;
+    if (c < C) {
+      float d = v[i] - m;
+      q += d * d;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  double dm = mean_d - (double)m;
+  double m2 = (double)q - (double)C * dm * dm;
+  float var = (float)((m2 > 0 ? m2 : 0.0) / (double)C);
+  float rs = 1.0f / sqrtf(var + eps);
+#pragma unroll
+  for (int i = 0; i < MAXV; i++) {
+    int c = i * 32 + lane;
+    if (c < C) {
+      float n = (v[i] - m) * rs;
+      if (w) n *= w[c];
+      if (b) n += b[c];
+      if (HALF_OUT) {
+        ((uint16_t *)yv)[row * ld_out + c] = f2h_bits(n);
+      } else {
+        ((float *)yv)[row * ld_out + c] = n;
+      }
+    } else if (HALF_OUT && c < ld_out) {
+      ((uint16_t *)yv)[row * ld_out + c] = 0;
+    }
+  }
+}
+
+void layernorm(const float *x, void *y, const float *w, const float *b, int64_t rows, int C,
+               float eps, bool half_out, int ld_out) {
+  if (rows <= 0) return;
+  if (C <= 1024) {
+    unsigned blocks = (unsigned)((rows + 3) / 4);
+    if (half_out) {
+      k_layernorm<true><<<blocks, 128, 0, stream()>>>(x, y, w, b, rows, C, eps, ld_out);
+    } else {
+      k_layernorm<false><<<blocks, 128, 0, stream()>>>(x, y, w, b, rows, C, eps, ld_out);
+    }
+    DCB_LAUNCHED();
+    return;
+  }
+  // long rows: generic two kernels (fp32 output only)
+  DCB_REQUIRE(!half_out, "layernorm: fp16 output needs C <= 1024");
+  float *st = nullptr;
+  DCB_CUDA(cudaMallocAsync(&st, (size_t)rows * 2 * sizeof(float), stream()));
+  row_stats(x, rows, C, st, st + rows);
+  k_norm_last<<<grid_for(rows * C, 256), 256, 0, stream()>>>(x, (float *)y, st, st + rows, w,
+                                                             b, rows, C, C, eps);
+  DCB_LAUNCHED();
+  DCB_CUDA(cudaFreeAsync(st, stream()));
+}
+
+}  // namespace dcb
+
+using namespace dcb;
+
+extern "C" {
+
+void dk_row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var) {
+  row_stats(x, rows, L, mean, var);
+}
+
+void dk_groupnorm_apply(const float *x, float *y, const float *mean, const float *var,
+                        const float *w, const float *b, int64_t B, int64_t C, int64_t S,
+                        int64_t G, float eps, int act) {
+  int64_t n = B * (act == 2 ? C / 2 : C) * S;
+  if (n <= 0) return;
+  k_groupnorm<<<grid_for(n, 256), 256, 0, stream()>>>(x, y, mean, var, w, b, B, C, S, G, eps,
+                                                      act);
+  DCB_LAUNCHED();
+}
+
+void dk_norm_apply_last(const float *x, float *y, const float *mean, const float *var,
+                        const float *w, const float *b, int64_t rows, int64_t L, int64_t C,
+                        float eps) {
+  if (rows * L <= 0) return;
+  k_norm_last<<<grid_for(rows * L, 256), 256, 0, stream()>>>(x, y, mean, var, w, b, rows, L, C,
+                                                             eps);
+  DCB_LAUNCHED();
+}
+
+void dk_affine_rows(const float *x, float *y, const float *mean, const float *var,
+                    int64_t rows, int64_t L, float eps, int denorm) {
+  if (rows * L <= 0) return;
+  k_affine_rows<<<grid_for(rows * L, 256), 256, 0, stream()>>>(x, y, mean, var, rows, L, eps,
+                                                               denorm);
+  DCB_LAUNCHED();
+}
+
+void dk_layernorm(const float *x, float *y, const float *w, const float *b, int64_t rows,
+                  int64_t C, float eps) {
+  layernorm(x, y, w, b, rows, (int)C, eps, false, (int)C);
+}
+
+}  // extern "C"

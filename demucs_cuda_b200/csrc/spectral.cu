@@ -1,0 +1,183 @@
+// Spectral part of the backend.h ABI (backend.h:133-144): Hann-windowed STFT, inverse
+// frames and overlap-add.  One CTA transforms one frame in shared memory (iterative radix-2
+// decimation in time over bit-reversed input, the same butterfly order as the reference's
+// fft_radix2, backend_cpu.c:549-567); twiddles exp(-2 pi i k / n) are evaluated in double
+// on the host and stored as float (fft.cu:9-63 does the same).
+#include <math.h>
+
+#include <vector>
+
+#include "common.cuh"
+
+namespace dcb {
+
+static float2 *g_tw = nullptr;
+static int g_tw_n = 0;
+
+const float2 *twiddles(int n) {
+  if (g_tw_n == n) return g_tw;
+  if (n <= 1 || (n & (n - 1)) || n > 8192) {
+    fail("fft size %d must be a power of two <= 8192", n);
+    return nullptr;
+  }
+  std::vector<float2> h(n / 2);
+  for (int k = 0; k < n / 2; k++) {
+    double a = -2.0 * 3.14159265358979323846 * (double)k / (double)n;
+    h[k] = make_float2((float)cos(a), (float)sin(a));
+  }
+  if (g_tw) {
+    DCB_CUDA(cudaStreamSynchronize(stream()));
+    DCB_CUDA(cudaFree(g_tw));
+  }
+  DCB_CUDA(cudaMalloc(&g_tw, (n / 2) * sizeof(float2)));
+  DCB_CUDA(cudaMemcpy(g_tw, h.data(), (n / 2) * sizeof(float2), cudaMemcpyHostToDevice));
+  g_tw_n = n;
+  return g_tw;
+}
+
+static __device__ __forceinline__ int bitrev(int i, int bits) {
+  return (int)(__brev((unsigned)i) >> (32 - bits));
+}
+
+// in-place forward DFT of bit-reversed data in shared memory
+static __device__ void fft_smem(float2 *buf, int n, const float2 *__restrict__ tw) {
+  for (int half = 1; half < n; half <<= 1) {
+    __syncthreads();
+    int step = n / (2 * half);
+    for (int j = threadIdx.x; j < n / 2; j += blockDim.x) {
+      int pos = j & (half - 1);
+      int i0 = (j / half) * 2 * half + pos, i1 = i0 + half;
+      float2 w = tw[pos * step];
+      float2 a = buf[i0], b = buf[i1];
+      float tr = w.x * b.x - w.y * b.y, ti = w.x * b.y + w.y * b.x;
+      buf[i1] = make_float2(a.x - tr, a.y - ti);
+      buf[i0] = make_float2(a.x + tr, a.y + ti);
+    }
+  }
+  __syncthreads();
+}
+
+__global__ void k_stft(const float *__restrict__ sig, float *__restrict__ out, int64_t L,
+                       int n, int bits, int hop, int frame0, int nframes, int nbins,
+                       const float *__restrict__ window, const float2 *__restrict__ tw) {
+  extern __shared__ float2 buf[];
+  int f = blockIdx.x;
+  int64_t r = blockIdx.y;
+  int64_t start = (int64_t)(frame0 + f) * hop;
+  const float *s = sig + r * L;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    int64_t t = start + i;
+    float v = t < L ? s[t] * window[i] : 0.f;
+    buf[bitrev(i, bits)] = make_float2(v, 0.f);
+  }
+  fft_smem(buf, n, tw);
+  float *ore = out + r * 2 * (int64_t)nbins * nframes;
+  float *oim = ore + (int64_t)nbins * nframes;
+  for (int k = threadIdx.x; k < nbins; k += blockDim.x) {
+    ore[(int64_t)k * nframes + f] = buf[k].x;
+    oim[(int64_t)k * nframes + f] = buf[k].y;
+  }
+}
+
+__global__ void k_istft_frames(const float *__restrict__ spec, float *__restrict__ frames,
+                               int nbins, int nframes, int pad_frames, int n, int bits,
+                               const float *__restrict__ window,
+                               const float2 *__restrict__ tw) {
+  extern __shared__ float2 buf[];
+  int NF = nframes + 2 * pad_frames;
+  int f = blockIdx.x;
+  int64_t r = blockIdx.y;
+  float *dst = frames + (r * NF + f) * (int64_t)n;
+  int fi = f - pad_frames;
+  if (fi < 0 || fi >= nframes) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = 0.f;
+    return;
+  }
+  const float *sre = spec + r * 2 * (int64_t)nbins * nframes;
+  const float *sim = sre + (int64_t)nbins * nframes;
+  for (int k = threadIdx.x; k < n; k += blockDim.x) {
+    int kk = k <= n / 2 ? k : n - k;
+    float xr = 0.f, xi = 0.f;
+    if (kk < nbins) {
+      xr = sre[(int64_t)kk * nframes + fi];
+      xi = sim[(int64_t)kk * nframes + fi];
+    }
+    if (k > n / 2) xi = -xi;
+    buf[bitrev(k, bits)] = make_float2(xr, -xi);
+  }
+  fft_smem(buf, n, tw);
+  float inv_n = 1.0f / (float)n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = buf[i].x * inv_n * window[i];
+}
+
+__global__ void k_ola(const float *__restrict__ frames, float *__restrict__ out, int64_t R,
+                      int nframes, int n, int hop, const float *__restrict__ window,
+                      int64_t start, int64_t length) {
+  int64_t out_len = (int64_t)hop * (nframes - 1) + n, total = R * length;
+  DCB_GRID_STRIDE(e, total) {
+    int64_t r = e / length, t = e - r * length, idx = start + t;
+    float num = 0.f, den = 0.f;
+    if (idx < out_len) {
+      int64_t f_hi = idx / hop;
+      if (f_hi > nframes - 1) f_hi = nframes - 1;
+      int64_t f_lo = idx - n + 1 <= 0 ? 0 : (idx - n + hop) / hop;
+      for (int64_t f = f_lo; f <= f_hi; f++) {
+        int64_t i = idx - f * hop;
+        if (i < 0 || i >= n) continue;
+        num += frames[(r * nframes + f) * n + i];
+        den += window[i] * window[i];
+      }
+    }
+    out[e] = den > 0.f ? num / den : 0.f;
+  }
+}
+
+static int log2i(int n) {
+  int b = 0;
+  while ((1 << b) < n) b++;
+  return b;
+}
+
+}  // namespace dcb
+
+using namespace dcb;
+
+extern "C" {
+
+void dk_stft(const float *sig, float *out, int64_t R, int64_t L, int n_fft, int hop,
+             int frame0, int nframes, int nbins, const float *window) {
+  if (R <= 0 || nframes <= 0) return;
+  const float2 *tw = twiddles(n_fft);
+  if (!tw) return;
+  DCB_REQUIRE(R <= 65535, "stft: %lld rows", (long long)R);
+  dim3 grid((unsigned)nframes, (unsigned)R);
+  size_t sm = (size_t)n_fft * sizeof(float2);
+  if (sm > 48 * 1024) DCB_CUDA(cudaFuncSetAttribute(k_stft, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  k_stft<<<grid, 512, sm, stream()>>>(sig, out, L, n_fft, log2i(n_fft), hop, frame0, nframes,
+                                      nbins, window, tw);
+  DCB_LAUNCHED();
+}
+
+void dk_istft_frames(const float *spec, float *frames, int64_t R, int nbins, int nframes,
+                     int pad_frames, int n_fft, const float *window) {
+  if (R <= 0) return;
+  const float2 *tw = twiddles(n_fft);
+  if (!tw) return;
+  DCB_REQUIRE(R <= 65535, "istft: %lld rows", (long long)R);
+  dim3 grid((unsigned)(nframes + 2 * pad_frames), (unsigned)R);
+  size_t sm = (size_t)n_fft * sizeof(float2);
+  if (sm > 48 * 1024) DCB_CUDA(cudaFuncSetAttribute(k_istft_frames, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  k_istft_frames<<<grid, 512, sm, stream()>>>(spec, frames, nbins, nframes, pad_frames, n_fft,
+                                              log2i(n_fft), window, tw);
+  DCB_LAUNCHED();
+}
+
+void dk_ola(const float *frames, float *out, int64_t R, int nframes, int n_fft, int hop,
+            const float *window, int64_t start, int64_t length) {
+  if (R * length <= 0) return;
+  k_ola<<<grid_for(R * length, 256), 256, 0, stream()>>>(frames, out, R, nframes, n_fft, hop,
+                                                         window, start, length);
+  DCB_LAUNCHED();
+}
+
+}  // extern "C"

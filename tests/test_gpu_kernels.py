@@ -1,0 +1,310 @@
+"""Kernel-level parity of the sm_100a backend against the reference's own CPU backend.
+
+Each case runs the reference implementation (oracle/_ref: backend_cpu.c + ops.c compiled
+from the reference sources, same fp16 operand rounding) and this library's kernel on the
+same seeded inputs.  Shapes follow the reference's tests/test_kernels.c (odd sizes that
+hit K padding and partial tiles) plus the htdemucs_6s GEMM shapes at reduced position
+counts.  Tolerances: the GEMM family agrees to fp32 accumulation order (rel L2 <= 2e-5,
+far inside test_kernels.c's 3e-3), norms 1e-5, spectral 1e-5, attention 2e-3 (the flash
+kernel rounds unnormalised probabilities to fp16, the reference normalised ones).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def dcb(torch_cuda):
+    import demucs_cuda_b200 as d
+    return d
+
+
+@pytest.fixture(scope="module")
+def ref():
+    from oracle import ref as r
+    return r
+
+
+def _dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr())
+
+
+def _half_np(a):
+    return np.asarray(a, np.float32).astype(np.float16)
+
+
+@pytest.mark.parametrize("simt", [0, 1])
+@pytest.mark.parametrize("M,N,K,batch,shareA,shareB", [
+    (256, 200, 72, 1, False, False),     # normal orientation, partial N tile, K < 2 blocks
+    (48, 1000, 32, 1, False, False),     # small M -> swapped orientation (conv weights as A)
+    (96, 5000, 384, 2, True, False),     # conv_core call: shared weights, batched positions
+    (300, 300, 48, 4, False, False),     # attention-like batched score GEMM
+    (384, 2688, 1536, 1, False, False),  # transformer linear2 / enc3 shapes
+    (37, 29, 56, 1, False, False),       # tiny odd shapes
+    (130, 1536, 384, 1, False, True),    # linear with the weight as B (ops.c:249)
+])
+def test_gemm_half(dcb, torch_cuda, M, N, K, batch, shareA, shareB, simt):
+    torch = torch_cuda
+    rng = np.random.default_rng(M * 7 + N)
+    A = _half_np(rng.standard_normal((1 if shareA else batch, M, K)))
+    B = _half_np(rng.standard_normal((1 if shareB else batch, N, K)))
+    ref = np.matmul(A.astype(np.float64), np.swapaxes(B.astype(np.float64), 1, 2))
+    ref = np.broadcast_to(ref, (batch, M, N))
+    At = torch.from_numpy(A).cuda()
+    Bt = torch.from_numpy(B).cuda()
+    old = dcb.set_option("simt", simt)
+    try:
+        Ct = dcb.gemm_half(At[0] if shareA else At, Bt[0] if shareB else Bt)
+        torch.cuda.synchronize()
+    finally:
+        dcb.set_option("simt", old)
+    got = Ct.cpu().numpy()
+    assert got.shape == (batch, M, N)
+    assert rel_l2(got, ref) < 2e-5
+    assert dcb.device_fault() == 0
+
+
+def test_gemm_half_alpha_beta(dcb, torch_cuda):
+    torch = torch_cuda
+    rng = np.random.default_rng(5)
+    A = _half_np(rng.standard_normal((1, 200, 64)))
+    B = _half_np(rng.standard_normal((1, 150, 64)))
+    C0 = rng.standard_normal((1, 200, 150)).astype(np.float32)
+    Ct = torch.from_numpy(C0.copy()).cuda()
+    dcb.gemm_half(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), Ct, alpha=0.5,
+                  beta=2.0)
+    ref = 0.5 * np.matmul(A.astype(np.float64), B[0].T.astype(np.float64)) + 2.0 * C0
+    assert rel_l2(Ct.cpu().numpy(), ref) < 2e-5
+
+
+def _geom(C_, H, W, KH, KW, SH, SW, PH, PW, DH=1, DW=1):
+    import demucs_cuda_b200 as d
+    g = d.DkConvGeom()
+    g.C, g.H, g.W, g.KH, g.KW, g.SH, g.SW, g.PH, g.PW, g.DH, g.DW = (C_, H, W, KH, KW, SH, SW,
+                                                                     PH, PW, DH, DW)
+    g.Ho = (H + 2 * PH - DH * (KH - 1) - 1) // SH + 1
+    g.Wo = (W + 2 * PW - DW * (KW - 1) - 1) // SW + 1
+    g.Kp = (KH * KW * C_ + 7) // 8 * 8
+    return g
+
+
+def _pack(w2d):
+    """fp16 rows padded to 8 (the loader rule, weights.c:306-310)."""
+    rows, K = w2d.shape
+    kp = (K + 7) // 8 * 8
+    out = np.zeros((rows, kp), np.float16)
+    out[:, :K] = w2d.astype(np.float32).astype(np.float16)
+    return out, kp
+
+
+@pytest.mark.parametrize("simt", [0, 1])
+@pytest.mark.parametrize("N,C_,H,W,O,KH,KW,SH,SW,PH,PW,DW,act", [
+    (2, 4, 64, 9, 24, 8, 1, 4, 1, 2, 0, 1, 0),     # test_kernels.c conv2d k8x1 s4 p2
+    (1, 9, 11, 13, 10, 3, 3, 1, 1, 1, 1, 1, 0),    # test_kernels.c conv2d 3x3
+    (2, 13, 1, 101, 17, 1, 8, 1, 4, 0, 2, 1, 0),   # conv1d k8 s4 p2 as H = 1
+    (1, 24, 1, 64, 6, 1, 3, 1, 1, 0, 4, 4, 0),     # conv1d k3 dil 4
+    (3, 48, 1, 77, 96, 1, 1, 1, 1, 0, 0, 1, 0),    # conv1d 1x1
+    (1, 4, 512, 40, 48, 8, 1, 4, 1, 2, 0, 1, 1),   # enc0 freq conv + GELU
+    (1, 48, 128, 40, 96, 1, 1, 1, 1, 0, 0, 1, 2),  # encoder rewrite 1x1 + GLU
+    (1, 96, 32, 30, 192, 3, 3, 1, 1, 1, 1, 1, 2),  # decoder rewrite 3x3 + GLU
+    (1, 384, 8, 20, 768, 3, 3, 1, 1, 1, 1, 1, 2),  # dec0 rewrite 3x3 + GLU (K = 3456)
+])
+def test_conv_fused(dcb, ref, torch_cuda, N, C_, H, W, O, KH, KW, SH, SW, PH, PW, DW, act,
+                    simt):
+    torch = torch_cuda
+    rng = np.random.default_rng(N * 1000 + C_ * 10 + O)
+    x = rng.uniform(-1, 1, (N, C_, H, W)).astype(np.float32)
+    w = rng.uniform(-1, 1, (O, KH, KW, C_)).astype(np.float32) / np.sqrt(KH * KW * C_)
+    b = rng.uniform(-1, 1, O).astype(np.float32)
+    if H == 1 and KH == 1:
+        r = ref.conv1d(x[:, :, 0, :], w[:, 0], b, SW, PW, DW)[:, :, None, :]
+    else:
+        r = ref.conv2d(x, w, b, SH, SW, PH, PW)
+    if act == 1:
+        from oracle import port
+        r = port.gelu(r)
+    elif act == 2:
+        from oracle import port
+        r = port.glu(r, axis=1)
+    g = _geom(C_, H, W, KH, KW, SH, SW, PH, PW, 1, DW)
+    wp, kp = _pack(w.reshape(O, -1))
+    xt, wt, bt = _dev(torch, x), torch.from_numpy(wp).cuda(), _dev(torch, b)
+    Oy = O // 2 if act == 2 else O
+    yt = torch.zeros((N, Oy, g.Ho, g.Wo), device="cuda")
+    old = dcb.set_option("simt", simt)
+    try:
+        dcb.lib().dkx_conv2d(_p(xt), N, C.byref(g), _p(wt), O, _p(bt), act, _p(yt))
+        dcb.check(True, "dkx_conv2d")
+        torch.cuda.synchronize()
+    finally:
+        dcb.set_option("simt", old)
+    assert rel_l2(yt.cpu().numpy(), r) < 2e-5
+    assert dcb.device_fault() == 0
+
+
+@pytest.mark.parametrize("simt", [0, 1])
+@pytest.mark.parametrize("N,C_,H,W,O,axis_h,gelu", [
+    (2, 24, 16, 9, 12, True, False),    # test_kernels.c conv_tr2d k8x1 s4
+    (2, 19, 1, 23, 11, False, False),   # test_kernels.c conv_tr k1x8 s1x4 (1-D)
+    (1, 48, 128, 30, 24, True, False),  # dec3 (last freq decoder, no GELU)
+    (1, 96, 32, 17, 48, True, True),    # freq decoder with GELU
+    (1, 48, 1, 500, 12, False, False),  # tdec3 shape class
+    (1, 192, 1, 345, 96, False, True),  # time decoder with GELU
+])
+def test_conv_tr_fused(dcb, ref, torch_cuda, N, C_, H, W, O, axis_h, gelu, simt):
+    torch = torch_cuda
+    rng = np.random.default_rng(N * 77 + C_ + O)
+    S, K = 4, 8
+    x = rng.uniform(-1, 1, (N, C_, H, W)).astype(np.float32)
+    wshape = (O, K, 1, C_) if axis_h else (O, 1, K, C_)
+    w = (rng.uniform(-1, 1, wshape) / np.sqrt(C_)).astype(np.float32)
+    b = rng.uniform(-1, 1, O).astype(np.float32)
+    full = ref.conv_tr2d(x, w, b, S if axis_h else 1, 1 if axis_h else S)
+    crop = 2
+    if axis_h:
+        out_len = full.shape[2] - 2 * crop
+        r = full[:, :, crop:crop + out_len]
+    else:
+        out_len = full.shape[3] - 2 * crop - 1
+        r = full[:, :, :, crop:crop + out_len]
+    if gelu:
+        from oracle import port
+        r = port.gelu(r)
+    wp, kp = _pack(w.reshape(O * K, C_))
+    xt, wt, bt = _dev(torch, x), torch.from_numpy(wp).cuda(), _dev(torch, b)
+    yt = torch.zeros(r.shape, device="cuda")
+    KH, KW = (K, 1) if axis_h else (1, K)
+    old = dcb.set_option("simt", simt)
+    try:
+        dcb.lib().dkx_conv_tr(_p(xt), N, C_, x.shape[2], x.shape[3], _p(wt), O, KH, KW, S,
+                              _p(bt), crop, out_len, int(gelu), _p(yt))
+        dcb.check(True, "dkx_conv_tr")
+        torch.cuda.synchronize()
+    finally:
+        dcb.set_option("simt", old)
+    assert rel_l2(yt.cpu().numpy(), r) < 2e-5
+    assert dcb.device_fault() == 0
+
+
+@pytest.mark.parametrize("R,IN,OUT", [(37, 50, 29), (130, 384, 1536), (2688, 384, 384)])
+def test_linear_fused(dcb, ref, torch_cuda, R, IN, OUT):
+    torch = torch_cuda
+    rng = np.random.default_rng(R + IN + OUT)
+    x = rng.uniform(-1, 1, (R, IN)).astype(np.float32)
+    w = (rng.uniform(-1, 1, (OUT, IN)) / np.sqrt(IN)).astype(np.float32)
+    b = rng.uniform(-1, 1, OUT).astype(np.float32)
+    r = ref.linear(x, w, b)
+    wp, kp = _pack(w)
+    yt = torch.zeros((R, OUT), device="cuda")
+    dcb.lib().dkx_linear(_p(_dev(torch, x)), R, IN, _p(torch.from_numpy(wp).cuda()), kp, OUT,
+                         _p(_dev(torch, b)), _p(yt))
+    dcb.check(True, "dkx_linear")
+    assert rel_l2(yt.cpu().numpy(), r) < 2e-5
+
+
+@pytest.mark.parametrize("simt", [0, 1])
+@pytest.mark.parametrize("B,Tq,Tk,D,H", [
+    (2, 33, 47, 64, 8),       # test_kernels.c
+    (1, 300, 300, 384, 8),    # test_kernels.c
+    (1, 700, 350, 384, 8),    # cross attention, partial key/query tiles
+])
+def test_attention_fused(dcb, ref, torch_cuda, B, Tq, Tk, D, H, simt):
+    torch = torch_cuda
+    rng = np.random.default_rng(Tq + Tk + D)
+    q = rng.uniform(-1, 1, (B, Tq, D)).astype(np.float32)
+    k = rng.uniform(-1, 1, (B, Tk, D)).astype(np.float32)
+    v = rng.uniform(-1, 1, (B, Tk, D)).astype(np.float32)
+    r = ref.attention(q, k, v, H)
+    yt = torch.zeros((B, Tq, D), device="cuda")
+    old = dcb.set_option("simt", simt)
+    try:
+        dcb.lib().dkx_attention(_p(_dev(torch, q)), _p(_dev(torch, k)), _p(_dev(torch, v)), B,
+                                Tq, Tk, H, D // H, _p(yt))
+        dcb.check(True, "dkx_attention")
+        torch.cuda.synchronize()
+    finally:
+        dcb.set_option("simt", old)
+    tol = 2e-3 if not simt else 1e-5
+    assert rel_l2(yt.cpu().numpy(), r) < tol
+    assert dcb.device_fault() == 0
+
+
+@pytest.mark.parametrize("B,C_,L,G,act", [(2, 12, 37, 1, 0), (2, 12, 37, 1, 1), (2, 12, 37, 1, 2),
+                                          (2, 16, 33, 4, 1), (3, 96, 20000, 1, 2)])
+def test_groupnorm(dcb, ref, torch_cuda, B, C_, L, G, act):
+    torch = torch_cuda
+    rng = np.random.default_rng(B + C_ + L)
+    x = (rng.uniform(-1, 1, (B, C_, L)) * 3 + 0.5).astype(np.float32)
+    w = rng.uniform(-1, 1, C_).astype(np.float32)
+    b = rng.uniform(-1, 1, C_).astype(np.float32)
+    r = ref.groupnorm(x, w, b, G, act)
+    xt = _dev(torch, x)
+    st = torch.zeros(2 * B * G, device="cuda")
+    L_ = dcb.lib()
+    L_.dk_row_stats(_p(xt), B * G, C_ // G * L, _p(st), C.c_void_p(st.data_ptr() + 4 * B * G))
+    yt = torch.zeros(r.shape, device="cuda")
+    L_.dk_groupnorm_apply(_p(xt), _p(yt), _p(st), C.c_void_p(st.data_ptr() + 4 * B * G),
+                          _p(_dev(torch, w)), _p(_dev(torch, b)), B, C_, L, G, 1e-5, act)
+    dcb.check(True, "groupnorm")
+    assert rel_l2(yt.cpu().numpy(), r) < 1e-5
+
+
+@pytest.mark.parametrize("R,C_", [(45, 384), (7, 1536), (1000, 64)])
+def test_layernorm(dcb, ref, torch_cuda, R, C_):
+    torch = torch_cuda
+    rng = np.random.default_rng(R + C_)
+    x = rng.uniform(-1, 1, (R, C_)).astype(np.float32)
+    w = rng.uniform(-1, 1, C_).astype(np.float32)
+    b = rng.uniform(-1, 1, C_).astype(np.float32)
+    r = ref.layernorm(x, w, b)
+    yt = torch.zeros((R, C_), device="cuda")
+    dcb.lib().dk_layernorm(_p(_dev(torch, x)), _p(yt), _p(_dev(torch, w)), _p(_dev(torch, b)),
+                           R, C_, 1e-5)
+    dcb.check(True, "layernorm")
+    assert rel_l2(yt.cpu().numpy(), r) < 1e-5
+
+
+@pytest.mark.parametrize("T", [44100, 343980])
+def test_spec_ispec(dcb, ref, torch_cuda, T):
+    """STFT (dk_stft after the two reflect pads) and iSTFT + OLA against stft.c's _spec /
+    _ispec on the reference CPU backend."""
+    torch = torch_cuda
+    from oracle import port
+    rng = np.random.default_rng(T)
+    mix = rng.uniform(-0.5, 0.5, (1, 2, T)).astype(np.float32)
+    z_ref = ref.spec(mix)
+    nfft, hop = 4096, 1024
+    le = -(-T // hop)
+    pad = (hop // 2) * 3
+    extra = pad + le * hop - T
+    L1, L2 = T + pad + extra, T + pad + extra + nfft
+    L_ = dcb.lib()
+    xm = _dev(torch, mix)
+    xp = torch.zeros((2, L1), device="cuda")
+    xc = torch.zeros((2, L2), device="cuda")
+    L_.dk_reflect_pad(_p(xm), _p(xp), 2, T, pad, extra)
+    L_.dk_reflect_pad(_p(xp), _p(xc), 2, L1, nfft // 2, nfft // 2)
+    win = _dev(torch, port.hann(nfft))
+    z = torch.zeros((1, 4, nfft // 2, le), device="cuda")
+    L_.dk_stft(_p(xc), _p(z), 2, L2, nfft, hop, 2, le, nfft // 2, _p(win))
+    dcb.check(True, "stft")
+    assert rel_l2(z.cpu().numpy(), z_ref) < 1e-5
+    # inverse on a random spectrum [1, 2 sources, 4 (2C), F, N]
+    zs = rng.standard_normal((1, 2, 4, nfft // 2, le)).astype(np.float32)
+    y_ref = ref.ispec(zs, T)
+    R, NF = 4, le + 4
+    fr = torch.zeros((R, NF, nfft), device="cuda")
+    L_.dk_istft_frames(_p(_dev(torch, zs)), _p(fr), R, nfft // 2, le, 2, nfft, _p(win))
+    y = torch.zeros((R, T), device="cuda")
+    L_.dk_ola(_p(fr), _p(y), R, NF, nfft, hop, _p(win), nfft // 2 + pad, T)
+    dcb.check(True, "istft")
+    assert rel_l2(y.cpu().numpy().reshape(y_ref.shape), y_ref) < 1e-5

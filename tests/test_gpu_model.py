@@ -1,0 +1,166 @@
+"""Model-level parity of the B200 engine against the reference (htdemucs_6s forward).
+
+Mirrors the reference's tests/test_compare.c: every stage is fed the reference's own output
+of the previous stage (teacher forcing) and compared under the BASELINE gate of 8e-4
+relative L2, then the end-to-end stems are compared (gate 1e-3 relative L2, i.e. SNR >= 60
+dB).  The reference run is oracle/_ref (the reference's CPU backend and model code); at
+full segment size the committed digest of that run (tests/golden/full_digest.json) is the
+oracle, because the single-threaded reference needs minutes per forward.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import ROOT, model_files, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+STAGE_GATE = 8e-4
+STEMS_GATE = 1e-3
+
+
+def _load(name):
+    import torch
+    import demucs_cuda_b200 as dcb
+    from demucs_cuda_b200 import synth
+    from oracle import ref
+    cfg, w, c = model_files(name)
+    ref.load(w, c)
+    mix = synth.segment_input(cfg, 1, 0)
+    stems, st = ref.forward(mix, stages=True)
+    model = dcb.Model(w, c)
+    return {"cfg": cfg, "mix": mix, "ref_stems": stems, "ref": st, "model": model,
+            "torch": torch}
+
+
+@pytest.fixture(scope="module")
+def tiny(torch_cuda):
+    return _load("tiny")
+
+
+@pytest.fixture(scope="module")
+def short(torch_cuda):
+    return _load("short")
+
+
+def _t(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def _forward_check(d):
+    torch = d["torch"]
+    out, st = d["model"].forward(_t(torch, d["mix"]), stages=True)
+    got = out.cpu().numpy()
+    e = rel_l2(got, d["ref_stems"])
+    print(f"stems rel_l2 {e:.3e}  SNR {-20 * np.log10(max(e, 1e-12)):.1f} dB")
+    for k, v in d["ref"].items():
+        if k in st:
+            print(f"  {k:16s} {rel_l2(st[k].cpu().numpy(), v):.3e}")
+    assert got.shape == d["ref_stems"].shape
+    assert e < STEMS_GATE
+
+
+def _teacher_forced(d):
+    torch = d["torch"]
+    m, R = d["model"], d["ref"]
+    depth = 4
+    worst = {}
+    for i in range(depth):
+        xin = R["x_norm"] if i == 0 else R[f"enc_{i - 1}"]
+        y = m.stage_encoder(0, i, _t(torch, xin)).cpu().numpy()
+        worst[f"enc_{i}"] = rel_l2(y, R[f"enc_{i}"])
+        tin = R["xt_norm"] if i == 0 else R[f"tenc_{i - 1}"]
+        y = m.stage_encoder(1, i, _t(torch, tin)).cpu().numpy()
+        worst[f"tenc_{i}"] = rel_l2(y, R[f"tenc_{i}"])
+    x, xt = m.stage_transformer(_t(torch, R[f"enc_{depth - 1}"]),
+                                _t(torch, R[f"tenc_{depth - 1}"]))
+    worst["transformer_x"] = rel_l2(x.cpu().numpy(), R["transformer_x"])
+    worst["transformer_xt"] = rel_l2(xt.cpu().numpy(), R["transformer_xt"])
+    tlens = [R["xt_norm"].shape[-1]] + [R[f"tenc_{i}"].shape[-1] for i in range(depth - 1)]
+    for i in range(depth):
+        xin = R["transformer_x"] if i == 0 else R[f"dec_{i - 1}"]
+        y = m.stage_decoder(0, i, _t(torch, xin), _t(torch, R[f"enc_{depth - 1 - i}"]))
+        worst[f"dec_{i}"] = rel_l2(y.cpu().numpy(), R[f"dec_{i}"])
+        tin = R["transformer_xt"] if i == 0 else R[f"tdec_{i - 1}"]
+        y = m.stage_decoder(1, i, _t(torch, tin), _t(torch, R[f"tenc_{depth - 1 - i}"]),
+                            tlens[depth - 1 - i])
+        worst[f"tdec_{i}"] = rel_l2(y.cpu().numpy(), R[f"tdec_{i}"])
+    for k, v in worst.items():
+        print(f"  teacher-forced {k:16s} {v:.3e}")
+    bad = {k: v for k, v in worst.items() if not v < STAGE_GATE}
+    assert not bad, bad
+
+
+def test_tiny_forward(tiny):
+    _forward_check(tiny)
+
+
+def test_tiny_stages_teacher_forced(tiny):
+    _teacher_forced(tiny)
+
+
+def test_short_forward(short):
+    _forward_check(short)
+
+
+def test_short_stages_teacher_forced(short):
+    _teacher_forced(short)
+
+
+def test_tiny_batch_consistency(tiny):
+    """A batch of segments gives each segment the result it gets alone (per-segment
+    normalisation and every kernel are per sample)."""
+    torch = tiny["torch"]
+    from demucs_cuda_b200 import synth
+    mix = synth.segment_input(tiny["cfg"], 3, 7)
+    m = tiny["model"]
+    batched = m.forward(_t(torch, mix)).cpu().numpy()
+    for b in range(3):
+        single = m.forward(_t(torch, mix[b:b + 1])).cpu().numpy()
+        assert rel_l2(batched[b:b + 1], single) < 1e-6
+
+
+def test_tiny_short_input_padding(tiny):
+    """Inputs shorter than the training length are zero padded and cut back
+    (htdemucs.c:141-147, 269-274)."""
+    torch = tiny["torch"]
+    from oracle import ref
+    from demucs_cuda_b200 import synth
+    cfg, w, c = model_files("tiny")
+    ref.load(w, c)
+    mix = synth.segment_input(cfg, 1, 3)[:, :, : cfg.valid_length - 1234]
+    r = ref.forward(mix)
+    got = tiny["model"].forward(_t(torch, mix)).cpu().numpy()
+    assert got.shape == r.shape
+    assert rel_l2(got, r) < STEMS_GATE
+
+
+def test_full_forward_vs_reference_digest(torch_cuda):
+    """Full-size htdemucs_6s segment (343980 samples): stems and every stage against the
+    reference run's committed digest."""
+    torch = torch_cuda
+    import demucs_cuda_b200 as dcb
+    from demucs_cuda_b200 import synth
+    path = os.path.join(ROOT, "tests", "golden", "full_digest.json")
+    if not os.path.exists(path):
+        pytest.skip("full_digest.json not generated")
+    dg = json.load(open(path))
+    cfg, w, c = model_files("full")
+    model = dcb.Model(w, c)
+    mix = synth.segment_input(cfg, 1, 0)
+    out, st = model.forward(_t(torch, mix), stages=True)
+    errs = {}
+    for k, d in dg["stages"].items():
+        if k not in st:
+            continue
+        a = st[k].cpu().numpy().ravel()
+        assert list(st[k].shape) == d["shape"], k
+        idx = np.linspace(0, a.size - 1, d["idx_count"]).astype(np.int64)
+        errs[k] = (rel_l2(a[idx], np.array(d["samples"])),
+                   abs(float((a.astype(np.float64) ** 2).sum()) / d["sumsq"] - 1.0))
+    for k, (e, s) in errs.items():
+        print(f"  {k:16s} samples rel {e:.3e}  energy rel {s:.3e}")
+    assert errs["stems"][0] < STEMS_GATE and errs["stems"][1] < 2 * STEMS_GATE
+    del model
