@@ -34,7 +34,8 @@ BACKEND_SYMBOLS = [
 ]
 FUSED_SYMBOLS = ["dkx_conv2d", "dkx_conv_tr", "dkx_linear", "dkx_attention"]
 ENGINE_SYMBOLS = [
-    "dcb_set_error_mode", "dcb_last_error", "dcb_set_stream", "dcb_get_stream",
+    "dcb_set_error_mode", "dcb_last_error", "dcb_set_stream", "dcb_use_own_stream",
+    "dcb_get_stream",
     "dcb_set_option", "dcb_kernel_launches", "dcb_device_fault", "dcb_model_load",
     "dcb_model_free", "dcb_model_info", "dcb_model_weight_bytes", "dcb_model_weight_block",
     "dcb_forward", "dcb_stage_encoder", "dcb_stage_decoder", "dcb_stage_transformer",
@@ -122,6 +123,7 @@ def lib(load_only: bool = False):
         "dcb_set_error_mode": (None, [i32]),
         "dcb_last_error": (C.c_char_p, [i32]),
         "dcb_set_stream": (None, [vp]),
+        "dcb_use_own_stream": (None, []),
         "dcb_get_stream": (vp, []),
         "dcb_set_option": (i32, [C.c_char_p, i32]),
         "dcb_kernel_launches": (C.c_uint64, []),

@@ -540,7 +540,7 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
     t_len.push_back(Lt);
     int Lo;
     float *xt2 = enc_time(m, i, xt, B, Lt, &Lo);
-    dfree(xt);
+    if (i == 0) dfree(xt);  // the normalised input; encoder outputs live on as skips
     xt = xt2;
     Lt = Lo;
     saved_t.push_back(xt);
@@ -549,7 +549,7 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
     fr_len.push_back(H);
     int Ho;
     float *x2 = enc_freq(m, i, x, B, H, W, &Ho);
-    dfree(x);
+    if (i == 0) dfree(x);
     x = x2;
     H = Ho;
     saved.push_back(x);

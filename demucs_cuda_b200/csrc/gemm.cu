@@ -444,12 +444,12 @@ static void launch_umma(const CUtensorMap &ta, const CUtensorMap &tb, Shape s, c
   if (stages < 2) stages = 2;
   s.stages = stages;
   const size_t smem = 1024 + stages * stage_bytes + (2 * stages + 1) * 8 + 16 + table;
-  DCB_REQUIRE(smem <= 227 * 1024, "gemm: shared memory %zu exceeds the per-CTA limit", smem);
-  static bool attr = false;
-  if (!attr) {
+  DCB_REQUIRE(smem <= 226 * 1024, "gemm: shared memory %zu exceeds the per-CTA limit", smem);
+  static size_t attr = 0;  // dynamic shared memory opted in so far for this instantiation
+  if (smem > attr) {
     DCB_CUDA(cudaFuncSetAttribute(k_umma<BN, GATHER>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    attr = true;
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr = smem;
   }
   s.tmem_cols = BN < 32 ? 32 : BN;
   for (int64_t b0 = 0; b0 < batch; b0 += 65535) {

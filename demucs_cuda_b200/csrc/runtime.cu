@@ -212,8 +212,10 @@ const char *dcb_last_error(int clear) {
 
 void dcb_set_stream(void *s) {
   g_ext_stream = (cudaStream_t)s;
-  g_use_ext = s != nullptr;
+  g_use_ext = true;
 }
+
+void dcb_use_own_stream(void) { g_use_ext = false; }
 
 void *dcb_get_stream(void) { return (void *)stream(); }
 

@@ -170,9 +170,11 @@ enum { DCB_ERRORS_FATAL = 0, DCB_ERRORS_RETURN = 1 };
 void dcb_set_error_mode(int mode);
 /* Last recorded error message ("" if none); clears it when clear != 0. */
 const char *dcb_last_error(int clear);
-/* Use an external stream (e.g. a framework's current stream) for every later call; NULL
- * restores the backend's own stream.  The pointer is a cudaStream_t. */
+/* Use an external stream (a cudaStream_t, e.g. a framework's current stream) for every
+ * later call; NULL selects the legacy default stream.  dcb_use_own_stream() returns to the
+ * backend's own non-blocking stream (the default, as backend_cuda.cu:41 creates one). */
 void dcb_set_stream(void *stream);
+void dcb_use_own_stream(void);
 void *dcb_get_stream(void);
 /* Backend options: "simt" (1 = CUDA-core kernels instead of tcgen05, for A/B checks),
  * "graphs" (1 = replay captured CUDA graphs for repeated forwards). Returns the old value. */

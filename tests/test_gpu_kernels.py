@@ -31,6 +31,8 @@ def ref():
 
 
 def _dev(torch, a):
+    """Device copy; callers keep the returned tensor alive until the kernels that read it
+    have finished (a temporary would be recycled by the caching allocator)."""
     return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda()
 
 
@@ -42,7 +44,7 @@ def _half_np(a):
     return np.asarray(a, np.float32).astype(np.float16)
 
 
-@pytest.mark.parametrize("simt", [0, 1])
+@pytest.mark.parametrize("simt", [pytest.param(0, id="umma"), pytest.param(1, id="simt")])
 @pytest.mark.parametrize("M,N,K,batch,shareA,shareB", [
     (256, 200, 72, 1, False, False),     # normal orientation, partial N tile, K < 2 blocks
     (48, 1000, 32, 1, False, False),     # small M -> swapped orientation (conv weights as A)
@@ -106,7 +108,7 @@ def _pack(w2d):
     return out, kp
 
 
-@pytest.mark.parametrize("simt", [0, 1])
+@pytest.mark.parametrize("simt", [pytest.param(0, id="umma"), pytest.param(1, id="simt")])
 @pytest.mark.parametrize("N,C_,H,W,O,KH,KW,SH,SW,PH,PW,DW,act", [
     (2, 4, 64, 9, 24, 8, 1, 4, 1, 2, 0, 1, 0),     # test_kernels.c conv2d k8x1 s4 p2
     (1, 9, 11, 13, 10, 3, 3, 1, 1, 1, 1, 1, 0),    # test_kernels.c conv2d 3x3
@@ -151,7 +153,7 @@ def test_conv_fused(dcb, ref, torch_cuda, N, C_, H, W, O, KH, KW, SH, SW, PH, PW
     assert dcb.device_fault() == 0
 
 
-@pytest.mark.parametrize("simt", [0, 1])
+@pytest.mark.parametrize("simt", [pytest.param(0, id="umma"), pytest.param(1, id="simt")])
 @pytest.mark.parametrize("N,C_,H,W,O,axis_h,gelu", [
     (2, 24, 16, 9, 12, True, False),    # test_kernels.c conv_tr2d k8x1 s4
     (2, 19, 1, 23, 11, False, False),   # test_kernels.c conv_tr k1x8 s1x4 (1-D)
@@ -205,13 +207,14 @@ def test_linear_fused(dcb, ref, torch_cuda, R, IN, OUT):
     r = ref.linear(x, w, b)
     wp, kp = _pack(w)
     yt = torch.zeros((R, OUT), device="cuda")
-    dcb.lib().dkx_linear(_p(_dev(torch, x)), R, IN, _p(torch.from_numpy(wp).cuda()), kp, OUT,
-                         _p(_dev(torch, b)), _p(yt))
+    keep = [_dev(torch, x), torch.from_numpy(wp).cuda(), _dev(torch, b)]  # alive until synced
+    dcb.lib().dkx_linear(_p(keep[0]), R, IN, _p(keep[1]), kp, OUT, _p(keep[2]), _p(yt))
     dcb.check(True, "dkx_linear")
+    torch.cuda.synchronize()
     assert rel_l2(yt.cpu().numpy(), r) < 2e-5
 
 
-@pytest.mark.parametrize("simt", [0, 1])
+@pytest.mark.parametrize("simt", [pytest.param(0, id="umma"), pytest.param(1, id="simt")])
 @pytest.mark.parametrize("B,Tq,Tk,D,H", [
     (2, 33, 47, 64, 8),       # test_kernels.c
     (1, 300, 300, 384, 8),    # test_kernels.c
@@ -227,8 +230,9 @@ def test_attention_fused(dcb, ref, torch_cuda, B, Tq, Tk, D, H, simt):
     yt = torch.zeros((B, Tq, D), device="cuda")
     old = dcb.set_option("simt", simt)
     try:
-        dcb.lib().dkx_attention(_p(_dev(torch, q)), _p(_dev(torch, k)), _p(_dev(torch, v)), B,
-                                Tq, Tk, H, D // H, _p(yt))
+        keep = [_dev(torch, q), _dev(torch, k), _dev(torch, v)]
+        dcb.lib().dkx_attention(_p(keep[0]), _p(keep[1]), _p(keep[2]), B, Tq, Tk, H, D // H,
+                                _p(yt))
         dcb.check(True, "dkx_attention")
         torch.cuda.synchronize()
     finally:
@@ -252,9 +256,11 @@ def test_groupnorm(dcb, ref, torch_cuda, B, C_, L, G, act):
     L_ = dcb.lib()
     L_.dk_row_stats(_p(xt), B * G, C_ // G * L, _p(st), C.c_void_p(st.data_ptr() + 4 * B * G))
     yt = torch.zeros(r.shape, device="cuda")
+    wt, bt = _dev(torch, w), _dev(torch, b)
     L_.dk_groupnorm_apply(_p(xt), _p(yt), _p(st), C.c_void_p(st.data_ptr() + 4 * B * G),
-                          _p(_dev(torch, w)), _p(_dev(torch, b)), B, C_, L, G, 1e-5, act)
+                          _p(wt), _p(bt), B, C_, L, G, 1e-5, act)
     dcb.check(True, "groupnorm")
+    torch.cuda.synchronize()
     assert rel_l2(yt.cpu().numpy(), r) < 1e-5
 
 
@@ -267,9 +273,10 @@ def test_layernorm(dcb, ref, torch_cuda, R, C_):
     b = rng.uniform(-1, 1, C_).astype(np.float32)
     r = ref.layernorm(x, w, b)
     yt = torch.zeros((R, C_), device="cuda")
-    dcb.lib().dk_layernorm(_p(_dev(torch, x)), _p(yt), _p(_dev(torch, w)), _p(_dev(torch, b)),
-                           R, C_, 1e-5)
+    keep = [_dev(torch, x), _dev(torch, w), _dev(torch, b)]
+    dcb.lib().dk_layernorm(_p(keep[0]), _p(yt), _p(keep[1]), _p(keep[2]), R, C_, 1e-5)
     dcb.check(True, "layernorm")
+    torch.cuda.synchronize()
     assert rel_l2(yt.cpu().numpy(), r) < 1e-5
 
 
@@ -303,7 +310,8 @@ def test_spec_ispec(dcb, ref, torch_cuda, T):
     y_ref = ref.ispec(zs, T)
     R, NF = 4, le + 4
     fr = torch.zeros((R, NF, nfft), device="cuda")
-    L_.dk_istft_frames(_p(_dev(torch, zs)), _p(fr), R, nfft // 2, le, 2, nfft, _p(win))
+    zst = _dev(torch, zs)
+    L_.dk_istft_frames(_p(zst), _p(fr), R, nfft // 2, le, 2, nfft, _p(win))
     y = torch.zeros((R, T), device="cuda")
     L_.dk_ola(_p(fr), _p(y), R, NF, nfft, hop, _p(win), nfft // 2 + pad, T)
     dcb.check(True, "istft")
