@@ -36,7 +36,8 @@ FUSED_SYMBOLS = ["dkx_conv2d", "dkx_conv_tr", "dkx_linear", "dkx_attention"]
 ENGINE_SYMBOLS = [
     "dcb_set_error_mode", "dcb_last_error", "dcb_set_stream", "dcb_use_own_stream",
     "dcb_get_stream",
-    "dcb_set_option", "dcb_kernel_launches", "dcb_device_fault", "dcb_model_load",
+    "dcb_set_option", "dcb_kernel_launches", "dcb_device_fault", "dcb_trace_start",
+    "dcb_trace_stop", "dcb_model_load",
     "dcb_model_free", "dcb_model_info", "dcb_model_weight_bytes", "dcb_model_weight_block",
     "dcb_forward", "dcb_stage_encoder", "dcb_stage_decoder", "dcb_stage_transformer",
     "dcb_apply_defaults", "dcb_apply", "dcb_apply_plan",
@@ -128,6 +129,9 @@ def lib(load_only: bool = False):
         "dcb_set_option": (i32, [C.c_char_p, i32]),
         "dcb_kernel_launches": (C.c_uint64, []),
         "dcb_device_fault": (C.c_uint32, [i32]),
+        "dcb_trace_start": (None, [C.c_uint32]),
+        "dcb_trace_stop": (i32, [C.POINTER(C.c_double), C.POINTER(C.c_double),
+                                 C.POINTER(C.c_double), C.POINTER(i32), i32]),
         "dcb_model_load": (vp, [C.c_char_p, C.c_char_p]),
         "dcb_model_free": (None, [vp]),
         "dcb_model_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32),
@@ -346,6 +350,27 @@ def set_option(name: str, value: int) -> int:
 
 def kernel_launches() -> int:
     return lib().dcb_kernel_launches()
+
+
+TRACE_CLASSES = ["conv", "conv_tr", "linear", "attention", "gemm_half"]
+
+
+def trace_start(classes=("conv", "conv_tr", "linear", "attention", "gemm_half")):
+    mask = 0
+    for c in classes:
+        mask |= 1 << TRACE_CLASSES.index(c)
+    lib().dcb_trace_start(mask)
+
+
+def trace_stop():
+    """Per-class {ms, flops, bytes, launches} of the traced launches."""
+    n = len(TRACE_CLASSES)
+    ms, fl, by = (C.c_double * n)(), (C.c_double * n)(), (C.c_double * n)()
+    ln = (C.c_int * n)()
+    lib().dcb_trace_stop(ms, fl, by, ln, n)
+    check(True, "trace")
+    return {c: {"ms": ms[i], "flops": fl[i], "bytes": by[i], "launches": ln[i]}
+            for i, c in enumerate(TRACE_CLASSES)}
 
 
 def device_fault(clear: bool = True) -> int:

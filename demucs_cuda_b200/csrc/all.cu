@@ -5,6 +5,7 @@
 #include "norm.cu"
 #include "operand.cu"
 #include "spectral.cu"
+#include "trace.cu"
 #include "gemm.cu"
 #include "attention.cu"
 #include "glue.cu"

@@ -321,6 +321,8 @@ void flash_attention(const uint16_t *q, const uint16_t *k, const uint16_t *vt, i
   a.scale = 1.0f / sqrtf((float)hd);
   a.o16 = o16;
   a.o32 = o32;
+  TraceScope ts(TR_ATTN, 4.0 * B * H * (double)Tq * Tk * hd,
+                2.0 * B * H * hd * (2.0 * Tq + 2.0 * Tk));
   if (!g_opt_simt) {
     CUtensorMap mq, mk, mv;
     bool ok = map3(&mq, q, hd, Tq, (uint64_t)B * H, hd, (uint64_t)Tq * hd, 64, kQ) &&

@@ -483,6 +483,9 @@ static void launch_simt(RowsA a, RowsA b, Shape s, const Gather &g, const Epi &e
   DCB_LAUNCHED();
 }
 
+void gemm_rows_launch(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch,
+                      const Epi &e, Shape s, Gather g);
+
 void gemm_rows(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch, const Epi &e) {
   if (M <= 0 || N <= 0 || batch <= 0) return;
   DCB_REQUIRE(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm: extents too large");
@@ -494,6 +497,20 @@ void gemm_rows(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch,
   s.a_shared = a.stride == 0;
   s.b_shared = b.stride == 0;
   Gather g{};
+  {
+    // algorithmic work of this call (unpadded extents)
+    const double mnk = 2.0 * (double)M * (double)N * (double)K * (double)batch;
+    double out_b = (double)M * N * batch * (e.mode == EPI_ROWS_F32 || e.mode == EPI_GEMM ? 4 : 2);
+    if (e.res || e.beta != 0.f) out_b *= 2;
+    const double in_b = 2.0 * ((double)M * K * (a.stride ? batch : 1) +
+                               (double)N * K * (b.stride ? batch : 1));
+    TraceScope ts(e.mode == EPI_GEMM ? TR_GEMM : TR_LINEAR, mnk, in_b + out_b);
+    gemm_rows_launch(M, N, K, a, b, batch, e, s, g);
+  }
+}
+
+void gemm_rows_launch(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch,
+                      const Epi &e, Shape s, Gather g) {
   if (!g_opt_simt && K > 0 && batch <= 65535) {
     const int bn = pick_bn(M, N, batch);
     CUtensorMap ta, tb;
@@ -523,6 +540,12 @@ void gemm_gather(const Gather &g, int64_t M, const uint16_t *w, int64_t N, int64
   s.b_shared = 1;
   const bool glu = e.mode == EPI_CONV && e.act == 2;
   const int bn = bn_hint ? bn_hint : gather_bn(M, N, glu);
+  const double images = (double)M / ((double)g.Ho * g.Wo);
+  const double n_alg = e.mode == EPI_CONVTR ? (double)e.O * e.stride : (glu ? 2.0 * e.O : e.O);
+  const double out_elems = e.mode == EPI_CONVTR ? (double)M * e.O * e.stride : (double)M * e.O;
+  const double x_b = images * g.C * g.H * g.W * 4.0 * (g.x2 ? 2 : 1);
+  TraceScope ts(e.mode == EPI_CONVTR ? TR_CONVTR : TR_CONV, 2.0 * M * n_alg * g.K,
+                x_b + n_alg * g.K * 2.0 + out_elems * 4.0 * (e.res ? 2 : 1));
   if (!g_opt_simt) {
     CUtensorMap tb;
     // inner extent = the padded row length: padding columns are zero in every packed

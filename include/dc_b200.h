@@ -183,6 +183,13 @@ int dcb_set_option(const char *name, int value);
 uint64_t dcb_kernel_launches(void);
 /* Device-side fault word: bounded waits that expire set a bit here (0 = healthy). */
 uint32_t dcb_device_fault(int clear);
+/* Kernel-class trace: bit c of mask enables class c (0 implicit-GEMM conv, 1 stride-phase
+ * transposed conv, 2 transformer linear, 3 flash attention, 4 dk_gemm_half).  Every
+ * launch of an enabled class is bracketed by CUDA events on the backend stream and tagged
+ * with its algorithmic FLOPs and bytes; dcb_trace_stop synchronises and returns per-class
+ * totals (milliseconds, FLOPs, bytes, launches) for classes < ncls. */
+void dcb_trace_start(uint32_t mask);
+int dcb_trace_stop(double *ms, double *flops, double *bytes, int *launches, int ncls);
 
 typedef struct DcbModel DcbModel;
 /* Load weights (safetensors, F32/F16/BF16, MLX layout) + model JSON (defaults =

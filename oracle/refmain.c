@@ -52,14 +52,18 @@ int main(int argc, char **argv) {
   } else {
     int reps = argc > 8 ? atoi(argv[8]) : 1;
     double best = 1e30, total = 0;
+    printf("{\"times_s\": [");
     for (int r = 0; r < reps; r++) {
       double t0 = now_s();
       dcref_forward_plain(mix, B, C, T, out);
       double dt = now_s() - t0;
       total += dt;
       best = dt < best ? dt : best;
+      printf("%s%.6f", r ? ", " : "", dt);
+      fflush(stdout);
     }
-    printf("{\"best_s\": %.6f, \"mean_s\": %.6f, \"repeats\": %d}\n", best, total / reps, reps);
+    printf("], \"best_s\": %.6f, \"mean_s\": %.6f, \"repeats\": %d}\n", best, total / reps,
+           reps);
   }
   free(out);
   free(mix);
