@@ -33,6 +33,7 @@ BACKEND_SYMBOLS = [
     "dk_istft_frames", "dk_ola",
 ]
 FUSED_SYMBOLS = ["dkx_conv2d", "dkx_conv_tr", "dkx_linear", "dkx_attention"]
+NOALLOC_SYMBOLS = ["dk_row_stats_noalloc"]
 ENGINE_SYMBOLS = [
     "dcb_set_error_mode", "dcb_last_error", "dcb_set_stream", "dcb_use_own_stream",
     "dcb_get_stream",
@@ -42,7 +43,7 @@ ENGINE_SYMBOLS = [
     "dcb_forward", "dcb_stage_encoder", "dcb_stage_decoder", "dcb_stage_transformer",
     "dcb_apply_defaults", "dcb_apply", "dcb_apply_plan",
 ]
-ALL_SYMBOLS = BACKEND_SYMBOLS + FUSED_SYMBOLS + ENGINE_SYMBOLS
+ALL_SYMBOLS = BACKEND_SYMBOLS + NOALLOC_SYMBOLS + FUSED_SYMBOLS + ENGINE_SYMBOLS
 
 
 class DkStrided(C.Structure):
@@ -101,6 +102,7 @@ def lib(load_only: bool = False):
         "dk_scale_add": (None, [vp, vp, vp, i64, i64, i64]),
         "dk_reflect_pad": (None, [vp, vp, i64, i64, i64, i64]),
         "dk_row_stats": (None, [vp, i64, i64, vp, vp]),
+        "dk_row_stats_noalloc": (i32, [vp, i64, i64, vp, vp]),
         "dk_groupnorm_apply": (None, [vp, vp, vp, vp, vp, vp, i64, i64, i64, i64, f32, i32]),
         "dk_norm_apply_last": (None, [vp, vp, vp, vp, vp, vp, i64, i64, i64, f32]),
         "dk_affine_rows": (None, [vp, vp, vp, vp, i64, i64, f32, i32]),

@@ -108,6 +108,63 @@ void row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var)
   DCB_LAUNCHED();
 }
 
+// ---- allocation-free row statistics (dk_row_stats_noalloc)
+// Some hosts cannot let a library allocate device memory: a real-time audio thread that
+// must never block (cudaMalloc / cudaFree may synchronise the whole device), or a host
+// application that hands all device memory to its own pool and budgets it exactly.  For
+// them the chunk partials of the row statistics live in this fixed array instead of the
+// buffer row_stats grows with cudaMalloc.  It is reserved on every GPU that loads the
+// library, for the life of the process: 1 MiB = kNoAllocPartials (row, chunk) partials of
+// three doubles each.
+constexpr int64_t kNoAllocPartials = 43690;
+static __device__ __align__(256) double g_rowstat_noalloc[kNoAllocPartials * 3];
+
+// Device address of g_rowstat_noalloc, looked up once per device.  On the host the array's
+// name is only a stand-in for the device symbol, so kernels must be given this address.
+static double *g_rowstat_noalloc_ptr[64] = {nullptr};
+
+static double *rowstat_noalloc_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    fail("dk_row_stats_noalloc: no usable current CUDA device");
+    return nullptr;
+  }
+  if (!g_rowstat_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_rowstat_noalloc);
+    if (e != cudaSuccess || !p) {
+      fail("dk_row_stats_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+           cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_rowstat_noalloc_ptr[dev] = (double *)p;
+  }
+  return g_rowstat_noalloc_ptr[dev];
+}
+
+int row_stats_noalloc(const float *x, int64_t rows, int64_t L, float *mean, float *var) {
+  if (rows <= 0 || L <= 0) return 0;
+  const int64_t nchunks = (L + kStatChunk - 1) / kStatChunk;
+  if (rows * nchunks > kNoAllocPartials) {
+    fail("dk_row_stats_noalloc: %lld rows x %lld chunks of %d elements need %lld partials, "
+         "more than the %lld this entry point reserves; use dk_row_stats",
+         (long long)rows, (long long)nchunks, kStatChunk, (long long)(rows * nchunks),
+         (long long)kNoAllocPartials);
+    return -1;
+  }
+  double *part = rowstat_noalloc_ptr();
+  if (!part) return -1;
+  // every (row, chunk) slot used below is written by k_chunk_stats before k_combine_stats
+  // reads it, so the previous call's contents never leak into this one
+  dim3 grid((unsigned)nchunks, (unsigned)rows);
+  k_chunk_stats<<<grid, kStatThreads, 0, stream()>>>(x, L, (int)nchunks, part);
+  DCB_LAUNCHED();
+  k_combine_stats<<<grid_for(rows, 128, 1 << 30), 128, 0, stream()>>>(part, rows, (int)nchunks,
+                                                                     mean, var);
+  DCB_LAUNCHED();
+  return failed() ? -1 : 0;
+}
+
 __global__ void k_groupnorm(const float *__restrict__ x, float *__restrict__ y,
                             const float *__restrict__ mean, const float *__restrict__ var,
                             const float *__restrict__ w, const float *__restrict__ b, int64_t B,
@@ -252,6 +309,10 @@ extern "C" {
 
 void dk_row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var) {
   row_stats(x, rows, L, mean, var);
+}
+
+int dk_row_stats_noalloc(const float *x, int64_t rows, int64_t L, float *mean, float *var) {
+  return row_stats_noalloc(x, rows, L, mean, var);
 }
 
 void dk_groupnorm_apply(const float *x, float *y, const float *mean, const float *var,

@@ -128,6 +128,18 @@ void dk_istft_frames(const float *spec, float *frames, int64_t R, int nbins, int
 void dk_ola(const float *frames, float *out, int64_t R, int nframes, int n_fft, int hop,
             const float *window, int64_t start, int64_t length);                        /* :143 */
 
+/* Allocation-free variant of dk_row_stats.  No counterpart in the reference: it exists for
+ * callers that cannot let the library allocate device memory -- a real-time audio thread
+ * that must never block (cudaMalloc/cudaFree can synchronise the whole device) or a host
+ * that gives all device memory to its own pool.  Same results as dk_row_stats; the chunk
+ * partials live in a fixed 1 MiB device array that every GPU loading the library keeps
+ * until exit, so rows * ceil(L / 8192) must not exceed 43690 (larger calls are rejected
+ * with an error and return -1).  Calls no cudaMalloc/cudaFree.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) with that device current.
+ * All calls share the one array: calls that overlap on the GPU (different streams, or
+ * different host threads) race and must be serialised by the caller.  Returns 0 or -1. */
+int dk_row_stats_noalloc(const float *x, int64_t rows, int64_t L, float *mean, float *var);
+
 /* ======================================================== Part 2: fused entry points */
 
 /* Activation applied in a GEMM epilogue. */
