@@ -41,7 +41,7 @@ ENGINE_SYMBOLS = [
     "dcb_trace_stop", "dcb_model_load",
     "dcb_model_free", "dcb_model_info", "dcb_model_weight_bytes", "dcb_model_weight_block",
     "dcb_forward", "dcb_stage_encoder", "dcb_stage_decoder", "dcb_stage_transformer",
-    "dcb_apply_defaults", "dcb_apply", "dcb_apply_plan",
+    "dcb_apply_defaults", "dcb_apply", "dcb_apply_plan", "dcb_py_randint", "dcb_segment_plan",
 ]
 ALL_SYMBOLS = BACKEND_SYMBOLS + NOALLOC_SYMBOLS + FUSED_SYMBOLS + ENGINE_SYMBOLS
 
@@ -145,6 +145,9 @@ def lib(load_only: bool = False):
         "dcb_stage_decoder": (i32, [vp, i32, i32, vp, vp, i32, i32, i32, i32, i32, vp,
                                     C.POINTER(i32)]),
         "dcb_stage_transformer": (i32, [vp, vp, vp, i32, i32, i32, i32, i32]),
+        "dcb_py_randint": (i32, [C.c_uint64, i32, i32, i32, C.POINTER(i32)]),
+        "dcb_segment_plan": (i32, [i32, f32, i32, C.POINTER(DcbApplyOpts), C.POINTER(i32),
+                                   C.POINTER(i32), i32]),
         "dcb_apply_defaults": (None, [C.POINTER(DcbApplyOpts)]),
         "dcb_apply": (i32, [vp, vp, i32, i32, vp, C.POINTER(DcbApplyOpts)]),
         "dcb_apply_plan": (i32, [vp, i32, C.POINTER(DcbApplyOpts), C.POINTER(i32),
@@ -344,6 +347,34 @@ def gemm_half(A, B, C_=None, alpha=1.0, beta=0.0):
                        beta, _ptr(C_), C_.stride(1), C_.stride(0), batch)
     check(True, "dk_gemm_half")
     return C_
+
+
+def apply_opts(shifts=1, overlap=0.25, transition_power=1.0, batch_size=8, seed=1,
+               use_seed=False, shard_index=0, shard_count=1):
+    o = DcbApplyOpts()
+    lib(load_only=True).dcb_apply_defaults(C.byref(o))
+    o.shifts, o.split, o.overlap = shifts, 1, overlap
+    o.transition_power, o.batch_size = transition_power, batch_size
+    o.seed, o.use_seed = seed, int(use_seed)
+    o.shard_index, o.shard_count = shard_index, shard_count
+    return o
+
+
+def py_randint(seed: int, lo: int, hi: int, n: int):
+    """CPython random.Random(seed).randint draws as the engine computes them (host only)."""
+    out = (C.c_int * n)()
+    lib(load_only=True).dcb_py_randint(seed, lo, hi, n, out)
+    return list(out)
+
+
+def segment_plan(length: int, samplerate=44100, segment=7.8, **kw):
+    """(offsets, call index per offset on this shard or -1) of the engine's scheduler."""
+    o = apply_opts(**kw)
+    L = lib(load_only=True)
+    n = L.dcb_segment_plan(samplerate, segment, length, C.byref(o), None, None, 0)
+    offs, calls = (C.c_int * n)(), (C.c_int * n)()
+    L.dcb_segment_plan(samplerate, segment, length, C.byref(o), offs, calls, n)
+    return list(offs), list(calls)
 
 
 def set_option(name: str, value: int) -> int:

@@ -929,6 +929,37 @@ void dcb_apply_defaults(DcbApplyOpts *o) {
   o->shard_count = 1;
 }
 
+int dcb_py_randint(uint64_t seed, int lo, int hi, int n, int *out) {
+  if (hi < lo || n < 0 || !out) return -1;
+  Mt rng;
+  rng.seed(seed);
+  for (int i = 0; i < n; i++) out[i] = rng.randint(lo, hi);
+  return 0;
+}
+
+int dcb_segment_plan(int samplerate, float segment, int length, const DcbApplyOpts *o,
+                     int *offsets, int *call_of, int cap) {
+  if (!o || length <= 0) return -1;
+  Cfg c;
+  c.samplerate = samplerate;
+  c.segment = segment;
+  Plan p = make_plan(c, length, *o);
+  if (p.stride <= 0) return -1;
+  const int n = (int)p.offsets.size();
+  if (n > cap) return n;
+  for (int i = 0; i < n; i++) {
+    offsets[i] = p.offsets[i];
+    call_of[i] = -1;
+  }
+  int call = 0;
+  for (auto &b : p.full_batches) {
+    for (int i : b) call_of[i] = call;
+    call++;
+  }
+  for (int i : p.tails) call_of[i] = call++;
+  return n;
+}
+
 int dcb_apply_plan(DcbModel *m, int T, const DcbApplyOpts *o, int *n_forwards, int *n_batched) {
   if (!m || !o) return -1;
   int len = T;

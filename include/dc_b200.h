@@ -251,6 +251,16 @@ typedef struct {
 void dcb_apply_defaults(DcbApplyOpts *o);
 /* mix [B][C][T] (device) -> out [B][S][C][T] (device). Returns 0 or -1. */
 int dcb_apply(DcbModel *m, const float *mix, int B, int T, float *out, const DcbApplyOpts *o);
+/* Host-only pieces of the scheduler (no GPU needed):
+ * dcb_py_randint: n draws of CPython's random.Random(seed).randint(lo, hi), the shift
+ *   generator of apply.c:5-107;
+ * dcb_segment_plan: the segment offsets of a track (apply.c:223-237) and, per offset, the
+ *   index of the forward call that runs it on this shard (full segments batched up to
+ *   batch_size, tails alone; -1 = another shard's segment).  Returns the offset count (the
+ *   arrays are filled only if it is <= cap). */
+int dcb_py_randint(uint64_t seed, int lo, int hi, int n, int *out);
+int dcb_segment_plan(int samplerate, float segment, int length, const DcbApplyOpts *o,
+                     int *offsets, int *call_of, int cap);
 /* Number of forward passes dcb_apply would run for a track of T samples. */
 int dcb_apply_plan(DcbModel *m, int T, const DcbApplyOpts *o, int *n_forwards, int *n_batched);
 

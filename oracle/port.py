@@ -588,8 +588,10 @@ def segment_plan(length, cfg: Config, overlap=0.25, batch_size=8):
 
 
 def apply_model(mix, W, cfg: Config, shifts=1, overlap=0.25, transition_power=1.0,
-                batch_size=8, seed=1, forward_fn=None):
-    """dc_apply_model (apply.c:179-306) with split=True."""
+                batch_size=8, seed=1, forward_fn=None, shard=(0, 1)):
+    """dc_apply_model (apply.c:179-306) with split=True.  shard = (index, count) keeps only
+    the segments i with i % count == index (the weight sum stays global), so the shards'
+    outputs add up to the unsharded result -- the data-parallel split the engine uses."""
     fwd = forward_fn or (lambda x: forward(x, W, cfg))
     B, C, length = mix.shape
     if shifts > 0:
@@ -602,15 +604,22 @@ def apply_model(mix, W, cfg: Config, shifts=1, overlap=0.25, transition_power=1.
             shifted = padded_chunk(padded, off, length + max_shift - off,
                                    length + max_shift - off)
             out = apply_model(shifted, W, cfg, 0, overlap, transition_power, batch_size,
-                              seed, forward_fn)
+                              seed, forward_fn, shard)
             tr = out[..., max_shift - off:]
             acc = tr if acc is None else (acc + tr).astype(F32)
         return (acc * F32(1.0 / shifts)).astype(F32)
     seg, stride, offsets, batches = segment_plan(length, cfg, overlap, batch_size)
     weight = ola_weight(seg, transition_power)
     sumw = np.zeros(length, dtype=np.float64)
+    for off in offsets:  # every segment's weight, whichever shard runs it
+        n = min(seg, length - off)
+        sumw[off:off + n] += weight[:n]
     out = np.zeros((B, cfg.n_sources, C, length), dtype=F32)
+    si, sc = shard
     for kind, idxs in batches:
+        idxs = [i for i in idxs if i % sc == si]
+        if not idxs:
+            continue
         if kind == "full":
             flat = np.concatenate([padded_chunk(mix, offsets[i], seg, cfg.valid_length)
                                    for i in idxs], axis=0)
@@ -619,7 +628,6 @@ def apply_model(mix, W, cfg: Config, shifts=1, overlap=0.25, transition_power=1.
                 off = offsets[i]
                 yk = center_trim(y[k * B:(k + 1) * B], seg)
                 out[..., off:off + seg] += (yk * weight).astype(F32)
-                sumw[off:off + seg] += weight
         else:
             i = idxs[0]
             this = length - offsets[i]
@@ -627,6 +635,5 @@ def apply_model(mix, W, cfg: Config, shifts=1, overlap=0.25, transition_power=1.
             y = fwd(padded_chunk(mix, offsets[i], this, valid))
             yk = center_trim(y, this)
             out[..., offsets[i]:] += (yk * weight[:this]).astype(F32)
-            sumw[offsets[i]:] += weight[:this]
     inv = np.where(sumw > 0, 1.0 / np.where(sumw > 0, sumw, 1), 0).astype(F32)
     return (out * inv).astype(F32)
