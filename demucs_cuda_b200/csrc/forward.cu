@@ -168,7 +168,11 @@ static void conv_tr(const ConvW &cw, const float *x, const Img &in, bool axis_h,
 // the time branch).
 static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
   const Img v = freq_rows(B, C, Fr, T);
-  float *stat = dalloc((size_t)B * Fr * 2);
+  const unsigned rows = (unsigned)((int64_t)B * Fr);
+  // one CTA per row when there are many short rows (frequency branch); chunked statistics
+  // across CTAs when a few rows are long (time branch, lowest frequency level)
+  const bool fused = rows >= 128 && (int64_t)2 * C * T <= (256 << 10);
+  float *stat = fused ? nullptr : dalloc((size_t)rows * 2);
   for (int d = 0; d < E.ndconv; d++) {
     const DConvW &dw = E.dconv[d];
     const int dil = 1 << d;
@@ -177,13 +181,17 @@ static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
     float *h = dalloc((size_t)B * hid * Fr * T);
     const Img hv = freq_rows(B, hid, Fr, T);
     conv(dw.c0, y, nullptr, v, 1, 1, 0, dil, 1, dil, 1, T, h, hv, 0);
-    // GroupNorm(1) + GELU
+    // GroupNorm(1) + GELU, in place
     RowView rh{h, Fr, (int64_t)hid * Fr * T, T, (int64_t)Fr * T, hid, T};
-    rowview_stats(rh, B, 1e-5f, stat, stat + (size_t)B * Fr, nullptr);
-    {
+    if (fused) {
+      k_gn_fused<0><<<rows, kGnFusedThreads, 0, stream()>>>(rh, h, dw.gn1.w, dw.gn1.b,
+                                                            nullptr, 0, 0, 0, 1e-5f);
+      DCB_LAUNCHED();
+    } else {
+      rowview_stats(rh, B, 1e-5f, stat, stat + rows, nullptr);
       const int64_t n = (int64_t)B * hid * Fr * T;
-      k_gn_gelu<<<grid_for(n, 256), 256, 0, stream()>>>(rh, h, stat, stat + (size_t)B * Fr,
-                                                       dw.gn1.w, dw.gn1.b, B);
+      k_gn_gelu<<<grid_for(n, 256), 256, 0, stream()>>>(rh, h, stat, stat + rows, dw.gn1.w,
+                                                       dw.gn1.b, B);
       DCB_LAUNCHED();
     }
     // conv 1x1 -> z [B, 2C, Fr, T]
@@ -193,12 +201,16 @@ static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
     dfree(h);
     // GroupNorm(1) + GLU, LayerScale residual into y
     RowView rz{z, Fr, (int64_t)C2 * Fr * T, T, (int64_t)Fr * T, C2, T};
-    rowview_stats(rz, B, 1e-5f, stat, stat + (size_t)B * Fr, nullptr);
-    {
+    if (fused) {
+      k_gn_fused<1><<<rows, kGnFusedThreads, 0, stream()>>>(
+          rz, y, dw.gn4.w, dw.gn4.b, dw.scale, (int64_t)C * Fr * T, T, (int64_t)Fr * T, 1e-5f);
+      DCB_LAUNCHED();
+    } else {
+      rowview_stats(rz, B, 1e-5f, stat, stat + rows, nullptr);
       const int64_t n = (int64_t)B * (C2 / 2) * Fr * T;
       k_gn_glu_res<<<grid_for(n, 256), 256, 0, stream()>>>(
-          rz, stat, stat + (size_t)B * Fr, dw.gn4.w, dw.gn4.b, dw.scale, y,
-          (int64_t)C * Fr * T, T, (int64_t)Fr * T, B);
+          rz, stat, stat + rows, dw.gn4.w, dw.gn4.b, dw.scale, y, (int64_t)C * Fr * T, T,
+          (int64_t)Fr * T, B);
       DCB_LAUNCHED();
     }
     dfree(z);

@@ -24,7 +24,6 @@
 
 namespace dcb {
 
-constexpr int kThreads = 192;
 constexpr int kBM = 128, kBK = 64;
 constexpr uint32_t kATileBytes = kBM * kBK * 2;
 
@@ -138,9 +137,89 @@ static __device__ __forceinline__ void store_glu(const Epi &e, int64_t o, const 
   e.y[off] = val;
 }
 
+// 16 consecutive accumulator columns of one row: vectorised stores where the layout allows
+// (e.vec, checked on the host), element stores otherwise
+static __device__ __forceinline__ void store_chunk16(const Epi &e, const Shape &s, int bz,
+                                                     int64_t m, int64_t n0, const RowInfo &ri,
+                                                     const float (&v)[16]) {
+  if (e.vec && n0 + 16 <= s.N) {
+    if (e.mode == EPI_ROWS_F32) {
+      float o[16];
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        float val = v[i] + (e.bias ? e.bias[n0 + i] : 0.f);
+        if (e.act == 1) val = gelu_f(val);
+        o[i] = val;
+      }
+      if (e.res) {
+        const float4 *rp = (const float4 *)(e.res + m * e.ldr + n0);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float4 r = rp[j];
+          o[4 * j] = r.x + e.gamma[n0 + 4 * j] * o[4 * j];
+          o[4 * j + 1] = r.y + e.gamma[n0 + 4 * j + 1] * o[4 * j + 1];
+          o[4 * j + 2] = r.z + e.gamma[n0 + 4 * j + 2] * o[4 * j + 2];
+          o[4 * j + 3] = r.w + e.gamma[n0 + 4 * j + 3] * o[4 * j + 3];
+        }
+      }
+      float4 *op = (float4 *)((float *)e.out + m * e.ldo + n0);
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        op[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+      return;
+    }
+    if (e.mode == EPI_ROWS_F16 || e.mode == EPI_HEADS) {
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        float a = v[i] + (e.bias ? e.bias[n0 + i] : 0.f);
+        float b = v[i + 1] + (e.bias ? e.bias[n0 + i + 1] : 0.f);
+        if (e.act == 1) {
+          a = gelu_f(a);
+          b = gelu_f(b);
+        }
+        w[i >> 1] = pack_h2(a, b);
+      }
+      uint16_t *dst;
+      if (e.mode == EPI_ROWS_F16) {
+        dst = (uint16_t *)e.out + m * e.ldo + n0;
+      } else {
+        // a 16-column chunk lies inside one section and one head (hd % 16 == 0)
+        const int sec = (int)(n0 / e.sec_cols);
+        const int cc = (int)(n0 - (int64_t)sec * e.sec_cols);
+        const int h = cc / e.hd, d0 = cc - h * e.hd;
+        const int64_t bh = (int64_t)ri.b * e.heads + h;
+        if (e.sec_layout[sec] != 0) {
+          uint16_t *col = e.sec_ptr[sec] + (bh * e.hd + d0) * e.Tp + ri.t;
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            col[(2 * i) * e.Tp] = (uint16_t)(w[i] & 0xffffu);
+            col[(2 * i + 1) * e.Tp] = (uint16_t)(w[i] >> 16);
+          }
+          return;
+        }
+        dst = e.sec_ptr[sec] + (bh * e.T + ri.t) * e.hd + d0;
+      }
+      uint4 *dp = (uint4 *)dst;
+      dp[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dp[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      return;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; i++) {
+    if (n0 + i < s.N) store_elem(e, s, bz, m, n0 + i, ri, v[i]);
+  }
+}
+
 // ------------------------------------------------------------- tensor-core kernel
+constexpr int kProdWarps = 8;             // warps 0-7: gather producers, then epilogue
+constexpr int kTmaWarp = kProdWarps;      // warp 8
+constexpr int kMmaWarp = kProdWarps + 1;  // warp 9
+constexpr int kThreads = 32 * (kProdWarps + 2);
+
 template <int BN, bool GATHER>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     k_umma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
            const Shape s, const Gather g, const Epi e) {
   extern __shared__ uint8_t smem_raw[];
@@ -167,13 +246,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; i++) {
-      mbar_init(&full[i], 1 + (GATHER ? 4 : 0));
+      mbar_init(&full[i], 1 + (GATHER ? kProdWarps : 0));
       mbar_init(&empty[i], 1);
     }
     mbar_init(done, 1);
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(tslot, (uint32_t)s.tmem_cols);
     tmem_relinquish();
   }
@@ -198,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tslot;
 
-  if (warp == 4) {
+  if (warp == kTmaWarp) {
     if (lane == 0) {
       tma_prefetch_desc(&tmB);
       if (!GATHER) tma_prefetch_desc(&tmA);
@@ -213,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!GATHER) tma_load_3d(sA + st * kATileBytes, &tmA, &full[st], kb * kBK, (int)m0, cA);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {
       const uint32_t idesc = idesc_f16_f32(kBM, BN);
       for (int kb = 0; kb < s.nkb; kb++) {
@@ -233,8 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       umma_commit(done);
     }
   } else {
-    // ---------------- warps 0-3: gather producer (optional), then the epilogue
-    const int r = threadIdx.x;  // tile row 0..127
+    // ---- warps 0-7: warp w serves TMEM lane quarter (w & 3) = tile rows 32(w&3)..+31
+    // and half (w >> 2) of the K columns (gather) / accumulator columns (epilogue)
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;  // tile row 0..127
     if (GATHER) {
       const int64_t p = m0 + r;
       int64_t base = 0;
@@ -250,23 +331,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float *__restrict__ x = g.x;
       const float *__restrict__ x2 = g.x2;
+      constexpr int KH2 = kBK / 2;  // 32 columns of each K block per thread
       for (int kb = 0; kb < s.nkb; kb++) {
         const int st = kb % stages;
         const uint32_t ph = (uint32_t)(kb / stages) & 1u;
         if (!mbar_wait(&empty[st], ph ^ 1u, kFaultEmpty)) break;
-        float v[kBK];
+        const int2 *kt = ktab + kb * kBK + half * KH2;
+        float v[KH2];
         if (x2) {
 #pragma unroll
-          for (int i = 0; i < kBK; i++) {
-            const int2 t = ktab[kb * kBK + i];
+          for (int i = 0; i < KH2; i++) {
+            const int2 t = kt[i];
             const int hh = h0 + (t.y & 0xffff), ww = w0 + (t.y >> 16);
             const bool ok = (unsigned)hh < (unsigned)g.H && (unsigned)ww < (unsigned)g.W;
             v[i] = ok ? __ldg(x + base + t.x) + __ldg(x2 + base + t.x) : 0.f;
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < kBK; i++) {
-            const int2 t = ktab[kb * kBK + i];
+          for (int i = 0; i < KH2; i++) {
+            const int2 t = kt[i];
             const int hh = h0 + (t.y & 0xffff), ww = w0 + (t.y >> 16);
             const bool ok = (unsigned)hh < (unsigned)g.H && (unsigned)ww < (unsigned)g.W;
             v[i] = ok ? __ldg(x + base + t.x) : 0.f;
@@ -274,8 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t a_base = smem_u32(sA + st * kATileBytes);
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
-          st_shared_v4(a_base + sw128_off(r, c), pack_h2(v[8 * c], v[8 * c + 1]),
+        for (int c = 0; c < 4; c++) {
+          st_shared_v4(a_base + sw128_off(r, half * 4 + c), pack_h2(v[8 * c], v[8 * c + 1]),
                        pack_h2(v[8 * c + 2], v[8 * c + 3]), pack_h2(v[8 * c + 4], v[8 * c + 5]),
                        pack_h2(v[8 * c + 6], v[8 * c + 7]));
         }
@@ -290,10 +373,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t m = m0 + r;
     const bool mv = m < s.M;
     const RowInfo ri = mv ? decode_row(e, m) : RowInfo{0, 0, 0, 0, 0};
-    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
     if (e.mode == EPI_CONV && e.act == 2) {
       const int hb = e.glu_half;
-      for (int c0 = 0; c0 < hb; c0 += 16) {
+      // the a-columns of this tile split between the two warp halves in 16-column steps
+      const int per = hb >= 32 ? hb / 2 : (half == 0 ? hb : 0);
+      const int c_beg = hb >= 32 ? half * per : 0;
+      for (int c0 = c_beg; c0 < c_beg + per; c0 += 16) {
         float va[16], vb[16];
         tmem_ld16(trow + c0, va);
         tmem_ld16(trow + hb + c0, vb);
@@ -304,24 +390,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     } else {
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      constexpr int PER = BN / 2;  // >= 16
+      for (int c0 = half * PER; c0 < half * PER + PER; c0 += 16) {
         float v[16];
         tmem_ld16(trow + c0, v);
         tmem_wait_ld();
-        if (mv) {
-#pragma unroll
-          for (int i = 0; i < 16; i++) {
-            const int64_t n = (int64_t)n0 + c0 + i;
-            if (n < s.N) store_elem(e, s, bz, m, n, ri, v[i]);
-          }
-        }
+        if (mv) store_chunk16(e, s, bz, m, (int64_t)n0 + c0, ri, v);
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, (uint32_t)s.tmem_cols);
   }
@@ -418,6 +499,25 @@ static bool encode_map(CUtensorMap *map, const void *base, uint64_t inner, uint6
   return r == CUDA_SUCCESS;
 }
 
+static bool al16(const void *p) { return ((uintptr_t)p & 15) == 0; }
+
+// can the epilogue store 16 consecutive columns with vector instructions?
+static bool vec_ok(const Epi &e, int64_t N) {
+  if (N % 16) return false;
+  switch (e.mode) {
+    case EPI_ROWS_F32:
+      return al16(e.out) && e.ldo % 4 == 0 && (!e.res || (al16(e.res) && e.ldr % 4 == 0));
+    case EPI_ROWS_F16:
+      return al16(e.out) && e.ldo % 8 == 0;
+    case EPI_HEADS:
+      for (int i = 0; i < 3; i++)
+        if (e.sec_ptr[i] && !al16(e.sec_ptr[i])) return false;
+      return e.hd % 16 == 0 && e.sec_cols % 16 == 0;
+    default:
+      return false;
+  }
+}
+
 static int pick_bn(int64_t M, int64_t N, int64_t batch) {
   int bn = 32;
   while (bn < 256 && bn < N) bn *= 2;
@@ -437,10 +537,12 @@ static void launch_umma(const CUtensorMap &ta, const CUtensorMap &tb, Shape s, c
                         const Epi &e, int64_t mtiles, int ntiles, int64_t batch) {
   const size_t table = GATHER ? (size_t)s.nkb * kBK * sizeof(int2) : 0;
   const size_t stage_bytes = kATileBytes + (size_t)BN * 128;
-  const size_t budget = 200 * 1024;
-  int stages = (int)((budget - table - 2048) / stage_bytes);
-  if (stages > 6) stages = 6;
-  if (stages > s.nkb + 1) stages = s.nkb + 1 > 2 ? s.nkb + 1 : 2;
+  // two CTAs per SM (TMEM <= 256 columns and <= ~110 KB shared memory each) so one
+  // CTA's gather / epilogue overlaps the other's MMAs
+  const size_t budget = 110 * 1024;
+  int stages = budget > table + 2048 ? (int)((budget - table - 2048) / stage_bytes) : 0;
+  if (stages > 8) stages = 8;
+  if (stages > s.nkb + 1) stages = s.nkb + 1;
   if (stages < 2) stages = 2;
   s.stages = stages;
   const size_t smem = 1024 + stages * stage_bytes + (2 * stages + 1) * 8 + 16 + table;
@@ -520,7 +622,9 @@ void gemm_rows_launch(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t
         encode_map(&tb, b.p, (uint64_t)K, (uint64_t)N, s.b_shared ? 1 : (uint64_t)batch,
                    (uint64_t)b.ld, (uint64_t)b.stride, (uint32_t)bn);
     if (ok) {
-      dispatch_umma<false>(bn, ta, tb, s, g, e, batch);
+      Epi ev = e;
+      ev.vec = vec_ok(e, N) ? 1 : 0;
+      dispatch_umma<false>(bn, ta, tb, s, g, ev, batch);
       return;
     }
   }

@@ -34,6 +34,7 @@ enum EpiMode : int {
 
 struct Epi {
   int mode = EPI_GEMM;
+  int vec = 0;  // 16-column vector stores allowed (set by the launcher after checks)
   const float *bias = nullptr;
   int act = 0;  // 0 none, 1 gelu, 2 glu
   // EPI_GEMM

@@ -166,6 +166,79 @@ __global__ void k_gn_glu_res(RowView v, const float *__restrict__ mean,
   }
 }
 
+// GroupNorm(1) of one strided row per CTA, fused with its consumer (DConv,
+// layers.c:31-44): statistics over the row's C x T elements in double (sum and sum of
+// squares; the reference's two passes in double agree to ~1e-15 for these magnitudes),
+// then a second pass over the now L2-resident row applies
+//   mode 0:  y = GELU(GN(x))                            (same layout as x, in place allowed)
+//   mode 1:  res[c] += scale[c] * GN(x)[c] * sigmoid(GN(x)[c + C/2]),  c < C/2
+constexpr int kGnFusedThreads = 256;
+
+template <int MODE>
+__global__ void __launch_bounds__(kGnFusedThreads)
+    k_gn_fused(RowView v, float *__restrict__ y, const float *__restrict__ w,
+               const float *__restrict__ bb, const float *__restrict__ scale, int64_t rsB,
+               int64_t rsF, int64_t rsC, float eps) {
+  __shared__ double sh[2][kGnFusedThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int64_t b = row / v.Fr, f = row - b * v.Fr;
+  const float *xr = v.x + b * v.sB + f * v.sF;
+  double s = 0.0, ss = 0.0;
+  for (int c = 0; c < v.C; c++) {
+    const float *xc = xr + c * v.sC;
+    for (int t = threadIdx.x; t < v.T; t += kGnFusedThreads) {
+      const double a = (double)xc[t];
+      s += a;
+      ss += a * a;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  }
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sh[0][wid] = s;
+    sh[1][wid] = ss;
+  }
+  __syncthreads();
+  s = 0.0;
+  ss = 0.0;
+  for (int i = 0; i < kGnFusedThreads / 32; i++) {
+    s += sh[0][i];
+    ss += sh[1][i];
+  }
+  const double n = (double)v.C * v.T;
+  const double md = s / n;
+  double vd = ss / n - md * md;
+  if (vd < 0.0) vd = 0.0;
+  const float m = (float)md;
+  const float rs = 1.0f / sqrtf((float)vd + eps);
+  if (MODE == 0) {
+    float *yr = y + b * v.sB + f * v.sF;
+    for (int c = 0; c < v.C; c++) {
+      const float *xc = xr + c * v.sC;
+      float *yc = yr + c * v.sC;
+      const float wc = w[c], bc = bb[c];
+      for (int t = threadIdx.x; t < v.T; t += kGnFusedThreads)
+        yc[t] = gelu_f((xc[t] - m) * rs * wc + bc);
+    }
+  } else {
+    const int H = v.C / 2;
+    float *rr = y + b * rsB + f * rsF;
+    for (int c = 0; c < H; c++) {
+      const float *xa = xr + c * v.sC, *xb = xr + (c + H) * v.sC;
+      float *rc = rr + c * rsC;
+      const float wa = w[c], ba = bb[c], wb = w[c + H], bbv = bb[c + H], sc = scale[c];
+      for (int t = threadIdx.x; t < v.T; t += kGnFusedThreads) {
+        const float na = (xa[t] - m) * rs * wa + ba;
+        const float nb = (xb[t] - m) * rs * wb + bbv;
+        rc[t] = rc[t] + na * sigmoid_f(nb) * sc;
+      }
+    }
+  }
+}
+
 // x[b][c][f][t] += emb[f][c] * alpha   (dc_add_freq_emb, htdemucs.c:114-134)
 __global__ void k_add_freq_emb(float *x, const float *__restrict__ emb, float alpha, int B,
                                int C, int Fr, int T, int emb_cols) {
