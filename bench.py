@@ -272,6 +272,8 @@ def b200_arm(args):
         e1.record()
         torch.cuda.synchronize()
         tr = dcb.trace_stop() if trace else None
+        if trace and args.trace_csv and rank == 0:
+            dcb.trace_dump(args.trace_csv)
         launches = dcb.kernel_launches() - n0
         ms = e0.elapsed_time(e1) / steps
         if world > 1:
@@ -392,6 +394,8 @@ def main():
     ap.add_argument("--shifts", type=int, default=1)
     ap.add_argument("--overlap", type=float, default=0.25)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--trace-csv", default="", help="write every traced GEMM-family launch "
+                    "of the timed region (class, ms, FLOPs, bytes, M, N, K) to this CSV")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)

@@ -38,7 +38,7 @@ ENGINE_SYMBOLS = [
     "dcb_set_error_mode", "dcb_last_error", "dcb_set_stream", "dcb_use_own_stream",
     "dcb_get_stream",
     "dcb_set_option", "dcb_kernel_launches", "dcb_device_fault", "dcb_trace_start",
-    "dcb_trace_stop", "dcb_model_load",
+    "dcb_trace_stop", "dcb_trace_dump", "dcb_model_load",
     "dcb_model_free", "dcb_model_info", "dcb_model_weight_bytes", "dcb_model_weight_block",
     "dcb_forward", "dcb_stage_encoder", "dcb_stage_decoder", "dcb_stage_transformer",
     "dcb_apply_defaults", "dcb_apply", "dcb_apply_plan", "dcb_py_randint", "dcb_segment_plan",
@@ -134,6 +134,7 @@ def lib(load_only: bool = False):
         "dcb_trace_start": (None, [C.c_uint32]),
         "dcb_trace_stop": (i32, [C.POINTER(C.c_double), C.POINTER(C.c_double),
                                  C.POINTER(C.c_double), C.POINTER(i32), i32]),
+        "dcb_trace_dump": (i32, [C.c_char_p]),
         "dcb_model_load": (vp, [C.c_char_p, C.c_char_p]),
         "dcb_model_free": (None, [vp]),
         "dcb_model_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32),
@@ -404,6 +405,10 @@ def trace_stop():
     check(True, "trace")
     return {c: {"ms": ms[i], "flops": fl[i], "bytes": by[i], "launches": ln[i]}
             for i, c in enumerate(TRACE_CLASSES)}
+
+
+def trace_dump(path: str) -> int:
+    return lib().dcb_trace_dump(path.encode())
 
 
 def device_fault(clear: bool = True) -> int:

@@ -5,12 +5,14 @@
 //
 // CTA = 128 query rows of one head, 192 threads:
 //   warps 0-3  one query row per thread: read the S row from TMEM, online softmax in fp32
-//              (running max / sum, rescale of the output accumulator kept in registers),
-//              write P as fp16 into shared memory in the UMMA A-operand layout, then fold
-//              the P V block product (read back from TMEM) into the accumulator;
+//              (exp2 domain, running max / sum; the O accumulator stays in TMEM and is
+//              rescaled there only when the maximum grows by more than 2^8), write P as
+//              fp16 into shared memory in the UMMA A-operand layout;
 //   warp 4     TMA producer: Q once, then K and V^T tiles of 128 keys into a 2-stage ring;
 //   warp 5     TMEM owner; lane 0 issues S = Q K^T (M=128, N=128, K=64) and
-//              O_blk = P V (M=128, N=64, K=128).
+//              O += P V (M=128, N=64, K=128) accumulating in TMEM over all key blocks.
+// 112 KB of shared memory and ~100 registers per thread: two CTAs share an SM, so one
+// CTA's softmax overlaps the other's MMAs.
 // Head dims up to 64 are zero-extended to 64 by TMA out-of-bounds fill; keys past Tk read
 // as zero and are masked out of the softmax.
 //
@@ -40,11 +42,12 @@ struct AttnArgs {
   float *o32;     // [B][Tq][H*hd] fp32 (may be null)
 };
 
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __launch_bounds__(kAttnThreads, 2)
     k_flash_attn(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  // dynamic shared memory only (no static), 1024-aligned for the SW128 operand tiles, so
+  // two CTAs fit on one SM
+  extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *sQ = smem;
   uint8_t *sK = sQ + kQBytes;
   uint8_t *sV = sK + kAttnStages * kKBytes;
@@ -56,14 +59,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t *s_full = kv_empty + kAttnStages;
   uint64_t *p_full = s_full + 1;
   uint64_t *o_full = p_full + 1;
-  uint64_t *o_free = o_full + 1;
-  uint32_t *tslot = (uint32_t *)(o_free + 1);
+  uint32_t *tslot = (uint32_t *)(o_full + 1);
+  uint32_t *s_abort = tslot + 1;
 
-  // a fault recorded by an earlier kernel: end this grid at once (uniform CTA decision)
-  __shared__ uint32_t s_abort;
-  if (threadIdx.x == 0) s_abort = fault_pending() ? 1u : 0u;
+  // a fault recorded by an earlier kernel, or a misaligned window: end this grid at once
+  if (threadIdx.x == 0) {
+    uint32_t ab = fault_pending() ? 1u : 0u;
+    if (smem_u32(smem) & 1023u) {
+      atomicOr(&g_dev_fault, kFaultAttn);
+      ab = 1u;
+    }
+    *s_abort = ab;
+  }
   __syncthreads();
-  if (s_abort) return;
+  if (*s_abort) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, bh = blockIdx.y;
   const int q0 = qt * kQ;
@@ -78,7 +87,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(s_full, 1);
     mbar_init(p_full, 4);
     mbar_init(o_full, 1);
-    mbar_init(o_free, 4);
     fence_mbar_init();
   }
   if (warp == 5) {
@@ -118,33 +126,36 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int st = j % kAttnStages;
         const uint32_t ph = (uint32_t)(j / kAttnStages) & 1u;
         if (!mbar_wait(&kv_full[st], ph, kFaultAttn)) break;
-        if (j > 0 && !mbar_wait(o_free, (uint32_t)(j - 1) & 1u, kFaultAttn)) break;
         tc_fence_after();
+        // S(j) may overwrite S(j-1): the softmax warps finished reading it before they
+        // arrived on p_full(j-1), which this thread waited for before PV(j-1)
         const uint64_t kd = sw128_desc(smem_u32(sK + st * kKBytes));
 #pragma unroll
         for (int k = 0; k < kHD / 16; k++) umma_f16(tS, qd + 2u * k, kd + 2u * k, id_s, k > 0);
         umma_commit(s_full);
         if (!mbar_wait(p_full, (uint32_t)j & 1u, kFaultAttn)) break;
         tc_fence_after();
+        // O += P(j) V(j); O lives in TMEM across all key blocks
 #pragma unroll
         for (int k = 0; k < kKV / 16; k++) {
           const uint32_t half = (uint32_t)(k >> 2) * (kPBytes / 2);
           const uint32_t vhalf = (uint32_t)(k >> 2) * (kVBytes / 2);
           const uint64_t pd = sw128_desc(smem_u32(sP) + half) + 2u * (k & 3);
           const uint64_t vd = sw128_desc(smem_u32(sV + st * kVBytes) + vhalf) + 2u * (k & 3);
-          umma_f16(tO, pd, vd, id_o, k > 0);
+          umma_f16(tO, pd, vd, id_o, (j > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(o_full);
         umma_commit(&kv_empty[st]);
       }
+      umma_commit(o_full);
     }
   } else {
-    // softmax / accumulate warps: one query row per thread
+    // softmax warps: one query row per thread, exp2 domain (scores pre-multiplied by
+    // scale * log2 e).  The running maximum m is only raised, and O (in TMEM) rescaled,
+    // when a block's maximum exceeds it by more than 8 (a factor 256): probabilities stay
+    // <= 256, well inside fp16, and most blocks need no rescale.
     const int r = threadIdx.x;
     const uint32_t lrow = (uint32_t)(warp * 32) << 16;
-    float o[kHD];
-#pragma unroll
-    for (int d = 0; d < kHD; d++) o[d] = 0.f;
+    const float sl2 = a.scale * 1.4426950408889634f;
     float m_run = -INFINITY, l_run = 0.f;
     const uint32_t p_base = smem_u32(sP);
     bool ok = true;
@@ -155,9 +166,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       tc_fence_after();
       const int kbase = j * kKV;
-      // pass 1: block max of scale * s (S is re-read from TMEM in pass 2 rather than
-      // held in registers)
-      float mx = m_run;
+      float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < kKV; c += 16) {
         float v[16];
@@ -165,13 +174,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 16; i++) {
-          if (kbase + c + i < a.Tk) mx = fmaxf(mx, v[i] * a.scale);
+          if (kbase + c + i < a.Tk) mx = fmaxf(mx, v[i] * sl2);
         }
       }
-      const float alpha = (m_run == -INFINITY) ? 0.f : expf(m_run - mx);
-      m_run = mx;
+      if (mx > m_run + 8.0f) {
+        if (j > 0) {
+          // rescale the accumulated O row and the running sum to the new maximum; every
+          // earlier PV has completed (s_full(j) was committed after them)
+          const float alpha = exp2f(m_run - mx);
+          l_run *= alpha;
+#pragma unroll
+          for (int c = 0; c < kHD; c += 16) {
+            float ov[16];
+            tmem_ld16(tO + lrow + c, ov);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; i++) ov[i] *= alpha;
+            tmem_st16(tO + lrow + c, ov);
+          }
+          tmem_wait_st();
+        }
+        m_run = mx;
+      }
       float psum = 0.f;
-      // pass 2: p = exp(scale * s - m) as fp16 into the P tile (row r, keys along K, SW128)
 #pragma unroll
       for (int c = 0; c < kKV; c += 16) {
         float v[16];
@@ -180,52 +205,46 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         uint32_t w[8];
 #pragma unroll
         for (int i = 0; i < 16; i += 2) {
-          const float p0 = kbase + c + i < a.Tk ? expf(v[i] * a.scale - mx) : 0.f;
-          const float p1 = kbase + c + i + 1 < a.Tk ? expf(v[i + 1] * a.scale - mx) : 0.f;
+          const float p0 = kbase + c + i < a.Tk ? exp2f(v[i] * sl2 - m_run) : 0.f;
+          const float p1 = kbase + c + i + 1 < a.Tk ? exp2f(v[i + 1] * sl2 - m_run) : 0.f;
           w[i >> 1] = pack_h2(p0, p1);
           // the row sum uses the rounded values the MMA multiplies
-          psum += h2f_bits((uint16_t)(w[i >> 1] & 0xffffu)) + h2f_bits((uint16_t)(w[i >> 1] >> 16));
+          psum += h2f_bits((uint16_t)(w[i >> 1] & 0xffffu)) +
+                  h2f_bits((uint16_t)(w[i >> 1] >> 16));
         }
         const int half = c >> 6, chunk = (c & 63) >> 3;
         const uint32_t rowp = p_base + half * (kPBytes / 2);
         st_shared_v4(rowp + sw128_off(r, chunk), w[0], w[1], w[2], w[3]);
         st_shared_v4(rowp + sw128_off(r, chunk + 1), w[4], w[5], w[6], w[7]);
       }
-      l_run = l_run * alpha + psum;
+      l_run += psum;
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
-      if (!mbar_wait(o_full, (uint32_t)j & 1u, kFaultAttn)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < kHD; c += 16) {
-        float v[16];
-        tmem_ld16(tO + lrow + c, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; i++) o[c + i] = o[c + i] * alpha + v[i];
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(o_free);
     }
-    // normalise and store
-    const int t = q0 + r;
-    if (t < a.Tq && ok) {
+    // normalise and store the finished O row
+    if (ok && mbar_wait(o_full, 0, kFaultAttn)) {
+      tc_fence_after();
+      const int t = q0 + r;
       const float inv = 1.0f / l_run;
       const int b = bh / a.H, h = bh - b * a.H;
       const int64_t D = (int64_t)a.H * a.hd;
       const int64_t off = ((int64_t)b * a.Tq + t) * D + (int64_t)h * a.hd;
 #pragma unroll
-      for (int d = 0; d < kHD; d++) {
-        if (d < a.hd) {
-          const float val = o[d] * inv;
-          if (a.o16) a.o16[off + d] = f2h_bits(val);
-          if (a.o32) a.o32[off + d] = val;
+      for (int c = 0; c < kHD; c += 16) {
+        float ov[16];
+        tmem_ld16(tO + lrow + c, ov);
+        tmem_wait_ld();
+        if (t < a.Tq) {
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            if (c + i < a.hd) {
+              const float val = ov[i] * inv;
+              if (a.o16) a.o16[off + c + i] = f2h_bits(val);
+              if (a.o32) a.o32[off + c + i] = val;
+            }
+          }
         }
       }
     }
@@ -322,14 +341,14 @@ void flash_attention(const uint16_t *q, const uint16_t *k, const uint16_t *vt, i
   a.o16 = o16;
   a.o32 = o32;
   TraceScope ts(TR_ATTN, 4.0 * B * H * (double)Tq * Tk * hd,
-                2.0 * B * H * hd * (2.0 * Tq + 2.0 * Tk));
+                2.0 * B * H * hd * (2.0 * Tq + 2.0 * Tk), (int64_t)B * H * Tq, Tk, hd);
   if (!g_opt_simt) {
     CUtensorMap mq, mk, mv;
     bool ok = map3(&mq, q, hd, Tq, (uint64_t)B * H, hd, (uint64_t)Tq * hd, 64, kQ) &&
               map3(&mk, k, hd, Tk, (uint64_t)B * H, hd, (uint64_t)Tk * hd, 64, kKV) &&
               map3(&mv, vt, Tk, hd, (uint64_t)B * H, Tkp, (uint64_t)hd * Tkp, 64, 64);
     if (ok) {
-      const size_t smem = 1024 + kQBytes + kAttnStages * (kKBytes + kVBytes) + kPBytes + 256;
+      const size_t smem = kQBytes + kAttnStages * (kKBytes + kVBytes) + kPBytes + 128;
       static bool attr = false;
       if (!attr) {
         DCB_CUDA(cudaFuncSetAttribute(k_flash_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,

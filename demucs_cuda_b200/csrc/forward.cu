@@ -28,6 +28,10 @@ static void dfree(void *p) {
   if (p) DCB_CUDA(cudaFreeAsync(p, stream()));
 }
 
+void ispec_fused(const float *x, float *out, const float *mean, const float *var, int B,
+                 int rows_per_b, int F, int N, int n_fft, int hop, const float *window,
+                 int64_t start, int64_t length, float eps);
+
 struct Stage {
   DcbStageFn fn = nullptr;
   void *user = nullptr;
@@ -610,16 +614,11 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
   // output (htdemucs.c:242-279)
   const int S = c.n_sources;
   const int Ctot = m->dec[depth - 1].Cout;  // S * 2C
-  const int64_t per_x = (int64_t)Ctot * H * W;
-  dk_affine_rows(x, x, mean, var, B, per_x, 1e-5f, 1);
-  const int NF = W + 4;
   const int64_t R = (int64_t)B * S * (Ctot / S / 2);
-  float *frames = dalloc((size_t)R * NF * nfft);
-  dk_istft_frames(x, frames, R, H, W, 2, nfft, m->window);
-  dfree(x);
   float *xi = dalloc((size_t)R * L);
-  dk_ola(frames, xi, R, NF, nfft, hop, m->window, (int64_t)nfft / 2 + pad, L);
-  dfree(frames);
+  ispec_fused(x, xi, mean, var, B, Ctot / 2, H, W, nfft, hop, m->window,
+              (int64_t)nfft / 2 + pad, L, 1e-5f);
+  dfree(x);
   sg.emit("ispec", xi, {B, S, (int)(Ctot / S / 2), L});
   const int keep = T < L ? T : L;
   {

@@ -606,7 +606,7 @@ void gemm_rows(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch,
     if (e.res || e.beta != 0.f) out_b *= 2;
     const double in_b = 2.0 * ((double)M * K * (a.stride ? batch : 1) +
                                (double)N * K * (b.stride ? batch : 1));
-    TraceScope ts(e.mode == EPI_GEMM ? TR_GEMM : TR_LINEAR, mnk, in_b + out_b);
+    TraceScope ts(e.mode == EPI_GEMM ? TR_GEMM : TR_LINEAR, mnk, in_b + out_b, M, N, K);
     gemm_rows_launch(M, N, K, a, b, batch, e, s, g);
   }
 }
@@ -649,7 +649,8 @@ void gemm_gather(const Gather &g, int64_t M, const uint16_t *w, int64_t N, int64
   const double out_elems = e.mode == EPI_CONVTR ? (double)M * e.O * e.stride : (double)M * e.O;
   const double x_b = images * g.C * g.H * g.W * 4.0 * (g.x2 ? 2 : 1);
   TraceScope ts(e.mode == EPI_CONVTR ? TR_CONVTR : TR_CONV, 2.0 * M * n_alg * g.K,
-                x_b + n_alg * g.K * 2.0 + out_elems * 4.0 * (e.res ? 2 : 1));
+                x_b + n_alg * g.K * 2.0 + out_elems * 4.0 * (e.res ? 2 : 1), M, (int64_t)n_alg,
+                g.K);
   if (!g_opt_simt) {
     CUtensorMap tb;
     // inner extent = the padded row length: padding columns are zero in every packed

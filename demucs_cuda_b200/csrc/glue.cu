@@ -83,21 +83,16 @@ __global__ void __launch_bounds__(kGnThreads)
 // reference's apply computes it, backend_cpu.c:254)
 __global__ void k_rowview_combine(const double *partial, int64_t rows, int nchunks, float eps,
                                   float *mean, float *rstd, float *var) {
-  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (r >= rows) return;
-  const double *p = partial + r * nchunks * 3;
-  double n = p[0], m = p[1], m2 = p[2];
-  for (int c = 1; c < nchunks; c++) {
-    const double nb = p[c * 3], mb = p[c * 3 + 1], m2b = p[c * 3 + 2];
-    const double nt = n + nb, d = mb - m;
-    m += d * nb / nt;
-    m2 += m2b + d * d * n * nb / nt;
-    n = nt;
+  double n, m, m2;
+  warp_merge_row(partial + r * nchunks * 3, nchunks, n, m, m2);
+  if ((threadIdx.x & 31) == 0) {
+    const float vf = (float)(m2 / n);
+    mean[r] = (float)m;
+    if (var) var[r] = vf;
+    if (rstd) rstd[r] = 1.0f / sqrtf(vf + eps);
   }
-  const float vf = (float)(m2 / n);
-  mean[r] = (float)m;
-  if (var) var[r] = vf;
-  if (rstd) rstd[r] = 1.0f / sqrtf(vf + eps);
 }
 
 static double *g_part = nullptr;
@@ -122,7 +117,7 @@ void rowview_stats(const RowView &v, int B, float eps, float *mean, float *rstd,
   dim3 grid(nchunks, (unsigned)rows);
   k_rowview_stats<<<grid, kGnThreads, 0, stream()>>>(v, nchunks, g_part);
   DCB_LAUNCHED();
-  k_rowview_combine<<<grid_for(rows, 128, 1 << 30), 128, 0, stream()>>>(g_part, rows, nchunks,
+  k_rowview_combine<<<grid_for(rows * 32, 128, 1 << 30), 128, 0, stream()>>>(g_part, rows, nchunks,
                                                                        eps, mean, rstd, var);
   DCB_LAUNCHED();
 }

@@ -67,21 +67,47 @@ __global__ void __launch_bounds__(kStatThreads)
   }
 }
 
+// Chan's parallel merge of (count, mean, M2) pairs
+static __device__ __forceinline__ void chan_merge(double &n, double &m, double &m2, double nb,
+                                                  double mb, double m2b) {
+  if (nb == 0.0) return;
+  if (n == 0.0) {
+    n = nb;
+    m = mb;
+    m2 = m2b;
+    return;
+  }
+  const double nt = n + nb, d = mb - m;
+  m += d * nb / nt;
+  m2 += m2b + d * d * n * nb / nt;
+  n = nt;
+}
+
+// one warp per row: each lane merges a strided subset of the chunk partials, then a
+// shuffle tree merges the 32 lane results
+static __device__ __forceinline__ void warp_merge_row(const double *p, int nchunks, double &n,
+                                                      double &m, double &m2) {
+  const int lane = threadIdx.x & 31;
+  n = m = m2 = 0.0;
+  for (int c = lane; c < nchunks; c += 32) chan_merge(n, m, m2, p[c * 3], p[c * 3 + 1], p[c * 3 + 2]);
+  for (int o = 16; o > 0; o >>= 1) {
+    const double nb = __shfl_xor_sync(0xffffffffu, n, o);
+    const double mb = __shfl_xor_sync(0xffffffffu, m, o);
+    const double m2b = __shfl_xor_sync(0xffffffffu, m2, o);
+    chan_merge(n, m, m2, nb, mb, m2b);
+  }
+}
+
 __global__ void k_combine_stats(const double *partial, int64_t rows, int nchunks, float *mean,
                                 float *var) {
-  int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (r >= rows) return;
-  const double *p = partial + r * nchunks * 3;
-  double n = p[0], m = p[1], m2 = p[2];
-  for (int c = 1; c < nchunks; c++) {
-    double nb = p[c * 3], mb = p[c * 3 + 1], m2b = p[c * 3 + 2];
-    double nt = n + nb, d = mb - m;
-    m += d * nb / nt;
-    m2 += m2b + d * d * n * nb / nt;
-    n = nt;
+  double n, m, m2;
+  warp_merge_row(partial + r * nchunks * 3, nchunks, n, m, m2);
+  if ((threadIdx.x & 31) == 0) {
+    mean[r] = (float)m;
+    var[r] = (float)(m2 / n);
   }
-  mean[r] = (float)m;
-  var[r] = (float)(m2 / n);
 }
 
 static double *g_stat_scratch = nullptr;
@@ -103,7 +129,7 @@ void row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var)
   dim3 grid(nchunks, (unsigned)rows);
   k_chunk_stats<<<grid, kStatThreads, 0, stream()>>>(x, L, nchunks, g_stat_scratch);
   DCB_LAUNCHED();
-  k_combine_stats<<<grid_for(rows, 128, 1 << 30), 128, 0, stream()>>>(g_stat_scratch, rows,
+  k_combine_stats<<<grid_for(rows * 32, 128, 1 << 30), 128, 0, stream()>>>(g_stat_scratch, rows,
                                                                      nchunks, mean, var);
   DCB_LAUNCHED();
 }
@@ -159,7 +185,7 @@ int row_stats_noalloc(const float *x, int64_t rows, int64_t L, float *mean, floa
   dim3 grid((unsigned)nchunks, (unsigned)rows);
   k_chunk_stats<<<grid, kStatThreads, 0, stream()>>>(x, L, (int)nchunks, part);
   DCB_LAUNCHED();
-  k_combine_stats<<<grid_for(rows, 128, 1 << 30), 128, 0, stream()>>>(part, rows, (int)nchunks,
+  k_combine_stats<<<grid_for(rows * 32, 128, 1 << 30), 128, 0, stream()>>>(part, rows, (int)nchunks,
                                                                      mean, var);
   DCB_LAUNCHED();
   return failed() ? -1 : 0;

@@ -132,10 +132,134 @@ __global__ void k_ola(const float *__restrict__ frames, float *__restrict__ out,
   }
 }
 
+// Decoder output x [B][S*2C][F][N] (channel 2q = real, 2q+1 = imaginary of row q = (s, c))
+// -> z [B*S*C][N][F] complex, frame-major, denormalised per batch
+// (v * (sqrt(var) + eps) + mean, htdemucs.c:251): 32x32 shared-memory tiles, coalesced on
+// both sides.
+__global__ void k_spec_frames_major(const float *__restrict__ x, float2 *__restrict__ z,
+                                    const float *__restrict__ mean,
+                                    const float *__restrict__ var, int rows_per_b, int F,
+                                    int N, float eps) {
+  __shared__ float tre[32][33], tim[32][33];
+  const int r = blockIdx.z;
+  const int b = r / rows_per_b, q = r - b * rows_per_b;
+  const int f0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  const float sd = sqrtf(var[b]) + eps, m = mean[b];
+  const float *xre = x + ((int64_t)b * 2 * rows_per_b + 2 * q) * F * (int64_t)N;
+  const float *xim = xre + (int64_t)F * N;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int f = f0 + i, n = n0 + threadIdx.x;
+    if (f < F && n < N) {
+      tre[i][threadIdx.x] = xre[(int64_t)f * N + n] * sd + m;
+      tim[i][threadIdx.x] = xim[(int64_t)f * N + n] * sd + m;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int n = n0 + i, f = f0 + threadIdx.x;
+    if (f < F && n < N)
+      z[((int64_t)r * N + n) * F + f] = make_float2(tre[threadIdx.x][i], tim[threadIdx.x][i]);
+  }
+}
+
+// Fused inverse STFT + overlap-add (dk_istft_frames + dk_ola, backend_cpu.c:596-662): CTA =
+// one row and kOlaHops consecutive hops of the padded OLA signal.  Every frame touching
+// them (pad frames are zero) is inverse-transformed in shared memory (conjugate -> forward
+// FFT -> conjugate, real part, 1/n, window) and added into the CTA's accumulator in
+// ascending frame order; outputs are divided by the summed squared window.
+constexpr int kOlaHops = 8;
+
+__global__ void __launch_bounds__(512)
+    k_istft_ola(const float2 *__restrict__ z, float *__restrict__ out, int N, int F, int n,
+                int bits, int hop, const float *__restrict__ window,
+                const float2 *__restrict__ tw, int64_t start, int64_t length, int j_first) {
+  extern __shared__ float2 sbuf[];
+  float *acc = (float *)(sbuf + n);
+  const int64_t r = blockIdx.y;
+  const int j0 = j_first + blockIdx.x * kOlaHops;
+  const int NF = N + 4;  // two zero pad frames on each side (stft.c:55-60)
+  const int span = kOlaHops * hop;
+  const int64_t a0 = (int64_t)j0 * hop;
+  for (int i = threadIdx.x; i < span; i += blockDim.x) acc[i] = 0.f;
+  const float inv_n = 1.0f / (float)n;
+  const int frames_per_window = n / hop;
+  int f_beg = j0 - frames_per_window + 1;
+  if (f_beg < 0) f_beg = 0;
+  int f_end = j0 + kOlaHops - 1;
+  if (f_end > NF - 1) f_end = NF - 1;
+  for (int f = f_beg; f <= f_end; f++) {
+    const int fi = f - 2;
+    if (fi < 0 || fi >= N) continue;  // pad frame: contributes zero
+    const float2 *zr = z + ((int64_t)r * N + fi) * F;
+    __syncthreads();  // previous frame's accumulate finished reading sbuf
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+      const int kk = k <= n / 2 ? k : n - k;
+      float2 v = kk < F ? zr[kk] : make_float2(0.f, 0.f);
+      if (k > n / 2) v.y = -v.y;
+      sbuf[(int)(__brev((unsigned)k) >> (32 - bits))] = make_float2(v.x, -v.y);
+    }
+    fft_smem(sbuf, n, tw);
+    const int64_t fpos = (int64_t)f * hop;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const int64_t rel = fpos + i - a0;
+      if (rel >= 0 && rel < span) acc[rel] += sbuf[i].x * inv_n * window[i];
+    }
+  }
+  __syncthreads();
+  const int64_t out_len = (int64_t)hop * (NF - 1) + n;
+  for (int i = threadIdx.x; i < span; i += blockDim.x) {
+    const int64_t idx = a0 + i, t = idx - start;
+    if (t < 0 || t >= length) continue;
+    float den = 0.f;
+    if (idx < out_len) {
+      int64_t f_hi = idx / hop;
+      if (f_hi > NF - 1) f_hi = NF - 1;
+      const int64_t f_lo = idx - n + 1 <= 0 ? 0 : (idx - n + hop) / hop;
+      for (int64_t f = f_lo; f <= f_hi; f++) {
+        const int64_t w = idx - f * hop;
+        if (w < 0 || w >= n) continue;
+        den += window[w] * window[w];
+      }
+    }
+    out[r * length + t] = den > 0.f ? acc[i] / den : 0.f;
+  }
+}
+
 static int log2i(int n) {
   int b = 0;
   while ((1 << b) < n) b++;
   return b;
+}
+
+// denormalise + inverse STFT + OLA of the decoder output (the engine's _ispec path):
+// x [B][2*rows_per_b][F][N] -> out [B*rows_per_b][length]
+void ispec_fused(const float *x, float *out, const float *mean, const float *var, int B,
+                 int rows_per_b, int F, int N, int n_fft, int hop, const float *window,
+                 int64_t start, int64_t length, float eps) {
+  const float2 *tw = twiddles(n_fft);
+  if (!tw) return;
+  const int64_t R = (int64_t)B * rows_per_b;
+  DCB_REQUIRE(R <= 65535 && F <= n_fft / 2 + 1, "ispec: %lld rows, %d bins", (long long)R, F);
+  float2 *z = nullptr;
+  DCB_CUDA(cudaMallocAsync(&z, (size_t)R * N * F * sizeof(float2), stream()));
+  dim3 tg((unsigned)((N + 31) / 32), (unsigned)((F + 31) / 32), (unsigned)R);
+  k_spec_frames_major<<<tg, dim3(32, 8), 0, stream()>>>(x, z, mean, var, rows_per_b, F, N,
+                                                         eps);
+  DCB_LAUNCHED();
+  const int j_first = (int)(start / hop);
+  const int j_last = (int)((start + length - 1) / hop);
+  const int groups = (j_last - j_first + 1 + kOlaHops - 1) / kOlaHops;
+  const size_t smem = (size_t)n_fft * sizeof(float2) + (size_t)kOlaHops * hop * sizeof(float);
+  static size_t attr = 0;
+  if (smem > attr) {
+    DCB_CUDA(cudaFuncSetAttribute(k_istft_ola, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    attr = smem;
+  }
+  k_istft_ola<<<dim3((unsigned)groups, (unsigned)R), 512, smem, stream()>>>(
+      z, out, N, F, n_fft, log2i(n_fft), hop, window, tw, start, length, j_first);
+  DCB_LAUNCHED();
+  DCB_CUDA(cudaFreeAsync(z, stream()));
 }
 
 }  // namespace dcb

@@ -14,6 +14,7 @@ struct TraceRec {
   int cls;
   cudaEvent_t a, b;
   double flops, bytes;
+  int64_t M, N, K;  // problem extents of the launch (for per-shape breakdowns)
 };
 
 static uint32_t g_trace_mask = 0;
@@ -34,8 +35,12 @@ static cudaEvent_t trace_event() {
 struct TraceScope {
   bool on;
   TraceRec rec;
-  TraceScope(int cls, double flops, double bytes) : on((g_trace_mask >> cls) & 1u) {
+  TraceScope(int cls, double flops, double bytes, int64_t M = 0, int64_t N = 0, int64_t K = 0)
+      : on((g_trace_mask >> cls) & 1u) {
     if (!on) return;
+    rec.M = M;
+    rec.N = N;
+    rec.K = K;
     rec.cls = cls;
     rec.flops = flops;
     rec.bytes = bytes;
@@ -81,6 +86,21 @@ int dcb_trace_stop(double *ms, double *flops, double *bytes, int *launches, int 
     bytes[r.cls] += r.bytes;
     launches[r.cls] += 1;
   }
+  return (int)g_trace.size();
+}
+
+int dcb_trace_dump(const char *path) {
+  FILE *f = fopen(path, "w");
+  if (!f) return -1;
+  DCB_CUDA(cudaStreamSynchronize(stream()));
+  fprintf(f, "class,ms,flops,bytes,M,N,K\n");
+  for (auto &r : g_trace) {
+    float t = 0.f;
+    DCB_CUDA(cudaEventElapsedTime(&t, r.a, r.b));
+    fprintf(f, "%d,%.6f,%.0f,%.0f,%lld,%lld,%lld\n", r.cls, t, r.flops, r.bytes,
+            (long long)r.M, (long long)r.N, (long long)r.K);
+  }
+  fclose(f);
   return (int)g_trace.size();
 }
 

@@ -202,6 +202,8 @@ uint32_t dcb_device_fault(int clear);
  * totals (milliseconds, FLOPs, bytes, launches) for classes < ncls. */
 void dcb_trace_start(uint32_t mask);
 int dcb_trace_stop(double *ms, double *flops, double *bytes, int *launches, int ncls);
+/* After dcb_trace_stop: write every traced launch (class, ms, FLOPs, bytes, M, N, K) as CSV. */
+int dcb_trace_dump(const char *path);
 
 typedef struct DcbModel DcbModel;
 /* Load weights (safetensors, F32/F16/BF16, MLX layout) + model JSON (defaults =
