@@ -31,6 +31,9 @@ static void dfree(void *p) {
 void ispec_fused(const float *x, float *out, const float *mean, const float *var, int B,
                  int rows_per_b, int F, int N, int n_fft, int hop, const float *window,
                  int64_t start, int64_t length, float eps);
+void spec_normalised(const float *xc, int B, int C, int64_t L, int n_fft, int hop, int frame0,
+                     int nframes, int nbins, const float *window, float *x, float *mean,
+                     float *var, float *mag);
 
 struct Stage {
   DcbStageFn fn = nullptr;
@@ -529,18 +532,17 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
   dk_reflect_pad(mix, xp, (int64_t)B * C, L, pad, extra);
   dk_reflect_pad(xp, xc, (int64_t)B * C, L1, nfft / 2, nfft / 2);
   dfree(xp);
-  float *mag = dalloc((size_t)B * 2 * C * nb * le);
-  dk_stft(xc, mag, (int64_t)B * C, L2, nfft, hop, 2, le, nb, m->window);
-  dfree(xc);
-  sg.emit("mag", mag, {B, 2 * C, nb, le});
-  // per-segment normalisation (htdemucs.c:152-159)
   float *stats = dalloc((size_t)B * 4);
   float *mean = stats, *var = stats + B, *meant = stats + 2 * B, *vart = stats + 3 * B;
   const int64_t per_mag = (int64_t)2 * C * nb * le;
-  row_stats(mag, B, per_mag, mean, var);
   float *x = dalloc((size_t)B * per_mag);
-  dk_affine_rows(mag, x, mean, var, B, per_mag, 1e-5f, 0);
-  dfree(mag);
+  float *mag = sg.fn ? dalloc((size_t)B * per_mag) : nullptr;
+  spec_normalised(xc, B, C, L2, nfft, hop, 2, le, nb, m->window, x, mean, var, mag);
+  dfree(xc);
+  if (mag) {
+    sg.emit("mag", mag, {B, 2 * C, nb, le});
+    dfree(mag);
+  }
   sg.emit("x_norm", x, {B, 2 * C, nb, le});
   row_stats(mix, B, (int64_t)C * L, meant, vart);
   float *xt = dalloc((size_t)B * C * L);

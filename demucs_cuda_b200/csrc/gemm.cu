@@ -374,20 +374,93 @@ __global__ void __launch_bounds__(kThreads, 2)
     const bool mv = m < s.M;
     const RowInfo ri = mv ? decode_row(e, m) : RowInfo{0, 0, 0, 0, 0};
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-    if (e.mode == EPI_CONV && e.act == 2) {
-      const int hb = e.glu_half;
-      // the a-columns of this tile split between the two warp halves in 16-column steps
-      const int per = hb >= 32 ? hb / 2 : (half == 0 ? hb : 0);
-      const int c_beg = hb >= 32 ? half * per : 0;
-      for (int c0 = c_beg; c0 < c_beg + per; c0 += 16) {
-        float va[16], vb[16];
-        tmem_ld16(trow + c0, va);
-        tmem_ld16(trow + hb + c0, vb);
-        tmem_wait_ld();
-        if (mv) {
+    if (e.mode == EPI_CONV) {
+      // Staged conv epilogue: chunks of up to 32 output channels go TMEM -> registers
+      // (bias, GELU / GLU) -> shared memory [channel][tile row] (the operand buffers are
+      // idle once `done` fired), then each warp stores 128 consecutive positions of one
+      // channel per step with 16-byte stores (scalar where positions are not contiguous).
+      float *stage = (float *)sA + half * (32 * kBM);
+      int64_t poff[4];
+      bool pv[4];
 #pragma unroll
-          for (int i = 0; i < 16; i++) store_glu(e, (int64_t)nt * hb + c0 + i, ri, va[i], vb[i]);
+      for (int i = 0; i < 4; i++) {
+        const int64_t mm = m0 + 4 * lane + i;
+        pv[i] = mm < s.M;
+        poff[i] = 0;
+        if (pv[i]) {
+          const RowInfo rq = decode_row(e, mm);
+          poff[i] = rq.base + (int64_t)rq.ho * e.oH + rq.wo;
         }
+      }
+      const bool contig = pv[3] && poff[1] == poff[0] + 1 && poff[2] == poff[0] + 2 &&
+                          poff[3] == poff[0] + 3;
+      const bool glu = e.act == 2;
+      const int ncols = glu ? e.glu_half : BN;
+      const int per = ncols >= 32 ? ncols / 2 : (half == 0 ? ncols : 0);
+      const int c_beg = ncols >= 32 ? half * per : 0;
+      const int obase = glu ? nt * e.glu_half : n0;
+      for (int c0 = c_beg; c0 < c_beg + per; c0 += 32) {
+        const int cw = c_beg + per - c0 >= 32 ? 32 : 16;
+        for (int sub = 0; sub < cw; sub += 16) {
+          float va[16];
+          tmem_ld16(trow + c0 + sub, va);
+          if (glu) {
+            float vb[16];
+            tmem_ld16(trow + e.glu_half + c0 + sub, vb);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              const int o = obase + c0 + sub + i;
+              float val = 0.f;
+              if (o < e.O) {
+                const float a = va[i] + (e.bias ? e.bias[o] : 0.f);
+                const float b = vb[i] + (e.bias ? e.bias[e.O + o] : 0.f);
+                val = a * sigmoid_f(b);
+              }
+              stage[(sub + i) * kBM + r] = val;
+            }
+          } else {
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              const int o = obase + c0 + sub + i;
+              float val = va[i] + ((e.bias && o < e.O) ? e.bias[o] : 0.f);
+              if (e.act == 1) val = gelu_f(val);
+              stage[(sub + i) * kBM + r] = val;
+            }
+          }
+        }
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + half), "r"(128) : "memory");
+        for (int cc = quarter; cc < cw; cc += 4) {
+          const int o = obase + c0 + cc;
+          if (o < e.O) {
+            const float4 v4 = *(const float4 *)(stage + cc * kBM + 4 * lane);
+            float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+            const int64_t a = poff[0] + (int64_t)o * e.oC;
+            const uintptr_t al = (uintptr_t)(e.y + a) | (e.res ? (uintptr_t)(e.res + a) : 0);
+            if (contig && (al & 15) == 0) {
+              if (e.res) {
+                const float4 rr = *(const float4 *)(e.res + a);
+                const float sc = e.scale[o];
+                vv[0] = rr.x + sc * vv[0];
+                vv[1] = rr.y + sc * vv[1];
+                vv[2] = rr.z + sc * vv[2];
+                vv[3] = rr.w + sc * vv[3];
+              }
+              *(float4 *)(e.y + a) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 4; i++) {
+                if (!pv[i]) continue;
+                const int64_t ai = poff[i] + (int64_t)o * e.oC;
+                float val = vv[i];
+                if (e.res) val = e.res[ai] + e.scale[o] * val;
+                e.y[ai] = val;
+              }
+            }
+          }
+        }
+        asm volatile("bar.sync %0, %1;" ::"r"(1 + half), "r"(128) : "memory");
       }
     } else {
       constexpr int PER = BN / 2;  // >= 16

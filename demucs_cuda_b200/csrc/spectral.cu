@@ -225,6 +225,206 @@ __global__ void __launch_bounds__(512)
   }
 }
 
+// ---------------------------------------------------------------- 4096-point Stockham FFT
+// Radix-16 Stockham autosort FFT for n = 4096 with 256 threads: three passes, each thread
+// holds 16 points in registers, applies the pass twiddles, does a 16-point DFT (radix 4 x 4)
+// and writes back to the same shared buffer after a barrier.  The buffer index is padded by
+// one element per 16 so every pass's loads and stores are (nearly) free of bank conflicts,
+// and the result comes out in natural order (no bit reversal).
+constexpr int kFftN = 4096;
+constexpr int kFftThreads = 256;
+constexpr int kFftPadded = kFftN + kFftN / 16;
+
+static __device__ __forceinline__ int fpad(int i) { return i + (i >> 4); }
+static __device__ __forceinline__ float2 cmulf(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+// in-place 4-point DFT (forward sign) of (a, b, c, d)
+static __device__ __forceinline__ void dft4(float2 &a, float2 &b, float2 &c, float2 &d) {
+  const float2 s0 = make_float2(a.x + c.x, a.y + c.y), d0 = make_float2(a.x - c.x, a.y - c.y);
+  const float2 s1 = make_float2(b.x + d.x, b.y + d.y), d1 = make_float2(b.x - d.x, b.y - d.y);
+  a = make_float2(s0.x + s1.x, s0.y + s1.y);
+  c = make_float2(s0.x - s1.x, s0.y - s1.y);
+  b = make_float2(d0.x + d1.y, d0.y - d1.x);  // d0 - i d1
+  d = make_float2(d0.x - d1.y, d0.y + d1.x);  // d0 + i d1
+}
+// 16-point forward DFT; on return X[k1 + 4 k2] sits in v[4 k1 + k2]
+static __device__ __forceinline__ void dft16(float2 (&v)[16]) {
+  // cos / sin of pi/8 and of pi/4
+  const float c1 = 0.92387953251128674f, s1 = 0.38268343236508978f, h = 0.70710678118654752f;
+#pragma unroll
+  for (int n2 = 0; n2 < 4; n2++) dft4(v[n2], v[n2 + 4], v[n2 + 8], v[n2 + 12]);
+  // twiddles W16^(n2 k1) at v[n2 + 4 k1]
+  v[5] = cmulf(v[5], make_float2(c1, -s1));    // W^1
+  v[9] = cmulf(v[9], make_float2(h, -h));      // W^2
+  v[13] = cmulf(v[13], make_float2(s1, -c1));  // W^3
+  v[6] = cmulf(v[6], make_float2(h, -h));      // W^2
+  v[10] = make_float2(v[10].y, -v[10].x);      // W^4 = -i
+  v[14] = cmulf(v[14], make_float2(-h, -h));   // W^6
+  v[7] = cmulf(v[7], make_float2(s1, -c1));    // W^3
+  v[11] = cmulf(v[11], make_float2(-h, -h));   // W^6
+  v[15] = cmulf(v[15], make_float2(-c1, s1));  // W^9
+#pragma unroll
+  for (int k1 = 0; k1 < 4; k1++) dft4(v[4 * k1], v[4 * k1 + 1], v[4 * k1 + 2], v[4 * k1 + 3]);
+}
+// forward DFT of buf (padded layout, natural order in and out); tw[e] = exp(-2 pi i e / 4096)
+static __device__ __forceinline__ void fft4096(float2 *buf, const float2 *__restrict__ tw) {
+  const int j = threadIdx.x;
+#pragma unroll
+  for (int pass = 0; pass < 3; pass++) {
+    const int lg = 4 * pass, Ns = 1 << lg;
+    float2 v[16];
+#pragma unroll
+    for (int r = 0; r < 16; r++) v[r] = buf[fpad(j + 256 * r)];
+    const int k = j & (Ns - 1);
+    if (pass > 0) {
+#pragma unroll
+      for (int r = 1; r < 16; r++) v[r] = cmulf(v[r], __ldg(tw + ((k * r) << (8 - lg))));
+    }
+    dft16(v);
+    __syncthreads();
+    const int idxD = ((j >> lg) << (lg + 4)) + k;
+#pragma unroll
+    for (int r = 0; r < 16; r++) buf[fpad(idxD + r * Ns)] = v[4 * (r & 3) + (r >> 2)];
+    __syncthreads();
+  }
+}
+
+static float2 *g_tw_full = nullptr;
+
+// exp(-2 pi i e / 4096) for e < 4096, evaluated in double on the host
+static const float2 *twiddles4096() {
+  if (g_tw_full) return g_tw_full;
+  std::vector<float2> h(kFftN);
+  for (int e = 0; e < kFftN; e++) {
+    const double a = -2.0 * 3.14159265358979323846 * (double)e / (double)kFftN;
+    h[e] = make_float2((float)cos(a), (float)sin(a));
+  }
+  DCB_CUDA(cudaMalloc(&g_tw_full, kFftN * sizeof(float2)));
+  DCB_CUDA(cudaMemcpy(g_tw_full, h.data(), kFftN * sizeof(float2), cudaMemcpyHostToDevice));
+  return g_tw_full;
+}
+
+// Hann-windowed STFT frames of sig [R][L] (frame f starts at (frame0 + f) * hop), written
+// frame-major: z [R][nframes][nbins] complex (coalesced stores).
+__global__ void __launch_bounds__(kFftThreads)
+    k_stft_fm(const float *__restrict__ sig, float2 *__restrict__ z, int64_t L, int hop,
+              int frame0, int nframes, int nbins, const float *__restrict__ window,
+              const float2 *__restrict__ tw) {
+  __shared__ float2 buf[kFftPadded];
+  const int f = blockIdx.x;
+  const int64_t r = blockIdx.y;
+  const int64_t start = (int64_t)(frame0 + f) * hop;
+  const float *s = sig + r * L;
+#pragma unroll
+  for (int q = 0; q < 16; q++) {
+    const int i = threadIdx.x + 256 * q;
+    const int64_t t = start + i;
+    buf[fpad(i)] = make_float2(t < L ? s[t] * window[i] : 0.f, 0.f);
+  }
+  __syncthreads();
+  fft4096(buf, tw);
+  float2 *out = z + (r * nframes + f) * (int64_t)nbins;
+  for (int k = threadIdx.x; k < nbins; k += kFftThreads) out[k] = buf[fpad(k)];
+}
+
+// z [R][N][F] complex (frame-major) -> x [B][2C][F][N] normalised per batch, (v - m) / sd
+// with sd = sqrt(var) + eps (the spectrogram normalisation of htdemucs.c:152-154)
+__global__ void k_fm_to_chw(const float2 *__restrict__ z, float *__restrict__ x,
+                            const float *__restrict__ mean, const float *__restrict__ var,
+                            int rows_per_b, int F, int N, float eps, int normalise) {
+  __shared__ float tre[32][33], tim[32][33];
+  const int r = blockIdx.z;
+  const int b = r / rows_per_b, q = r - b * rows_per_b;
+  const int f0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  float sd = 1.f, m = 0.f;
+  if (normalise) {
+    sd = sqrtf(var[b]) + eps;
+    m = mean[b];
+  }
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int n = n0 + i, f = f0 + threadIdx.x;
+    if (f < F && n < N) {
+      const float2 v = z[((int64_t)r * N + n) * F + f];
+      tre[threadIdx.x][i] = v.x;
+      tim[threadIdx.x][i] = v.y;
+    }
+  }
+  __syncthreads();
+  float *xre = x + ((int64_t)b * 2 * rows_per_b + 2 * q) * F * (int64_t)N;
+  float *xim = xre + (int64_t)F * N;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int f = f0 + i, n = n0 + threadIdx.x;
+    if (f < F && n < N) {
+      xre[(int64_t)f * N + n] = (tre[i][threadIdx.x] - m) / sd;
+      xim[(int64_t)f * N + n] = (tim[i][threadIdx.x] - m) / sd;
+    }
+  }
+}
+
+// fused inverse STFT + OLA for n = 4096 (see k_istft_ola): 256 threads, the CTA's
+// accumulator (kOlaHops hops) in registers, one padded FFT buffer in shared memory
+__global__ void __launch_bounds__(kFftThreads)
+    k_istft_ola4096(const float2 *__restrict__ z, float *__restrict__ out, int N, int F, int hop,
+                    const float *__restrict__ window, const float2 *__restrict__ tw,
+                    int64_t start, int64_t length, int j_first) {
+  __shared__ float2 buf[kFftPadded];
+  constexpr int n = kFftN;
+  constexpr int Q = kOlaHops * 1024 / kFftThreads;  // accumulator entries per thread (hop 1024)
+  const int64_t r = blockIdx.y;
+  const int j0 = j_first + blockIdx.x * kOlaHops;
+  const int NF = N + 4;
+  const int64_t a0 = (int64_t)j0 * hop;
+  float acc[Q];
+#pragma unroll
+  for (int q = 0; q < Q; q++) acc[q] = 0.f;
+  const float inv_n = 1.0f / (float)n;
+  int f_beg = j0 - n / hop + 1;
+  if (f_beg < 0) f_beg = 0;
+  int f_end = j0 + kOlaHops - 1;
+  if (f_end > NF - 1) f_end = NF - 1;
+  for (int f = f_beg; f <= f_end; f++) {
+    const int fi = f - 2;
+    if (fi < 0 || fi >= N) continue;
+    const float2 *zr = z + ((int64_t)r * N + fi) * F;
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 16; q++) {
+      const int k = threadIdx.x + 256 * q;
+      const int kk = k <= n / 2 ? k : n - k;
+      float2 v = kk < F ? zr[kk] : make_float2(0.f, 0.f);
+      if (k > n / 2) v.y = -v.y;
+      buf[fpad(k)] = make_float2(v.x, -v.y);
+    }
+    __syncthreads();
+    fft4096(buf, tw);
+    const int64_t off = a0 - (int64_t)f * hop;
+#pragma unroll
+    for (int q = 0; q < Q; q++) {
+      const int64_t i = off + threadIdx.x + 256 * q;
+      if (i >= 0 && i < n) acc[q] += buf[fpad((int)i)].x * inv_n * window[i];
+    }
+  }
+  const int64_t out_len = (int64_t)hop * (NF - 1) + n;
+#pragma unroll
+  for (int q = 0; q < Q; q++) {
+    const int64_t idx = a0 + threadIdx.x + 256 * q, t = idx - start;
+    if (t < 0 || t >= length) continue;
+    float den = 0.f;
+    if (idx < out_len) {
+      int64_t f_hi = idx / hop;
+      if (f_hi > NF - 1) f_hi = NF - 1;
+      const int64_t f_lo = idx - n + 1 <= 0 ? 0 : (idx - n + hop) / hop;
+      for (int64_t g = f_lo; g <= f_hi; g++) {
+        const int64_t w = idx - g * hop;
+        if (w < 0 || w >= n) continue;
+        den += window[w] * window[w];
+      }
+    }
+    out[r * length + t] = den > 0.f ? acc[q] / den : 0.f;
+  }
+}
+
 static int log2i(int n) {
   int b = 0;
   while ((1 << b) < n) b++;
@@ -256,8 +456,38 @@ void ispec_fused(const float *x, float *out, const float *mean, const float *var
                                   (int)smem));
     attr = smem;
   }
-  k_istft_ola<<<dim3((unsigned)groups, (unsigned)R), 512, smem, stream()>>>(
-      z, out, N, F, n_fft, log2i(n_fft), hop, window, tw, start, length, j_first);
+  if (n_fft == kFftN && hop == 1024) {
+    k_istft_ola4096<<<dim3((unsigned)groups, (unsigned)R), kFftThreads, 0, stream()>>>(
+        z, out, N, F, hop, window, twiddles4096(), start, length, j_first);
+  } else {
+    k_istft_ola<<<dim3((unsigned)groups, (unsigned)R), 512, smem, stream()>>>(
+        z, out, N, F, n_fft, log2i(n_fft), hop, window, tw, start, length, j_first);
+  }
+  DCB_LAUNCHED();
+  DCB_CUDA(cudaFreeAsync(z, stream()));
+}
+
+// HTDemucs _spec + per-segment normalisation (stft.c:29-47, htdemucs.c:152-154): the
+// padded signal xc [R = B*C][L] -> x [B][2C][nbins][nframes] normalised; mean/var receive
+// the per-batch statistics; mag (optional) receives the unnormalised spectrogram.
+void spec_normalised(const float *xc, int B, int C, int64_t L, int n_fft, int hop, int frame0,
+                     int nframes, int nbins, const float *window, float *x, float *mean,
+                     float *var, float *mag) {
+  const int64_t R = (int64_t)B * C;
+  DCB_REQUIRE(n_fft == kFftN && R <= 65535, "spec: n_fft %d (this path needs 4096)", n_fft);
+  float2 *z = nullptr;
+  DCB_CUDA(cudaMallocAsync(&z, (size_t)R * nframes * nbins * sizeof(float2), stream()));
+  k_stft_fm<<<dim3((unsigned)nframes, (unsigned)R), kFftThreads, 0, stream()>>>(
+      xc, z, L, hop, frame0, nframes, nbins, window, twiddles4096());
+  DCB_LAUNCHED();
+  // the statistics cover the same elements in any order
+  row_stats((const float *)z, B, (int64_t)C * nframes * nbins * 2, mean, var);
+  dim3 tg((unsigned)((nframes + 31) / 32), (unsigned)((nbins + 31) / 32), (unsigned)R);
+  if (mag) {
+    k_fm_to_chw<<<tg, dim3(32, 8), 0, stream()>>>(z, mag, mean, var, C, nbins, nframes, 0.f, 0);
+    DCB_LAUNCHED();
+  }
+  k_fm_to_chw<<<tg, dim3(32, 8), 0, stream()>>>(z, x, mean, var, C, nbins, nframes, 1e-5f, 1);
   DCB_LAUNCHED();
   DCB_CUDA(cudaFreeAsync(z, stream()));
 }
