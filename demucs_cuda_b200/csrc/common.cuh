@@ -19,6 +19,9 @@ void fail(const char *fmt, ...);
 bool failed();  // an error is pending in return mode
 cudaStream_t stream();
 void count_launch();
+void add_launches(uint64_t n);
+uint64_t launches_now();
+void set_stream_override(cudaStream_t s);
 
 #define DCB_CUDA(call)                                                                   \
   do {                                                                                   \

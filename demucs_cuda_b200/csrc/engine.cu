@@ -339,6 +339,16 @@ struct TLayerW {
   float *gamma1 = nullptr, *gamma2 = nullptr;
 };
 
+// One captured forward (htdemucs.c:136-280) for a batch shape, with persistent input and
+// output buffers so the graph's pointers stay valid across replays.
+struct FwdGraph {
+  int B = 0, T = 0;
+  float *in = nullptr, *out = nullptr;
+  bool warmed = false;
+  cudaGraphExec_t exec = nullptr;
+  uint64_t launches = 0;  // kernels per replay
+};
+
 }  // namespace dcb
 
 struct DcbModel {
@@ -356,6 +366,10 @@ struct DcbModel {
   int D = 0, hidden = 0;
   // cached positional embeddings, keyed by token-grid shape
   std::unordered_map<long long, float *> pos_cache;
+  // CUDA graphs of the segment forward (option "graphs"), replayed on `cap`
+  std::vector<dcb::FwdGraph> graphs;
+  cudaStream_t cap = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_out = nullptr;
 };
 
 namespace dcb {
@@ -739,6 +753,15 @@ DcbModel *dcb_model_load(const char *st_path, const char *cfg_path) {
 void dcb_model_free(DcbModel *m) {
   if (!m) return;
   cudaStreamSynchronize(stream());
+  if (m->cap) cudaStreamSynchronize(m->cap);
+  for (auto &g : m->graphs) {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    cudaFree(g.in);
+    cudaFree(g.out);
+  }
+  if (m->ev_in) cudaEventDestroy(m->ev_in);
+  if (m->ev_out) cudaEventDestroy(m->ev_out);
+  if (m->cap) cudaStreamDestroy(m->cap);
   for (auto &kv : m->pos_cache) cudaFree(kv.second);
   if (m->block) cudaFree(m->block);
   delete m;

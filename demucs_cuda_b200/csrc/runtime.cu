@@ -41,7 +41,12 @@ void fail(const char *fmt, ...) {
 
 bool failed() { return g_err[0] != 0; }
 
+static cudaStream_t g_override = nullptr;  // capture stream while a CUDA graph is recorded
+
+void set_stream_override(cudaStream_t s) { g_override = s; }
+
 cudaStream_t stream() {
+  if (g_override) return g_override;
   if (g_use_ext) return g_ext_stream;
   if (!g_own_stream) {
     DCB_CUDA(cudaStreamCreateWithFlags(&g_own_stream, cudaStreamNonBlocking));
@@ -50,6 +55,8 @@ cudaStream_t stream() {
 }
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void add_launches(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+uint64_t launches_now() { return g_launches.load(); }
 
 uint16_t host_f2h(float f) {
   uint32_t x;
