@@ -317,8 +317,13 @@ struct NormW {
 };
 struct DConvW {
   ConvW c0, c3;
+  ConvW c3g;  // c3 with its output halves interleaved for a GLU epilogue
   NormW gn1, gn4;
   float *scale = nullptr;
+  // fp64 constants of c3 (fp16 weights W16 [2C][hid], bias b) giving the GroupNorm
+  // statistics of z = W16 . h + b from the sums and Gram matrix of h:
+  // G = W16^T W16 [hid][hid], u = column sums of W16, v = W16^T b, sum(b), sum(b^2)
+  double *zc = nullptr;
 };
 struct EncW {
   ConvW conv, rewrite;
@@ -366,6 +371,10 @@ struct DcbModel {
   int D = 0, hidden = 0;
   // cached positional embeddings, keyed by token-grid shape
   std::unordered_map<long long, float *> pos_cache;
+  // transition weights of the overlap-add for (segment length, power), on the device
+  float *ola_w = nullptr;
+  int ola_seg = 0;
+  float ola_pow = 0.f;
   // CUDA graphs of the segment forward (option "graphs"), replayed on `cap`
   std::vector<dcb::FwdGraph> graphs;
   cudaStream_t cap = nullptr;
@@ -555,10 +564,35 @@ static bool load_norm(Loader &L, Staging &st, const std::string &p, NormW &nw, i
   return true;
 }
 
+// DConvW::zc for the 1x1 conv at `prefix` (weights [2C][hid] rounded to fp16 as the GEMM
+// uses them)
+static bool dconv_zconst(Loader &L, Staging &st, const std::string &prefix, DConvW &dw) {
+  const int O = dw.c3.O, hid = dw.c3.K;
+  if (dw.c3.KH != 1 || dw.c3.KW != 1) return true;  // not a 1x1 conv: no fused statistics
+  std::vector<float> w = L.f32(prefix + ".conv.weight");
+  std::vector<float> b = L.f32(prefix + ".conv.bias", (size_t)O);
+  if (w.size() != (size_t)O * hid || b.empty()) return false;
+  std::vector<double> zc((size_t)hid * hid + 2 * hid + 2, 0.0);
+  double *G = zc.data(), *u = G + hid * hid, *v = u + hid;
+  for (int c = 0; c < O; c++) {
+    for (int j = 0; j < hid; j++) {
+      const double wj = host_h2f(host_f2h(w[(size_t)c * hid + j]));
+      u[j] += wj;
+      v[j] += (double)b[c] * wj;
+      for (int k = 0; k < hid; k++) G[j * hid + k] += wj * host_h2f(host_f2h(w[(size_t)c * hid + k]));
+    }
+    zc[(size_t)hid * hid + 2 * hid] += b[c];
+    zc[(size_t)hid * hid + 2 * hid + 1] += (double)b[c] * b[c];
+  }
+  st.add(zc.data(), zc.size() * sizeof(double), (void **)&dw.zc);
+  return true;
+}
+
 static int glu_bn_for(int O2) {
-  // fixed N tile for GLU convs: 2*O2 columns rounded up to a power of two, at most 256
+  // fixed N tile for GLU convs: 2*O2 columns rounded up to a power of two, at most 128
+  // (the widest tile of the gather kernel)
   int bn = 32;
-  while (bn < 256 && bn < 2 * O2) bn *= 2;
+  while (bn < 128 && bn < 2 * O2) bn *= 2;
   return bn;
 }
 
@@ -644,6 +678,8 @@ DcbModel *dcb_model_load(const char *st_path, const char *cfg_path) {
         std::string base(p);
         ok &= load_conv(L, st, base + ".0", dw.c0, false, 0);
         if (ok) ok &= load_conv(L, st, base + ".3", dw.c3, false, 0);
+        if (ok) ok &= load_conv(L, st, base + ".3", dw.c3g, true, glu_bn_for(dw.c3.O / 2));
+        if (ok) ok &= dconv_zconst(L, st, base + ".3", dw);
         if (ok) ok &= load_norm(L, st, base + ".1", dw.gn1, dw.c0.O);
         if (ok) ok &= load_norm(L, st, base + ".4", dw.gn4, dw.c3.O);
         if (ok) {
@@ -763,6 +799,7 @@ void dcb_model_free(DcbModel *m) {
   if (m->ev_out) cudaEventDestroy(m->ev_out);
   if (m->cap) cudaStreamDestroy(m->cap);
   for (auto &kv : m->pos_cache) cudaFree(kv.second);
+  cudaFree(m->ola_w);
   if (m->block) cudaFree(m->block);
   delete m;
 }

@@ -86,7 +86,9 @@ static Img freq_rows(int B, int C, int Fr, int T) {
 
 static void conv(const ConvW &cw, const float *x, const float *x2, const Img &in, int SH, int SW,
                  int PH, int PW, int DH, int DW, int Ho, int Wo, float *y, const Img &out,
-                 int act, const float *res = nullptr, const float *scale = nullptr) {
+                 int act, const float *res = nullptr, const float *scale = nullptr,
+                 const float *gn_mean = nullptr, const float *gn_rstd = nullptr,
+                 const NormW *gn = nullptr) {
   Gather g{};
   g.x = x;
   g.x2 = x2;
@@ -119,13 +121,17 @@ static void conv(const ConvW &cw, const float *x, const float *x2, const Img &in
   e.oN2s = out.sN2;
   e.oC = out.sC;
   e.oH = out.sH;
-  e.O = act == 2 ? cw.O / 2 : cw.O;
+  e.O = act >= 2 ? cw.O / 2 : cw.O;
   e.Ho = Ho;
   e.Wo = Wo;
   e.res = res;
   e.scale = scale;
+  e.gn_mean = gn_mean;
+  e.gn_rstd = gn_rstd;
+  e.gn_w = gn ? gn->w : nullptr;
+  e.gn_b = gn ? gn->b : nullptr;
   const int64_t M = (int64_t)in.N1 * in.N2 * Ho * Wo;
-  gemm_gather(g, M, cw.w, cw.rows, cw.ld, e, act == 2 ? cw.glu_bn : 0);
+  gemm_gather(g, M, cw.w, cw.rows, cw.ld, e, act >= 2 ? cw.glu_bn : 0);
 }
 
 // stride-phase transposed conv along H (freq) or W (time), crop + optional GELU
@@ -179,7 +185,7 @@ static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
   // one CTA per row when there are many short rows (frequency branch); chunked statistics
   // across CTAs when a few rows are long (time branch, lowest frequency level)
   const bool fused = rows >= 128 && (int64_t)2 * C * T <= (256 << 10);
-  float *stat = fused ? nullptr : dalloc((size_t)rows * 2);
+  float *stat = dalloc((size_t)rows * 2);
   for (int d = 0; d < E.ndconv; d++) {
     const DConvW &dw = E.dconv[d];
     const int dil = 1 << d;
@@ -190,6 +196,25 @@ static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
     conv(dw.c0, y, nullptr, v, 1, 1, 0, dil, 1, dil, 1, T, h, hv, 0);
     // GroupNorm(1) + GELU, in place
     RowView rh{h, Fr, (int64_t)hid * Fr * T, T, (int64_t)Fr * T, hid, T};
+    if (fused && dw.zc) {
+      // the GroupNorm statistics of z = conv1x1(h) come with the GELU pass, and the 1x1
+      // conv applies GroupNorm + GLU + LayerScale + residual in its epilogue: z is never
+      // written
+      const size_t sm = (size_t)hid * T * sizeof(float);
+      static size_t attr = 0;
+      if (sm > 48 * 1024 && sm > attr) {
+        DCB_CUDA(cudaFuncSetAttribute(k_gn_gelu_zstats,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        attr = sm;
+      }
+      k_gn_gelu_zstats<<<rows, kGnFusedThreads, sm, stream()>>>(
+          rh, h, dw.gn1.w, dw.gn1.b, 1e-5f, dw.zc, C2, stat, stat + rows);
+      DCB_LAUNCHED();
+      conv(dw.c3g, h, nullptr, hv, 1, 1, 0, 0, 1, 1, 1, T, y, v, 3, y, dw.scale, stat,
+           stat + rows, &dw.gn4);
+      dfree(h);
+      continue;
+    }
     if (fused) {
       k_gn_fused<0><<<rows, kGnFusedThreads, 0, stream()>>>(rh, h, dw.gn1.w, dw.gn1.b,
                                                             nullptr, 0, 0, 0, 1e-5f);
@@ -836,15 +861,19 @@ static int apply_split(DcbModel *m, const float *mix, int B, int length, float *
     fail("apply: invalid overlap %f", (double)o.overlap);
     return -1;
   }
-  std::vector<float> w = ola_weight(p.seg, o.transition_power);
-  std::vector<double> sumw((size_t)length, 0.0);
-  for (size_t i = 0; i < p.offsets.size(); i++) {
-    const int off = p.offsets[i];
-    const int n = length - off < p.seg ? length - off : p.seg;
-    for (int t = 0; t < n; t++) sumw[off + t] += w[t];
+  if (!m->ola_w || m->ola_seg != p.seg || m->ola_pow != o.transition_power) {
+    // the weights depend only on (segment, power): computed on the host once (float math
+    // as apply.c:116-133) and kept on the device
+    std::vector<float> w = ola_weight(p.seg, o.transition_power);
+    DCB_CUDA(cudaStreamSynchronize(stream()));
+    cudaFree(m->ola_w);
+    m->ola_w = nullptr;
+    DCB_CUDA(cudaMalloc(&m->ola_w, (size_t)p.seg * 4));
+    DCB_CUDA(cudaMemcpy(m->ola_w, w.data(), (size_t)p.seg * 4, cudaMemcpyHostToDevice));
+    m->ola_seg = p.seg;
+    m->ola_pow = o.transition_power;
   }
-  float *wdev = dalloc(p.seg);
-  DCB_CUDA(cudaMemcpyAsync(wdev, w.data(), p.seg * 4, cudaMemcpyHostToDevice, stream()));
+  const float *wdev = m->ola_w;
   const int64_t rows = (int64_t)B * S * C;
   DCB_CUDA(cudaMemsetAsync(out, 0, (size_t)rows * length * 4, stream()));
   for (const auto &bt : p.full_batches) {
@@ -889,16 +918,10 @@ static int apply_split(DcbModel *m, const float *mix, int B, int length, float *
         out, slot->out, wdev, (int)rows, length, valid, off, y0, this_len);
     DCB_LAUNCHED();
   }
-  std::vector<float> inv((size_t)length);
-  for (int t = 0; t < length; t++) inv[t] = sumw[t] > 0.0 ? (float)(1.0 / sumw[t]) : 0.0f;
-  float *invd = dalloc(length);
-  DCB_CUDA(cudaMemcpyAsync(invd, inv.data(), (size_t)length * 4, cudaMemcpyHostToDevice, stream()));
-  k_scale_time<<<grid_for(rows * length, 256), 256, 0, stream()>>>(out, invd, rows, length);
+  // divide by the weight sum of every segment (all shards'), summed on the device
+  k_scale_ola<<<grid_for(length, 256), 256, 0, stream()>>>(out, wdev, rows, length, p.seg,
+                                                           p.stride, (int)p.offsets.size());
   DCB_LAUNCHED();
-  // host vectors must outlive the async copies
-  DCB_CUDA(cudaStreamSynchronize(stream()));
-  dfree(invd);
-  dfree(wdev);
   return 0;
 }
 
@@ -1065,7 +1088,11 @@ int dcb_apply(DcbModel *m, const float *mix, int B, int T, float *out, const Dcb
     fail("apply: split=0 is not supported by this engine");
     return -1;
   }
-  if (o->shifts <= 0) return apply_split(m, mix, B, T, out, *o);
+  if (o->shifts <= 0) {
+    if (apply_split(m, mix, B, T, out, *o) < 0) return -1;
+    DCB_CUDA(cudaStreamSynchronize(stream()));
+    return failed() ? -1 : 0;
+  }
   const int max_shift = (int)(0.5f * (float)c.samplerate);
   const int Lp = T + 2 * max_shift;
   float *padded = dalloc((size_t)B * C * Lp);

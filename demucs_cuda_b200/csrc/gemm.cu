@@ -1,15 +1,13 @@
 // tcgen05 GEMM family for sm_100a.
 //
-// One CTA computes a 128 x BN output tile with a warp-specialised pipeline:
-//   warps 0-3  A-operand producers when A is gathered (implicit im2col from fp32
-//              activations, converted to fp16 with round-to-nearest-even as the reference's
-//              dk_im2col_half does), then the epilogue (TMEM -> registers -> fused
-//              bias / GELU / GLU / residual / layout transform -> global);
-//   warp 4     TMA producer (B tiles, and A tiles when A is already fp16 rows);
-//   warp 5     TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=BN, K=16 steps) and
-//              tcgen05.commit, which frees operand stages and finally signals the epilogue.
-// Operands use the K-major SWIZZLE_128B layout (see umma.cuh); a STAGES-deep smem ring
-// (mbarrier full/empty pairs) overlaps loads with MMAs.
+// Persistent CTAs (two per SM) walk 128 x BN output tiles with a warp-specialised pipeline:
+// gather warps build the A operand by implicit im2col from fp32 activations (converted to
+// fp16 with round-to-nearest-even, as the reference's dk_im2col_half does) or a TMA warp
+// loads fp16 rows; the TMA warp loads B tiles; one thread issues tcgen05.mma into a TMEM
+// accumulator that is double-buffered, so the epilogue warps (TMEM -> registers -> fused
+// bias / GELU / GLU / residual / layout transform -> global) of one tile overlap the loads
+// and MMAs of the next.  Operands use the K-major SWIZZLE_128B layout (see umma.cuh); a
+// ring of shared-memory stages with mbarrier full/empty pairs feeds the MMAs.
 //
 // The same kernels serve dk_gemm_half (backend.h:117-122), the implicit-GEMM convolutions
 // (replacing im2col + GEMM + bias, ops.c:31-77), the stride-phase transposed convolutions
@@ -32,7 +30,7 @@ struct Shape {
   int nkb;      // K blocks of 64
   int stages;
   int a_shared, b_shared;
-  int tmem_cols;
+  int mtiles, ntiles, batch;  // output tiles of 128 x BN per batch entry
 };
 
 // ------------------------------------------------------------- epilogue
@@ -127,10 +125,15 @@ static __device__ __forceinline__ void store_elem(const Epi &e, const Shape &s, 
 
 // GLU pair (a = column c of the tile's first half, b = same column of the second half)
 static __device__ __forceinline__ void store_glu(const Epi &e, int64_t o, const RowInfo &ri,
-                                                 float va, float vb) {
+                                                 float va, float vb, int64_t img) {
   if (o >= e.O) return;
   float a = va + (e.bias ? e.bias[o] : 0.f);
   float b = vb + (e.bias ? e.bias[e.O + o] : 0.f);
+  if (e.act == 3) {
+    const float mu = e.gn_mean[img], rs = e.gn_rstd[img];
+    a = (a - mu) * rs * e.gn_w[o] + e.gn_b[o];
+    b = (b - mu) * rs * e.gn_w[e.O + o] + e.gn_b[e.O + o];
+  }
   float val = a * sigmoid_f(b);
   int64_t off = ri.base + o * e.oC + (int64_t)ri.ho * e.oH + ri.wo;
   if (e.res) val = e.res[off] + e.scale[o] * val;
@@ -213,25 +216,57 @@ static __device__ __forceinline__ void store_chunk16(const Epi &e, const Shape &
 }
 
 // ------------------------------------------------------------- tensor-core kernel
-constexpr int kProdWarps = 8;             // warps 0-7: gather producers, then epilogue
-constexpr int kTmaWarp = kProdWarps;      // warp 8
-constexpr int kMmaWarp = kProdWarps + 1;  // warp 9
-constexpr int kThreads = 32 * (kProdWarps + 2);
+// Persistent: each CTA walks output tiles blockIdx.x, +gridDim.x, ... (N tiles fastest, so
+// a gathered A row block is re-read from L1/L2 while it is hot).  Warp roles:
+//   warps 0-3 (0-7 without a gather)  epilogue: TMEM lane quarter (warp & 3); with 8 warps
+//                                     warp >> 2 picks the half of the tile's columns;
+//   warps 4-7 (gather only)            A producers: one tile row per thread, 64 K columns
+//                                     per stage (implicit im2col, fp32 -> fp16 RNE);
+//   warp 8                             TMA: B tiles (and A tiles when A is fp16 rows);
+//   warp 9                             TMEM allocation; lane 0 issues tcgen05.mma.
+// The accumulator is double-buffered in TMEM for N tiles up to 128 columns, so the
+// epilogue of tile i overlaps the operand loads and MMAs of tile i+1.
+constexpr int kTmaWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kThreads = 320;
+
+template <int BN, bool GATHER>
+struct UmmaCfg {
+  static constexpr int kEpiWarps = GATHER ? 4 : 8;
+  static constexpr int kBufs = BN <= 128 ? 2 : 1;
+  static constexpr int kAccCols = BN < 32 ? 32 : BN;
+  static constexpr int kTmemCols = kAccCols * kBufs;  // a power of two >= 32
+  static constexpr uint32_t kBTileBytes = BN * 128;
+  static constexpr int kStageFloats = GATHER ? 4 * 32 * 32 : 0;  // per-warp transposes
+};
+
+static __device__ __forceinline__ void tile_coords(const Shape &s, int64_t tile, int &bz,
+                                                   int64_t &m0, int &nt) {
+  const int64_t per_b = (int64_t)s.mtiles * s.ntiles;
+  bz = (int)(tile / per_b);
+  const int64_t rem = tile - (int64_t)bz * per_b;
+  const int64_t mt = rem / s.ntiles;
+  nt = (int)(rem - mt * s.ntiles);
+  m0 = mt * kBM;
+}
 
 template <int BN, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 2)
     k_umma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
            const Shape s, const Gather g, const Epi e) {
+  using Cfg = UmmaCfg<BN, GATHER>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  constexpr uint32_t kBTileBytes = BN * 128;
   const int stages = s.stages;
   uint8_t *sA = smem;
   uint8_t *sB = smem + stages * kATileBytes;
-  uint64_t *full = (uint64_t *)(sB + stages * kBTileBytes);
+  float *stg = (float *)(sB + stages * Cfg::kBTileBytes);
+  uint64_t *full = (uint64_t *)(stg + Cfg::kStageFloats);
   uint64_t *empty = full + stages;
-  uint64_t *done = empty + stages;
-  uint32_t *tslot = (uint32_t *)(done + 1);
+  uint64_t *acc_full = empty + stages;
+  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *fin = acc_empty + 2;
+  uint32_t *tslot = (uint32_t *)(fin + 1);
   int2 *ktab = (int2 *)(tslot + 2);
 
   // a fault recorded by an earlier kernel: end this grid at once (uniform CTA decision)
@@ -240,20 +275,22 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (s_abort) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nt = blockIdx.y, bz = blockIdx.z;
-  const int64_t m0 = (int64_t)blockIdx.x * kBM;
-  const int n0 = nt * BN;
+  const int64_t ntiles_total = (int64_t)s.mtiles * s.ntiles * s.batch;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; i++) {
-      mbar_init(&full[i], 1 + (GATHER ? kProdWarps : 0));
+      mbar_init(&full[i], 1 + (GATHER ? 4 : 0));
       mbar_init(&empty[i], 1);
     }
-    mbar_init(done, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], Cfg::kEpiWarps);
+    }
+    mbar_init(fin, 1);
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
-    tmem_alloc(tslot, (uint32_t)s.tmem_cols);
+    tmem_alloc(tslot, (uint32_t)Cfg::kTmemCols);
     tmem_relinquish();
   }
   if (GATHER) {
@@ -281,47 +318,78 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       tma_prefetch_desc(&tmB);
       if (!GATHER) tma_prefetch_desc(&tmA);
-      const uint32_t bytes = kBTileBytes + (GATHER ? 0u : kATileBytes);
-      const int cA = s.a_shared ? 0 : bz, cB = s.b_shared ? 0 : bz;
-      for (int kb = 0; kb < s.nkb; kb++) {
-        const int st = kb % stages;
-        const uint32_t ph = (uint32_t)(kb / stages) & 1u;
-        if (!mbar_wait(&empty[st], ph ^ 1u, kFaultEmpty)) break;
-        mbar_expect_tx(&full[st], bytes);
-        tma_load_3d(sB + st * kBTileBytes, &tmB, &full[st], kb * kBK, n0, cB);
-        if (!GATHER) tma_load_3d(sA + st * kATileBytes, &tmA, &full[st], kb * kBK, (int)m0, cA);
+      const uint32_t bytes = Cfg::kBTileBytes + (GATHER ? 0u : kATileBytes);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
+        int bz, nt;
+        int64_t m0;
+        tile_coords(s, tile, bz, m0, nt);
+        const int cA = s.a_shared ? 0 : bz, cB = s.b_shared ? 0 : bz;
+        for (int kb = 0; kb < s.nkb; kb++, it++) {
+          const int st = (int)(it % (uint32_t)stages);
+          const uint32_t ph = (it / (uint32_t)stages) & 1u;
+          if (!mbar_wait(&empty[st], ph ^ 1u, kFaultEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[st], bytes);
+          tma_load_3d(sB + st * Cfg::kBTileBytes, &tmB, &full[st], kb * kBK, nt * BN, cB);
+          if (!GATHER)
+            tma_load_3d(sA + st * kATileBytes, &tmA, &full[st], kb * kBK, (int)m0, cA);
+        }
       }
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       const uint32_t idesc = idesc_f16_f32(kBM, BN);
-      for (int kb = 0; kb < s.nkb; kb++) {
-        const int st = kb % stages;
-        const uint32_t ph = (uint32_t)(kb / stages) & 1u;
-        if (!mbar_wait(&full[st], ph, kFaultFull)) break;
+      uint32_t it = 0, local = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x, local++) {
+        const uint32_t buf = local % (uint32_t)Cfg::kBufs;
+        const uint32_t use = local / (uint32_t)Cfg::kBufs;
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
         tc_fence_after();
-        const uint64_t ad = sw128_desc(smem_u32(sA + st * kATileBytes));
-        const uint64_t bd = sw128_desc(smem_u32(sB + st * kBTileBytes));
+        const uint32_t d = tmem + buf * (uint32_t)Cfg::kAccCols;
+        for (int kb = 0; kb < s.nkb; kb++, it++) {
+          const int st = (int)(it % (uint32_t)stages);
+          const uint32_t ph = (it / (uint32_t)stages) & 1u;
+          if (!mbar_wait(&full[st], ph, kFaultFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(smem_u32(sA + st * kATileBytes));
+          const uint64_t bd = sw128_desc(smem_u32(sB + st * Cfg::kBTileBytes));
 #pragma unroll
-        for (int k = 0; k < kBK / 16; k++) {
-          // +32 bytes per K=16 step inside the 128-byte swizzle row (>> 4 = 2)
-          umma_f16(tmem, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < kBK / 16; k++) {
+            // +32 bytes per K=16 step inside the 128-byte swizzle row (>> 4 = 2)
+            umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[st]);
         }
-        umma_commit(&empty[st]);
+        if (ok) umma_commit(&acc_full[buf]);
       }
-      umma_commit(done);
+      // every MMA of this CTA has completed before the accumulator is released
+      umma_commit(fin);
+      mbar_wait(fin, 0, kFaultDone);
     }
-  } else {
-    // ---- warps 0-7: warp w serves TMEM lane quarter (w & 3) = tile rows 32(w&3)..+31
-    // and half (w >> 2) of the K columns (gather) / accumulator columns (epilogue)
-    const int quarter = warp & 3, half = warp >> 2;
-    const int r = quarter * 32 + lane;  // tile row 0..127
-    if (GATHER) {
+  } else if (GATHER && warp >= 4) {
+    // ---- warps 4-7: A producers, tile row r = 32 (warp - 4) + lane, all 64 K columns
+    const int r = (warp - 4) * 32 + lane;
+    const float *__restrict__ x = g.x;
+    const float *__restrict__ x2 = g.x2;
+    const int64_t hw = (int64_t)g.Ho * g.Wo;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
+      int bz, nt;
+      int64_t m0;
+      tile_coords(s, tile, bz, m0, nt);
       const int64_t p = m0 + r;
       int64_t base = 0;
       int h0 = -(1 << 20), w0 = 0;
       if (p < s.M) {
-        const int64_t hw = (int64_t)g.Ho * g.Wo;
         const int64_t n = p / hw, rem = p - n * hw;
         const int ho = (int)(rem / g.Wo), wo = (int)(rem - (int64_t)ho * g.Wo);
         const int64_t n1 = n / g.N2, n2 = n - n1 * g.N2;
@@ -329,36 +397,38 @@ __global__ void __launch_bounds__(kThreads, 2)
         w0 = wo * g.SW - g.PW;
         base = n1 * g.sN1 + n2 * g.sN2 + (int64_t)h0 * g.sH + w0;
       }
-      const float *__restrict__ x = g.x;
-      const float *__restrict__ x2 = g.x2;
-      constexpr int KH2 = kBK / 2;  // 32 columns of each K block per thread
-      for (int kb = 0; kb < s.nkb; kb++) {
-        const int st = kb % stages;
-        const uint32_t ph = (uint32_t)(kb / stages) & 1u;
-        if (!mbar_wait(&empty[st], ph ^ 1u, kFaultEmpty)) break;
-        const int2 *kt = ktab + kb * kBK + half * KH2;
-        float v[KH2];
+      for (int kb = 0; kb < s.nkb; kb++, it++) {
+        const int st = (int)(it % (uint32_t)stages);
+        const uint32_t ph = (it / (uint32_t)stages) & 1u;
+        if (!mbar_wait(&empty[st], ph ^ 1u, kFaultEmpty)) {
+          ok = false;
+          break;
+        }
+        const int2 *kt = ktab + kb * kBK;
+        const uint32_t a_base = smem_u32(sA + st * kATileBytes);
+        // all 64 loads of the row are issued before the first shared-memory store
+        // (predicated loads in select form, so that none waits for another)
+        float v[kBK];
         if (x2) {
 #pragma unroll
-          for (int i = 0; i < KH2; i++) {
+          for (int i = 0; i < kBK; i++) {
             const int2 t = kt[i];
             const int hh = h0 + (t.y & 0xffff), ww = w0 + (t.y >> 16);
-            const bool ok = (unsigned)hh < (unsigned)g.H && (unsigned)ww < (unsigned)g.W;
-            v[i] = ok ? __ldg(x + base + t.x) + __ldg(x2 + base + t.x) : 0.f;
+            const bool in = (unsigned)hh < (unsigned)g.H && (unsigned)ww < (unsigned)g.W;
+            v[i] = in ? __ldg(x + base + t.x) + __ldg(x2 + base + t.x) : 0.f;
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < KH2; i++) {
+          for (int i = 0; i < kBK; i++) {
             const int2 t = kt[i];
             const int hh = h0 + (t.y & 0xffff), ww = w0 + (t.y >> 16);
-            const bool ok = (unsigned)hh < (unsigned)g.H && (unsigned)ww < (unsigned)g.W;
-            v[i] = ok ? __ldg(x + base + t.x) : 0.f;
+            const bool in = (unsigned)hh < (unsigned)g.H && (unsigned)ww < (unsigned)g.W;
+            v[i] = in ? __ldg(x + base + t.x) : 0.f;
           }
         }
-        const uint32_t a_base = smem_u32(sA + st * kATileBytes);
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
-          st_shared_v4(a_base + sw128_off(r, half * 4 + c), pack_h2(v[8 * c], v[8 * c + 1]),
+        for (int c = 0; c < 8; c++) {
+          st_shared_v4(a_base + sw128_off(r, c), pack_h2(v[8 * c], v[8 * c + 1]),
                        pack_h2(v[8 * c + 2], v[8 * c + 3]), pack_h2(v[8 * c + 4], v[8 * c + 5]),
                        pack_h2(v[8 * c + 6], v[8 * c + 7]));
         }
@@ -367,74 +437,94 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (lane == 0) mbar_arrive(&full[st]);
       }
     }
-
-    mbar_wait(done, 0, kFaultDone);
-    tc_fence_after();
-    const int64_t m = m0 + r;
-    const bool mv = m < s.M;
-    const RowInfo ri = mv ? decode_row(e, m) : RowInfo{0, 0, 0, 0, 0};
-    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-    if (e.mode == EPI_CONV) {
-      // Staged conv epilogue: chunks of up to 32 output channels go TMEM -> registers
-      // (bias, GELU / GLU) -> shared memory [channel][tile row] (the operand buffers are
-      // idle once `done` fired), then each warp stores 128 consecutive positions of one
-      // channel per step with 16-byte stores (scalar where positions are not contiguous).
-      float *stage = (float *)sA + half * (32 * kBM);
-      int64_t poff[4];
-      bool pv[4];
+  } else if (warp < Cfg::kEpiWarps) {
+    // ---- epilogue warps: TMEM lane quarter q = rows 32q..32q+31 of the tile
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;
+    float *wst = stg + quarter * (32 * 32);  // [32 columns][32 rows] of this warp (conv)
+    uint32_t local = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles_total; tile += gridDim.x, local++) {
+      int bz, nt;
+      int64_t m0;
+      tile_coords(s, tile, bz, m0, nt);
+      const int n0 = nt * BN;
+      const uint32_t buf = local % (uint32_t)Cfg::kBufs;
+      const uint32_t use = local / (uint32_t)Cfg::kBufs;
+      if (!mbar_wait(&acc_full[buf], use & 1u, kFaultDone)) break;
+      tc_fence_after();
+      const uint32_t trow =
+          tmem + buf * (uint32_t)Cfg::kAccCols + ((uint32_t)(quarter * 32) << 16);
+      const int64_t m = m0 + r;
+      if (GATHER && e.mode == EPI_CONV) {
+        // Staged conv epilogue: chunks of up to 32 output channels go TMEM -> registers
+        // (bias, GELU / GLU) -> this warp's transpose buffer [channel][row], then lane l
+        // stores rows 4(l & 7)..+3 of channel (l >> 3) + 4j: 16-byte stores where the four
+        // positions are contiguous and aligned, element stores otherwise.
+        const int rq = 4 * (lane & 7);
+        int64_t poff[4];
+        bool pv[4];
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int64_t mm = m0 + 4 * lane + i;
-        pv[i] = mm < s.M;
-        poff[i] = 0;
-        if (pv[i]) {
-          const RowInfo rq = decode_row(e, mm);
-          poff[i] = rq.base + (int64_t)rq.ho * e.oH + rq.wo;
-        }
-      }
-      const bool contig = pv[3] && poff[1] == poff[0] + 1 && poff[2] == poff[0] + 2 &&
-                          poff[3] == poff[0] + 3;
-      const bool glu = e.act == 2;
-      const int ncols = glu ? e.glu_half : BN;
-      const int per = ncols >= 32 ? ncols / 2 : (half == 0 ? ncols : 0);
-      const int c_beg = ncols >= 32 ? half * per : 0;
-      const int obase = glu ? nt * e.glu_half : n0;
-      for (int c0 = c_beg; c0 < c_beg + per; c0 += 32) {
-        const int cw = c_beg + per - c0 >= 32 ? 32 : 16;
-        for (int sub = 0; sub < cw; sub += 16) {
-          float va[16];
-          tmem_ld16(trow + c0 + sub, va);
-          if (glu) {
-            float vb[16];
-            tmem_ld16(trow + e.glu_half + c0 + sub, vb);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-              const int o = obase + c0 + sub + i;
-              float val = 0.f;
-              if (o < e.O) {
-                const float a = va[i] + (e.bias ? e.bias[o] : 0.f);
-                const float b = vb[i] + (e.bias ? e.bias[e.O + o] : 0.f);
-                val = a * sigmoid_f(b);
-              }
-              stage[(sub + i) * kBM + r] = val;
-            }
-          } else {
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-              const int o = obase + c0 + sub + i;
-              float val = va[i] + ((e.bias && o < e.O) ? e.bias[o] : 0.f);
-              if (e.act == 1) val = gelu_f(val);
-              stage[(sub + i) * kBM + r] = val;
-            }
+        for (int i = 0; i < 4; i++) {
+          const int64_t mm = m0 + quarter * 32 + rq + i;
+          pv[i] = mm < s.M;
+          poff[i] = 0;
+          if (pv[i]) {
+            const RowInfo ri = decode_row(e, mm);
+            poff[i] = ri.base + (int64_t)ri.ho * e.oH + ri.wo;
           }
         }
-        asm volatile("bar.sync %0, %1;" ::"r"(1 + half), "r"(128) : "memory");
-        for (int cc = quarter; cc < cw; cc += 4) {
-          const int o = obase + c0 + cc;
-          if (o < e.O) {
-            const float4 v4 = *(const float4 *)(stage + cc * kBM + 4 * lane);
+        const bool contig = pv[3] && poff[1] == poff[0] + 1 && poff[2] == poff[0] + 2 &&
+                            poff[3] == poff[0] + 3;
+        const bool glu = e.act >= 2;
+        // act 3: GroupNorm statistics of this lane's row (one image per Ho * Wo rows)
+        float gmu = 0.f, grs = 0.f;
+        if (e.act == 3 && m < s.M) {
+          const int64_t img = m / ((int64_t)e.Ho * e.Wo);
+          gmu = e.gn_mean[img];
+          grs = e.gn_rstd[img];
+        }
+        const int ncols = glu ? e.glu_half : BN;
+        const int obase = glu ? nt * e.glu_half : n0;
+        for (int c0 = 0; c0 < ncols; c0 += 32) {
+          const int cw = ncols - c0 >= 32 ? 32 : 16;
+          for (int sub = 0; sub < cw; sub += 16) {
+            float va[16];
+            tmem_ld16(trow + c0 + sub, va);
+            if (glu) {
+              float vb[16];
+              tmem_ld16(trow + e.glu_half + c0 + sub, vb);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; i++) {
+                const int o = obase + c0 + sub + i;
+                float val = 0.f;
+                if (o < e.O) {
+                  float a = va[i] + (e.bias ? e.bias[o] : 0.f);
+                  float b = vb[i] + (e.bias ? e.bias[e.O + o] : 0.f);
+                  if (e.act == 3) {
+                    a = (a - gmu) * grs * e.gn_w[o] + e.gn_b[o];
+                    b = (b - gmu) * grs * e.gn_w[e.O + o] + e.gn_b[e.O + o];
+                  }
+                  val = a * sigmoid_f(b);
+                }
+                wst[(sub + i) * 32 + lane] = val;
+              }
+            } else {
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; i++) {
+                const int o = obase + c0 + sub + i;
+                float val = va[i] + ((e.bias && o < e.O) ? e.bias[o] : 0.f);
+                if (e.act == 1) val = gelu_f(val);
+                wst[(sub + i) * 32 + lane] = val;
+              }
+            }
+          }
+          __syncwarp();
+          for (int cc = lane >> 3; cc < cw; cc += 4) {
+            const int o = obase + c0 + cc;
+            if (o >= e.O) continue;
+            const float4 v4 = *(const float4 *)(wst + cc * 32 + rq);
             float vv[4] = {v4.x, v4.y, v4.z, v4.w};
             const int64_t a = poff[0] + (int64_t)o * e.oC;
             const uintptr_t al = (uintptr_t)(e.y + a) | (e.res ? (uintptr_t)(e.res + a) : 0);
@@ -459,17 +549,24 @@ __global__ void __launch_bounds__(kThreads, 2)
               }
             }
           }
+          __syncwarp();
         }
-        asm volatile("bar.sync %0, %1;" ::"r"(1 + half), "r"(128) : "memory");
+      } else {
+        const bool mv = m < s.M;
+        const RowInfo ri = mv ? decode_row(e, m) : RowInfo{0, 0, 0, 0, 0};
+        constexpr int PER = Cfg::kEpiWarps == 8 ? (BN / 2 < 16 ? 16 : BN / 2) : BN;
+        const int cbeg = Cfg::kEpiWarps == 8 ? half * PER : 0;
+        for (int c0 = cbeg; c0 < cbeg + PER && c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(trow + c0, v);
+          tmem_wait_ld();
+          if (mv) store_chunk16(e, s, bz, m, (int64_t)n0 + c0, ri, v);
+        }
       }
-    } else {
-      constexpr int PER = BN / 2;  // >= 16
-      for (int c0 = half * PER; c0 < half * PER + PER; c0 += 16) {
-        float v[16];
-        tmem_ld16(trow + c0, v);
-        tmem_wait_ld();
-        if (mv) store_chunk16(e, s, bz, m, (int64_t)n0 + c0, ri, v);
-      }
+      // this warp's TMEM reads are complete: release the accumulator buffer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
 
@@ -477,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
-    tmem_dealloc(tmem, (uint32_t)s.tmem_cols);
+    tmem_dealloc(tmem, (uint32_t)Cfg::kTmemCols);
   }
 }
 
@@ -490,7 +587,7 @@ __global__ void k_simt(RowsA a, RowsA b, const Shape s, const Gather g, const Ep
   const int64_t total = (int64_t)s.M * ncols;
   DCB_GRID_STRIDE(idx, total) {
     const int64_t n = idx / s.M, m = idx - n * s.M;
-    const bool glu = e.mode == EPI_CONV && e.act == 2;
+    const bool glu = e.mode == EPI_CONV && e.act >= 2;
     // B rows used: n, or the interleaved GLU pair of output channel n
     int64_t rb0 = n, rb1 = -1;
     if (glu) {
@@ -532,7 +629,7 @@ __global__ void k_simt(RowsA a, RowsA b, const Shape s, const Gather g, const Ep
     }
     const RowInfo ri = decode_row(e, m);
     if (glu) {
-      store_glu(e, n, ri, acc0, acc1);
+      store_glu(e, n, ri, acc0, acc1, m / ((int64_t)e.Ho * e.Wo));
     } else {
       store_elem(e, s, bz, m, n, ri, acc0);
     }
@@ -600,25 +697,43 @@ static int pick_bn(int64_t M, int64_t N, int64_t batch) {
 }
 
 int gather_bn(int64_t M, int64_t N, bool glu) {
+  // at most 128 columns: a double-buffered accumulator, two CTAs per SM
   int bn = pick_bn(M, N, 1);
+  if (bn > 128) bn = 128;
   if (glu && bn < 32) bn = 32;
   return bn;
+}
+
+static int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  DCB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    n[dev] = v;
+  }
+  return n[dev];
 }
 
 template <int BN, bool GATHER>
 static void launch_umma(const CUtensorMap &ta, const CUtensorMap &tb, Shape s, const Gather &g,
                         const Epi &e, int64_t mtiles, int ntiles, int64_t batch) {
+  using Cfg = UmmaCfg<BN, GATHER>;
   const size_t table = GATHER ? (size_t)s.nkb * kBK * sizeof(int2) : 0;
-  const size_t stage_bytes = kATileBytes + (size_t)BN * 128;
-  // two CTAs per SM (TMEM <= 256 columns and <= ~110 KB shared memory each) so one
-  // CTA's gather / epilogue overlaps the other's MMAs
-  const size_t budget = 110 * 1024;
-  int stages = budget > table + 2048 ? (int)((budget - table - 2048) / stage_bytes) : 0;
+  const size_t stage_bytes = kATileBytes + (size_t)Cfg::kBTileBytes;
+  const size_t fixed = 1024 + (size_t)Cfg::kStageFloats * 4 + 16 + table;
+  // two persistent CTAs per SM: <= 111 KB of dynamic shared memory and <= 256 TMEM
+  // columns each
+  const size_t budget = 111 * 1024;  // + 1 KB static + 1 KB reserved, twice <= 228 KB
+  int stages = budget > fixed + 8 * 24 ? (int)((budget - fixed - 8 * 24) / (stage_bytes + 16))
+                                       : 0;
   if (stages > 8) stages = 8;
-  if (stages > s.nkb + 1) stages = s.nkb + 1;
   if (stages < 2) stages = 2;
   s.stages = stages;
-  const size_t smem = 1024 + stages * stage_bytes + (2 * stages + 1) * 8 + 16 + table;
+  const size_t smem = fixed + (size_t)stages * stage_bytes + (2 * (size_t)stages + 5) * 8;
   DCB_REQUIRE(smem <= 226 * 1024, "gemm: shared memory %zu exceeds the per-CTA limit", smem);
   static size_t attr = 0;  // dynamic shared memory opted in so far for this instantiation
   if (smem > attr) {
@@ -626,13 +741,15 @@ static void launch_umma(const CUtensorMap &ta, const CUtensorMap &tb, Shape s, c
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr = smem;
   }
-  s.tmem_cols = BN < 32 ? 32 : BN;
-  for (int64_t b0 = 0; b0 < batch; b0 += 65535) {
-    DCB_REQUIRE(b0 == 0, "gemm: batch > 65535 on the tensor-core path");
-    dim3 grid((unsigned)mtiles, (unsigned)ntiles, (unsigned)(batch < 65535 ? batch : 65535));
-    k_umma<BN, GATHER><<<grid, kThreads, smem, stream()>>>(ta, tb, s, g, e);
-    DCB_LAUNCHED();
-  }
+  DCB_REQUIRE(mtiles < (1ll << 31) && batch < (1ll << 31), "gemm: too many tiles");
+  s.mtiles = (int)mtiles;
+  s.ntiles = ntiles;
+  s.batch = (int)batch;
+  const int64_t tiles = mtiles * ntiles * batch;
+  const int64_t slots = 2ll * sm_count();
+  const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
+  k_umma<BN, GATHER><<<grid, kThreads, smem, stream()>>>(ta, tb, s, g, e);
+  DCB_LAUNCHED();
 }
 
 template <bool GATHER>
@@ -644,7 +761,13 @@ static void dispatch_umma(int bn, const CUtensorMap &ta, const CUtensorMap &tb, 
     case 32: launch_umma<32, GATHER>(ta, tb, s, g, e, mt, ntl, batch); break;
     case 64: launch_umma<64, GATHER>(ta, tb, s, g, e, mt, ntl, batch); break;
     case 128: launch_umma<128, GATHER>(ta, tb, s, g, e, mt, ntl, batch); break;
-    default: launch_umma<256, GATHER>(ta, tb, s, g, e, mt, ntl, batch); break;
+    default:
+      if constexpr (GATHER) {
+        DCB_REQUIRE(false, "conv: N tile %d is wider than the gather kernel's 128", bn);
+      } else {
+        launch_umma<256, GATHER>(ta, tb, s, g, e, mt, ntl, batch);
+      }
+      break;
   }
 }
 
@@ -715,7 +838,7 @@ void gemm_gather(const Gather &g, int64_t M, const uint16_t *w, int64_t N, int64
   s.nkb = (g.K + kBK - 1) / kBK;
   s.a_shared = 1;
   s.b_shared = 1;
-  const bool glu = e.mode == EPI_CONV && e.act == 2;
+  const bool glu = e.mode == EPI_CONV && e.act >= 2;
   const int bn = bn_hint ? bn_hint : gather_bn(M, N, glu);
   const double images = (double)M / ((double)g.Ho * g.Wo);
   const double n_alg = e.mode == EPI_CONVTR ? (double)e.O * e.stride : (glu ? 2.0 * e.O : e.O);

@@ -36,7 +36,7 @@ struct Epi {
   int mode = EPI_GEMM;
   int vec = 0;  // 16-column vector stores allowed (set by the launcher after checks)
   const float *bias = nullptr;
-  int act = 0;  // 0 none, 1 gelu, 2 glu
+  int act = 0;  // 0 none, 1 gelu, 2 glu, 3 GroupNorm + glu (EPI_CONV)
   // EPI_GEMM
   float *C = nullptr;
   int64_t ldc = 0, strideC = 0;
@@ -51,6 +51,9 @@ struct Epi {
   int glu_half = 0;    // columns per half inside one N tile (GLU)
   const float *res = nullptr;  // EPI_CONV: y = res + scale[o] * value (DConv residual)
   const float *scale = nullptr;
+  // act 3: GroupNorm(1) of the pre-GLU output with per-image statistics (image = row /
+  // (Ho * Wo)) and the affine of all 2 * O channels, then GLU
+  const float *gn_mean = nullptr, *gn_rstd = nullptr, *gn_w = nullptr, *gn_b = nullptr;
   // EPI_CONVTR
   int stride = 4, crop = 0, out_len = 0, axis_h = 1;
   // EPI_ROWS_*

@@ -234,6 +234,121 @@ __global__ void __launch_bounds__(kGnFusedThreads)
   }
 }
 
+// DConv hidden rows (layers.c:24-53, the freq branch viewed as B*Fr rows [hid][T]):
+// GroupNorm(1) + GELU in place, one CTA per row, and the GroupNorm(1) statistics of the
+// row's next 1x1 conv output z = W16 . fp16(h) + b without forming z.  With S_j the sums
+// and Q the Gram matrix of fp16(h) over t, and zc = {G = W16^T W16, u = column sums of
+// W16, v = W16^T b, sum b, sum b^2} (fp64):
+//   sum z   = T sum(b) + u . S
+//   sum z^2 = <G, Q> + 2 v . S + T sum(b^2)
+// zmean / zrstd receive the mean and 1 / sqrt(var + eps) of z over its C2 * T values.
+__global__ void __launch_bounds__(kGnFusedThreads)
+    k_gn_gelu_zstats(RowView v, float *__restrict__ y, const float *__restrict__ w,
+                     const float *__restrict__ bb, float eps, const double *__restrict__ zc,
+                     int C2, float *__restrict__ zmean, float *__restrict__ zrstd) {
+  extern __shared__ float hs[];  // [hid][T]: fp16-rounded GELU outputs of this row
+  __shared__ double sh[2][kGnFusedThreads / 32];
+  const int64_t row = blockIdx.x;
+  const int64_t b = row / v.Fr, f = row - b * v.Fr;
+  const float *xr = v.x + b * v.sB + f * v.sF;
+  const int hid = v.C, T = v.T;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  double s = 0.0, ss = 0.0;
+  for (int c = 0; c < hid; c++) {
+    const float *xc = xr + c * v.sC;
+    for (int t = threadIdx.x; t < T; t += kGnFusedThreads) {
+      const double a = (double)xc[t];
+      s += a;
+      ss += a * a;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  }
+  if (lane == 0) {
+    sh[0][wid] = s;
+    sh[1][wid] = ss;
+  }
+  __syncthreads();
+  s = 0.0;
+  ss = 0.0;
+  for (int i = 0; i < kGnFusedThreads / 32; i++) {
+    s += sh[0][i];
+    ss += sh[1][i];
+  }
+  const double n = (double)hid * T;
+  const double md = s / n;
+  double vd = ss / n - md * md;
+  if (vd < 0.0) vd = 0.0;
+  const float m = (float)md;
+  const float rs = 1.0f / sqrtf((float)vd + eps);
+  float *yr = y + b * v.sB + f * v.sF;
+  for (int c = 0; c < hid; c++) {
+    const float *xc = xr + c * v.sC;
+    float *yc = yr + c * v.sC;
+    const float wc = w[c], bc = bb[c];
+    for (int t = threadIdx.x; t < T; t += kGnFusedThreads) {
+      const float h = gelu_f((xc[t] - m) * rs * wc + bc);
+      yc[t] = h;
+      hs[c * T + t] = __half2float(__float2half_rn(h));
+    }
+  }
+  __syncthreads();  // every thread has read sh[] and written hs[]
+  // one warp per entry: the hid (hid + 1) / 2 upper Gram entries, then the hid sums
+  const double *G = zc, *u = zc + hid * hid, *vv = u + hid;
+  const int npair = hid * (hid + 1) / 2;
+  double psum = 0.0, psq = 0.0;
+  for (int p = wid; p < npair + hid; p += kGnFusedThreads / 32) {
+    int j, k;
+    if (p < npair) {
+      j = 0;
+      int q = p;
+      while (q >= hid - j) {
+        q -= hid - j;
+        j++;
+      }
+      k = j + q;
+    } else {
+      j = p - npair;
+      k = -1;
+    }
+    const float *hj = hs + j * T;
+    const float *hk = k >= 0 ? hs + k * T : nullptr;
+    double acc = 0.0;
+    for (int t = lane; t < T; t += 32) acc += (double)(hk ? hj[t] * hk[t] : hj[t]);
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (k >= 0) {
+      psq += (j == k ? 1.0 : 2.0) * G[j * hid + k] * acc;
+    } else {
+      psum += u[j] * acc;
+      psq += 2.0 * vv[j] * acc;
+    }
+  }
+  __syncthreads();  // sh[] is reused
+  if (lane == 0) {
+    sh[0][wid] = psum;
+    sh[1][wid] = psq;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double sz = 0.0, szz = 0.0;
+    for (int i = 0; i < kGnFusedThreads / 32; i++) {
+      sz += sh[0][i];
+      szz += sh[1][i];
+    }
+    const double sb = zc[hid * hid + 2 * hid], sb2 = zc[hid * hid + 2 * hid + 1];
+    sz += (double)T * sb;
+    szz += (double)T * sb2;
+    const double nz = (double)C2 * T;
+    const double mz = sz / nz;
+    double vz = szz / nz - mz * mz;
+    if (vz < 0.0) vz = 0.0;
+    zmean[row] = (float)mz;
+    zrstd[row] = 1.0f / sqrtf((float)vz + eps);
+  }
+}
+
 // x[b][c][f][t] += emb[f][c] * alpha   (dc_add_freq_emb, htdemucs.c:114-134)
 __global__ void k_add_freq_emb(float *x, const float *__restrict__ emb, float alpha, int B,
                                int C, int Fr, int T, int emb_cols) {
@@ -344,6 +459,22 @@ __global__ void k_accumulate(float *out, const float *__restrict__ y,
 }
 
 // y = x * s[t] (final division by the summed transition weights)
+// x[r][t] *= 1 / sum_i w[t - off_i] over the segments i covering t (offsets i * stride,
+// i < noff): the weight normalisation of dc_apply_model (apply.c:295-300), summed in fp64
+// in segment order as the reference does, without a host-side weight-sum array.
+__global__ void k_scale_ola(float *x, const float *__restrict__ w, int64_t rows, int64_t L,
+                            int seg, int stride, int noff) {
+  DCB_GRID_STRIDE(t, L) {
+    const int64_t lo = t < seg ? 0 : (t - seg) / stride + 1;
+    int64_t hi = t / stride;
+    if (hi > noff - 1) hi = noff - 1;
+    double s = 0.0;
+    for (int64_t i = lo; i <= hi; i++) s += (double)w[t - i * stride];
+    const float inv = s > 0.0 ? (float)(1.0 / s) : 0.0f;
+    for (int64_t r = 0; r < rows; r++) x[r * L + t] *= inv;
+  }
+}
+
 __global__ void k_scale_time(float *x, const float *__restrict__ s, int64_t rows, int64_t L) {
   const int64_t total = rows * L;
   DCB_GRID_STRIDE(i, total) { x[i] = x[i] * s[i % L]; }
