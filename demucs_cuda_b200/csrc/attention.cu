@@ -3,23 +3,24 @@
 // [GEMM S = Q K^T -> dk_softmax_to_half -> GEMM O = P V] loop (ops.c:390-443,
 // attn.cu:26-89).
 //
-// CTA = 128 query rows of one head, 192 threads:
-//   warps 0-3  one query row per thread: read the S row from TMEM, online softmax in fp32
-//              (exp2 domain, running max / sum; the O accumulator stays in TMEM and is
-//              rescaled there only when the maximum grows by more than 2^8), write P as
-//              fp16 into shared memory in the UMMA A-operand layout;
-//   warp 4     TMA producer: Q once, then K and V^T tiles of 128 keys into a 2-stage ring;
-//   warp 5     TMEM owner; lane 0 issues S = Q K^T (M=128, N=128, K=64) and
-//              O += P V (M=128, N=64, K=128) accumulating in TMEM over all key blocks.
-// 112 KB of shared memory and ~100 registers per thread: two CTAs share an SM, so one
-// CTA's softmax overlaps the other's MMAs.
-// Head dims up to 64 are zero-extended to 64 by TMA out-of-bounds fill; keys past Tk read
-// as zero and are masked out of the softmax.
+// CTA = 128 query rows of one head, 192 threads, key blocks of 64:
+//   warps 0-3  one query row per thread: read the 64 scores of a key block from TMEM once,
+//              online softmax in fp32 (exp2 domain, running max / sum; the O accumulator
+//              stays in TMEM and is rescaled there only when the maximum grows by more
+//              than 2^8), write P as fp16 into shared memory in the UMMA A-operand layout;
+//   warp 4     TMA producer: Q once, then K and V^T blocks into a 3-stage ring;
+//   warp 5     TMEM owner; lane 0 issues S = Q K^T (M=128, N=64, K=64) into one of two
+//              TMEM score buffers and O += P V (M=128, N=64, K=64) from one of two P
+//              buffers, so the scores of block j+1 (and j+2) are computed while the
+//              softmax warps work on block j.
+// TMEM: S0 | S1 | O (64 columns each, 256 allocated); 97 KB of shared memory: two CTAs
+// share an SM.  Head dims up to 64 are zero-extended to 64 by TMA out-of-bounds fill; keys
+// past Tk read as zero and are masked out of the softmax.
 //
 // Inputs are fp16 exactly as the reference rounds them (split_heads of the fp32
 // projections): Q [BH][Tq][hd], K [BH][Tk][hd], V^T [BH][hd][Tkp].  The reference rounds
 // the normalised probabilities to fp16; here the unnormalised exp(s - m_running) is
-// rounded and the division by the row sum happens at the end (same fp16 operand width).
+// rounded (same fp16 operand width) and O is divided by the fp32 row sum at the end.
 #include <cudaTypedefs.h>
 #include <math.h>
 
@@ -28,12 +29,13 @@
 namespace dcb {
 
 constexpr int kAttnThreads = 192;
-constexpr int kQ = 128, kKV = 128, kHD = 64;
+constexpr int kQ = 128, kKV = 64, kHD = 64;
 constexpr uint32_t kQBytes = kQ * kHD * 2;      // 16 KB
-constexpr uint32_t kKBytes = kKV * kHD * 2;     // 16 KB
-constexpr uint32_t kVBytes = kHD * kKV * 2;     // 16 KB (two 64-key halves)
-constexpr uint32_t kPBytes = kQ * kKV * 2;      // 32 KB (two 64-key halves)
-constexpr int kAttnStages = 2;
+constexpr uint32_t kKBytes = kKV * kHD * 2;     // 8 KB
+constexpr uint32_t kVBytes = kHD * kKV * 2;     // 8 KB
+constexpr uint32_t kPBytes = kQ * kKV * 2;      // 16 KB per buffer
+constexpr int kAttnStages = 3;
+constexpr size_t kAttnSmem = kQBytes + kAttnStages * (kKBytes + kVBytes) + 2 * kPBytes + 256;
 
 struct AttnArgs {
   int Tq, Tk, H, hd, BH;
@@ -52,13 +54,14 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   uint8_t *sK = sQ + kQBytes;
   uint8_t *sV = sK + kAttnStages * kKBytes;
   uint8_t *sP = sV + kAttnStages * kVBytes;
-  uint64_t *bar = (uint64_t *)(sP + kPBytes);
+  uint64_t *bar = (uint64_t *)(sP + 2 * kPBytes);
   uint64_t *q_full = bar;
   uint64_t *kv_full = bar + 1;                 // [stages]
   uint64_t *kv_empty = kv_full + kAttnStages;  // [stages]
-  uint64_t *s_full = kv_empty + kAttnStages;
-  uint64_t *p_full = s_full + 1;
-  uint64_t *o_full = p_full + 1;
+  uint64_t *s_full = kv_empty + kAttnStages;   // [2] score buffers
+  uint64_t *p_full = s_full + 2;               // [2] P buffers written
+  uint64_t *p_empty = p_full + 2;              // [2] PV of a P buffer complete
+  uint64_t *o_full = p_empty + 2;
   uint32_t *tslot = (uint32_t *)(o_full + 1);
   uint32_t *s_abort = tslot + 1;
 
@@ -84,8 +87,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_empty[i], 1);
+    }
     mbar_init(o_full, 1);
     fence_mbar_init();
   }
@@ -97,7 +103,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t tS = tmem, tO = tmem + 128;
+  const uint32_t tO = tmem + 2 * kKV;
 
   if (warp == 4) {
     if (lane == 0) {
@@ -113,7 +119,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         mbar_expect_tx(&kv_full[st], kKBytes + kVBytes);
         tma_load_3d(sK + st * kKBytes, &tmK, &kv_full[st], 0, j * kKV, bh);
         tma_load_3d(sV + st * kVBytes, &tmV, &kv_full[st], j * kKV, 0, bh);
-        tma_load_3d(sV + st * kVBytes + kVBytes / 2, &tmV, &kv_full[st], j * kKV + 64, 0, bh);
       }
     }
   } else if (warp == 5) {
@@ -122,34 +127,38 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       const uint32_t id_o = idesc_f16_f32(kQ, kHD);
       bool ok = mbar_wait(q_full, 0, kFaultAttn);
       const uint64_t qd = sw128_desc(smem_u32(sQ));
-      for (int j = 0; j < nkv && ok; j++) {
+      // S(j) = Q K(j)^T into score buffer j & 1
+      auto issue_s = [&](int j) -> bool {
         const int st = j % kAttnStages;
-        const uint32_t ph = (uint32_t)(j / kAttnStages) & 1u;
-        if (!mbar_wait(&kv_full[st], ph, kFaultAttn)) break;
+        if (!mbar_wait(&kv_full[st], (uint32_t)(j / kAttnStages) & 1u, kFaultAttn)) return false;
         tc_fence_after();
-        // S(j) may overwrite S(j-1): the softmax warps finished reading it before they
-        // arrived on p_full(j-1), which this thread waited for before PV(j-1)
         const uint64_t kd = sw128_desc(smem_u32(sK + st * kKBytes));
+        const uint32_t dS = tmem + (uint32_t)(j & 1) * kKV;
 #pragma unroll
-        for (int k = 0; k < kHD / 16; k++) umma_f16(tS, qd + 2u * k, kd + 2u * k, id_s, k > 0);
-        umma_commit(s_full);
-        if (!mbar_wait(p_full, (uint32_t)j & 1u, kFaultAttn)) break;
+        for (int k = 0; k < kHD / 16; k++) umma_f16(dS, qd + 2u * k, kd + 2u * k, id_s, k > 0);
+        umma_commit(&s_full[j & 1]);
+        return true;
+      };
+      for (int j = 0; j < nkv && j < 2 && ok; j++) ok = issue_s(j);
+      for (int j = 0; j < nkv && ok; j++) {
+        if (!mbar_wait(&p_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn)) break;
         tc_fence_after();
         // O += P(j) V(j); O lives in TMEM across all key blocks
+        const int st = j % kAttnStages;
+        const uint64_t pd = sw128_desc(smem_u32(sP + (j & 1) * kPBytes));
+        const uint64_t vd = sw128_desc(smem_u32(sV + st * kVBytes));
 #pragma unroll
-        for (int k = 0; k < kKV / 16; k++) {
-          const uint32_t half = (uint32_t)(k >> 2) * (kPBytes / 2);
-          const uint32_t vhalf = (uint32_t)(k >> 2) * (kVBytes / 2);
-          const uint64_t pd = sw128_desc(smem_u32(sP) + half) + 2u * (k & 3);
-          const uint64_t vd = sw128_desc(smem_u32(sV + st * kVBytes) + vhalf) + 2u * (k & 3);
-          umma_f16(tO, pd, vd, id_o, (j > 0 || k > 0) ? 1u : 0u);
-        }
+        for (int k = 0; k < kKV / 16; k++)
+          umma_f16(tO, pd + 2u * k, vd + 2u * k, id_o, (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&p_empty[j & 1]);
         umma_commit(&kv_empty[st]);
+        // score buffer j & 1 is free: the softmax warps read S(j) before arriving on p_full
+        if (j + 2 < nkv) ok = issue_s(j + 2);
       }
       umma_commit(o_full);
     }
   } else {
-    // softmax warps: one query row per thread, exp2 domain (scores pre-multiplied by
+    // softmax warps: one query row per thread, exp2 domain (scores scaled by
     // scale * log2 e).  The running maximum m is only raised, and O (in TMEM) rescaled,
     // when a block's maximum exceeds it by more than 8 (a factor 256): probabilities stay
     // <= 256, well inside fp16, and most blocks need no rescale.
@@ -157,31 +166,38 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const uint32_t lrow = (uint32_t)(warp * 32) << 16;
     const float sl2 = a.scale * 1.4426950408889634f;
     float m_run = -INFINITY, l_run = 0.f;
-    const uint32_t p_base = smem_u32(sP);
     bool ok = true;
     for (int j = 0; j < nkv && ok; j++) {
-      if (!mbar_wait(s_full, (uint32_t)j & 1u, kFaultAttn)) {
+      if (!mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      float v[kKV];
+      const uint32_t tS = tmem + (uint32_t)(j & 1) * kKV + lrow;
+#pragma unroll
+      for (int c = 0; c < kKV; c += 16) tmem_ld16(tS + c, *(float(*)[16])(v + c));
+      tmem_wait_ld();
       const int kbase = j * kKV;
-      float mx = -INFINITY;
+      if (kbase + kKV > a.Tk) {
 #pragma unroll
-      for (int c = 0; c < kKV; c += 16) {
-        float v[16];
-        tmem_ld16(tS + lrow + c, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-          if (kbase + c + i < a.Tk) mx = fmaxf(mx, v[i] * sl2);
-        }
+        for (int i = 0; i < kKV; i++)
+          if (kbase + i >= a.Tk) v[i] = -INFINITY;
       }
-      if (mx > m_run + 8.0f) {
+      float mx = v[0];
+#pragma unroll
+      for (int i = 1; i < kKV; i++) mx = fmaxf(mx, v[i]);
+      const float ms = mx * sl2;
+      if (ms > m_run + 8.0f) {
         if (j > 0) {
-          // rescale the accumulated O row and the running sum to the new maximum; every
-          // earlier PV has completed (s_full(j) was committed after them)
-          const float alpha = exp2f(m_run - mx);
+          // rescale the accumulated O row and the running sum to the new maximum once
+          // PV(j-1) has completed
+          if (!mbar_wait(&p_empty[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, kFaultAttn)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float alpha = exp2f(m_run - ms);
           l_run *= alpha;
 #pragma unroll
           for (int c = 0; c < kHD; c += 16) {
@@ -194,34 +210,32 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
           }
           tmem_wait_st();
         }
-        m_run = mx;
+        m_run = ms;
+      }
+      // P buffer j & 1 is free once PV(j-2) has completed
+      if (j >= 2 &&
+          !mbar_wait(&p_empty[j & 1], (uint32_t)((j - 2) >> 1) & 1u, kFaultAttn)) {
+        ok = false;
+        break;
       }
       float psum = 0.f;
+      uint32_t w[kKV / 2];
 #pragma unroll
-      for (int c = 0; c < kKV; c += 16) {
-        float v[16];
-        tmem_ld16(tS + lrow + c, v);
-        tmem_wait_ld();
-        uint32_t w[8];
-#pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const float p0 = kbase + c + i < a.Tk ? exp2f(v[i] * sl2 - m_run) : 0.f;
-          const float p1 = kbase + c + i + 1 < a.Tk ? exp2f(v[i + 1] * sl2 - m_run) : 0.f;
-          w[i >> 1] = pack_h2(p0, p1);
-          // the row sum uses the rounded values the MMA multiplies
-          psum += h2f_bits((uint16_t)(w[i >> 1] & 0xffffu)) +
-                  h2f_bits((uint16_t)(w[i >> 1] >> 16));
-        }
-        const int half = c >> 6, chunk = (c & 63) >> 3;
-        const uint32_t rowp = p_base + half * (kPBytes / 2);
-        st_shared_v4(rowp + sw128_off(r, chunk), w[0], w[1], w[2], w[3]);
-        st_shared_v4(rowp + sw128_off(r, chunk + 1), w[4], w[5], w[6], w[7]);
+      for (int i = 0; i < kKV; i += 2) {
+        const float p0 = exp2f(fmaf(v[i], sl2, -m_run));
+        const float p1 = exp2f(fmaf(v[i + 1], sl2, -m_run));
+        psum += p0 + p1;
+        w[i >> 1] = pack_h2(p0, p1);
       }
       l_run += psum;
+      const uint32_t prow = smem_u32(sP + (j & 1) * kPBytes);
+#pragma unroll
+      for (int c = 0; c < 8; c++)
+        st_shared_v4(prow + sw128_off(r, c), w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[j & 1]);
     }
     // normalise and store the finished O row
     if (ok && mbar_wait(o_full, 0, kFaultAttn)) {
@@ -348,7 +362,7 @@ void flash_attention(const uint16_t *q, const uint16_t *k, const uint16_t *vt, i
               map3(&mk, k, hd, Tk, (uint64_t)B * H, hd, (uint64_t)Tk * hd, 64, kKV) &&
               map3(&mv, vt, Tk, hd, (uint64_t)B * H, Tkp, (uint64_t)hd * Tkp, 64, 64);
     if (ok) {
-      const size_t smem = kQBytes + kAttnStages * (kKBytes + kVBytes) + kPBytes + 128;
+      const size_t smem = kAttnSmem;
       static bool attr = false;
       if (!attr) {
         DCB_CUDA(cudaFuncSetAttribute(k_flash_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -305,6 +305,11 @@ struct ConvW {             // B operand of a conv GEMM plus its epilogue constan
   int O = 0, C = 0, KH = 1, KW = 1, K = 0;
   float *bias = nullptr;
   int glu_bn = 0;          // N tile of the GLU interleave (0 = plain)
+  // the same rows in the TMA im2col kernel's K order (tap-major, channels zero-padded to
+  // ncb blocks of 64 per tap), for convs with at least 32 input channels
+  uint16_t *wt = nullptr;
+  int64_t ldt = 0;
+  int ncb = 0;
 };
 struct LinW {
   uint16_t *w = nullptr;   // [out][ld]
@@ -449,6 +454,28 @@ static void stage_f32(Staging &st, const std::vector<float> &v, float **slot) {
   st.add(v.data(), v.size() * sizeof(float), (void **)slot);
 }
 
+// rows [rows][kp] with K = (kh, kw, c) (channels fastest) -> the TMA im2col K order
+// (kh, channel block, kw, c) with channels zero-padded to ncb = ceil(C / 64) blocks
+static void stage_tma_order(Staging &st, ConvW &cw, const std::vector<uint16_t> &packed,
+                            int rows, int64_t kp, int KH, int KW, int C) {
+  if (C < 32) return;
+  const int ncb = (C + 63) / 64;
+  const int64_t ldt = (int64_t)KH * KW * ncb * 64;
+  std::vector<uint16_t> t((size_t)rows * ldt, 0);
+  for (int r = 0; r < rows; r++)
+    for (int kh = 0; kh < KH; kh++)
+      for (int kw = 0; kw < KW; kw++)
+        for (int cb = 0; cb < ncb; cb++) {
+          const int n = C - cb * 64 < 64 ? C - cb * 64 : 64;
+          memcpy(&t[(size_t)r * ldt + (((size_t)kh * ncb + cb) * KW + kw) * 64],
+                 &packed[(size_t)r * kp + ((size_t)kh * KW + kw) * C + (size_t)cb * 64],
+                 (size_t)n * 2);
+        }
+  cw.ncb = ncb;
+  cw.ldt = ldt;
+  st.add(t.data(), t.size() * 2, (void **)&cw.wt);
+}
+
 // GEMM weight in the loader layout: rows o, reduction over the flattened rest, fp16 RNE,
 // K padded to 8 (weights.c:306-310, 338-347)
 static std::vector<uint16_t> pack_rows(const std::vector<float> &w, int rows, int K, int64_t kp) {
@@ -492,6 +519,7 @@ static bool load_conv(Loader &L, Staging &st, const std::string &prefix, ConvW &
     cw.rows = cw.O;
   }
   st.add(packed.data(), packed.size() * 2, (void **)&cw.w);
+  stage_tma_order(st, cw, packed, cw.rows, kp, cw.KH, cw.KW, cw.C);
   stage_f32(st, b, &cw.bias);
   return true;
 }
@@ -526,6 +554,9 @@ static bool load_convtr(Loader &L, Staging &st, const std::string &prefix, ConvW
   cw.ld = ld;
   cw.rows = O * S;
   st.add(ph.data(), ph.size() * 2, (void **)&cw.w);
+  // taps along H, as the frequency decoders use them (the time decoders' convs take the
+  // gather kernel)
+  stage_tma_order(st, cw, ph, cw.rows, ld, 2, 1, C);
   stage_f32(st, b, &cw.bias);
   return true;
 }

@@ -131,7 +131,7 @@ static void conv(const ConvW &cw, const float *x, const float *x2, const Img &in
   e.gn_w = gn ? gn->w : nullptr;
   e.gn_b = gn ? gn->b : nullptr;
   const int64_t M = (int64_t)in.N1 * in.N2 * Ho * Wo;
-  gemm_gather(g, M, cw.w, cw.rows, cw.ld, e, act >= 2 ? cw.glu_bn : 0);
+  gemm_gather(g, M, cw.w, cw.rows, cw.ld, e, act >= 2 ? cw.glu_bn : 0, cw.wt, cw.ldt, cw.ncb);
 }
 
 // stride-phase transposed conv along H (freq) or W (time), crop + optional GELU
@@ -173,7 +173,8 @@ static void conv_tr(const ConvW &cw, const float *x, const Img &in, bool axis_h,
   e.crop = crop;
   e.out_len = out_len;
   e.axis_h = axis_h ? 1 : 0;
-  gemm_gather(g, (int64_t)in.N1 * in.N2 * g.Ho * g.Wo, cw.w, cw.rows, cw.ld, e);
+  gemm_gather(g, (int64_t)in.N1 * in.N2 * g.Ho * g.Wo, cw.w, cw.rows, cw.ld, e, 0, cw.wt,
+              cw.ldt, cw.ncb);
 }
 
 // ------------------------------------------------------------------ layers

@@ -250,6 +250,127 @@ static __device__ __forceinline__ void tile_coords(const Shape &s, int64_t tile,
   m0 = mt * kBM;
 }
 
+// Epilogue of one 128 x BN accumulator tile (TMEM columns from `tacc`) by NW warps: warp w
+// reads TMEM lane quarter (w & 3); with NW == 8, w >> 2 picks the half of the columns.
+// Rows r >= row_lim of the tile are outside the output.  EPI_CONV goes through `wst`, this
+// warp's [CW columns][32 rows] transpose buffer, so that lane l stores rows 4(l & 7)..+3 of
+// one channel with a 16-byte store; other modes store per row (store_chunk16).
+template <int BN, int NW, int CW>
+static __device__ __forceinline__ void epilogue_tile(const Shape &s, const Epi &e, uint32_t tacc,
+                                                     int warp, int lane, int bz, int64_t m0,
+                                                     int nt, int row_lim, float *wst) {
+  const int quarter = warp & 3, half = NW == 8 ? (warp >> 2) : 0;
+  const int r = quarter * 32 + lane;
+  const uint32_t trow = tacc + ((uint32_t)(quarter * 32) << 16);
+  const int n0 = nt * BN;
+  const int64_t m = m0 + r;
+  if (e.mode == EPI_CONV && wst) {
+    const int rq = 4 * (lane & 7);
+    int64_t poff[4];
+    bool pv[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      pv[i] = quarter * 32 + rq + i < row_lim;
+      poff[i] = 0;
+      if (pv[i]) {
+        const RowInfo ri = decode_row(e, m0 + quarter * 32 + rq + i);
+        poff[i] = ri.base + (int64_t)ri.ho * e.oH + ri.wo;
+      }
+    }
+    const bool contig = pv[3] && poff[1] == poff[0] + 1 && poff[2] == poff[0] + 2 &&
+                        poff[3] == poff[0] + 3;
+    const bool glu = e.act >= 2;
+    // act 3: GroupNorm statistics of this lane's row (one image per Ho * Wo rows)
+    float gmu = 0.f, grs = 0.f;
+    if (e.act == 3 && r < row_lim) {
+      const int64_t img = m / ((int64_t)e.Ho * e.Wo);
+      gmu = e.gn_mean[img];
+      grs = e.gn_rstd[img];
+    }
+    const int ncols = glu ? e.glu_half : BN;
+    const int per = NW == 8 ? (ncols >= 32 ? ncols / 2 : (half == 0 ? ncols : 0)) : ncols;
+    const int cbeg = NW == 8 && ncols >= 32 ? half * per : 0;
+    const int obase = glu ? nt * e.glu_half : n0;
+    for (int c0 = cbeg; c0 < cbeg + per; c0 += CW) {
+      const int cw = cbeg + per - c0 >= CW ? CW : 16;
+      for (int sub = 0; sub < cw; sub += 16) {
+        float va[16];
+        tmem_ld16(trow + c0 + sub, va);
+        if (glu) {
+          float vb[16];
+          tmem_ld16(trow + e.glu_half + c0 + sub, vb);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const int o = obase + c0 + sub + i;
+            float val = 0.f;
+            if (o < e.O) {
+              float a = va[i] + (e.bias ? e.bias[o] : 0.f);
+              float b = vb[i] + (e.bias ? e.bias[e.O + o] : 0.f);
+              if (e.act == 3) {
+                a = (a - gmu) * grs * e.gn_w[o] + e.gn_b[o];
+                b = (b - gmu) * grs * e.gn_w[e.O + o] + e.gn_b[e.O + o];
+              }
+              val = a * sigmoid_f(b);
+            }
+            wst[(sub + i) * 32 + lane] = val;
+          }
+        } else {
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const int o = obase + c0 + sub + i;
+            float val = va[i] + ((e.bias && o < e.O) ? e.bias[o] : 0.f);
+            if (e.act == 1) val = gelu_f(val);
+            wst[(sub + i) * 32 + lane] = val;
+          }
+        }
+      }
+      __syncwarp();
+      for (int cc = lane >> 3; cc < cw; cc += 4) {
+        const int o = obase + c0 + cc;
+        if (o >= e.O) continue;
+        const float4 v4 = *(const float4 *)(wst + cc * 32 + rq);
+        float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+        const int64_t a = poff[0] + (int64_t)o * e.oC;
+        const uintptr_t al = (uintptr_t)(e.y + a) | (e.res ? (uintptr_t)(e.res + a) : 0);
+        if (contig && (al & 15) == 0) {
+          if (e.res) {
+            const float4 rr = *(const float4 *)(e.res + a);
+            const float sc = e.scale[o];
+            vv[0] = rr.x + sc * vv[0];
+            vv[1] = rr.y + sc * vv[1];
+            vv[2] = rr.z + sc * vv[2];
+            vv[3] = rr.w + sc * vv[3];
+          }
+          *(float4 *)(e.y + a) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            if (!pv[i]) continue;
+            const int64_t ai = poff[i] + (int64_t)o * e.oC;
+            float val = vv[i];
+            if (e.res) val = e.res[ai] + e.scale[o] * val;
+            e.y[ai] = val;
+          }
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    const bool mv = r < row_lim;
+    const RowInfo ri = mv ? decode_row(e, m) : RowInfo{0, 0, 0, 0, 0};
+    constexpr int PER = NW == 8 ? (BN / 2 < 16 ? 16 : BN / 2) : BN;
+    const int cbeg = NW == 8 ? half * PER : 0;
+    for (int c0 = cbeg; c0 < cbeg + PER && c0 < BN; c0 += 16) {
+      float v[16];
+      tmem_ld16(trow + c0, v);
+      tmem_wait_ld();
+      if (mv) store_chunk16(e, s, bz, m, (int64_t)n0 + c0, ri, v);
+    }
+  }
+}
+
 template <int BN, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 2)
     k_umma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -438,131 +559,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
   } else if (warp < Cfg::kEpiWarps) {
-    // ---- epilogue warps: TMEM lane quarter q = rows 32q..32q+31 of the tile
-    const int quarter = warp & 3, half = warp >> 2;
-    const int r = quarter * 32 + lane;
-    float *wst = stg + quarter * (32 * 32);  // [32 columns][32 rows] of this warp (conv)
+    // ---- epilogue warps: TMEM lane quarter (warp & 3) = rows 32q..32q+31 of the tile
+    float *wst = stg + (warp & 3) * (32 * 32);  // [32 columns][32 rows] of this warp (conv)
     uint32_t local = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles_total; tile += gridDim.x, local++) {
       int bz, nt;
       int64_t m0;
       tile_coords(s, tile, bz, m0, nt);
-      const int n0 = nt * BN;
       const uint32_t buf = local % (uint32_t)Cfg::kBufs;
       const uint32_t use = local / (uint32_t)Cfg::kBufs;
       if (!mbar_wait(&acc_full[buf], use & 1u, kFaultDone)) break;
       tc_fence_after();
-      const uint32_t trow =
-          tmem + buf * (uint32_t)Cfg::kAccCols + ((uint32_t)(quarter * 32) << 16);
-      const int64_t m = m0 + r;
-      if (GATHER && e.mode == EPI_CONV) {
-        // Staged conv epilogue: chunks of up to 32 output channels go TMEM -> registers
-        // (bias, GELU / GLU) -> this warp's transpose buffer [channel][row], then lane l
-        // stores rows 4(l & 7)..+3 of channel (l >> 3) + 4j: 16-byte stores where the four
-        // positions are contiguous and aligned, element stores otherwise.
-        const int rq = 4 * (lane & 7);
-        int64_t poff[4];
-        bool pv[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int64_t mm = m0 + quarter * 32 + rq + i;
-          pv[i] = mm < s.M;
-          poff[i] = 0;
-          if (pv[i]) {
-            const RowInfo ri = decode_row(e, mm);
-            poff[i] = ri.base + (int64_t)ri.ho * e.oH + ri.wo;
-          }
-        }
-        const bool contig = pv[3] && poff[1] == poff[0] + 1 && poff[2] == poff[0] + 2 &&
-                            poff[3] == poff[0] + 3;
-        const bool glu = e.act >= 2;
-        // act 3: GroupNorm statistics of this lane's row (one image per Ho * Wo rows)
-        float gmu = 0.f, grs = 0.f;
-        if (e.act == 3 && m < s.M) {
-          const int64_t img = m / ((int64_t)e.Ho * e.Wo);
-          gmu = e.gn_mean[img];
-          grs = e.gn_rstd[img];
-        }
-        const int ncols = glu ? e.glu_half : BN;
-        const int obase = glu ? nt * e.glu_half : n0;
-        for (int c0 = 0; c0 < ncols; c0 += 32) {
-          const int cw = ncols - c0 >= 32 ? 32 : 16;
-          for (int sub = 0; sub < cw; sub += 16) {
-            float va[16];
-            tmem_ld16(trow + c0 + sub, va);
-            if (glu) {
-              float vb[16];
-              tmem_ld16(trow + e.glu_half + c0 + sub, vb);
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 16; i++) {
-                const int o = obase + c0 + sub + i;
-                float val = 0.f;
-                if (o < e.O) {
-                  float a = va[i] + (e.bias ? e.bias[o] : 0.f);
-                  float b = vb[i] + (e.bias ? e.bias[e.O + o] : 0.f);
-                  if (e.act == 3) {
-                    a = (a - gmu) * grs * e.gn_w[o] + e.gn_b[o];
-                    b = (b - gmu) * grs * e.gn_w[e.O + o] + e.gn_b[e.O + o];
-                  }
-                  val = a * sigmoid_f(b);
-                }
-                wst[(sub + i) * 32 + lane] = val;
-              }
-            } else {
-              tmem_wait_ld();
-#pragma unroll
-              for (int i = 0; i < 16; i++) {
-                const int o = obase + c0 + sub + i;
-                float val = va[i] + ((e.bias && o < e.O) ? e.bias[o] : 0.f);
-                if (e.act == 1) val = gelu_f(val);
-                wst[(sub + i) * 32 + lane] = val;
-              }
-            }
-          }
-          __syncwarp();
-          for (int cc = lane >> 3; cc < cw; cc += 4) {
-            const int o = obase + c0 + cc;
-            if (o >= e.O) continue;
-            const float4 v4 = *(const float4 *)(wst + cc * 32 + rq);
-            float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-            const int64_t a = poff[0] + (int64_t)o * e.oC;
-            const uintptr_t al = (uintptr_t)(e.y + a) | (e.res ? (uintptr_t)(e.res + a) : 0);
-            if (contig && (al & 15) == 0) {
-              if (e.res) {
-                const float4 rr = *(const float4 *)(e.res + a);
-                const float sc = e.scale[o];
-                vv[0] = rr.x + sc * vv[0];
-                vv[1] = rr.y + sc * vv[1];
-                vv[2] = rr.z + sc * vv[2];
-                vv[3] = rr.w + sc * vv[3];
-              }
-              *(float4 *)(e.y + a) = make_float4(vv[0], vv[1], vv[2], vv[3]);
-            } else {
-#pragma unroll
-              for (int i = 0; i < 4; i++) {
-                if (!pv[i]) continue;
-                const int64_t ai = poff[i] + (int64_t)o * e.oC;
-                float val = vv[i];
-                if (e.res) val = e.res[ai] + e.scale[o] * val;
-                e.y[ai] = val;
-              }
-            }
-          }
-          __syncwarp();
-        }
-      } else {
-        const bool mv = m < s.M;
-        const RowInfo ri = mv ? decode_row(e, m) : RowInfo{0, 0, 0, 0, 0};
-        constexpr int PER = Cfg::kEpiWarps == 8 ? (BN / 2 < 16 ? 16 : BN / 2) : BN;
-        const int cbeg = Cfg::kEpiWarps == 8 ? half * PER : 0;
-        for (int c0 = cbeg; c0 < cbeg + PER && c0 < BN; c0 += 16) {
-          float v[16];
-          tmem_ld16(trow + c0, v);
-          tmem_wait_ld();
-          if (mv) store_chunk16(e, s, bz, m, (int64_t)n0 + c0, ri, v);
-        }
-      }
+      const int64_t left = (int64_t)s.M - m0;
+      epilogue_tile<BN, Cfg::kEpiWarps, 32>(s, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp,
+                                            lane, bz, m0, nt, left < kBM ? (int)left : kBM,
+                                            GATHER ? wst : nullptr);
       // this warp's TMEM reads are complete: release the accumulator buffer
       tc_fence_before();
       __syncwarp();
@@ -573,6 +584,377 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_before();
   __syncthreads();
   if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, (uint32_t)Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------- TMA im2col conv kernel
+// Convolutions over fp32 activations whose positions along W are contiguous (stride 1 in
+// W, every other stride a multiple of 16 bytes): the freq-branch convs of the model.  A
+// tile is 128 consecutive output positions of one output line (n, ho).  K runs over
+// (kh, 64-channel block, kw, channel): for each (kh, channel block) the TMA warp loads
+// one fp32 box x[n][c0..c0+63][h][w_al..w_al+BW) (w_al = the first input position of the
+// tile rounded down to a 16-byte boundary; rows, positions and channels outside the
+// tensor read as zero, which is the convolution's zero padding) that serves every W tap;
+// four converter warps turn it into one fp16 (round-to-nearest-even) K-major
+// SWIZZLE_128B A tile per W tap, one output position per thread, adding the skip tensor
+// when there is one; the TMA warp also streams the B tiles; one thread issues
+// tcgen05.mma.  The box ring and the operand ring are separate, so a box is refilled as
+// soon as its A tiles are built.  One persistent CTA per SM: 512 TMEM columns hold two
+// accumulators of up to 256 columns, so the epilogue (8 warps) of a tile overlaps the
+// next tile's loads and MMAs.  All rows of a tile share (n, ho): the epilogue addresses
+// each output column once per tile and stores 4 consecutive positions per 16-byte store.
+// Weights are in (kh, channel block, kw) order with channels zero-padded to whole blocks
+// of 64: B[n][((kh * ncb + cb) * KW + kw) * 64 + c].
+struct ConvTma {
+  int KH, KW, SH, PH, DH, PW, DW;
+  int Ho, Wo;
+  int ncb;        // 64-channel blocks
+  int64_t lines;  // output lines (images * Ho)
+  int tpl;        // tiles of 128 positions per line
+  int N2;         // images = n1 * N2 + n2
+  int N, nkb, ntiles;
+  int bw;         // box width (positions), a multiple of 4
+  int xstages, stages;
+};
+
+constexpr int kCtThreads = 448;  // warps 0-7 epilogue, 8-11 converters, 12 TMA, 13 MMA
+constexpr int kCtBoxMax = 256;   // TMA box extent limit
+constexpr int kCtEpiCW = 16;     // epilogue transpose chunk (columns)
+
+template <int BN, bool X2>
+struct CtCfg {
+  static constexpr uint32_t kBBytes = BN * 128;
+  static constexpr uint32_t kABStage = kATileBytes + kBBytes;  // a multiple of 1024
+  static constexpr int kAccCols = BN < 32 ? 32 : BN;
+  static constexpr int kTmemCols = kAccCols * 2;  // two accumulators, a power of two
+};
+
+static __device__ __forceinline__ void tma_load_5d(void *dst, const CUtensorMap *map,
+                                                   uint64_t *bar, int c0, int c1, int c2,
+                                                   int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
+// sigmoid with the hardware exp2 / reciprocal approximations (relative error ~1e-6)
+static __device__ __forceinline__ float sigmoid_fast(float x) {
+  return __fdividef(1.0f, 1.0f + __expf(-x));
+}
+
+// tile -> (line, first position, N tile); N tiles fastest
+static __device__ __forceinline__ void ct_tile(const ConvTma &c, int64_t tile, int64_t &line,
+                                               int &wo0, int &nt) {
+  nt = (int)(tile % c.ntiles);
+  const int64_t rest = tile / c.ntiles;
+  line = rest / c.tpl;
+  wo0 = (int)(rest - line * c.tpl) * kBM;
+}
+
+// Epilogue of a line tile (EPI_CONV, or EPI_CONVTR along H) by 8 warps: warp w reads TMEM
+// lane quarter (w & 3) = positions 32q..32q+31 and half (w >> 2) of the columns, 16
+// columns per step through its [16][32] transpose buffer `wst`.
+template <int BN>
+static __device__ __forceinline__ void ct_epilogue(const ConvTma &c, const Epi &e, uint32_t tacc,
+                                                   int warp, int lane, int64_t line, int wo0,
+                                                   int nt, float *wst) {
+  const int quarter = warp & 3, half = warp >> 2;
+  const uint32_t trow = tacc + ((uint32_t)(quarter * 32) << 16);
+  const int64_t n = line / c.Ho;
+  const int ho = (int)(line - n * c.Ho);
+  const int64_t n1 = n / e.oN2, n2 = n - n1 * e.oN2;
+  const int64_t base = n1 * e.oN1 + n2 * e.oN2s + (int64_t)wo0 + quarter * 32;
+  const int row_lim = c.Wo - wo0 - quarter * 32;  // valid positions of this warp: r < row_lim
+  const int rq = 4 * (lane & 7);
+  const bool full4 = rq + 4 <= row_lim;
+  const bool glu = e.mode == EPI_CONV && e.act >= 2;
+  float gmu = 0.f, grs = 0.f;
+  if (e.mode == EPI_CONV && e.act == 3) {
+    gmu = e.gn_mean[n];
+    grs = e.gn_rstd[n];
+  }
+  const int ncols = glu ? e.glu_half : BN;
+  const int per = ncols >= 32 ? ncols / 2 : (half == 0 ? ncols : 0);
+  const int cbeg = ncols >= 32 ? half * per : 0;
+  const int obase = glu ? nt * e.glu_half : nt * BN;
+  for (int c0 = cbeg; c0 < cbeg + per; c0 += 16) {
+    float va[16];
+    tmem_ld16(trow + c0, va);
+    if (glu) {
+      float vb[16];
+      tmem_ld16(trow + e.glu_half + c0, vb);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const int o = obase + c0 + i;
+        float val = 0.f;
+        if (o < e.O) {
+          float a = va[i] + (e.bias ? e.bias[o] : 0.f);
+          float b = vb[i] + (e.bias ? e.bias[e.O + o] : 0.f);
+          if (e.act == 3) {
+            a = (a - gmu) * grs * e.gn_w[o] + e.gn_b[o];
+            b = (b - gmu) * grs * e.gn_w[e.O + o] + e.gn_b[e.O + o];
+          }
+          val = a * sigmoid_fast(b);
+        }
+        wst[i * 32 + lane] = val;
+      }
+    } else {
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const int col = obase + c0 + i;
+        const int o = e.mode == EPI_CONVTR ? col / e.stride : col;
+        float val = va[i] + ((e.bias && o < e.O) ? e.bias[o] : 0.f);
+        if (e.act == 1) val = gelu_f(val);
+        wst[i * 32 + lane] = val;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int p = 0; p < 4; p++) {
+      const int cc = (lane >> 3) + 4 * p;
+      const int col = obase + c0 + cc;
+      int64_t off;
+      if (e.mode == EPI_CONVTR) {
+        const int o = col / e.stride, s = col - o * e.stride;
+        const int t = ho * e.stride + s - e.crop;
+        if (o >= e.O || t < 0 || t >= e.out_len) continue;
+        off = base + (int64_t)o * e.oC + (int64_t)t * e.oH;
+      } else {
+        if (col >= e.O) continue;
+        off = base + (int64_t)col * e.oC + (int64_t)ho * e.oH;
+      }
+      const float4 v4 = *(const float4 *)(wst + cc * 32 + rq);
+      float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+      const int64_t a = off + rq;
+      const uintptr_t al = (uintptr_t)(e.y + a) | (e.res ? (uintptr_t)(e.res + a) : 0);
+      if (full4 && (al & 15) == 0) {
+        if (e.res) {
+          const float4 rr = *(const float4 *)(e.res + a);
+          const float sc = e.scale[col];
+          vv[0] = rr.x + sc * vv[0];
+          vv[1] = rr.y + sc * vv[1];
+          vv[2] = rr.z + sc * vv[2];
+          vv[3] = rr.w + sc * vv[3];
+        }
+        *(float4 *)(e.y + a) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          if (rq + i >= row_lim) continue;
+          float val = vv[i];
+          if (e.res) val = e.res[a + i] + e.scale[col] * val;
+          e.y[a + i] = val;
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
+template <int BN, bool X2>
+__global__ void __launch_bounds__(kCtThreads, 1)
+    k_conv_tma(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmX2,
+               const __grid_constant__ CUtensorMap tmB, const ConvTma c, const Epi e) {
+  using Cfg = CtCfg<BN, X2>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int stages = c.stages, xstages = c.xstages;
+  const uint32_t xbytes = (uint32_t)c.bw * 64 * 4;  // one box (a multiple of 1024 bytes)
+  const uint32_t xstage = xbytes * (X2 ? 2 : 1);
+  // [operand stages: A tile | B tile][box stages: x box | x2 box][epilogue buffers]
+  uint8_t *sAB = smem;
+  uint8_t *sX = smem + (size_t)stages * Cfg::kABStage;
+  float *stg = (float *)(sX + (size_t)xstages * xstage);  // 8 warps x [16][32] fp32
+  uint64_t *xfull = (uint64_t *)(stg + 8 * kCtEpiCW * 32);
+  uint64_t *xempty = xfull + xstages;
+  uint64_t *bfull = xempty + xstages;
+  uint64_t *afull = bfull + stages;
+  uint64_t *empty = afull + stages;
+  uint64_t *acc_full = empty + stages;
+  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *fin = acc_empty + 2;
+  uint32_t *tslot = (uint32_t *)(fin + 1);
+
+  __shared__ uint32_t s_abort;
+  if (threadIdx.x == 0) s_abort = fault_pending() ? 1u : 0u;
+  __syncthreads();
+  if (s_abort) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t ntiles_total = c.lines * c.tpl * c.ntiles;
+  const int ngroups = c.KH * c.ncb;  // boxes per tile
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < xstages; i++) {
+      mbar_init(&xfull[i], 1);
+      mbar_init(&xempty[i], 4);
+    }
+    for (int i = 0; i < stages; i++) {
+      mbar_init(&bfull[i], 1);
+      mbar_init(&afull[i], 4);
+      mbar_init(&empty[i], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);
+    }
+    mbar_init(fin, 1);
+    fence_mbar_init();
+  }
+  if (warp == 13) {
+    tmem_alloc(tslot, (uint32_t)Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 12) {
+    // ---- TMA producer: per (kh, channel block) one box, then the KW B tiles
+    if (lane == 0) {
+      tma_prefetch_desc(&tmX);
+      if (X2) tma_prefetch_desc(&tmX2);
+      tma_prefetch_desc(&tmB);
+      uint32_t it = 0, xi = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
+        int64_t line;
+        int wo0, nt;
+        ct_tile(c, tile, line, wo0, nt);
+        const int64_t n = line / c.Ho;
+        const int ho = (int)(line - n * c.Ho);
+        const int n1 = (int)(n / c.N2), n2 = (int)(n - (int64_t)n1 * c.N2);
+        const int w_al = (wo0 - c.PW) & ~3;  // 16-byte aligned box start
+        for (int grp = 0; ok && grp < ngroups; grp++, xi++) {
+          const int kh = grp / c.ncb, cb = grp - kh * c.ncb;
+          const int xs = (int)(xi % (uint32_t)xstages);
+          if (!mbar_wait(&xempty[xs], ((xi / (uint32_t)xstages) & 1u) ^ 1u, kFaultEmpty)) {
+            ok = false;
+            break;
+          }
+          const int h = ho * c.SH - c.PH + kh * c.DH;
+          uint8_t *xb = sX + (size_t)xs * xstage;
+          mbar_expect_tx(&xfull[xs], xstage);
+          tma_load_5d(xb, &tmX, &xfull[xs], w_al, h, cb * 64, n2, n1);
+          if (X2) tma_load_5d(xb + xbytes, &tmX2, &xfull[xs], w_al, h, cb * 64, n2, n1);
+          for (int kw = 0; kw < c.KW; kw++, it++) {
+            const int st = (int)(it % (uint32_t)stages);
+            if (!mbar_wait(&empty[st], ((it / (uint32_t)stages) & 1u) ^ 1u, kFaultEmpty)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&bfull[st], Cfg::kBBytes);
+            tma_load_3d(sAB + (size_t)st * Cfg::kABStage + kATileBytes, &tmB, &bfull[st],
+                        (grp * c.KW + kw) * kBK, nt * BN, 0);
+          }
+        }
+      }
+    }
+  } else if (warp == 13) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16_f32(kBM, BN);
+      uint32_t it = 0, local = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x, local++) {
+        const uint32_t buf = local & 1u, use = local >> 1;
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * (uint32_t)Cfg::kAccCols;
+        for (int kb = 0; kb < c.nkb; kb++, it++) {
+          const int st = (int)(it % (uint32_t)stages);
+          const uint32_t ph = (it / (uint32_t)stages) & 1u;
+          if (!mbar_wait(&afull[st], ph, kFaultFull) || !mbar_wait(&bfull[st], ph, kFaultFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t *sb = sAB + (size_t)st * Cfg::kABStage;
+          const uint64_t ad = sw128_desc(smem_u32(sb));
+          const uint64_t bd = sw128_desc(smem_u32(sb + kATileBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; k++)
+            umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[st]);
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+      umma_commit(fin);
+      mbar_wait(fin, 0, kFaultDone);
+    }
+  } else if (warp >= 8) {
+    // ---- converters: output position r of the tile, 64 channels per A tile
+    const int r = (warp - 8) * 32 + lane;
+    uint32_t it = 0, xi = 0;
+    bool ok = true;
+    for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
+      int64_t line;
+      int wo0, nt;
+      ct_tile(c, tile, line, wo0, nt);
+      const int sh0 = (wo0 - c.PW) - ((wo0 - c.PW) & ~3);
+      for (int grp = 0; ok && grp < ngroups; grp++, xi++) {
+        const int xs = (int)(xi % (uint32_t)xstages);
+        if (!mbar_wait(&xfull[xs], (xi / (uint32_t)xstages) & 1u, kFaultFull)) {
+          ok = false;
+          break;
+        }
+        const float *xb = (const float *)(sX + (size_t)xs * xstage);
+        for (int kw = 0; kw < c.KW; kw++, it++) {
+          const int st = (int)(it % (uint32_t)stages);
+          if (!mbar_wait(&empty[st], ((it / (uint32_t)stages) & 1u) ^ 1u, kFaultEmpty)) {
+            ok = false;
+            break;
+          }
+          const float *xs_r = xb + r + sh0 + kw * c.DW;
+          const uint32_t a_base = smem_u32(sAB + (size_t)st * Cfg::kABStage);
+#pragma unroll
+          for (int cc = 0; cc < 8; cc++) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              v[i] = xs_r[(cc * 8 + i) * c.bw];
+              if (X2) v[i] += xs_r[(cc * 8 + i) * c.bw + 64 * c.bw];
+            }
+            st_shared_v4(a_base + sw128_off(r, cc), pack_h2(v[0], v[1]), pack_h2(v[2], v[3]),
+                         pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&afull[st]);
+        }
+        // every A tile of this box is built: the box may be refilled
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xempty[xs]);
+      }
+    }
+  } else {
+    // ---- epilogue warps 0-7
+    float *wst = stg + warp * (kCtEpiCW * 32);
+    uint32_t local = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles_total; tile += gridDim.x, local++) {
+      int64_t line;
+      int wo0, nt;
+      ct_tile(c, tile, line, wo0, nt);
+      const uint32_t buf = local & 1u, use = local >> 1;
+      if (!mbar_wait(&acc_full[buf], use & 1u, kFaultDone)) break;
+      tc_fence_after();
+      ct_epilogue<BN>(c, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp, lane, line, wo0, nt,
+                      wst);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 13) {
     tc_fence_after();
     tmem_dealloc(tmem, (uint32_t)Cfg::kTmemCols);
   }
@@ -827,8 +1209,118 @@ void gemm_rows_launch(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t
   launch_simt<false>(a, b, s, g, e, N, batch);
 }
 
+// fp32 activation view (W, H, C, N2, N1) as a 5-D tensor map with bw x 1 x 64 x 1 x 1
+// boxes; strides of extent-1 dimensions are irrelevant and set to the span below them
+static bool encode_act5(CUtensorMap *map, const float *x, const Gather &g, int64_t n1_count,
+                        int bw) {
+  if (!get_encoder() || !x || ((uintptr_t)x & 15)) return false;
+  const int64_t ext[5] = {g.W, g.H, g.C, g.N2, n1_count};
+  const int64_t st[4] = {g.sH, g.sC, g.sN2, g.sN1};
+  cuuint64_t dims[5], strides[4];
+  for (int i = 0; i < 5; i++) {
+    if (ext[i] <= 0 || ext[i] > (1ll << 31)) return false;
+    dims[i] = (cuuint64_t)ext[i];
+  }
+  int64_t span = ((int64_t)g.W * 4 + 15) / 16 * 16;
+  for (int i = 0; i < 4; i++) {
+    int64_t b = st[i] * 4;
+    if (ext[i + 1] == 1 || b == 0) b = span;
+    if (b % 16 || b <= 0 || b >= (1ll << 40)) return false;
+    strides[i] = (cuuint64_t)b;
+    if (b * ext[i + 1] > span) span = b * ext[i + 1];
+  }
+  cuuint32_t box[5] = {(cuuint32_t)bw, 1, 64, 1, 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float *>(x), dims, strides,
+                  box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, bool X2>
+static void launch_conv_tma(const CUtensorMap &tx, const CUtensorMap &tx2, const CUtensorMap &tb,
+                            ConvTma c, const Epi &e) {
+  using Cfg = CtCfg<BN, X2>;
+  const size_t xstage = (size_t)c.bw * 64 * 4 * (X2 ? 2 : 1);
+  const size_t budget = 226 * 1024;
+  const size_t fixed = 1024 + (size_t)8 * kCtEpiCW * 32 * 4 + 5 * 8 + 16;
+  auto need = [&](int xs, int st) {
+    return fixed + (size_t)xs * (xstage + 16) + (size_t)st * (Cfg::kABStage + 24);
+  };
+  int xs = X2 ? 2 : 3, st = 6;
+  while (st > 2 && need(xs, st) > budget) st--;
+  if (need(xs, st) > budget) xs = 2;
+  DCB_REQUIRE(need(xs, st) <= budget, "conv: TMA im2col stages do not fit in shared memory");
+  c.xstages = xs;
+  c.stages = st;
+  const size_t smem = need(xs, st);
+  static size_t attr = 0;
+  if (smem > attr) {
+    DCB_CUDA(cudaFuncSetAttribute(k_conv_tma<BN, X2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    attr = smem;
+  }
+  const int64_t tiles = c.lines * c.tpl * c.ntiles;
+  const int64_t sms = sm_count();
+  const unsigned grid = (unsigned)(tiles < sms ? tiles : sms);
+  k_conv_tma<BN, X2><<<grid, kCtThreads, smem, stream()>>>(tx, tx2, tb, c, e);
+  DCB_LAUNCHED();
+}
+
+// TMA im2col path of gemm_gather: true when it launched
+static bool conv_tma(const Gather &g, int64_t M, const uint16_t *wt, int64_t N, int64_t ldt,
+                     int ncb, const Epi &e, int bn) {
+  if (!wt || ncb <= 0 || g.SW != 1 || g.C < 32 || g.Wo < 64) return false;
+  if (e.mode == EPI_CONVTR && !e.axis_h) return false;  // taps along W: no line tiles
+  const int bw = (131 + (g.KW - 1) * g.DW + 3) / 4 * 4;
+  if (bw > kCtBoxMax) return false;
+  if ((int64_t)g.KH * g.KW * ncb * kBK != ldt) return false;
+  const int64_t hw = (int64_t)g.Ho * g.Wo;
+  if (hw <= 0 || M % hw) return false;
+  const int64_t images = M / hw;
+  if (images % g.N2) return false;
+  const bool x2 = g.x2 != nullptr;
+  if (x2 && bn > 128) bn = 128;
+  CUtensorMap tx, tx2, tb;
+  if (!encode_act5(&tx, g.x, g, images / g.N2, bw)) return false;
+  if (x2 && !encode_act5(&tx2, g.x2, g, images / g.N2, bw)) return false;
+  if (!encode_map(&tb, wt, (uint64_t)ldt, (uint64_t)N, 1, (uint64_t)ldt, 0, (uint32_t)bn))
+    return false;
+  ConvTma c{};
+  c.KH = g.KH;
+  c.KW = g.KW;
+  c.SH = g.SH;
+  c.PH = g.PH;
+  c.DH = g.DH;
+  c.PW = g.PW;
+  c.DW = g.DW;
+  c.Ho = g.Ho;
+  c.Wo = g.Wo;
+  c.ncb = ncb;
+  c.lines = images * g.Ho;
+  c.tpl = (g.Wo + kBM - 1) / kBM;
+  c.N2 = g.N2;
+  c.bw = bw;
+  c.N = (int)N;
+  c.nkb = g.KH * g.KW * ncb;
+  c.ntiles = (int)((N + bn - 1) / bn);
+  Epi e2 = e;
+  if (e.mode == EPI_CONV && e.act >= 2) e2.glu_half = bn / 2;
+  if (!x2) tx2 = tx;
+  switch (bn) {
+    case 32: x2 ? launch_conv_tma<32, true>(tx, tx2, tb, c, e2)
+                : launch_conv_tma<32, false>(tx, tx2, tb, c, e2); break;
+    case 64: x2 ? launch_conv_tma<64, true>(tx, tx2, tb, c, e2)
+                : launch_conv_tma<64, false>(tx, tx2, tb, c, e2); break;
+    case 128: x2 ? launch_conv_tma<128, true>(tx, tx2, tb, c, e2)
+                 : launch_conv_tma<128, false>(tx, tx2, tb, c, e2); break;
+    default: launch_conv_tma<256, false>(tx, tx2, tb, c, e2); break;
+  }
+  return true;
+}
+
 void gemm_gather(const Gather &g, int64_t M, const uint16_t *w, int64_t N, int64_t ldw,
-                 const Epi &e, int bn_hint) {
+                 const Epi &e, int bn_hint, const uint16_t *wt, int64_t ldt, int ncb) {
   if (M <= 0 || N <= 0) return;
   DCB_REQUIRE(M < (1ll << 31), "conv: too many output positions");
   Shape s{};
@@ -848,6 +1340,13 @@ void gemm_gather(const Gather &g, int64_t M, const uint16_t *w, int64_t N, int64
                 x_b + n_alg * g.K * 2.0 + out_elems * 4.0 * (e.res ? 2 : 1), M, (int64_t)n_alg,
                 g.K);
   if (!g_opt_simt) {
+    // TMA im2col kernel (freq-branch convs); its N tile may be wider than the gather
+    // kernel's, except for GLU convs whose weights are interleaved per N tile
+    int bt = bn;
+    if (!glu && !bn_hint) {
+      bt = pick_bn(M, N, 1);
+    }
+    if (conv_tma(g, M, wt, N, ldt, ncb, e, bt)) return;
     CUtensorMap tb;
     // inner extent = the padded row length: padding columns are zero in every packed
     // weight, and a multiple-of-8 extent keeps the tensor map within TMA's 16-byte rules

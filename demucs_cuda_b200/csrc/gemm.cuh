@@ -77,7 +77,8 @@ struct RowsA {
 void gemm_rows(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch, const Epi &e);
 // C = gather(x) . B^T with B [N][K] fp16 rows (TMA); M = images * Ho * Wo
 void gemm_gather(const Gather &g, int64_t M, const uint16_t *w, int64_t N, int64_t ldw,
-                 const Epi &e, int bn_hint = 0);
+                 const Epi &e, int bn_hint = 0, const uint16_t *wt = nullptr,
+                 int64_t ldt = 0, int ncb = 0);
 // N tile used by gemm_gather for a given column count (the GLU interleave depends on it)
 int gather_bn(int64_t M, int64_t N, bool glu);
 
