@@ -178,8 +178,37 @@ static void conv_tr(const ConvW &cw, const float *x, const Img &in, bool axis_h,
 }
 
 // ------------------------------------------------------------------ layers
+// y += scale * GLU(GroupNorm(conv1x1(h))) of a DConv layer on CUDA cores (hid <= 24)
+static void dconv_tail(const DConvW &dw, const float *h, float *y, int B, int C, int hid,
+                       int Fr, int T, const float *zmean, const float *zrstd) {
+  const int hidp = (hid + 3) / 4 * 4;
+  const size_t sm = ((size_t)2 * C * hidp + 7 * (size_t)C) * sizeof(float);
+  const int64_t total = (int64_t)B * Fr * T;
+  const unsigned grid = grid_for(total, 256, 148 * 4);
+  const int64_t hsB = (int64_t)hid * Fr * T, hsC = (int64_t)Fr * T;
+  const int64_t ysB = (int64_t)C * Fr * T, ysC = (int64_t)Fr * T;
+#define DCB_TAIL(P)                                                                            \
+  k_dconv_tail<P><<<grid, 256, sm, stream()>>>(h, y, dw.c3.w, dw.c3.ld, dw.c3.bias, dw.gn4.w, \
+                                              dw.gn4.b, dw.scale, zmean, zrstd, B, C, hid,   \
+                                              Fr, T, hsB, hsC, ysB, ysC)
+  switch (hidp) {
+    case 4: DCB_TAIL(4); break;
+    case 8: DCB_TAIL(8); break;
+    case 12: DCB_TAIL(12); break;
+    case 16: DCB_TAIL(16); break;
+    case 20: DCB_TAIL(20); break;
+    default: DCB_TAIL(24); break;
+  }
+#undef DCB_TAIL
+  DCB_LAUNCHED();
+}
+
 // DConv residual branch (layers.c:24-53) applied in place on y [B, C, Fr, T] (Fr = 1 for
-// the time branch).
+// the time branch): conv k3 (dilation 2^d) -> GroupNorm(1) + GELU -> conv 1x1 ->
+// GroupNorm(1) + GLU -> LayerScale -> residual.  The second GroupNorm's statistics come
+// from the sums and Gram matrix of the hidden rows (the 1x1 conv output is never formed),
+// and the 1x1 conv runs fused with everything after it: on CUDA cores for hidden widths
+// <= 24, as a tensor-core conv with a GroupNorm + GLU epilogue above.
 static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
   const Img v = freq_rows(B, C, Fr, T);
   const unsigned rows = (unsigned)((int64_t)B * Fr);
@@ -191,16 +220,14 @@ static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
     const DConvW &dw = E.dconv[d];
     const int dil = 1 << d;
     const int hid = dw.c0.O, C2 = dw.c3.O;
+    DCB_REQUIRE(dw.zc != nullptr, "dconv: the 1x1 conv of layer %d is not 1x1", d);
     // conv k3, dilation 2^d, padding 2^d -> h [B, hid, Fr, T]
     float *h = dalloc((size_t)B * hid * Fr * T);
     const Img hv = freq_rows(B, hid, Fr, T);
     conv(dw.c0, y, nullptr, v, 1, 1, 0, dil, 1, dil, 1, T, h, hv, 0);
-    // GroupNorm(1) + GELU, in place
     RowView rh{h, Fr, (int64_t)hid * Fr * T, T, (int64_t)Fr * T, hid, T};
-    if (fused && dw.zc) {
-      // the GroupNorm statistics of z = conv1x1(h) come with the GELU pass, and the 1x1
-      // conv applies GroupNorm + GLU + LayerScale + residual in its epilogue: z is never
-      // written
+    if (fused) {
+      // GroupNorm(1) + GELU in place with the z statistics, one CTA per row
       const size_t sm = (size_t)hid * T * sizeof(float);
       static size_t attr = 0;
       if (sm > 48 * 1024 && sm > attr) {
@@ -211,42 +238,33 @@ static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
       k_gn_gelu_zstats<<<rows, kGnFusedThreads, sm, stream()>>>(
           rh, h, dw.gn1.w, dw.gn1.b, 1e-5f, dw.zc, C2, stat, stat + rows);
       DCB_LAUNCHED();
-      conv(dw.c3g, h, nullptr, hv, 1, 1, 0, 0, 1, 1, 1, T, y, v, 3, y, dw.scale, stat,
-           stat + rows, &dw.gn4);
-      dfree(h);
-      continue;
-    }
-    if (fused) {
-      k_gn_fused<0><<<rows, kGnFusedThreads, 0, stream()>>>(rh, h, dw.gn1.w, dw.gn1.b,
-                                                            nullptr, 0, 0, 0, 1e-5f);
-      DCB_LAUNCHED();
     } else {
       rowview_stats(rh, B, 1e-5f, stat, stat + rows, nullptr);
       const int64_t n = (int64_t)B * hid * Fr * T;
       k_gn_gelu<<<grid_for(n, 256), 256, 0, stream()>>>(rh, h, stat, stat + rows, dw.gn1.w,
                                                        dw.gn1.b, B);
       DCB_LAUNCHED();
-    }
-    // conv 1x1 -> z [B, 2C, Fr, T]
-    float *z = dalloc((size_t)B * C2 * Fr * T);
-    const Img zv = freq_rows(B, C2, Fr, T);
-    conv(dw.c3, h, nullptr, hv, 1, 1, 0, 0, 1, 1, 1, T, z, zv, 0);
-    dfree(h);
-    // GroupNorm(1) + GLU, LayerScale residual into y
-    RowView rz{z, Fr, (int64_t)C2 * Fr * T, T, (int64_t)Fr * T, C2, T};
-    if (fused) {
-      k_gn_fused<1><<<rows, kGnFusedThreads, 0, stream()>>>(
-          rz, y, dw.gn4.w, dw.gn4.b, dw.scale, (int64_t)C * Fr * T, T, (int64_t)Fr * T, 1e-5f);
+      // z statistics from the Gram matrix of fp16(h), accumulated over chunks of each row
+      const int npair = hid * (hid + 1) / 2;
+      const int chunk = kGramChunk * 6 / hid >= kGramChunk ? kGramChunk : 12288 / hid;
+      double *acc = (double *)dalloc((size_t)rows * (npair + hid) * 2);
+      DCB_CUDA(cudaMemsetAsync(acc, 0, (size_t)rows * (npair + hid) * sizeof(double), stream()));
+      const dim3 gg((unsigned)((T + chunk - 1) / chunk), rows);
+      k_gram_chunk<<<gg, 256, (size_t)hid * chunk * sizeof(float), stream()>>>(rh, chunk, acc);
       DCB_LAUNCHED();
+      k_zstats_final<<<(rows + 127) / 128, 128, 0, stream()>>>(acc, dw.zc, hid, T, C2,
+                                                              (int)rows, 1e-5f, stat,
+                                                              stat + rows);
+      DCB_LAUNCHED();
+      dfree(acc);
+    }
+    if (hid <= 24) {
+      dconv_tail(dw, h, y, B, C, hid, Fr, T, stat, stat + rows);
     } else {
-      rowview_stats(rz, B, 1e-5f, stat, stat + rows, nullptr);
-      const int64_t n = (int64_t)B * (C2 / 2) * Fr * T;
-      k_gn_glu_res<<<grid_for(n, 256), 256, 0, stream()>>>(
-          rz, stat, stat + rows, dw.gn4.w, dw.gn4.b, dw.scale, y, (int64_t)C * Fr * T, T,
-          (int64_t)Fr * T, B);
-      DCB_LAUNCHED();
+      conv(dw.c3g, h, nullptr, hv, 1, 1, 0, 0, 1, 1, 1, T, y, v, 3, y, dw.scale, stat,
+           stat + rows, &dw.gn4);
     }
-    dfree(z);
+    dfree(h);
   }
   dfree(stat);
 }

@@ -137,102 +137,9 @@ __global__ void k_gn_gelu(RowView v, float *__restrict__ y, const float *__restr
   }
 }
 
-// res[c] += scale[c] * (GN(x)[c] * sigmoid(GN(x)[c + C/2])) for c < C/2 (DConv tail,
-// layers.c:38-44); res has C/2 channels with channel stride rsC and the same b/f/t strides
-// pattern given by (rsB, rsF).
-__global__ void k_gn_glu_res(RowView v, const float *__restrict__ mean,
-                             const float *__restrict__ rstd, const float *__restrict__ w,
-                             const float *__restrict__ bb, const float *__restrict__ scale,
-                             float *__restrict__ res, int64_t rsB, int64_t rsF, int64_t rsC,
-                             int B) {
-  const int H = v.C / 2;
-  const int64_t per = (int64_t)H * v.T, total = (int64_t)B * v.Fr * per;
-  DCB_GRID_STRIDE(i, total) {
-    const int64_t row = i / per, e = i - row * per;
-    const int64_t c = e / v.T, t = e - c * v.T;
-    const int64_t b = row / v.Fr, f = row - b * v.Fr;
-    const float *xb = v.x + b * v.sB + f * v.sF + t;
-    const float m = mean[row], rs = rstd[row];
-    const float na = (xb[c * v.sC] - m) * rs * w[c] + bb[c];
-    const float nb = (xb[(c + H) * v.sC] - m) * rs * w[c + H] + bb[c + H];
-    const float g = na * sigmoid_f(nb);
-    float *rp = res + b * rsB + f * rsF + c * rsC + t;
-    *rp = *rp + g * scale[c];
-  }
-}
 
-// GroupNorm(1) of one strided row per CTA, fused with its consumer (DConv,
-// layers.c:31-44): statistics over the row's C x T elements in double (sum and sum of
-// squares; the reference's two passes in double agree to ~1e-15 for these magnitudes),
-// then a second pass over the now L2-resident row applies
-//   mode 0:  y = GELU(GN(x))                            (same layout as x, in place allowed)
-//   mode 1:  res[c] += scale[c] * GN(x)[c] * sigmoid(GN(x)[c + C/2]),  c < C/2
+// threads of the one-CTA-per-row GroupNorm kernels
 constexpr int kGnFusedThreads = 256;
-
-template <int MODE>
-__global__ void __launch_bounds__(kGnFusedThreads)
-    k_gn_fused(RowView v, float *__restrict__ y, const float *__restrict__ w,
-               const float *__restrict__ bb, const float *__restrict__ scale, int64_t rsB,
-               int64_t rsF, int64_t rsC, float eps) {
-  __shared__ double sh[2][kGnFusedThreads / 32];
-  const int64_t row = blockIdx.x;
-  const int64_t b = row / v.Fr, f = row - b * v.Fr;
-  const float *xr = v.x + b * v.sB + f * v.sF;
-  double s = 0.0, ss = 0.0;
-  for (int c = 0; c < v.C; c++) {
-    const float *xc = xr + c * v.sC;
-    for (int t = threadIdx.x; t < v.T; t += kGnFusedThreads) {
-      const double a = (double)xc[t];
-      s += a;
-      ss += a * a;
-    }
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    s += __shfl_xor_sync(0xffffffffu, s, o);
-    ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  }
-  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) {
-    sh[0][wid] = s;
-    sh[1][wid] = ss;
-  }
-  __syncthreads();
-  s = 0.0;
-  ss = 0.0;
-  for (int i = 0; i < kGnFusedThreads / 32; i++) {
-    s += sh[0][i];
-    ss += sh[1][i];
-  }
-  const double n = (double)v.C * v.T;
-  const double md = s / n;
-  double vd = ss / n - md * md;
-  if (vd < 0.0) vd = 0.0;
-  const float m = (float)md;
-  const float rs = 1.0f / sqrtf((float)vd + eps);
-  if (MODE == 0) {
-    float *yr = y + b * v.sB + f * v.sF;
-    for (int c = 0; c < v.C; c++) {
-      const float *xc = xr + c * v.sC;
-      float *yc = yr + c * v.sC;
-      const float wc = w[c], bc = bb[c];
-      for (int t = threadIdx.x; t < v.T; t += kGnFusedThreads)
-        yc[t] = gelu_f((xc[t] - m) * rs * wc + bc);
-    }
-  } else {
-    const int H = v.C / 2;
-    float *rr = y + b * rsB + f * rsF;
-    for (int c = 0; c < H; c++) {
-      const float *xa = xr + c * v.sC, *xb = xr + (c + H) * v.sC;
-      float *rc = rr + c * rsC;
-      const float wa = w[c], ba = bb[c], wb = w[c + H], bbv = bb[c + H], sc = scale[c];
-      for (int t = threadIdx.x; t < v.T; t += kGnFusedThreads) {
-        const float na = (xa[t] - m) * rs * wa + ba;
-        const float nb = (xb[t] - m) * rs * wb + bbv;
-        rc[t] = rc[t] + na * sigmoid_f(nb) * sc;
-      }
-    }
-  }
-}
 
 // DConv hidden rows (layers.c:24-53, the freq branch viewed as B*Fr rows [hid][T]):
 // GroupNorm(1) + GELU in place, one CTA per row, and the GroupNorm(1) statistics of the
@@ -346,6 +253,144 @@ __global__ void __launch_bounds__(kGnFusedThreads)
     if (vz < 0.0) vz = 0.0;
     zmean[row] = (float)mz;
     zrstd[row] = 1.0f / sqrtf((float)vz + eps);
+  }
+}
+
+// Sums S_j and upper Gram entries Q_jk (j <= k) of fp16(h) over one chunk of a DConv
+// hidden row [hid][T], accumulated in fp64 into acc[row][npair + hid] (npair = hid (hid +
+// 1) / 2, the sums last): the statistics of z = W16 . fp16(h) + b for rows too long for
+// one CTA.  Block (chunk, row); the chunk is staged in shared memory [hid][len].
+constexpr int kGramChunk = 1024;
+__global__ void __launch_bounds__(256)
+    k_gram_chunk(RowView v, int chunk, double *__restrict__ acc) {
+  extern __shared__ float hs[];
+  const int64_t row = blockIdx.y;
+  const int64_t b = row / v.Fr, f = row - b * v.Fr;
+  const int hid = v.C;
+  const int64_t t0 = (int64_t)blockIdx.x * chunk;
+  const int len = (int)(v.T - t0 < chunk ? v.T - t0 : chunk);
+  const float *xr = v.x + b * v.sB + f * v.sF + t0;
+  for (int i = threadIdx.x; i < hid * len; i += blockDim.x) {
+    const int j = i / len, t = i - j * len;
+    hs[j * len + t] = __half2float(__float2half_rn(xr[(int64_t)j * v.sC + t]));
+  }
+  __syncthreads();
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npair = hid * (hid + 1) / 2;
+  for (int p = wid; p < npair + hid; p += blockDim.x / 32) {
+    int j, k;
+    if (p < npair) {
+      j = 0;
+      int q = p;
+      while (q >= hid - j) {
+        q -= hid - j;
+        j++;
+      }
+      k = j + q;
+    } else {
+      j = p - npair;
+      k = -1;
+    }
+    const float *hj = hs + j * len;
+    const float *hk = k >= 0 ? hs + k * len : nullptr;
+    double a = 0.0;
+    for (int t = lane; t < len; t += 32) a += (double)(hk ? hj[t] * hk[t] : hj[t]);
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) atomicAdd(&acc[row * (npair + hid) + p], a);
+  }
+}
+
+// GroupNorm statistics of z from the accumulated sums (see k_gn_gelu_zstats), one thread
+// per row
+__global__ void k_zstats_final(const double *__restrict__ acc, const double *__restrict__ zc,
+                               int hid, int64_t T, int C2, int rows, float eps,
+                               float *__restrict__ zmean, float *__restrict__ zrstd) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const int npair = hid * (hid + 1) / 2;
+  const double *a = acc + (int64_t)row * (npair + hid);
+  const double *G = zc, *u = zc + hid * hid, *vv = u + hid;
+  double sz = (double)T * zc[hid * hid + 2 * hid], szz = (double)T * zc[hid * hid + 2 * hid + 1];
+  int p = 0;
+  for (int j = 0; j < hid; j++)
+    for (int k = j; k < hid; k++, p++) szz += (j == k ? 1.0 : 2.0) * G[j * hid + k] * a[p];
+  for (int j = 0; j < hid; j++) {
+    sz += u[j] * a[npair + j];
+    szz += 2.0 * vv[j] * a[npair + j];
+  }
+  const double nz = (double)C2 * T;
+  const double mz = sz / nz;
+  double vz = szz / nz - mz * mz;
+  if (vz < 0.0) vz = 0.0;
+  zmean[row] = (float)mz;
+  zrstd[row] = 1.0f / sqrtf((float)vz + eps);
+}
+
+// DConv tail on CUDA cores for small hidden widths (layers.c:24-53, hid = C / 8 <= 24):
+// y[c] += scale[c] * GLU(GroupNorm(W16 . fp16(h) + b)) per position, with the GroupNorm
+// statistics of each row (b, f) precomputed.  A 1x1 conv of K = hid is a handful of MACs
+// per output, too few for a tensor-core tile; here one thread per position keeps fp16(h)
+// in registers and reads the weights [2C][HIDP] as fp32 from shared memory (broadcast).
+// Products of fp16 values are exact in fp32 and summed in fp32, as the tensor cores do.
+template <int HIDP>
+__global__ void __launch_bounds__(256)
+    k_dconv_tail(const float *__restrict__ h, float *__restrict__ y, const uint16_t *__restrict__ w16,
+                 int64_t ldw, const float *__restrict__ bias, const float *__restrict__ gw,
+                 const float *__restrict__ gb, const float *__restrict__ scale,
+                 const float *__restrict__ zmean, const float *__restrict__ zrstd, int B, int C,
+                 int hid, int Fr, int64_t T, int64_t hsB, int64_t hsC, int64_t ysB,
+                 int64_t ysC) {
+  extern __shared__ float sm[];
+  float *sw = sm;                    // [2C][HIDP]
+  float *sbias = sw + 2 * C * HIDP;  // [2C]
+  float *sgw = sbias + 2 * C;        // [2C]
+  float *sgb = sgw + 2 * C;          // [2C]
+  float *ssc = sgb + 2 * C;          // [C]
+  for (int i = threadIdx.x; i < 2 * C * HIDP; i += blockDim.x) {
+    const int c = i / HIDP, j = i - c * HIDP;
+    sw[i] = j < hid ? h2f_bits(w16[(int64_t)c * ldw + j]) : 0.f;
+  }
+  for (int i = threadIdx.x; i < 2 * C; i += blockDim.x) {
+    sbias[i] = bias[i];
+    sgw[i] = gw[i];
+    sgb[i] = gb[i];
+    if (i < C) ssc[i] = scale[i];
+  }
+  __syncthreads();
+  const int64_t total = (int64_t)B * Fr * T;
+  for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < total;
+       p += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = p / T, t = p - row * T;
+    const int64_t b = row / Fr, f = row - b * Fr;
+    const float mu = zmean[row], rs = zrstd[row];
+    const float *hp = h + b * hsB + f * T + t;
+    float hv[HIDP];
+#pragma unroll
+    for (int j = 0; j < HIDP; j++)
+      hv[j] = j < hid ? __half2float(__float2half_rn(hp[(int64_t)j * hsC])) : 0.f;
+    float *yp = y + b * ysB + f * T + t;
+    for (int c = 0; c < C; c++) {
+      const float4 *wa = (const float4 *)(sw + c * HIDP);
+      const float4 *wb = (const float4 *)(sw + (C + c) * HIDP);
+      float a = 0.f, g = 0.f;
+#pragma unroll
+      for (int j = 0; j < HIDP / 4; j++) {
+        const float4 x = wa[j], z = wb[j];
+        a = fmaf(x.x, hv[4 * j], a);
+        a = fmaf(x.y, hv[4 * j + 1], a);
+        a = fmaf(x.z, hv[4 * j + 2], a);
+        a = fmaf(x.w, hv[4 * j + 3], a);
+        g = fmaf(z.x, hv[4 * j], g);
+        g = fmaf(z.y, hv[4 * j + 1], g);
+        g = fmaf(z.z, hv[4 * j + 2], g);
+        g = fmaf(z.w, hv[4 * j + 3], g);
+      }
+      a = (a + sbias[c] - mu) * rs * sgw[c] + sgb[c];
+      g = (g + sbias[C + c] - mu) * rs * sgw[C + c] + sgb[C + c];
+      const float v = a * __fdividef(1.0f, 1.0f + __expf(-g));
+      float *yc = yp + (int64_t)c * ysC;
+      *yc = *yc + ssc[c] * v;
+    }
   }
 }
 
