@@ -184,9 +184,14 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         for (int i = 0; i < kKV; i++)
           if (kbase + i >= a.Tk) v[i] = -INFINITY;
       }
-      float mx = v[0];
+      // tree reductions: short dependency chains for the per-block max and sum
+      float m8[8];
 #pragma unroll
-      for (int i = 1; i < kKV; i++) mx = fmaxf(mx, v[i]);
+      for (int i = 0; i < 8; i++) m8[i] = v[i];
+#pragma unroll
+      for (int i = 8; i < kKV; i++) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       const float ms = mx * sl2;
       if (ms > m_run + 8.0f) {
         if (j > 0) {
@@ -218,16 +223,16 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         ok = false;
         break;
       }
-      float psum = 0.f;
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t w[kKV / 2];
 #pragma unroll
       for (int i = 0; i < kKV; i += 2) {
         const float p0 = exp2f(fmaf(v[i], sl2, -m_run));
         const float p1 = exp2f(fmaf(v[i + 1], sl2, -m_run));
-        psum += p0 + p1;
+        ps[(i >> 1) & 7] += p0 + p1;
         w[i >> 1] = pack_h2(p0, p1);
       }
-      l_run += psum;
+      l_run += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       const uint32_t prow = smem_u32(sP + (j & 1) * kPBytes);
 #pragma unroll
       for (int c = 0; c < 8; c++)

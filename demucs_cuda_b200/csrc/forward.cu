@@ -252,7 +252,7 @@ static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
       const dim3 gg((unsigned)((T + chunk - 1) / chunk), rows);
       k_gram_chunk<<<gg, 256, (size_t)hid * chunk * sizeof(float), stream()>>>(rh, chunk, acc);
       DCB_LAUNCHED();
-      k_zstats_final<<<(rows + 127) / 128, 128, 0, stream()>>>(acc, dw.zc, hid, T, C2,
+      k_zstats_final<<<(rows + 3) / 4, 128, 0, stream()>>>(acc, dw.zc, hid, T, C2,
                                                               (int)rows, 1e-5f, stat,
                                                               stat + rows);
       DCB_LAUNCHED();

@@ -684,32 +684,41 @@ static __device__ __forceinline__ void ct_epilogue(const ConvTma &c, const Epi &
   for (int c0 = cbeg; c0 < cbeg + per; c0 += 16) {
     float va[16];
     tmem_ld16(trow + c0, va);
+    // per-column constants: lane i < 16 loads column i's, shuffles hand them out
+    const int li = lane & 15;
+    const int colx = obase + c0 + li;
     if (glu) {
       float vb[16];
       tmem_ld16(trow + e.glu_half + c0, vb);
+      const bool okc = colx < e.O;
+      const float ba = okc && e.bias ? e.bias[colx] : 0.f;
+      const float bb = okc && e.bias ? e.bias[e.O + colx] : 0.f;
+      float wa = 1.f, wb = 1.f, za = 0.f, zb = 0.f;
+      if (e.act == 3 && okc) {
+        wa = e.gn_w[colx] * grs;
+        wb = e.gn_w[e.O + colx] * grs;
+        za = e.gn_b[colx];
+        zb = e.gn_b[e.O + colx];
+      }
       tmem_wait_ld();
 #pragma unroll
       for (int i = 0; i < 16; i++) {
-        const int o = obase + c0 + i;
-        float val = 0.f;
-        if (o < e.O) {
-          float a = va[i] + (e.bias ? e.bias[o] : 0.f);
-          float b = vb[i] + (e.bias ? e.bias[e.O + o] : 0.f);
-          if (e.act == 3) {
-            a = (a - gmu) * grs * e.gn_w[o] + e.gn_b[o];
-            b = (b - gmu) * grs * e.gn_w[e.O + o] + e.gn_b[e.O + o];
-          }
-          val = a * sigmoid_fast(b);
+        const float bai = __shfl_sync(0xffffffffu, ba, i);
+        const float bbi = __shfl_sync(0xffffffffu, bb, i);
+        float a = va[i] + bai, b = vb[i] + bbi;
+        if (e.act == 3) {
+          a = (a - gmu) * __shfl_sync(0xffffffffu, wa, i) + __shfl_sync(0xffffffffu, za, i);
+          b = (b - gmu) * __shfl_sync(0xffffffffu, wb, i) + __shfl_sync(0xffffffffu, zb, i);
         }
-        wst[i * 32 + lane] = val;
+        wst[i * 32 + lane] = obase + c0 + i < e.O ? a * sigmoid_fast(b) : 0.f;
       }
     } else {
+      const int ox = e.mode == EPI_CONVTR ? colx / e.stride : colx;
+      const float bx = (e.bias && ox < e.O) ? e.bias[ox] : 0.f;
       tmem_wait_ld();
 #pragma unroll
       for (int i = 0; i < 16; i++) {
-        const int col = obase + c0 + i;
-        const int o = e.mode == EPI_CONVTR ? col / e.stride : col;
-        float val = va[i] + ((e.bias && o < e.O) ? e.bias[o] : 0.f);
+        float val = va[i] + __shfl_sync(0xffffffffu, bx, i);
         if (e.act == 1) val = gelu_f(val);
         wst[i * 32 + lane] = val;
       }

@@ -300,30 +300,45 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// GroupNorm statistics of z from the accumulated sums (see k_gn_gelu_zstats), one thread
-// per row
+// GroupNorm statistics of z from the accumulated sums (see k_gn_gelu_zstats), one warp per
+// row: lanes split the Gram entries, fp64 shuffle reduction
 __global__ void k_zstats_final(const double *__restrict__ acc, const double *__restrict__ zc,
                                int hid, int64_t T, int C2, int rows, float eps,
                                float *__restrict__ zmean, float *__restrict__ zrstd) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const int npair = hid * (hid + 1) / 2;
   const double *a = acc + (int64_t)row * (npair + hid);
   const double *G = zc, *u = zc + hid * hid, *vv = u + hid;
-  double sz = (double)T * zc[hid * hid + 2 * hid], szz = (double)T * zc[hid * hid + 2 * hid + 1];
-  int p = 0;
-  for (int j = 0; j < hid; j++)
-    for (int k = j; k < hid; k++, p++) szz += (j == k ? 1.0 : 2.0) * G[j * hid + k] * a[p];
-  for (int j = 0; j < hid; j++) {
+  double sz = 0.0, szz = 0.0;
+  for (int p = lane; p < npair; p += 32) {
+    int j = 0, q = p;
+    while (q >= hid - j) {
+      q -= hid - j;
+      j++;
+    }
+    const int k = j + q;
+    szz += (j == k ? 1.0 : 2.0) * G[j * hid + k] * a[p];
+  }
+  for (int j = lane; j < hid; j += 32) {
     sz += u[j] * a[npair + j];
     szz += 2.0 * vv[j] * a[npair + j];
   }
-  const double nz = (double)C2 * T;
-  const double mz = sz / nz;
-  double vz = szz / nz - mz * mz;
-  if (vz < 0.0) vz = 0.0;
-  zmean[row] = (float)mz;
-  zrstd[row] = 1.0f / sqrtf((float)vz + eps);
+  for (int o = 16; o > 0; o >>= 1) {
+    sz += __shfl_xor_sync(0xffffffffu, sz, o);
+    szz += __shfl_xor_sync(0xffffffffu, szz, o);
+  }
+  if (lane == 0) {
+    sz += (double)T * zc[hid * hid + 2 * hid];
+    szz += (double)T * zc[hid * hid + 2 * hid + 1];
+    const double nz = (double)C2 * T;
+    const double mz = sz / nz;
+    double vz = szz / nz - mz * mz;
+    if (vz < 0.0) vz = 0.0;
+    zmean[row] = (float)mz;
+    zrstd[row] = 1.0f / sqrtf((float)vz + eps);
+  }
 }
 
 // DConv tail on CUDA cores for small hidden widths (layers.c:24-53, hid = C / 8 <= 24):

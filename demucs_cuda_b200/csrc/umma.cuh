@@ -86,8 +86,8 @@ static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; i++) {
-    if (mbar_try_sleep(bar, parity, kSuspendNs)) return true;
-    if ((i & 15u) == 0) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 255u) == 0) {
       if (fault_pending()) return false;
       if (global_ns() - t0 > kWaitNs) {
         atomicOr(&g_dev_fault, fault);
