@@ -524,9 +524,10 @@ static bool load_conv(Loader &L, Staging &st, const std::string &prefix, ConvW &
   return true;
 }
 
-// transposed conv weight [O][Ktaps][(1)][C] -> phase matrix B[(o, r)][(j', c)] =
+// transposed conv weight [O][Ktaps][(1)][C] -> phase matrix B[(r, o)][(j', c)] =
 // W[o][r + S (1 - j')][c] (tap j' = 0 reads input q-1, j' = 1 reads input q)
-static bool load_convtr(Loader &L, Staging &st, const std::string &prefix, ConvW &cw, int S) {
+static bool load_convtr(Loader &L, Staging &st, const std::string &prefix, ConvW &cw, int S,
+                        bool axis_h) {
   const StEntry *e = L.get(prefix + ".conv.weight");
   if (!e) return false;
   const int nd = (int)e->shape.size();
@@ -546,7 +547,7 @@ static bool load_convtr(Loader &L, Staging &st, const std::string &prefix, ConvW
       for (int jp = 0; jp < 2; jp++) {
         const int tap = r + S * (1 - jp);
         for (int c = 0; c < C; c++)
-          ph[((size_t)o * S + r) * ld + jp * C + c] = host_f2h(w[((size_t)o * Kt + tap) * C + c]);
+          ph[((size_t)r * O + o) * ld + jp * C + c] = host_f2h(w[((size_t)o * Kt + tap) * C + c]);
       }
   cw.O = O;
   cw.C = C;
@@ -554,9 +555,8 @@ static bool load_convtr(Loader &L, Staging &st, const std::string &prefix, ConvW
   cw.ld = ld;
   cw.rows = O * S;
   st.add(ph.data(), ph.size() * 2, (void **)&cw.w);
-  // taps along H, as the frequency decoders use them (the time decoders' convs take the
-  // gather kernel)
-  stage_tma_order(st, cw, ph, cw.rows, ld, 2, 1, C);
+  // the two taps run along H (frequency decoders) or W (time decoders)
+  stage_tma_order(st, cw, ph, cw.rows, ld, axis_h ? 2 : 1, axis_h ? 1 : 2, C);
   stage_f32(st, b, &cw.bias);
   return true;
 }
@@ -728,7 +728,7 @@ DcbModel *dcb_model_load(const char *st_path, const char *cfg_path) {
     ok &= rw != nullptr;
     if (ok) ok &= load_conv(L, st, p, d.rewrite, true, glu_bn_for(rw->shape[0] / 2));
     snprintf(p, sizeof(p), "decoder.%d.conv_tr", i);
-    if (ok) ok &= load_convtr(L, st, p, d.convtr, c.stride);
+    if (ok) ok &= load_convtr(L, st, p, d.convtr, c.stride, true);
     d.Cin = d.rewrite.C;
     d.Cout = d.convtr.O;
     DecW &t = m->tdec[i];
@@ -737,7 +737,7 @@ DcbModel *dcb_model_load(const char *st_path, const char *cfg_path) {
     ok &= rt != nullptr;
     if (ok) ok &= load_conv(L, st, p, t.rewrite, true, glu_bn_for(rt->shape[0] / 2));
     snprintf(p, sizeof(p), "tdecoder.%d.conv_tr", i);
-    if (ok) ok &= load_convtr(L, st, p, t.convtr, c.stride);
+    if (ok) ok &= load_convtr(L, st, p, t.convtr, c.stride, false);
     t.Cin = t.rewrite.C;
     t.Cout = t.convtr.O;
   }

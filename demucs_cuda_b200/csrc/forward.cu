@@ -177,20 +177,117 @@ static void conv_tr(const ConvW &cw, const float *x, const Img &in, bool axis_h,
               cw.ldt, cw.ncb);
 }
 
+// ------------------------------------------------------------------ fp16 companions
+// fp16 channels-last copy of an activation [images][C][H][W]: [images][H][Wp][C] (Wp = W,
+// or W rounded up to a multiple of 4 with zero positions past W where a stride-4 conv
+// reads it), written by the producing kernel and read by the next conv through TMA.
+struct Half16 {
+  uint16_t *p = nullptr;
+  int64_t images = 0;
+  int C = 0, H = 1, W = 0, Wp = 0;
+  HalfAct act() const { return HalfAct{p, images, C, H, W, Wp}; }
+  // [images * H][1][Wp][C]: the DConv view (frequency rows are images)
+  HalfAct rows() const { return HalfAct{p, images * H, C, 1, W, Wp}; }
+};
+
+static Half16 half_alloc(int64_t images, int C, int H, int W, bool pad4) {
+  Half16 h;
+  if (C % 8) return h;  // no companion: the convs read the fp32 tensor
+  h.images = images;
+  h.C = C;
+  h.H = H;
+  h.W = W;
+  h.Wp = pad4 ? (W + 3) / 4 * 4 : W;
+  const size_t n = (size_t)images * H * h.Wp * C;
+  h.p = halloc(n);
+  if (h.Wp != W) DCB_CUDA(cudaMemsetAsync(h.p, 0, n * 2, stream()));
+  return h;
+}
+
+// fp16 companion of an fp32 NCHW tensor [images][C][H][W] (+ addend of the same layout)
+static Half16 to_half(const float *x, const float *add, int64_t images, int C, int H, int W,
+                      bool pad4) {
+  Half16 h = half_alloc(images, C, H, W, pad4);
+  if (!h.p) return h;
+  const int64_t n = images * H * (int64_t)W * (C / 8);
+  k_to_half_cl<<<grid_for(n, 256), 256, 0, stream()>>>(x, add, h.p, images, C, H, W, h.Wp,
+                                                       (int64_t)C * H * W, (int64_t)H * W, W);
+  DCB_LAUNCHED();
+  return h;
+}
+
+// point the epilogue's fp16 copy at h (its [images][H][Wp][C] layout)
+static void epi_half(Epi &e, const Half16 &h) {
+  e.yh = h.p;
+  e.yhH = h.H;
+  e.yhW = h.Wp;
+  e.yhC = h.C;
+}
+
+// conv through the fp16 companion when the TMA kernel covers it, else the gather kernel on
+// the fp32 tensor (then the companion, if wanted, is converted from the fp32 output)
+static void conv_any(const ConvW &cw, const float *x, const Half16 *xh, const Img &in, int SH,
+                     int SW, int PH, int PW, int DH, int DW, int Ho, int Wo, float *y,
+                     const Img &out, int act, Half16 *yh, bool rows_view,
+                     const float *emb = nullptr, float emb_alpha = 0.f, int emb_ld = 0) {
+  Epi e;
+  e.mode = EPI_CONV;
+  e.bias = cw.bias;
+  e.act = act;
+  e.y = y;
+  e.oN2 = out.N2;
+  e.oN1 = out.sN1;
+  e.oN2s = out.sN2;
+  e.oC = out.sC;
+  e.oH = out.sH;
+  e.O = act >= 2 ? cw.O / 2 : cw.O;
+  e.Ho = Ho;
+  e.Wo = Wo;
+  e.emb = emb;
+  e.emb_alpha = emb_alpha;
+  e.emb_ld = emb_ld;
+  if (yh && yh->p) epi_half(e, *yh);
+  if (xh && xh->p && cw.wt) {
+    const HalfAct a = rows_view ? xh->rows() : xh->act();
+    if (conv_half(a, cw.KH, cw.KW, SH, SW, PH, PW, DH, DW, Ho, Wo, cw.wt, cw.rows, cw.ldt,
+                  cw.ncb, e, act >= 2 ? cw.glu_bn : 0))
+      return;
+  }
+  DCB_REQUIRE(x != nullptr && y != nullptr, "conv: the gather kernel needs fp32 tensors");
+  conv(cw, x, nullptr, in, SH, SW, PH, PW, DH, DW, Ho, Wo, y, out, act);
+  if (emb) {
+    const int64_t n = (int64_t)out.N1 * e.O * Ho * Wo;
+    k_add_freq_emb<<<grid_for(n, 256), 256, 0, stream()>>>(y, emb, emb_alpha, out.N1, e.O, Ho,
+                                                          Wo, emb_ld);
+    DCB_LAUNCHED();
+  }
+  if (yh && yh->p) {
+    // fp32 output -> companion; out is contiguous [N1*N2 images][C][Ho][Wo] or rows
+    const int64_t n = (int64_t)yh->images * yh->H * yh->W * (yh->C / 8);
+    k_to_half_cl<<<grid_for(n, 256), 256, 0, stream()>>>(
+        y, nullptr, yh->p, yh->images, yh->C, yh->H, yh->W, yh->Wp, out.sN1,
+        rows_view ? (int64_t)yh->H * yh->W : out.sC, yh->W);
+    DCB_LAUNCHED();
+  }
+}
+
 // ------------------------------------------------------------------ layers
-// y += scale * GLU(GroupNorm(conv1x1(h))) of a DConv layer on CUDA cores (hid <= 24)
+// y += scale * GLU(GroupNorm(conv1x1(h))) of a DConv layer on CUDA cores (hid <= 24), also
+// refreshing the fp16 companion of y
 static void dconv_tail(const DConvW &dw, const float *h, float *y, int B, int C, int hid,
-                       int Fr, int T, const float *zmean, const float *zrstd) {
+                       int Fr, int T, const float *zmean, const float *zrstd, Half16 *yh) {
   const int hidp = (hid + 3) / 4 * 4;
   const size_t sm = ((size_t)2 * C * hidp + 7 * (size_t)C) * sizeof(float);
   const int64_t total = (int64_t)B * Fr * T;
   const unsigned grid = grid_for(total, 256, 148 * 4);
   const int64_t hsB = (int64_t)hid * Fr * T, hsC = (int64_t)Fr * T;
   const int64_t ysB = (int64_t)C * Fr * T, ysC = (int64_t)Fr * T;
+  uint16_t *yhp = yh ? yh->p : nullptr;
+  const int64_t pitch = yh ? yh->Wp : 0;
 #define DCB_TAIL(P)                                                                            \
   k_dconv_tail<P><<<grid, 256, sm, stream()>>>(h, y, dw.c3.w, dw.c3.ld, dw.c3.bias, dw.gn4.w, \
                                               dw.gn4.b, dw.scale, zmean, zrstd, B, C, hid,   \
-                                              Fr, T, hsB, hsC, ysB, ysC)
+                                              Fr, T, hsB, hsC, ysB, ysC, yhp, pitch)
   switch (hidp) {
     case 4: DCB_TAIL(4); break;
     case 8: DCB_TAIL(8); break;
@@ -204,12 +301,13 @@ static void dconv_tail(const DConvW &dw, const float *h, float *y, int B, int C,
 }
 
 // DConv residual branch (layers.c:24-53) applied in place on y [B, C, Fr, T] (Fr = 1 for
-// the time branch): conv k3 (dilation 2^d) -> GroupNorm(1) + GELU -> conv 1x1 ->
-// GroupNorm(1) + GLU -> LayerScale -> residual.  The second GroupNorm's statistics come
-// from the sums and Gram matrix of the hidden rows (the 1x1 conv output is never formed),
-// and the 1x1 conv runs fused with everything after it: on CUDA cores for hidden widths
-// <= 24, as a tensor-core conv with a GroupNorm + GLU epilogue above.
-static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
+// the time branch) and its fp16 companion yh ([B][Fr][Wp][C], read by the k3 convs):
+// conv k3 (dilation 2^d) -> GroupNorm(1) + GELU -> conv 1x1 -> GroupNorm(1) + GLU ->
+// LayerScale -> residual.  The second GroupNorm's statistics come from the sums and Gram
+// matrix of the hidden rows (the 1x1 conv output is never formed), and the 1x1 conv runs
+// fused with everything after it: on CUDA cores for hidden widths <= 24, as a tensor-core
+// conv with a GroupNorm + GLU epilogue above.
+static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int T) {
   const Img v = freq_rows(B, C, Fr, T);
   const unsigned rows = (unsigned)((int64_t)B * Fr);
   // one CTA per row when there are many short rows (frequency branch); chunked statistics
@@ -224,7 +322,7 @@ static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
     // conv k3, dilation 2^d, padding 2^d -> h [B, hid, Fr, T]
     float *h = dalloc((size_t)B * hid * Fr * T);
     const Img hv = freq_rows(B, hid, Fr, T);
-    conv(dw.c0, y, nullptr, v, 1, 1, 0, dil, 1, dil, 1, T, h, hv, 0);
+    conv_any(dw.c0, y, yh, v, 1, 1, 0, dil, 1, dil, 1, T, h, hv, 0, nullptr, true);
     RowView rh{h, Fr, (int64_t)hid * Fr * T, T, (int64_t)Fr * T, hid, T};
     if (fused) {
       // GroupNorm(1) + GELU in place with the z statistics, one CTA per row
@@ -252,96 +350,165 @@ static void dconv(const EncW &E, float *y, int B, int C, int Fr, int T) {
       const dim3 gg((unsigned)((T + chunk - 1) / chunk), rows);
       k_gram_chunk<<<gg, 256, (size_t)hid * chunk * sizeof(float), stream()>>>(rh, chunk, acc);
       DCB_LAUNCHED();
-      k_zstats_final<<<(rows + 3) / 4, 128, 0, stream()>>>(acc, dw.zc, hid, T, C2,
-                                                              (int)rows, 1e-5f, stat,
-                                                              stat + rows);
+      k_zstats_final<<<(rows + 3) / 4, 128, 0, stream()>>>(acc, dw.zc, hid, T, C2, (int)rows,
+                                                          1e-5f, stat, stat + rows);
       DCB_LAUNCHED();
       dfree(acc);
     }
     if (hid <= 24) {
-      dconv_tail(dw, h, y, B, C, hid, Fr, T, stat, stat + rows);
+      dconv_tail(dw, h, y, B, C, hid, Fr, T, stat, stat + rows, yh);
     } else {
       conv(dw.c3g, h, nullptr, hv, 1, 1, 0, 0, 1, 1, 1, T, y, v, 3, y, dw.scale, stat,
            stat + rows, &dw.gn4);
+      if (yh && yh->p) {
+        const int64_t n = rows * (int64_t)T * (C / 8);
+        k_to_half_cl<<<grid_for(n, 256), 256, 0, stream()>>>(y, nullptr, yh->p, B, C, Fr, T,
+                                                             yh->Wp, (int64_t)C * Fr * T,
+                                                             (int64_t)Fr * T, T);
+        DCB_LAUNCHED();
+      }
     }
     dfree(h);
   }
   dfree(stat);
 }
 
-// freq encoder (dc_henc with freq = 1): x [B, Cin, H, W] -> [B, Cout, H/S, W]
-static float *enc_freq(DcbModel *m, int idx, const float *x, int B, int H, int W, int *Ho_out) {
+// freq encoder (dc_henc with freq = 1): x [B, Cin, H, W] (+ fp16 companion xh, or null) ->
+// z [B, Cout, H/S, W] and its companion zh
+static float *enc_freq(DcbModel *m, int idx, const float *x, const Half16 *xh, int B, int H,
+                       int W, int *Ho_out, Half16 *zh) {
   const EncW &E = m->enc[idx];
   const int S = m->cfg.stride, K = m->cfg.kernel_size, pad = K / 4;
   const int Ho = (H + 2 * pad - K) / S + 1;
   const int C = E.Cout;
   float *y = dalloc((size_t)B * C * Ho * W);
-  conv(E.conv, x, nullptr, contiguous(B, E.Cin, H, W), S, 1, pad, 0, 1, 1, Ho, W, y,
-       contiguous(B, C, Ho, W), 1);
-  dconv(E, y, B, C, Ho, W);
+  Half16 yh = half_alloc(B, C, Ho, W, false);
+  conv_any(E.conv, x, xh, contiguous(B, E.Cin, H, W), S, 1, pad, 0, 1, 1, Ho, W, y,
+           contiguous(B, C, Ho, W), 1, &yh, false);
+  dconv(E, y, &yh, B, C, Ho, W);
   float *z = dalloc((size_t)B * C * Ho * W);
+  *zh = half_alloc(B, C, Ho, W, false);
   const int ce = m->cfg.context_enc;
-  conv(E.rewrite, y, nullptr, contiguous(B, C, Ho, W), 1, 1, ce, ce, 1, 1, Ho, W, z,
-       contiguous(B, C, Ho, W), 2);
+  const bool emb = idx == 0 && m->freq_emb;
+  conv_any(E.rewrite, y, &yh, contiguous(B, C, Ho, W), 1, 1, ce, ce, 1, 1, Ho, W, z,
+           contiguous(B, C, Ho, W), 2, zh, false, emb ? m->freq_emb : nullptr,
+           m->cfg.freq_emb * m->cfg.emb_scale, m->fe_cols);
   dfree(y);
-  if (idx == 0 && m->freq_emb) {
-    const int64_t n = (int64_t)B * C * Ho * W;
-    k_add_freq_emb<<<grid_for(n, 256), 256, 0, stream()>>>(
-        z, m->freq_emb, m->cfg.freq_emb * m->cfg.emb_scale, B, C, Ho, W, m->fe_cols);
-    DCB_LAUNCHED();
-  }
+  dfree(yh.p);
   *Ho_out = Ho;
   return z;
 }
 
-// time encoder: x [B, Cin, L] -> [B, Cout, ceil(L/S)]
-static float *enc_time(DcbModel *m, int idx, const float *x, int B, int L, int *Lo_out) {
+// time encoder: x [B, Cin, L] (+ companion) -> z [B, Cout, ceil(L/S)] and its companion
+static float *enc_time(DcbModel *m, int idx, const float *x, const Half16 *xh, int B, int L,
+                       int *Lo_out, Half16 *zh) {
   const EncW &E = m->tenc[idx];
   const int S = m->cfg.stride, K = m->cfg.kernel_size, pad = K / 4;
   const int Lp = (L + S - 1) / S * S;  // zero pad to a multiple of the stride (layers.c:88-94)
   const int Lo = (Lp + 2 * pad - K) / S + 1;
   const int C = E.Cout;
   float *y = dalloc((size_t)B * C * Lo);
-  conv(E.conv, x, nullptr, contiguous(B, E.Cin, 1, L), 1, S, 0, pad, 1, 1, 1, Lo, y,
-       contiguous(B, C, 1, Lo), 1);
-  dconv(E, y, B, C, 1, Lo);
+  Half16 yh = half_alloc(B, C, 1, Lo, false);
+  conv_any(E.conv, x, xh, contiguous(B, E.Cin, 1, L), 1, S, 0, pad, 1, 1, 1, Lo, y,
+           contiguous(B, C, 1, Lo), 1, &yh, false);
+  dconv(E, y, &yh, B, C, 1, Lo);
   float *z = dalloc((size_t)B * C * Lo);
+  *zh = half_alloc(B, C, 1, Lo, true);  // read with stride 4 by the next encoder
   const int ce = m->cfg.context_enc;
-  conv(E.rewrite, y, nullptr, contiguous(B, C, 1, Lo), 1, 1, 0, ce, 1, 1, 1, Lo, z,
-       contiguous(B, C, 1, Lo), 2);
+  conv_any(E.rewrite, y, &yh, contiguous(B, C, 1, Lo), 1, 1, 0, ce, 1, 1, 1, Lo, z,
+           contiguous(B, C, 1, Lo), 2, zh, false);
   dfree(y);
+  dfree(yh.p);
   *Lo_out = Lo;
   return z;
 }
 
-// freq decoder: x, skip [B, Cin, H, W] -> [B, Cout, S*H, W]  (dc_hdec, layers.c:143-220)
-static float *dec_freq(DcbModel *m, int idx, const float *x, const float *skip, int B, int H,
-                       int W, bool last) {
+// transposed conv of a decoder from the fp16 companion zh of its input: y (fp32, optional)
+// and the fp16 companion of (y + skip_next) for the next decoder (optional)
+static bool convtr_half(const ConvW &cw, const Half16 &zh, bool axis_h, int S, int crop,
+                        int out_len, bool gelu, float *y, const Img &out, const float *skip_next,
+                        Half16 *yh) {
+  Epi e;
+  e.mode = EPI_CONVTR;
+  e.bias = cw.bias;
+  e.act = gelu ? 1 : 0;
+  e.y = y;
+  e.oN2 = out.N2;
+  e.oN1 = out.sN1;
+  e.oN2s = out.sN2;
+  e.oC = out.sC;
+  e.oH = out.sH;
+  e.O = cw.O;
+  e.stride = S;
+  e.crop = crop;
+  e.out_len = out_len;
+  e.axis_h = axis_h ? 1 : 0;
+  e.hskip = skip_next;
+  if (yh) epi_half(e, *yh);
+  const int Ho = axis_h ? zh.H + 1 : 1, Wo = axis_h ? zh.W : zh.W + 1;
+  e.Ho = Ho;
+  e.Wo = Wo;
+  return conv_half(zh.act(), axis_h ? 2 : 1, axis_h ? 1 : 2, 1, 1, axis_h ? 1 : 0,
+                   axis_h ? 0 : 1, 1, 1, Ho, Wo, cw.wt, cw.rows, cw.ldt, cw.ncb, e, 0);
+}
+
+// freq decoder (dc_hdec, layers.c:143-220): input x + skip given as its fp16 companion xs
+// (x, skip fp32 for the fallback path) -> y [B, Cout, S*H, W] (fp32 when want_y) and, when
+// skip_next is given, the companion of y + skip_next for the next decoder
+static float *dec_freq(DcbModel *m, int idx, const float *x, const float *skip, const Half16 *xs,
+                       int B, int H, int W, bool last, bool want_y, const float *skip_next,
+                       Half16 *yh) {
   const DecW &D = m->dec[idx];
   const int C = D.Cin, S = m->cfg.stride, c = m->cfg.context, pad = m->cfg.kernel_size / 4;
+  const int out_len = (H - 1) * S + m->cfg.kernel_size - 2 * pad;
+  const Img oimg = contiguous(B, D.Cout, out_len, W);
+  const bool tma = xs && xs->p && D.rewrite.wt && D.convtr.wt;
+  float *y = want_y || !tma ? dalloc((size_t)B * D.Cout * out_len * W) : nullptr;
+  if (tma) {
+    if (yh) *yh = half_alloc(B, D.Cout, out_len, W, false);
+    Half16 zh = half_alloc(B, C, H, W, false);
+    conv_any(D.rewrite, nullptr, xs, contiguous(B, C, H, W), 1, 1, c, c, 1, 1, H, W, nullptr,
+             contiguous(B, C, H, W), 2, &zh, false);
+    if (!convtr_half(D.convtr, zh, true, S, pad, out_len, !last, y, oimg, skip_next, yh))
+      fail("decoder %d: transposed conv not supported", idx);
+    dfree(zh.p);
+    return y;
+  }
+  // fp32 path (channel counts the TMA kernel does not take)
   float *z = dalloc((size_t)B * C * H * W);
   conv(D.rewrite, x, skip, contiguous(B, C, H, W), 1, 1, c, c, 1, 1, H, W, z,
        contiguous(B, C, H, W), 2);
-  const int out_len = (H - 1) * S + m->cfg.kernel_size - 2 * pad;
-  float *y = dalloc((size_t)B * D.Cout * out_len * W);
-  conv_tr(D.convtr, z, contiguous(B, C, H, W), true, S, pad, out_len, !last, y,
-          contiguous(B, D.Cout, out_len, W));
+  conv_tr(D.convtr, z, contiguous(B, C, H, W), true, S, pad, out_len, !last, y, oimg);
   dfree(z);
+  if (yh) *yh = to_half(y, skip_next, B, D.Cout, out_len, W, false);
   return y;
 }
 
-// time decoder: x, skip [B, Cin, L] -> [B, Cout, length]
-static float *dec_time(DcbModel *m, int idx, const float *x, const float *skip, int B, int L,
-                       int length, bool last) {
+// time decoder: input x + skip as the companion xs -> y [B, Cout, length]
+static float *dec_time(DcbModel *m, int idx, const float *x, const float *skip, const Half16 *xs,
+                       int B, int L, int length, bool last, bool want_y, const float *skip_next,
+                       Half16 *yh) {
   const DecW &D = m->tdec[idx];
   const int C = D.Cin, S = m->cfg.stride, c = m->cfg.context, pad = m->cfg.kernel_size / 4;
+  const Img oimg = contiguous(B, D.Cout, 1, length);
+  const bool tma = xs && xs->p && D.rewrite.wt && D.convtr.wt;
+  float *y = want_y || !tma ? dalloc((size_t)B * D.Cout * length) : nullptr;
+  if (tma) {
+    if (yh) *yh = half_alloc(B, D.Cout, 1, length, false);
+    Half16 zh = half_alloc(B, C, 1, L, false);
+    conv_any(D.rewrite, nullptr, xs, contiguous(B, C, 1, L), 1, 1, 0, c, 1, 1, 1, L, nullptr,
+             contiguous(B, C, 1, L), 2, &zh, false);
+    if (!convtr_half(D.convtr, zh, false, S, pad, length, !last, y, oimg, skip_next, yh))
+      fail("time decoder %d: transposed conv not supported", idx);
+    dfree(zh.p);
+    return y;
+  }
   float *z = dalloc((size_t)B * C * L);
   conv(D.rewrite, x, skip, contiguous(B, C, 1, L), 1, 1, 0, c, 1, 1, 1, L, z,
        contiguous(B, C, 1, L), 2);
-  float *y = dalloc((size_t)B * D.Cout * length);
-  conv_tr(D.convtr, z, contiguous(B, C, 1, L), false, S, pad, length, !last, y,
-          contiguous(B, D.Cout, 1, length));
+  conv_tr(D.convtr, z, contiguous(B, C, 1, L), false, S, pad, length, !last, y, oimg);
   dfree(z);
+  if (yh) *yh = to_half(y, skip_next, B, D.Cout, 1, length, false);
   return y;
 }
 
@@ -598,11 +765,17 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
   std::vector<int> fr_len, t_len;  // H of the freq input, length of the time input
   int H = nb, W = le, Lt = L;
   char name[32];
+  // fp16 channels-last companions of the encoder inputs (none for the first encoders,
+  // whose few input channels take the gather kernel)
+  Half16 xh_t, xh_f;
   for (int i = 0; i < depth; i++) {
     t_len.push_back(Lt);
     int Lo;
-    float *xt2 = enc_time(m, i, xt, B, Lt, &Lo);
+    Half16 zt;
+    float *xt2 = enc_time(m, i, xt, i ? &xh_t : nullptr, B, Lt, &Lo, &zt);
     if (i == 0) dfree(xt);  // the normalised input; encoder outputs live on as skips
+    dfree(xh_t.p);
+    xh_t = zt;
     xt = xt2;
     Lt = Lo;
     saved_t.push_back(xt);
@@ -610,14 +783,19 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
     sg.emit(name, xt, {B, m->tenc[i].Cout, Lt});
     fr_len.push_back(H);
     int Ho;
-    float *x2 = enc_freq(m, i, x, B, H, W, &Ho);
+    Half16 zf;
+    float *x2 = enc_freq(m, i, x, i ? &xh_f : nullptr, B, H, W, &Ho, &zf);
     if (i == 0) dfree(x);
+    dfree(xh_f.p);
+    xh_f = zf;
     x = x2;
     H = Ho;
     saved.push_back(x);
     snprintf(name, sizeof(name), "enc_%d", i);
     sg.emit(name, x, {B, m->enc[i].Cout, H, W});
   }
+  dfree(xh_t.p);
+  dfree(xh_f.p);
   // the encoder outputs are kept as skips; the transformer works on copies
   const int D = m->D;
   float *tx = dalloc((size_t)B * D * H * W), *txt = dalloc((size_t)B * D * Lt);
@@ -628,35 +806,56 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
   sg.emit("transformer_xt", txt, {B, D, Lt});
   x = tx;
   xt = txt;
-  // decoders (htdemucs.c:198-237)
+  // decoders (htdemucs.c:198-237).  Each decoder reads x + skip as an fp16 companion, which
+  // the previous decoder's transposed conv writes (the first: a conversion of the
+  // transformer output); the fp32 outputs are formed only where something reads them.
+  Half16 xs_f = to_half(x, saved.back(), B, D, H, W, false);
+  Half16 xs_t = to_half(xt, saved_t.back(), B, D, 1, Lt, false);
+  // a decoder also writes its fp32 output when the next one reads fp32 (its channel counts
+  // take the gather kernel)
+  auto tma_dec = [&](const DecW &d) {
+    return d.rewrite.wt && d.convtr.wt && d.Cin % 8 == 0;
+  };
   for (int i = 0; i < depth; i++) {
     const bool last = i == depth - 1;
+    const bool want_y = last || sg.fn || !tma_dec(m->dec[i + 1]);
+    const bool want_yt = last || sg.fn || !tma_dec(m->tdec[i + 1]);
     float *skip = saved.back();
     saved.pop_back();
     const int Hin = H;
     H = fr_len.back();
     fr_len.pop_back();
-    float *x2 = dec_freq(m, i, x, skip, B, Hin, W, last);
+    Half16 ys;
+    float *x2 = dec_freq(m, i, x, skip, &xs_f, B, Hin, W, last, want_y,
+                         last ? nullptr : saved.back(), last ? nullptr : &ys);
     dfree(x);
     dfree(skip);
+    dfree(xs_f.p);
+    xs_f = ys;
     x = x2;
     if (H != (Hin - 1) * c.stride + c.kernel_size - 2 * (c.kernel_size / 4)) {
       fail("decoder %d: frequency length mismatch", i);
     }
     snprintf(name, sizeof(name), "dec_%d", i);
-    sg.emit(name, x, {B, m->dec[i].Cout, H, W});
+    if (x) sg.emit(name, x, {B, m->dec[i].Cout, H, W});
     float *skip_t = saved_t.back();
     saved_t.pop_back();
     const int Lin = Lt;
     Lt = t_len.back();
     t_len.pop_back();
-    float *xt2 = dec_time(m, i, xt, skip_t, B, Lin, Lt, last);
+    Half16 yt;
+    float *xt2 = dec_time(m, i, xt, skip_t, &xs_t, B, Lin, Lt, last, want_yt,
+                          last ? nullptr : saved_t.back(), last ? nullptr : &yt);
     dfree(xt);
     dfree(skip_t);
+    dfree(xs_t.p);
+    xs_t = yt;
     xt = xt2;
     snprintf(name, sizeof(name), "tdec_%d", i);
-    sg.emit(name, xt, {B, m->tdec[i].Cout, Lt});
+    if (xt) sg.emit(name, xt, {B, m->tdec[i].Cout, Lt});
   }
+  dfree(xs_f.p);
+  dfree(xs_t.p);
   // output (htdemucs.c:242-279)
   const int S = c.n_sources;
   const int Ctot = m->dec[depth - 1].Cout;  // S * 2C
@@ -974,10 +1173,14 @@ int dcb_stage_encoder(DcbModel *m, int branch, int idx, const float *x, int B, i
     out_shape[3] = W;
     if (!y) return 0;
     int ho;
-    float *z = enc_freq(m, idx, x, B, H, W, &ho);
+    Half16 xh = idx > 0 ? to_half(x, nullptr, B, C, H, W, false) : Half16{};
+    Half16 zh;
+    float *z = enc_freq(m, idx, x, idx > 0 ? &xh : nullptr, B, H, W, &ho, &zh);
     DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * E.Cout * Ho * W * 4, cudaMemcpyDeviceToDevice,
                              stream()));
     dfree(z);
+    dfree(zh.p);
+    dfree(xh.p);
   } else {
     const EncW &E = m->tenc[idx];
     if (C != E.Cin) return -1;
@@ -989,10 +1192,14 @@ int dcb_stage_encoder(DcbModel *m, int branch, int idx, const float *x, int B, i
     out_shape[3] = 0;
     if (!y) return 0;
     int lo;
-    float *z = enc_time(m, idx, x, B, L, &lo);
+    Half16 xh = idx > 0 ? to_half(x, nullptr, B, C, 1, L, true) : Half16{};
+    Half16 zh;
+    float *z = enc_time(m, idx, x, idx > 0 ? &xh : nullptr, B, L, &lo, &zh);
     DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * E.Cout * Lo * 4, cudaMemcpyDeviceToDevice,
                              stream()));
     dfree(z);
+    dfree(zh.p);
+    dfree(xh.p);
   }
   DCB_CUDA(cudaStreamSynchronize(stream()));
   return failed() ? -1 : 0;
@@ -1012,10 +1219,12 @@ int dcb_stage_decoder(DcbModel *m, int branch, int idx, const float *x, const fl
     out_shape[2] = Ho;
     out_shape[3] = W;
     if (!y) return 0;
-    float *z = dec_freq(m, idx, x, skip, B, H, W, last);
+    Half16 xs = to_half(x, skip, B, C, H, W, false);
+    float *z = dec_freq(m, idx, x, skip, &xs, B, H, W, last, true, nullptr, nullptr);
     DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * D.Cout * Ho * W * 4, cudaMemcpyDeviceToDevice,
                              stream()));
     dfree(z);
+    dfree(xs.p);
   } else {
     const DecW &D = m->tdec[idx];
     if (C != D.Cin) return -1;
@@ -1024,10 +1233,12 @@ int dcb_stage_decoder(DcbModel *m, int branch, int idx, const float *x, const fl
     out_shape[2] = length;
     out_shape[3] = 0;
     if (!y) return 0;
-    float *z = dec_time(m, idx, x, skip, B, W, length, last);
+    Half16 xs = to_half(x, skip, B, C, 1, W, false);
+    float *z = dec_time(m, idx, x, skip, &xs, B, W, length, last, true, nullptr, nullptr);
     DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * D.Cout * length * 4, cudaMemcpyDeviceToDevice,
                              stream()));
     dfree(z);
+    dfree(xs.p);
   }
   DCB_CUDA(cudaStreamSynchronize(stream()));
   return failed() ? -1 : 0;

@@ -79,8 +79,9 @@ static __device__ __forceinline__ void store_elem(const Epi &e, const Shape &s, 
       break;
     }
     case EPI_CONVTR: {
-      int o = (int)(n / e.stride), r = (int)(n - (int64_t)o * e.stride);
-      if (o >= e.O) return;
+      // columns are (phase r, channel o), channels fastest
+      int r = (int)(n / e.O), o = (int)(n - (int64_t)r * e.O);
+      if (r >= e.stride) return;
       int q = e.axis_h ? ri.ho : ri.wo;
       int t = q * e.stride + r - e.crop;
       if (t < 0 || t >= e.out_len) return;
@@ -597,8 +598,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 // one fp32 box x[n][c0..c0+63][h][w_al..w_al+BW) (w_al = the first input position of the
 // tile rounded down to a 16-byte boundary; rows, positions and channels outside the
 // tensor read as zero, which is the convolution's zero padding) that serves every W tap;
-// four converter warps turn it into one fp16 (round-to-nearest-even) K-major
-// SWIZZLE_128B A tile per W tap, one output position per thread, adding the skip tensor
+// eight converter warps turn it into one fp16 (round-to-nearest-even) K-major
+// SWIZZLE_128B A tile per W tap, (one output position, 32 channels) per thread, adding the skip tensor
 // when there is one; the TMA warp also streams the B tiles; one thread issues
 // tcgen05.mma.  The box ring and the operand ring are separate, so a box is refilled as
 // soon as its A tiles are built.  One persistent CTA per SM: 512 TMEM columns hold two
@@ -619,7 +620,8 @@ struct ConvTma {
   int xstages, stages;
 };
 
-constexpr int kCtThreads = 448;  // warps 0-7 epilogue, 8-11 converters, 12 TMA, 13 MMA
+constexpr int kCtThreads = 576;  // warps 0-7 epilogue, 8-15 converters, 16 TMA, 17 MMA
+constexpr int kCtTmaWarp = 16, kCtMmaWarp = 17;
 constexpr int kCtBoxMax = 256;   // TMA box extent limit
 constexpr int kCtEpiCW = 16;     // epilogue transpose chunk (columns)
 
@@ -713,7 +715,7 @@ static __device__ __forceinline__ void ct_epilogue(const ConvTma &c, const Epi &
         wst[i * 32 + lane] = obase + c0 + i < e.O ? a * sigmoid_fast(b) : 0.f;
       }
     } else {
-      const int ox = e.mode == EPI_CONVTR ? colx / e.stride : colx;
+      const int ox = e.mode == EPI_CONVTR ? colx % e.O : colx;
       const float bx = (e.bias && ox < e.O) ? e.bias[ox] : 0.f;
       tmem_wait_ld();
 #pragma unroll
@@ -730,9 +732,9 @@ static __device__ __forceinline__ void ct_epilogue(const ConvTma &c, const Epi &
       const int col = obase + c0 + cc;
       int64_t off;
       if (e.mode == EPI_CONVTR) {
-        const int o = col / e.stride, s = col - o * e.stride;
+        const int s = col / e.O, o = col - s * e.O;
         const int t = ho * e.stride + s - e.crop;
-        if (o >= e.O || t < 0 || t >= e.out_len) continue;
+        if (s >= e.stride || t < 0 || t >= e.out_len) continue;
         off = base + (int64_t)o * e.oC + (int64_t)t * e.oH;
       } else {
         if (col >= e.O) continue;
@@ -801,11 +803,11 @@ __global__ void __launch_bounds__(kCtThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < xstages; i++) {
       mbar_init(&xfull[i], 1);
-      mbar_init(&xempty[i], 4);
+      mbar_init(&xempty[i], 8);
     }
     for (int i = 0; i < stages; i++) {
       mbar_init(&bfull[i], 1);
-      mbar_init(&afull[i], 4);
+      mbar_init(&afull[i], 8);
       mbar_init(&empty[i], 1);
     }
     for (int b = 0; b < 2; b++) {
@@ -815,7 +817,7 @@ __global__ void __launch_bounds__(kCtThreads, 1)
     mbar_init(fin, 1);
     fence_mbar_init();
   }
-  if (warp == 13) {
+  if (warp == kCtMmaWarp) {
     tmem_alloc(tslot, (uint32_t)Cfg::kTmemCols);
     tmem_relinquish();
   }
@@ -824,7 +826,7 @@ __global__ void __launch_bounds__(kCtThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tslot;
 
-  if (warp == 12) {
+  if (warp == kCtTmaWarp) {
     // ---- TMA producer: per (kh, channel block) one box, then the KW B tiles
     if (lane == 0) {
       tma_prefetch_desc(&tmX);
@@ -865,7 +867,7 @@ __global__ void __launch_bounds__(kCtThreads, 1)
         }
       }
     }
-  } else if (warp == 13) {
+  } else if (warp == kCtMmaWarp) {
     // ---- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16_f32(kBM, BN);
@@ -898,8 +900,10 @@ __global__ void __launch_bounds__(kCtThreads, 1)
       mbar_wait(fin, 0, kFaultDone);
     }
   } else if (warp >= 8) {
-    // ---- converters: output position r of the tile, 64 channels per A tile
-    const int r = (warp - 8) * 32 + lane;
+    // ---- converters: warp w = 8 + (half << 2) + q builds rows 32q..32q+31 (one output
+    // position per thread) and channels 32 half..32 half+31 of each A tile
+    const int cw = warp - 8;
+    const int r = (cw & 3) * 32 + lane, ch0 = (cw >> 2) * 32;
     uint32_t it = 0, xi = 0;
     bool ok = true;
     for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
@@ -920,19 +924,20 @@ __global__ void __launch_bounds__(kCtThreads, 1)
             ok = false;
             break;
           }
-          const float *xs_r = xb + r + sh0 + kw * c.DW;
+          const float *xs_r = xb + (size_t)ch0 * c.bw + r + sh0 + kw * c.DW;
           const uint32_t a_base = smem_u32(sAB + (size_t)st * Cfg::kABStage);
+          float v[32];
 #pragma unroll
-          for (int cc = 0; cc < 8; cc++) {
-            float v[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-              v[i] = xs_r[(cc * 8 + i) * c.bw];
-              if (X2) v[i] += xs_r[(cc * 8 + i) * c.bw + 64 * c.bw];
-            }
-            st_shared_v4(a_base + sw128_off(r, cc), pack_h2(v[0], v[1]), pack_h2(v[2], v[3]),
-                         pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+          for (int i = 0; i < 32; i++) {
+            v[i] = xs_r[i * c.bw];
+            if (X2) v[i] += xs_r[i * c.bw + 64 * c.bw];
           }
+#pragma unroll
+          for (int cc = 0; cc < 4; cc++)
+            st_shared_v4(a_base + sw128_off(r, (ch0 >> 3) + cc), pack_h2(v[8 * cc], v[8 * cc + 1]),
+                         pack_h2(v[8 * cc + 2], v[8 * cc + 3]),
+                         pack_h2(v[8 * cc + 4], v[8 * cc + 5]),
+                         pack_h2(v[8 * cc + 6], v[8 * cc + 7]));
           fence_async_smem();
           __syncwarp();
           if (lane == 0) mbar_arrive(&afull[st]);
@@ -963,7 +968,376 @@ __global__ void __launch_bounds__(kCtThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 13) {
+  if (warp == kCtMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, (uint32_t)Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------- fp16 channels-last conv
+// Implicit-GEMM convolution whose A operand is an fp16 channels-last activation
+// [images][H][W][C] written by the producing layer.  A tile is 128 consecutive output
+// positions of one output line (n, ho); K blocks are (kh, 64-channel block, kw) and each
+// is ONE TMA box of 64 channels x 128 positions, which lands in shared memory exactly as
+// the K-major SWIZZLE_128B UMMA operand: the tap's position offset is the box coordinate,
+// positions and channels outside the tensor read as zero (the zero padding), a stride of 4
+// along W is a 5-D view (C, 4, W/4, H, images) of the same tensor.  No thread touches the
+// operand: a TMA warp streams A and B tiles into a shared-memory ring, one thread issues
+// tcgen05.mma into one of two TMEM accumulators, and 4 epilogue warps drain the other
+// (bias / GELU / GLU / GroupNorm-GLU / transposed-conv phase scatter, fp32 NCHW output
+// and/or the fp16 channels-last copy for the next conv).  Two CTAs per SM for N tiles up
+// to 128 columns.
+struct ConvH {
+  int KH, KW, SH, SW, PH, PW, DH, DW;
+  int Ho, Wo;
+  int ncb;        // 64-channel blocks
+  int64_t lines;  // output lines (images * Ho)
+  int tpl;        // tiles of 128 positions per line
+  int N, nkb, ntiles, stages;
+};
+
+constexpr int kChEpiWarps = 4;
+constexpr int kChTmaWarp = kChEpiWarps, kChMmaWarp = kChEpiWarps + 1;
+constexpr int kChThreads = 32 * (kChEpiWarps + 2);
+
+template <int BN>
+struct ChCfg {
+  static constexpr uint32_t kStage = kATileBytes + BN * 128;  // a multiple of 1024
+  static constexpr int kAccCols = BN < 32 ? 32 : BN;
+  static constexpr int kTmemCols = 2 * kAccCols;
+};
+
+static __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map,
+                                                   uint64_t *bar, int c0, int c1, int c2,
+                                                   int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+static __device__ __forceinline__ void ch_tile(const ConvH &c, int64_t tile, int64_t &line,
+                                               int &wo0, int &nt) {
+  nt = (int)(tile % c.ntiles);
+  const int64_t rest = tile / c.ntiles;
+  line = rest / c.tpl;
+  wo0 = (int)(rest - line * c.tpl) * kBM;
+}
+
+// Epilogue of one line tile by 4 warps (warp w: rows 32w..32w+31, every column), 16
+// columns per step.  Values go (1) from registers to the fp16 channels-last copy, 16
+// consecutive channels of a position per thread, and (2) through the warp's [16][32]
+// transpose buffer to the fp32 NCHW output, 4 consecutive positions per 16-byte store.
+template <int BN>
+static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e, uint32_t tacc,
+                                                   int warp, int lane, int64_t line, int wo0,
+                                                   int nt, float *wst) {
+  const uint32_t trow = tacc + ((uint32_t)(warp * 32) << 16);
+  const int64_t n = line / c.Ho;
+  const int ho = (int)(line - n * c.Ho);
+  const int64_t n1 = n / e.oN2, n2 = n - n1 * e.oN2;
+  const int64_t base = n1 * e.oN1 + n2 * e.oN2s;
+  const int r = warp * 32 + lane;
+  const int row_lim = c.Wo - wo0;  // tile rows r < row_lim are outputs
+  const bool rv = r < row_lim;
+  const int q = wo0 + r;           // output position along W (conv, conv_tr along H) or q
+  const bool convtr = e.mode == EPI_CONVTR;
+  const bool glu = !convtr && e.act >= 2;
+  float gmu = 0.f, grs = 0.f;
+  if (glu && e.act == 3) {
+    gmu = e.gn_mean[n];
+    grs = e.gn_rstd[n];
+  }
+  const int ncols = glu ? e.glu_half : BN;
+  const int obase = glu ? nt * e.glu_half : nt * BN;
+  const int ncol_total = convtr ? e.O * e.stride : e.O;
+  const int li = lane & 15;
+  for (int c0 = 0; c0 < ncols; c0 += 16) {
+    const int col0 = obase + c0;
+    if (col0 >= ncol_total) break;
+    float va[16];
+    tmem_ld16(trow + c0, va);
+    // per-column constants: lane i < 16 loads column i's, shuffles hand them out
+    const int colx = col0 + li;
+    const int ox = convtr ? colx % e.O : colx;
+    const bool okc = convtr ? colx < ncol_total : colx < e.O;
+    float val[16];
+    if (glu) {
+      float vb[16];
+      tmem_ld16(trow + e.glu_half + c0, vb);
+      const float ba = okc && e.bias ? e.bias[colx] : 0.f;
+      const float bb = okc && e.bias ? e.bias[e.O + colx] : 0.f;
+      float wa = 1.f, wb = 1.f, za = 0.f, zb = 0.f;
+      if (e.act == 3 && okc) {
+        wa = e.gn_w[colx] * grs;
+        wb = e.gn_w[e.O + colx] * grs;
+        za = e.gn_b[colx];
+        zb = e.gn_b[e.O + colx];
+      }
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        float a = va[i] + __shfl_sync(0xffffffffu, ba, i);
+        float b = vb[i] + __shfl_sync(0xffffffffu, bb, i);
+        if (e.act == 3) {
+          a = (a - gmu) * __shfl_sync(0xffffffffu, wa, i) + __shfl_sync(0xffffffffu, za, i);
+          b = (b - gmu) * __shfl_sync(0xffffffffu, wb, i) + __shfl_sync(0xffffffffu, zb, i);
+        }
+        val[i] = a * sigmoid_fast(b);
+      }
+    } else {
+      const float bx = (e.bias && okc) ? e.bias[ox] : 0.f;
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        float v = va[i] + __shfl_sync(0xffffffffu, bx, i);
+        if (e.act == 1) v = gelu_f(v);
+        val[i] = v;
+      }
+    }
+    if (e.emb) {
+      const float ex = okc ? e.emb_alpha * e.emb[(int64_t)ho * e.emb_ld + colx] : 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; i++) val[i] += __shfl_sync(0xffffffffu, ex, i);
+    }
+    // transposed conv: the chunk's phase s (uniform when O is a multiple of 16)
+    const int s0 = convtr ? col0 / e.O : 0;
+    const bool s_uniform = !convtr || (col0 + 15) / e.O == s0;
+    // ---- (1) fp16 channels-last copy
+    if (e.yh && rv) {
+      int h = ho, w = q;
+      bool ok = true;
+      if (convtr) {
+        const int t = (e.axis_h ? ho : q) * e.stride + s0 - e.crop;
+        ok = t >= 0 && t < e.out_len;
+        if (e.axis_h) h = t; else { h = 0; w = t; }
+      }
+      const int o0 = convtr ? col0 - s0 * e.O : col0;
+      if (ok && s_uniform) {
+        uint16_t *dst = e.yh + (((int64_t)n * e.yhH + h) * e.yhW + w) * e.yhC + o0;
+        const int64_t soff = base + (int64_t)o0 * e.oC + (int64_t)h * e.oH + w;
+        float hv[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          hv[i] = val[i];
+          if (e.hskip && o0 + i < e.O) hv[i] += e.hskip[soff + (int64_t)i * e.oC];
+        }
+        if (o0 + 16 <= e.O && (((uintptr_t)dst) & 15) == 0) {
+          uint4 *d4 = (uint4 *)dst;
+          d4[0] = make_uint4(pack_h2(hv[0], hv[1]), pack_h2(hv[2], hv[3]), pack_h2(hv[4], hv[5]),
+                             pack_h2(hv[6], hv[7]));
+          d4[1] = make_uint4(pack_h2(hv[8], hv[9]), pack_h2(hv[10], hv[11]),
+                             pack_h2(hv[12], hv[13]), pack_h2(hv[14], hv[15]));
+        } else {
+          for (int i = 0; i < 16 && o0 + i < e.O; i++) dst[i] = f2h_bits(hv[i]);
+        }
+      } else if (!s_uniform) {
+        for (int i = 0; i < 16; i++) {
+          const int col = col0 + i;
+          if (col >= ncol_total) break;
+          const int s = col / e.O, o = col - s * e.O;
+          const int t = (e.axis_h ? ho : q) * e.stride + s - e.crop;
+          if (t < 0 || t >= e.out_len) continue;
+          const int hh = e.axis_h ? t : 0, ww = e.axis_h ? q : t;
+          float v = val[i];
+          if (e.hskip) v += e.hskip[base + (int64_t)o * e.oC + (int64_t)hh * e.oH + ww];
+          e.yh[(((int64_t)n * e.yhH + hh) * e.yhW + ww) * e.yhC + o] = f2h_bits(v);
+        }
+      }
+    }
+    // ---- (2) fp32 NCHW output through the transpose buffer
+    if (e.y) {
+#pragma unroll
+      for (int i = 0; i < 16; i++) wst[i * 32 + lane] = val[i];
+      __syncwarp();
+      const int rq = 4 * (lane & 7);
+      const int rl = warp * 32 + rq;  // first of this lane's 4 rows
+#pragma unroll
+      for (int p = 0; p < 4; p++) {
+        const int cc = (lane >> 3) + 4 * p;
+        const int col = col0 + cc;
+        if (col >= ncol_total || (!convtr && col >= e.O)) continue;
+        const float4 v4 = *(const float4 *)(wst + cc * 32 + rq);
+        const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+        if (convtr && !e.axis_h) {
+          // phase scatter along W: output t = S q + s - crop
+          const int s = col / e.O, o = col - s * e.O;
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const int t = (wo0 + rl + i) * e.stride + s - e.crop;
+            if (rl + i < row_lim && t >= 0 && t < e.out_len)
+              e.y[base + (int64_t)o * e.oC + (int64_t)ho * e.oH + t] = vv[i];
+          }
+          continue;
+        }
+        int64_t off;
+        if (convtr) {
+          const int s = col / e.O, o = col - s * e.O;
+          const int t = ho * e.stride + s - e.crop;
+          if (t < 0 || t >= e.out_len) continue;
+          off = base + (int64_t)o * e.oC + (int64_t)t * e.oH + wo0 + rl;
+        } else {
+          off = base + (int64_t)col * e.oC + (int64_t)ho * e.oH + wo0 + rl;
+        }
+        const uintptr_t al = (uintptr_t)(e.y + off) | (e.res ? (uintptr_t)(e.res + off) : 0);
+        if (rl + 4 <= row_lim && (al & 15) == 0) {
+          float4 o4 = make_float4(vv[0], vv[1], vv[2], vv[3]);
+          if (e.res) {
+            const float4 rr = *(const float4 *)(e.res + off);
+            const float sc = e.scale[col];
+            o4 = make_float4(rr.x + sc * vv[0], rr.y + sc * vv[1], rr.z + sc * vv[2],
+                             rr.w + sc * vv[3]);
+          }
+          *(float4 *)(e.y + off) = o4;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            if (rl + i >= row_lim) continue;
+            float v = vv[i];
+            if (e.res) v = e.res[off + i] + e.scale[col] * v;
+            e.y[off + i] = v;
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kChThreads, 1)
+    k_conv_h(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+             const ConvH c, const Epi e) {
+  using Cfg = ChCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int stages = c.stages;
+  float *stg = (float *)(smem + (size_t)stages * Cfg::kStage);  // 4 warps x [16][32] fp32
+  uint64_t *full = (uint64_t *)(stg + kChEpiWarps * 16 * 32);
+  uint64_t *empty = full + stages;
+  uint64_t *acc_full = empty + stages;
+  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *fin = acc_empty + 2;
+  uint32_t *tslot = (uint32_t *)(fin + 1);
+
+  __shared__ uint32_t s_abort;
+  if (threadIdx.x == 0) s_abort = fault_pending() ? 1u : 0u;
+  __syncthreads();
+  if (s_abort) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t ntiles_total = c.lines * c.tpl * c.ntiles;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kChEpiWarps);
+    }
+    mbar_init(fin, 1);
+    fence_mbar_init();
+  }
+  if (warp == kChMmaWarp) {
+    tmem_alloc(tslot, (uint32_t)Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == kChTmaWarp) {
+    // ---- TMA producer: per K block one A box (64 channels x 128 positions) and a B tile
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
+        int64_t line;
+        int wo0, nt;
+        ch_tile(c, tile, line, wo0, nt);
+        const int64_t n = line / c.Ho;
+        const int ho = (int)(line - n * c.Ho);
+        for (int kb = 0; kb < c.nkb; kb++, it++) {
+          const int st = (int)(it % (uint32_t)stages);
+          if (!mbar_wait(&empty[st], ((it / (uint32_t)stages) & 1u) ^ 1u, kFaultEmpty)) {
+            ok = false;
+            break;
+          }
+          const int grp = kb / c.KW, kw = kb - grp * c.KW;
+          const int kh = grp / c.ncb, cb = grp - kh * c.ncb;
+          const int h = ho * c.SH - c.PH + kh * c.DH;
+          const int d = kw * c.DW - c.PW;  // tap offset along W
+          uint8_t *sb = smem + (size_t)st * Cfg::kStage;
+          mbar_expect_tx(&full[st], Cfg::kStage);
+          if (c.SW == 1) {
+            tma_load_4d(sb, &tmA, &full[st], cb * 64, wo0 + d, h, (int)n);
+          } else {
+            // input position 4 (wo0 + r) + d = 4 (q0 + r) + phase
+            const int phase = ((d % 4) + 4) % 4, q0 = wo0 + (d - phase) / 4;
+            tma_load_5d(sb, &tmA, &full[st], cb * 64, phase, q0, h, (int)n);
+          }
+          tma_load_3d(sb + kATileBytes, &tmB, &full[st], kb * kBK, nt * BN, 0);
+        }
+      }
+    }
+  } else if (warp == kChMmaWarp) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16_f32(kBM, BN);
+      uint32_t it = 0, local = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x, local++) {
+        const uint32_t buf = local & 1u, use = local >> 1;
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * (uint32_t)Cfg::kAccCols;
+        for (int kb = 0; kb < c.nkb; kb++, it++) {
+          const int st = (int)(it % (uint32_t)stages);
+          if (!mbar_wait(&full[st], (it / (uint32_t)stages) & 1u, kFaultFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint8_t *sb = smem + (size_t)st * Cfg::kStage;
+          const uint64_t ad = sw128_desc(smem_u32(sb));
+          const uint64_t bd = sw128_desc(smem_u32(sb + kATileBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; k++)
+            umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit(&empty[st]);
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+      umma_commit(fin);
+      mbar_wait(fin, 0, kFaultDone);
+    }
+  } else {
+    // ---- epilogue warps 0-3
+    float *wst = stg + warp * (16 * 32);
+    uint32_t local = 0;
+    for (int64_t tile = blockIdx.x; tile < ntiles_total; tile += gridDim.x, local++) {
+      int64_t line;
+      int wo0, nt;
+      ch_tile(c, tile, line, wo0, nt);
+      const uint32_t buf = local & 1u, use = local >> 1;
+      if (!mbar_wait(&acc_full[buf], use & 1u, kFaultDone)) break;
+      tc_fence_after();
+      ch_epilogue<BN>(c, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp, lane, line, wo0, nt,
+                      wst);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kChMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, (uint32_t)Cfg::kTmemCols);
   }
@@ -1276,6 +1650,132 @@ static void launch_conv_tma(const CUtensorMap &tx, const CUtensorMap &tx2, const
   DCB_LAUNCHED();
 }
 
+// fp16 channels-last activation as a TMA tensor map: 4-D (C, Wp, H, images), or with a
+// stride of 4 along W the 5-D view (C, 4, Wp / 4, H, images); boxes of 64 channels x 128
+// positions with the 128-byte swizzle of the UMMA operand
+static bool encode_half(CUtensorMap *map, const HalfAct &x, bool w4) {
+  if (!get_encoder() || !x.p || ((uintptr_t)x.p & 15) || x.C % 8 || x.Wp < x.W) return false;
+  if (w4 && x.Wp % 4) return false;
+  const uint64_t rowb = (uint64_t)x.C * 2;  // bytes per position
+  cuuint64_t dims[5], strides[4];
+  cuuint32_t box[5], es[5] = {1, 1, 1, 1, 1};
+  int rank;
+  if (!w4) {
+    rank = 4;
+    dims[0] = (cuuint64_t)x.C;
+    dims[1] = (cuuint64_t)x.Wp;
+    dims[2] = (cuuint64_t)x.H;
+    dims[3] = (cuuint64_t)x.images;
+    strides[0] = rowb;
+    strides[1] = rowb * x.Wp;
+    strides[2] = rowb * x.Wp * x.H;
+    box[0] = 64;
+    box[1] = kBM;
+    box[2] = 1;
+    box[3] = 1;
+  } else {
+    rank = 5;
+    dims[0] = (cuuint64_t)x.C;
+    dims[1] = 4;
+    dims[2] = (cuuint64_t)(x.Wp / 4);
+    dims[3] = (cuuint64_t)x.H;
+    dims[4] = (cuuint64_t)x.images;
+    strides[0] = rowb;
+    strides[1] = rowb * 4;
+    strides[2] = rowb * x.Wp;
+    strides[3] = rowb * x.Wp * x.H;
+    box[0] = 64;
+    box[1] = 1;
+    box[2] = kBM;
+    box[3] = 1;
+    box[4] = 1;
+  }
+  for (int i = 0; i < rank - 1; i++)
+    if (strides[i] % 16 || strides[i] >= (1ull << 40)) return false;
+  return g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank, const_cast<uint16_t *>(x.p), dims,
+                  strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+static void launch_conv_h(const CUtensorMap &ta, const CUtensorMap &tb, ConvH c, const Epi &e) {
+  using Cfg = ChCfg<BN>;
+  // two CTAs per SM when the accumulators fit (<= 256 TMEM columns each)
+  const bool two = Cfg::kTmemCols <= 256;
+  const size_t budget = two ? 111 * 1024 : 226 * 1024;
+  const size_t fixed = 1024 + (size_t)kChEpiWarps * 16 * 32 * 4 + 5 * 8 + 16;
+  int stages = (int)((budget - fixed) / (Cfg::kStage + 16));
+  if (stages > 8) stages = 8;
+  DCB_REQUIRE(stages >= 2, "conv: stages do not fit in shared memory");
+  c.stages = stages;
+  const size_t smem = fixed + (size_t)stages * (Cfg::kStage + 16);
+  static size_t attr = 0;
+  if (smem > attr) {
+    DCB_CUDA(cudaFuncSetAttribute(k_conv_h<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem));
+    attr = smem;
+  }
+  const int64_t tiles = c.lines * c.tpl * c.ntiles;
+  const int64_t slots = (two ? 2 : 1) * (int64_t)sm_count();
+  const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
+  k_conv_h<BN><<<grid, kChThreads, smem, stream()>>>(ta, tb, c, e);
+  DCB_LAUNCHED();
+}
+
+bool conv_half(const HalfAct &x, int KH, int KW, int SH, int SW, int PH, int PW, int DH, int DW,
+               int Ho, int Wo, const uint16_t *wt, int64_t N, int64_t ldt, int ncb, const Epi &e,
+               int bn_hint) {
+  if (g_opt_simt || !wt || ncb <= 0 || (SW != 1 && SW != 4) || Ho <= 0 || Wo <= 0 || N <= 0)
+    return false;
+  if ((int64_t)KH * KW * ncb * kBK != ldt || (ncb - 1) * 64 >= x.C) return false;
+  if (e.mode != EPI_CONV && e.mode != EPI_CONVTR) return false;
+  if (e.mode == EPI_CONVTR && e.act >= 2) return false;
+  const bool glu = e.mode == EPI_CONV && e.act >= 2;
+  int bn = bn_hint ? bn_hint : pick_bn((int64_t)x.images * Ho * Wo, N, 1);
+  if (glu && !bn_hint) return false;  // the GLU interleave fixes the N tile
+  CUtensorMap ta, tb;
+  if (!encode_half(&ta, x, SW == 4)) return false;
+  if (!encode_map(&tb, wt, (uint64_t)ldt, (uint64_t)N, 1, (uint64_t)ldt, 0, (uint32_t)bn))
+    return false;
+  ConvH c{};
+  c.KH = KH;
+  c.KW = KW;
+  c.SH = SH;
+  c.SW = SW;
+  c.PH = PH;
+  c.PW = PW;
+  c.DH = DH;
+  c.DW = DW;
+  c.Ho = Ho;
+  c.Wo = Wo;
+  c.ncb = ncb;
+  c.lines = x.images * Ho;
+  c.tpl = (Wo + kBM - 1) / kBM;
+  c.N = (int)N;
+  c.nkb = KH * KW * ncb;
+  c.ntiles = (int)((N + bn - 1) / bn);
+  Epi e2 = e;
+  if (glu) e2.glu_half = bn / 2;
+  {
+    const int64_t M = x.images * Ho * Wo;
+    const double n_alg = e.mode == EPI_CONVTR ? (double)e.O * e.stride : (glu ? 2.0 * e.O : e.O);
+    const int Kt = KH * KW * x.C;
+    const double out_b = (double)M * n_alg / (glu ? 2 : 1) *
+                         ((e.y ? 4.0 : 0.0) + (e.yh ? 2.0 + (e.hskip ? 4.0 : 0.0) : 0.0));
+    TraceScope ts(e.mode == EPI_CONVTR ? TR_CONVTR : TR_CONV, 2.0 * M * n_alg * Kt,
+                  (double)x.images * x.H * x.W * x.C * 2.0 + n_alg * Kt * 2.0 + out_b, M,
+                  (int64_t)n_alg, Kt);
+    switch (bn) {
+      case 32: launch_conv_h<32>(ta, tb, c, e2); break;
+      case 64: launch_conv_h<64>(ta, tb, c, e2); break;
+      case 128: launch_conv_h<128>(ta, tb, c, e2); break;
+      default: launch_conv_h<256>(ta, tb, c, e2); break;
+    }
+  }
+  return true;
+}
+
 // TMA im2col path of gemm_gather: true when it launched
 static bool conv_tma(const Gather &g, int64_t M, const uint16_t *wt, int64_t N, int64_t ldt,
                      int ncb, const Epi &e, int bn) {
@@ -1399,13 +1899,13 @@ void glu_interleave(const uint16_t *w, uint16_t *out, int O, int64_t kp, int bn)
 }
 
 // -------- transposed-conv phase matrix: W_tr [O][KH][KW][C] (rows o*KH*KW + k, stride kp)
-// -> B[(o, r)][(j', c)] = W[o][r + S (1 - j')][c], j' = 0 reads input q-1, j' = 1 input q.
+// -> B[(r, o)][(j', c)] = W[o][r + S (1 - j')][c], j' = 0 reads input q-1, j' = 1 input q.
 __global__ void k_convtr_phase(const uint16_t *__restrict__ w, uint16_t *__restrict__ out,
                                int O, int C, int Ktaps, int S, int64_t kp, int64_t ldo) {
   int64_t total = (int64_t)O * S * ldo;
   DCB_GRID_STRIDE(i, total) {
     int64_t row = i / ldo, col = i - row * ldo;
-    int o = (int)(row / S), r = (int)(row % S);
+    int r = (int)(row / O), o = (int)(row % O);  // rows (phase, channel), channels fastest
     uint16_t v = 0;
     if (col < 2 * C) {
       int jp = (int)(col / C), c = (int)(col % C);

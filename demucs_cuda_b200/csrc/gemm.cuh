@@ -26,7 +26,7 @@ struct Gather {
 enum EpiMode : int {
   EPI_GEMM = 0,    // C = alpha acc + beta C (dk_gemm_half); swapped -> transposed store
   EPI_CONV = 1,    // y[n][o][ho][wo] = act(acc + bias); GLU pairs interleaved columns
-  EPI_CONVTR = 2,  // stride-phase scatter: column (o, r) -> output t = S q + r - crop
+  EPI_CONVTR = 2,  // stride-phase scatter: column (r, o) -> output t = S q + r - crop
   EPI_ROWS_F32 = 3,  // out[m][n] = acc + bias (+ res[m][n] + gamma[n] * (...))
   EPI_ROWS_F16 = 4,  // out16[m][n] = fp16(act(acc + bias))
   EPI_HEADS = 5,     // fp16 head-split sections [B][H][T][hd] / [B][H][hd][Tp]
@@ -56,6 +56,18 @@ struct Epi {
   const float *gn_mean = nullptr, *gn_rstd = nullptr, *gn_w = nullptr, *gn_b = nullptr;
   // EPI_CONVTR
   int stride = 4, crop = 0, out_len = 0, axis_h = 1;
+  // fp16 channels-last copy of an EPI_CONV / EPI_CONVTR output (the A operand of the next
+  // conv): element (n, o, h, w) of the output at yh[((n * yhH + h) * yhW + w) * yhC + o];
+  // hskip (fp32, laid out like y) is added first (the decoders' skip connections).  y may
+  // be null when only the copy is needed.
+  uint16_t *yh = nullptr;
+  int yhH = 1, yhW = 1, yhC = 0;
+  const float *hskip = nullptr;
+  // frequency embedding added to the output (first frequency encoder, htdemucs.c:114-134):
+  // value += emb_alpha * emb[h * emb_ld + o]
+  const float *emb = nullptr;
+  float emb_alpha = 0.f;
+  int emb_ld = 0;
   // EPI_ROWS_*
   void *out = nullptr;
   int64_t ldo = 0, ldr = 0;
@@ -79,6 +91,20 @@ void gemm_rows(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch,
 void gemm_gather(const Gather &g, int64_t M, const uint16_t *w, int64_t N, int64_t ldw,
                  const Epi &e, int bn_hint = 0, const uint16_t *wt = nullptr,
                  int64_t ldt = 0, int ncb = 0);
+// fp16 channels-last activation [images][H][W][C] (W padded to Wp with zeros) feeding the
+// TMA implicit-GEMM conv
+struct HalfAct {
+  const uint16_t *p = nullptr;
+  int64_t images = 0;
+  int C = 0, H = 1, W = 0, Wp = 0;
+};
+// conv / transposed conv over a HalfAct: taps (KH, KW), stride SH along H and SW (1 or 4)
+// along W, padding PH/PW, dilation DH/DW; B = weights in the TMA K order (ldt, ncb).
+// Returns false (nothing launched) when the call is outside what the kernel covers.
+bool conv_half(const HalfAct &x, int KH, int KW, int SH, int SW, int PH, int PW, int DH, int DW,
+               int Ho, int Wo, const uint16_t *wt, int64_t N, int64_t ldt, int ncb, const Epi &e,
+               int bn_hint);
+
 // N tile used by gemm_gather for a given column count (the GLU interleave depends on it)
 int gather_bn(int64_t M, int64_t N, bool glu);
 

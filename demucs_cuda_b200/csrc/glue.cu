@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(256)
                  const float *__restrict__ gb, const float *__restrict__ scale,
                  const float *__restrict__ zmean, const float *__restrict__ zrstd, int B, int C,
                  int hid, int Fr, int64_t T, int64_t hsB, int64_t hsC, int64_t ysB,
-                 int64_t ysC) {
+                 int64_t ysC, uint16_t *__restrict__ yh, int64_t yh_pitch) {
   extern __shared__ float sm[];
   float *sw = sm;                    // [2C][HIDP]
   float *sbias = sw + 2 * C * HIDP;  // [2C]
@@ -384,6 +384,9 @@ __global__ void __launch_bounds__(256)
     for (int j = 0; j < HIDP; j++)
       hv[j] = j < hid ? __half2float(__float2half_rn(hp[(int64_t)j * hsC])) : 0.f;
     float *yp = y + b * ysB + f * T + t;
+    // fp16 channels-last copy of the updated row: yh[(row * yh_pitch + t) * C + c]
+    uint16_t *yhp = yh ? yh + ((int64_t)row * yh_pitch + t) * C : nullptr;
+    uint32_t hw[4];
     for (int c = 0; c < C; c++) {
       const float4 *wa = (const float4 *)(sw + c * HIDP);
       const float4 *wb = (const float4 *)(sw + (C + c) * HIDP);
@@ -404,7 +407,17 @@ __global__ void __launch_bounds__(256)
       g = (g + sbias[C + c] - mu) * rs * sgw[C + c] + sgb[C + c];
       const float v = a * __fdividef(1.0f, 1.0f + __expf(-g));
       float *yc = yp + (int64_t)c * ysC;
-      *yc = *yc + ssc[c] * v;
+      const float nv = *yc + ssc[c] * v;
+      *yc = nv;
+      if (yhp) {
+        // 8 channels per 16-byte store (C is a multiple of 8)
+        const uint32_t hb = f2h_bits(nv);
+        if (c & 1)
+          hw[(c >> 1) & 3] |= hb << 16;
+        else
+          hw[(c >> 1) & 3] = hb;
+        if ((c & 7) == 7) *(uint4 *)(yhp + c - 7) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      }
     }
   }
 }
@@ -465,6 +478,33 @@ __global__ void k_tokens_ln_pos(const float *__restrict__ x, float *__restrict__
   for (int i = 0; i < 32; i++) {
     const int c = i * 32 + lane;
     if (c < C) o[c] = ((v[i] - m) * rs * w[c] + bb[c]) + pp[c];
+  }
+}
+
+// fp32 [n][C][H][W] (strides sN, sC, sH, 1; optional addend laid out the same) ->
+// fp16 channels-last [n][H][Wp][C], round to nearest even: the A operand of the next conv
+// (the reference rounds the same fp32 values in dk_im2col_half).  One thread per
+// (position, 8 channels); C is a multiple of 8.
+__global__ void k_to_half_cl(const float *__restrict__ x, const float *__restrict__ add,
+                             uint16_t *__restrict__ y, int64_t images, int C, int H, int W,
+                             int Wp, int64_t sN, int64_t sC, int64_t sH) {
+  const int C8 = C / 8;
+  const int64_t total = images * H * (int64_t)W * C8;
+  DCB_GRID_STRIDE(i, total) {
+    const int64_t w = i % W, r = i / W;
+    const int c8 = (int)(r % C8);
+    const int64_t r2 = r / C8;
+    const int64_t h = r2 % H, n = r2 / H;
+    const int64_t src = n * sN + (int64_t)c8 * 8 * sC + h * sH + w;
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      v[k] = x[src + k * sC];
+      if (add) v[k] += add[src + k * sC];
+    }
+    uint4 *d = (uint4 *)(y + ((n * H + h) * Wp + w) * C + c8 * 8);
+    *d = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]),
+                    pack_h2(v[6], v[7]));
   }
 }
 
