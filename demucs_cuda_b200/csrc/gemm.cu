@@ -1734,6 +1734,8 @@ bool conv_half(const HalfAct &x, int KH, int KW, int SH, int SW, int PH, int PW,
   const bool glu = e.mode == EPI_CONV && e.act >= 2;
   int bn = bn_hint ? bn_hint : pick_bn((int64_t)x.images * Ho * Wo, N, 1);
   if (glu && !bn_hint) return false;  // the GLU interleave fixes the N tile
+  // at most 128 columns: two CTAs (8 epilogue warps) per SM drain the accumulators
+  if (bn > 128) bn = 128;
   CUtensorMap ta, tb;
   if (!encode_half(&ta, x, SW == 4)) return false;
   if (!encode_map(&tb, wt, (uint64_t)ldt, (uint64_t)N, 1, (uint64_t)ldt, 0, (uint32_t)bn))
