@@ -1017,33 +1017,41 @@ static __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap 
       : "memory");
 }
 
+// tile -> (line, first position, N tile), N tiles fastest (tile counts fit in 31 bits)
 static __device__ __forceinline__ void ch_tile(const ConvH &c, int64_t tile, int64_t &line,
                                                int &wo0, int &nt) {
-  nt = (int)(tile % c.ntiles);
-  const int64_t rest = tile / c.ntiles;
-  line = rest / c.tpl;
-  wo0 = (int)(rest - line * c.tpl) * kBM;
+  const int t = (int)tile;
+  const int rest = t / c.ntiles;
+  nt = t - rest * c.ntiles;
+  const int ln = rest / c.tpl;
+  line = ln;
+  wo0 = (rest - ln * c.tpl) * kBM;
 }
 
 // Epilogue of one line tile by 4 warps (warp w: rows 32w..32w+31, every column), 16
 // columns per step.  Values go (1) from registers to the fp16 channels-last copy, 16
 // consecutive channels of a position per thread, and (2) through the warp's [16][32]
 // transpose buffer to the fp32 NCHW output, 4 consecutive positions per 16-byte store.
+// Transposed-conv columns are (phase s, channel o), channels fastest; (s, o) of the
+// chunk start advance incrementally (no divisions in the loop).
 template <int BN>
 static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e, uint32_t tacc,
                                                    int warp, int lane, int64_t line, int wo0,
                                                    int nt, float *wst) {
   const uint32_t trow = tacc + ((uint32_t)(warp * 32) << 16);
-  const int64_t n = line / c.Ho;
-  const int ho = (int)(line - n * c.Ho);
-  const int64_t n1 = n / e.oN2, n2 = n - n1 * e.oN2;
-  const int64_t base = n1 * e.oN1 + n2 * e.oN2s;
+  const int ln = (int)line;
+  const int n = ln / c.Ho;
+  const int ho = ln - n * c.Ho;
+  const int n1 = n / e.oN2, n2 = n - n1 * e.oN2;
+  const int64_t base = (int64_t)n1 * e.oN1 + (int64_t)n2 * e.oN2s;
   const int r = warp * 32 + lane;
   const int row_lim = c.Wo - wo0;  // tile rows r < row_lim are outputs
   const bool rv = r < row_lim;
   const int q = wo0 + r;           // output position along W (conv, conv_tr along H) or q
   const bool convtr = e.mode == EPI_CONVTR;
   const bool glu = !convtr && e.act >= 2;
+  const bool gelu = e.act == 1;
+  const int O = e.O;
   float gmu = 0.f, grs = 0.f;
   if (glu && e.act == 3) {
     gmu = e.gn_mean[n];
@@ -1051,29 +1059,61 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
   }
   const int ncols = glu ? e.glu_half : BN;
   const int obase = glu ? nt * e.glu_half : nt * BN;
-  const int ncol_total = convtr ? e.O * e.stride : e.O;
+  const int ncol_total = convtr ? O * e.stride : O;
   const int li = lane & 15;
+  // transposed conv: phase and channel of the chunk's first column
+  int s0 = convtr ? obase / O : 0;
+  int o0 = convtr ? obase - s0 * O : obase;
+  const bool o16 = O % 16 == 0;  // every chunk then lies in one phase
+  const int rq = 4 * (lane & 7);
+  const int rl = warp * 32 + rq;  // first of this lane's 4 rows in the NCHW pass
   for (int c0 = 0; c0 < ncols; c0 += 16) {
     const int col0 = obase + c0;
     if (col0 >= ncol_total) break;
     float va[16];
     tmem_ld16(trow + c0, va);
+    // output coordinates of this lane's row for the chunk (conv: (ho, q))
+    int h = ho, w = q;
+    bool tok = true;
+    if (convtr) {
+      const int t = (e.axis_h ? ho : q) * e.stride + s0 - e.crop;
+      tok = t >= 0 && t < e.out_len;
+      if (e.axis_h) {
+        h = t;
+      } else {
+        h = 0;
+        w = t;
+      }
+    }
+    const bool cl_fast = (!convtr || o16) && o0 + 16 <= O;  // 16 channels of one position
+    // skip-connection values for the fp16 copy, loaded before the accumulator wait
+    float sk[16];
+    const bool want_h = e.yh && rv && tok && cl_fast;
+    if (want_h && e.hskip) {
+      const float *sp = e.hskip + base + (int64_t)o0 * e.oC + (int64_t)h * e.oH + w;
+#pragma unroll
+      for (int i = 0; i < 16; i++) sk[i] = sp[(int64_t)i * e.oC];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; i++) sk[i] = 0.f;
+    }
     // per-column constants: lane i < 16 loads column i's, shuffles hand them out
-    const int colx = col0 + li;
-    const int ox = convtr ? colx % e.O : colx;
-    const bool okc = convtr ? colx < ncol_total : colx < e.O;
+    const int oxl = o0 + li;  // channel of column li when the chunk lies in one phase
+    int ox = oxl;
+    if (convtr && !o16) ox = (col0 + li) % O;
+    const bool okc = convtr ? col0 + li < ncol_total : oxl < O;
     float val[16];
     if (glu) {
       float vb[16];
       tmem_ld16(trow + e.glu_half + c0, vb);
-      const float ba = okc && e.bias ? e.bias[colx] : 0.f;
-      const float bb = okc && e.bias ? e.bias[e.O + colx] : 0.f;
+      const float ba = okc && e.bias ? e.bias[oxl] : 0.f;
+      const float bb = okc && e.bias ? e.bias[O + oxl] : 0.f;
       float wa = 1.f, wb = 1.f, za = 0.f, zb = 0.f;
       if (e.act == 3 && okc) {
-        wa = e.gn_w[colx] * grs;
-        wb = e.gn_w[e.O + colx] * grs;
-        za = e.gn_b[colx];
-        zb = e.gn_b[e.O + colx];
+        wa = e.gn_w[oxl] * grs;
+        wb = e.gn_w[O + oxl] * grs;
+        za = e.gn_b[oxl];
+        zb = e.gn_b[O + oxl];
       }
       tmem_wait_ld();
 #pragma unroll
@@ -1092,58 +1132,49 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
 #pragma unroll
       for (int i = 0; i < 16; i++) {
         float v = va[i] + __shfl_sync(0xffffffffu, bx, i);
-        if (e.act == 1) v = gelu_f(v);
+        if (gelu) v = gelu_f(v);
         val[i] = v;
       }
     }
     if (e.emb) {
-      const float ex = okc ? e.emb_alpha * e.emb[(int64_t)ho * e.emb_ld + colx] : 0.f;
+      const float ex = okc ? e.emb_alpha * e.emb[(int64_t)ho * e.emb_ld + oxl] : 0.f;
 #pragma unroll
       for (int i = 0; i < 16; i++) val[i] += __shfl_sync(0xffffffffu, ex, i);
     }
-    // transposed conv: the chunk's phase s (uniform when O is a multiple of 16)
-    const int s0 = convtr ? col0 / e.O : 0;
-    const bool s_uniform = !convtr || (col0 + 15) / e.O == s0;
     // ---- (1) fp16 channels-last copy
-    if (e.yh && rv) {
-      int h = ho, w = q;
-      bool ok = true;
-      if (convtr) {
-        const int t = (e.axis_h ? ho : q) * e.stride + s0 - e.crop;
-        ok = t >= 0 && t < e.out_len;
-        if (e.axis_h) h = t; else { h = 0; w = t; }
-      }
-      const int o0 = convtr ? col0 - s0 * e.O : col0;
-      if (ok && s_uniform) {
-        uint16_t *dst = e.yh + (((int64_t)n * e.yhH + h) * e.yhW + w) * e.yhC + o0;
-        const int64_t soff = base + (int64_t)o0 * e.oC + (int64_t)h * e.oH + w;
-        float hv[16];
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-          hv[i] = val[i];
-          if (e.hskip && o0 + i < e.O) hv[i] += e.hskip[soff + (int64_t)i * e.oC];
+    if (want_h) {
+      uint16_t *dst = e.yh + (((int64_t)n * e.yhH + h) * e.yhW + w) * e.yhC + o0;
+      uint4 *d4 = (uint4 *)dst;
+      d4[0] = make_uint4(pack_h2(val[0] + sk[0], val[1] + sk[1]),
+                         pack_h2(val[2] + sk[2], val[3] + sk[3]),
+                         pack_h2(val[4] + sk[4], val[5] + sk[5]),
+                         pack_h2(val[6] + sk[6], val[7] + sk[7]));
+      d4[1] = make_uint4(pack_h2(val[8] + sk[8], val[9] + sk[9]),
+                         pack_h2(val[10] + sk[10], val[11] + sk[11]),
+                         pack_h2(val[12] + sk[12], val[13] + sk[13]),
+                         pack_h2(val[14] + sk[14], val[15] + sk[15]));
+    } else if (e.yh && rv) {
+      // partial chunk (channel tail, or a transposed-conv chunk across two phases)
+      for (int i = 0; i < 16; i++) {
+        const int col = col0 + i;
+        if (col >= ncol_total) break;
+        int ss = s0, o = o0 + i;
+        if (convtr) {
+          ss = col / O;
+          o = col - ss * O;
+        } else if (o >= O) {
+          break;
         }
-        if (o0 + 16 <= e.O && (((uintptr_t)dst) & 15) == 0) {
-          uint4 *d4 = (uint4 *)dst;
-          d4[0] = make_uint4(pack_h2(hv[0], hv[1]), pack_h2(hv[2], hv[3]), pack_h2(hv[4], hv[5]),
-                             pack_h2(hv[6], hv[7]));
-          d4[1] = make_uint4(pack_h2(hv[8], hv[9]), pack_h2(hv[10], hv[11]),
-                             pack_h2(hv[12], hv[13]), pack_h2(hv[14], hv[15]));
-        } else {
-          for (int i = 0; i < 16 && o0 + i < e.O; i++) dst[i] = f2h_bits(hv[i]);
-        }
-      } else if (!s_uniform) {
-        for (int i = 0; i < 16; i++) {
-          const int col = col0 + i;
-          if (col >= ncol_total) break;
-          const int s = col / e.O, o = col - s * e.O;
-          const int t = (e.axis_h ? ho : q) * e.stride + s - e.crop;
+        int hh = ho, ww = q;
+        if (convtr) {
+          const int t = (e.axis_h ? ho : q) * e.stride + ss - e.crop;
           if (t < 0 || t >= e.out_len) continue;
-          const int hh = e.axis_h ? t : 0, ww = e.axis_h ? q : t;
-          float v = val[i];
-          if (e.hskip) v += e.hskip[base + (int64_t)o * e.oC + (int64_t)hh * e.oH + ww];
-          e.yh[(((int64_t)n * e.yhH + hh) * e.yhW + ww) * e.yhC + o] = f2h_bits(v);
+          hh = e.axis_h ? t : 0;
+          ww = e.axis_h ? q : t;
         }
+        float v = val[i];
+        if (e.hskip) v += e.hskip[base + (int64_t)o * e.oC + (int64_t)hh * e.oH + ww];
+        e.yh[(((int64_t)n * e.yhH + hh) * e.yhW + ww) * e.yhC + o] = f2h_bits(v);
       }
     }
     // ---- (2) fp32 NCHW output through the transpose buffer
@@ -1151,21 +1182,31 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
 #pragma unroll
       for (int i = 0; i < 16; i++) wst[i * 32 + lane] = val[i];
       __syncwarp();
-      const int rq = 4 * (lane & 7);
-      const int rl = warp * 32 + rq;  // first of this lane's 4 rows
 #pragma unroll
       for (int p = 0; p < 4; p++) {
         const int cc = (lane >> 3) + 4 * p;
         const int col = col0 + cc;
-        if (col >= ncol_total || (!convtr && col >= e.O)) continue;
+        if (col >= ncol_total) continue;
+        // (phase, channel) of the column without a division when O >= 16
+        int ss = s0, o = o0 + cc;
+        if (convtr) {
+          if (O >= 16) {
+            if (o >= O) {
+              o -= O;
+              ss++;
+            }
+          } else {
+            ss = col / O;
+            o = col - ss * O;
+          }
+        }
         const float4 v4 = *(const float4 *)(wst + cc * 32 + rq);
         const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
         if (convtr && !e.axis_h) {
           // phase scatter along W: output t = S q + s - crop
-          const int s = col / e.O, o = col - s * e.O;
 #pragma unroll
           for (int i = 0; i < 4; i++) {
-            const int t = (wo0 + rl + i) * e.stride + s - e.crop;
+            const int t = (wo0 + rl + i) * e.stride + ss - e.crop;
             if (rl + i < row_lim && t >= 0 && t < e.out_len)
               e.y[base + (int64_t)o * e.oC + (int64_t)ho * e.oH + t] = vv[i];
           }
@@ -1173,8 +1214,7 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
         }
         int64_t off;
         if (convtr) {
-          const int s = col / e.O, o = col - s * e.O;
-          const int t = ho * e.stride + s - e.crop;
+          const int t = ho * e.stride + ss - e.crop;
           if (t < 0 || t >= e.out_len) continue;
           off = base + (int64_t)o * e.oC + (int64_t)t * e.oH + wo0 + rl;
         } else {
@@ -1201,6 +1241,16 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
         }
       }
       __syncwarp();
+    }
+    // next chunk's (phase, channel)
+    if (convtr) {
+      o0 += 16;
+      while (o0 >= O) {
+        o0 -= O;
+        s0++;
+      }
+    } else {
+      o0 += 16;
     }
   }
 }
