@@ -1503,9 +1503,20 @@ static bool vec_ok(const Epi &e, int64_t N) {
   }
 }
 
+// N tile: the widest of 256 / 128 / 64 / 32 whose padding (tiles * bn - N) is smallest
+// (a narrower tile only when it wastes fewer columns), then narrowed while the grid has
+// fewer tiles than SMs
 static int pick_bn(int64_t M, int64_t N, int64_t batch) {
   int bn = 32;
   while (bn < 256 && bn < N) bn *= 2;
+  int64_t best = ((N + bn - 1) / bn) * bn - N;
+  for (int c = bn / 2; c >= 64; c /= 2) {
+    const int64_t waste = ((N + c - 1) / c) * c - N;
+    if (waste < best) {
+      best = waste;
+      bn = c;
+    }
+  }
   const int64_t mt = (M + kBM - 1) / kBM;
   while (bn > 32 && mt * ((N + bn - 1) / bn) * batch < 148) bn /= 2;
   return bn;

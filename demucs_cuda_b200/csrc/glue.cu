@@ -293,8 +293,15 @@ __global__ void __launch_bounds__(256)
     }
     const float *hj = hs + j * len;
     const float *hk = k >= 0 ? hs + k * len : nullptr;
-    double a = 0.0;
-    for (int t = lane; t < len; t += 32) a += (double)(hk ? hj[t] * hk[t] : hj[t]);
+    // products of fp16 values are exact in fp32; a lane's <= 32 terms are summed in fp32,
+    // lanes and chunks in fp64
+    float a32 = 0.f;
+    if (hk) {
+      for (int t = lane; t < len; t += 32) a32 = fmaf(hj[t], hk[t], a32);
+    } else {
+      for (int t = lane; t < len; t += 32) a32 += hj[t];
+    }
+    double a = (double)a32;
     for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
     if (lane == 0) atomicAdd(&acc[row * (npair + hid) + p], a);
   }
@@ -386,38 +393,39 @@ __global__ void __launch_bounds__(256)
     float *yp = y + b * ysB + f * T + t;
     // fp16 channels-last copy of the updated row: yh[(row * yh_pitch + t) * C + c]
     uint16_t *yhp = yh ? yh + ((int64_t)row * yh_pitch + t) * C : nullptr;
-    uint32_t hw[4];
-    for (int c = 0; c < C; c++) {
-      const float4 *wa = (const float4 *)(sw + c * HIDP);
-      const float4 *wb = (const float4 *)(sw + (C + c) * HIDP);
-      float a = 0.f, g = 0.f;
+    // 8 channels per step: their residual loads are issued together (C % 8 == 0)
+    for (int c0 = 0; c0 < C; c0 += 8) {
+      float yv[8];
 #pragma unroll
-      for (int j = 0; j < HIDP / 4; j++) {
-        const float4 x = wa[j], z = wb[j];
-        a = fmaf(x.x, hv[4 * j], a);
-        a = fmaf(x.y, hv[4 * j + 1], a);
-        a = fmaf(x.z, hv[4 * j + 2], a);
-        a = fmaf(x.w, hv[4 * j + 3], a);
-        g = fmaf(z.x, hv[4 * j], g);
-        g = fmaf(z.y, hv[4 * j + 1], g);
-        g = fmaf(z.z, hv[4 * j + 2], g);
-        g = fmaf(z.w, hv[4 * j + 3], g);
+      for (int k = 0; k < 8; k++) yv[k] = yp[(int64_t)(c0 + k) * ysC];
+      float nv[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int c = c0 + k;
+        const float4 *wa = (const float4 *)(sw + c * HIDP);
+        const float4 *wb = (const float4 *)(sw + (C + c) * HIDP);
+        float a = 0.f, g = 0.f;
+#pragma unroll
+        for (int j = 0; j < HIDP / 4; j++) {
+          const float4 x = wa[j], z = wb[j];
+          a = fmaf(x.x, hv[4 * j], a);
+          a = fmaf(x.y, hv[4 * j + 1], a);
+          a = fmaf(x.z, hv[4 * j + 2], a);
+          a = fmaf(x.w, hv[4 * j + 3], a);
+          g = fmaf(z.x, hv[4 * j], g);
+          g = fmaf(z.y, hv[4 * j + 1], g);
+          g = fmaf(z.z, hv[4 * j + 2], g);
+          g = fmaf(z.w, hv[4 * j + 3], g);
+        }
+        a = (a + sbias[c] - mu) * rs * sgw[c] + sgb[c];
+        g = (g + sbias[C + c] - mu) * rs * sgw[C + c] + sgb[C + c];
+        nv[k] = yv[k] + ssc[c] * (a * __fdividef(1.0f, 1.0f + __expf(-g)));
       }
-      a = (a + sbias[c] - mu) * rs * sgw[c] + sgb[c];
-      g = (g + sbias[C + c] - mu) * rs * sgw[C + c] + sgb[C + c];
-      const float v = a * __fdividef(1.0f, 1.0f + __expf(-g));
-      float *yc = yp + (int64_t)c * ysC;
-      const float nv = *yc + ssc[c] * v;
-      *yc = nv;
-      if (yhp) {
-        // 8 channels per 16-byte store (C is a multiple of 8)
-        const uint32_t hb = f2h_bits(nv);
-        if (c & 1)
-          hw[(c >> 1) & 3] |= hb << 16;
-        else
-          hw[(c >> 1) & 3] = hb;
-        if ((c & 7) == 7) *(uint4 *)(yhp + c - 7) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-      }
+#pragma unroll
+      for (int k = 0; k < 8; k++) yp[(int64_t)(c0 + k) * ysC] = nv[k];
+      if (yhp)
+        *(uint4 *)(yhp + c0) = make_uint4(pack_h2(nv[0], nv[1]), pack_h2(nv[2], nv[3]),
+                                          pack_h2(nv[4], nv[5]), pack_h2(nv[6], nv[7]));
     }
   }
 }
