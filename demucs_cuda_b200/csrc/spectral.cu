@@ -383,18 +383,28 @@ __global__ void __launch_bounds__(kFftThreads)
   if (f_beg < 0) f_beg = 0;
   int f_end = j0 + kOlaHops - 1;
   if (f_end > NF - 1) f_end = NF - 1;
-  for (int f = f_beg; f <= f_end; f++) {
-    const int fi = f - 2;
-    if (fi < 0 || fi >= N) continue;
-    const float2 *zr = z + ((int64_t)r * N + fi) * F;
+  // two frames per complex transform: both inverse transforms are real, so with
+  // Y = X_f + i X_{f+1} (each X Hermitian-extended to 4096 bins) the real part of IFFT(Y)
+  // is frame f and the imaginary part frame f+1.  IFFT(Y) = conj(FFT(conj(Y))) / n.
+  for (int f = f_beg; f <= f_end; f += 2) {
+    const int fa = f - 2, fb = f - 1;  // spectrum frames of output frames f and f + 1
+    const bool va = fa >= 0 && fa < N, vb = f + 1 <= f_end && fb >= 0 && fb < N;
+    if (!va && !vb) continue;
+    const float2 *za = z + ((int64_t)r * N + fa) * F;
+    const float2 *zb = z + ((int64_t)r * N + fb) * F;
     __syncthreads();
 #pragma unroll
     for (int q = 0; q < 16; q++) {
       const int k = threadIdx.x + 256 * q;
       const int kk = k <= n / 2 ? k : n - k;
-      float2 v = kk < F ? zr[kk] : make_float2(0.f, 0.f);
-      if (k > n / 2) v.y = -v.y;
-      buf[fpad(k)] = make_float2(v.x, -v.y);
+      float2 a = va && kk < F ? za[kk] : make_float2(0.f, 0.f);
+      float2 b = vb && kk < F ? zb[kk] : make_float2(0.f, 0.f);
+      if (k > n / 2) {
+        a.y = -a.y;
+        b.y = -b.y;
+      }
+      // conj(Y) = conj(a + i b) = (a.x - b.y) - i (a.y + b.x)
+      buf[fpad(k)] = make_float2(a.x - b.y, -(a.y + b.x));
     }
     __syncthreads();
     fft4096(buf, tw);
@@ -402,7 +412,11 @@ __global__ void __launch_bounds__(kFftThreads)
 #pragma unroll
     for (int q = 0; q < Q; q++) {
       const int64_t i = off + threadIdx.x + 256 * q;
-      if (i >= 0 && i < n) acc[q] += buf[fpad((int)i)].x * inv_n * window[i];
+      float sum = 0.f;
+      if (va && i >= 0 && i < n) sum += buf[fpad((int)i)].x * inv_n * window[i];
+      const int64_t i2 = i - hop;  // frame f + 1 starts one hop later
+      if (vb && i2 >= 0 && i2 < n) sum += -buf[fpad((int)i2)].y * inv_n * window[i2];
+      acc[q] += sum;
     }
   }
   const int64_t out_len = (int64_t)hop * (NF - 1) + n;
