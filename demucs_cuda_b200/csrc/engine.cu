@@ -305,8 +305,8 @@ struct ConvW {             // B operand of a conv GEMM plus its epilogue constan
   int O = 0, C = 0, KH = 1, KW = 1, K = 0;
   float *bias = nullptr;
   int glu_bn = 0;          // N tile of the GLU interleave (0 = plain)
-  // the same rows in the TMA im2col kernel's K order (tap-major, channels zero-padded to
-  // ncb blocks of 64 per tap), for convs with at least 32 input channels
+  // the same rows in the TMA conv kernels' K order (kh, channel block, kw, channel), the
+  // channels zero-padded to ncb blocks of 64
   uint16_t *wt = nullptr;
   int64_t ldt = 0;
   int ncb = 0;
@@ -458,7 +458,6 @@ static void stage_f32(Staging &st, const std::vector<float> &v, float **slot) {
 // (kh, channel block, kw, c) with channels zero-padded to ncb = ceil(C / 64) blocks
 static void stage_tma_order(Staging &st, ConvW &cw, const std::vector<uint16_t> &packed,
                             int rows, int64_t kp, int KH, int KW, int C) {
-  if (C < 32) return;
   const int ncb = (C + 63) / 64;
   const int64_t ldt = (int64_t)KH * KW * ncb * 64;
   std::vector<uint16_t> t((size_t)rows * ldt, 0);

@@ -204,14 +204,17 @@ static Half16 half_alloc(int64_t images, int C, int H, int W, bool pad4) {
   return h;
 }
 
-// fp16 companion of an fp32 NCHW tensor [images][C][H][W] (+ addend of the same layout)
-static Half16 to_half(const float *x, const float *add, int64_t images, int C, int H, int W,
-                      bool pad4) {
+// fp16 companion of an fp32 NCHW tensor [images][Cs][H][W] (+ addend of the same layout)
+// with C >= Cs channels (the extra ones zero; C = Cs when Cs is a multiple of 8)
+static Half16 to_half(const float *x, const float *add, int64_t images, int Cs, int H, int W,
+                      bool pad4, int C = 0) {
+  if (C == 0) C = Cs;
   Half16 h = half_alloc(images, C, H, W, pad4);
   if (!h.p) return h;
   const int64_t n = images * H * (int64_t)W * (C / 8);
   k_to_half_cl<<<grid_for(n, 256), 256, 0, stream()>>>(x, add, h.p, images, C, H, W, h.Wp,
-                                                       (int64_t)C * H * W, (int64_t)H * W, W);
+                                                       (int64_t)Cs * H * W, (int64_t)H * W, W,
+                                                       Cs);
   DCB_LAUNCHED();
   return h;
 }
@@ -266,7 +269,7 @@ static void conv_any(const ConvW &cw, const float *x, const Half16 *xh, const Im
     const int64_t n = (int64_t)yh->images * yh->H * yh->W * (yh->C / 8);
     k_to_half_cl<<<grid_for(n, 256), 256, 0, stream()>>>(
         y, nullptr, yh->p, yh->images, yh->C, yh->H, yh->W, yh->Wp, out.sN1,
-        rows_view ? (int64_t)yh->H * yh->W : out.sC, yh->W);
+        rows_view ? (int64_t)yh->H * yh->W : out.sC, yh->W, yh->C);
     DCB_LAUNCHED();
   }
 }
@@ -364,7 +367,7 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
         const int64_t n = rows * (int64_t)T * (C / 8);
         k_to_half_cl<<<grid_for(n, 256), 256, 0, stream()>>>(y, nullptr, yh->p, B, C, Fr, T,
                                                              yh->Wp, (int64_t)C * Fr * T,
-                                                             (int64_t)Fr * T, T);
+                                                             (int64_t)Fr * T, T, C);
         DCB_LAUNCHED();
       }
     }
@@ -767,12 +770,14 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
   char name[32];
   // fp16 channels-last companions of the encoder inputs (none for the first encoders,
   // whose few input channels take the gather kernel)
-  Half16 xh_t, xh_f;
+  // (the first ones: the normalised inputs with their few channels padded to 8)
+  Half16 xh_t = to_half(xt, nullptr, B, C, 1, L, true, (C + 7) / 8 * 8);
+  Half16 xh_f = to_half(x, nullptr, B, 2 * C, nb, le, false, (2 * C + 7) / 8 * 8);
   for (int i = 0; i < depth; i++) {
     t_len.push_back(Lt);
     int Lo;
     Half16 zt;
-    float *xt2 = enc_time(m, i, xt, i ? &xh_t : nullptr, B, Lt, &Lo, &zt);
+    float *xt2 = enc_time(m, i, xt, &xh_t, B, Lt, &Lo, &zt);
     if (i == 0) dfree(xt);  // the normalised input; encoder outputs live on as skips
     dfree(xh_t.p);
     xh_t = zt;
@@ -784,7 +789,7 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
     fr_len.push_back(H);
     int Ho;
     Half16 zf;
-    float *x2 = enc_freq(m, i, x, i ? &xh_f : nullptr, B, H, W, &Ho, &zf);
+    float *x2 = enc_freq(m, i, x, &xh_f, B, H, W, &Ho, &zf);
     if (i == 0) dfree(x);
     dfree(xh_f.p);
     xh_f = zf;
@@ -1173,9 +1178,9 @@ int dcb_stage_encoder(DcbModel *m, int branch, int idx, const float *x, int B, i
     out_shape[3] = W;
     if (!y) return 0;
     int ho;
-    Half16 xh = idx > 0 ? to_half(x, nullptr, B, C, H, W, false) : Half16{};
+    Half16 xh = to_half(x, nullptr, B, C, H, W, false, (C + 7) / 8 * 8);
     Half16 zh;
-    float *z = enc_freq(m, idx, x, idx > 0 ? &xh : nullptr, B, H, W, &ho, &zh);
+    float *z = enc_freq(m, idx, x, &xh, B, H, W, &ho, &zh);
     DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * E.Cout * Ho * W * 4, cudaMemcpyDeviceToDevice,
                              stream()));
     dfree(z);
@@ -1192,9 +1197,9 @@ int dcb_stage_encoder(DcbModel *m, int branch, int idx, const float *x, int B, i
     out_shape[3] = 0;
     if (!y) return 0;
     int lo;
-    Half16 xh = idx > 0 ? to_half(x, nullptr, B, C, 1, L, true) : Half16{};
+    Half16 xh = to_half(x, nullptr, B, C, 1, L, true, (C + 7) / 8 * 8);
     Half16 zh;
-    float *z = enc_time(m, idx, x, idx > 0 ? &xh : nullptr, B, L, &lo, &zh);
+    float *z = enc_time(m, idx, x, &xh, B, L, &lo, &zh);
     DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * E.Cout * Lo * 4, cudaMemcpyDeviceToDevice,
                              stream()));
     dfree(z);

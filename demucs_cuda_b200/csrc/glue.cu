@@ -489,13 +489,14 @@ __global__ void k_tokens_ln_pos(const float *__restrict__ x, float *__restrict__
   }
 }
 
-// fp32 [n][C][H][W] (strides sN, sC, sH, 1; optional addend laid out the same) ->
+// fp32 [n][Cs][H][W] (strides sN, sC, sH, 1; optional addend laid out the same) ->
 // fp16 channels-last [n][H][Wp][C], round to nearest even: the A operand of the next conv
-// (the reference rounds the same fp32 values in dk_im2col_half).  One thread per
-// (position, 8 channels); C is a multiple of 8.
+// (the reference rounds the same fp32 values in dk_im2col_half).  Channels Cs..C-1 are
+// zero (C, a multiple of 8, pads inputs with few channels).  One thread per (position,
+// 8 channels).
 __global__ void k_to_half_cl(const float *__restrict__ x, const float *__restrict__ add,
                              uint16_t *__restrict__ y, int64_t images, int C, int H, int W,
-                             int Wp, int64_t sN, int64_t sC, int64_t sH) {
+                             int Wp, int64_t sN, int64_t sC, int64_t sH, int Cs) {
   const int C8 = C / 8;
   const int64_t total = images * H * (int64_t)W * C8;
   DCB_GRID_STRIDE(i, total) {
@@ -507,8 +508,11 @@ __global__ void k_to_half_cl(const float *__restrict__ x, const float *__restric
     float v[8];
 #pragma unroll
     for (int k = 0; k < 8; k++) {
-      v[k] = x[src + k * sC];
-      if (add) v[k] += add[src + k * sC];
+      v[k] = 0.f;
+      if (c8 * 8 + k < Cs) {
+        v[k] = x[src + k * sC];
+        if (add) v[k] += add[src + k * sC];
+      }
     }
     uint4 *d = (uint4 *)(y + ((n * H + h) * Wp + w) * C + c8 * 8);
     *d = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]),
