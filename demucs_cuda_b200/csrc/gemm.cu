@@ -996,7 +996,7 @@ struct ConvH {
   int N, nkb, ntiles, stages;
 };
 
-constexpr int kChEpiWarps = 4;
+constexpr int kChEpiWarps = 8;  // warp & 3: TMEM lane quarter, warp >> 2: column half
 constexpr int kChTmaWarp = kChEpiWarps, kChMmaWarp = kChEpiWarps + 1;
 constexpr int kChThreads = 32 * (kChEpiWarps + 2);
 
@@ -1038,13 +1038,14 @@ template <int BN>
 static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e, uint32_t tacc,
                                                    int warp, int lane, int64_t line, int wo0,
                                                    int nt, float *wst) {
-  const uint32_t trow = tacc + ((uint32_t)(warp * 32) << 16);
+  const int quarter = warp & 3, half = warp >> 2;
+  const uint32_t trow = tacc + ((uint32_t)(quarter * 32) << 16);
   const int ln = (int)line;
   const int n = ln / c.Ho;
   const int ho = ln - n * c.Ho;
   const int n1 = n / e.oN2, n2 = n - n1 * e.oN2;
   const int64_t base = (int64_t)n1 * e.oN1 + (int64_t)n2 * e.oN2s;
-  const int r = warp * 32 + lane;
+  const int r = quarter * 32 + lane;
   const int row_lim = c.Wo - wo0;  // tile rows r < row_lim are outputs
   const bool rv = r < row_lim;
   const int q = wo0 + r;           // output position along W (conv, conv_tr along H) or q
@@ -1058,7 +1059,10 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
     grs = e.gn_rstd[n];
   }
   const int ncols = glu ? e.glu_half : BN;
-  const int obase = glu ? nt * e.glu_half : nt * BN;
+  // the two warps of a lane quarter take one half of the columns each (16-column chunks)
+  const int per = ncols >= 32 ? ncols / 2 : (half == 0 ? ncols : 0);
+  const int cbeg = ncols >= 32 ? half * per : 0;
+  const int obase = (glu ? nt * e.glu_half : nt * BN) + cbeg;
   const int ncol_total = convtr ? O * e.stride : O;
   const int li = lane & 15;
   // transposed conv: phase and channel of the chunk's first column
@@ -1066,12 +1070,12 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
   int o0 = convtr ? obase - s0 * O : obase;
   const bool o16 = O % 16 == 0;  // every chunk then lies in one phase
   const int rq = 4 * (lane & 7);
-  const int rl = warp * 32 + rq;  // first of this lane's 4 rows in the NCHW pass
-  for (int c0 = 0; c0 < ncols; c0 += 16) {
+  const int rl = quarter * 32 + rq;  // first of this lane's 4 rows in the NCHW pass
+  for (int c0 = 0; c0 < per; c0 += 16) {
     const int col0 = obase + c0;
     if (col0 >= ncol_total) break;
     float va[16];
-    tmem_ld16(trow + c0, va);
+    tmem_ld16(trow + cbeg + c0, va);
     // output coordinates of this lane's row for the chunk (conv: (ho, q))
     int h = ho, w = q;
     bool tok = true;
@@ -1105,7 +1109,7 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
     float val[16];
     if (glu) {
       float vb[16];
-      tmem_ld16(trow + e.glu_half + c0, vb);
+      tmem_ld16(trow + e.glu_half + cbeg + c0, vb);
       const float ba = okc && e.bias ? e.bias[oxl] : 0.f;
       const float bb = okc && e.bias ? e.bias[O + oxl] : 0.f;
       float wa = 1.f, wb = 1.f, za = 0.f, zb = 0.f;
@@ -1177,70 +1181,75 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
         e.yh[(((int64_t)n * e.yhH + hh) * e.yhW + ww) * e.yhC + o] = f2h_bits(v);
       }
     }
-    // ---- (2) fp32 NCHW output through the transpose buffer
+    // ---- (2) fp32 NCHW output through the transpose buffer, 8 columns at a time
     if (e.y) {
 #pragma unroll
-      for (int i = 0; i < 16; i++) wst[i * 32 + lane] = val[i];
-      __syncwarp();
+      for (int hh = 0; hh < 2; hh++) {
 #pragma unroll
-      for (int p = 0; p < 4; p++) {
-        const int cc = (lane >> 3) + 4 * p;
-        const int col = col0 + cc;
-        if (col >= ncol_total) continue;
-        // (phase, channel) of the column without a division when O >= 16
-        int ss = s0, o = o0 + cc;
-        if (convtr) {
-          if (O >= 16) {
-            if (o >= O) {
-              o -= O;
-              ss++;
+        for (int i = 0; i < 8; i++) wst[i * 32 + lane] = val[hh * 8 + i];
+        __syncwarp();
+#pragma unroll
+        for (int p = 0; p < 2; p++) {
+          const int cl = (lane >> 3) + 4 * p;
+          const int cc = hh * 8 + cl;
+          const int col = col0 + cc;
+          if (col >= ncol_total) continue;
+          // (phase, channel) of the column without a division when O >= 16
+          int ss = s0, o = o0 + cc;
+          if (convtr) {
+            if (O >= 16) {
+              if (o >= O) {
+                o -= O;
+                ss++;
+              }
+            } else {
+              ss = col / O;
+              o = col - ss * O;
             }
+          }
+          const float4 v4 = *(const float4 *)(wst + cl * 32 + rq);
+          const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+          if (convtr && !e.axis_h) {
+            // phase scatter along W: output t = S q + s - crop
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              const int t = (wo0 + rl + i) * e.stride + ss - e.crop;
+              if (rl + i < row_lim && t >= 0 && t < e.out_len)
+                e.y[base + (int64_t)o * e.oC + (int64_t)ho * e.oH + t] = vv[i];
+            }
+            continue;
+          }
+          int64_t off;
+          if (convtr) {
+            const int t = ho * e.stride + ss - e.crop;
+            if (t < 0 || t >= e.out_len) continue;
+            off = base + (int64_t)o * e.oC + (int64_t)t * e.oH + wo0 + rl;
           } else {
-            ss = col / O;
-            o = col - ss * O;
+            off = base + (int64_t)col * e.oC + (int64_t)ho * e.oH + wo0 + rl;
           }
-        }
-        const float4 v4 = *(const float4 *)(wst + cc * 32 + rq);
-        const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
-        if (convtr && !e.axis_h) {
-          // phase scatter along W: output t = S q + s - crop
+          const uintptr_t al =
+              (uintptr_t)(e.y + off) | (e.res ? (uintptr_t)(e.res + off) : 0);
+          if (rl + 4 <= row_lim && (al & 15) == 0) {
+            float4 o4 = make_float4(vv[0], vv[1], vv[2], vv[3]);
+            if (e.res) {
+              const float4 rr = *(const float4 *)(e.res + off);
+              const float sc = e.scale[col];
+              o4 = make_float4(rr.x + sc * vv[0], rr.y + sc * vv[1], rr.z + sc * vv[2],
+                               rr.w + sc * vv[3]);
+            }
+            *(float4 *)(e.y + off) = o4;
+          } else {
 #pragma unroll
-          for (int i = 0; i < 4; i++) {
-            const int t = (wo0 + rl + i) * e.stride + ss - e.crop;
-            if (rl + i < row_lim && t >= 0 && t < e.out_len)
-              e.y[base + (int64_t)o * e.oC + (int64_t)ho * e.oH + t] = vv[i];
-          }
-          continue;
-        }
-        int64_t off;
-        if (convtr) {
-          const int t = ho * e.stride + ss - e.crop;
-          if (t < 0 || t >= e.out_len) continue;
-          off = base + (int64_t)o * e.oC + (int64_t)t * e.oH + wo0 + rl;
-        } else {
-          off = base + (int64_t)col * e.oC + (int64_t)ho * e.oH + wo0 + rl;
-        }
-        const uintptr_t al = (uintptr_t)(e.y + off) | (e.res ? (uintptr_t)(e.res + off) : 0);
-        if (rl + 4 <= row_lim && (al & 15) == 0) {
-          float4 o4 = make_float4(vv[0], vv[1], vv[2], vv[3]);
-          if (e.res) {
-            const float4 rr = *(const float4 *)(e.res + off);
-            const float sc = e.scale[col];
-            o4 = make_float4(rr.x + sc * vv[0], rr.y + sc * vv[1], rr.z + sc * vv[2],
-                             rr.w + sc * vv[3]);
-          }
-          *(float4 *)(e.y + off) = o4;
-        } else {
-#pragma unroll
-          for (int i = 0; i < 4; i++) {
-            if (rl + i >= row_lim) continue;
-            float v = vv[i];
-            if (e.res) v = e.res[off + i] + e.scale[col] * v;
-            e.y[off + i] = v;
+            for (int i = 0; i < 4; i++) {
+              if (rl + i >= row_lim) continue;
+              float v = vv[i];
+              if (e.res) v = e.res[off + i] + e.scale[col] * v;
+              e.y[off + i] = v;
+            }
           }
         }
+        __syncwarp();
       }
-      __syncwarp();
     }
     // next chunk's (phase, channel)
     if (convtr) {
@@ -1256,15 +1265,15 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
 }
 
 template <int BN>
-__global__ void __launch_bounds__(kChThreads, 1)
+__global__ void __launch_bounds__(kChThreads, 2)
     k_conv_h(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
              const ConvH c, const Epi e) {
   using Cfg = ChCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int stages = c.stages;
-  float *stg = (float *)(smem + (size_t)stages * Cfg::kStage);  // 4 warps x [16][32] fp32
-  uint64_t *full = (uint64_t *)(stg + kChEpiWarps * 16 * 32);
+  float *stg = (float *)(smem + (size_t)stages * Cfg::kStage);  // 8 warps x [8][32] fp32
+  uint64_t *full = (uint64_t *)(stg + kChEpiWarps * 8 * 32);
   uint64_t *empty = full + stages;
   uint64_t *acc_full = empty + stages;
   uint64_t *acc_empty = acc_full + 2;
@@ -1368,7 +1377,7 @@ __global__ void __launch_bounds__(kChThreads, 1)
     }
   } else {
     // ---- epilogue warps 0-3
-    float *wst = stg + warp * (16 * 32);
+    float *wst = stg + warp * (8 * 32);
     uint32_t local = 0;
     for (int64_t tile = blockIdx.x; tile < ntiles_total; tile += gridDim.x, local++) {
       int64_t line;
@@ -1765,7 +1774,7 @@ static void launch_conv_h(const CUtensorMap &ta, const CUtensorMap &tb, ConvH c,
   // two CTAs per SM when the accumulators fit (<= 256 TMEM columns each)
   const bool two = Cfg::kTmemCols <= 256;
   const size_t budget = two ? 111 * 1024 : 226 * 1024;
-  const size_t fixed = 1024 + (size_t)kChEpiWarps * 16 * 32 * 4 + 5 * 8 + 16;
+  const size_t fixed = 1024 + (size_t)kChEpiWarps * 8 * 32 * 4 + 5 * 8 + 16;
   int stages = (int)((budget - fixed) / (Cfg::kStage + 16));
   if (stages > 8) stages = 8;
   DCB_REQUIRE(stages >= 2, "conv: stages do not fit in shared memory");
