@@ -310,6 +310,9 @@ struct ConvW {             // B operand of a conv GEMM plus its epilogue constan
   uint16_t *wt = nullptr;
   int64_t ldt = 0;
   int ncb = 0;
+  // 8-tap convs over <= 8 input channels (the first encoders): K = (tap, channel padded to
+  // 8) = 64, matching the im2col'd fp16 copy of their input
+  uint16_t *wi = nullptr;
 };
 struct LinW {
   uint16_t *w = nullptr;   // [out][ld]
@@ -519,6 +522,14 @@ static bool load_conv(Loader &L, Staging &st, const std::string &prefix, ConvW &
   }
   st.add(packed.data(), packed.size() * 2, (void **)&cw.w);
   stage_tma_order(st, cw, packed, cw.rows, kp, cw.KH, cw.KW, cw.C);
+  if (cw.C <= 8 && cw.KH * cw.KW == 8) {
+    std::vector<uint16_t> t((size_t)cw.rows * 64, 0);
+    for (int r = 0; r < cw.rows; r++)
+      for (int tap = 0; tap < 8; tap++)
+        memcpy(&t[(size_t)r * 64 + tap * 8], &packed[(size_t)r * kp + (size_t)tap * cw.C],
+               (size_t)cw.C * 2);
+    st.add(t.data(), t.size() * 2, (void **)&cw.wi);
+  }
   stage_f32(st, b, &cw.bias);
   return true;
 }

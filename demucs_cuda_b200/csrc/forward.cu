@@ -185,6 +185,7 @@ struct Half16 {
   uint16_t *p = nullptr;
   int64_t images = 0;
   int C = 0, H = 1, W = 0, Wp = 0;
+  int im2col = 0;  // 1: the 8-tap im2col of a few-channel input, read by a 1x1 conv
   HalfAct act() const { return HalfAct{p, images, C, H, W, Wp}; }
   // [images * H][1][Wp][C]: the DConv view (frequency rows are images)
   HalfAct rows() const { return HalfAct{p, images * H, C, 1, W, Wp}; }
@@ -215,6 +216,19 @@ static Half16 to_half(const float *x, const float *add, int64_t images, int Cs, 
   k_to_half_cl<<<grid_for(n, 256), 256, 0, stream()>>>(x, add, h.p, images, C, H, W, h.Wp,
                                                        (int64_t)Cs * H * W, (int64_t)H * W, W,
                                                        Cs);
+  DCB_LAUNCHED();
+  return h;
+}
+
+// im2col'd fp16 copy of a few-channel input for an 8-tap, stride-S conv along H (axis 0) or
+// W (axis 1): [images][Ho][Wo][64]
+static Half16 im2col8(const float *x, int64_t images, int C, int H, int W, int Ho, int Wo,
+                      int S, int P, int axis) {
+  Half16 h = half_alloc(images, 64, Ho, Wo, false);
+  h.im2col = 1;
+  const int64_t n = images * Ho * (int64_t)Wo * 8;
+  k_im2col8_half<<<grid_for(n, 256), 256, 0, stream()>>>(x, h.p, images, C, H, W, Ho, Wo, S, P,
+                                                         axis);
   DCB_LAUNCHED();
   return h;
 }
@@ -250,7 +264,11 @@ static void conv_any(const ConvW &cw, const float *x, const Half16 *xh, const Im
   e.emb_alpha = emb_alpha;
   e.emb_ld = emb_ld;
   if (yh && yh->p) epi_half(e, *yh);
-  if (xh && xh->p && cw.wt) {
+  if (xh && xh->p && xh->im2col && cw.wi) {
+    // the input is already im2col'd: a 1x1 conv with K = 8 taps x 8 channels
+    if (conv_half(xh->act(), 1, 1, 1, 1, 0, 0, 1, 1, Ho, Wo, cw.wi, cw.rows, 64, 1, e, 0))
+      return;
+  } else if (xh && xh->p && cw.wt) {
     const HalfAct a = rows_view ? xh->rows() : xh->act();
     if (conv_half(a, cw.KH, cw.KW, SH, SW, PH, PW, DH, DW, Ho, Wo, cw.wt, cw.rows, cw.ldt,
                   cw.ncb, e, act >= 2 ? cw.glu_bn : 0))
@@ -374,6 +392,19 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
     dfree(h);
   }
   dfree(stat);
+}
+
+// fp16 copy of a first encoder's input: the im2col'd form when its conv has 8 taps over
+// <= 8 channels (the model inputs), else the channel-padded channels-last form
+static Half16 first_input(DcbModel *m, bool freq, const float *x, int B, int C, int H, int W) {
+  const EncW &E = freq ? m->enc[0] : m->tenc[0];
+  const int S = m->cfg.stride, K = m->cfg.kernel_size, pad = K / 4;
+  if (E.conv.wi && C <= 8 && K == 8) {
+    if (freq) return im2col8(x, B, C, H, W, (H + 2 * pad - K) / S + 1, W, S, pad, 0);
+    const int Lp = (W + S - 1) / S * S;
+    return im2col8(x, B, C, 1, W, 1, (Lp + 2 * pad - K) / S + 1, S, pad, 1);
+  }
+  return to_half(x, nullptr, B, C, H, W, !freq, (C + 7) / 8 * 8);
 }
 
 // freq encoder (dc_henc with freq = 1): x [B, Cin, H, W] (+ fp16 companion xh, or null) ->
@@ -771,8 +802,8 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
   // fp16 channels-last companions of the encoder inputs (none for the first encoders,
   // whose few input channels take the gather kernel)
   // (the first ones: the normalised inputs with their few channels padded to 8)
-  Half16 xh_t = to_half(xt, nullptr, B, C, 1, L, true, (C + 7) / 8 * 8);
-  Half16 xh_f = to_half(x, nullptr, B, 2 * C, nb, le, false, (2 * C + 7) / 8 * 8);
+  Half16 xh_t = first_input(m, false, xt, B, C, 1, L);
+  Half16 xh_f = first_input(m, true, x, B, 2 * C, nb, le);
   for (int i = 0; i < depth; i++) {
     t_len.push_back(Lt);
     int Lo;
@@ -1178,7 +1209,8 @@ int dcb_stage_encoder(DcbModel *m, int branch, int idx, const float *x, int B, i
     out_shape[3] = W;
     if (!y) return 0;
     int ho;
-    Half16 xh = to_half(x, nullptr, B, C, H, W, false, (C + 7) / 8 * 8);
+    Half16 xh = idx == 0 ? first_input(m, true, x, B, C, H, W)
+                         : to_half(x, nullptr, B, C, H, W, false, (C + 7) / 8 * 8);
     Half16 zh;
     float *z = enc_freq(m, idx, x, &xh, B, H, W, &ho, &zh);
     DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * E.Cout * Ho * W * 4, cudaMemcpyDeviceToDevice,
@@ -1197,7 +1229,8 @@ int dcb_stage_encoder(DcbModel *m, int branch, int idx, const float *x, int B, i
     out_shape[3] = 0;
     if (!y) return 0;
     int lo;
-    Half16 xh = to_half(x, nullptr, B, C, 1, L, true, (C + 7) / 8 * 8);
+    Half16 xh = idx == 0 ? first_input(m, false, x, B, C, 1, L)
+                         : to_half(x, nullptr, B, C, 1, L, true, (C + 7) / 8 * 8);
     Half16 zh;
     float *z = enc_time(m, idx, x, &xh, B, L, &lo, &zh);
     DCB_CUDA(cudaMemcpyAsync(y, z, (size_t)B * E.Cout * Lo * 4, cudaMemcpyDeviceToDevice,

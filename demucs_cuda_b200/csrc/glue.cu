@@ -520,6 +520,33 @@ __global__ void k_to_half_cl(const float *__restrict__ x, const float *__restric
   }
 }
 
+// im2col of a few-channel fp32 input [n][C][H][W] (C <= 8) for an 8-tap conv, as the fp16
+// A operand of a 1x1 conv: y[n][ho][wo][tap * 8 + c], round to nearest even; taps along H
+// (axis 0: h = ho S - P + tap, w = wo) or along W (axis 1: h = ho, w = wo S - P + tap);
+// taps outside the input and channels c >= C are zero (the conv's zero padding).  Threads
+// run over positions fastest (coalesced reads), one (position, tap) each.
+__global__ void k_im2col8_half(const float *__restrict__ x, uint16_t *__restrict__ y,
+                               int64_t images, int C, int H, int W, int Ho, int Wo, int S, int P,
+                               int axis) {
+  const int64_t npos = images * Ho * (int64_t)Wo;
+  const int64_t total = npos * 8;
+  DCB_GRID_STRIDE(i, total) {
+    const int tap = (int)(i / npos);
+    const int64_t pos = i - (int64_t)tap * npos;
+    const int64_t wo = pos % Wo, r = pos / Wo;
+    const int64_t ho = r % Ho, n = r / Ho;
+    const int64_t h = axis == 0 ? ho * S - P + tap : ho;
+    const int64_t w = axis == 0 ? wo : wo * S - P + tap;
+    float v[8];
+    const bool in = h >= 0 && h < H && w >= 0 && w < W;
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+      v[c] = in && c < C ? x[((n * C + c) * H + h) * (int64_t)W + w] : 0.f;
+    *(uint4 *)(y + pos * 64 + tap * 8) = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]),
+                                                   pack_h2(v[4], v[5]), pack_h2(v[6], v[7]));
+  }
+}
+
 // tok [B, Fr*T1, C] (token t*Fr + f) -> x [B, C, Fr, T1]
 __global__ void k_tokens_to_chw(const float *__restrict__ tok, float *__restrict__ x, int B,
                                 int C, int Fr, int T1) {
