@@ -345,6 +345,12 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
     const Img hv = freq_rows(B, hid, Fr, T);
     conv_any(dw.c0, y, yh, v, 1, 1, 0, dil, 1, dil, 1, T, h, hv, 0, nullptr, true);
     RowView rh{h, Fr, (int64_t)hid * Fr * T, T, (int64_t)Fr * T, hid, T};
+    // hidden widths >= 24: the hidden rows as fp16 channels-last (channels padded to 8),
+    // the A operand of a tensor-core 1x1 conv (narrower ones run on CUDA cores, where the
+    // few MACs per output are cheaper than the tensor-core epilogue)
+    const int hidp = (hid + 7) / 8 * 8;
+    Half16 h16 =
+        hid >= 24 && dw.c3g.wt && yh && yh->p ? half_alloc(B, hidp, Fr, T, false) : Half16{};
     if (fused) {
       // GroupNorm(1) + GELU in place with the z statistics, one CTA per row
       const size_t sm = (size_t)hid * T * sizeof(float);
@@ -355,7 +361,7 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
         attr = sm;
       }
       k_gn_gelu_zstats<<<rows, kGnFusedThreads, sm, stream()>>>(
-          rh, h, dw.gn1.w, dw.gn1.b, 1e-5f, dw.zc, C2, stat, stat + rows);
+          rh, h, dw.gn1.w, dw.gn1.b, 1e-5f, dw.zc, C2, stat, stat + rows, h16.p, hidp);
       DCB_LAUNCHED();
     } else {
       rowview_stats(rh, B, 1e-5f, stat, stat + rows, nullptr);
@@ -363,12 +369,19 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
       k_gn_gelu<<<grid_for(n, 256), 256, 0, stream()>>>(rh, h, stat, stat + rows, dw.gn1.w,
                                                        dw.gn1.b, B);
       DCB_LAUNCHED();
+      if (h16.p) {
+        const int64_t nh = (int64_t)B * Fr * T * (hidp / 8);
+        k_to_half_cl<<<grid_for(nh, 256), 256, 0, stream()>>>(
+            h, nullptr, h16.p, B, hidp, Fr, T, T, (int64_t)hid * Fr * T, (int64_t)Fr * T, T, hid);
+        DCB_LAUNCHED();
+      }
       // z statistics from the Gram matrix of fp16(h), accumulated over chunks of each row
       const int npair = hid * (hid + 1) / 2;
       const int chunk = kGramChunk * 6 / hid >= kGramChunk ? kGramChunk : 12288 / hid;
       double *acc = (double *)dalloc((size_t)rows * (npair + hid) * 2);
       DCB_CUDA(cudaMemsetAsync(acc, 0, (size_t)rows * (npair + hid) * sizeof(double), stream()));
-      const dim3 gg((unsigned)((T + chunk - 1) / chunk), rows);
+      const dim3 gg((unsigned)((T + chunk - 1) / chunk), rows,
+                    (unsigned)((npair + hid + kGramPairs - 1) / kGramPairs));
       k_gram_chunk<<<gg, 256, (size_t)hid * chunk * sizeof(float), stream()>>>(rh, chunk, acc);
       DCB_LAUNCHED();
       k_zstats_final<<<(rows + 3) / 4, 128, 0, stream()>>>(acc, dw.zc, hid, T, C2, (int)rows,
@@ -376,7 +389,36 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
       DCB_LAUNCHED();
       dfree(acc);
     }
-    if (hid <= 24) {
+    bool done = false;
+    if (h16.p) {
+      // 1x1 conv + GroupNorm + GLU + LayerScale + residual in one tensor-core conv epilogue
+      Epi e;
+      e.mode = EPI_CONV;
+      e.bias = dw.c3g.bias;
+      e.act = 3;
+      e.y = y;
+      e.oN2 = v.N2;
+      e.oN1 = v.sN1;
+      e.oN2s = v.sN2;
+      e.oC = v.sC;
+      e.oH = v.sH;
+      e.O = C;
+      e.Ho = 1;
+      e.Wo = T;
+      e.res = y;
+      e.scale = dw.scale;
+      e.gn_mean = stat;
+      e.gn_rstd = stat + rows;
+      e.gn_w = dw.gn4.w;
+      e.gn_b = dw.gn4.b;
+      epi_half(e, *yh);
+      e.yhH = 1;  // images are the rows (b, f) of yh's [B][Fr][T][C] layout
+      done = conv_half(h16.rows(), 1, 1, 1, 1, 0, 0, 1, 1, 1, T, dw.c3g.wt, dw.c3g.rows,
+                       dw.c3g.ldt, dw.c3g.ncb, e, dw.c3g.glu_bn);
+    }
+    dfree(h16.p);
+    if (done) {
+    } else if (hid <= 24) {
       dconv_tail(dw, h, y, B, C, hid, Fr, T, stat, stat + rows, yh);
     } else {
       conv(dw.c3g, h, nullptr, hv, 1, 1, 0, 0, 1, 1, 1, T, y, v, 3, y, dw.scale, stat,

@@ -1090,11 +1090,13 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
       }
     }
     const bool cl_fast = (!convtr || o16) && o0 + 16 <= O;  // 16 channels of one position
-    // skip-connection values for the fp16 copy, loaded before the accumulator wait
+    // skip-connection (or residual) values for the fp16 copy, loaded before the
+    // accumulator wait
     float sk[16];
     const bool want_h = e.yh && rv && tok && cl_fast;
-    if (want_h && e.hskip) {
-      const float *sp = e.hskip + base + (int64_t)o0 * e.oC + (int64_t)h * e.oH + w;
+    const float *skp = e.hskip ? e.hskip : e.res;
+    if (want_h && skp) {
+      const float *sp = skp + base + (int64_t)o0 * e.oC + (int64_t)h * e.oH + w;
 #pragma unroll
       for (int i = 0; i < 16; i++) sk[i] = sp[(int64_t)i * e.oC];
     } else {
@@ -1145,18 +1147,27 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
 #pragma unroll
       for (int i = 0; i < 16; i++) val[i] += __shfl_sync(0xffffffffu, ex, i);
     }
-    // ---- (1) fp16 channels-last copy
+    // ---- (1) fp16 channels-last copy: value + skip, or res + scale[o] * value
+    float mul[16];
+    if (e.res && !e.hskip && e.yh) {
+      // (uniform branch: every lane takes part in the shuffles)
+      const float scx = okc ? e.scale[oxl] : 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; i++) mul[i] = __shfl_sync(0xffffffffu, scx, i);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; i++) mul[i] = 1.f;
+    }
     if (want_h) {
+      float hv[16];
+#pragma unroll
+      for (int i = 0; i < 16; i++) hv[i] = fmaf(val[i], mul[i], sk[i]);
       uint16_t *dst = e.yh + (((int64_t)n * e.yhH + h) * e.yhW + w) * e.yhC + o0;
       uint4 *d4 = (uint4 *)dst;
-      d4[0] = make_uint4(pack_h2(val[0] + sk[0], val[1] + sk[1]),
-                         pack_h2(val[2] + sk[2], val[3] + sk[3]),
-                         pack_h2(val[4] + sk[4], val[5] + sk[5]),
-                         pack_h2(val[6] + sk[6], val[7] + sk[7]));
-      d4[1] = make_uint4(pack_h2(val[8] + sk[8], val[9] + sk[9]),
-                         pack_h2(val[10] + sk[10], val[11] + sk[11]),
-                         pack_h2(val[12] + sk[12], val[13] + sk[13]),
-                         pack_h2(val[14] + sk[14], val[15] + sk[15]));
+      d4[0] = make_uint4(pack_h2(hv[0], hv[1]), pack_h2(hv[2], hv[3]), pack_h2(hv[4], hv[5]),
+                         pack_h2(hv[6], hv[7]));
+      d4[1] = make_uint4(pack_h2(hv[8], hv[9]), pack_h2(hv[10], hv[11]),
+                         pack_h2(hv[12], hv[13]), pack_h2(hv[14], hv[15]));
     } else if (e.yh && rv) {
       // partial chunk (channel tail, or a transposed-conv chunk across two phases)
       for (int i = 0; i < 16; i++) {
@@ -1177,7 +1188,9 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
           ww = e.axis_h ? q : t;
         }
         float v = val[i];
-        if (e.hskip) v += e.hskip[base + (int64_t)o * e.oC + (int64_t)hh * e.oH + ww];
+        const int64_t so = base + (int64_t)o * e.oC + (int64_t)hh * e.oH + ww;
+        if (e.hskip) v += e.hskip[so];
+        else if (e.res) v = e.res[so] + e.scale[o] * v;
         e.yh[(((int64_t)n * e.yhH + hh) * e.yhW + ww) * e.yhC + o] = f2h_bits(v);
       }
     }

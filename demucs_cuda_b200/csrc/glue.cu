@@ -152,7 +152,8 @@ constexpr int kGnFusedThreads = 256;
 __global__ void __launch_bounds__(kGnFusedThreads)
     k_gn_gelu_zstats(RowView v, float *__restrict__ y, const float *__restrict__ w,
                      const float *__restrict__ bb, float eps, const double *__restrict__ zc,
-                     int C2, float *__restrict__ zmean, float *__restrict__ zrstd) {
+                     int C2, float *__restrict__ zmean, float *__restrict__ zrstd,
+                     uint16_t *__restrict__ h16, int hidp) {
   extern __shared__ float hs[];  // [hid][T]: fp16-rounded GELU outputs of this row
   __shared__ double sh[2][kGnFusedThreads / 32];
   const int64_t row = blockIdx.x;
@@ -202,6 +203,20 @@ __global__ void __launch_bounds__(kGnFusedThreads)
     }
   }
   __syncthreads();  // every thread has read sh[] and written hs[]
+  // fp16 channels-last copy of the row (the 1x1 conv's A operand): h16[(row T + t) hidp + c],
+  // channels hid..hidp-1 zero
+  if (h16) {
+    for (int t = threadIdx.x; t < T; t += kGnFusedThreads) {
+      uint16_t *dst = h16 + ((int64_t)row * T + t) * hidp;
+      for (int c8 = 0; c8 < hidp; c8 += 8) {
+        float q[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) q[k] = c8 + k < hid ? hs[(c8 + k) * T + t] : 0.f;
+        *(uint4 *)(dst + c8) = make_uint4(pack_h2(q[0], q[1]), pack_h2(q[2], q[3]),
+                                          pack_h2(q[4], q[5]), pack_h2(q[6], q[7]));
+      }
+    }
+  }
   // one warp per entry: the hid (hid + 1) / 2 upper Gram entries, then the hid sums
   const double *G = zc, *u = zc + hid * hid, *vv = u + hid;
   const int npair = hid * (hid + 1) / 2;
@@ -259,8 +274,10 @@ __global__ void __launch_bounds__(kGnFusedThreads)
 // Sums S_j and upper Gram entries Q_jk (j <= k) of fp16(h) over one chunk of a DConv
 // hidden row [hid][T], accumulated in fp64 into acc[row][npair + hid] (npair = hid (hid +
 // 1) / 2, the sums last): the statistics of z = W16 . fp16(h) + b for rows too long for
-// one CTA.  Block (chunk, row); the chunk is staged in shared memory [hid][len].
+// one CTA.  Block (chunk, row, group of kGramPairs entries); the chunk is staged in shared
+// memory [hid][len].
 constexpr int kGramChunk = 1024;
+constexpr int kGramPairs = 64;  // Gram entries per block (8 per warp)
 __global__ void __launch_bounds__(256)
     k_gram_chunk(RowView v, int chunk, double *__restrict__ acc) {
   extern __shared__ float hs[];
@@ -277,7 +294,8 @@ __global__ void __launch_bounds__(256)
   __syncthreads();
   const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int npair = hid * (hid + 1) / 2;
-  for (int p = wid; p < npair + hid; p += blockDim.x / 32) {
+  const int p_end = min(npair + hid, (int)(blockIdx.z + 1) * kGramPairs);
+  for (int p = blockIdx.z * kGramPairs + wid; p < p_end; p += blockDim.x / 32) {
     int j, k;
     if (p < npair) {
       j = 0;
