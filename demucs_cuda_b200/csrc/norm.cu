@@ -303,9 +303,95 @@ __global__ void k_layernorm(const float *__restrict__ x, void *__restrict__ yv,
   }
 }
 
+// Rows of C = 128 * NV floats: each lane holds NV float4 (16-byte loads; fp16 output as
+// 8-byte stores).  Same statistics as k_layernorm (sum in fp32 across lanes, the second
+// moment about the fp32 mean with the fp64 correction).
+template <int NV, bool HALF_OUT>
+__global__ void __launch_bounds__(128)
+    k_layernorm_v4(const float *__restrict__ x, void *__restrict__ yv,
+                   const float *__restrict__ w, const float *__restrict__ b, int64_t rows,
+                   float eps, int ld_out) {
+  constexpr int C = 128 * NV;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4 *p = (const float4 *)(x + row * C);
+  float4 v[NV];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    v[i] = p[i * 32 + lane];
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const double mean_d = (double)s / (double)C;
+  const float m = (float)mean_d;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    const float a = v[i].x - m, bq = v[i].y - m, c = v[i].z - m, d = v[i].w - m;
+    q += (a * a + bq * bq) + (c * c + d * d);
+  }
+  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const double dm = mean_d - (double)m;
+  const double m2 = (double)q - (double)C * dm * dm;
+  const float var = (float)((m2 > 0 ? m2 : 0.0) / (double)C);
+  const float rs = 1.0f / sqrtf(var + eps);
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    const int c0 = (i * 32 + lane) * 4;
+    float n[4] = {(v[i].x - m) * rs, (v[i].y - m) * rs, (v[i].z - m) * rs, (v[i].w - m) * rs};
+    if (w) {
+      const float4 wv = *(const float4 *)(w + c0);
+      n[0] *= wv.x;
+      n[1] *= wv.y;
+      n[2] *= wv.z;
+      n[3] *= wv.w;
+    }
+    if (b) {
+      const float4 bv = *(const float4 *)(b + c0);
+      n[0] += bv.x;
+      n[1] += bv.y;
+      n[2] += bv.z;
+      n[3] += bv.w;
+    }
+    if (HALF_OUT) {
+      *(uint2 *)((uint16_t *)yv + row * ld_out + c0) =
+          make_uint2(pack_h2(n[0], n[1]), pack_h2(n[2], n[3]));
+    } else {
+      *(float4 *)((float *)yv + row * ld_out + c0) = make_float4(n[0], n[1], n[2], n[3]);
+    }
+  }
+}
+
 void layernorm(const float *x, void *y, const float *w, const float *b, int64_t rows, int C,
                float eps, bool half_out, int ld_out) {
   if (rows <= 0) return;
+  // vector path: C = 128 * NV with aligned rows and parameters (and no output padding)
+  const bool vec = C % 128 == 0 && C <= 1024 && ld_out == C && ((uintptr_t)x & 15) == 0 &&
+                   ((uintptr_t)y & 15) == 0 && (!w || ((uintptr_t)w & 15) == 0) &&
+                   (!b || ((uintptr_t)b & 15) == 0);
+  if (vec) {
+    const unsigned blocks = (unsigned)((rows + 3) / 4);
+#define DCB_LNV(NV)                                                                       \
+  if (half_out)                                                                           \
+    k_layernorm_v4<NV, true><<<blocks, 128, 0, stream()>>>(x, y, w, b, rows, eps, ld_out);  \
+  else                                                                                    \
+    k_layernorm_v4<NV, false><<<blocks, 128, 0, stream()>>>(x, y, w, b, rows, eps, ld_out)
+    switch (C / 128) {
+      case 1: DCB_LNV(1); break;
+      case 2: DCB_LNV(2); break;
+      case 3: DCB_LNV(3); break;
+      case 4: DCB_LNV(4); break;
+      case 5: DCB_LNV(5); break;
+      case 6: DCB_LNV(6); break;
+      case 7: DCB_LNV(7); break;
+      default: DCB_LNV(8); break;
+    }
+#undef DCB_LNV
+    DCB_LAUNCHED();
+    return;
+  }
   if (C <= 1024) {
     unsigned blocks = (unsigned)((rows + 3) / 4);
     if (half_out) {
