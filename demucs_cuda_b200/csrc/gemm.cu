@@ -1658,7 +1658,11 @@ void gemm_rows(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch,
 void gemm_rows_launch(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch,
                       const Epi &e, Shape s, Gather g) {
   if (!g_opt_simt && K > 0 && batch <= 65535) {
-    const int bn = pick_bn(M, N, batch);
+    int bn = pick_bn(M, N, batch);
+    // short GEMMs (the transformer's): narrower N tiles until the persistent CTAs get two
+    // tiles each, so loads and epilogues of consecutive tiles overlap
+    const int64_t mt = (M + kBM - 1) / kBM;
+    while (bn > 64 && mt * ((N + bn - 1) / bn) * batch < 4ll * sm_count()) bn /= 2;
     CUtensorMap ta, tb;
     const bool ok =
         encode_map(&ta, a.p, (uint64_t)K, (uint64_t)M, s.a_shared ? 1 : (uint64_t)batch,
