@@ -363,8 +363,9 @@ __global__ void k_fm_to_chw(const float2 *__restrict__ z, float *__restrict__ x,
 }
 
 // fused inverse STFT + OLA for n = 4096 (see k_istft_ola): 256 threads, the CTA's
-// accumulator (kOlaHops hops) in registers, one padded FFT buffer in shared memory
-__global__ void __launch_bounds__(kFftThreads)
+// accumulator (kOlaHops hops) in registers, one padded FFT buffer in shared memory; three
+// CTAs per SM (registers capped at 85) so one CTA's FFT barriers overlap another's work
+__global__ void __launch_bounds__(kFftThreads, 3)
     k_istft_ola4096(const float2 *__restrict__ z, float *__restrict__ out, int N, int F, int hop,
                     const float *__restrict__ window, const float2 *__restrict__ tw,
                     int64_t start, int64_t length, int j_first) {
