@@ -1103,9 +1103,12 @@ struct Mt {
 struct Plan {
   int seg = 0, stride = 0;
   std::vector<int> offsets;
-  // forwards of this shard: indices into offsets; full segments batched, tails alone
-  std::vector<std::vector<int>> full_batches;
-  std::vector<int> tails;
+  // forwards of this shard: indices into offsets.  Every segment of the shard is padded to
+  // the training length (tails centred, as apply.c:282-293 pads them), so full segments and
+  // tails share one forward shape; they are grouped into the fewest batches of at most
+  // batch_size, with sizes differing by at most one (each segment's result does not depend
+  // on its batch: normalisation and every kernel are per item).
+  std::vector<std::vector<int>> batches;
 };
 
 static Plan make_plan(const Cfg &c, int length, const DcbApplyOpts &o) {
@@ -1116,20 +1119,18 @@ static Plan make_plan(const Cfg &c, int length, const DcbApplyOpts &o) {
   for (int off = 0; off < length; off += p.stride) p.offsets.push_back(off);
   const int bs = o.batch_size < 1 ? 1 : (o.batch_size > 32 ? 32 : o.batch_size);
   const int cnt = o.shard_count > 1 ? o.shard_count : 1;
-  std::vector<int> cur;
-  for (int i = 0; i < (int)p.offsets.size(); i++) {
-    if (i % cnt != (cnt > 1 ? o.shard_index : 0)) continue;
-    if (length - p.offsets[i] >= p.seg) {
-      cur.push_back(i);
-      if ((int)cur.size() >= bs) {
-        p.full_batches.push_back(cur);
-        cur.clear();
-      }
-    } else {
-      p.tails.push_back(i);
-    }
+  std::vector<int> mine;
+  for (int i = 0; i < (int)p.offsets.size(); i++)
+    if (i % cnt == (cnt > 1 ? o.shard_index : 0)) mine.push_back(i);
+  const int n = (int)mine.size();
+  if (n == 0) return p;
+  const int nb = (n + bs - 1) / bs, q = n / nb, r = n % nb;
+  int at = 0;
+  for (int b = 0; b < nb; b++) {
+    const int sz = q + (b < r ? 1 : 0);
+    p.batches.emplace_back(mine.begin() + at, mine.begin() + at + sz);
+    at += sz;
   }
-  if (!cur.empty()) p.full_batches.push_back(cur);
   return p;
 }
 
@@ -1172,47 +1173,34 @@ static int apply_split(DcbModel *m, const float *mix, int B, int length, float *
   const float *wdev = m->ola_w;
   const int64_t rows = (int64_t)B * S * C;
   DCB_CUDA(cudaMemsetAsync(out, 0, (size_t)rows * length * 4, stream()));
-  for (const auto &bt : p.full_batches) {
+  for (const auto &bt : p.batches) {
     const int nbt = (int)bt.size();
     FwdGraph *slot = forward_slot(m, nbt * B, Lv);
     if (!slot) return -1;
     float *flat = slot->in;
     for (int k = 0; k < nbt; k++) {
+      // segment (or tail) centred in the training length (apply.c:254-293)
       const int off = p.offsets[bt[k]];
-      const int64_t start = off - (Lv - p.seg) / 2;
+      const int this_len = length - off < p.seg ? length - off : p.seg;
+      if (this_len > Lv) {
+        fail("apply: segment longer than the training length");
+        return -1;
+      }
+      const int64_t start = off - (Lv - this_len) / 2;
       k_chunk<<<grid_for((int64_t)B * C * Lv, 256), 256, 0, stream()>>>(
           mix, flat + (size_t)k * B * C * Lv, B, C, length, start, Lv, (int64_t)C * Lv);
       DCB_LAUNCHED();
     }
     if (forward_slot_run(m, slot) < 0) return -1;
     const float *y = slot->out;
-    const int y0 = (Lv - p.seg) / 2;  // center_trim(y, seg)
     for (int k = 0; k < nbt; k++) {
       const int off = p.offsets[bt[k]];
-      k_accumulate<<<grid_for(rows * p.seg, 256), 256, 0, stream()>>>(
-          out, y + (size_t)k * rows * Lv, wdev, (int)rows, length, Lv, off, y0, p.seg);
+      const int this_len = length - off < p.seg ? length - off : p.seg;
+      const int y0 = (Lv - this_len) / 2;  // center_trim
+      k_accumulate<<<grid_for(rows * this_len, 256), 256, 0, stream()>>>(
+          out, y + (size_t)k * rows * Lv, wdev, (int)rows, length, Lv, off, y0, this_len);
       DCB_LAUNCHED();
     }
-  }
-  for (int i : p.tails) {
-    const int off = p.offsets[i];
-    const int this_len = length - off;
-    const int valid = this_len < Lv ? Lv : this_len;
-    if (valid > Lv) {
-      fail("apply: tail segment longer than the training length");
-      return -1;
-    }
-    FwdGraph *slot = forward_slot(m, B, valid);
-    if (!slot) return -1;
-    const int64_t start = off - (valid - this_len) / 2;
-    k_chunk<<<grid_for((int64_t)B * C * valid, 256), 256, 0, stream()>>>(
-        mix, slot->in, B, C, length, start, valid, (int64_t)C * valid);
-    DCB_LAUNCHED();
-    if (forward_slot_run(m, slot) < 0) return -1;
-    const int y0 = (valid - this_len) / 2;
-    k_accumulate<<<grid_for(rows * this_len, 256), 256, 0, stream()>>>(
-        out, slot->out, wdev, (int)rows, length, valid, off, y0, this_len);
-    DCB_LAUNCHED();
   }
   // divide by the weight sum of every segment (all shards'), summed on the device
   k_scale_ola<<<grid_for(length, 256), 256, 0, stream()>>>(out, wdev, rows, length, p.seg,
@@ -1367,11 +1355,10 @@ int dcb_segment_plan(int samplerate, float segment, int length, const DcbApplyOp
     call_of[i] = -1;
   }
   int call = 0;
-  for (auto &b : p.full_batches) {
+  for (auto &b : p.batches) {
     for (int i : b) call_of[i] = call;
     call++;
   }
-  for (int i : p.tails) call_of[i] = call++;
   return n;
 }
 
@@ -1381,10 +1368,9 @@ int dcb_apply_plan(DcbModel *m, int T, const DcbApplyOpts *o, int *n_forwards, i
   if (o->shifts > 0) len = T + (int)(0.5f * (float)m->cfg.samplerate);  // upper bound
   Plan p = make_plan(m->cfg, len, *o);
   int fw = 0;
-  for (auto &b : p.full_batches) fw += (int)b.size();
-  if (n_forwards) *n_forwards = (fw + (int)p.tails.size()) * (o->shifts > 0 ? o->shifts : 1);
-  if (n_batched) *n_batched = ((int)p.full_batches.size() + (int)p.tails.size()) *
-                              (o->shifts > 0 ? o->shifts : 1);
+  for (auto &b : p.batches) fw += (int)b.size();
+  if (n_forwards) *n_forwards = fw * (o->shifts > 0 ? o->shifts : 1);
+  if (n_batched) *n_batched = (int)p.batches.size() * (o->shifts > 0 ? o->shifts : 1);
   return 0;
 }
 

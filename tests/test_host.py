@@ -14,18 +14,25 @@ def test_shift_rng_is_cpython_randint(seed):
 
 
 @pytest.mark.parametrize("length", [10_584_000, 343_980, 400_000, 1000, 1_000_001])
-def test_segment_plan_matches_port(length):
+@pytest.mark.parametrize("bs", [1, 3, 8])
+def test_segment_plan_matches_port(length, bs):
+    """Same segment offsets as dc_apply_model; every segment in exactly one forward call,
+    calls of at most batch_size segments, as few calls as possible, sizes within one of
+    each other (tails are padded to the training length like full segments, so they batch
+    with them; a segment's result does not depend on its batch)."""
     import demucs_cuda_b200 as d
     from oracle import port
     pc = port.Config({})
-    seg, stride, offsets, batches = port.segment_plan(length, pc, 0.25, 8)
-    offs, calls = d.segment_plan(length, overlap=0.25, batch_size=8)
+    seg, stride, offsets, batches = port.segment_plan(length, pc, 0.25, bs)
+    offs, calls = d.segment_plan(length, overlap=0.25, batch_size=bs)
     assert offs == offsets
-    # one shard: the same forward calls as dc_apply_model (full segments batched, tails alone)
     groups = {}
     for i, c in enumerate(calls):
         groups.setdefault(c, []).append(i)
-    assert sorted(groups.values()) == sorted(idx for _, idx in batches)
+    assert sorted(i for g in groups.values() for i in g) == list(range(len(offs)))
+    sizes = [len(g) for g in groups.values()]
+    assert max(sizes) <= bs and max(sizes) - min(sizes) <= 1
+    assert len(groups) == -(-len(offs) // bs)
 
 
 @pytest.mark.parametrize("count", [2, 3, 4, 8])
@@ -40,9 +47,11 @@ def test_shards_cover_every_segment_once(count):
 
 
 def test_240s_track_plan_counts():
-    """42 segment forwards (40 full + 2 tails) per shift."""
+    """42 segment forwards (40 full + 2 tails) per shift, in 6 forward
+    calls of 7 segments at batch size 8."""
     import demucs_cuda_b200 as d
     offs, calls = d.segment_plan(10_584_000 + 22050 - 7000)  # shifted track length range
     assert len(offs) in (42, 43)
     offs, calls = d.segment_plan(10_584_000)
-    assert len(offs) == 42 and max(calls) + 1 == 7  # 5 batches of 8 + 2 tails
+    assert len(offs) == 42 and max(calls) + 1 == 6
+    assert all(calls.count(c) == 7 for c in range(6))
