@@ -1177,30 +1177,32 @@ static int apply_split(DcbModel *m, const float *mix, int B, int length, float *
     const int nbt = (int)bt.size();
     FwdGraph *slot = forward_slot(m, nbt * B, Lv);
     if (!slot) return -1;
-    float *flat = slot->in;
+    // items (segment or tail) centred in the training length (apply.c:254-293)
+    SegList sl{};
+    sl.cnt = nbt;
+    int64_t lo = length, hi = 0;
     for (int k = 0; k < nbt; k++) {
-      // segment (or tail) centred in the training length (apply.c:254-293)
       const int off = p.offsets[bt[k]];
       const int this_len = length - off < p.seg ? length - off : p.seg;
-      if (this_len > Lv) {
+      if (this_len > Lv || k >= 32) {
         fail("apply: segment longer than the training length");
         return -1;
       }
-      const int64_t start = off - (Lv - this_len) / 2;
-      k_chunk<<<grid_for((int64_t)B * C * Lv, 256), 256, 0, stream()>>>(
-          mix, flat + (size_t)k * B * C * Lv, B, C, length, start, Lv, (int64_t)C * Lv);
-      DCB_LAUNCHED();
+      sl.start[k] = off - (Lv - this_len) / 2;
+      sl.off[k] = off;
+      sl.y0[k] = (Lv - this_len) / 2;  // center_trim
+      sl.n[k] = this_len;
+      lo = off < lo ? off : lo;
+      hi = off + this_len > hi ? off + this_len : hi;
     }
+    const int64_t per = (int64_t)B * C * Lv;
+    k_chunk_batch<<<dim3(grid_for(per, 256, 148 * 8), (unsigned)nbt), 256, 0, stream()>>>(
+        mix, slot->in, B, C, length, Lv, sl);
+    DCB_LAUNCHED();
     if (forward_slot_run(m, slot) < 0) return -1;
-    const float *y = slot->out;
-    for (int k = 0; k < nbt; k++) {
-      const int off = p.offsets[bt[k]];
-      const int this_len = length - off < p.seg ? length - off : p.seg;
-      const int y0 = (Lv - this_len) / 2;  // center_trim
-      k_accumulate<<<grid_for(rows * this_len, 256), 256, 0, stream()>>>(
-          out, y + (size_t)k * rows * Lv, wdev, (int)rows, length, Lv, off, y0, this_len);
-      DCB_LAUNCHED();
-    }
+    k_accumulate_batch<<<grid_for(rows * (hi - lo), 256), 256, 0, stream()>>>(
+        out, slot->out, wdev, (int)rows, length, Lv, lo, hi, sl);
+    DCB_LAUNCHED();
   }
   // divide by the weight sum of every segment (all shards'), summed on the device
   k_scale_ola<<<grid_for(length, 256), 256, 0, stream()>>>(out, wdev, rows, length, p.seg,

@@ -615,6 +615,49 @@ __global__ void k_accumulate(float *out, const float *__restrict__ y,
   }
 }
 
+// segments of one forward call: start / output offset / trim / length per item
+struct SegList {
+  int64_t start[32];  // first mix sample of the item's padded chunk
+  int64_t off[32];    // output position of the item's first kept sample
+  int64_t y0[32];     // first kept sample inside the item's output
+  int64_t n[32];      // kept samples
+  int cnt;
+};
+
+// every item's padded chunk of mix (zeros outside [0, total)) into flat[k][b][c][len];
+// blockIdx.y = item
+__global__ void k_chunk_batch(const float *__restrict__ mix, float *__restrict__ flat, int Bm,
+                              int C, int64_t total, int64_t len, SegList sl) {
+  const int k = blockIdx.y;
+  const int64_t n = (int64_t)Bm * C * len;
+  float *out = flat + (int64_t)k * n;
+  const int64_t start = sl.start[k];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i % len, r = i / len;
+    const int64_t s = start + t;
+    out[i] = (s >= 0 && s < total) ? mix[r * total + s] : 0.f;
+  }
+}
+
+// out[r][t] += y[k][r][y0_k + t - off_k] * w[t - off_k] for the items k covering t, added in
+// item (segment) order as apply.c:157-169 adds them, over the call's output range [lo, hi)
+__global__ void k_accumulate_batch(float *out, const float *__restrict__ y,
+                                   const float *__restrict__ w, int rows, int64_t out_len,
+                                   int64_t y_len, int64_t lo, int64_t hi, SegList sl) {
+  const int64_t span = hi - lo, total = (int64_t)rows * span;
+  DCB_GRID_STRIDE(i, total) {
+    const int64_t t = lo + i % span, r = i / span;
+    float acc = out[r * out_len + t];
+    for (int k = 0; k < sl.cnt; k++) {
+      const int64_t u = t - sl.off[k];
+      if (u >= 0 && u < sl.n[k])
+        acc += y[((int64_t)k * rows + r) * y_len + sl.y0[k] + u] * w[u];
+    }
+    out[r * out_len + t] = acc;
+  }
+}
+
 // y = x * s[t] (final division by the summed transition weights)
 // x[r][t] *= 1 / sum_i w[t - off_i] over the segments i covering t (offsets i * stride,
 // i < noff): the weight normalisation of dc_apply_model (apply.c:295-300), summed in fp64

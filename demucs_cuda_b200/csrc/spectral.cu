@@ -362,81 +362,78 @@ __global__ void k_fm_to_chw(const float2 *__restrict__ z, float *__restrict__ x,
   }
 }
 
-// fused inverse STFT + OLA for n = 4096 (see k_istft_ola): 256 threads, the CTA's
-// accumulator (kOlaHops hops) in registers, one padded FFT buffer in shared memory; three
-// CTAs per SM (registers capped at 85) so one CTA's FFT barriers overlap another's work
-__global__ void __launch_bounds__(kFftThreads, 3)
-    k_istft_ola4096(const float2 *__restrict__ z, float *__restrict__ out, int N, int F, int hop,
-                    const float *__restrict__ window, const float2 *__restrict__ tw,
-                    int64_t start, int64_t length, int j_first) {
+
+// inverse STFT for n = 4096, hop 1024, in two passes.  Pass 1: one CTA per (row, pair of
+// output frames f, f + 1) inverts both spectra with one complex FFT (Y = X_f + i X_{f+1},
+// both Hermitian-extended; IFFT(Y) = conj(FFT(conj(Y))) / n, real part frame f, imaginary
+// part frame f + 1) and writes the windowed frames fw[row][f - f_lo][4096].  Output frame f
+// uses spectrum frame f - 2 (the two frames of padding of the reference's istft).
+__global__ void __launch_bounds__(kFftThreads)
+    k_ifft_frames4096(const float2 *__restrict__ z, float *__restrict__ fw, int N, int F,
+                      const float *__restrict__ window, const float2 *__restrict__ tw,
+                      int f_lo, int nfw) {
   __shared__ float2 buf[kFftPadded];
   constexpr int n = kFftN;
-  constexpr int Q = kOlaHops * 1024 / kFftThreads;  // accumulator entries per thread (hop 1024)
   const int64_t r = blockIdx.y;
-  const int j0 = j_first + blockIdx.x * kOlaHops;
-  const int NF = N + 4;
-  const int64_t a0 = (int64_t)j0 * hop;
-  float acc[Q];
+  const int f = f_lo + 2 * blockIdx.x;
+  const int fa = f - 2, fb = f - 1;
+  const bool va = fa >= 0 && fa < N, vb = f + 1 < f_lo + nfw && fb >= 0 && fb < N;
+  if (!va && !vb) return;  // pass 2 skips frames without a spectrum
+  const float2 *za = z + (r * N + fa) * F;
+  const float2 *zb = z + (r * N + fb) * F;
 #pragma unroll
-  for (int q = 0; q < Q; q++) acc[q] = 0.f;
-  const float inv_n = 1.0f / (float)n;
-  int f_beg = j0 - n / hop + 1;
-  if (f_beg < 0) f_beg = 0;
-  int f_end = j0 + kOlaHops - 1;
-  if (f_end > NF - 1) f_end = NF - 1;
-  // two frames per complex transform: both inverse transforms are real, so with
-  // Y = X_f + i X_{f+1} (each X Hermitian-extended to 4096 bins) the real part of IFFT(Y)
-  // is frame f and the imaginary part frame f+1.  IFFT(Y) = conj(FFT(conj(Y))) / n.
-  for (int f = f_beg; f <= f_end; f += 2) {
-    const int fa = f - 2, fb = f - 1;  // spectrum frames of output frames f and f + 1
-    const bool va = fa >= 0 && fa < N, vb = f + 1 <= f_end && fb >= 0 && fb < N;
-    if (!va && !vb) continue;
-    const float2 *za = z + ((int64_t)r * N + fa) * F;
-    const float2 *zb = z + ((int64_t)r * N + fb) * F;
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < 16; q++) {
-      const int k = threadIdx.x + 256 * q;
-      const int kk = k <= n / 2 ? k : n - k;
-      float2 a = va && kk < F ? za[kk] : make_float2(0.f, 0.f);
-      float2 b = vb && kk < F ? zb[kk] : make_float2(0.f, 0.f);
-      if (k > n / 2) {
-        a.y = -a.y;
-        b.y = -b.y;
-      }
-      // conj(Y) = conj(a + i b) = (a.x - b.y) - i (a.y + b.x)
-      buf[fpad(k)] = make_float2(a.x - b.y, -(a.y + b.x));
+  for (int q = 0; q < 16; q++) {
+    const int k = threadIdx.x + 256 * q;
+    const int kk = k <= n / 2 ? k : n - k;
+    float2 a = va && kk < F ? za[kk] : make_float2(0.f, 0.f);
+    float2 b = vb && kk < F ? zb[kk] : make_float2(0.f, 0.f);
+    if (k > n / 2) {
+      a.y = -a.y;
+      b.y = -b.y;
     }
-    __syncthreads();
-    fft4096(buf, tw);
-    const int64_t off = a0 - (int64_t)f * hop;
-#pragma unroll
-    for (int q = 0; q < Q; q++) {
-      const int64_t i = off + threadIdx.x + 256 * q;
-      float sum = 0.f;
-      if (va && i >= 0 && i < n) sum += buf[fpad((int)i)].x * inv_n * window[i];
-      const int64_t i2 = i - hop;  // frame f + 1 starts one hop later
-      if (vb && i2 >= 0 && i2 < n) sum += -buf[fpad((int)i2)].y * inv_n * window[i2];
-      acc[q] += sum;
-    }
+    buf[fpad(k)] = make_float2(a.x - b.y, -(a.y + b.x));
   }
-  const int64_t out_len = (int64_t)hop * (NF - 1) + n;
+  __syncthreads();
+  fft4096(buf, tw);
+  const float inv_n = 1.0f / (float)n;
+  float *oa = fw + (r * nfw + (f - f_lo)) * (int64_t)n;
+  float *ob = oa + n;
 #pragma unroll
-  for (int q = 0; q < Q; q++) {
-    const int64_t idx = a0 + threadIdx.x + 256 * q, t = idx - start;
-    if (t < 0 || t >= length) continue;
-    float den = 0.f;
+  for (int q = 0; q < 16; q++) {
+    const int i = threadIdx.x + 256 * q;
+    const float2 v = buf[fpad(i)];
+    const float wi = window[i] * inv_n;
+    if (va) oa[i] = v.x * wi;
+    if (vb) ob[i] = -v.y * wi;
+  }
+}
+
+// Pass 2: out[row][t] = sum of the windowed frames covering start + t (frames with a
+// spectrum) / sum of the squared window over every frame covering it (the reference's
+// window-sum division), for t in [0, length)
+__global__ void k_ola_frames4096(const float *__restrict__ fw, float *__restrict__ out,
+                                 int64_t R, int N, int NF, const float *__restrict__ window,
+                                 int f_lo, int nfw, int64_t start, int64_t length) {
+  constexpr int n = kFftN, hop = 1024;
+  const int64_t total = R * length;
+  const int64_t out_len = (int64_t)hop * (NF - 1) + n;
+  DCB_GRID_STRIDE(i, total) {
+    const int64_t r = i / length, t = i - r * length, idx = start + t;
+    float acc = 0.f, den = 0.f;
     if (idx < out_len) {
-      int64_t f_hi = idx / hop;
-      if (f_hi > NF - 1) f_hi = NF - 1;
-      const int64_t f_lo = idx - n + 1 <= 0 ? 0 : (idx - n + hop) / hop;
-      for (int64_t g = f_lo; g <= f_hi; g++) {
+      int64_t g_hi = idx / hop;
+      if (g_hi > NF - 1) g_hi = NF - 1;
+      const int64_t g_lo = idx - n + 1 <= 0 ? 0 : (idx - n + hop) / hop;
+      for (int64_t g = g_lo; g <= g_hi; g++) {
         const int64_t w = idx - g * hop;
         if (w < 0 || w >= n) continue;
         den += window[w] * window[w];
+        const int64_t fi = g - 2;
+        if (fi >= 0 && fi < N && g >= f_lo && g < f_lo + nfw)
+          acc += fw[(r * nfw + (g - f_lo)) * (int64_t)n + w];
       }
     }
-    out[r * length + t] = den > 0.f ? acc[q] / den : 0.f;
+    out[r * length + t] = den > 0.f ? acc / den : 0.f;
   }
 }
 
@@ -472,8 +469,24 @@ void ispec_fused(const float *x, float *out, const float *mean, const float *var
     attr = smem;
   }
   if (n_fft == kFftN && hop == 1024) {
-    k_istft_ola4096<<<dim3((unsigned)groups, (unsigned)R), kFftThreads, 0, stream()>>>(
-        z, out, N, F, hop, window, twiddles4096(), start, length, j_first);
+    // frames covering [start, start + length): NF = N + 4 output frames in all
+    const int NF = N + 4;
+    // first frame reaching past start: floor((start - n) / hop) + 1
+    const int64_t a = start - n_fft;
+    int f_lo = (int)((a >= 0 ? a / hop : -((-a + hop - 1) / hop))) + 1;
+    if (f_lo < 0) f_lo = 0;
+    int f_hi = (int)((start + length - 1) / hop);
+    if (f_hi > NF - 1) f_hi = NF - 1;
+    const int nfw = f_hi - f_lo + 1;
+    float *fw = nullptr;
+    DCB_CUDA(cudaMallocAsync(&fw, (size_t)R * nfw * n_fft * sizeof(float), stream()));
+    k_ifft_frames4096<<<dim3((unsigned)((nfw + 1) / 2), (unsigned)R), kFftThreads, 0,
+                        stream()>>>(z, fw, N, F, window, twiddles4096(), f_lo, nfw);
+    DCB_LAUNCHED();
+    k_ola_frames4096<<<grid_for(R * length, 256), 256, 0, stream()>>>(
+        fw, out, R, N, NF, window, f_lo, nfw, start, length);
+    DCB_LAUNCHED();
+    DCB_CUDA(cudaFreeAsync(fw, stream()));
   } else {
     k_istft_ola<<<dim3((unsigned)groups, (unsigned)R), 512, smem, stream()>>>(
         z, out, N, F, n_fft, log2i(n_fft), hop, window, tw, start, length, j_first);
