@@ -55,20 +55,6 @@ static __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) 
       : "memory");
   return ok != 0;
 }
-// try_wait that lets the hardware suspend the thread until the phase completes or about
-// `ns` nanoseconds pass, so waiting warps do not take issue slots from working ones
-static __device__ __forceinline__ bool mbar_try_sleep(uint64_t *bar, uint32_t parity,
-                                                      uint32_t ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
-      : "memory");
-  return ok != 0;
-}
 static __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -81,7 +67,6 @@ static __device__ __forceinline__ bool fault_pending() {
 // kWaitNs of wall-clock time, or at once if another CTA already recorded a fault, so a
 // protocol error ends every CTA of the grid quickly instead of hanging the GPU.
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s; legitimate waits are microseconds
-constexpr uint32_t kSuspendNs = 20000;  // per try_wait; the phase completing wakes it
 static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t fault) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = global_ns();

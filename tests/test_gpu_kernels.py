@@ -316,3 +316,20 @@ def test_spec_ispec(dcb, ref, torch_cuda, T):
     L_.dk_ola(_p(fr), _p(y), R, NF, nfft, hop, _p(win), nfft // 2 + pad, T)
     dcb.check(True, "istft")
     assert rel_l2(y.cpu().numpy().reshape(y_ref.shape), y_ref) < 1e-5
+
+
+def test_gelu_against_erf(dcb, torch_cuda):
+    """The kernels' GELU (the exact erf form, as layers.c computes it) against
+    x / 2 (1 + erf(x / sqrt 2)) in float64, |error| <= 3e-7 (|x| + 1) over a dense range."""
+    import math
+    torch = torch_cuda
+    x = torch.linspace(-12.0, 12.0, 2_000_001, device="cuda", dtype=torch.float32)
+    y = torch.empty_like(x)
+    L_ = dcb.lib()
+    L_.dk_unary(1, _p(x), _p(y), x.numel(), C.c_float(1.0), C.c_float(0.0))
+    torch.cuda.synchronize()
+    xs = x.double().cpu().numpy()[::97]
+    ref = 0.5 * xs * (1.0 + np.array([math.erf(v / math.sqrt(2.0)) for v in xs]))
+    got = y.double().cpu().numpy()[::97]
+    err = np.abs(got - ref) / (np.abs(xs) + 1.0)
+    assert err.max() <= 3e-7, err.max()
