@@ -44,13 +44,6 @@ struct AttnArgs {
   float *o32;     // [B][Tq][H*hd] fp32 (may be null)
 };
 
-// 2^x with the MUFU.EX2 instruction (PTX ex2.approx.ftz.f32, relative error ~2^-22): the
-// probabilities are rounded to fp16 right after
-static __device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 __global__ void __launch_bounds__(kAttnThreads, 2)
     k_flash_attn(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,

@@ -49,6 +49,7 @@ void set_stream_override(cudaStream_t s);
 // option values (dcb_set_option)
 extern int g_opt_simt;
 extern int g_opt_graphs;
+extern int g_opt_generic_epi;  // channels-last convs take the generic epilogue
 
 // device fault word written by bounded waits (see umma.cuh); the library is one
 // translation unit (all.cu), so the definition lives here
@@ -66,8 +67,27 @@ static inline unsigned grid_for(int64_t n, int threads, int64_t cap = 148 * 32) 
 
 // ------------------------------------------------------------------ numerics
 // GELU in the erf form the reference uses (backend_cpu.c:144, cuda_common.cuh:42-44).
+// 2^x by the hardware approximation (ex2.approx.ftz: relative error ~2^-22, results below
+// 2^-126 flush to zero)
+static __device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// GELU, x Phi(x) with Phi(x) = (1 + erf(x / sqrt 2)) / 2 (the exact form of layers.c).
+// erf(z), z >= 0, from Abramowitz & Stegun 7.1.26: 1 - (a1 t + ... + a5 t^5) exp(-z^2),
+// t = 1 / (1 + p z), |error| <= 1.5e-7.  The tail h = (1 - erf(|x| / sqrt 2)) / 2 is formed
+// directly (coefficients pre-halved), so Phi = 1 - h for x >= 0 and h for x < 0 without
+// cancellation.  |GELU error| <= 3e-7 (|x| + 1) against float64 erf (pinned by a GPU test).
 static __device__ __forceinline__ float gelu_f(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+  float p = fmaf(0.5307027145f, t, -0.7265760135f);  // a5 / 2, a4 / 2
+  p = fmaf(p, t, 0.7107068705f);                      // a3 / 2
+  p = fmaf(p, t, -0.142248368f);                      // a2 / 2
+  p = fmaf(p, t, 0.127414796f);                       // a1 / 2
+  const float h = p * t * ex2_approx(x * x * -0.72134752044448170f);  // exp(-x^2 / 2)
+  return x * (x >= 0.f ? 1.0f - h : h);
 }
 static __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 // fp32 -> fp16 bits, round to nearest even (the reference's dc_f32_to_f16 rule).

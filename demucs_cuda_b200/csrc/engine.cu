@@ -304,6 +304,7 @@ struct ConvW {             // B operand of a conv GEMM plus its epilogue constan
   int rows = 0;            // B rows (columns of the GEMM)
   int O = 0, C = 0, KH = 1, KW = 1, K = 0;
   float *bias = nullptr;
+  float *bias_x = nullptr; // transposed convs: bias per GEMM column (phase, channel)
   int glu_bn = 0;          // N tile of the GLU interleave (0 = plain)
   // the same rows in the TMA conv kernels' K order (kh, channel block, kw, channel), the
   // channels zero-padded to ncb blocks of 64
@@ -568,6 +569,11 @@ static bool load_convtr(Loader &L, Staging &st, const std::string &prefix, ConvW
   // the two taps run along H (frequency decoders) or W (time decoders)
   stage_tma_order(st, cw, ph, cw.rows, ld, axis_h ? 2 : 1, axis_h ? 1 : 2, C);
   stage_f32(st, b, &cw.bias);
+  // the bias per GEMM column (phase r, channel o)
+  std::vector<float> bx((size_t)O * S);
+  for (int r = 0; r < S; r++)
+    for (int o = 0; o < O; o++) bx[(size_t)r * O + o] = b[o];
+  stage_f32(st, bx, &cw.bias_x);
   return true;
 }
 

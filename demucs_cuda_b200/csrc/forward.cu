@@ -507,6 +507,7 @@ static bool convtr_half(const ConvW &cw, const Half16 &zh, bool axis_h, int S, i
   Epi e;
   e.mode = EPI_CONVTR;
   e.bias = cw.bias;
+  e.bias_x = cw.bias_x;
   e.act = gelu ? 1 : 0;
   e.y = y;
   e.oN2 = out.N2;

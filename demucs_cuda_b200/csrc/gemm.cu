@@ -1277,7 +1277,242 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
   }
 }
 
-template <int BN>
+// 16 consecutive column constants p[0..15] (16-byte aligned): four 16-byte loads of one
+// address per lane, served by the L1 broadcast
+static __device__ __forceinline__ void ld_cols16(const float *p, float (&d)[16]) {
+  const float4 *p4 = (const float4 *)p;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const float4 t = __ldg(p4 + j);
+    d[4 * j] = t.x;
+    d[4 * j + 1] = t.y;
+    d[4 * j + 2] = t.z;
+    d[4 * j + 3] = t.w;
+  }
+}
+
+// Specialised epilogue for the common layer shapes: every 16-column chunk is full (output
+// columns a multiple of 16), column constants come from 16-byte aligned arrays (a
+// transposed conv's bias expanded per (phase, channel) column), and the activation (ACT: 0
+// none, 1 GELU, 2 GLU, 3 GroupNorm + GLU + LayerScale residual) and the output geometry
+// (CT: 0 conv, 1 transposed conv along H, 2 along W) are compile-time.  The output value
+// y of a DConv residual layer (res + scale * value) is formed once and serves both the
+// fp16 channels-last copy and the fp32 NCHW output.  NCHW rows go through the warp's
+// transpose buffer as 16-byte stores when they are 16-byte aligned (e.y_al), else straight
+// from registers (lanes are consecutive positions, so each column is one coalesced store).
+template <int BN, int ACT, int CT>
+static __device__ __forceinline__ void ch_epi_fast(const ConvH &c, const Epi &e, uint32_t tacc,
+                                                   int warp, int lane, int64_t line, int wo0,
+                                                   int nt, float *wst) {
+  constexpr bool GLU = ACT >= 2;
+  const int quarter = warp & 3, half = warp >> 2;
+  const uint32_t trow = tacc + ((uint32_t)(quarter * 32) << 16);
+  const int ln = (int)line;
+  const int n = ln / c.Ho;
+  const int ho = ln - n * c.Ho;
+  const int n1 = n / e.oN2, n2 = n - n1 * e.oN2;
+  const int64_t base = (int64_t)n1 * e.oN1 + (int64_t)n2 * e.oN2s;
+  const int r = quarter * 32 + lane;
+  const int row_lim = c.Wo - wo0;
+  const bool rv = r < row_lim;
+  const int q = wo0 + r;
+  const int O = e.O;
+  const int ncols = GLU ? e.glu_half : BN;
+  const int per = ncols >= 32 ? ncols / 2 : (half == 0 ? ncols : 0);
+  const int cbeg = ncols >= 32 ? half * per : 0;
+  const int obase = (GLU ? nt * e.glu_half : nt * BN) + cbeg;
+  const int ncol_total = CT != 0 ? O * e.stride : O;
+  float gmu = 0.f, grs = 0.f;
+  if constexpr (ACT == 3) {
+    gmu = e.gn_mean[n];
+    grs = e.gn_rstd[n];
+  }
+  const int rq = 4 * (lane & 7);
+  const int rl = quarter * 32 + rq;  // first of this lane's 4 rows in the staged NCHW pass
+  int s0 = 0, o0 = obase;            // (phase, channel) of the chunk's first column
+  if constexpr (CT != 0) {
+    s0 = obase / O;
+    o0 = obase - s0 * O;
+  }
+  const float *cb = CT != 0 ? e.bias_x : e.bias;
+  for (int c0 = 0; c0 < per; c0 += 16) {
+    const int col0 = obase + c0;
+    if (col0 >= ncol_total) break;
+    float va[16], vb[16];
+    tmem_ld16(trow + cbeg + c0, va);
+    if constexpr (GLU) tmem_ld16(trow + e.glu_half + cbeg + c0, vb);
+    // this lane's output position for the chunk's phase
+    int h = ho, w = q;
+    bool tok = true;
+    if constexpr (CT == 1) {
+      h = ho * e.stride + s0 - e.crop;
+      tok = h >= 0 && h < e.out_len;
+    } else if constexpr (CT == 2) {
+      h = 0;
+      w = q * e.stride + s0 - e.crop;
+      tok = w >= 0 && w < e.out_len;
+    }
+    // skip connection of a decoder (transposed convs), laid out like y
+    float sk[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) sk[i] = 0.f;
+    if constexpr (CT != 0) {
+      if (e.hskip != nullptr && rv && tok) {
+        const float *sp = e.hskip + base + (int64_t)o0 * e.oC + (int64_t)h * e.oH + w;
+#pragma unroll
+        for (int i = 0; i < 16; i++) sk[i] = sp[(int64_t)i * e.oC];
+      }
+    }
+    float ka[16];
+    if (cb) {
+      ld_cols16(cb + col0, ka);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; i++) ka[i] = 0.f;
+    }
+    float v[16];
+    if constexpr (ACT == 2) {
+      float kb[16];
+      if (cb) {
+        ld_cols16(cb + O + col0, kb);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) kb[i] = 0.f;
+      }
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; i++) v[i] = (va[i] + ka[i]) * sigmoid_fast(vb[i] + kb[i]);
+    } else if constexpr (ACT == 3) {
+      // GroupNorm of the pre-GLU value: ((acc + bias) - mean) * rstd * g + beta, one GLU
+      // half at a time (register pressure)
+      float g[16], z[16];
+      ld_cols16(e.gn_w + col0, g);
+      ld_cols16(e.gn_b + col0, z);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; i++) va[i] = fmaf((va[i] + ka[i]) - gmu, g[i] * grs, z[i]);
+      ld_cols16(cb + O + col0, ka);
+      ld_cols16(e.gn_w + O + col0, g);
+      ld_cols16(e.gn_b + O + col0, z);
+#pragma unroll
+      for (int i = 0; i < 16; i++)
+        v[i] = va[i] * sigmoid_fast(fmaf((vb[i] + ka[i]) - gmu, g[i] * grs, z[i]));
+      // the residual (y itself, read before this thread's rows are rewritten)
+      if (rv) {
+        const float *sp = e.res + base + (int64_t)col0 * e.oC + (int64_t)ho * e.oH + q;
+#pragma unroll
+        for (int i = 0; i < 16; i++) sk[i] = sp[(int64_t)i * e.oC];
+      }
+    } else {
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        v[i] = va[i] + ka[i];
+        if constexpr (ACT == 1) v[i] = gelu_f(v[i]);
+      }
+    }
+    if constexpr (CT == 0 && ACT != 3) {
+      if (e.emb) {
+        float em[16];
+        ld_cols16(e.emb + (int64_t)ho * e.emb_ld + col0, em);
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = fmaf(e.emb_alpha, em[i], v[i]);
+      }
+    }
+    // output value: res + scale * value (ACT 3); the fp16 copy adds the skip
+    if constexpr (ACT == 3) {
+      float sc[16];
+      ld_cols16(e.scale + col0, sc);
+#pragma unroll
+      for (int i = 0; i < 16; i++) v[i] = fmaf(sc[i], v[i], sk[i]);
+    }
+    if (e.yh && rv && tok) {
+      float hv[16];
+#pragma unroll
+      for (int i = 0; i < 16; i++) hv[i] = ACT == 3 ? v[i] : v[i] + sk[i];
+      uint4 *d4 = (uint4 *)(e.yh + (((int64_t)n * e.yhH + h) * e.yhW + w) * e.yhC + o0);
+      d4[0] = make_uint4(pack_h2(hv[0], hv[1]), pack_h2(hv[2], hv[3]), pack_h2(hv[4], hv[5]),
+                         pack_h2(hv[6], hv[7]));
+      d4[1] = make_uint4(pack_h2(hv[8], hv[9]), pack_h2(hv[10], hv[11]),
+                         pack_h2(hv[12], hv[13]), pack_h2(hv[14], hv[15]));
+    }
+    if (e.y) {
+      if (CT != 2 && e.y_al) {
+        // 8 columns at a time through the transpose buffer: lane = (column, 4 rows)
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+#pragma unroll
+          for (int i = 0; i < 8; i++) wst[i * 32 + lane] = v[hh * 8 + i];
+          __syncwarp();
+#pragma unroll
+          for (int p = 0; p < 2; p++) {
+            const int cl = (lane >> 3) + 4 * p;
+            const int cc = hh * 8 + cl;
+            int64_t off;
+            bool ok = true;
+            if constexpr (CT == 0) {
+              off = base + (int64_t)(col0 + cc) * e.oC + (int64_t)ho * e.oH + wo0 + rl;
+            } else {
+              int o = o0 + cc, ss = s0;
+              if (o >= O) {
+                o -= O;
+                ss++;
+              }
+              const int t = ho * e.stride + ss - e.crop;
+              ok = t >= 0 && t < e.out_len;
+              off = base + (int64_t)o * e.oC + (int64_t)t * e.oH + wo0 + rl;
+            }
+            if (ok) {
+              const float4 v4 = *(const float4 *)(wst + cl * 32 + rq);
+              if (rl + 4 <= row_lim) {
+                *(float4 *)(e.y + off) = v4;
+              } else {
+                const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                  if (rl + i < row_lim) e.y[off + i] = vv[i];
+              }
+            }
+          }
+          __syncwarp();
+        }
+      } else if (rv) {
+        // lanes are consecutive positions: one coalesced store per column
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          if constexpr (CT == 0) {
+            e.y[base + (int64_t)(col0 + i) * e.oC + (int64_t)ho * e.oH + q] = v[i];
+          } else {
+            int o = o0 + i, ss = s0;
+            if (o >= O) {
+              o -= O;
+              ss++;
+            }
+            if constexpr (CT == 1) {
+              const int t = ho * e.stride + ss - e.crop;
+              if (t >= 0 && t < e.out_len)
+                e.y[base + (int64_t)o * e.oC + (int64_t)t * e.oH + q] = v[i];
+            } else {
+              const int t = q * e.stride + ss - e.crop;
+              if (t >= 0 && t < e.out_len)
+                e.y[base + (int64_t)o * e.oC + (int64_t)ho * e.oH + t] = v[i];
+            }
+          }
+        }
+      }
+    }
+    // next chunk's (phase, channel); O >= 16, so at most one wrap
+    o0 += 16;
+    if constexpr (CT != 0) {
+      if (o0 >= O) {
+        o0 -= O;
+        s0++;
+      }
+    }
+  }
+}
+
+template <int BN, int EK>
 __global__ void __launch_bounds__(kChThreads, 2)
     k_conv_h(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
              const ConvH c, const Epi e) {
@@ -1336,7 +1571,7 @@ __global__ void __launch_bounds__(kChThreads, 2)
         const int ho = (int)(line - n * c.Ho);
         for (int kb = 0; kb < c.nkb; kb++, it++) {
           const int st = (int)(it % (uint32_t)stages);
-          if (!mbar_wait(&empty[st], ((it / (uint32_t)stages) & 1u) ^ 1u, kFaultEmpty)) {
+          if (!mbar_wait_sleep(&empty[st], ((it / (uint32_t)stages) & 1u) ^ 1u, kFaultEmpty)) {
             ok = false;
             break;
           }
@@ -1365,12 +1600,12 @@ __global__ void __launch_bounds__(kChThreads, 2)
       bool ok = true;
       for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x, local++) {
         const uint32_t buf = local & 1u, use = local >> 1;
-        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
+        if (!mbar_wait_sleep(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * (uint32_t)Cfg::kAccCols;
         for (int kb = 0; kb < c.nkb; kb++, it++) {
           const int st = (int)(it % (uint32_t)stages);
-          if (!mbar_wait(&full[st], (it / (uint32_t)stages) & 1u, kFaultFull)) {
+          if (!mbar_wait_sleep(&full[st], (it / (uint32_t)stages) & 1u, kFaultFull)) {
             ok = false;
             break;
           }
@@ -1397,10 +1632,16 @@ __global__ void __launch_bounds__(kChThreads, 2)
       int wo0, nt;
       ch_tile(c, tile, line, wo0, nt);
       const uint32_t buf = local & 1u, use = local >> 1;
-      if (!mbar_wait(&acc_full[buf], use & 1u, kFaultDone)) break;
+      if (!mbar_wait_sleep(&acc_full[buf], use & 1u, kFaultDone)) break;
       tc_fence_after();
-      ch_epilogue<BN>(c, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp, lane, line, wo0, nt,
-                      wst);
+      // EK 0: generic epilogue; else the specialised one for ACT = (EK - 1) % 4 and
+      // output geometry CT = (EK - 1) / 4
+      if constexpr (EK == 0)
+        ch_epilogue<BN>(c, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp, lane, line, wo0, nt,
+                        wst);
+      else
+        ch_epi_fast<BN, (EK - 1) % 4, (EK - 1) / 4>(
+            c, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp, lane, line, wo0, nt, wst);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -1785,8 +2026,9 @@ static bool encode_half(CUtensorMap *map, const HalfAct &x, bool w4) {
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
-static void launch_conv_h(const CUtensorMap &ta, const CUtensorMap &tb, ConvH c, const Epi &e) {
+template <int BN, int EK>
+static void launch_conv_h_k(const CUtensorMap &ta, const CUtensorMap &tb, ConvH c,
+                            const Epi &e) {
   using Cfg = ChCfg<BN>;
   // two CTAs per SM when the accumulators fit (<= 256 TMEM columns each)
   const bool two = Cfg::kTmemCols <= 256;
@@ -1799,15 +2041,64 @@ static void launch_conv_h(const CUtensorMap &ta, const CUtensorMap &tb, ConvH c,
   const size_t smem = fixed + (size_t)stages * (Cfg::kStage + 16);
   static size_t attr = 0;
   if (smem > attr) {
-    DCB_CUDA(cudaFuncSetAttribute(k_conv_h<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)smem));
+    DCB_CUDA(cudaFuncSetAttribute(k_conv_h<BN, EK>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr = smem;
   }
   const int64_t tiles = c.lines * c.tpl * c.ntiles;
   const int64_t slots = (two ? 2 : 1) * (int64_t)sm_count();
   const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
-  k_conv_h<BN><<<grid, kChThreads, smem, stream()>>>(ta, tb, c, e);
+  k_conv_h<BN, EK><<<grid, kChThreads, smem, stream()>>>(ta, tb, c, e);
   DCB_LAUNCHED();
+}
+
+template <int BN>
+static void launch_conv_h(const CUtensorMap &ta, const CUtensorMap &tb, ConvH c, const Epi &e,
+                          int ek) {
+  switch (ek) {
+    case 1: launch_conv_h_k<BN, 1>(ta, tb, c, e); break;
+    case 2: launch_conv_h_k<BN, 2>(ta, tb, c, e); break;
+    case 3: launch_conv_h_k<BN, 3>(ta, tb, c, e); break;
+    case 4: launch_conv_h_k<BN, 4>(ta, tb, c, e); break;
+    case 5: launch_conv_h_k<BN, 5>(ta, tb, c, e); break;
+    case 6: launch_conv_h_k<BN, 6>(ta, tb, c, e); break;
+    case 9: launch_conv_h_k<BN, 9>(ta, tb, c, e); break;
+    case 10: launch_conv_h_k<BN, 10>(ta, tb, c, e); break;
+    default: launch_conv_h_k<BN, 0>(ta, tb, c, e); break;
+  }
+}
+
+// Epilogue kind of a channels-last conv: 0 = the generic epilogue, else 1 + ACT + 4 * CT
+// for the specialised one when its layout conditions hold (see ch_epi_fast); also sets
+// e.y_al when the NCHW rows take 16-byte stores.
+static int conv_epi_kind(Epi &e, int bn) {
+  const bool tr = e.mode == EPI_CONVTR;
+  const int act = e.act;
+  const int O = e.O;
+  e.y_al = 0;
+  if (e.y && al16(e.y) && e.oC % 4 == 0 && e.oH % 4 == 0 && e.oN1 % 4 == 0 &&
+      e.oN2s % 4 == 0)
+    e.y_al = 1;
+  if (tr) {
+    if (act > 1 || e.res || O < 16 || (O * e.stride) % 16 != 0) return 0;
+    if (e.yh && O % 16 != 0) return 0;
+    if (e.hskip && (!e.yh || O % 16 != 0)) return 0;  // skip rows are read 16 channels at a time
+    if (e.bias && (!e.bias_x || !al16(e.bias_x))) return 0;
+    if (e.emb) return 0;
+    return 1 + act + 4 * (e.axis_h ? 1 : 2);
+  }
+  if (O % 16 != 0 || e.hskip) return 0;
+  if (act >= 2 && (bn / 2) % 16 != 0) return 0;
+  if (e.bias && !al16(e.bias)) return 0;
+  if (e.emb && (act == 3 || !al16(e.emb) || e.emb_ld % 4 != 0)) return 0;
+  if (act == 3) {
+    if (!e.bias || !e.res || !e.scale || !e.gn_w || !e.gn_b || !al16(e.gn_w) ||
+        !al16(e.gn_b) || !al16(e.scale))
+      return 0;
+  } else if (e.res) {
+    return 0;
+  }
+  return 1 + act;
 }
 
 bool conv_half(const HalfAct &x, int KH, int KW, int SH, int SW, int PH, int PW, int DH, int DW,
@@ -1855,11 +2146,12 @@ bool conv_half(const HalfAct &x, int KH, int KW, int SH, int SW, int PH, int PW,
     TraceScope ts(e.mode == EPI_CONVTR ? TR_CONVTR : TR_CONV, 2.0 * M * n_alg * Kt,
                   (double)x.images * x.H * x.W * x.C * 2.0 + n_alg * Kt * 2.0 + out_b, M,
                   (int64_t)n_alg, Kt);
+    const int ek = g_opt_generic_epi ? 0 : conv_epi_kind(e2, bn);
     switch (bn) {
-      case 32: launch_conv_h<32>(ta, tb, c, e2); break;
-      case 64: launch_conv_h<64>(ta, tb, c, e2); break;
-      case 128: launch_conv_h<128>(ta, tb, c, e2); break;
-      default: launch_conv_h<256>(ta, tb, c, e2); break;
+      case 32: launch_conv_h<32>(ta, tb, c, e2, ek); break;
+      case 64: launch_conv_h<64>(ta, tb, c, e2, ek); break;
+      case 128: launch_conv_h<128>(ta, tb, c, e2, ek); break;
+      default: launch_conv_h<256>(ta, tb, c, e2, ek); break;
     }
   }
   return true;

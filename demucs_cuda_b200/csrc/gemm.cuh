@@ -36,6 +36,10 @@ struct Epi {
   int mode = EPI_GEMM;
   int vec = 0;  // 16-column vector stores allowed (set by the launcher after checks)
   const float *bias = nullptr;
+  // EPI_CONVTR: the bias per GEMM column (phase, channel), 16-byte aligned (the
+  // specialised channels-last epilogue reads it; null: bias[channel])
+  const float *bias_x = nullptr;
+  int y_al = 0;  // NCHW rows of y are 16-byte aligned (set by the channels-last launcher)
   int act = 0;  // 0 none, 1 gelu, 2 glu, 3 GroupNorm + glu (EPI_CONV)
   // EPI_GEMM
   float *C = nullptr;

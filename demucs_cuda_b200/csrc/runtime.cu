@@ -22,6 +22,7 @@ static thread_local char g_err[1024] = "";
 static std::atomic<uint64_t> g_launches{0};
 int g_opt_simt = 0;
 int g_opt_graphs = 0;
+int g_opt_generic_epi = 0;
 
 void fail(const char *fmt, ...) {
   char msg[1024];
@@ -234,6 +235,9 @@ int dcb_set_option(const char *name, int value) {
   } else if (!strcmp(name, "graphs")) {
     old = g_opt_graphs;
     g_opt_graphs = value;
+  } else if (!strcmp(name, "generic_epilogue")) {
+    old = g_opt_generic_epi;
+    g_opt_generic_epi = value;
   } else {
     fail("unknown option '%s'", name);
   }

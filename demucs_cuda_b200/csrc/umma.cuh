@@ -55,6 +55,19 @@ static __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) 
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: a waiting thread sleeps (up to the hint, in ns) until
+// the phase completes instead of re-polling, leaving issue slots to the working warps
+static __device__ __forceinline__ bool mbar_try_sleep(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
+      : "memory");
+  return ok != 0;
+}
 static __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -73,6 +86,23 @@ static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
   for (uint32_t i = 1;; i++) {
     if (mbar_try(bar, parity)) return true;
     if ((i & 255u) == 0) {
+      if (fault_pending()) return false;
+      if (global_ns() - t0 > kWaitNs) {
+        atomicOr(&g_dev_fault, fault);
+        return false;
+      }
+    }
+  }
+}
+
+// mbar_wait through mbar_try_sleep (same bound and fault protocol)
+static __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity,
+                                                       uint32_t fault) {
+  if (mbar_try_sleep(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; i++) {
+    if (mbar_try_sleep(bar, parity)) return true;
+    if ((i & 15u) == 0) {
       if (fault_pending()) return false;
       if (global_ns() - t0 > kWaitNs) {
         atomicOr(&g_dev_fault, fault);

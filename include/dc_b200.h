@@ -189,7 +189,9 @@ void dcb_set_stream(void *stream);
 void dcb_use_own_stream(void);
 void *dcb_get_stream(void);
 /* Backend options: "simt" (1 = CUDA-core kernels instead of tcgen05, for A/B checks),
- * "graphs" (1 = replay captured CUDA graphs for repeated forwards). Returns the old value. */
+ * "graphs" (1 = replay captured CUDA graphs for repeated forwards), "generic_epilogue"
+ * (1 = channels-last convs use their generic epilogue instead of the specialised ones, for
+ * A/B checks). Returns the old value. */
 int dcb_set_option(const char *name, int value);
 /* Number of this library's kernels launched so far (monotonic). */
 uint64_t dcb_kernel_launches(void);

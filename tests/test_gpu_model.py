@@ -109,6 +109,42 @@ def test_short_stages_teacher_forced(short):
     _teacher_forced(short)
 
 
+def test_short_specialised_epilogue_matches_generic(short):
+    """The channels-last convs' specialised epilogues (compile-time activation and output
+    geometry, vector column constants) give the generic epilogue's result: every
+    teacher-forced stage agrees to fp32 rounding (fused multiply-adds round differently,
+    which can move an fp16 companion element by one unit), and the end-to-end stems agree
+    well inside the fp16 noise of the path."""
+    import demucs_cuda_b200 as dcb
+    torch = short["torch"]
+    m, R = short["model"], short["ref"]
+
+    def run():
+        out = {"stems": m.forward(_t(torch, short["mix"])).cpu().numpy()}
+        for i in range(4):
+            xin = R["x_norm"] if i == 0 else R[f"enc_{i - 1}"]
+            out[f"enc_{i}"] = m.stage_encoder(0, i, _t(torch, xin)).cpu().numpy()
+            tin = R["xt_norm"] if i == 0 else R[f"tenc_{i - 1}"]
+            out[f"tenc_{i}"] = m.stage_encoder(1, i, _t(torch, tin)).cpu().numpy()
+            xin = R["transformer_x"] if i == 0 else R[f"dec_{i - 1}"]
+            out[f"dec_{i}"] = m.stage_decoder(0, i, _t(torch, xin),
+                                              _t(torch, R[f"enc_{3 - i}"])).cpu().numpy()
+        return out
+
+    fast = run()
+    old = dcb.set_option("generic_epilogue", 1)
+    try:
+        generic = run()
+    finally:
+        dcb.set_option("generic_epilogue", old)
+    errs = {k: rel_l2(fast[k], generic[k]) for k in fast}
+    for k, v in errs.items():
+        print(f"  specialised vs generic {k:8s} {v:.3e}")
+    assert errs.pop("stems") < 2e-4
+    assert max(errs.values()) < 3e-5, errs
+    assert dcb.device_fault() == 0
+
+
 def test_tiny_batch_consistency(tiny):
     """A batch of segments gives each segment the result it gets alone (per-segment
     normalisation and every kernel are per sample)."""
