@@ -256,7 +256,116 @@ static __device__ __forceinline__ void tile_coords(const Shape &s, int64_t tile,
 // Rows r >= row_lim of the tile are outside the output.  EPI_CONV goes through `wst`, this
 // warp's [CW columns][32 rows] transpose buffer, so that lane l stores rows 4(l & 7)..+3 of
 // one channel with a 16-byte store; other modes store per row (store_chunk16).
-template <int BN, int NW, int CW>
+// 16 consecutive column constants p[0..15] (16-byte aligned): four 16-byte loads of one
+// address per lane, served by the L1 broadcast
+static __device__ __forceinline__ void ld_cols16(const float *p, float (&d)[16]) {
+  const float4 *p4 = (const float4 *)p;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const float4 t = __ldg(p4 + j);
+    d[4 * j] = t.x;
+    d[4 * j + 1] = t.y;
+    d[4 * j + 2] = t.z;
+    d[4 * j + 3] = t.w;
+  }
+}
+
+// Row-mode epilogue (EPI_ROWS_F32 / EPI_ROWS_F16 / EPI_HEADS) for 16-byte aligned outputs
+// and column constants (e.cvec, checked on the host): bias / gamma and the residual row
+// are loaded while the accumulator load is in flight.
+template <int BN, int NW>
+static __device__ __forceinline__ void rows_epi_fast(const Shape &s, const Epi &e,
+                                                     uint32_t trow, int half, int r, int64_t m,
+                                                     int n0, int row_lim) {
+  const bool mv = r < row_lim;
+  const RowInfo ri = mv ? decode_row(e, m) : RowInfo{0, 0, 0, 0, 0};
+  constexpr int PER = NW == 8 ? (BN / 2 < 16 ? 16 : BN / 2) : BN;
+  const int cbeg = NW == 8 ? half * PER : 0;
+  for (int c0 = cbeg; c0 < cbeg + PER && c0 < BN; c0 += 16) {
+    const int64_t n = (int64_t)n0 + c0;
+    if (n >= s.N) break;
+    float v[16], bb[16];
+    tmem_ld16(trow + c0, v);
+    if (e.bias) {
+      ld_cols16(e.bias + n, bb);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; i++) bb[i] = 0.f;
+    }
+    if (e.mode == EPI_ROWS_F32) {
+      float rr[16], gg[16];
+      if (e.res) {
+        ld_cols16(e.gamma + n, gg);
+        if (mv) {
+          const float4 *rp = (const float4 *)(e.res + m * e.ldr + n);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const float4 t = rp[j];
+            rr[4 * j] = t.x;
+            rr[4 * j + 1] = t.y;
+            rr[4 * j + 2] = t.z;
+            rr[4 * j + 3] = t.w;
+          }
+        }
+      }
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; i++) v[i] += bb[i];
+      if (e.act == 1) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = gelu_f(v[i]);
+      }
+      if (e.res) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = fmaf(gg[i], v[i], rr[i]);
+      }
+      if (mv) {
+        float4 *op = (float4 *)((float *)e.out + m * e.ldo + n);
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          op[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      }
+    } else {
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; i++) v[i] += bb[i];
+      if (e.act == 1) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = gelu_f(v[i]);
+      }
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) w[i] = pack_h2(v[2 * i], v[2 * i + 1]);
+      if (mv) {
+        uint16_t *dst;
+        if (e.mode == EPI_ROWS_F16) {
+          dst = (uint16_t *)e.out + m * e.ldo + n;
+        } else {
+          // EPI_HEADS: a 16-column chunk lies inside one section and one head
+          const int sec = (int)(n / e.sec_cols);
+          const int cc = (int)(n - (int64_t)sec * e.sec_cols);
+          const int h = cc / e.hd, d0 = cc - h * e.hd;
+          const int64_t bh = (int64_t)ri.b * e.heads + h;
+          if (e.sec_layout[sec] != 0) {
+            uint16_t *col = e.sec_ptr[sec] + (bh * e.hd + d0) * e.Tp + ri.t;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              col[(2 * i) * e.Tp] = (uint16_t)(w[i] & 0xffffu);
+              col[(2 * i + 1) * e.Tp] = (uint16_t)(w[i] >> 16);
+            }
+            continue;
+          }
+          dst = e.sec_ptr[sec] + (bh * e.T + ri.t) * e.hd + d0;
+        }
+        uint4 *dp = (uint4 *)dst;
+        dp[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dp[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    }
+  }
+}
+
+template <int BN, int NW, int CW, int EK>
 static __device__ __forceinline__ void epilogue_tile(const Shape &s, const Epi &e, uint32_t tacc,
                                                      int warp, int lane, int bz, int64_t m0,
                                                      int nt, int row_lim, float *wst) {
@@ -265,7 +374,9 @@ static __device__ __forceinline__ void epilogue_tile(const Shape &s, const Epi &
   const uint32_t trow = tacc + ((uint32_t)(quarter * 32) << 16);
   const int n0 = nt * BN;
   const int64_t m = m0 + r;
-  if (e.mode == EPI_CONV && wst) {
+  if constexpr (EK == 1) {
+    rows_epi_fast<BN, NW>(s, e, trow, half, r, m, n0, row_lim);
+  } else if (e.mode == EPI_CONV && wst) {
     const int rq = 4 * (lane & 7);
     int64_t poff[4];
     bool pv[4];
@@ -372,7 +483,7 @@ static __device__ __forceinline__ void epilogue_tile(const Shape &s, const Epi &
   }
 }
 
-template <int BN, bool GATHER>
+template <int BN, bool GATHER, int EK>
 __global__ void __launch_bounds__(kThreads, 2)
     k_umma(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
            const Shape s, const Gather g, const Epi e) {
@@ -451,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int kb = 0; kb < s.nkb; kb++, it++) {
           const int st = (int)(it % (uint32_t)stages);
           const uint32_t ph = (it / (uint32_t)stages) & 1u;
-          if (!mbar_wait(&empty[st], ph ^ 1u, kFaultEmpty)) {
+          if (!mbar_wait_sleep(&empty[st], ph ^ 1u, kFaultEmpty)) {
             ok = false;
             break;
           }
@@ -470,13 +581,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x, local++) {
         const uint32_t buf = local % (uint32_t)Cfg::kBufs;
         const uint32_t use = local / (uint32_t)Cfg::kBufs;
-        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
+        if (!mbar_wait_sleep(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * (uint32_t)Cfg::kAccCols;
         for (int kb = 0; kb < s.nkb; kb++, it++) {
           const int st = (int)(it % (uint32_t)stages);
           const uint32_t ph = (it / (uint32_t)stages) & 1u;
-          if (!mbar_wait(&full[st], ph, kFaultFull)) {
+          if (!mbar_wait_sleep(&full[st], ph, kFaultFull)) {
             ok = false;
             break;
           }
@@ -522,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int kb = 0; kb < s.nkb; kb++, it++) {
         const int st = (int)(it % (uint32_t)stages);
         const uint32_t ph = (it / (uint32_t)stages) & 1u;
-        if (!mbar_wait(&empty[st], ph ^ 1u, kFaultEmpty)) {
+        if (!mbar_wait_sleep(&empty[st], ph ^ 1u, kFaultEmpty)) {
           ok = false;
           break;
         }
@@ -569,10 +680,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       tile_coords(s, tile, bz, m0, nt);
       const uint32_t buf = local % (uint32_t)Cfg::kBufs;
       const uint32_t use = local / (uint32_t)Cfg::kBufs;
-      if (!mbar_wait(&acc_full[buf], use & 1u, kFaultDone)) break;
+      if (!mbar_wait_sleep(&acc_full[buf], use & 1u, kFaultDone)) break;
       tc_fence_after();
       const int64_t left = (int64_t)s.M - m0;
-      epilogue_tile<BN, Cfg::kEpiWarps, 32>(s, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp,
+      epilogue_tile<BN, Cfg::kEpiWarps, 32, EK>(s, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp,
                                             lane, bz, m0, nt, left < kBM ? (int)left : kBM,
                                             GATHER ? wst : nullptr);
       // this warp's TMEM reads are complete: release the accumulator buffer
@@ -1277,20 +1388,6 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
   }
 }
 
-// 16 consecutive column constants p[0..15] (16-byte aligned): four 16-byte loads of one
-// address per lane, served by the L1 broadcast
-static __device__ __forceinline__ void ld_cols16(const float *p, float (&d)[16]) {
-  const float4 *p4 = (const float4 *)p;
-#pragma unroll
-  for (int j = 0; j < 4; j++) {
-    const float4 t = __ldg(p4 + j);
-    d[4 * j] = t.x;
-    d[4 * j + 1] = t.y;
-    d[4 * j + 2] = t.z;
-    d[4 * j + 3] = t.w;
-  }
-}
-
 // Specialised epilogue for the common layer shapes: every 16-column chunk is full (output
 // columns a multiple of 16), column constants come from 16-byte aligned arrays (a
 // transposed conv's bias expanded per (phase, channel) column), and the activation (ACT: 0
@@ -1807,7 +1904,7 @@ static int sm_count() {
   return n[dev];
 }
 
-template <int BN, bool GATHER>
+template <int BN, bool GATHER, int EK>
 static void launch_umma(const CUtensorMap &ta, const CUtensorMap &tb, Shape s, const Gather &g,
                         const Epi &e, int64_t mtiles, int ntiles, int64_t batch) {
   using Cfg = UmmaCfg<BN, GATHER>;
@@ -1826,7 +1923,7 @@ static void launch_umma(const CUtensorMap &ta, const CUtensorMap &tb, Shape s, c
   DCB_REQUIRE(smem <= 226 * 1024, "gemm: shared memory %zu exceeds the per-CTA limit", smem);
   static size_t attr = 0;  // dynamic shared memory opted in so far for this instantiation
   if (smem > attr) {
-    DCB_CUDA(cudaFuncSetAttribute(k_umma<BN, GATHER>,
+    DCB_CUDA(cudaFuncSetAttribute(k_umma<BN, GATHER, EK>,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr = smem;
   }
@@ -1837,7 +1934,7 @@ static void launch_umma(const CUtensorMap &ta, const CUtensorMap &tb, Shape s, c
   const int64_t tiles = mtiles * ntiles * batch;
   const int64_t slots = 2ll * sm_count();
   const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
-  k_umma<BN, GATHER><<<grid, kThreads, smem, stream()>>>(ta, tb, s, g, e);
+  k_umma<BN, GATHER, EK><<<grid, kThreads, smem, stream()>>>(ta, tb, s, g, e);
   DCB_LAUNCHED();
 }
 
@@ -1846,15 +1943,26 @@ static void dispatch_umma(int bn, const CUtensorMap &ta, const CUtensorMap &tb, 
                           const Gather &g, const Epi &e, int64_t batch) {
   const int64_t mt = (s.M + kBM - 1) / kBM;
   const int ntl = (int)((s.N + bn - 1) / bn);
+  if constexpr (!GATHER) {
+    if (e.cvec) {
+      switch (bn) {
+        case 32: launch_umma<32, false, 1>(ta, tb, s, g, e, mt, ntl, batch); break;
+        case 64: launch_umma<64, false, 1>(ta, tb, s, g, e, mt, ntl, batch); break;
+        case 128: launch_umma<128, false, 1>(ta, tb, s, g, e, mt, ntl, batch); break;
+        default: launch_umma<256, false, 1>(ta, tb, s, g, e, mt, ntl, batch); break;
+      }
+      return;
+    }
+  }
   switch (bn) {
-    case 32: launch_umma<32, GATHER>(ta, tb, s, g, e, mt, ntl, batch); break;
-    case 64: launch_umma<64, GATHER>(ta, tb, s, g, e, mt, ntl, batch); break;
-    case 128: launch_umma<128, GATHER>(ta, tb, s, g, e, mt, ntl, batch); break;
+    case 32: launch_umma<32, GATHER, 0>(ta, tb, s, g, e, mt, ntl, batch); break;
+    case 64: launch_umma<64, GATHER, 0>(ta, tb, s, g, e, mt, ntl, batch); break;
+    case 128: launch_umma<128, GATHER, 0>(ta, tb, s, g, e, mt, ntl, batch); break;
     default:
       if constexpr (GATHER) {
         DCB_REQUIRE(false, "conv: N tile %d is wider than the gather kernel's 128", bn);
       } else {
-        launch_umma<256, GATHER>(ta, tb, s, g, e, mt, ntl, batch);
+        launch_umma<256, GATHER, 0>(ta, tb, s, g, e, mt, ntl, batch);
       }
       break;
   }
@@ -1913,6 +2021,10 @@ void gemm_rows_launch(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t
     if (ok) {
       Epi ev = e;
       ev.vec = vec_ok(e, N) ? 1 : 0;
+      ev.cvec = ev.vec && !g_opt_generic_epi && (!e.bias || al16(e.bias)) &&
+                (!e.res || (e.gamma && al16(e.gamma)))
+                    ? 1
+                    : 0;
       dispatch_umma<false>(bn, ta, tb, s, g, ev, batch);
       return;
     }

@@ -40,6 +40,7 @@ struct Epi {
   // specialised channels-last epilogue reads it; null: bias[channel])
   const float *bias_x = nullptr;
   int y_al = 0;  // NCHW rows of y are 16-byte aligned (set by the channels-last launcher)
+  int cvec = 0;  // row modes: vector stores and 16-byte aligned column constants (launcher)
   int act = 0;  // 0 none, 1 gelu, 2 glu, 3 GroupNorm + glu (EPI_CONV)
   // EPI_GEMM
   float *C = nullptr;

@@ -110,8 +110,9 @@ def test_short_stages_teacher_forced(short):
 
 
 def test_short_specialised_epilogue_matches_generic(short):
-    """The channels-last convs' specialised epilogues (compile-time activation and output
-    geometry, vector column constants) give the generic epilogue's result: every
+    """The specialised epilogues (channels-last convs: compile-time activation and output
+    geometry, vector column constants; row-mode GEMMs: vector bias / gamma / residual
+    loads) give the generic epilogues' result: every
     teacher-forced stage agrees to fp32 rounding (fused multiply-adds round differently,
     which can move an fp16 companion element by one unit), and the end-to-end stems agree
     well inside the fp16 noise of the path."""
@@ -129,6 +130,9 @@ def test_short_specialised_epilogue_matches_generic(short):
             xin = R["transformer_x"] if i == 0 else R[f"dec_{i - 1}"]
             out[f"dec_{i}"] = m.stage_decoder(0, i, _t(torch, xin),
                                               _t(torch, R[f"enc_{3 - i}"])).cpu().numpy()
+        x, xt = m.stage_transformer(_t(torch, R["enc_3"]), _t(torch, R["tenc_3"]))
+        out["transformer_x"] = x.cpu().numpy()
+        out["transformer_xt"] = xt.cpu().numpy()
         return out
 
     fast = run()
