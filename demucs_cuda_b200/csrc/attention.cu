@@ -3,19 +3,23 @@
 // [GEMM S = Q K^T -> dk_softmax_to_half -> GEMM O = P V] loop (ops.c:390-443,
 // attn.cu:26-89).
 //
-// CTA = 128 query rows of one head, 192 threads, key blocks of 64:
+// CTA = 128 query rows of one head, 224 threads, key blocks of 64:
 //   warps 0-3  one query row per thread: read the 64 scores of a key block from TMEM once,
 //              online softmax in fp32 (exp2 domain, running max / sum; the O accumulator
 //              stays in TMEM and is rescaled there only when the maximum grows by more
 //              than 2^8), write P as fp16 into shared memory in the UMMA A-operand layout;
-//   warp 4     TMA producer: Q once, then K and V^T blocks into a 3-stage ring;
-//   warp 5     TMEM owner; lane 0 issues S = Q K^T (M=128, N=64, K=64) into one of two
-//              TMEM score buffers and O += P V (M=128, N=64, K=64) from one of two P
-//              buffers, so the scores of block j+1 (and j+2) are computed while the
-//              softmax warps work on block j.
-// TMEM: S0 | S1 | O (64 columns each, 256 allocated); 97 KB of shared memory: two CTAs
-// share an SM.  Head dims up to 64 are zero-extended to 64 by TMA out-of-bounds fill; keys
-// past Tk read as zero and are masked out of the softmax.
+//   warp 4     TMA producer: Q once, then K blocks into a 4-stage ring (a stage is free
+//              once S of its block has completed);
+//   warp 6     TMA producer: V^T blocks into a 3-stage ring (free once P V of its block
+//              has completed);
+//   warp 5     TMEM owner; lane 0 issues S = Q K^T (M=128, N=64, K=hd) into one of two
+//              TMEM score buffers and O += P V (M=128, N=hd, K=64) from one of two P
+//              buffers.  S(j+2) is issued as soon as the softmax warps have read S(j) out
+//              of TMEM (s_empty), so it runs while they exponentiate block j.
+// TMEM: S0 | S1 | O | row sums (64 + 64 + 64 + 16 columns, 256 allocated); 107 KB of
+// shared memory: two CTAs share an SM.  Head dims up to 64 are zero-extended to a multiple of 16 (the MMA K of
+// S and N of P V) by TMA out-of-bounds fill; keys past Tk read as zero and are masked out
+// of the softmax.
 //
 // Inputs are fp16 exactly as the reference rounds them (split_heads of the fp32
 // projections): Q [BH][Tq][hd], K [BH][Tk][hd], V^T [BH][hd][Tkp].  The reference rounds
@@ -28,14 +32,18 @@
 
 namespace dcb {
 
-constexpr int kAttnThreads = 192;
+constexpr int kAttnThreads = 224;
 constexpr int kQ = 128, kKV = 64, kHD = 64;
 constexpr uint32_t kQBytes = kQ * kHD * 2;      // 16 KB
 constexpr uint32_t kKBytes = kKV * kHD * 2;     // 8 KB
 constexpr uint32_t kVBytes = kHD * kKV * 2;     // 8 KB
 constexpr uint32_t kPBytes = kQ * kKV * 2;      // 16 KB per buffer
-constexpr int kAttnStages = 3;
-constexpr size_t kAttnSmem = kQBytes + kAttnStages * (kKBytes + kVBytes) + 2 * kPBytes + 256;
+constexpr int kKStages = 4, kVStages = 3;  // K is released after S, V only after P V
+constexpr uint32_t kOnesBytes = 16 * kKV * 2;  // 16 x 64 fp16 ones: the row-sum operand
+constexpr size_t kAttnSmem =
+    kQBytes + kKStages * kKBytes + kVStages * kVBytes + 2 * kPBytes + kOnesBytes + 256;
+constexpr int kSumCol = 64;       // TMEM column (after O) of the row sums of P
+constexpr float kLazyLog2 = 2.0f; // rescale when a block maximum exceeds the running one by 4x
 
 struct AttnArgs {
   int Tq, Tk, H, hd, BH;
@@ -45,6 +53,13 @@ struct AttnArgs {
 };
 
 
+// 2^x of two fp16 values (PTX ex2.approx.f16x2)
+static __device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
 __global__ void __launch_bounds__(kAttnThreads, 2)
     k_flash_attn(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
@@ -53,15 +68,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *sQ = smem;
   uint8_t *sK = sQ + kQBytes;
-  uint8_t *sV = sK + kAttnStages * kKBytes;
-  uint8_t *sP = sV + kAttnStages * kVBytes;
-  uint64_t *bar = (uint64_t *)(sP + 2 * kPBytes);
+  uint8_t *sV = sK + kKStages * kKBytes;
+  uint8_t *sP = sV + kVStages * kVBytes;
+  uint8_t *sOnes = sP + 2 * kPBytes;
+  uint64_t *bar = (uint64_t *)(sOnes + kOnesBytes);
   uint64_t *q_full = bar;
-  uint64_t *kv_full = bar + 1;                 // [stages]
-  uint64_t *kv_empty = kv_full + kAttnStages;  // [stages]
-  uint64_t *s_full = kv_empty + kAttnStages;   // [2] score buffers
-  uint64_t *p_full = s_full + 2;               // [2] P buffers written
-  uint64_t *p_empty = p_full + 2;              // [2] PV of a P buffer complete
+  uint64_t *k_full = bar + 1;              // [kKStages]
+  uint64_t *k_empty = k_full + kKStages;   // [kKStages]
+  uint64_t *v_full = k_empty + kKStages;   // [kVStages]
+  uint64_t *v_empty = v_full + kVStages;   // [kVStages]
+  uint64_t *s_full = v_empty + kVStages;   // [2] score buffers computed
+  uint64_t *s_empty = s_full + 2;          // [2] score buffers read by the softmax warps
+  uint64_t *p_full = s_empty + 2;          // [2] P buffers written
+  uint64_t *p_empty = p_full + 2;          // [2] PV of a P buffer complete
   uint64_t *o_full = p_empty + 2;
   uint32_t *tslot = (uint32_t *)(o_full + 1);
   uint32_t *s_abort = tslot + 1;
@@ -84,12 +103,17 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < kAttnStages; i++) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+    for (int i = 0; i < kKStages; i++) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < kVStages; i++) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&p_empty[i], 1);
     }
@@ -99,6 +123,13 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   if (warp == 5) {
     tmem_alloc(tslot, 256);
     tmem_relinquish();
+  }
+  if (threadIdx.x < kOnesBytes / 16) {
+    // fp16 1.0 everywhere (the swizzled layout of a constant tile is the tile itself),
+    // published to the tensor core's async proxy
+    st_shared_v4(smem_u32(sOnes) + threadIdx.x * 16, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u,
+                 0x3C003C00u);
+    fence_async_smem();
   }
   tc_fence_before();
   __syncthreads();
@@ -110,66 +141,92 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
       mbar_expect_tx(q_full, kQBytes);
       tma_load_3d(sQ, &tmQ, q_full, 0, q0, bh);
       for (int j = 0; j < nkv; j++) {
-        const int st = j % kAttnStages;
-        const uint32_t ph = (uint32_t)(j / kAttnStages) & 1u;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1u, kFaultAttn)) break;
-        mbar_expect_tx(&kv_full[st], kKBytes + kVBytes);
-        tma_load_3d(sK + st * kKBytes, &tmK, &kv_full[st], 0, j * kKV, bh);
-        tma_load_3d(sV + st * kVBytes, &tmV, &kv_full[st], j * kKV, 0, bh);
+        const int st = j % kKStages;
+        const uint32_t ph = (uint32_t)(j / kKStages) & 1u;
+        if (!mbar_wait_sleep(&k_empty[st], ph ^ 1u, kFaultAttn)) break;
+        mbar_expect_tx(&k_full[st], kKBytes);
+        tma_load_3d(sK + st * kKBytes, &tmK, &k_full[st], 0, j * kKV, bh);
+      }
+    }
+  } else if (warp == 6) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmV);
+      for (int j = 0; j < nkv; j++) {
+        const int st = j % kVStages;
+        const uint32_t ph = (uint32_t)(j / kVStages) & 1u;
+        if (!mbar_wait_sleep(&v_empty[st], ph ^ 1u, kFaultAttn)) break;
+        mbar_expect_tx(&v_full[st], kVBytes);
+        tma_load_3d(sV + st * kVBytes, &tmV, &v_full[st], j * kKV, 0, bh);
       }
     }
   } else if (warp == 5) {
     if (lane == 0) {
+      // the head dim rounded up to the MMA granule: K steps of S, N of P V
+      const int hd16 = (a.hd + 15) / 16;
       const uint32_t id_s = idesc_f16_f32(kQ, kKV);
-      const uint32_t id_o = idesc_f16_f32(kQ, kHD);
-      bool ok = mbar_wait(q_full, 0, kFaultAttn);
+      const uint32_t id_o = idesc_f16_f32(kQ, 16 * hd16);
+      const uint32_t id_l = idesc_f16_f32(kQ, 16);
+      const uint64_t od = sw128_desc(smem_u32(sOnes));
+      bool ok = mbar_wait_sleep(q_full, 0, kFaultAttn);
       const uint64_t qd = sw128_desc(smem_u32(sQ));
-      // S(j) = Q K(j)^T into score buffer j & 1
+      // S(j) = Q K(j)^T into score buffer j & 1; K stage released when it completes
       auto issue_s = [&](int j) -> bool {
-        const int st = j % kAttnStages;
-        if (!mbar_wait(&kv_full[st], (uint32_t)(j / kAttnStages) & 1u, kFaultAttn)) return false;
+        const int st = j % kKStages;
+        if (!mbar_wait_sleep(&k_full[st], (uint32_t)(j / kKStages) & 1u, kFaultAttn))
+          return false;
         tc_fence_after();
         const uint64_t kd = sw128_desc(smem_u32(sK + st * kKBytes));
         const uint32_t dS = tmem + (uint32_t)(j & 1) * kKV;
-#pragma unroll
-        for (int k = 0; k < kHD / 16; k++) umma_f16(dS, qd + 2u * k, kd + 2u * k, id_s, k > 0);
+        for (int k = 0; k < hd16; k++) umma_f16(dS, qd + 2u * k, kd + 2u * k, id_s, k > 0);
         umma_commit(&s_full[j & 1]);
+        umma_commit(&k_empty[st]);
         return true;
       };
       for (int j = 0; j < nkv && j < 2 && ok; j++) ok = issue_s(j);
       for (int j = 0; j < nkv && ok; j++) {
-        if (!mbar_wait(&p_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn)) break;
+        // S(j + 2) into buffer j & 1 as soon as the softmax warps have read S(j)
+        if (j + 2 < nkv) {
+          if (!mbar_wait_sleep(&s_empty[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn)) break;
+          tc_fence_after();
+          if (!(ok = issue_s(j + 2))) break;
+        }
+        // O lives in TMEM across all key blocks
+        const int sv = j % kVStages;
+        if (!mbar_wait_sleep(&p_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn)) break;
+        if (!mbar_wait_sleep(&v_full[sv], (uint32_t)(j / kVStages) & 1u, kFaultAttn)) break;
         tc_fence_after();
-        // O += P(j) V(j); O lives in TMEM across all key blocks
-        const int st = j % kAttnStages;
         const uint64_t pd = sw128_desc(smem_u32(sP + (j & 1) * kPBytes));
-        const uint64_t vd = sw128_desc(smem_u32(sV + st * kVBytes));
+        const uint64_t vd = sw128_desc(smem_u32(sV + sv * kVBytes));
+        // O += P(j) V(j); the row sums of the fp16 P accumulate in column kSumCol
 #pragma unroll
-        for (int k = 0; k < kKV / 16; k++)
-          umma_f16(tO, pd + 2u * k, vd + 2u * k, id_o, (j > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < kKV / 16; k++) {
+          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+          umma_f16(tO, pd + 2u * k, vd + 2u * k, id_o, acc);
+          umma_f16(tO + kSumCol, pd + 2u * k, od + 2u * k, id_l, acc);
+        }
         umma_commit(&p_empty[j & 1]);
-        umma_commit(&kv_empty[st]);
-        // score buffer j & 1 is free: the softmax warps read S(j) before arriving on p_full
-        if (j + 2 < nkv) ok = issue_s(j + 2);
+        umma_commit(&v_empty[sv]);
       }
       umma_commit(o_full);
     }
   } else {
     // softmax warps: one query row per thread, exp2 domain (scores scaled by
     // scale * log2 e).  The running maximum m is only raised, and O (in TMEM) rescaled,
-    // when a block's maximum exceeds it by more than 8 (a factor 256): probabilities stay
-    // <= 256, well inside fp16, and most blocks need no rescale.
+    // when a block's maximum exceeds it by more than kLazyLog2: probabilities stay <= 4 and
+    // most blocks need no rescale.  P = 2^(s - m) is evaluated two at a time in fp16
+    // (ex2.approx.f16x2 of the fp16-rounded exponent; the exponent's rounding error is at
+    // most 2^-11 * 2 for the largest probabilities), which is the operand precision P V
+    // uses anyway; the row sum comes from the tensor core (P times a ones tile).
     const int r = threadIdx.x;
     const uint32_t lrow = (uint32_t)(warp * 32) << 16;
     const float sl2 = a.scale * 1.4426950408889634f;
-    float m_run = -INFINITY, l_run = 0.f;
+    float m_run = -INFINITY;
     bool ok = true;
     for (int j = 0; j < nkv && ok; j++) {
-      if (!mbar_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn)) {
+      if (!mbar_wait_sleep(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn)) {
         ok = false;
         break;
       }
@@ -179,6 +236,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 #pragma unroll
       for (int c = 0; c < kKV; c += 16) tmem_ld16(tS + c, *(float(*)[16])(v + c));
       tmem_wait_ld();
+      // score buffer j & 1 may take S(j + 2) now
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[j & 1]);
       const int kbase = j * kKV;
       if (kbase + kKV > a.Tk) {
 #pragma unroll
@@ -194,7 +255,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                              fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       const float ms = mx * sl2;
-      if (ms > m_run + 8.0f) {
+      if (ms > m_run + kLazyLog2) {
         if (j > 0) {
           // rescale the accumulated O row and the running sum to the new maximum once
           // PV(j-1) has completed
@@ -204,9 +265,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
           }
           tc_fence_after();
           const float alpha = exp2f(m_run - ms);
-          l_run *= alpha;
 #pragma unroll
-          for (int c = 0; c < kHD; c += 16) {
+          for (int c = 0; c < kSumCol + 16; c += 16) {
             float ov[16];
             tmem_ld16(tO + lrow + c, ov);
             tmem_wait_ld();
@@ -224,16 +284,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         ok = false;
         break;
       }
-      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t w[kKV / 2];
 #pragma unroll
-      for (int i = 0; i < kKV; i += 2) {
-        const float p0 = ex2_approx(fmaf(v[i], sl2, -m_run));
-        const float p1 = ex2_approx(fmaf(v[i + 1], sl2, -m_run));
-        ps[(i >> 1) & 7] += p0 + p1;
-        w[i >> 1] = pack_h2(p0, p1);
-      }
-      l_run += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      for (int i = 0; i < kKV; i += 2)
+        w[i >> 1] = ex2_h2(pack_h2(fmaf(v[i], sl2, -m_run), fmaf(v[i + 1], sl2, -m_run)));
       const uint32_t prow = smem_u32(sP + (j & 1) * kPBytes);
 #pragma unroll
       for (int c = 0; c < 8; c++)
@@ -247,7 +301,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     if (ok && mbar_wait(o_full, 0, kFaultAttn)) {
       tc_fence_after();
       const int t = q0 + r;
-      const float inv = 1.0f / l_run;
+      float lsum[16];
+      tmem_ld16(tO + lrow + kSumCol, lsum);
+      tmem_wait_ld();
+      const float inv = 1.0f / lsum[0];
       const int b = bh / a.H, h = bh - b * a.H;
       const int64_t D = (int64_t)a.H * a.hd;
       const int64_t off = ((int64_t)b * a.Tq + t) * D + (int64_t)h * a.hd;

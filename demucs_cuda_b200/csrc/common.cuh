@@ -99,7 +99,10 @@ static __device__ __forceinline__ float h2f_bits(uint16_t h) {
 }
 // two floats -> packed fp16x2 (low = a)
 static __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-  return (uint32_t)f2h_bits(a) | ((uint32_t)f2h_bits(b) << 16);
+  // one packed conversion (both halves round to nearest even): d = {hi: b, lo: a}
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
+  return d;
 }
 
 // host side RNE conversion (IEEE 754 binary32 -> binary16)
