@@ -300,7 +300,7 @@ static void dconv_tail(const DConvW &dw, const float *h, float *y, int B, int C,
   const int hidp = (hid + 3) / 4 * 4;
   const size_t sm = ((size_t)2 * C * hidp + 7 * (size_t)C) * sizeof(float);
   const int64_t total = (int64_t)B * Fr * T;
-  const unsigned grid = grid_for(total, 256, 148 * 4);
+  const unsigned grid = grid_for(total, 256, 148 * 8);
   const int64_t hsB = (int64_t)hid * Fr * T, hsC = (int64_t)Fr * T;
   const int64_t ysB = (int64_t)C * Fr * T, ysC = (int64_t)Fr * T;
   uint16_t *yhp = yh ? yh->p : nullptr;
@@ -377,12 +377,12 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
       }
       // z statistics from the Gram matrix of fp16(h), accumulated over chunks of each row
       const int npair = hid * (hid + 1) / 2;
-      const int chunk = kGramChunk * 6 / hid >= kGramChunk ? kGramChunk : 12288 / hid;
+      const int hid4 = (hid + 3) / 4 * 4;
+      const int chunk = kGramChunk * 6 / hid4 >= kGramChunk ? kGramChunk : 12288 / hid4;
       double *acc = (double *)dalloc((size_t)rows * (npair + hid) * 2);
       DCB_CUDA(cudaMemsetAsync(acc, 0, (size_t)rows * (npair + hid) * sizeof(double), stream()));
-      const dim3 gg((unsigned)((T + chunk - 1) / chunk), rows,
-                    (unsigned)((npair + hid + kGramPairs - 1) / kGramPairs));
-      k_gram_chunk<<<gg, 256, (size_t)hid * chunk * sizeof(float), stream()>>>(rh, chunk, acc);
+      const dim3 gg((unsigned)((T + chunk - 1) / chunk), rows);
+      k_gram_chunk<<<gg, 256, (size_t)hid4 * chunk * sizeof(float), stream()>>>(rh, chunk, acc);
       DCB_LAUNCHED();
       k_zstats_final<<<(rows + 3) / 4, 128, 0, stream()>>>(acc, dw.zc, hid, T, C2, (int)rows,
                                                           1e-5f, stat, stat + rows);
