@@ -233,6 +233,45 @@ __global__ void k_norm_last(const float *__restrict__ x, float *__restrict__ y,
   }
 }
 
+// k_norm_last for rows of L = n * C floats with C % 4 == 0 (16-byte aligned): grid (blocks,
+// rows), float4 per thread step, the channel index advanced incrementally (no divisions in
+// the loop)
+__global__ void k_norm_last4(const float4 *__restrict__ x, float4 *__restrict__ y,
+                             const float *__restrict__ mean, const float *__restrict__ var,
+                             const float *__restrict__ w, const float *__restrict__ b, int L4,
+                             int C4, float eps) {
+  const int r = blockIdx.y;
+  const float m = mean[r], rs = 1.0f / sqrtf(var[r] + eps);
+  const float4 *xr = x + (int64_t)r * L4;
+  float4 *yr = y + (int64_t)r * L4;
+  const float4 *w4 = (const float4 *)w, *b4 = (const float4 *)b;
+  const int stride = gridDim.x * blockDim.x;
+  const int cstep = stride % C4;
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  int c = i % C4;
+  for (; i < L4; i += stride) {
+    const float4 v = xr[i];
+    float4 o = make_float4((v.x - m) * rs, (v.y - m) * rs, (v.z - m) * rs, (v.w - m) * rs);
+    if (w4) {
+      const float4 g = w4[c];
+      o.x *= g.x;
+      o.y *= g.y;
+      o.z *= g.z;
+      o.w *= g.w;
+    }
+    if (b4) {
+      const float4 h = b4[c];
+      o.x += h.x;
+      o.y += h.y;
+      o.z += h.z;
+      o.w += h.w;
+    }
+    yr[i] = o;
+    c += cstep;
+    if (c >= C4) c -= C4;
+  }
+}
+
 __global__ void k_affine_rows(const float *__restrict__ x, float *__restrict__ y,
                               const float *__restrict__ mean, const float *__restrict__ var,
                               int64_t rows, int64_t L, float eps, int denorm) {
@@ -441,8 +480,16 @@ void dk_norm_apply_last(const float *x, float *y, const float *mean, const float
                         const float *w, const float *b, int64_t rows, int64_t L, int64_t C,
                         float eps) {
   if (rows * L <= 0) return;
-  k_norm_last<<<grid_for(rows * L, 256), 256, 0, stream()>>>(x, y, mean, var, w, b, rows, L, C,
-                                                             eps);
+  const bool al = ((uintptr_t)x | (uintptr_t)y | (uintptr_t)w | (uintptr_t)b) % 16 == 0;
+  if (al && C % 4 == 0 && L % C == 0 && L / 4 < (1ll << 31) && rows <= 65535) {
+    const int L4 = (int)(L / 4), C4 = (int)(C / 4);
+    const unsigned bx = grid_for(L4, 256, (148 * 8 + rows - 1) / rows);
+    k_norm_last4<<<dim3(bx, (unsigned)rows), 256, 0, stream()>>>(
+        (const float4 *)x, (float4 *)y, mean, var, w, b, L4, C4, eps);
+  } else {
+    k_norm_last<<<grid_for(rows * L, 256), 256, 0, stream()>>>(x, y, mean, var, w, b, rows, L,
+                                                               C, eps);
+  }
   DCB_LAUNCHED();
 }
 
