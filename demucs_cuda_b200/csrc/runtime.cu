@@ -23,6 +23,7 @@ static std::atomic<uint64_t> g_launches{0};
 int g_opt_simt = 0;
 int g_opt_graphs = 0;
 int g_opt_generic_epi = 0;
+extern int g_stream_istft;
 
 void fail(const char *fmt, ...) {
   char msg[1024];
@@ -235,6 +236,9 @@ int dcb_set_option(const char *name, int value) {
   } else if (!strcmp(name, "graphs")) {
     old = g_opt_graphs;
     g_opt_graphs = value;
+  } else if (!strcmp(name, "stream_istft")) {
+    old = g_stream_istft;
+    g_stream_istft = value;
   } else if (!strcmp(name, "generic_epilogue")) {
     old = g_opt_generic_epi;
     g_opt_generic_epi = value;

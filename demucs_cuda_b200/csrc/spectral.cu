@@ -390,6 +390,11 @@ __global__ void __launch_bounds__(kFftThreads)
     if (k > n / 2) {
       a.y = -a.y;
       b.y = -b.y;
+    } else if (k == 0) {
+      // the reference keeps the real part of a complex IFFT, which drops the DC bin's
+      // imaginary part; in the two-frame pairing it would leak into the other frame
+      a.y = 0.f;
+      b.y = 0.f;
     }
     buf[fpad(k)] = make_float2(a.x - b.y, -(a.y + b.x));
   }
@@ -437,6 +442,108 @@ __global__ void k_ola_frames4096(const float *__restrict__ fw, float *__restrict
   }
 }
 
+// Fused inverse STFT + overlap-add for n = 4096, hop 1024 (the reference's istft with its
+// window-sum division): one CTA per (row, run of kStreamHops consecutive output hops).  The
+// CTA inverts the frames covering its hops in ascending order, two real frames per complex
+// FFT (as k_ifft_frames4096), adds each windowed frame into a ring of four hop
+// accumulators in shared memory, and writes hop g as soon as frame g (its last
+// contributor) is in; the three frames before the run are recomputed by the CTA (3 of
+// kStreamHops + 3 frames), so no frame buffer goes through HBM.
+constexpr int kStreamHops = 32;
+int g_stream_istft = 1;  // 0: the two-pass inverse STFT (frames through HBM), for A/B checks
+
+__global__ void __launch_bounds__(kFftThreads)
+    k_istft_stream4096(const float2 *__restrict__ z, float *__restrict__ out, int N, int F,
+                       int NF, const float *__restrict__ window,
+                       const float2 *__restrict__ tw, int64_t start, int64_t length,
+                       int g_first) {
+  extern __shared__ float2 sbuf[];  // [kFftPadded] FFT buffer, then the ring [4][1024]
+  float2 *buf = sbuf;
+  float *ring = (float *)(sbuf + kFftPadded);
+  constexpr int n = kFftN, hop = 1024;
+  const int64_t r = blockIdx.y;
+  const int k0 = g_first + blockIdx.x * kStreamHops;  // first output hop of this CTA
+  const int k1 = min(k0 + kStreamHops, NF + 3);       // hops past NF + 2 hold no samples
+  const float inv_n = 1.0f / (float)n;
+  for (int i = threadIdx.x; i < 4 * hop; i += kFftThreads) ring[i] = 0.f;
+  int g = k0 - 3 < 0 ? 0 : k0 - 3;
+  __syncthreads();
+  for (; g < k1; g += 2) {
+    // frames g and g + 1 (those past NF - 1 do not exist; spectra of frame g: g - 2)
+    const int fa = g - 2, fb = g - 1;
+    // (frame g + 1 enters the FFT whenever it has a spectrum, so every frame comes out of
+    // the same pair, and rounding, as in k_ifft_frames4096; it is added only inside the run)
+    const bool va = g < NF && fa >= 0 && fa < N;
+    const bool vb = g + 1 < NF && fb >= 0 && fb < N;
+    if (va || vb) {
+      const float2 *za = z + (r * N + fa) * F;
+      const float2 *zb = z + (r * N + fb) * F;
+#pragma unroll
+      for (int q = 0; q < 16; q++) {
+        const int k = threadIdx.x + 256 * q;
+        const int kk = k <= n / 2 ? k : n - k;
+        float2 a = va && kk < F ? za[kk] : make_float2(0.f, 0.f);
+        float2 b = vb && kk < F ? zb[kk] : make_float2(0.f, 0.f);
+        if (k > n / 2) {
+          a.y = -a.y;
+          b.y = -b.y;
+        } else if (k == 0) {
+          // the reference keeps the real part of a complex IFFT, which drops the DC bin's
+          // imaginary part; in the two-frame pairing it would leak into the other frame
+          a.y = 0.f;
+          b.y = 0.f;
+        }
+        buf[fpad(k)] = make_float2(a.x - b.y, -(a.y + b.x));
+      }
+      __syncthreads();
+      fft4096(buf, tw);
+    }
+    // add frame g (real part) then frame g + 1 (imaginary part), finishing one hop each
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+      const int ge = g + e;
+      if (ge >= k1) break;
+      if (e == 0 ? va : vb) {  // (ge < k1 here)
+#pragma unroll
+        for (int q = 0; q < 16; q++) {
+          const int i = threadIdx.x + 256 * q;
+          const float2 v = buf[fpad(i)];
+          const float x = (e == 0 ? v.x : -v.y) * (window[i] * inv_n);
+          ring[(((ge + (i >> 10)) & 3) << 10) + (i & 1023)] += x;
+        }
+      }
+      __syncthreads();
+      // hop ge is complete: samples ge * hop + w, divided by the squared-window sum of
+      // every frame covering them
+      if (ge >= k0) {
+        float *slot = ring + ((ge & 3) << 10);
+        for (int w = threadIdx.x; w < hop; w += kFftThreads) {
+          const int64_t idx = (int64_t)ge * hop + w;
+          const int64_t t = idx - start;
+          if (t >= 0 && t < length) {
+            float den = 0.f;  // ascending frames, as the two-pass overlap-add sums
+#pragma unroll
+            for (int i = 3; i >= 0; i--) {
+              const int gi = ge - i;
+              if (gi >= 0 && gi < NF) {
+                const float wv = window[i * hop + w];
+                den += wv * wv;
+              }
+            }
+            out[r * length + t] = den > 0.f ? slot[w] / den : 0.f;
+          }
+          slot[w] = 0.f;
+        }
+      } else {
+        // a hop before the run: only cleared (its other frames belong to the previous CTA)
+        float *slot = ring + ((ge & 3) << 10);
+        for (int w = threadIdx.x; w < hop; w += kFftThreads) slot[w] = 0.f;
+      }
+      __syncthreads();
+    }
+  }
+}
+
 static int log2i(int n) {
   int b = 0;
   while ((1 << b) < n) b++;
@@ -467,6 +574,27 @@ void ispec_fused(const float *x, float *out, const float *mean, const float *var
     DCB_CUDA(cudaFuncSetAttribute(k_istft_ola, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)smem));
     attr = smem;
+  }
+  if (n_fft == kFftN && hop == 1024 && g_stream_istft &&
+      (start + length - 1) / hop <= (int64_t)N + 6) {
+    // output frames NF = N + 4 (two of padding on each side); hops covering the samples
+    // (the signal ends with hop NF + 2)
+    const int NF = N + 4;
+    const int g_first = (int)(start / hop);
+    const int g_last = (int)((start + length - 1) / hop);
+    const int runs = (g_last - g_first + kStreamHops) / kStreamHops;
+    const size_t sm = (size_t)kFftPadded * sizeof(float2) + 4 * 1024 * sizeof(float);
+    static bool attr = false;
+    if (!attr) {
+      DCB_CUDA(cudaFuncSetAttribute(k_istft_stream4096,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+      attr = true;
+    }
+    k_istft_stream4096<<<dim3((unsigned)runs, (unsigned)R), kFftThreads, sm, stream()>>>(
+        z, out, N, F, NF, window, twiddles4096(), start, length, g_first);
+    DCB_LAUNCHED();
+    DCB_CUDA(cudaFreeAsync(z, stream()));
+    return;
   }
   if (n_fft == kFftN && hop == 1024) {
     // frames covering [start, start + length): NF = N + 4 output frames in all

@@ -191,7 +191,8 @@ void *dcb_get_stream(void);
 /* Backend options: "simt" (1 = CUDA-core kernels instead of tcgen05, for A/B checks),
  * "graphs" (1 = replay captured CUDA graphs for repeated forwards), "generic_epilogue"
  * (1 = channels-last convs use their generic epilogue instead of the specialised ones, for
- * A/B checks). Returns the old value. */
+ * A/B checks), "stream_istft" (0 = the two-pass inverse STFT instead of the fused
+ * streaming one, for A/B checks). Returns the old value. */
 int dcb_set_option(const char *name, int value);
 /* Number of this library's kernels launched so far (monotonic). */
 uint64_t dcb_kernel_launches(void);

@@ -149,6 +149,25 @@ def test_short_specialised_epilogue_matches_generic(short):
     assert dcb.device_fault() == 0
 
 
+def test_short_streaming_istft_matches_two_pass(short):
+    """The fused streaming inverse STFT (frames inverted and overlap-added in shared
+    memory) gives the two-pass path's stems (windowed frames through HBM, then the
+    overlap-add with the window-sum division)."""
+    import demucs_cuda_b200 as dcb
+    torch = short["torch"]
+    x = _t(torch, short["mix"])
+    fused = short["model"].forward(x).cpu().numpy()
+    old = dcb.set_option("stream_istft", 0)
+    try:
+        two_pass = short["model"].forward(x).cpu().numpy()
+    finally:
+        dcb.set_option("stream_istft", old)
+    e = rel_l2(fused, two_pass)
+    print(f"streaming vs two-pass inverse STFT: rel_l2 {e:.3e}")
+    assert e < 1e-6
+    assert dcb.device_fault() == 0
+
+
 def test_tiny_batch_consistency(tiny):
     """A batch of segments gives each segment the result it gets alone (per-segment
     normalisation and every kernel are per sample)."""
