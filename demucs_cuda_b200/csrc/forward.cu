@@ -227,8 +227,15 @@ static Half16 im2col8(const float *x, int64_t images, int C, int H, int W, int H
   Half16 h = half_alloc(images, 64, Ho, Wo, false);
   h.im2col = 1;
   const int64_t n = images * Ho * (int64_t)Wo * 8;
-  k_im2col8_half<<<grid_for(n, 256), 256, 0, stream()>>>(x, h.p, images, C, H, W, Ho, Wo, S, P,
-                                                         axis);
+  const int64_t lines = images * Ho;
+  if (lines <= 65535) {
+    const unsigned bx = grid_for(Wo, 256, (148 * 16 + lines - 1) / lines);
+    k_im2col8_lines<<<dim3(bx, (unsigned)lines), 256, 0, stream()>>>(x, h.p, C, H, W, Ho, Wo, S,
+                                                                     P, axis);
+  } else {
+    k_im2col8_half<<<grid_for(n, 256), 256, 0, stream()>>>(x, h.p, images, C, H, W, Ho, Wo, S,
+                                                           P, axis);
+  }
   DCB_LAUNCHED();
   return h;
 }
@@ -1201,8 +1208,14 @@ static int apply_split(DcbModel *m, const float *mix, int B, int length, float *
         mix, slot->in, B, C, length, Lv, sl);
     DCB_LAUNCHED();
     if (forward_slot_run(m, slot) < 0) return -1;
-    k_accumulate_batch<<<grid_for(rows * (hi - lo), 256), 256, 0, stream()>>>(
-        out, slot->out, wdev, (int)rows, length, Lv, lo, hi, sl);
+    if (rows <= 65535 && hi - lo < (1ll << 31)) {
+      const unsigned bx = grid_for(hi - lo, 256, (148 * 16 + rows - 1) / rows);
+      k_accumulate_rows<<<dim3(bx, (unsigned)rows), 256, 0, stream()>>>(
+          out, slot->out, wdev, (int)rows, length, Lv, lo, (int)(hi - lo), sl);
+    } else {
+      k_accumulate_batch<<<grid_for(rows * (hi - lo), 256), 256, 0, stream()>>>(
+          out, slot->out, wdev, (int)rows, length, Lv, lo, hi, sl);
+    }
     DCB_LAUNCHED();
   }
   // divide by the weight sum of every segment (all shards'), summed on the device

@@ -2008,6 +2008,9 @@ void gemm_rows_launch(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t
                       const Epi &e, Shape s, Gather g) {
   if (!g_opt_simt && K > 0 && batch <= 65535) {
     int bn = pick_bn(M, N, batch);
+    // at most 128 columns: the accumulator is then double-buffered in TMEM, so a tile's
+    // epilogue overlaps the next tile's MMAs
+    if (bn > 128) bn = 128;
     // short GEMMs (the transformer's): narrower N tiles until the persistent CTAs get two
     // tiles each, so loads and epilogues of consecutive tiles overlap
     const int64_t mt = (M + kBM - 1) / kBM;

@@ -583,6 +583,29 @@ __global__ void k_im2col8_half(const float *__restrict__ x, uint16_t *__restrict
   }
 }
 
+// k_im2col8_half with one thread per position writing its 8 taps (128 contiguous bytes) and
+// the line (n, ho) from the grid: block (position block, line)
+__global__ void k_im2col8_lines(const float *__restrict__ x, uint16_t *__restrict__ y, int C,
+                                int H, int W, int Ho, int Wo, int S, int P, int axis) {
+  const int line = blockIdx.y;
+  const int n = line / Ho, ho = line - n * Ho;
+  for (int wo = blockIdx.x * blockDim.x + threadIdx.x; wo < Wo; wo += gridDim.x * blockDim.x) {
+    uint4 *dst = (uint4 *)(y + ((int64_t)line * Wo + wo) * 64);
+#pragma unroll
+    for (int tap = 0; tap < 8; tap++) {
+      const int h = axis == 0 ? ho * S - P + tap : ho;
+      const int w = axis == 0 ? wo : wo * S - P + tap;
+      const bool in = h >= 0 && h < H && w >= 0 && w < W;
+      float v[8];
+#pragma unroll
+      for (int c = 0; c < 8; c++)
+        v[c] = in && c < C ? x[(((int64_t)n * C + c) * H + h) * (int64_t)W + w] : 0.f;
+      dst[tap] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]),
+                            pack_h2(v[6], v[7]));
+    }
+  }
+}
+
 // tok [B, Fr*T1, C] (token t*Fr + f) -> x [B, C, Fr, T1]
 __global__ void k_tokens_to_chw(const float *__restrict__ tok, float *__restrict__ x, int B,
                                 int C, int Fr, int T1) {
@@ -673,6 +696,24 @@ __global__ void k_accumulate_batch(float *out, const float *__restrict__ y,
         acc += y[((int64_t)k * rows + r) * y_len + sl.y0[k] + u] * w[u];
     }
     out[r * out_len + t] = acc;
+  }
+}
+
+// k_accumulate_batch over a (position block, row) grid: 32-bit position loop, same sums
+__global__ void k_accumulate_rows(float *out, const float *__restrict__ y,
+                                  const float *__restrict__ w, int rows, int64_t out_len,
+                                  int64_t y_len, int64_t lo, int span, SegList sl) {
+  const int r = blockIdx.y;
+  float *orow = out + (int64_t)r * out_len;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < span; i += gridDim.x * blockDim.x) {
+    const int64_t t = lo + i;
+    float acc = orow[t];
+    for (int k = 0; k < sl.cnt; k++) {
+      const int64_t u = t - sl.off[k];
+      if (u >= 0 && u < sl.n[k])
+        acc += y[((int64_t)k * rows + r) * y_len + sl.y0[k] + u] * w[u];
+    }
+    orow[t] = acc;
   }
 }
 
