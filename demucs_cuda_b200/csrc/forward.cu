@@ -227,15 +227,8 @@ static Half16 im2col8(const float *x, int64_t images, int C, int H, int W, int H
   Half16 h = half_alloc(images, 64, Ho, Wo, false);
   h.im2col = 1;
   const int64_t n = images * Ho * (int64_t)Wo * 8;
-  const int64_t lines = images * Ho;
-  if (lines <= 65535) {
-    const unsigned bx = grid_for(Wo, 256, (148 * 16 + lines - 1) / lines);
-    k_im2col8_lines<<<dim3(bx, (unsigned)lines), 256, 0, stream()>>>(x, h.p, C, H, W, Ho, Wo, S,
-                                                                     P, axis);
-  } else {
-    k_im2col8_half<<<grid_for(n, 256), 256, 0, stream()>>>(x, h.p, images, C, H, W, Ho, Wo, S,
-                                                           P, axis);
-  }
+  k_im2col8_half<<<grid_for(n, 256), 256, 0, stream()>>>(x, h.p, images, C, H, W, Ho, Wo, S, P,
+                                                         axis);
   DCB_LAUNCHED();
   return h;
 }
@@ -384,12 +377,12 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
       }
       // z statistics from the Gram matrix of fp16(h), accumulated over chunks of each row
       const int npair = hid * (hid + 1) / 2;
-      const int hid4 = (hid + 3) / 4 * 4;
-      const int chunk = kGramChunk * 6 / hid4 >= kGramChunk ? kGramChunk : 12288 / hid4;
+      const int chunk = kGramChunk * 6 / hid >= kGramChunk ? kGramChunk : 12288 / hid;
       double *acc = (double *)dalloc((size_t)rows * (npair + hid) * 2);
       DCB_CUDA(cudaMemsetAsync(acc, 0, (size_t)rows * (npair + hid) * sizeof(double), stream()));
-      const dim3 gg((unsigned)((T + chunk - 1) / chunk), rows);
-      k_gram_chunk<<<gg, 256, (size_t)hid4 * chunk * sizeof(float), stream()>>>(rh, chunk, acc);
+      const dim3 gg((unsigned)((T + chunk - 1) / chunk), rows,
+                    (unsigned)((npair + hid + kGramPairs - 1) / kGramPairs));
+      k_gram_chunk<<<gg, 256, (size_t)hid * chunk * sizeof(float), stream()>>>(rh, chunk, acc);
       DCB_LAUNCHED();
       k_zstats_final<<<(rows + 3) / 4, 128, 0, stream()>>>(acc, dw.zc, hid, T, C2, (int)rows,
                                                           1e-5f, stat, stat + rows);
@@ -1208,14 +1201,8 @@ static int apply_split(DcbModel *m, const float *mix, int B, int length, float *
         mix, slot->in, B, C, length, Lv, sl);
     DCB_LAUNCHED();
     if (forward_slot_run(m, slot) < 0) return -1;
-    if (rows <= 65535 && hi - lo < (1ll << 31)) {
-      const unsigned bx = grid_for(hi - lo, 256, (148 * 16 + rows - 1) / rows);
-      k_accumulate_rows<<<dim3(bx, (unsigned)rows), 256, 0, stream()>>>(
-          out, slot->out, wdev, (int)rows, length, Lv, lo, (int)(hi - lo), sl);
-    } else {
-      k_accumulate_batch<<<grid_for(rows * (hi - lo), 256), 256, 0, stream()>>>(
-          out, slot->out, wdev, (int)rows, length, Lv, lo, hi, sl);
-    }
+    k_accumulate_batch<<<grid_for(rows * (hi - lo), 256), 256, 0, stream()>>>(
+        out, slot->out, wdev, (int)rows, length, Lv, lo, hi, sl);
     DCB_LAUNCHED();
   }
   // divide by the weight sum of every segment (all shards'), summed on the device

@@ -273,69 +273,55 @@ __global__ void __launch_bounds__(kGnFusedThreads)
 
 // Sums S_j and upper Gram entries Q_jk (j <= k) of fp16(h) over one chunk of a DConv
 // hidden row [hid][T], accumulated in fp64 into acc[row][npair + hid] (npair = hid (hid +
-// 1) / 2 in j-major order, the sums last): the statistics of z = W16 . fp16(h) + b for rows
-// too long for one CTA.  Block (chunk, row); the chunk is staged once in shared memory
-// [hid rounded up to 4][len] and each warp takes 4 x 4 tiles (J <= K) of the Gram matrix:
-// lanes split the positions, 16 products per position from 8 shared loads.
+// 1) / 2, the sums last): the statistics of z = W16 . fp16(h) + b for rows too long for
+// one CTA.  Block (chunk, row, group of kGramPairs entries); the chunk is staged in shared
+// memory [hid][len].
 constexpr int kGramChunk = 1024;
+constexpr int kGramPairs = 64;  // Gram entries per block (8 per warp)
 __global__ void __launch_bounds__(256)
     k_gram_chunk(RowView v, int chunk, double *__restrict__ acc) {
   extern __shared__ float hs[];
   const int64_t row = blockIdx.y;
   const int64_t b = row / v.Fr, f = row - b * v.Fr;
-  const int hid = v.C, hid4 = (hid + 3) & ~3;
+  const int hid = v.C;
   const int64_t t0 = (int64_t)blockIdx.x * chunk;
   const int len = (int)(v.T - t0 < chunk ? v.T - t0 : chunk);
   const float *xr = v.x + b * v.sB + f * v.sF + t0;
-  for (int i = threadIdx.x; i < hid4 * len; i += blockDim.x) {
+  for (int i = threadIdx.x; i < hid * len; i += blockDim.x) {
     const int j = i / len, t = i - j * len;
-    hs[j * len + t] = j < hid ? __half2float(__float2half_rn(xr[(int64_t)j * v.sC + t])) : 0.f;
+    hs[j * len + t] = __half2float(__float2half_rn(xr[(int64_t)j * v.sC + t]));
   }
   __syncthreads();
-  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int npair = hid * (hid + 1) / 2;
-  double *ar = acc + row * (npair + hid);
-  const int nt = hid4 / 4, ntiles = nt * (nt + 1) / 2;
-  for (int ti = wid; ti < ntiles; ti += nw) {
-    int J = 0, q = ti;
-    while (q >= nt - J) {
-      q -= nt - J;
-      J++;
+  const int p_end = min(npair + hid, (int)(blockIdx.z + 1) * kGramPairs);
+  for (int p = blockIdx.z * kGramPairs + wid; p < p_end; p += blockDim.x / 32) {
+    int j, k;
+    if (p < npair) {
+      j = 0;
+      int q = p;
+      while (q >= hid - j) {
+        q -= hid - j;
+        j++;
+      }
+      k = j + q;
+    } else {
+      j = p - npair;
+      k = -1;
     }
-    const int K = J + q;
-    const float *hj = hs + 4 * J * len, *hk = hs + 4 * K * len;
+    const float *hj = hs + j * len;
+    const float *hk = k >= 0 ? hs + k * len : nullptr;
     // products of fp16 values are exact in fp32; a lane's <= 32 terms are summed in fp32,
     // lanes and chunks in fp64
-    float s16[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) s16[i] = 0.f;
-    for (int t = lane; t < len; t += 32) {
-      float x[4], y[4];
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        x[i] = hj[i * len + t];
-        y[i] = hk[i * len + t];
-      }
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int l = 0; l < 4; l++) s16[4 * i + l] = fmaf(x[i], y[l], s16[4 * i + l]);
+    float a32 = 0.f;
+    if (hk) {
+      for (int t = lane; t < len; t += 32) a32 = fmaf(hj[t], hk[t], a32);
+    } else {
+      for (int t = lane; t < len; t += 32) a32 += hj[t];
     }
-#pragma unroll
-    for (int e = 0; e < 16; e++) {
-      double d = (double)s16[e];
-      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-      const int j = 4 * J + (e >> 2), k = 4 * K + (e & 3);
-      if (lane == 0 && j <= k && k < hid)
-        atomicAdd(&ar[j * hid - j * (j - 1) / 2 + (k - j)], d);
-    }
-  }
-  for (int j = wid; j < hid; j += nw) {
-    float s = 0.f;
-    for (int t = lane; t < len; t += 32) s += hs[j * len + t];
-    double d = (double)s;
-    for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-    if (lane == 0) atomicAdd(&ar[npair + j], d);
+    double a = (double)a32;
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) atomicAdd(&acc[row * (npair + hid) + p], a);
   }
 }
 
@@ -351,10 +337,14 @@ __global__ void k_zstats_final(const double *__restrict__ acc, const double *__r
   const double *a = acc + (int64_t)row * (npair + hid);
   const double *G = zc, *u = zc + hid * hid, *vv = u + hid;
   double sz = 0.0, szz = 0.0;
-  // entries (j, k >= j) in j-major order: p = sum_{i < j} (hid - i) + (k - j)
-  for (int j = 0, p0 = 0; j < hid; p0 += hid - j, j++) {
-    for (int q = lane; q < hid - j; q += 32)
-      szz += (q == 0 ? 1.0 : 2.0) * G[j * hid + j + q] * a[p0 + q];
+  for (int p = lane; p < npair; p += 32) {
+    int j = 0, q = p;
+    while (q >= hid - j) {
+      q -= hid - j;
+      j++;
+    }
+    const int k = j + q;
+    szz += (j == k ? 1.0 : 2.0) * G[j * hid + k] * a[p];
   }
   for (int j = lane; j < hid; j += 32) {
     sz += u[j] * a[npair + j];
@@ -583,29 +573,6 @@ __global__ void k_im2col8_half(const float *__restrict__ x, uint16_t *__restrict
   }
 }
 
-// k_im2col8_half with one thread per position writing its 8 taps (128 contiguous bytes) and
-// the line (n, ho) from the grid: block (position block, line)
-__global__ void k_im2col8_lines(const float *__restrict__ x, uint16_t *__restrict__ y, int C,
-                                int H, int W, int Ho, int Wo, int S, int P, int axis) {
-  const int line = blockIdx.y;
-  const int n = line / Ho, ho = line - n * Ho;
-  for (int wo = blockIdx.x * blockDim.x + threadIdx.x; wo < Wo; wo += gridDim.x * blockDim.x) {
-    uint4 *dst = (uint4 *)(y + ((int64_t)line * Wo + wo) * 64);
-#pragma unroll
-    for (int tap = 0; tap < 8; tap++) {
-      const int h = axis == 0 ? ho * S - P + tap : ho;
-      const int w = axis == 0 ? wo : wo * S - P + tap;
-      const bool in = h >= 0 && h < H && w >= 0 && w < W;
-      float v[8];
-#pragma unroll
-      for (int c = 0; c < 8; c++)
-        v[c] = in && c < C ? x[(((int64_t)n * C + c) * H + h) * (int64_t)W + w] : 0.f;
-      dst[tap] = make_uint4(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]), pack_h2(v[4], v[5]),
-                            pack_h2(v[6], v[7]));
-    }
-  }
-}
-
 // tok [B, Fr*T1, C] (token t*Fr + f) -> x [B, C, Fr, T1]
 __global__ void k_tokens_to_chw(const float *__restrict__ tok, float *__restrict__ x, int B,
                                 int C, int Fr, int T1) {
@@ -696,24 +663,6 @@ __global__ void k_accumulate_batch(float *out, const float *__restrict__ y,
         acc += y[((int64_t)k * rows + r) * y_len + sl.y0[k] + u] * w[u];
     }
     out[r * out_len + t] = acc;
-  }
-}
-
-// k_accumulate_batch over a (position block, row) grid: 32-bit position loop, same sums
-__global__ void k_accumulate_rows(float *out, const float *__restrict__ y,
-                                  const float *__restrict__ w, int rows, int64_t out_len,
-                                  int64_t y_len, int64_t lo, int span, SegList sl) {
-  const int r = blockIdx.y;
-  float *orow = out + (int64_t)r * out_len;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < span; i += gridDim.x * blockDim.x) {
-    const int64_t t = lo + i;
-    float acc = orow[t];
-    for (int k = 0; k < sl.cnt; k++) {
-      const int64_t u = t - sl.off[k];
-      if (u >= 0 && u < sl.n[k])
-        acc += y[((int64_t)k * rows + r) * y_len + sl.y0[k] + u] * w[u];
-    }
-    orow[t] = acc;
   }
 }
 
