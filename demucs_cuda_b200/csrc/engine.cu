@@ -636,10 +636,13 @@ static bool dconv_zconst(Loader &L, Staging &st, const std::string &prefix, DCon
 }
 
 static int glu_bn_for(int O2) {
-  // fixed N tile for GLU convs: 2*O2 columns rounded up to a power of two, at most 128
-  // (the widest tile of the gather kernel)
+  // fixed N tile for GLU convs: 2*O2 columns rounded up to a power of two, at most 128, or
+  // 96 where that pads fewer columns (O2 = 48, 96: the channels-last conv kernel takes it;
+  // the gather path then runs on CUDA cores)
   int bn = 32;
   while (bn < 128 && bn < 2 * O2) bn *= 2;
+  const int64_t pad = (2 * O2 + bn - 1) / bn * bn, pad96 = (2 * O2 + 95) / 96 * 96;
+  if (2 * O2 > 64 && pad96 < pad) bn = 96;
   return bn;
 }
 

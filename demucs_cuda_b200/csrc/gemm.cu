@@ -1115,7 +1115,8 @@ template <int BN>
 struct ChCfg {
   static constexpr uint32_t kStage = kATileBytes + BN * 128;  // a multiple of 1024
   static constexpr int kAccCols = BN < 32 ? 32 : BN;
-  static constexpr int kTmemCols = 2 * kAccCols;
+  // two accumulators, allocated as a power of two columns (96-column tiles take 256)
+  static constexpr int kTmemCols = 2 * kAccCols <= 64 ? 64 : 2 * kAccCols <= 128 ? 128 : 256;
 };
 
 static __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map,
@@ -1170,9 +1171,10 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
     grs = e.gn_rstd[n];
   }
   const int ncols = glu ? e.glu_half : BN;
-  // the two warps of a lane quarter take one half of the columns each (16-column chunks)
-  const int per = ncols >= 32 ? ncols / 2 : (half == 0 ? ncols : 0);
-  const int cbeg = ncols >= 32 ? half * per : 0;
+  // the two warps of a lane quarter split the 16-column chunks (the first takes the odd one)
+  const int nch = ncols >> 4, h0 = (nch + 1) >> 1;
+  const int per = 16 * (half == 0 ? h0 : nch - h0);
+  const int cbeg = half == 0 ? 0 : 16 * h0;
   const int obase = (glu ? nt * e.glu_half : nt * BN) + cbeg;
   const int ncol_total = convtr ? O * e.stride : O;
   const int li = lane & 15;
@@ -1415,8 +1417,9 @@ static __device__ __forceinline__ void ch_epi_fast(const ConvH &c, const Epi &e,
   const int q = wo0 + r;
   const int O = e.O;
   const int ncols = GLU ? e.glu_half : BN;
-  const int per = ncols >= 32 ? ncols / 2 : (half == 0 ? ncols : 0);
-  const int cbeg = ncols >= 32 ? half * per : 0;
+  const int nch = ncols >> 4, h0 = (nch + 1) >> 1;  // chunks of the two column halves
+  const int per = 16 * (half == 0 ? h0 : nch - h0);
+  const int cbeg = half == 0 ? 0 : 16 * h0;
   const int obase = (GLU ? nt * e.glu_half : nt * BN) + cbeg;
   const int ncol_total = CT != 0 ? O * e.stride : O;
   float gmu = 0.f, grs = 0.f;
@@ -2265,6 +2268,7 @@ bool conv_half(const HalfAct &x, int KH, int KW, int SH, int SW, int PH, int PW,
     switch (bn) {
       case 32: launch_conv_h<32>(ta, tb, c, e2, ek); break;
       case 64: launch_conv_h<64>(ta, tb, c, e2, ek); break;
+      case 96: launch_conv_h<96>(ta, tb, c, e2, ek); break;
       case 128: launch_conv_h<128>(ta, tb, c, e2, ek); break;
       default: launch_conv_h<256>(ta, tb, c, e2, ek); break;
     }
@@ -2344,7 +2348,9 @@ void gemm_gather(const Gather &g, int64_t M, const uint16_t *w, int64_t N, int64
   TraceScope ts(e.mode == EPI_CONVTR ? TR_CONVTR : TR_CONV, 2.0 * M * n_alg * g.K,
                 x_b + n_alg * g.K * 2.0 + out_elems * 4.0 * (e.res ? 2 : 1), M, (int64_t)n_alg,
                 g.K);
-  if (!g_opt_simt) {
+  // a GLU N tile the tensor-core gather kernels do not take (96: the channels-last kernel's)
+  const bool odd_tile = bn != 32 && bn != 64 && bn != 128;
+  if (!g_opt_simt && !odd_tile) {
     // TMA im2col kernel (freq-branch convs); its N tile may be wider than the gather
     // kernel's, except for GLU convs whose weights are interleaved per N tile
     int bt = bn;
