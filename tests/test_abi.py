@@ -65,3 +65,20 @@ def test_pack_half_rounding_matches_reference_rule():
     assert (got == want).all()
     nan = L.dk_pack_half(float("nan"), 0)
     assert (nan & 0x7c00) == 0x7c00 and (nan & 0x3ff) != 0
+
+
+def test_backend_options_round_trip():
+    """dcb_set_option (host-only) takes every option include/dc_b200.h documents and returns
+    the previous value, so A/B tests can switch a path and put it back."""
+    import ctypes
+    import demucs_cuda_b200 as d
+    L = d.lib(load_only=True)
+    L.dcb_set_option.argtypes = [ctypes.c_char_p, ctypes.c_int]
+    L.dcb_set_option.restype = ctypes.c_int
+    header = open(HEADER).read()
+    defaults = {"simt": 0, "graphs": 0, "generic_epilogue": 0, "stream_istft": 1}
+    for name, default in defaults.items():
+        assert f'"{name}"' in header, name
+        old = L.dcb_set_option(name.encode(), 1 - default)
+        assert old == default, (name, old)
+        assert L.dcb_set_option(name.encode(), old) == 1 - default, name
