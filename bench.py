@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""htdemucs_6s source separation throughput on B200.
+"""htdemucs_6s source separation throughput on B200 (the 240 s track workload).
 
 One step = the whole of dc_apply_model (apply.c:179-306) on a 240 s synthetic stereo track:
 shifts = 1, 7.8 s segments at overlap 0.25, batches of 8 segments -> 42 segment forwards of

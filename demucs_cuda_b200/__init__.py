@@ -78,8 +78,22 @@ def lib(load_only: bool = False):
         raise BackendError(f"{LIB_PATH} is missing: build it with `python -m "
                            "demucs_cuda_b200.build` (or __graft_entry__.build())")
     L = C.CDLL(LIB_PATH)
+    for name, (res, args) in signatures().items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    if not load_only:
+        L.dcb_set_error_mode(1)  # record errors; Python raises them
+    _lib = L
+    return L
+
+
+def signatures():
+    """ctypes (restype, argtypes) of every exported function, by name.  The Part-1 entries
+    are the reference backend.h signatures, so the same table also binds the reference's
+    own CPU backend for side-by-side checks."""
     i64, i32, f32, vp, sz = C.c_int64, C.c_int, C.c_float, C.c_void_p, C.c_size_t
-    sig = {
+    return {
         "dk_pack_half": (C.c_uint16, [f32, i32]),
         "dk_init": (i32, [i32, C.c_char_p, sz]),
         "dk_backend_name": (C.c_char_p, []),
@@ -154,14 +168,6 @@ def lib(load_only: bool = False):
         "dcb_apply_plan": (i32, [vp, i32, C.POINTER(DcbApplyOpts), C.POINTER(i32),
                                  C.POINTER(i32)]),
     }
-    for name, (res, args) in sig.items():
-        fn = getattr(L, name)
-        fn.restype = res
-        fn.argtypes = args
-    if not load_only:
-        L.dcb_set_error_mode(1)  # record errors; Python raises them
-    _lib = L
-    return L
 
 
 def check(ok=True, what="call"):

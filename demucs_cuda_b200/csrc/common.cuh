@@ -17,6 +17,9 @@ namespace dcb {
 // return (dcb_set_error_mode).
 void fail(const char *fmt, ...);
 bool failed();  // an error is pending in return mode
+// number of errors this thread has recorded (return mode); a call that compares it before
+// and after knows whether it raised one itself, whatever error was already pending
+uint64_t error_count();
 cudaStream_t stream();
 void count_launch();
 void add_launches(uint64_t n);
@@ -54,6 +57,12 @@ extern int g_opt_generic_epi;  // channels-last convs take the generic epilogue
 // device fault word written by bounded waits (see umma.cuh); the library is one
 // translation unit (all.cu), so the definition lives here
 __device__ uint32_t g_dev_fault = 0;
+// limit of every bounded wait in nanoseconds (option "wait_limit_ms"; default 2 s)
+__device__ uint64_t g_wait_ns = 2000000000ull;
+// One-shot test hook (option "test_withhold_arrive"): while non-zero, the first tensor-core
+// GEMM CTA that reaches its first operand stage consumes the flag and does not release that
+// stage, so the producer's next wait on it can only end by the bounded-wait limit.
+__device__ uint32_t g_test_withhold = 0;
 
 static inline unsigned grid_for(int64_t n, int threads, int64_t cap = 148 * 32) {
   int64_t b = (n + threads - 1) / threads;

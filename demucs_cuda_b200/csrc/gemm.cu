@@ -572,6 +572,14 @@ __global__ void __launch_bounds__(kThreads, 2)
             tma_load_3d(sA + st * kATileBytes, &tmA, &full[st], kb * kBK, (int)m0, cA);
         }
       }
+      if (!ok && !GATHER) {
+        // fault path: the last `stages` armed stages may still have copies in flight; let
+        // them land before the CTA exits (each stage's latest phase completes by its own
+        // transaction bytes alone when the operands come only from TMA)
+        for (uint32_t j = it > (uint32_t)stages ? it - (uint32_t)stages : 0u; j < it; j++) {
+          mbar_drain(&full[j % (uint32_t)stages], (j / (uint32_t)stages) & 1u);
+        }
+      }
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
@@ -599,7 +607,12 @@ __global__ void __launch_bounds__(kThreads, 2)
             // +32 bytes per K=16 step inside the 128-byte swizzle row (>> 4 = 2)
             umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
           }
-          umma_commit(&empty[st]);
+          if (it == 0 && *(volatile uint32_t *)&g_test_withhold != 0u &&
+              atomicExch(&g_test_withhold, 0u) != 0u) {
+            // test hook (option "test_withhold_arrive"): stage 0 is never released
+          } else {
+            umma_commit(&empty[st]);
+          }
         }
         if (ok) umma_commit(&acc_full[buf]);
       }

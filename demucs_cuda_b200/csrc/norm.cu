@@ -4,6 +4,8 @@
 // deviation, backend_cpu.c:227-243) with the row split into chunks: each CTA computes its
 // chunk's mean and centred sum of squares from registers, and a second kernel merges the
 // chunks with Chan's parallel formula in double (norm.cu:42-107 does the same merge).
+#include <atomic>
+
 #include "common.cuh"
 
 namespace dcb {
@@ -24,12 +26,13 @@ static __device__ __forceinline__ T block_sum(T v, T *sh) {
   return r;
 }
 
-// partial[row][chunk] = {count, mean, M2}
+// partial[row][chunk] = {count, mean, M2}; one CTA per (row, chunk) pair, the pairs
+// flattened on grid.x so the row count is not bounded by grid.y's 65535
 __global__ void __launch_bounds__(kStatThreads)
     k_chunk_stats(const float *__restrict__ x, int64_t L, int nchunks, double *partial) {
   __shared__ double sh[kStatThreads / 32];
-  int64_t row = blockIdx.y;
-  int chunk = blockIdx.x;
+  const int64_t row = blockIdx.x / (unsigned)nchunks;
+  const int chunk = (int)(blockIdx.x - row * nchunks);
   int64_t c0 = (int64_t)chunk * kStatChunk;
   int64_t n = L - c0 < kStatChunk ? L - c0 : kStatChunk;
   const float *p = x + row * L + c0;
@@ -115,6 +118,10 @@ static size_t g_stat_cap = 0;
 
 void row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var) {
   if (rows <= 0 || L <= 0) return;
+  DCB_REQUIRE(L / kStatChunk < 0x7fffffff && rows < 0x7fffffff &&
+                  rows * ((L + kStatChunk - 1) / kStatChunk) < 0x7fffffff,
+              "row_stats: %lld rows of %lld elements exceed the launch limits",
+              (long long)rows, (long long)L);
   int nchunks = (int)((L + kStatChunk - 1) / kStatChunk);
   size_t need = (size_t)rows * nchunks * 3 * sizeof(double);
   if (need > g_stat_cap) {
@@ -126,8 +133,8 @@ void row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var)
     DCB_CUDA(cudaMalloc(&g_stat_scratch, cap));
     g_stat_cap = cap;
   }
-  dim3 grid(nchunks, (unsigned)rows);
-  k_chunk_stats<<<grid, kStatThreads, 0, stream()>>>(x, L, nchunks, g_stat_scratch);
+  k_chunk_stats<<<(unsigned)(rows * nchunks), kStatThreads, 0, stream()>>>(x, L, nchunks,
+                                                                          g_stat_scratch);
   DCB_LAUNCHED();
   k_combine_stats<<<grid_for(rows * 32, 128, 1 << 30), 128, 0, stream()>>>(g_stat_scratch, rows,
                                                                      nchunks, mean, var);
@@ -145,9 +152,13 @@ void row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var)
 constexpr int64_t kNoAllocPartials = 43690;
 static __device__ __align__(256) double g_rowstat_noalloc[kNoAllocPartials * 3];
 
-// Device address of g_rowstat_noalloc, looked up once per device.  On the host the array's
-// name is only a stand-in for the device symbol, so kernels must be given this address.
-static double *g_rowstat_noalloc_ptr[64] = {nullptr};
+// Device address of g_rowstat_noalloc, looked up once per device with that device current
+// (on the host the array's name is only a stand-in for the device symbol, so kernels must
+// be given this address).  Entries are published with release ordering, so two host
+// threads that race on a device's first call both see a complete pointer (at worst both
+// look it up).  The cache does not survive cudaDeviceReset: a host that resets a device
+// must not call this entry point on it again in the same process.
+static std::atomic<double *> g_rowstat_noalloc_ptr[64];
 
 static double *rowstat_noalloc_ptr() {
   int dev = 0;
@@ -155,81 +166,159 @@ static double *rowstat_noalloc_ptr() {
     fail("dk_row_stats_noalloc: no usable current CUDA device");
     return nullptr;
   }
-  if (!g_rowstat_noalloc_ptr[dev]) {
-    void *p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_rowstat_noalloc);
-    if (e != cudaSuccess || !p) {
-      fail("dk_row_stats_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-           cudaGetErrorString(e));
-      return nullptr;
-    }
-    g_rowstat_noalloc_ptr[dev] = (double *)p;
+  double *cached = g_rowstat_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (cached) return cached;
+  void *p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_rowstat_noalloc);
+  if (e != cudaSuccess || !p) {
+    fail("dk_row_stats_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+         cudaGetErrorString(e));
+    return nullptr;
   }
-  return g_rowstat_noalloc_ptr[dev];
+  g_rowstat_noalloc_ptr[dev].store((double *)p, std::memory_order_release);
+  return (double *)p;
 }
 
 int row_stats_noalloc(const float *x, int64_t rows, int64_t L, float *mean, float *var) {
   if (rows <= 0 || L <= 0) return 0;
+  // errors raised by this call, not one an earlier call left pending on this thread
+  const uint64_t err0 = error_count();
   const int64_t nchunks = (L + kStatChunk - 1) / kStatChunk;
-  if (rows * nchunks > kNoAllocPartials) {
-    fail("dk_row_stats_noalloc: %lld rows x %lld chunks of %d elements need %lld partials, "
-         "more than the %lld this entry point reserves; use dk_row_stats",
-         (long long)rows, (long long)nchunks, kStatChunk, (long long)(rows * nchunks),
-         (long long)kNoAllocPartials);
+  // each factor is checked before the product, so the product cannot overflow
+  if (rows > kNoAllocPartials || nchunks > kNoAllocPartials ||
+      rows * nchunks > kNoAllocPartials) {
+    fail("dk_row_stats_noalloc: %lld rows x %lld chunks of %d elements need more than the "
+         "%lld partials this entry point reserves; use dk_row_stats",
+         (long long)rows, (long long)nchunks, kStatChunk, (long long)kNoAllocPartials);
     return -1;
   }
   double *part = rowstat_noalloc_ptr();
   if (!part) return -1;
   // every (row, chunk) slot used below is written by k_chunk_stats before k_combine_stats
   // reads it, so the previous call's contents never leak into this one
-  dim3 grid((unsigned)nchunks, (unsigned)rows);
-  k_chunk_stats<<<grid, kStatThreads, 0, stream()>>>(x, L, (int)nchunks, part);
+  k_chunk_stats<<<(unsigned)(rows * nchunks), kStatThreads, 0, stream()>>>(x, L, (int)nchunks,
+                                                                          part);
   DCB_LAUNCHED();
   k_combine_stats<<<grid_for(rows * 32, 128, 1 << 30), 128, 0, stream()>>>(part, rows, (int)nchunks,
                                                                      mean, var);
   DCB_LAUNCHED();
-  return failed() ? -1 : 0;
+  return error_count() != err0 ? -1 : 0;
 }
 
-__global__ void k_groupnorm(const float *__restrict__ x, float *__restrict__ y,
-                            const float *__restrict__ mean, const float *__restrict__ var,
-                            const float *__restrict__ w, const float *__restrict__ b, int64_t B,
-                            int64_t C, int64_t S, int64_t G, float eps, int act) {
-  int64_t cpg = C / G;
-  if (act == 2) {
-    int64_t H = C / 2, n = B * H * S;
-    DCB_GRID_STRIDE(i, n) {
-      int64_t s = i % S, t = i / S, c = t % H, bi = t / H;
-      int64_t ga = c / cpg, gb = (c + H) / cpg;
-      float ra = 1.0f / sqrtf(var[bi * G + ga] + eps);
-      float rb = 1.0f / sqrtf(var[bi * G + gb] + eps);
-      float xa = x[(bi * C + c) * S + s], xb = x[(bi * C + c + H) * S + s];
-      float na = (xa - mean[bi * G + ga]) * ra * w[c] + b[c];
-      float nb = (xb - mean[bi * G + gb]) * rb * w[c + H] + b[c + H];
-      y[i] = na * sigmoid_f(nb);
+// ---- row-segment kernels of the ABI's apply steps (GroupNorm apply, GroupNorm(1) over the
+// last axis, per-row affine).  The work unit is one (row, segment) pair: a warp takes a
+// unit, loads the row's normalisation constants once, and streams the segment's
+// kSegFloats elements (float4 steps when the row length and the pointers allow it).
+constexpr int64_t kSegFloats = 2048;
+
+static inline unsigned seg_grid(int64_t units) {
+  return grid_for(units * 32, 256, 148 * 16);
+}
+
+static __device__ __forceinline__ float gn_one(float v, float m, float rs, float wc, float bc,
+                                               int act) {
+  const float n = (v - m) * rs * wc + bc;
+  return act == 1 ? gelu_f(n) : n;
+}
+
+// GroupNorm apply over x [B][C][S] (act 0 plain, 1 GELU); rows = B * C
+__global__ void __launch_bounds__(256)
+    k_gn_apply_rows(const float *__restrict__ x, float *__restrict__ y,
+                    const float *__restrict__ mean, const float *__restrict__ var,
+                    const float *__restrict__ w, const float *__restrict__ b, int64_t C,
+                    int64_t S, int64_t G, float eps, int act, int64_t rows, int64_t nseg,
+                    int vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t cpg = C / G;
+  for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < rows * nseg;
+       u += nwarps) {
+    const int64_t r = u / nseg, sg = u - r * nseg;
+    const int64_t bi = r / C, c = r - bi * C, gi = bi * G + c / cpg;
+    const float m = mean[gi], rs = 1.0f / sqrtf(var[gi] + eps), wc = w[c], bc = b[c];
+    const float *xr = x + r * S;
+    float *yr = y + r * S;
+    const int64_t e0 = sg * kSegFloats, e1 = e0 + kSegFloats < S ? e0 + kSegFloats : S;
+    if (vec) {
+      for (int64_t j = e0 / 4 + lane; j < e1 / 4; j += 32) {
+        float4 v = ((const float4 *)xr)[j];
+        v.x = gn_one(v.x, m, rs, wc, bc, act);
+        v.y = gn_one(v.y, m, rs, wc, bc, act);
+        v.z = gn_one(v.z, m, rs, wc, bc, act);
+        v.w = gn_one(v.w, m, rs, wc, bc, act);
+        ((float4 *)yr)[j] = v;
+      }
+    } else {
+      for (int64_t j = e0 + lane; j < e1; j += 32) yr[j] = gn_one(xr[j], m, rs, wc, bc, act);
     }
-    return;
-  }
-  int64_t n = B * C * S;
-  DCB_GRID_STRIDE(i, n) {
-    int64_t t = i / S, c = t % C, bi = t / C, g = c / cpg;
-    float rs = 1.0f / sqrtf(var[bi * G + g] + eps);
-    float v = (x[i] - mean[bi * G + g]) * rs * w[c] + b[c];
-    y[i] = act == 1 ? gelu_f(v) : v;
   }
 }
 
-__global__ void k_norm_last(const float *__restrict__ x, float *__restrict__ y,
-                            const float *__restrict__ mean, const float *__restrict__ var,
-                            const float *__restrict__ w, const float *__restrict__ b,
-                            int64_t rows, int64_t L, int64_t C, float eps) {
-  int64_t n = rows * L;
-  DCB_GRID_STRIDE(i, n) {
-    int64_t r = i / L, c = (i - r * L) % C;
-    float v = (x[i] - mean[r]) * (1.0f / sqrtf(var[r] + eps));
-    if (w) v *= w[c];
-    if (b) v += b[c];
-    y[i] = v;
+// GroupNorm + GLU over the channel halves: y [B][C/2][S] from x [B][C][S]; rows = B * C/2,
+// each output row reads its value row c and gate row c + C/2
+__global__ void __launch_bounds__(256)
+    k_gn_glu_rows(const float *__restrict__ x, float *__restrict__ y,
+                  const float *__restrict__ mean, const float *__restrict__ var,
+                  const float *__restrict__ w, const float *__restrict__ b, int64_t C,
+                  int64_t S, int64_t G, float eps, int64_t rows, int64_t nseg, int vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t H = C / 2, cpg = C / G;
+  for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < rows * nseg;
+       u += nwarps) {
+    const int64_t r = u / nseg, sg = u - r * nseg;
+    const int64_t bi = r / H, c = r - bi * H;
+    const int64_t ga = bi * G + c / cpg, gb = bi * G + (c + H) / cpg;
+    const float ma = mean[ga], ra = 1.0f / sqrtf(var[ga] + eps), wa = w[c], ba = b[c];
+    const float mb = mean[gb], rb = 1.0f / sqrtf(var[gb] + eps), wb = w[c + H], bb = b[c + H];
+    const float *xa = x + (bi * C + c) * S, *xb = xa + H * S;
+    float *yr = y + r * S;
+    const int64_t e0 = sg * kSegFloats, e1 = e0 + kSegFloats < S ? e0 + kSegFloats : S;
+    if (vec) {
+      for (int64_t j = e0 / 4 + lane; j < e1 / 4; j += 32) {
+        const float4 va = ((const float4 *)xa)[j], vb = ((const float4 *)xb)[j];
+        float4 o;
+        o.x = gn_one(va.x, ma, ra, wa, ba, 0) * sigmoid_f(gn_one(vb.x, mb, rb, wb, bb, 0));
+        o.y = gn_one(va.y, ma, ra, wa, ba, 0) * sigmoid_f(gn_one(vb.y, mb, rb, wb, bb, 0));
+        o.z = gn_one(va.z, ma, ra, wa, ba, 0) * sigmoid_f(gn_one(vb.z, mb, rb, wb, bb, 0));
+        o.w = gn_one(va.w, ma, ra, wa, ba, 0) * sigmoid_f(gn_one(vb.w, mb, rb, wb, bb, 0));
+        ((float4 *)yr)[j] = o;
+      }
+    } else {
+      for (int64_t j = e0 + lane; j < e1; j += 32) {
+        yr[j] = gn_one(xa[j], ma, ra, wa, ba, 0) * sigmoid_f(gn_one(xb[j], mb, rb, wb, bb, 0));
+      }
+    }
+  }
+}
+
+// Normalisation over whole rows of L elements with an affine on the last axis of length C
+// (channel j % C): the scalar path of dk_norm_apply_last for rows that k_norm_last4 does not
+// take.  A lane's channel index starts at (e0 + lane) % C and advances by 32 % C per step.
+__global__ void __launch_bounds__(256)
+    k_norm_last(const float *__restrict__ x, float *__restrict__ y,
+                const float *__restrict__ mean, const float *__restrict__ var,
+                const float *__restrict__ w, const float *__restrict__ b, int64_t rows,
+                int64_t L, int64_t C, float eps, int64_t nseg) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t step = 32 % C;
+  for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < rows * nseg;
+       u += nwarps) {
+    const int64_t r = u / nseg, sg = u - r * nseg;
+    const float m = mean[r], rs = 1.0f / sqrtf(var[r] + eps);
+    const float *xr = x + r * L;
+    float *yr = y + r * L;
+    const int64_t e0 = sg * kSegFloats, e1 = e0 + kSegFloats < L ? e0 + kSegFloats : L;
+    int64_t c = (e0 + lane) % C;
+    for (int64_t j = e0 + lane; j < e1; j += 32) {
+      float v = (xr[j] - m) * rs;
+      if (w) v *= w[c];
+      if (b) v += b[c];
+      yr[j] = v;
+      c += step;
+      if (c >= C) c -= C;
+    }
   }
 }
 
@@ -272,14 +361,38 @@ __global__ void k_norm_last4(const float4 *__restrict__ x, float4 *__restrict__ 
   }
 }
 
-__global__ void k_affine_rows(const float *__restrict__ x, float *__restrict__ y,
-                              const float *__restrict__ mean, const float *__restrict__ var,
-                              int64_t rows, int64_t L, float eps, int denorm) {
-  int64_t n = rows * L;
-  DCB_GRID_STRIDE(i, n) {
-    int64_t r = i / L;
-    float sd = sqrtf(var[r]) + eps, m = mean[r], v = x[i];
-    y[i] = denorm ? v * sd + m : (v - m) / sd;
+// HTDemucs input normalisation / output denormalisation per row (x - m) / (sd + eps) or
+// x (sd + eps) + m with sd = sqrt(var): one warp per (row, segment) unit, the row's
+// constants formed once per unit
+__global__ void __launch_bounds__(256)
+    k_affine_rows(const float *__restrict__ x, float *__restrict__ y,
+                  const float *__restrict__ mean, const float *__restrict__ var, int64_t rows,
+                  int64_t L, float eps, int denorm, int64_t nseg, int vec) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < rows * nseg;
+       u += nwarps) {
+    const int64_t r = u / nseg, sg = u - r * nseg;
+    const float sd = sqrtf(var[r]) + eps, m = mean[r];
+    const float *xr = x + r * L;
+    float *yr = y + r * L;
+    const int64_t e0 = sg * kSegFloats, e1 = e0 + kSegFloats < L ? e0 + kSegFloats : L;
+    if (vec) {
+      for (int64_t j = e0 / 4 + lane; j < e1 / 4; j += 32) {
+        float4 v = ((const float4 *)xr)[j];
+        if (denorm) {
+          v = make_float4(v.x * sd + m, v.y * sd + m, v.z * sd + m, v.w * sd + m);
+        } else {
+          v = make_float4((v.x - m) / sd, (v.y - m) / sd, (v.z - m) / sd, (v.w - m) / sd);
+        }
+        ((float4 *)yr)[j] = v;
+      }
+    } else {
+      for (int64_t j = e0 + lane; j < e1; j += 32) {
+        const float v = xr[j];
+        yr[j] = denorm ? v * sd + m : (v - m) / sd;
+      }
+    }
   }
 }
 
@@ -446,8 +559,9 @@ void layernorm(const float *x, void *y, const float *w, const float *b, int64_t 
   float *st = nullptr;
   DCB_CUDA(cudaMallocAsync(&st, (size_t)rows * 2 * sizeof(float), stream()));
   row_stats(x, rows, C, st, st + rows);
-  k_norm_last<<<grid_for(rows * C, 256), 256, 0, stream()>>>(x, (float *)y, st, st + rows, w,
-                                                             b, rows, C, C, eps);
+  const int64_t nseg = (C + kSegFloats - 1) / kSegFloats;
+  k_norm_last<<<seg_grid(rows * nseg), 256, 0, stream()>>>(x, (float *)y, st, st + rows, w, b,
+                                                           rows, C, C, eps, nseg);
   DCB_LAUNCHED();
   DCB_CUDA(cudaFreeAsync(st, stream()));
 }
@@ -469,17 +583,28 @@ int dk_row_stats_noalloc(const float *x, int64_t rows, int64_t L, float *mean, f
 void dk_groupnorm_apply(const float *x, float *y, const float *mean, const float *var,
                         const float *w, const float *b, int64_t B, int64_t C, int64_t S,
                         int64_t G, float eps, int act) {
-  int64_t n = B * (act == 2 ? C / 2 : C) * S;
-  if (n <= 0) return;
-  k_groupnorm<<<grid_for(n, 256), 256, 0, stream()>>>(x, y, mean, var, w, b, B, C, S, G, eps,
-                                                      act);
+  if (B <= 0 || C <= 0 || S <= 0) return;
+  DCB_REQUIRE(G > 0 && C % G == 0 && (act != 2 || C % 2 == 0),
+              "groupnorm_apply: C %lld, groups %lld, act %d", (long long)C, (long long)G, act);
+  const int64_t nseg = (S + kSegFloats - 1) / kSegFloats;
+  const int vec = S % 4 == 0 && (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
+  if (act == 2) {
+    const int64_t rows = B * (C / 2);
+    k_gn_glu_rows<<<seg_grid(rows * nseg), 256, 0, stream()>>>(x, y, mean, var, w, b, C, S, G,
+                                                               eps, rows, nseg, vec);
+  } else {
+    const int64_t rows = B * C;
+    k_gn_apply_rows<<<seg_grid(rows * nseg), 256, 0, stream()>>>(x, y, mean, var, w, b, C, S,
+                                                                 G, eps, act, rows, nseg, vec);
+  }
   DCB_LAUNCHED();
 }
 
 void dk_norm_apply_last(const float *x, float *y, const float *mean, const float *var,
                         const float *w, const float *b, int64_t rows, int64_t L, int64_t C,
                         float eps) {
-  if (rows * L <= 0) return;
+  if (rows <= 0 || L <= 0) return;
+  DCB_REQUIRE(C > 0, "norm_apply_last: C %lld", (long long)C);
   const bool al = ((uintptr_t)x | (uintptr_t)y | (uintptr_t)w | (uintptr_t)b) % 16 == 0;
   if (al && C % 4 == 0 && L % C == 0 && L / 4 < (1ll << 31) && rows <= 65535) {
     const int L4 = (int)(L / 4), C4 = (int)(C / 4);
@@ -487,17 +612,20 @@ void dk_norm_apply_last(const float *x, float *y, const float *mean, const float
     k_norm_last4<<<dim3(bx, (unsigned)rows), 256, 0, stream()>>>(
         (const float4 *)x, (float4 *)y, mean, var, w, b, L4, C4, eps);
   } else {
-    k_norm_last<<<grid_for(rows * L, 256), 256, 0, stream()>>>(x, y, mean, var, w, b, rows, L,
-                                                               C, eps);
+    const int64_t nseg = (L + kSegFloats - 1) / kSegFloats;
+    k_norm_last<<<seg_grid(rows * nseg), 256, 0, stream()>>>(x, y, mean, var, w, b, rows, L, C,
+                                                             eps, nseg);
   }
   DCB_LAUNCHED();
 }
 
 void dk_affine_rows(const float *x, float *y, const float *mean, const float *var,
                     int64_t rows, int64_t L, float eps, int denorm) {
-  if (rows * L <= 0) return;
-  k_affine_rows<<<grid_for(rows * L, 256), 256, 0, stream()>>>(x, y, mean, var, rows, L, eps,
-                                                               denorm);
+  if (rows <= 0 || L <= 0) return;
+  const int64_t nseg = (L + kSegFloats - 1) / kSegFloats;
+  const int vec = L % 4 == 0 && (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
+  k_affine_rows<<<seg_grid(rows * nseg), 256, 0, stream()>>>(x, y, mean, var, rows, L, eps,
+                                                             denorm, nseg, vec);
   DCB_LAUNCHED();
 }
 

@@ -19,6 +19,7 @@ static bool g_use_ext = false;
 static char g_name[256] = "cuda-sm100a";
 static int g_err_mode = DCB_ERRORS_FATAL;
 static thread_local char g_err[1024] = "";
+static thread_local uint64_t g_err_count = 0;  // errors recorded on this thread so far
 static std::atomic<uint64_t> g_launches{0};
 int g_opt_simt = 0;
 int g_opt_graphs = 0;
@@ -36,12 +37,14 @@ void fail(const char *fmt, ...) {
     fflush(stderr);
     exit(1);
   }
+  g_err_count++;
   if (!g_err[0]) {
     snprintf(g_err, sizeof(g_err), "%s", msg);
   }
 }
 
 bool failed() { return g_err[0] != 0; }
+uint64_t error_count() { return g_err_count; }
 
 static cudaStream_t g_override = nullptr;  // capture stream while a CUDA graph is recorded
 
@@ -242,6 +245,23 @@ int dcb_set_option(const char *name, int value) {
   } else if (!strcmp(name, "generic_epilogue")) {
     old = g_opt_generic_epi;
     g_opt_generic_epi = value;
+  } else if (!strcmp(name, "wait_limit_ms")) {
+    // limit of every bounded device-side wait (default 2000 ms)
+    if (value < 1) {
+      fail("wait_limit_ms must be >= 1 (got %d)", value);
+      return -1;
+    }
+    uint64_t ns = 0;
+    DCB_CUDA(cudaMemcpyFromSymbol(&ns, g_wait_ns, sizeof(ns)));
+    old = (int)(ns / 1000000ull);
+    ns = (uint64_t)value * 1000000ull;
+    DCB_CUDA(cudaMemcpyToSymbol(g_wait_ns, &ns, sizeof(ns)));
+  } else if (!strcmp(name, "test_withhold_arrive")) {
+    // test hook: the next tensor-core GEMM CTA keeps its first operand stage (see umma.cuh)
+    uint32_t v = value ? 1u : 0u, prev = 0;
+    DCB_CUDA(cudaMemcpyFromSymbol(&prev, g_test_withhold, sizeof(prev)));
+    DCB_CUDA(cudaMemcpyToSymbol(g_test_withhold, &v, sizeof(v)));
+    old = (int)prev;
   } else {
     fail("unknown option '%s'", name);
   }

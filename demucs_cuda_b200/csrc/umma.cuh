@@ -77,17 +77,22 @@ static __device__ __forceinline__ bool fault_pending() {
   return *(volatile uint32_t *)&g_dev_fault != 0;
 }
 // Bounded wait: false (and a fault bit) if the phase has not completed within
-// kWaitNs of wall-clock time, or at once if another CTA already recorded a fault, so a
-// protocol error ends every CTA of the grid quickly instead of hanging the GPU.
-constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s; legitimate waits are microseconds
+// g_wait_ns of wall-clock time, or at once if another CTA already recorded a fault, so a
+// protocol error ends every CTA of the grid quickly instead of hanging the GPU.  The limit
+// is 2 s (legitimate waits are microseconds); the host may shorten it (option
+// "wait_limit_ms") so that a test can make a wait expire quickly.
+// (g_wait_ns and the test hook g_test_withhold are defined in common.cuh.)
+static __device__ __forceinline__ uint64_t wait_limit_ns() {
+  return *(volatile uint64_t *)&g_wait_ns;
+}
 static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t fault) {
   if (mbar_try(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
+  const uint64_t t0 = global_ns(), lim = wait_limit_ns();
   for (uint32_t i = 1;; i++) {
     if (mbar_try(bar, parity)) return true;
     if ((i & 255u) == 0) {
       if (fault_pending()) return false;
-      if (global_ns() - t0 > kWaitNs) {
+      if (global_ns() - t0 > lim) {
         atomicOr(&g_dev_fault, fault);
         return false;
       }
@@ -99,17 +104,28 @@ static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
 static __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity,
                                                        uint32_t fault) {
   if (mbar_try_sleep(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
+  const uint64_t t0 = global_ns(), lim = wait_limit_ns();
   for (uint32_t i = 1;; i++) {
     if (mbar_try_sleep(bar, parity)) return true;
     if ((i & 15u) == 0) {
       if (fault_pending()) return false;
-      if (global_ns() - t0 > kWaitNs) {
+      if (global_ns() - t0 > lim) {
         atomicOr(&g_dev_fault, fault);
         return false;
       }
     }
   }
+}
+
+// Fault-path drain: wait (bounded by the same limit, but not cut short by the fault word)
+// for a phase that this CTA's own copies complete, so that no copy is still landing in
+// shared memory when the CTA exits.  Returns whether the phase completed.
+static __device__ __forceinline__ bool mbar_drain(uint64_t *bar, uint32_t parity) {
+  const uint64_t t0 = global_ns(), lim = wait_limit_ns();
+  while (!mbar_try(bar, parity)) {
+    if (global_ns() - t0 > lim) return false;
+  }
+  return true;
 }
 
 // generic-proxy smem writes -> visible to the async proxy (UMMA operand reads)

@@ -8,7 +8,7 @@ reference's shapes:
   Kaiming-uniform (bound 1/sqrt(fan_in), PyTorch's conv/linear default) from a numpy
   PCG64 stream, written as an fp32 safetensors file plus the model JSON
   (config.c:106-155 keys);
-* inputs: the BASELINE configurations -- a U[-0.5, 0.5] stereo segment (config 0) and a
+* inputs: the benchmark configurations -- a U[-0.5, 0.5] stereo segment (one forward) and a
   240 s sum of sinusoids plus noise (config 4).
 
 Both the reference oracle and this package load the same files, so both see identical

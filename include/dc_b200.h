@@ -133,11 +133,15 @@ void dk_ola(const float *frames, float *out, int64_t R, int nframes, int n_fft, 
  * that must never block (cudaMalloc/cudaFree can synchronise the whole device) or a host
  * that gives all device memory to its own pool.  Same results as dk_row_stats; the chunk
  * partials live in a fixed 1 MiB device array that every GPU loading the library keeps
- * until exit, so rows * ceil(L / 8192) must not exceed 43690 (larger calls are rejected
- * with an error and return -1).  Calls no cudaMalloc/cudaFree.  The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress) with that device current.
- * All calls share the one array: calls that overlap on the GPU (different streams, or
- * different host threads) race and must be serialised by the caller.  Returns 0 or -1. */
+ * until exit, so rows * ceil(L / 8192) must not exceed 43690.  A larger call is an error
+ * like any other: fatal in the default error mode (message, exit(1)); with
+ * DCB_ERRORS_RETURN it is recorded for dcb_last_error() and the call returns -1 before any
+ * launch.  Calls no cudaMalloc/cudaFree.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress) with that device current and caches it; the cache
+ * does not survive cudaDeviceReset.  All calls share the one array: calls that overlap on
+ * the GPU (different streams, or different host threads) race and must be serialised by
+ * the caller.  Returns 0, or -1 if this call recorded an error (an error left pending by
+ * an earlier call does not make it fail). */
 int dk_row_stats_noalloc(const float *x, int64_t rows, int64_t L, float *mean, float *var);
 
 /* ======================================================== Part 2: fused entry points */
@@ -192,7 +196,10 @@ void *dcb_get_stream(void);
  * "graphs" (1 = replay captured CUDA graphs for repeated forwards), "generic_epilogue"
  * (1 = channels-last convs use their generic epilogue instead of the specialised ones, for
  * A/B checks), "stream_istft" (0 = the two-pass inverse STFT instead of the fused
- * streaming one, for A/B checks). Returns the old value. */
+ * streaming one, for A/B checks), "wait_limit_ms" (limit of every bounded device-side
+ * wait, default 2000; tests shorten it), "test_withhold_arrive" (1 = the next tensor-core
+ * GEMM CTA does not release its first operand stage, so a bounded wait expires and sets
+ * the device fault word: the failure-detection test).  Returns the old value. */
 int dcb_set_option(const char *name, int value);
 /* Number of this library's kernels launched so far (monotonic). */
 uint64_t dcb_kernel_launches(void);

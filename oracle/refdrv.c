@@ -4,7 +4,10 @@
  * unchanged sources (worker-cuda/src/*.c, backend_cpu.c) by oracle/Makefile into
  * oracle/_ref/libdcref.so.  Only tests/, __graft_entry__.smoke() and bench.py's CPU
  * baseline leg load that library, always as the checker or the timed CPU baseline,
- * never as the product path.
+ * never as the product path.  The Makefile's `abi` target links the same file and the
+ * same reference model sources against libdc_b200.so instead of backend_cpu.c
+ * (oracle/_ref/abi/dcabi): the reference's own model code driving this library through
+ * its backend.h ABI, which the GPU tests compare with the CPU build.
  *
  * It exposes plain-pointer entry points (host float arrays, since the CPU backend's
  * "device" pointers are host pointers, backend_cpu.c:46-51) so Python can call:
@@ -31,11 +34,22 @@ static DcWeights g_w;
 static DcModel g_m;
 static int g_loaded = 0;
 
+/* Copies go through dc_to_host (tensor.c), so this driver runs unchanged over either
+ * backend: the reference's CPU backend (host pointers) or a GPU backend linked in its place
+ * (device pointers). */
+static void to_host(DcTensor t, float *out) {
+  float *h = dc_to_host(t);
+  memcpy(out, h, (size_t)dc_numel(t) * sizeof(float));
+  free(h);
+}
+
 static void emit(dcref_stage_fn fn, void *user, const char *name, DcTensor t) {
   if (!fn) {
     return;
   }
-  fn(name, dc_data(t), t.ndim, t.shape, user);
+  float *h = dc_to_host(t);
+  fn(name, h, t.ndim, t.shape, user);
+  free(h);
 }
 
 int dcref_load(const char *weights, const char *config) {
@@ -188,7 +202,7 @@ int dcref_forward(const float *mix_h, int B, int C, int T, float *out, dcref_sta
   emit(fn, user, "stems", y);
   int tout = y.shape[3];
   if (out) {
-    memcpy(out, dc_data(y), (size_t)dc_numel(y) * sizeof(float));
+    to_host(y, out);
   }
   dc_free(y);
   dc_free(mean);
@@ -206,7 +220,7 @@ int dcref_forward_plain(const float *mix_h, int B, int C, int T, float *out) {
   int s3[3] = {B, C, T};
   DcTensor mix = dc_from_host(mix_h, s3, 3);
   DcTensor y = dc_htdemucs_forward(&g_m, mix);
-  memcpy(out, dc_data(y), (size_t)dc_numel(y) * sizeof(float));
+  to_host(y, out);
   int tout = y.shape[3];
   dc_free(y);
   dc_free(mix);
@@ -233,7 +247,7 @@ int dcref_apply(const float *mix_h, int B, int C, int T, float *out, int shifts,
   int s3[3] = {B, C, T};
   DcTensor mix = dc_from_host(mix_h, s3, 3);
   DcTensor y = dc_apply_model(&g_m, mix, &o);
-  memcpy(out, dc_data(y), (size_t)dc_numel(y) * sizeof(float));
+  to_host(y, out);
   dc_free(y);
   dc_free(mix);
   return 0;
@@ -242,7 +256,7 @@ int dcref_apply(const float *mix_h, int B, int C, int T, float *out, int shifts,
 /* ------------------------------------------------------------ ops level */
 
 static void copy_out(DcTensor y, float *out) {
-  memcpy(out, dc_data(y), (size_t)dc_numel(y) * sizeof(float));
+  to_host(y, out);
   dc_free(y);
 }
 
@@ -397,7 +411,7 @@ int dcref_spec(const float *mix, int B, int C, int T, int nfft, float *out) {
   DcTensor z = dc_htdemucs_spec_cac(&st, mt);
   int frames = z.shape[3];
   if (out) {
-    memcpy(out, dc_data(z), (size_t)dc_numel(z) * sizeof(float));
+    to_host(z, out);
   }
   dc_free(z);
   dc_free(mt);

@@ -7,9 +7,10 @@ import subprocess
 import pytest
 
 from conftest import ROOT
+from oracle import REFERENCE_SRC
 
 HEADER = os.path.join(ROOT, "include", "dc_b200.h")
-REF_BACKEND_H = "/root/reference/worker-cuda/src/backend.h"
+REF_BACKEND_H = os.path.join(REFERENCE_SRC, "backend.h")
 
 
 def declared_functions(path):

@@ -13,7 +13,7 @@ import pytest
 
 from conftest import ROOT, rel_l2
 
-REF_SRC = "/root/reference/worker-cuda/src"
+from oracle import REFERENCE_SRC as REF_SRC
 REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libdcref.so")
 TWINS = os.path.join(ROOT, "demucs_cuda_b200", "twins", "dkx_cpu.c")
 

@@ -219,6 +219,8 @@ def test_linear_fused(dcb, ref, torch_cuda, R, IN, OUT):
     (2, 33, 47, 64, 8),       # test_kernels.c
     (1, 300, 300, 384, 8),    # test_kernels.c
     (1, 700, 350, 384, 8),    # cross attention, partial key/query tiles
+    (2, 257, 131, 512, 8),    # head dim 64 (dim 512, 8 heads), partial tiles both ways
+    (1, 1024, 700, 512, 8),   # head dim 64, cross-attention shape class
 ])
 def test_attention_fused(dcb, ref, torch_cuda, B, Tq, Tk, D, H, simt):
     torch = torch_cuda

@@ -1,7 +1,7 @@
 """Model-level parity of the B200 engine against the reference (htdemucs_6s forward).
 
 Mirrors the reference's tests/test_compare.c: every stage is fed the reference's own output
-of the previous stage (teacher forcing) and compared under the BASELINE gate of 8e-4
+of the previous stage (teacher forcing) and compared under the stage gate of 8e-4
 relative L2, then the end-to-end stems are compared (gate 1e-3 relative L2, i.e. SNR >= 60
 dB).  The reference run is oracle/_ref (the reference's CPU backend and model code); at
 full segment size the committed digest of that run (tests/golden/full_digest.json) is the

@@ -47,7 +47,7 @@ def test_shards_cover_every_segment_once(count):
 
 
 def test_240s_track_plan_counts():
-    """42 segment forwards (40 full + 2 tails) per shift, in 6 forward
+    """The 240 s benchmark track: 42 segment forwards (40 full + 2 tails) per shift, in 6 forward
     calls of 7 segments at batch size 8."""
     import demucs_cuda_b200 as d
     offs, calls = d.segment_plan(10_584_000 + 22050 - 7000)  # shifted track length range

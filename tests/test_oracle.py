@@ -110,7 +110,7 @@ def test_port_ops_vs_reference(case):
 
 def test_port_teacher_forced_stages_vs_reference():
     """Each model stage of the port fed the reference's previous-stage output, as
-    test_compare.c does, against the reference's stage output (BASELINE gate 8e-4)."""
+    test_compare.c does, against the reference's stage output (stage gate 8e-4)."""
     ref = _ref()
     from demucs_cuda_b200 import synth
     from oracle import port

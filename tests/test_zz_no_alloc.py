@@ -57,3 +57,29 @@ def test_noalloc_rejects_oversized(torch_cuda):
     assert r == -1
     with pytest.raises(dcb.BackendError, match="reserves"):
         dcb.check(True, "oversized")
+
+
+def test_noalloc_reports_only_its_own_errors(torch_cuda):
+    """An error left pending on this thread by an earlier, unrelated call does not make a
+    good call fail; a call whose factors would overflow the partials product is rejected
+    before any launch."""
+    torch = torch_cuda
+    import demucs_cuda_b200 as dcb
+    L_ = dcb.lib()
+    dcb.check(True, "clean start")
+    assert L_.dcb_set_option(b"no-such-option", 1) == -1   # records an error, left pending
+    x = torch.randn(4, 1000, device="cuda")
+    st = torch.zeros(8, device="cuda")
+    r = L_.dk_row_stats_noalloc(C.c_void_p(x.data_ptr()), 4, 1000, C.c_void_p(st.data_ptr()),
+                                C.c_void_p(st.data_ptr() + 16))
+    torch.cuda.synchronize()
+    assert r == 0
+    assert "no-such-option" in L_.dcb_last_error(1).decode()
+    xd = x.double().cpu().numpy()
+    assert np.abs(st[:4].cpu().numpy() - xd.mean(axis=1)).max() < 1e-5
+    # 3 rows x 2^27 chunks: each factor is checked before the product
+    r = L_.dk_row_stats_noalloc(C.c_void_p(x.data_ptr()), 3, 1 << 40, C.c_void_p(st.data_ptr()),
+                                C.c_void_p(st.data_ptr() + 16))
+    assert r == -1
+    with pytest.raises(dcb.BackendError, match="reserves"):
+        dcb.check(True, "overflowing factors")
