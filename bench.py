@@ -4,9 +4,10 @@
 One step = the whole of dc_apply_model (apply.c:179-306) on a 240 s synthetic stereo track:
 shifts = 1, 7.8 s segments at overlap 0.25, batches of 8 segments -> 42 segment forwards of
 the full htdemucs_6s model (random-init fp16 weights), transition-weighted overlap-add.
-With N GPUs (one process each, torchrun) the packed weight block is NCCL-broadcast from
-rank 0 once, the segments are sharded across ranks (strong scaling: the track is fixed),
-and the weighted stems are summed onto rank 0 with one NCCL reduce per step.
+With N GPUs (one process each, torchrun) rank 0's packed weight block is NCCL-broadcast
+once to ranks that hold only the layout, the segments are split into N contiguous blocks
+(strong scaling: the track is fixed), each rank computes its weighted stems over its own
+output window only, and rank 0 gathers the windows (NCCL) and overlap-adds them.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
@@ -225,8 +226,10 @@ def b200_arm(args):
     if world > 1:
         dist.barrier()
     w, c = model_files()
-    model = dcb.Model(w, c)
-    # weights: NCCL broadcast of rank 0's packed block (all ranks pack identically)
+    # weights: rank 0 reads and packs the file; the other ranks build the same layout from
+    # the safetensors header alone (a zeroed device block) and receive rank 0's packed
+    # block through one NCCL broadcast, checked word for word afterwards
+    model = dcb.Model(w, c, layout_only=(world > 1 and rank != 0))
     bcast_ms = None
     if world > 1:
         ptr, nbytes = model.weight_block()
@@ -236,6 +239,14 @@ def b200_arm(args):
         dist.broadcast(view, src=0)
         torch.cuda.synchronize()
         bcast_ms = (time.time() - t0) * 1e3
+        words = view[: nbytes // 4 * 4].view(torch.int32).to(torch.int64)
+        pos = torch.arange(words.numel(), device="cuda", dtype=torch.int64) % 65521 + 1
+        ck = torch.stack([words.sum(), (words * pos).sum()])
+        del words, pos
+        allck = [torch.empty_like(ck) for _ in range(world)]
+        dist.all_gather(allck, ck)
+        if any(not torch.equal(a, allck[0]) for a in allck):
+            raise RuntimeError("weight block differs from rank 0's after the broadcast")
     x = track(args.seconds)
     T = x.shape[-1]
     mix_host = torch.from_numpy(x).pin_memory()
@@ -245,11 +256,25 @@ def b200_arm(args):
     kw = dict(shifts=args.shifts, overlap=args.overlap, batch_size=args.batch,
               shard_index=rank, shard_count=world)
     nfw, nbatched = model.apply_plan(T, **kw)
+    rows = model.n_sources * 2
+    if world > 1:
+        # each rank's share is non-zero only on its output window: ranks write their window,
+        # rank 0 gathers them (NCCL over NVLink) and overlap-adds them into the stems
+        spans = [model.apply_window(T, **dict(kw, shard_index=r)) for r in range(world)]
+        wmax = max(h - l for l, h in spans)
+        win = torch.empty((rows, wmax), device="cuda", dtype=torch.float32)
+        gbuf = (torch.empty((world, rows, wmax), device="cuda", dtype=torch.float32)
+                if rank == 0 else None)
+        glist = list(gbuf.unbind(0)) if rank == 0 else None
 
     def step():
-        model.apply(mix, out=out, **kw)
-        if world > 1:
-            dist.reduce(out, dst=0)
+        if world == 1:
+            model.apply(mix, out=out, **kw)
+            return
+        model.apply_shard(mix, win, **kw)
+        dist.gather(win, gather_list=glist, dst=0)
+        if rank == 0:
+            dcb.merge_windows(out, gbuf, [l for l, _ in spans], [h for _, h in spans])
 
     def step_e2e():
         mix.copy_(mix_host, non_blocking=True)
@@ -366,7 +391,10 @@ def b200_arm(args):
                                    f"{args.batch}, {nfw} segment forwards in {nbatched} "
                                    "forward calls (this rank)",
                        "model": "htdemucs_6s", "segment_samples": 343980,
-                       "parallelism": f"segment data parallel x{world}",
+                       "parallelism": f"segment data parallel x{world}" + (
+                           f": contiguous segment blocks per rank, output windows of at most "
+                           f"{wmax} samples gathered to rank 0 (NCCL) and overlap-added"
+                           if world > 1 else ""),
                        "l2": "inputs and activations larger than L2 (126 MB) every step",
                        "weight_broadcast_ms": bcast_ms},
             "e2e": {"value": e2e, "unit": UNIT, "ms_per_step": ms_e2e,

@@ -38,10 +38,12 @@ ENGINE_SYMBOLS = [
     "dcb_set_error_mode", "dcb_last_error", "dcb_set_stream", "dcb_use_own_stream",
     "dcb_get_stream",
     "dcb_set_option", "dcb_kernel_launches", "dcb_device_fault", "dcb_trace_start",
-    "dcb_trace_stop", "dcb_trace_dump", "dcb_model_load",
+    "dcb_trace_stop", "dcb_trace_dump", "dcb_model_load", "dcb_model_load_layout",
+    "dcb_model_save_packed", "dcb_model_load_packed",
     "dcb_model_free", "dcb_model_info", "dcb_model_weight_bytes", "dcb_model_weight_block",
     "dcb_forward", "dcb_stage_encoder", "dcb_stage_decoder", "dcb_stage_transformer",
     "dcb_apply_defaults", "dcb_apply", "dcb_apply_plan", "dcb_py_randint", "dcb_segment_plan",
+    "dcb_apply_window", "dcb_apply_shard", "dcb_merge_windows",
 ]
 ALL_SYMBOLS = BACKEND_SYMBOLS + NOALLOC_SYMBOLS + FUSED_SYMBOLS + ENGINE_SYMBOLS
 
@@ -150,6 +152,9 @@ def signatures():
                                  C.POINTER(C.c_double), C.POINTER(i32), i32]),
         "dcb_trace_dump": (i32, [C.c_char_p]),
         "dcb_model_load": (vp, [C.c_char_p, C.c_char_p]),
+        "dcb_model_load_layout": (vp, [C.c_char_p, C.c_char_p]),
+        "dcb_model_save_packed": (i32, [vp, C.c_char_p]),
+        "dcb_model_load_packed": (vp, [C.c_char_p]),
         "dcb_model_free": (None, [vp]),
         "dcb_model_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32),
                                  C.POINTER(i32), C.POINTER(f32)]),
@@ -167,6 +172,11 @@ def signatures():
         "dcb_apply": (i32, [vp, vp, i32, i32, vp, C.POINTER(DcbApplyOpts)]),
         "dcb_apply_plan": (i32, [vp, i32, C.POINTER(DcbApplyOpts), C.POINTER(i32),
                                  C.POINTER(i32)]),
+        "dcb_apply_window": (i32, [i32, f32, i32, i32, C.POINTER(DcbApplyOpts),
+                                   C.POINTER(i64), C.POINTER(i64)]),
+        "dcb_apply_shard": (i32, [vp, vp, i32, i32, vp, i64, C.POINTER(DcbApplyOpts)]),
+        "dcb_merge_windows": (i32, [vp, i64, i64, vp, i64, i64, C.POINTER(i64),
+                                    C.POINTER(i64), i32]),
     }
 
 
@@ -199,12 +209,23 @@ def _ptr(t):
 
 
 class Model:
-    """htdemucs_6s on the B200 engine (weights packed once on the device)."""
+    """htdemucs_6s on the B200 engine (weights packed once on the device).
 
-    def __init__(self, weights: str, config: str):
+    Model(weights, config) reads and packs a safetensors file; with layout_only=True only
+    its header is read and the device block is left zeroed for the caller to fill (the
+    data-parallel ranks receive rank 0's block by broadcast); Model.from_packed(path) loads
+    a pre-packed image written by save_packed()."""
+
+    def __init__(self, weights: str, config: str = "", layout_only: bool = False,
+                 packed: str = ""):
         require_gpu()
         L = lib()
-        self._h = L.dcb_model_load(weights.encode(), config.encode())
+        if packed:
+            self._h = L.dcb_model_load_packed(packed.encode())
+        elif layout_only:
+            self._h = L.dcb_model_load_layout(weights.encode(), config.encode())
+        else:
+            self._h = L.dcb_model_load(weights.encode(), config.encode())
         if not self._h:
             check(False, "model load")
         ns, ac, vl, sr = C.c_int(), C.c_int(), C.c_int(), C.c_int()
@@ -213,6 +234,15 @@ class Model:
                          C.byref(seg))
         self.n_sources, self.audio_channels = ns.value, ac.value
         self.valid_length, self.samplerate, self.segment = vl.value, sr.value, seg.value
+
+    @classmethod
+    def from_packed(cls, path: str) -> "Model":
+        return cls("", packed=path)
+
+    def save_packed(self, path: str):
+        """Write the pre-packed on-disk image (dcb_model_save_packed)."""
+        r = lib().dcb_model_save_packed(self._h, path.encode())
+        check(r == 0, "save_packed")
 
     def close(self):
         if getattr(self, "_h", None):
@@ -325,6 +355,27 @@ class Model:
         check(r == 0, "apply")
         return out
 
+    def apply_window(self, T: int, **kw):
+        """(lo, hi): the output window of this shard's share (dcb_apply_window)."""
+        o = self.apply_opts(**kw)
+        lo, hi = C.c_int64(), C.c_int64()
+        r = lib().dcb_apply_window(self.samplerate, self.segment, self.valid_length, T,
+                                   C.byref(o), C.byref(lo), C.byref(hi))
+        check(r == 0, "apply_window")
+        return lo.value, hi.value
+
+    def apply_shard(self, mix, win, **kw):
+        """This shard's share of apply() over its window only: win [B*S*C, ld] (CUDA),
+        column j = time lo + j (dcb_apply_shard)."""
+        use_torch_stream()
+        mix = mix.contiguous()
+        B, Cc, T = mix.shape
+        o = self.apply_opts(**kw)
+        r = lib().dcb_apply_shard(self._h, _ptr(mix), B, T, _ptr(win), win.stride(0),
+                                  C.byref(o))
+        check(r == 0, "apply_shard")
+        return win
+
     def apply_plan(self, T: int, **kw):
         o = self.apply_opts(**kw)
         nf, nb = C.c_int(), C.c_int()
@@ -354,6 +405,20 @@ def gemm_half(A, B, C_=None, alpha=1.0, beta=0.0):
                        beta, _ptr(C_), C_.stride(1), C_.stride(0), batch)
     check(True, "dk_gemm_half")
     return C_
+
+
+def merge_windows(out, wins, lo, hi):
+    """out [rows, T] = overlap-add of the gathered shard windows wins [n, rows, ld] placed at
+    lo[i] .. hi[i] (dcb_merge_windows)."""
+    use_torch_stream()
+    n = len(lo)
+    los, his = (C.c_int64 * n)(*lo), (C.c_int64 * n)(*hi)
+    o2 = out.reshape(-1, out.shape[-1])   # a view of the contiguous [.., T] output
+    rows, T = o2.shape
+    r = lib().dcb_merge_windows(_ptr(o2), rows, T, _ptr(wins), wins.stride(1),
+                                wins.stride(0), los, his, n)
+    check(r == 0, "merge_windows")
+    return out
 
 
 def apply_opts(shifts=1, overlap=0.25, transition_power=1.0, batch_size=8, seed=1,

@@ -143,22 +143,29 @@ static void apply_keys(Cfg &c, const char *js, bool kw) {
 #undef KF
 }
 
-static bool load_config(const char *path, Cfg &c) {
+// The model JSON's text (empty text = the htdemucs_6s defaults).
+static bool read_text(const char *path, std::string &js) {
+  js.clear();
+  if (!path || !path[0]) return true;
+  FILE *f = fopen(path, "rb");
+  if (!f) {
+    fail("cannot read config %s", path);
+    return false;
+  }
+  char buf[4096];
+  size_t n;
+  while ((n = fread(buf, 1, sizeof(buf), f)) > 0) js.append(buf, n);
+  fclose(f);
+  return true;
+}
+
+static bool load_config(const std::string &js, Cfg &c) {
   c = Cfg();
   c.valid_length = (int)(c.segment * (float)c.samplerate);
-  FILE *f = path && path[0] ? fopen(path, "rb") : nullptr;
-  if (f) {
-    std::string js;
-    char buf[4096];
-    size_t n;
-    while ((n = fread(buf, 1, sizeof(buf), f)) > 0) js.append(buf, n);
-    fclose(f);
+  if (!js.empty()) {
     apply_keys(c, js.c_str(), false);
     const char *kw = find_key(js.c_str(), "kwargs");
     if (kw) apply_keys(c, kw, true);
-  } else if (path && path[0]) {
-    fail("cannot read config %s", path);
-    return false;
   }
   c.hop = c.nfft / 4;
   if (c.valid_length <= 0) c.valid_length = (int)(c.segment * (float)c.samplerate);
@@ -369,6 +376,9 @@ struct DcbModel {
   dcb::Cfg cfg;
   void *block = nullptr;
   size_t block_bytes = 0;
+  // what the layout was built from (kept for the packed on-disk image)
+  std::string cfg_text, st_header;
+  uint64_t st_data_len = 0;
   int depth = 0;
   dcb::EncW enc[8], tenc[8];
   dcb::DecW dec[8], tdec[8];
@@ -407,13 +417,14 @@ struct Staging {
 
 struct Loader {
   std::unordered_map<std::string, StEntry> ents;
-  const uint8_t *data = nullptr;
+  const uint8_t *data = nullptr;  // null: layout only (every element reads as zero)
   size_t data_len = 0;
   std::string missing;
 
   bool has(const std::string &n) const { return ents.count(n) != 0; }
   // element i as float (F32 / F16 / BF16, weights.c:216-236)
   float at(const StEntry &e, size_t i) const {
+    if (!data) return 0.f;
     const uint8_t *p = data + e.begin;
     if (e.dtype == "F32") {
       float v;
@@ -646,64 +657,14 @@ static int glu_bn_for(int O2) {
   return bn;
 }
 
-}  // namespace dcb
-
-using namespace dcb;
-
-extern "C" {
-
-DcbModel *dcb_model_load(const char *st_path, const char *cfg_path) {
-  DcbModel *m = new DcbModel();
-  if (!load_config(cfg_path, m->cfg)) {
-    delete m;
-    return nullptr;
-  }
+// Every GEMM operand and parameter of the model staged into `st` in the device block's
+// layout (the loader rule of weights.c:298-349 plus this engine's derived forms).  With a
+// layout-only loader (no tensor data) the layout is the same and the bytes are zeros.
+static bool stage_model(DcbModel *m, Loader &L, Staging &st, const char *what) {
   const Cfg &c = m->cfg;
-  FILE *f = fopen(st_path, "rb");
-  if (!f) {
-    fail("cannot read weights %s", st_path);
-    delete m;
-    return nullptr;
-  }
-  std::vector<uint8_t> file;
-  {
-    uint8_t buf[1 << 16];
-    size_t n;
-    while ((n = fread(buf, 1, sizeof(buf), f)) > 0) file.insert(file.end(), buf, buf + n);
-    fclose(f);
-  }
-  if (file.size() < 8) {
-    fail("weights file too small: %s", st_path);
-    delete m;
-    return nullptr;
-  }
-  uint64_t hlen = 0;
-  for (int i = 7; i >= 0; i--) hlen = (hlen << 8) | file[i];
-  Loader L;
-  if (8 + hlen > file.size() ||
-      !parse_st_header((const char *)file.data() + 8, (size_t)hlen, L.ents)) {
-    fail("corrupt safetensors header in %s", st_path);
-    delete m;
-    return nullptr;
-  }
-  L.data = file.data() + 8 + hlen;
-  L.data_len = file.size() - 8 - hlen;
-  for (auto &kv : L.ents) {
-    size_t numel = 1;
-    for (int s : kv.second.shape) numel *= (size_t)s;
-    const StEntry &e = kv.second;
-    if ((e.dtype != "F32" && e.dtype != "F16" && e.dtype != "BF16") || e.end < e.begin ||
-        e.end > L.data_len || e.end - e.begin != numel * dtype_size(e.dtype)) {
-      fail("bad tensor entry %s (%s)", kv.first.c_str(), e.dtype.c_str());
-      delete m;
-      return nullptr;
-    }
-  }
-
-  Staging st;
+  char p[160];
   bool ok = true;
   m->depth = c.depth;
-  char p[160];
   for (int i = 0; i < c.depth && ok; i++) {
     EncW &e = m->enc[i];
     snprintf(p, sizeof(p), "encoder.%d.conv", i);
@@ -806,24 +767,31 @@ DcbModel *dcb_model_load(const char *st_path, const char *cfg_path) {
     m->hidden = m->layers[0][0].lin1.out;
   }
   if (!ok) {
-    fail("weights %s: missing or malformed tensor '%s'", st_path, L.missing.c_str());
-    delete m;
-    return nullptr;
+    fail("weights %s: missing or malformed tensor '%s'", what, L.missing.c_str());
+    return false;
   }
   // periodic Hann window in double, stored as float (stft.c:5-20)
   std::vector<float> win(c.nfft);
   for (int i = 0; i < c.nfft; i++)
     win[i] = (float)(0.5 - 0.5 * cos(2.0 * 3.14159265358979323846 * (double)i / (double)c.nfft));
   stage_f32(st, win, &m->window);
+  return true;
+}
 
+// Allocate the device block, fill it from `src` (st's bytes, a packed image, or nothing: a
+// zeroed block that a broadcast fills) and point every staged slot into it.
+static bool upload_block(DcbModel *m, Staging &st, const uint8_t *src) {
   m->block_bytes = st.bytes.size();
   if (cudaMalloc(&m->block, m->block_bytes ? m->block_bytes : 1) != cudaSuccess) {
     (void)cudaGetLastError();
     fail("out of device memory uploading weights (%.1f MB)", (double)m->block_bytes / 1048576.0);
-    delete m;
-    return nullptr;
+    return false;
   }
-  DCB_CUDA(cudaMemcpy(m->block, st.bytes.data(), m->block_bytes, cudaMemcpyHostToDevice));
+  if (src) {
+    DCB_CUDA(cudaMemcpy(m->block, src, m->block_bytes, cudaMemcpyHostToDevice));
+  } else {
+    DCB_CUDA(cudaMemset(m->block, 0, m->block_bytes));
+  }
   for (auto &fx : st.fix) *fx.second = (uint8_t *)m->block + fx.first;
   // the stream-ordered pool keeps freed activation memory for reuse
   cudaMemPool_t pool;
@@ -833,7 +801,204 @@ DcbModel *dcb_model_load(const char *st_path, const char *cfg_path) {
     uint64_t thr = UINT64_MAX;
     cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
   }
+  return !failed();
+}
+
+// A model from its config text and safetensors header; `data` (the tensor bytes, or null
+// for layout only) and `block` (a packed block image to upload instead of the staged
+// bytes, or null).
+static DcbModel *build_model(const std::string &cfg_text, const std::string &header,
+                             const uint8_t *data, uint64_t data_len, const uint8_t *block,
+                             uint64_t block_bytes, bool zero_block, const char *what) {
+  DcbModel *m = new DcbModel();
+  if (!load_config(cfg_text, m->cfg)) {
+    delete m;
+    return nullptr;
+  }
+  m->cfg_text = cfg_text;
+  m->st_header = header;
+  m->st_data_len = data_len;
+  Loader L;
+  if (!parse_st_header(header.data(), header.size(), L.ents)) {
+    fail("corrupt safetensors header in %s", what);
+    delete m;
+    return nullptr;
+  }
+  L.data = data;
+  L.data_len = data_len;
+  for (auto &kv : L.ents) {
+    size_t numel = 1;
+    for (int s : kv.second.shape) numel *= (size_t)s;
+    const StEntry &e = kv.second;
+    if ((e.dtype != "F32" && e.dtype != "F16" && e.dtype != "BF16") || e.end < e.begin ||
+        e.end > L.data_len || e.end - e.begin != numel * dtype_size(e.dtype)) {
+      fail("bad tensor entry %s (%s)", kv.first.c_str(), e.dtype.c_str());
+      delete m;
+      return nullptr;
+    }
+  }
+  Staging st;
+  if (!stage_model(m, L, st, what)) {
+    delete m;
+    return nullptr;
+  }
+  if (block && block_bytes != st.bytes.size()) {
+    fail("%s: packed block of %llu bytes, the layout needs %zu", what,
+         (unsigned long long)block_bytes, st.bytes.size());
+    delete m;
+    return nullptr;
+  }
+  if (!upload_block(m, st, block ? block : (zero_block ? nullptr : st.bytes.data()))) {
+    dcb_model_free(m);
+    return nullptr;
+  }
   return m;
+}
+
+// safetensors file: 8-byte little-endian header length, JSON header, tensor data
+static bool read_st(const char *path, bool header_only, std::string &header,
+                    std::vector<uint8_t> &data, uint64_t &data_len) {
+  FILE *f = fopen(path, "rb");
+  if (!f) {
+    fail("cannot read weights %s", path);
+    return false;
+  }
+  uint8_t lb[8];
+  bool ok = fread(lb, 1, 8, f) == 8;
+  uint64_t hlen = 0;
+  for (int i = 7; i >= 0; i--) hlen = (hlen << 8) | lb[i];
+  fseeko(f, 0, SEEK_END);
+  const uint64_t size = (uint64_t)ftello(f);
+  ok = ok && hlen <= size - 8 && size >= 8;
+  if (ok) {
+    header.resize(hlen);
+    fseeko(f, 8, SEEK_SET);
+    ok = fread(&header[0], 1, hlen, f) == hlen;
+  }
+  data_len = ok ? size - 8 - hlen : 0;
+  if (ok && !header_only) {
+    data.resize(data_len);
+    ok = fread(data.data(), 1, data_len, f) == data_len;
+  }
+  fclose(f);
+  if (!ok) fail("weights file %s is truncated or not safetensors", path);
+  return ok;
+}
+
+static DcbModel *load_model(const char *st_path, const char *cfg_path, bool layout_only) {
+  std::string cfg_text, header;
+  std::vector<uint8_t> data;
+  uint64_t data_len = 0;
+  if (!read_text(cfg_path, cfg_text) || !read_st(st_path, layout_only, header, data, data_len))
+    return nullptr;
+  return build_model(cfg_text, header, layout_only ? nullptr : data.data(), data_len, nullptr, 0,
+                     layout_only, st_path);
+}
+
+}  // namespace dcb
+
+using namespace dcb;
+
+extern "C" {
+
+DcbModel *dcb_model_load(const char *st_path, const char *cfg_path) {
+  return dcb::load_model(st_path, cfg_path, false);
+}
+
+DcbModel *dcb_model_load_layout(const char *st_path, const char *cfg_path) {
+  return dcb::load_model(st_path, cfg_path, true);
+}
+
+// Packed image: "DCBPACK1", then u64-length-prefixed config text, safetensors header,
+// safetensors data length (u64), block bytes, and an FNV-1a 64 checksum of the block.
+static const char kPackMagic[8] = {'D', 'C', 'B', 'P', 'A', 'C', 'K', '1'};
+
+static uint64_t fnv1a64(const uint8_t *p, size_t n) {
+  uint64_t h = 1469598103934665603ull;
+  for (size_t i = 0; i < n; i++) {
+    h ^= p[i];
+    h *= 1099511628211ull;
+  }
+  return h;
+}
+
+int dcb_model_save_packed(const DcbModel *m, const char *path) {
+  if (!m || !m->block || !path) return -1;
+  std::vector<uint8_t> blk(m->block_bytes);
+  DCB_CUDA(cudaDeviceSynchronize());
+  DCB_CUDA(cudaMemcpy(blk.data(), m->block, m->block_bytes, cudaMemcpyDeviceToHost));
+  if (failed()) return -1;
+  FILE *f = fopen(path, "wb");
+  if (!f) {
+    fail("cannot write %s", path);
+    return -1;
+  }
+  auto put64 = [&](uint64_t v) {
+    uint8_t b[8];
+    for (int i = 0; i < 8; i++) b[i] = (uint8_t)(v >> (8 * i));
+    return fwrite(b, 1, 8, f) == 8;
+  };
+  bool ok = fwrite(kPackMagic, 1, 8, f) == 8;
+  ok = ok && put64(m->cfg_text.size()) &&
+       fwrite(m->cfg_text.data(), 1, m->cfg_text.size(), f) == m->cfg_text.size();
+  ok = ok && put64(m->st_header.size()) &&
+       fwrite(m->st_header.data(), 1, m->st_header.size(), f) == m->st_header.size();
+  ok = ok && put64(m->st_data_len) && put64(blk.size()) &&
+       fwrite(blk.data(), 1, blk.size(), f) == blk.size();
+  ok = ok && put64(fnv1a64(blk.data(), blk.size()));
+  ok = (fclose(f) == 0) && ok;
+  if (!ok) {
+    fail("short write to %s", path);
+    return -1;
+  }
+  return 0;
+}
+
+DcbModel *dcb_model_load_packed(const char *path) {
+  FILE *f = path ? fopen(path, "rb") : nullptr;
+  if (!f) {
+    fail("cannot read packed weights %s", path ? path : "(null)");
+    return nullptr;
+  }
+  auto get64 = [&](uint64_t &v) {
+    uint8_t b[8];
+    if (fread(b, 1, 8, f) != 8) return false;
+    v = 0;
+    for (int i = 7; i >= 0; i--) v = (v << 8) | b[i];
+    return true;
+  };
+  char magic[8];
+  std::string cfg_text, header;
+  std::vector<uint8_t> blk;
+  uint64_t n = 0, data_len = 0, sum = 0;
+  bool ok = fread(magic, 1, 8, f) == 8 && !memcmp(magic, kPackMagic, 8);
+  ok = ok && get64(n) && n < (1u << 24);
+  if (ok) {
+    cfg_text.resize(n);
+    ok = fread(&cfg_text[0], 1, n, f) == n;
+  }
+  ok = ok && get64(n) && n < (1u << 28);
+  if (ok) {
+    header.resize(n);
+    ok = fread(&header[0], 1, n, f) == n;
+  }
+  ok = ok && get64(data_len) && get64(n) && n < ((uint64_t)1 << 36);
+  if (ok) {
+    blk.resize(n);
+    ok = fread(blk.data(), 1, n, f) == n;
+  }
+  ok = ok && get64(sum);
+  fclose(f);
+  if (!ok) {
+    fail("%s is not a packed weight image (or is truncated)", path);
+    return nullptr;
+  }
+  if (fnv1a64(blk.data(), blk.size()) != sum) {
+    fail("%s: packed block checksum mismatch", path);
+    return nullptr;
+  }
+  return dcb::build_model(cfg_text, header, nullptr, data_len, blk.data(), blk.size(), false,
+                          path);
 }
 
 void dcb_model_free(DcbModel *m) {

@@ -1101,14 +1101,38 @@ struct Mt {
   }
 };
 
+// Fewest groups of at most bs of the items v, in order, sizes differing by at most one:
+// every segment is padded to the training length (tails centred, as apply.c:282-293 pads
+// them), so full segments and tails share one forward shape, and a segment's result does
+// not depend on its batch (normalisation and every kernel are per item).
+static std::vector<std::vector<int>> balanced_batches(const std::vector<int> &v, int bs) {
+  std::vector<std::vector<int>> out;
+  const int n = (int)v.size();
+  bs = bs < 1 ? 1 : (bs > 32 ? 32 : bs);
+  if (n == 0) return out;
+  const int nb = (n + bs - 1) / bs, q = n / nb, r = n % nb;
+  int at = 0;
+  for (int b = 0; b < nb; b++) {
+    const int sz = q + (b < r ? 1 : 0);
+    out.emplace_back(v.begin() + at, v.begin() + at + sz);
+    at += sz;
+  }
+  return out;
+}
+
+// Items [b, e) of n that shard s of cnt runs: one contiguous block, sizes within one.
+static void shard_block(int n, const DcbApplyOpts &o, int &b, int &e) {
+  const int cnt = o.shard_count > 1 ? o.shard_count : 1;
+  const int s = cnt > 1 ? o.shard_index : 0;
+  b = (int)((int64_t)n * s / cnt);
+  e = (int)((int64_t)n * (s + 1) / cnt);
+}
+
+// One split pass over `length` samples (apply.c:223-237): segment offsets, and this shard's
+// forward calls as indices into them.
 struct Plan {
   int seg = 0, stride = 0;
   std::vector<int> offsets;
-  // forwards of this shard: indices into offsets.  Every segment of the shard is padded to
-  // the training length (tails centred, as apply.c:282-293 pads them), so full segments and
-  // tails share one forward shape; they are grouped into the fewest batches of at most
-  // batch_size, with sizes differing by at most one (each segment's result does not depend
-  // on its batch: normalisation and every kernel are per item).
   std::vector<std::vector<int>> batches;
 };
 
@@ -1118,20 +1142,11 @@ static Plan make_plan(const Cfg &c, int length, const DcbApplyOpts &o) {
   p.stride = (int)((1.0f - o.overlap) * (float)p.seg);
   if (p.stride <= 0) return p;
   for (int off = 0; off < length; off += p.stride) p.offsets.push_back(off);
-  const int bs = o.batch_size < 1 ? 1 : (o.batch_size > 32 ? 32 : o.batch_size);
-  const int cnt = o.shard_count > 1 ? o.shard_count : 1;
+  int b, e;
+  shard_block((int)p.offsets.size(), o, b, e);
   std::vector<int> mine;
-  for (int i = 0; i < (int)p.offsets.size(); i++)
-    if (i % cnt == (cnt > 1 ? o.shard_index : 0)) mine.push_back(i);
-  const int n = (int)mine.size();
-  if (n == 0) return p;
-  const int nb = (n + bs - 1) / bs, q = n / nb, r = n % nb;
-  int at = 0;
-  for (int b = 0; b < nb; b++) {
-    const int sz = q + (b < r ? 1 : 0);
-    p.batches.emplace_back(mine.begin() + at, mine.begin() + at + sz);
-    at += sz;
-  }
+  for (int i = b; i < e; i++) mine.push_back(i);
+  p.batches = balanced_batches(mine, o.batch_size);
   return p;
 }
 
@@ -1147,68 +1162,134 @@ static std::vector<float> ola_weight(int n, float power) {
   return w;
 }
 
-// split pass of dc_apply_model (apply.c:223-306) on mix [B, C, length]; accumulates this
-// shard's weighted segments into out [B, S, C, length] (zeroed here) and multiplies by the
-// inverse of the full weight sum, so the shards' outputs sum to the complete result.
-static int apply_split(DcbModel *m, const float *mix, int B, int length, float *out,
-                       const DcbApplyOpts &o) {
+// The whole of dc_apply_model's plan (apply.c:179-306) in the coordinates of the final
+// output.  Shift pass i (apply.c:184-207) views the track, padded by max_shift zeros on
+// both sides, from offset off_i: view position p holds mix[p - d_i] with
+// d_i = max_shift - off_i, over a view of T + d_i samples, which is split into segments at
+// offsets 0, stride, 2 stride, ...  Each segment is one item: its padded chunk is read
+// straight from the mix (no padded or shifted copies of the track) and its kept samples
+// land at output positions p - d_i, weighted by the transition weight, the inverse of its
+// pass's weight sum (apply.c:295-300) and 1 / shifts (the average over passes).  The items
+// of all passes are ordered by output position; a shard runs one contiguous block of them,
+// so its output window [lo, hi) spans about 1 / shard_count of the track.
+struct Sched {
+  int seg = 0, stride = 0;
+  float scale = 1.f;
+  std::vector<int> pass_noff;  // segments of each pass (their weights sum at each position)
+  std::vector<SegItem> items;
+  std::vector<std::vector<int>> batches;  // this shard's forward calls (indices into items)
+  int64_t lo = 0, hi = 0;                 // this shard's output window
+};
+
+static bool make_sched(const Cfg &c, int T, const DcbApplyOpts &o, Sched &sc) {
+  sc.seg = (int)((float)c.samplerate * c.segment);
+  sc.stride = (int)((1.0f - o.overlap) * (float)sc.seg);
+  if (sc.stride <= 0 || sc.seg <= 0) {
+    fail("apply: invalid overlap %f", (double)o.overlap);
+    return false;
+  }
+  const int Lv = c.valid_length;
+  const int npass = o.shifts > 0 ? o.shifts : 1;
+  const int max_shift = o.shifts > 0 ? (int)(0.5f * (float)c.samplerate) : 0;
+  sc.scale = 1.0f / (float)npass;
+  Mt rng;
+  rng.seed(o.use_seed ? (uint64_t)o.seed : 1u);
+  for (int i = 0; i < npass; i++) {
+    const int64_t d = o.shifts > 0 ? max_shift - rng.randint(0, max_shift) : 0;
+    const int64_t L = (int64_t)T + d;  // view length: length + max_shift - offset
+    int noff = 0;
+    for (int64_t off = 0; off < L; off += sc.stride, noff++) {
+      SegItem it;
+      it.n = L - off < sc.seg ? L - off : sc.seg;
+      if (it.n > Lv) {
+        fail("apply: segment longer than the training length");
+        return false;
+      }
+      it.y0 = (Lv - it.n) / 2;  // padded_chunk centring / center_trim
+      it.view0 = off;
+      it.out0 = off - d;
+      it.start = off - it.y0 - d;
+      it.pass = i;
+      sc.items.push_back(it);
+    }
+    sc.pass_noff.push_back(noff);
+  }
+  std::stable_sort(sc.items.begin(), sc.items.end(),
+                   [](const SegItem &a, const SegItem &b) { return a.out0 < b.out0; });
+  int b, e;
+  shard_block((int)sc.items.size(), o, b, e);
+  std::vector<int> mine;
+  sc.lo = T;
+  sc.hi = 0;
+  for (int k = b; k < e; k++) {
+    mine.push_back(k);
+    const SegItem &it = sc.items[k];
+    const int64_t a0 = it.out0 < 0 ? 0 : it.out0;
+    const int64_t a1 = it.out0 + it.n > T ? T : it.out0 + it.n;
+    if (a0 < sc.lo) sc.lo = a0;
+    if (a1 > sc.hi) sc.hi = a1;
+  }
+  if (o.shard_count <= 1) {
+    sc.lo = 0;
+    sc.hi = T;
+  }
+  if (sc.hi < sc.lo) sc.hi = sc.lo;
+  sc.batches = balanced_batches(mine, o.batch_size);
+  return true;
+}
+
+// The shard's weighted segments of mix [B, C, T] into its window: win[r][j] += (share of
+// output position lo + j) for rows r < B S C, j < hi - lo (row stride ld; the caller zeroes
+// the window first).
+static int apply_window(DcbModel *m, const float *mix, int B, int T, const Sched &sc,
+                        float *win, int64_t ld, float power) {
   const Cfg &c = m->cfg;
   const int C = c.audio_channels, S = c.n_sources, Lv = c.valid_length;
-  Plan p = make_plan(c, length, o);
-  if (p.stride <= 0) {
-    fail("apply: invalid overlap %f", (double)o.overlap);
-    return -1;
-  }
-  if (!m->ola_w || m->ola_seg != p.seg || m->ola_pow != o.transition_power) {
+  if (!m->ola_w || m->ola_seg != sc.seg || m->ola_pow != power) {
     // the weights depend only on (segment, power): computed on the host once (float math
     // as apply.c:116-133) and kept on the device
-    std::vector<float> w = ola_weight(p.seg, o.transition_power);
+    std::vector<float> w = ola_weight(sc.seg, power);
     DCB_CUDA(cudaStreamSynchronize(stream()));
     cudaFree(m->ola_w);
     m->ola_w = nullptr;
-    DCB_CUDA(cudaMalloc(&m->ola_w, (size_t)p.seg * 4));
-    DCB_CUDA(cudaMemcpy(m->ola_w, w.data(), (size_t)p.seg * 4, cudaMemcpyHostToDevice));
-    m->ola_seg = p.seg;
-    m->ola_pow = o.transition_power;
+    DCB_CUDA(cudaMalloc(&m->ola_w, (size_t)sc.seg * 4));
+    DCB_CUDA(cudaMemcpy(m->ola_w, w.data(), (size_t)sc.seg * 4, cudaMemcpyHostToDevice));
+    m->ola_seg = sc.seg;
+    m->ola_pow = power;
   }
-  const float *wdev = m->ola_w;
-  const int64_t rows = (int64_t)B * S * C;
-  DCB_CUDA(cudaMemsetAsync(out, 0, (size_t)rows * length * 4, stream()));
-  for (const auto &bt : p.batches) {
+  const int rows = B * S * C;
+  for (const auto &bt : sc.batches) {
     const int nbt = (int)bt.size();
     FwdGraph *slot = forward_slot(m, nbt * B, Lv);
     if (!slot) return -1;
-    // items (segment or tail) centred in the training length (apply.c:254-293)
-    SegList sl{};
-    sl.cnt = nbt;
-    int64_t lo = length, hi = 0;
+    BatchItems bi{};
+    bi.cnt = nbt;
+    int64_t t0 = sc.hi, t1 = sc.lo;
     for (int k = 0; k < nbt; k++) {
-      const int off = p.offsets[bt[k]];
-      const int this_len = length - off < p.seg ? length - off : p.seg;
-      if (this_len > Lv || k >= 32) {
-        fail("apply: segment longer than the training length");
-        return -1;
-      }
-      sl.start[k] = off - (Lv - this_len) / 2;
-      sl.off[k] = off;
-      sl.y0[k] = (Lv - this_len) / 2;  // center_trim
-      sl.n[k] = this_len;
-      lo = off < lo ? off : lo;
-      hi = off + this_len > hi ? off + this_len : hi;
+      const SegItem &it = sc.items[bt[k]];
+      bi.start[k] = it.start;
+      bi.out0[k] = it.out0;
+      bi.view0[k] = it.view0;
+      bi.y0[k] = it.y0;
+      bi.n[k] = it.n;
+      bi.noff[k] = sc.pass_noff[it.pass];
+      t0 = it.out0 < t0 ? it.out0 : t0;
+      t1 = it.out0 + it.n > t1 ? it.out0 + it.n : t1;
     }
+    t0 = t0 < sc.lo ? sc.lo : t0;
+    t1 = t1 > sc.hi ? sc.hi : t1;
     const int64_t per = (int64_t)B * C * Lv;
     k_chunk_batch<<<dim3(grid_for(per, 256, 148 * 8), (unsigned)nbt), 256, 0, stream()>>>(
-        mix, slot->in, B, C, length, Lv, sl);
+        mix, slot->in, B, C, T, Lv, bi);
     DCB_LAUNCHED();
     if (forward_slot_run(m, slot) < 0) return -1;
-    k_accumulate_batch<<<grid_for(rows * (hi - lo), 256), 256, 0, stream()>>>(
-        out, slot->out, wdev, (int)rows, length, Lv, lo, hi, sl);
-    DCB_LAUNCHED();
+    if (t1 > t0) {
+      k_accumulate_items<<<grid_for(t1 - t0, 256, 148 * 16), 256, 0, stream()>>>(
+          win, ld, sc.lo, slot->out, m->ola_w, rows, Lv, t0, t1, sc.seg, sc.stride, sc.scale,
+          bi);
+      DCB_LAUNCHED();
+    }
   }
-  // divide by the weight sum of every segment (all shards'), summed on the device
-  k_scale_ola<<<grid_for(length, 256), 256, 0, stream()>>>(out, wdev, rows, length, p.seg,
-                                                           p.stride, (int)p.offsets.size());
-  DCB_LAUNCHED();
   return 0;
 }
 
@@ -1366,65 +1447,90 @@ int dcb_segment_plan(int samplerate, float segment, int length, const DcbApplyOp
 }
 
 int dcb_apply_plan(DcbModel *m, int T, const DcbApplyOpts *o, int *n_forwards, int *n_batched) {
-  if (!m || !o) return -1;
-  int len = T;
-  if (o->shifts > 0) len = T + (int)(0.5f * (float)m->cfg.samplerate);  // upper bound
-  Plan p = make_plan(m->cfg, len, *o);
+  if (!m || !o || T <= 0) return -1;
+  Sched sc;
+  if (!make_sched(m->cfg, T, *o, sc)) return -1;
   int fw = 0;
-  for (auto &b : p.batches) fw += (int)b.size();
-  if (n_forwards) *n_forwards = fw * (o->shifts > 0 ? o->shifts : 1);
-  if (n_batched) *n_batched = (int)p.batches.size() * (o->shifts > 0 ? o->shifts : 1);
+  for (auto &b : sc.batches) fw += (int)b.size();
+  if (n_forwards) *n_forwards = fw;
+  if (n_batched) *n_batched = (int)sc.batches.size();
   return 0;
 }
 
-// dc_apply_model (apply.c:179-306): shifts wrap the split pass
+int dcb_apply_window(int samplerate, float segment, int valid_length, int T,
+                     const DcbApplyOpts *o, int64_t *lo, int64_t *hi) {
+  if (!o || T <= 0 || samplerate <= 0 || valid_length <= 0) return -1;
+  Cfg c;
+  c.samplerate = samplerate;
+  c.segment = segment;
+  c.valid_length = valid_length;
+  Sched sc;
+  if (!make_sched(c, T, *o, sc)) return -1;
+  if (lo) *lo = sc.lo;
+  if (hi) *hi = sc.hi;
+  return 0;
+}
+
+// dc_apply_model (apply.c:179-306): the whole output, or (shard_count > 1) this shard's
+// share of it with zeros elsewhere, so that the shards' outputs sum to the full result
 int dcb_apply(DcbModel *m, const float *mix, int B, int T, float *out, const DcbApplyOpts *o) {
   if (!m || !o || B <= 0 || T <= 0) return -1;
-  const Cfg &c = m->cfg;
-  const int C = c.audio_channels, S = c.n_sources;
-  const int64_t rows = (int64_t)B * S * C;
   if (!o->split) {
     fail("apply: split=0 is not supported by this engine");
     return -1;
   }
-  if (o->shifts <= 0) {
-    if (apply_split(m, mix, B, T, out, *o) < 0) return -1;
-    DCB_CUDA(cudaStreamSynchronize(stream()));
-    return failed() ? -1 : 0;
-  }
-  const int max_shift = (int)(0.5f * (float)c.samplerate);
-  const int Lp = T + 2 * max_shift;
-  float *padded = dalloc((size_t)B * C * Lp);
-  k_chunk<<<grid_for((int64_t)B * C * Lp, 256), 256, 0, stream()>>>(mix, padded, B, C, T,
-                                                                    -max_shift, Lp, (int64_t)C * Lp);
-  DCB_LAUNCHED();
-  Mt rng;
-  rng.seed(o->use_seed ? (uint64_t)o->seed : 1u);
+  Sched sc;
+  if (!make_sched(m->cfg, T, *o, sc)) return -1;
+  const int64_t rows = (int64_t)B * m->cfg.n_sources * m->cfg.audio_channels;
   DCB_CUDA(cudaMemsetAsync(out, 0, (size_t)rows * T * 4, stream()));
-  for (int i = 0; i < o->shifts; i++) {
-    const int off = rng.randint(0, max_shift);
-    const int Ls = T + max_shift - off;
-    float *shifted = dalloc((size_t)B * C * Ls);
-    k_chunk<<<grid_for((int64_t)B * C * Ls, 256), 256, 0, stream()>>>(padded, shifted, B, C, Lp,
-                                                                      off, Ls, (int64_t)C * Ls);
-    DCB_LAUNCHED();
-    float *part = dalloc((size_t)rows * Ls);
-    DcbApplyOpts inner = *o;
-    inner.shifts = 0;
-    if (apply_split(m, shifted, B, Ls, part, inner) < 0) return -1;
-    dfree(shifted);
-    // out += part[..., max_shift - off :] / shifts
-    float *wone = dalloc(T);
-    k_fill<<<grid_for(T, 256), 256, 0, stream()>>>(wone, T, 1.0f / (float)o->shifts);
-    DCB_LAUNCHED();
-    k_accumulate<<<grid_for(rows * T, 256), 256, 0, stream()>>>(out, part, wone, (int)rows, T, Ls,
-                                                               0, max_shift - off, T);
-    DCB_LAUNCHED();
-    dfree(wone);
-    dfree(part);
-  }
-  dfree(padded);
+  if (apply_window(m, mix, B, T, sc, out + sc.lo, T, o->transition_power) < 0) return -1;
   DCB_CUDA(cudaStreamSynchronize(stream()));
+  return failed() ? -1 : 0;
+}
+
+int dcb_apply_shard(DcbModel *m, const float *mix, int B, int T, float *win, int64_t ld,
+                    const DcbApplyOpts *o) {
+  if (!m || !o || B <= 0 || T <= 0 || !win) return -1;
+  if (!o->split) {
+    fail("apply: split=0 is not supported by this engine");
+    return -1;
+  }
+  Sched sc;
+  if (!make_sched(m->cfg, T, *o, sc)) return -1;
+  if (ld < sc.hi - sc.lo) {
+    fail("apply_shard: row stride %lld is shorter than the window (%lld samples)",
+         (long long)ld, (long long)(sc.hi - sc.lo));
+    return -1;
+  }
+  const int64_t rows = (int64_t)B * m->cfg.n_sources * m->cfg.audio_channels;
+  if (sc.hi > sc.lo) {
+    DCB_CUDA(cudaMemset2DAsync(win, (size_t)ld * 4, 0, (size_t)(sc.hi - sc.lo) * 4,
+                               (size_t)rows, stream()));
+  }
+  if (apply_window(m, mix, B, T, sc, win, ld, o->transition_power) < 0) return -1;
+  return failed() ? -1 : 0;
+}
+
+int dcb_merge_windows(float *out, int64_t rows, int64_t T, const float *wins, int64_t ld,
+                      int64_t win_stride, const int64_t *lo, const int64_t *hi, int n) {
+  if (!out || rows <= 0 || T <= 0 || n < 0 || n > 64 || (n > 0 && (!wins || !lo || !hi))) {
+    fail("merge_windows: invalid arguments (n = %d, at most 64 windows)", n);
+    return -1;
+  }
+  WinList wl{};
+  wl.n = n;
+  for (int i = 0; i < n; i++) {
+    if (lo[i] < 0 || hi[i] > T || hi[i] - lo[i] > ld) {
+      fail("merge_windows: window %d [%lld, %lld) outside the track or wider than %lld", i,
+           (long long)lo[i], (long long)hi[i], (long long)ld);
+      return -1;
+    }
+    wl.lo[i] = lo[i];
+    wl.hi[i] = hi[i];
+  }
+  k_merge_windows<<<grid_for(T, 256, 148 * 16), 256, 0, stream()>>>(out, rows, T, wins, ld,
+                                                                    win_stride, wl);
+  DCB_LAUNCHED();
   return failed() ? -1 : 0;
 }
 

@@ -612,34 +612,33 @@ __global__ void k_chunk(const float *__restrict__ mix, float *__restrict__ out, 
   }
 }
 
-// out[b][src][c][off + t] += y[b][src][c][y0 + t] * w[t], t < n  (apply.c:157-169)
-__global__ void k_accumulate(float *out, const float *__restrict__ y,
-                             const float *__restrict__ w, int rows, int64_t out_len,
-                             int64_t y_len, int64_t off, int64_t y0, int64_t n) {
-  const int64_t total = (int64_t)rows * n;
-  DCB_GRID_STRIDE(i, total) {
-    const int64_t t = i % n, r = i / n;
-    out[r * out_len + off + t] += y[r * y_len + y0 + t] * w[t];
-  }
-}
+// One segment forward of dc_apply_model placed in the final output (see Sched in
+// forward.cu): chunk start in the mix, output / view position of its first kept sample,
+// centre-trim offset and kept length, and the pass it belongs to.
+struct SegItem {
+  int64_t start, out0, view0, y0, n;
+  int pass;
+};
 
-// segments of one forward call: start / output offset / trim / length per item
-struct SegList {
+// the items of one forward call, by value in the kernel parameters
+struct BatchItems {
   int64_t start[32];  // first mix sample of the item's padded chunk
-  int64_t off[32];    // output position of the item's first kept sample
-  int64_t y0[32];     // first kept sample inside the item's output
+  int64_t out0[32];   // output position of the item's first kept sample
+  int64_t view0[32];  // its position in the item's pass view (weight-sum index)
+  int64_t y0[32];     // first kept sample inside the item's model output
   int64_t n[32];      // kept samples
+  int noff[32];       // segments of the item's pass
   int cnt;
 };
 
-// every item's padded chunk of mix (zeros outside [0, total)) into flat[k][b][c][len];
-// blockIdx.y = item
+// every item's padded chunk of mix (zeros outside [0, total)) into flat[k][b][c][len]
+// (apply.c:135-154 padded_chunk); blockIdx.y = item
 __global__ void k_chunk_batch(const float *__restrict__ mix, float *__restrict__ flat, int Bm,
-                              int C, int64_t total, int64_t len, SegList sl) {
+                              int C, int64_t total, int64_t len, BatchItems bi) {
   const int k = blockIdx.y;
   const int64_t n = (int64_t)Bm * C * len;
   float *out = flat + (int64_t)k * n;
-  const int64_t start = sl.start[k];
+  const int64_t start = bi.start[k];
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t t = i % len, r = i / len;
@@ -648,44 +647,60 @@ __global__ void k_chunk_batch(const float *__restrict__ mix, float *__restrict__
   }
 }
 
-// out[r][t] += y[k][r][y0_k + t - off_k] * w[t - off_k] for the items k covering t, added in
-// item (segment) order as apply.c:157-169 adds them, over the call's output range [lo, hi)
-__global__ void k_accumulate_batch(float *out, const float *__restrict__ y,
-                                   const float *__restrict__ w, int rows, int64_t out_len,
-                                   int64_t y_len, int64_t lo, int64_t hi, SegList sl) {
-  const int64_t span = hi - lo, total = (int64_t)rows * span;
-  DCB_GRID_STRIDE(i, total) {
-    const int64_t t = lo + i % span, r = i / span;
-    float acc = out[r * out_len + t];
-    for (int k = 0; k < sl.cnt; k++) {
-      const int64_t u = t - sl.off[k];
-      if (u >= 0 && u < sl.n[k])
-        acc += y[((int64_t)k * rows + r) * y_len + sl.y0[k] + u] * w[u];
+// Inverse of a pass's summed transition weights at view position p: the segments at
+// offsets q stride (q < noff) that cover p, summed in fp64 in segment order as
+// apply.c:295-300 sums them.
+static __device__ __forceinline__ float inv_weight_sum(const float *__restrict__ w, int64_t p,
+                                                       int seg, int stride, int noff) {
+  const int64_t qlo = p < seg ? 0 : (p - seg) / stride + 1;
+  int64_t qhi = p / stride;
+  if (qhi > noff - 1) qhi = noff - 1;
+  double s = 0.0;
+  for (int64_t q = qlo; q <= qhi; q++) s += (double)w[p - q * stride];
+  return s > 0.0 ? (float)(1.0 / s) : 0.0f;
+}
+
+// win[r][t - lo] += y[k][r][y0_k + u] * w[u] * inv_sum_k(view0_k + u) * scale, u = t - out0_k,
+// for every item k of the call that covers output position t in [t0, t1) (accumulate,
+// apply.c:157-169; the weight-sum division, apply.c:295-306; the shift average,
+// apply.c:203-207), in item order
+__global__ void k_accumulate_items(float *win, int64_t ld, int64_t lo,
+                                   const float *__restrict__ y, const float *__restrict__ w,
+                                   int rows, int64_t y_len, int64_t t0, int64_t t1, int seg,
+                                   int stride, float scale, BatchItems bi) {
+  DCB_GRID_STRIDE(i, t1 - t0) {
+    const int64_t t = t0 + i;
+    float *col = win + (t - lo);
+    for (int k = 0; k < bi.cnt; k++) {
+      const int64_t u = t - bi.out0[k];
+      if (u < 0 || u >= bi.n[k]) continue;
+      const float cw = w[u] * inv_weight_sum(w, bi.view0[k] + u, seg, stride, bi.noff[k]) * scale;
+      const float *yk = y + (int64_t)k * rows * y_len + bi.y0[k] + u;
+      for (int r = 0; r < rows; r++) col[r * ld] += yk[(int64_t)r * y_len] * cw;
     }
-    out[r * out_len + t] = acc;
   }
 }
 
-// y = x * s[t] (final division by the summed transition weights)
-// x[r][t] *= 1 / sum_i w[t - off_i] over the segments i covering t (offsets i * stride,
-// i < noff): the weight normalisation of dc_apply_model (apply.c:295-300), summed in fp64
-// in segment order as the reference does, without a host-side weight-sum array.
-__global__ void k_scale_ola(float *x, const float *__restrict__ w, int64_t rows, int64_t L,
-                            int seg, int stride, int noff) {
-  DCB_GRID_STRIDE(t, L) {
-    const int64_t lo = t < seg ? 0 : (t - seg) / stride + 1;
-    int64_t hi = t / stride;
-    if (hi > noff - 1) hi = noff - 1;
-    double s = 0.0;
-    for (int64_t i = lo; i <= hi; i++) s += (double)w[t - i * stride];
-    const float inv = s > 0.0 ? (float)(1.0 / s) : 0.0f;
-    for (int64_t r = 0; r < rows; r++) x[r * L + t] *= inv;
-  }
-}
+// output windows of the shards (sorted by lo)
+struct WinList {
+  int64_t lo[64], hi[64];
+  int n;
+};
 
-__global__ void k_scale_time(float *x, const float *__restrict__ s, int64_t rows, int64_t L) {
-  const int64_t total = rows * L;
-  DCB_GRID_STRIDE(i, total) { x[i] = x[i] * s[i % L]; }
+// out[r][t] = sum over windows w covering t of wins[w * wstride + r * ld + t - lo_w]
+// (zero where none does): the root's overlap-add of the gathered shard outputs
+__global__ void k_merge_windows(float *__restrict__ out, int64_t rows, int64_t T,
+                                const float *__restrict__ wins, int64_t ld, int64_t wstride,
+                                WinList wl) {
+  DCB_GRID_STRIDE(t, T) {
+    for (int64_t r = 0; r < rows; r++) {
+      float acc = 0.f;
+      for (int i = 0; i < wl.n; i++)
+        if (t >= wl.lo[i] && t < wl.hi[i])
+          acc += wins[(int64_t)i * wstride + r * ld + (t - wl.lo[i])];
+      out[r * T + t] = acc;
+    }
+  }
 }
 
 }  // namespace dcb

@@ -222,6 +222,17 @@ DcbModel *dcb_model_load(const char *safetensors_path, const char *config_json_p
 void dcb_model_free(DcbModel *m);
 int dcb_model_info(const DcbModel *m, int *n_sources, int *audio_channels, int *valid_length,
                    int *samplerate, float *segment);
+/* The same model's layout from the safetensors header alone (no tensor data is read): the
+ * device block is allocated and zeroed for the caller to fill, e.g. by an NCCL broadcast of
+ * another rank's dcb_model_weight_block.  NULL on error. */
+DcbModel *dcb_model_load_layout(const char *safetensors_path, const char *config_json_path);
+/* Pre-packed on-disk image of a loaded model: the config, the safetensors header and the
+ * device block exactly as packed (fp16 GEMM operands with GLU-interleaved rows, the TMA K
+ * order, transposed-conv phase matrices, fp64 DConv statistic constants), with a checksum.
+ * dcb_model_load_packed rebuilds the layout from the stored header and uploads the block
+ * as stored: no fp32 tensor data is read or converted.  0 / NULL on error. */
+int dcb_model_save_packed(const DcbModel *m, const char *path);
+DcbModel *dcb_model_load_packed(const char *path);
 /* Device bytes of the packed weight block (the NCCL broadcast payload) and its pointer. */
 size_t dcb_model_weight_bytes(const DcbModel *m);
 void *dcb_model_weight_block(DcbModel *m);
@@ -253,16 +264,33 @@ typedef struct {
   int batch_size;
   unsigned seed;
   int use_seed;
-  /* segment subset for data-parallel sharding: this caller runs only the forwards whose
-   * index (in dc_apply_model's order) i satisfies i % shard_count == shard_index and
-   * accumulates their weighted stems; the weight sum covers every segment, so summing the
-   * shard outputs over all shards gives the full result. shard_count 0/1 = everything. */
+  /* segment subset for data-parallel sharding: this caller runs only block shard_index of
+   * shard_count contiguous blocks of the segment forwards (all shift passes, in output
+   * order) and accumulates their weighted stems; the weight sums cover every segment, so
+   * summing the shard outputs over all shards gives the full result.  shard_count 0/1 =
+   * everything. */
   int shard_index;
   int shard_count;
 } DcbApplyOpts;
 void dcb_apply_defaults(DcbApplyOpts *o);
-/* mix [B][C][T] (device) -> out [B][S][C][T] (device). Returns 0 or -1. */
+/* mix [B][C][T] (device) -> out [B][S][C][T] (device). Returns 0 or -1.  With
+ * shard_count > 1, out holds this shard's share (zero outside its window), so the shards'
+ * outputs sum to the full result. */
 int dcb_apply(DcbModel *m, const float *mix, int B, int T, float *out, const DcbApplyOpts *o);
+/* Data-parallel form of dcb_apply.  The segments of all shift passes, ordered by output
+ * position, are split into shard_count contiguous blocks; a shard's share of the output is
+ * non-zero only on its window [lo, hi) along time (about 1 / shard_count of the track plus
+ * the overlaps).  dcb_apply_window (host only) gives the window; dcb_apply_shard writes the
+ * share over the window only: win [B*S*C rows][ld], column j = time lo + j for
+ * j < hi - lo (ld >= hi - lo; later columns untouched).  dcb_merge_windows is the root's
+ * overlap-add after gathering the n shards' windows (window i at wins + i * win_stride,
+ * rows of stride ld): out [rows][T] = their sum, zero where no window covers (n <= 64). */
+int dcb_apply_window(int samplerate, float segment, int valid_length, int T,
+                     const DcbApplyOpts *o, int64_t *lo, int64_t *hi);
+int dcb_apply_shard(DcbModel *m, const float *mix, int B, int T, float *win, int64_t ld,
+                    const DcbApplyOpts *o);
+int dcb_merge_windows(float *out, int64_t rows, int64_t T, const float *wins, int64_t ld,
+                      int64_t win_stride, const int64_t *lo, const int64_t *hi, int n);
 /* Host-only pieces of the scheduler (no GPU needed):
  * dcb_py_randint: n draws of CPython's random.Random(seed).randint(lo, hi), the shift
  *   generator of apply.c:5-107;

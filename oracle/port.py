@@ -590,8 +590,9 @@ def segment_plan(length, cfg: Config, overlap=0.25, batch_size=8):
 def apply_model(mix, W, cfg: Config, shifts=1, overlap=0.25, transition_power=1.0,
                 batch_size=8, seed=1, forward_fn=None, shard=(0, 1)):
     """dc_apply_model (apply.c:179-306) with split=True.  shard = (index, count) keeps only
-    the segments i with i % count == index (the weight sum stays global), so the shards'
-    outputs add up to the unsharded result -- the data-parallel split the engine uses."""
+    the segments of one contiguous block of the offsets, [n index / count, n (index + 1) /
+    count) (the weight sum stays global), so the shards' outputs add up to the unsharded
+    result; with shifts = 0 this is the engine's data-parallel split."""
     fwd = forward_fn or (lambda x: forward(x, W, cfg))
     B, C, length = mix.shape
     if shifts > 0:
@@ -616,8 +617,9 @@ def apply_model(mix, W, cfg: Config, shifts=1, overlap=0.25, transition_power=1.
         sumw[off:off + n] += weight[:n]
     out = np.zeros((B, cfg.n_sources, C, length), dtype=F32)
     si, sc = shard
+    b0, b1 = len(offsets) * si // sc, len(offsets) * (si + 1) // sc
     for kind, idxs in batches:
-        idxs = [i for i in idxs if i % sc == si]
+        idxs = [i for i in idxs if b0 <= i < b1]
         if not idxs:
             continue
         if kind == "full":

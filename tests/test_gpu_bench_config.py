@@ -60,7 +60,7 @@ def test_full_width_batch7_graph_replay_matches_single_segments(torch_cuda):
     cfg, w, c = model_files("full")
     seg = cfg.valid_length
     stride = int(0.75 * seg)
-    T = 6 * stride + seg - 1000          # exactly 7 segment offsets, the last one a tail
+    T = 7 * stride - 1000                # offsets 0 .. 6 stride: 7 segments, the last a tail
     mix = synth.track_input(T / cfg.samplerate, cfg.samplerate, seed=3)[:, :, :T]
     mix = np.ascontiguousarray(mix, np.float32)
     model = dcb.Model(w, c)

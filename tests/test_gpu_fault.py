@@ -17,7 +17,10 @@ from conftest import rel_l2
 
 pytestmark = pytest.mark.gpu
 
-FAULT_FULL, FAULT_EMPTY = 1, 2  # umma.cuh: operand stage never filled / never released
+# umma.cuh: operand stage never filled / never released / accumulator never completed.
+# Every role of the stuck CTA is waiting; whichever wait began first expires first (the
+# epilogue's, on the accumulator) and the others then see the word and end.
+FAULT_FULL, FAULT_EMPTY, FAULT_DONE = 1, 2, 4
 
 
 def test_bounded_wait_expires_then_recovers(torch_cuda):
@@ -40,7 +43,7 @@ def test_bounded_wait_expires_then_recovers(torch_cuda):
         dt = time.time() - t0
         fault = dcb.device_fault(clear=False)
         print(f"withheld stage: kernel returned after {dt:.2f} s, fault word {fault:#x}")
-        assert fault & (FAULT_FULL | FAULT_EMPTY), fault
+        assert fault & (FAULT_FULL | FAULT_EMPTY | FAULT_DONE), fault
         assert dt < 30
         # the hook is one-shot: it was consumed by the faulting launch
         assert dcb.set_option("test_withhold_arrive", 0) == 0
@@ -54,6 +57,7 @@ def test_bounded_wait_expires_then_recovers(torch_cuda):
     finally:
         dcb.set_option("test_withhold_arrive", 0)
         dcb.set_option("wait_limit_ms", limit0)
+        dcb.device_fault(clear=True)   # never leave the word set for later tests
     got = dcb.gemm_half(At, Bt)
     torch.cuda.synchronize()
     assert rel_l2(got.cpu().numpy()[0], want) < 2e-5

@@ -1,6 +1,9 @@
-"""Data-parallel host logic on CPU with world_size 2 (gloo): the weight broadcast from rank 0,
-the engine's segment sharding (dcb_segment_plan) and the stem reduction reproduce the
-single-process dc_apply_model result.  Same steps bench.py runs over NCCL on GPUs."""
+"""Data-parallel host logic on CPU with world_size 2 (gloo), the same steps bench.py runs
+over NCCL on GPUs: rank 0's weights reach the other rank only through a broadcast; the
+engine's scheduler (dcb_segment_plan, dcb_apply_window) assigns each rank one contiguous
+block of segments and an output window; each rank's share of dc_apply_model is zero outside
+its window; the windows, padded to one width, are gathered to rank 0 and overlap-added
+there, which reproduces the single-process result."""
 import json
 import os
 import socket
@@ -19,6 +22,17 @@ def _free_port():
     p = s.getsockname()[1]
     s.close()
     return p
+
+
+def _window(length, pc, rank, world):
+    import ctypes as C
+    import demucs_cuda_b200 as d
+    o = d.apply_opts(shifts=0, batch_size=2, shard_index=rank, shard_count=world)
+    lo, hi = C.c_int64(), C.c_int64()
+    r = d.lib(load_only=True).dcb_apply_window(pc.samplerate, pc.segment, pc.valid_length,
+                                               length, C.byref(o), C.byref(lo), C.byref(hi))
+    assert r == 0
+    return lo.value, hi.value
 
 
 def _worker(rank, world, port, out_path):
@@ -45,20 +59,33 @@ def _worker(rank, world, port, out_path):
             W[n] = flat[off:off + k].numpy().reshape(W[n].shape)
             off += k
         pc = P.Config(json.load(open(c)))
+        length = 70000
         rng = np.random.default_rng(5)
-        mix = rng.uniform(-0.5, 0.5, (1, 2, 70000)).astype(np.float32)
-        # the shard assignment comes from the engine's own scheduler
-        _, calls = d.segment_plan(70000, pc.samplerate, pc.segment, shifts=0, batch_size=2,
-                                  shard_index=rank, shard_count=world)
+        mix = rng.uniform(-0.5, 0.5, (1, 2, length)).astype(np.float32)
+        # the shard assignment and windows come from the engine's own scheduler
+        offs, calls = d.segment_plan(length, pc.samplerate, pc.segment, shifts=0,
+                                     batch_size=2, shard_index=rank, shard_count=world)
         mine = [i for i, cidx in enumerate(calls) if cidx >= 0]
-        assert all(i % world == rank for i in mine)
+        assert mine == list(range(mine[0], mine[-1] + 1))   # one contiguous block
+        spans = [_window(length, pc, r, world) for r in range(world)]
+        lo, hi = spans[rank]
         part = P.apply_model(mix, W, pc, shifts=0, batch_size=2, shard=(rank, world))
-        t = torch.from_numpy(part.copy())
-        dist.reduce(t, dst=0)
+        outside = np.concatenate([part[..., :lo].ravel(), part[..., hi:].ravel()])
+        assert not outside.any()   # the share is zero outside the window
+        wmax = max(h - l for l, h in spans)
+        win = np.zeros((part.shape[1] * part.shape[2], wmax), np.float32)
+        win[:, :hi - lo] = part.reshape(-1, length)[:, lo:hi]
+        t = torch.from_numpy(win)
+        gl = [torch.empty_like(t) for _ in range(world)] if rank == 0 else None
+        dist.gather(t, gather_list=gl, dst=0)
         if rank == 0:
+            merged = np.zeros((win.shape[0], length), np.float32)
+            for (l, h), g in zip(spans, gl):
+                merged[:, l:h] += g.numpy()[:, :h - l]
             full = P.apply_model(mix, W, pc, shifts=0, batch_size=2)
             with open(out_path, "w") as f:
-                json.dump({"rel": rel_l2(t.numpy(), full), "n_mine": len(mine)}, f)
+                json.dump({"rel": rel_l2(merged, full.reshape(-1, length)),
+                           "n_mine": len(mine), "spans": spans}, f)
     finally:
         dist.destroy_process_group()
 
@@ -69,3 +96,5 @@ def test_two_rank_sharded_apply(tmp_path):
     res = json.load(open(out))
     assert res["n_mine"] >= 1
     assert res["rel"] < 1e-6
+    (l0, h0), (l1, h1) = res["spans"]
+    assert l0 == 0 and h1 == 70000 and l1 < h0   # the windows overlap where segments do
