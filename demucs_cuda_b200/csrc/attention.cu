@@ -7,7 +7,8 @@
 //   warps 0-3  one query row per thread: read the 64 scores of a key block from TMEM once,
 //              online softmax in fp32 (exp2 domain, running max / sum; the O accumulator
 //              stays in TMEM and is rescaled there only when the maximum grows by more
-//              than 2^8), write P as fp16 into shared memory in the UMMA A-operand layout;
+//              than 2^kLazyLog2), write P as fp16 into shared memory in the UMMA A-operand
+//              layout;
 //   warp 4     TMA producer: Q once, then K blocks into a 4-stage ring (a stage is free
 //              once S of its block has completed);
 //   warp 6     TMA producer: V^T blocks into a 3-stage ring (free once P V of its block
@@ -24,7 +25,8 @@
 // Inputs are fp16 exactly as the reference rounds them (split_heads of the fp32
 // projections): Q [BH][Tq][hd], K [BH][Tk][hd], V^T [BH][hd][Tkp].  The reference rounds
 // the normalised probabilities to fp16; here the unnormalised exp(s - m_running) is
-// rounded (same fp16 operand width) and O is divided by the fp32 row sum at the end.
+// rounded (same fp16 operand width) and O is divided at the end by the row sum of those
+// fp16 values (accumulated in fp32 by the tensor core).
 #include <cudaTypedefs.h>
 #include <math.h>
 
@@ -53,11 +55,18 @@ struct AttnArgs {
 };
 
 
-// 2^x of two fp16 values (PTX ex2.approx.f16x2)
-static __device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
-  return y;
+// Two non-negative floats below 65520 -> packed fp16x2 (low = a) without the XU pipe, which
+// the exponentials already saturate (the packed conversion cvt.rn.f16x2.f32 runs there, at
+// two passes per instruction).  Scaling by 2^-112 moves the fp32 exponent onto the fp16
+// bias; values below 2^-14 become fp32 subnormals whose bits are exactly the fp16
+// subnormal's shifted up by 13 (the multiply keeps subnormals: no flush-to-zero in this
+// build); adding 0x1000 rounds at bit 13 (half away from zero: differs from nearest-even
+// only on exact ties) and bits 13..28 are the fp16 pattern.  One FMUL per value on the FMA
+// pipe, integer adds and a byte permute on the ALU.
+static __device__ __forceinline__ uint32_t pack_h2_alu(float a, float b) {
+  const uint32_t ua = __float_as_uint(a * 0x1p-112f) + 0x1000u;
+  const uint32_t ub = __float_as_uint(b * 0x1p-112f) + 0x1000u;
+  return __byte_perm(ua >> 13, ub >> 13, 0x5410);
 }
 
 __global__ void __launch_bounds__(kAttnThreads, 2)
@@ -216,9 +225,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     // softmax warps: one query row per thread, exp2 domain (scores scaled by
     // scale * log2 e).  The running maximum m is only raised, and O (in TMEM) rescaled,
     // when a block's maximum exceeds it by more than kLazyLog2: probabilities stay <= 4 and
-    // most blocks need no rescale.  P = 2^(s - m) is evaluated two at a time in fp16
-    // (ex2.approx.f16x2 of the fp16-rounded exponent; the exponent's rounding error is at
-    // most 2^-11 * 2 for the largest probabilities), which is the operand precision P V
+    // most blocks need no rescale.  P = 2^(s - m) is evaluated in fp32 (ex2.approx on the
+    // fp32 exponent, relative error ~2^-22) and rounded to fp16, the operand precision P V
     // uses anyway; the row sum comes from the tensor core (P times a ones tile).
     const int r = threadIdx.x;
     const uint32_t lrow = (uint32_t)(warp * 32) << 16;
@@ -284,10 +292,14 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         ok = false;
         break;
       }
+      // P = 2^(s - m) by one fp32 ex2 (a single XU pass per value; the fp16x2 form takes two
+      // passes per pair for the exponential and two more for converting its argument), then
+      // packed to fp16 off the XU pipe
       uint32_t w[kKV / 2];
 #pragma unroll
       for (int i = 0; i < kKV; i += 2)
-        w[i >> 1] = ex2_h2(pack_h2(fmaf(v[i], sl2, -m_run), fmaf(v[i + 1], sl2, -m_run)));
+        w[i >> 1] = pack_h2_alu(ex2_approx(fmaf(v[i], sl2, -m_run)),
+                                ex2_approx(fmaf(v[i + 1], sl2, -m_run)));
       const uint32_t prow = smem_u32(sP + (j & 1) * kPBytes);
 #pragma unroll
       for (int c = 0; c < 8; c++)

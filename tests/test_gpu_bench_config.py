@@ -7,7 +7,13 @@ segments per call, replayed as CUDA graphs (option "graphs"), through dc_apply_m
 * full configuration (7.8 s segments, the benchmark's shapes): dcb_apply running the 7
   segments of a 43 s track as ONE batched forward replayed from a graph, against the same
   track with every segment forwarded alone and eagerly -- that single-segment path is the
-  one tests/test_gpu_model.py pins to the reference's digest at this size.
+  one tests/test_gpu_model.py pins to the reference's digest at this size.  The two agree
+  to fp16 rounding noise, not bit for bit: the first stage that differs is the first
+  encoder whose DConv runs as a tensor-core conv (frequency encoder 2), where the batch
+  changes how tiles map to CTAs and so the order of its fp32 partial sums; a last-bit
+  difference before an fp16 operand rounding moves that operand by one unit, and the
+  forward carries it to about 5e-5 of the stems (the path's own error against the
+  reference is of the same size).  Each run is bit-reproducible.
 """
 import numpy as np
 import pytest
@@ -76,6 +82,7 @@ def test_full_width_batch7_graph_replay_matches_single_segments(torch_cuda):
     for i, o in enumerate(outs):
         e = rel_l2(o, single)
         print(f"call {i}: batch-7 forward (graphs) vs 7 single forwards rel_l2 {e:.3e}")
-        assert e < 1e-6
+        assert e < 2e-4
+    assert rel_l2(outs[2], outs[0]) < 1e-6   # replay == eager capture, same batch
     assert dcb.device_fault() == 0
     del model
