@@ -233,8 +233,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const float sl2 = a.scale * 1.4426950408889634f;
     float m_run = -INFINITY;
     bool ok = true;
+    // tcgen05.ld / st are warp-collective (.sync.aligned): every decision in front of a TMEM
+    // access is made warp-uniform (a wait's outcome with warp_all, the rescale by __any_sync)
     for (int j = 0; j < nkv && ok; j++) {
-      if (!mbar_wait_sleep(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn)) {
+      if (!warp_all(mbar_wait_sleep(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn))) {
         ok = false;
         break;
       }
@@ -263,16 +265,20 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                              fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       const float ms = mx * sl2;
-      if (ms > m_run + kLazyLog2) {
+      // raise this row's maximum when its block maximum exceeds it by more than kLazyLog2;
+      // the warp rescales when any of its rows does (rows that keep their maximum scale by 1)
+      const bool raise = ms > m_run + kLazyLog2;
+      if (__any_sync(0xffffffffu, raise)) {
         if (j > 0) {
-          // rescale the accumulated O row and the running sum to the new maximum once
-          // PV(j-1) has completed
-          if (!mbar_wait(&p_empty[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u, kFaultAttn)) {
+          // rescale the accumulated O rows and running sums to the new maxima once PV(j-1)
+          // has completed
+          if (!warp_all(mbar_wait(&p_empty[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u,
+                                  kFaultAttn))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const float alpha = exp2f(m_run - ms);
+          const float alpha = raise ? exp2f(m_run - ms) : 1.0f;
 #pragma unroll
           for (int c = 0; c < kSumCol + 16; c += 16) {
             float ov[16];
@@ -284,11 +290,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
           }
           tmem_wait_st();
         }
-        m_run = ms;
+        if (raise) m_run = ms;
       }
       // P buffer j & 1 is free once PV(j-2) has completed
-      if (j >= 2 &&
-          !mbar_wait(&p_empty[j & 1], (uint32_t)((j - 2) >> 1) & 1u, kFaultAttn)) {
+      if (j >= 2 && !warp_all(mbar_wait(&p_empty[j & 1], (uint32_t)((j - 2) >> 1) & 1u,
+                                        kFaultAttn))) {
         ok = false;
         break;
       }
@@ -310,7 +316,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       if (lane == 0) mbar_arrive(&p_full[j & 1]);
     }
     // normalise and store the finished O row
-    if (ok && mbar_wait(o_full, 0, kFaultAttn)) {
+    if (warp_all(ok && mbar_wait(o_full, 0, kFaultAttn))) {
       tc_fence_after();
       const int t = q0 + r;
       float lsum[16];

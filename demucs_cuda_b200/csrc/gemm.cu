@@ -693,7 +693,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tile_coords(s, tile, bz, m0, nt);
       const uint32_t buf = local % (uint32_t)Cfg::kBufs;
       const uint32_t use = local / (uint32_t)Cfg::kBufs;
-      if (!mbar_wait_sleep(&acc_full[buf], use & 1u, kFaultDone)) break;
+      if (!warp_all(mbar_wait_sleep(&acc_full[buf], use & 1u, kFaultDone))) break;
       tc_fence_after();
       const int64_t left = (int64_t)s.M - m0;
       epilogue_tile<BN, Cfg::kEpiWarps, 32, EK>(s, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp,
@@ -1080,7 +1080,7 @@ __global__ void __launch_bounds__(kCtThreads, 1)
       int wo0, nt;
       ct_tile(c, tile, line, wo0, nt);
       const uint32_t buf = local & 1u, use = local >> 1;
-      if (!mbar_wait(&acc_full[buf], use & 1u, kFaultDone)) break;
+      if (!warp_all(mbar_wait(&acc_full[buf], use & 1u, kFaultDone))) break;
       tc_fence_after();
       ct_epilogue<BN>(c, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp, lane, line, wo0, nt,
                       wst);
@@ -1745,7 +1745,7 @@ __global__ void __launch_bounds__(kChThreads, 2)
       int wo0, nt;
       ch_tile(c, tile, line, wo0, nt);
       const uint32_t buf = local & 1u, use = local >> 1;
-      if (!mbar_wait_sleep(&acc_full[buf], use & 1u, kFaultDone)) break;
+      if (!warp_all(mbar_wait_sleep(&acc_full[buf], use & 1u, kFaultDone))) break;
       tc_fence_after();
       // EK 0: generic epilogue; else the specialised one for ACT = (EK - 1) % 4 and
       // output geometry CT = (EK - 1) / 4

@@ -100,6 +100,12 @@ static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
   }
 }
 
+// Warp-uniform outcome of a wait: tcgen05.ld / st (and the epilogues built on them) are
+// .sync.aligned, so all 32 lanes must take the same path after a wait; a lane that gave up
+// at the time limit while another saw the phase complete would otherwise leave the warp
+// divergent in front of a TMEM access.  Every lane of the warp must call it.
+static __device__ __forceinline__ bool warp_all(bool ok) { return __all_sync(0xffffffffu, ok); }
+
 // mbar_wait through mbar_try_sleep (same bound and fault protocol)
 static __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity,
                                                        uint32_t fault) {
