@@ -3,17 +3,20 @@
 // [GEMM S = Q K^T -> dk_softmax_to_half -> GEMM O = P V] loop (ops.c:390-443,
 // attn.cu:26-89).
 //
-// CTA = 128 query rows of one head, 224 threads, key blocks of 64:
-//   warps 0-3  one query row per thread: read the 64 scores of a key block from TMEM once,
-//              online softmax in fp32 (exp2 domain, running max / sum; the O accumulator
-//              stays in TMEM and is rescaled there only when the maximum grows by more
-//              than 2^kLazyLog2), write P as fp16 into shared memory in the UMMA A-operand
+// CTA = 128 query rows of one head, 352 threads, key blocks of 64:
+//   warps 0-7  softmax: warp w serves TMEM lane quarter w & 3 (query rows 32 (w & 3) ..
+//              +31, one per lane) and column half w >> 2 (32 of the block's 64 keys), so
+//              eight warps share the exponentials; the two warps of a quarter exchange
+//              their half-block maxima through shared memory and an mbarrier.  Online
+//              softmax in fp32 (exp2 domain, running max; the O accumulator stays in TMEM
+//              and is rescaled there only when the maximum grows by more than
+//              2^kLazyLog2), P written as fp16 into shared memory in the UMMA A-operand
 //              layout;
-//   warp 4     TMA producer: Q once, then K blocks into a 4-stage ring (a stage is free
+//   warp 8     TMA producer: Q once, then K blocks into a 4-stage ring (a stage is free
 //              once S of its block has completed);
-//   warp 6     TMA producer: V^T blocks into a 3-stage ring (free once P V of its block
+//   warp 10    TMA producer: V^T blocks into a 3-stage ring (free once P V of its block
 //              has completed);
-//   warp 5     TMEM owner; lane 0 issues S = Q K^T (M=128, N=64, K=hd) into one of two
+//   warp 9     TMEM owner; lane 0 issues S = Q K^T (M=128, N=64, K=hd) into one of two
 //              TMEM score buffers and O += P V (M=128, N=hd, K=64) from one of two P
 //              buffers.  S(j+2) is issued as soon as the softmax warps have read S(j) out
 //              of TMEM (s_empty), so it runs while they exponentiate block j.
@@ -34,7 +37,8 @@
 
 namespace dcb {
 
-constexpr int kAttnThreads = 224;
+constexpr int kAttnThreads = 352;
+constexpr int kSoftWarps = 8, kKWarp = 8, kMmaWarpA = 9, kVWarp = 10;
 constexpr int kQ = 128, kKV = 64, kHD = 64;
 constexpr uint32_t kQBytes = kQ * kHD * 2;      // 16 KB
 constexpr uint32_t kKBytes = kKV * kHD * 2;     // 8 KB
@@ -42,8 +46,10 @@ constexpr uint32_t kVBytes = kHD * kKV * 2;     // 8 KB
 constexpr uint32_t kPBytes = kQ * kKV * 2;      // 16 KB per buffer
 constexpr int kKStages = 4, kVStages = 3;  // K is released after S, V only after P V
 constexpr uint32_t kOnesBytes = 16 * kKV * 2;  // 16 x 64 fp16 ones: the row-sum operand
-constexpr size_t kAttnSmem =
-    kQBytes + kKStages * kKBytes + kVStages * kVBytes + 2 * kPBytes + kOnesBytes + 256;
+constexpr uint32_t kRedBytes = 2 * 2 * kQ * 4;  // half-block maxima [block parity][half][row]
+// + 512: the 32 mbarriers (256 B), the TMEM slot and the abort flag
+constexpr size_t kAttnSmem = kQBytes + kKStages * kKBytes + kVStages * kVBytes + 2 * kPBytes +
+                             kOnesBytes + kRedBytes + 512;
 constexpr int kSumCol = 64;       // TMEM column (after O) of the row sums of P
 constexpr float kLazyLog2 = 2.0f; // rescale when a block maximum exceeds the running one by 4x
 
@@ -55,19 +61,32 @@ struct AttnArgs {
 };
 
 
-// Two non-negative floats below 65520 -> packed fp16x2 (low = a) without the XU pipe, which
-// the exponentials already saturate (the packed conversion cvt.rn.f16x2.f32 runs there, at
-// two passes per instruction).  Scaling by 2^-112 moves the fp32 exponent onto the fp16
-// bias; values below 2^-14 become fp32 subnormals whose bits are exactly the fp16
-// subnormal's shifted up by 13 (the multiply keeps subnormals: no flush-to-zero in this
-// build); adding 0x1000 rounds at bit 13 (half away from zero: differs from nearest-even
-// only on exact ties) and bits 13..28 are the fp16 pattern.  One FMUL per value on the FMA
-// pipe, integer adds and a byte permute on the ALU.
-static __device__ __forceinline__ uint32_t pack_h2_alu(float a, float b) {
-  const uint32_t ua = __float_as_uint(a * 0x1p-112f) + 0x1000u;
-  const uint32_t ub = __float_as_uint(b * 0x1p-112f) + 0x1000u;
-  return __byte_perm(ua >> 13, ub >> 13, 0x5410);
+// 2^x of two fp16 values (PTX ex2.approx.f16x2)
+static __device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
 }
+// (x0, x1) = (a0, a1) * s + c by one packed fp32 FMA (sm_100 fma.rn.f32x2; each lane rounds
+// as fmaf does)
+static __device__ __forceinline__ void fma2(float &x0, float &x1, float a0, float a1, float s,
+                                            float c) {
+  asm("{\n\t.reg .b64 ra, rs, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rs, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rs, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(x0), "=f"(x1)
+      : "f"(a0), "f"(a1), "f"(s), "f"(c));
+}
+// max of three floats in one instruction (sm_100 three-input max.f32)
+static __device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 
 __global__ void __launch_bounds__(kAttnThreads, 2)
     k_flash_attn(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -80,7 +99,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   uint8_t *sV = sK + kKStages * kKBytes;
   uint8_t *sP = sV + kVStages * kVBytes;
   uint8_t *sOnes = sP + 2 * kPBytes;
-  uint64_t *bar = (uint64_t *)(sOnes + kOnesBytes);
+  float *sRed = (float *)(sOnes + kOnesBytes);
+  uint64_t *bar = (uint64_t *)((uint8_t *)sRed + kRedBytes);
   uint64_t *q_full = bar;
   uint64_t *k_full = bar + 1;              // [kKStages]
   uint64_t *k_empty = k_full + kKStages;   // [kKStages]
@@ -91,7 +111,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   uint64_t *p_full = s_empty + 2;          // [2] P buffers written
   uint64_t *p_empty = p_full + 2;          // [2] PV of a P buffer complete
   uint64_t *o_full = p_empty + 2;
-  uint32_t *tslot = (uint32_t *)(o_full + 1);
+  uint64_t *xch = o_full + 1;              // [4 quarters][2] half-block maxima written
+  uint32_t *tslot = (uint32_t *)(xch + 8);
   uint32_t *s_abort = tslot + 1;
 
   // a fault recorded by an earlier kernel, or a misaligned window: end this grid at once
@@ -122,14 +143,15 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&s_empty[i], kSoftWarps);
+      mbar_init(&p_full[i], kSoftWarps);
       mbar_init(&p_empty[i], 1);
     }
     mbar_init(o_full, 1);
+    for (int i = 0; i < 8; i++) mbar_init(&xch[i], 2);
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarpA) {
     tmem_alloc(tslot, 256);
     tmem_relinquish();
   }
@@ -146,7 +168,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   const uint32_t tmem = *tslot;
   const uint32_t tO = tmem + 2 * kKV;
 
-  if (warp == 4) {
+  if (warp == kKWarp) {
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -160,7 +182,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         tma_load_3d(sK + st * kKBytes, &tmK, &k_full[st], 0, j * kKV, bh);
       }
     }
-  } else if (warp == 6) {
+  } else if (warp == kVWarp) {
     if (lane == 0) {
       tma_prefetch_desc(&tmV);
       for (int j = 0; j < nkv; j++) {
@@ -171,7 +193,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         tma_load_3d(sV + st * kVBytes, &tmV, &v_full[st], j * kKV, 0, bh);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarpA) {
     if (lane == 0) {
       // the head dim rounded up to the MMA granule: K steps of S, N of P V
       const int hd16 = (a.hd + 15) / 16;
@@ -222,56 +244,73 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       umma_commit(o_full);
     }
   } else {
-    // softmax warps: one query row per thread, exp2 domain (scores scaled by
-    // scale * log2 e).  The running maximum m is only raised, and O (in TMEM) rescaled,
-    // when a block's maximum exceeds it by more than kLazyLog2: probabilities stay <= 4 and
-    // most blocks need no rescale.  P = 2^(s - m) is evaluated in fp32 (ex2.approx on the
-    // fp32 exponent, relative error ~2^-22) and rounded to fp16, the operand precision P V
-    // uses anyway; the row sum comes from the tensor core (P times a ones tile).
-    const int r = threadIdx.x;
-    const uint32_t lrow = (uint32_t)(warp * 32) << 16;
+    // softmax warps: warp w serves query rows 32 q .. 32 q + 31 (q = w & 3, the TMEM lane
+    // quarter it may access), one per lane, and columns 32 h .. 32 h + 31 (h = w >> 2) of
+    // each 64-key block; exp2 domain (scores scaled by scale * log2 e).  The running maximum
+    // m is only raised, and O (in TMEM) rescaled, when a block's maximum exceeds it by more
+    // than kLazyLog2: probabilities stay <= 4 and most blocks need no rescale.  The block
+    // maximum is the larger of the two warps' half-block maxima (exchanged through shared
+    // memory under an mbarrier of the warp pair), so both warps keep the same m.
+    // P = 2^(s - m) is evaluated two at a time in fp16 (packed fp32 FMA for the exponent,
+    // ex2.approx.f16x2 of its fp16 rounding: at most 2^-11 * 2 error in the exponent of the
+    // largest probabilities), the operand precision P V uses anyway; the row sums come from
+    // the tensor core (P times a ones tile).  tcgen05.ld / st are warp-collective
+    // (.sync.aligned): every decision in front of a TMEM access is warp-uniform (a wait's
+    // outcome through warp_all, the rescale through __any_sync).
+    const int q = warp & 3, h = warp >> 2;
+    const int r = q * 32 + lane;
+    const uint32_t lrow = (uint32_t)(q * 32) << 16;
     const float sl2 = a.scale * 1.4426950408889634f;
     float m_run = -INFINITY;
     bool ok = true;
-    // tcgen05.ld / st are warp-collective (.sync.aligned): every decision in front of a TMEM
-    // access is made warp-uniform (a wait's outcome with warp_all, the rescale by __any_sync)
     for (int j = 0; j < nkv && ok; j++) {
       if (!warp_all(mbar_wait_sleep(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float v[kKV];
-      const uint32_t tS = tmem + (uint32_t)(j & 1) * kKV + lrow;
-#pragma unroll
-      for (int c = 0; c < kKV; c += 16) tmem_ld16(tS + c, *(float(*)[16])(v + c));
+      float v[32];
+      const uint32_t tS = tmem + (uint32_t)(j & 1) * kKV + (uint32_t)h * 32 + lrow;
+      tmem_ld16(tS, *(float(*)[16])v);
+      tmem_ld16(tS + 16, *(float(*)[16])(v + 16));
       tmem_wait_ld();
-      // score buffer j & 1 may take S(j + 2) now
+      // score buffer j & 1 may take S(j + 2) once all eight warps have read it
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[j & 1]);
-      const int kbase = j * kKV;
-      if (kbase + kKV > a.Tk) {
+      const int kbase = j * kKV + h * 32;
+      if (kbase + 32 > a.Tk) {
 #pragma unroll
-        for (int i = 0; i < kKV; i++)
+        for (int i = 0; i < 32; i++)
           if (kbase + i >= a.Tk) v[i] = -INFINITY;
       }
-      // tree reductions: short dependency chains for the per-block max and sum
-      float m8[8];
+      // half-block maximum by three-input max, four independent chains
+      float m4[4];
 #pragma unroll
-      for (int i = 0; i < 8; i++) m8[i] = v[i];
-#pragma unroll
-      for (int i = 8; i < kKV; i++) m8[i & 7] = fmaxf(m8[i & 7], v[i]);
-      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-      const float ms = mx * sl2;
+      for (int c = 0; c < 4; c++) {
+        const float *vc = v + 8 * c;
+        m4[c] = fmaxf(max3(max3(vc[0], vc[1], vc[2]), vc[3], vc[4]), max3(vc[5], vc[6], vc[7]));
+      }
+      const float mh = fmaxf(max3(m4[0], m4[1], m4[2]), m4[3]);
+      // exchange with the other warp of this quarter through shared memory; the pair's
+      // mbarrier (two arrivals, alternating buffers: block j + 2 reuses this one) orders the
+      // writes before the reads, and its wait is bounded like every other
+      float *rb = sRed + (j & 1) * 2 * kQ;
+      rb[h * kQ + r] = mh;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xch[q * 2 + (j & 1)]);
+      if (!warp_all(mbar_wait(&xch[q * 2 + (j & 1)], (uint32_t)(j >> 1) & 1u, kFaultAttn))) {
+        ok = false;
+        break;
+      }
+      const float ms = fmaxf(mh, rb[(1 - h) * kQ + r]) * sl2;
       // raise this row's maximum when its block maximum exceeds it by more than kLazyLog2;
       // the warp rescales when any of its rows does (rows that keep their maximum scale by 1)
       const bool raise = ms > m_run + kLazyLog2;
       if (__any_sync(0xffffffffu, raise)) {
         if (j > 0) {
-          // rescale the accumulated O rows and running sums to the new maxima once PV(j-1)
-          // has completed
+          // rescale this warp's half of the accumulated O rows (and, for h = 0, the running
+          // sums) to the new maxima once PV(j-1) has completed
           if (!warp_all(mbar_wait(&p_empty[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u,
                                   kFaultAttn))) {
             ok = false;
@@ -280,13 +319,16 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
           tc_fence_after();
           const float alpha = raise ? exp2f(m_run - ms) : 1.0f;
 #pragma unroll
-          for (int c = 0; c < kSumCol + 16; c += 16) {
+          for (int c = 0; c < 48; c += 16) {
+            // h = 0: O columns 0..31 and the sums; h = 1: O columns 32..63
+            if (c == 32 && h == 1) break;
+            const uint32_t col = c < 32 ? (uint32_t)(h * 32 + c) : (uint32_t)kSumCol;
             float ov[16];
-            tmem_ld16(tO + lrow + c, ov);
+            tmem_ld16(tO + lrow + col, ov);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; i++) ov[i] *= alpha;
-            tmem_st16(tO + lrow + c, ov);
+            tmem_st16(tO + lrow + col, ov);
           }
           tmem_wait_st();
         }
@@ -298,24 +340,26 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         ok = false;
         break;
       }
-      // P = 2^(s - m) by one fp32 ex2 (a single XU pass per value; the fp16x2 form takes two
-      // passes per pair for the exponential and two more for converting its argument), then
-      // packed to fp16 off the XU pipe
-      uint32_t w[kKV / 2];
+      uint32_t w[16];
+      const float nm = -m_run;
 #pragma unroll
-      for (int i = 0; i < kKV; i += 2)
-        w[i >> 1] = pack_h2_alu(ex2_approx(fmaf(v[i], sl2, -m_run)),
-                                ex2_approx(fmaf(v[i + 1], sl2, -m_run)));
+      for (int i = 0; i < 32; i += 2) {
+        float x0, x1;
+        fma2(x0, x1, v[i], v[i + 1], sl2, nm);
+        w[i >> 1] = ex2_h2(pack_h2(x0, x1));
+      }
+      // this half's four 16-byte chunks (8 keys each) of row r, SW128 A-operand layout
       const uint32_t prow = smem_u32(sP + (j & 1) * kPBytes);
 #pragma unroll
-      for (int c = 0; c < 8; c++)
-        st_shared_v4(prow + sw128_off(r, c), w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+      for (int c = 0; c < 4; c++)
+        st_shared_v4(prow + sw128_off(r, 4 * h + c), w[4 * c], w[4 * c + 1], w[4 * c + 2],
+                     w[4 * c + 3]);
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[j & 1]);
     }
-    // normalise and store the finished O row
+    // normalise and store this warp's half of the finished O row
     if (warp_all(ok && mbar_wait(o_full, 0, kFaultAttn))) {
       tc_fence_after();
       const int t = q0 + r;
@@ -323,11 +367,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       tmem_ld16(tO + lrow + kSumCol, lsum);
       tmem_wait_ld();
       const float inv = 1.0f / lsum[0];
-      const int b = bh / a.H, h = bh - b * a.H;
+      const int b = bh / a.H, hh = bh - b * a.H;
       const int64_t D = (int64_t)a.H * a.hd;
-      const int64_t off = ((int64_t)b * a.Tq + t) * D + (int64_t)h * a.hd;
+      const int64_t off = ((int64_t)b * a.Tq + t) * D + (int64_t)hh * a.hd;
 #pragma unroll
-      for (int c = 0; c < kHD; c += 16) {
+      for (int c = h * 32; c < h * 32 + 32; c += 16) {
         float ov[16];
         tmem_ld16(tO + lrow + c, ov);
         tmem_wait_ld();
@@ -346,7 +390,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarpA) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
   }
