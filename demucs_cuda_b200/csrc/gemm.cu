@@ -2009,10 +2009,12 @@ void gemm_rows(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch,
   s.b_shared = b.stride == 0;
   Gather g{};
   {
-    // algorithmic work of this call (unpadded extents)
+    // algorithmic work of this call (unpadded extents) and its minimum bytes: the fp16
+    // operands once and the output once at its precision (plus C's read when beta != 0,
+    // part of the GEMM's definition); a fused residual's read is the design's extra traffic
     const double mnk = 2.0 * (double)M * (double)N * (double)K * (double)batch;
     double out_b = (double)M * N * batch * (e.mode == EPI_ROWS_F32 || e.mode == EPI_GEMM ? 4 : 2);
-    if (e.res || e.beta != 0.f) out_b *= 2;
+    if (e.beta != 0.f) out_b *= 2;
     const double in_b = 2.0 * ((double)M * K * (a.stride ? batch : 1) +
                                (double)N * K * (b.stride ? batch : 1));
     TraceScope ts(e.mode == EPI_GEMM ? TR_GEMM : TR_LINEAR, mnk, in_b + out_b, M, N, K);
@@ -2272,8 +2274,10 @@ bool conv_half(const HalfAct &x, int KH, int KW, int SH, int SW, int PH, int PW,
     const int64_t M = x.images * Ho * Wo;
     const double n_alg = e.mode == EPI_CONVTR ? (double)e.O * e.stride : (glu ? 2.0 * e.O : e.O);
     const int Kt = KH * KW * x.C;
-    const double out_b = (double)M * n_alg / (glu ? 2 : 1) *
-                         ((e.y ? 4.0 : 0.0) + (e.yh ? 2.0 + (e.hskip ? 4.0 : 0.0) : 0.0));
+    // minimum bytes: the fp16 input and weights once and the output once at its precision
+    // (fp32 when the fp32 tensor is written, else the fp16 copy); the extra fp16
+    // channels-last copy and the decoder skip read are the design's traffic, not counted
+    const double out_b = (double)M * n_alg / (glu ? 2 : 1) * (e.y ? 4.0 : (e.yh ? 2.0 : 0.0));
     TraceScope ts(e.mode == EPI_CONVTR ? TR_CONVTR : TR_CONV, 2.0 * M * n_alg * Kt,
                   (double)x.images * x.H * x.W * x.C * 2.0 + n_alg * Kt * 2.0 + out_b, M,
                   (int64_t)n_alg, Kt);
@@ -2357,10 +2361,12 @@ void gemm_gather(const Gather &g, int64_t M, const uint16_t *w, int64_t N, int64
   const double images = (double)M / ((double)g.Ho * g.Wo);
   const double n_alg = e.mode == EPI_CONVTR ? (double)e.O * e.stride : (glu ? 2.0 * e.O : e.O);
   const double out_elems = e.mode == EPI_CONVTR ? (double)M * e.O * e.stride : (double)M * e.O;
-  const double x_b = images * g.C * g.H * g.W * 4.0 * (g.x2 ? 2 : 1);
+  // minimum bytes: the input once at the precision it is read in (fp32 here), the fp16
+  // weights once and the fp32 output once (a second summed input and a fused residual are
+  // the design's traffic)
+  const double x_b = images * g.C * g.H * g.W * 4.0;
   TraceScope ts(e.mode == EPI_CONVTR ? TR_CONVTR : TR_CONV, 2.0 * M * n_alg * g.K,
-                x_b + n_alg * g.K * 2.0 + out_elems * 4.0 * (e.res ? 2 : 1), M, (int64_t)n_alg,
-                g.K);
+                x_b + n_alg * g.K * 2.0 + out_elems * 4.0, M, (int64_t)n_alg, g.K);
   // a GLU N tile the tensor-core gather kernels do not take (96: the channels-last kernel's)
   const bool odd_tile = bn != 32 && bn != 64 && bn != 128;
   if (!g_opt_simt && !odd_tile) {
