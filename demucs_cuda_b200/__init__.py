@@ -43,7 +43,7 @@ ENGINE_SYMBOLS = [
     "dcb_model_free", "dcb_model_info", "dcb_model_weight_bytes", "dcb_model_weight_block",
     "dcb_forward", "dcb_stage_encoder", "dcb_stage_decoder", "dcb_stage_transformer",
     "dcb_apply_defaults", "dcb_apply", "dcb_apply_plan", "dcb_py_randint", "dcb_segment_plan",
-    "dcb_apply_window", "dcb_apply_shard", "dcb_merge_windows",
+    "dcb_apply_window", "dcb_apply_shard", "dcb_merge_windows", "dcb_apply_host",
 ]
 ALL_SYMBOLS = BACKEND_SYMBOLS + NOALLOC_SYMBOLS + FUSED_SYMBOLS + ENGINE_SYMBOLS
 
@@ -175,6 +175,7 @@ def signatures():
         "dcb_apply_window": (i32, [i32, f32, i32, i32, C.POINTER(DcbApplyOpts),
                                    C.POINTER(i64), C.POINTER(i64)]),
         "dcb_apply_shard": (i32, [vp, vp, i32, i32, vp, i64, C.POINTER(DcbApplyOpts)]),
+        "dcb_apply_host": (i32, [vp, vp, i32, i32, vp, C.POINTER(DcbApplyOpts)]),
         "dcb_merge_windows": (i32, [vp, i64, i64, vp, i64, i64, C.POINTER(i64),
                                     C.POINTER(i64), i32]),
     }
@@ -354,6 +355,18 @@ class Model:
         r = lib().dcb_apply(self._h, _ptr(mix), B, T, _ptr(out), C.byref(o))
         check(r == 0, "apply")
         return out
+
+    def apply_host(self, mix_h, out_h, **kw):
+        """dc_apply_model on host (CPU) tensors mix_h [B, C, T] -> out_h [B, S, C, T], the
+        copies overlapped with the compute (dcb_apply_host); pinned tensors overlap best."""
+        use_torch_stream()
+        assert not mix_h.is_cuda and not out_h.is_cuda
+        assert mix_h.is_contiguous() and out_h.is_contiguous()
+        B, Cc, T = mix_h.shape
+        o = self.apply_opts(**kw)
+        r = lib().dcb_apply_host(self._h, _ptr(mix_h), B, T, _ptr(out_h), C.byref(o))
+        check(r == 0, "apply_host")
+        return out_h
 
     def apply_window(self, T: int, **kw):
         """(lo, hi): the output window of this shard's share (dcb_apply_window)."""

@@ -398,6 +398,11 @@ struct DcbModel {
   std::vector<dcb::FwdGraph> graphs;
   cudaStream_t cap = nullptr;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+  // dcb_apply_host: copy stream, its two events and the device track / stems buffers
+  cudaStream_t hcp = nullptr;
+  cudaEvent_t hev_in = nullptr, hev_out = nullptr;
+  float *hmix = nullptr, *hout = nullptr;
+  size_t hmix_cap = 0, hout_cap = 0;
 };
 
 namespace dcb {
@@ -1014,6 +1019,12 @@ void dcb_model_free(DcbModel *m) {
   if (m->ev_out) cudaEventDestroy(m->ev_out);
   if (m->cap) cudaStreamDestroy(m->cap);
   for (auto &kv : m->pos_cache) cudaFree(kv.second);
+  if (m->hcp) cudaStreamSynchronize(m->hcp);
+  if (m->hev_in) cudaEventDestroy(m->hev_in);
+  if (m->hev_out) cudaEventDestroy(m->hev_out);
+  if (m->hcp) cudaStreamDestroy(m->hcp);
+  cudaFree(m->hmix);
+  cudaFree(m->hout);
   cudaFree(m->ola_w);
   if (m->block) cudaFree(m->block);
   delete m;

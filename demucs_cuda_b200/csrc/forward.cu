@@ -1241,8 +1241,16 @@ static bool make_sched(const Cfg &c, int T, const DcbApplyOpts &o, Sched &sc) {
 // The shard's weighted segments of mix [B, C, T] into its window: win[r][j] += (share of
 // output position lo + j) for rows r < B S C, j < hi - lo (row stride ld; the caller zeroes
 // the window first).
+// Optional per-batch hooks of apply_window: before(k) runs on the host before batch k is
+// enqueued (after the batch's input span is known), after(k) once its accumulation is.
+struct BatchHooks {
+  virtual void before(int k, int64_t in_lo, int64_t in_hi) = 0;
+  virtual void after(int k) = 0;
+  virtual ~BatchHooks() {}
+};
+
 static int apply_window(DcbModel *m, const float *mix, int B, int T, const Sched &sc,
-                        float *win, int64_t ld, float power) {
+                        float *win, int64_t ld, float power, BatchHooks *hooks = nullptr) {
   const Cfg &c = m->cfg;
   const int C = c.audio_channels, S = c.n_sources, Lv = c.valid_length;
   if (!m->ola_w || m->ola_seg != sc.seg || m->ola_pow != power) {
@@ -1258,7 +1266,8 @@ static int apply_window(DcbModel *m, const float *mix, int B, int T, const Sched
     m->ola_pow = power;
   }
   const int rows = B * S * C;
-  for (const auto &bt : sc.batches) {
+  for (int kb = 0; kb < (int)sc.batches.size(); kb++) {
+    const auto &bt = sc.batches[kb];
     const int nbt = (int)bt.size();
     FwdGraph *slot = forward_slot(m, nbt * B, Lv);
     if (!slot) return -1;
@@ -1279,6 +1288,14 @@ static int apply_window(DcbModel *m, const float *mix, int B, int T, const Sched
     t0 = t0 < sc.lo ? sc.lo : t0;
     t1 = t1 > sc.hi ? sc.hi : t1;
     const int64_t per = (int64_t)B * C * Lv;
+    if (hooks) {
+      int64_t in_lo = T, in_hi = 0;
+      for (int k = 0; k < nbt; k++) {
+        in_lo = bi.start[k] < in_lo ? bi.start[k] : in_lo;
+        in_hi = bi.start[k] + Lv > in_hi ? bi.start[k] + Lv : in_hi;
+      }
+      hooks->before(kb, in_lo < 0 ? 0 : in_lo, in_hi > T ? T : in_hi);
+    }
     k_chunk_batch<<<dim3(grid_for(per, 256, 148 * 8), (unsigned)nbt), 256, 0, stream()>>>(
         mix, slot->in, B, C, T, Lv, bi);
     DCB_LAUNCHED();
@@ -1289,9 +1306,51 @@ static int apply_window(DcbModel *m, const float *mix, int B, int T, const Sched
           bi);
       DCB_LAUNCHED();
     }
+    if (hooks) hooks->after(kb);
   }
   return 0;
 }
+
+// dcb_apply_host's copy pipeline on a second stream: before batch k, the part of the track it
+// reads that is not on the device yet goes host -> device and the batch waits for it; after
+// batch k, the output samples that no later batch touches (those before the first output
+// position of batch k + 1; segments are in output order) go device -> host while the next
+// batches compute.
+struct HostPipe : BatchHooks {
+  DcbModel *m;
+  const Sched *sc;
+  const float *mix_h;
+  float *out_h;
+  int64_t T = 0, rows_in = 0, rows_out = 0, in_done = 0, out_done = 0;
+  void before(int k, int64_t lo, int64_t hi) override {
+    (void)k;
+    (void)lo;
+    if (hi > in_done) {
+      DCB_CUDA(cudaMemcpy2DAsync(m->hmix + in_done, (size_t)T * 4, mix_h + in_done,
+                                 (size_t)T * 4, (size_t)(hi - in_done) * 4, (size_t)rows_in,
+                                 cudaMemcpyHostToDevice, m->hcp));
+      in_done = hi;
+      DCB_CUDA(cudaEventRecord(m->hev_in, m->hcp));
+      DCB_CUDA(cudaStreamWaitEvent(stream(), m->hev_in, 0));
+    }
+  }
+  void after(int k) override {
+    int64_t fin = T;
+    if (k + 1 < (int)sc->batches.size()) {
+      for (int i : sc->batches[k + 1]) fin = sc->items[i].out0 < fin ? sc->items[i].out0 : fin;
+    }
+    if (fin < 0) fin = 0;
+    if (fin > out_done) flush(fin);
+  }
+  void flush(int64_t fin) {
+    DCB_CUDA(cudaEventRecord(m->hev_out, stream()));
+    DCB_CUDA(cudaStreamWaitEvent(m->hcp, m->hev_out, 0));
+    DCB_CUDA(cudaMemcpy2DAsync(out_h + out_done, (size_t)T * 4, m->hout + out_done,
+                               (size_t)T * 4, (size_t)(fin - out_done) * 4, (size_t)rows_out,
+                               cudaMemcpyDeviceToHost, m->hcp));
+    out_done = fin;
+  }
+};
 
 }  // namespace dcb
 
@@ -1484,6 +1543,69 @@ int dcb_apply(DcbModel *m, const float *mix, int B, int T, float *out, const Dcb
   const int64_t rows = (int64_t)B * m->cfg.n_sources * m->cfg.audio_channels;
   DCB_CUDA(cudaMemsetAsync(out, 0, (size_t)rows * T * 4, stream()));
   if (apply_window(m, mix, B, T, sc, out + sc.lo, T, o->transition_power) < 0) return -1;
+  DCB_CUDA(cudaStreamSynchronize(stream()));
+  return failed() ? -1 : 0;
+}
+
+int dcb_apply_host(DcbModel *m, const float *mix_h, int B, int T, float *out_h,
+                   const DcbApplyOpts *o) {
+  if (!m || !o || !mix_h || !out_h || B <= 0 || T <= 0) return -1;
+  if (!o->split || o->shard_count > 1) {
+    fail("apply_host: needs split=1 and the whole track (shards use dcb_apply_shard)");
+    return -1;
+  }
+  Sched sc;
+  if (!make_sched(m->cfg, T, *o, sc)) return -1;
+  const int C = m->cfg.audio_channels;
+  const int64_t rows = (int64_t)B * m->cfg.n_sources * C;
+  const size_t nin = (size_t)B * C * T, nout = (size_t)rows * T;
+  if (!m->hcp) {
+    DCB_CUDA(cudaStreamCreateWithFlags(&m->hcp, cudaStreamNonBlocking));
+    DCB_CUDA(cudaEventCreateWithFlags(&m->hev_in, cudaEventDisableTiming));
+    DCB_CUDA(cudaEventCreateWithFlags(&m->hev_out, cudaEventDisableTiming));
+  }
+  if (nin > m->hmix_cap || nout > m->hout_cap) {
+    DCB_CUDA(cudaStreamSynchronize(stream()));
+    DCB_CUDA(cudaStreamSynchronize(m->hcp));
+    if (nin > m->hmix_cap) {
+      cudaFree(m->hmix);
+      m->hmix = nullptr;
+      m->hmix_cap = 0;
+      if (cudaMalloc(&m->hmix, nin * 4) != cudaSuccess) {
+        (void)cudaGetLastError();
+        fail("apply_host: out of device memory for the track (%.1f MB)", nin * 4 / 1e6);
+        return -1;
+      }
+      m->hmix_cap = nin;
+    }
+    if (nout > m->hout_cap) {
+      cudaFree(m->hout);
+      m->hout = nullptr;
+      m->hout_cap = 0;
+      if (cudaMalloc(&m->hout, nout * 4) != cudaSuccess) {
+        (void)cudaGetLastError();
+        fail("apply_host: out of device memory for the stems (%.1f MB)", nout * 4 / 1e6);
+        return -1;
+      }
+      m->hout_cap = nout;
+    }
+  }
+  if (failed()) return -1;
+  // the copy stream starts after everything already queued on the caller's stream
+  DCB_CUDA(cudaEventRecord(m->hev_out, stream()));
+  DCB_CUDA(cudaStreamWaitEvent(m->hcp, m->hev_out, 0));
+  HostPipe hp;
+  hp.m = m;
+  hp.sc = &sc;
+  hp.mix_h = mix_h;
+  hp.out_h = out_h;
+  hp.T = T;
+  hp.rows_in = (int64_t)B * C;
+  hp.rows_out = rows;
+  DCB_CUDA(cudaMemsetAsync(m->hout, 0, nout * 4, stream()));
+  if (apply_window(m, m->hmix, B, T, sc, m->hout, T, o->transition_power, &hp) < 0) return -1;
+  if (hp.out_done < T) hp.flush(T);
+  DCB_CUDA(cudaStreamSynchronize(m->hcp));
   DCB_CUDA(cudaStreamSynchronize(stream()));
   return failed() ? -1 : 0;
 }

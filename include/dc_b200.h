@@ -277,6 +277,14 @@ void dcb_apply_defaults(DcbApplyOpts *o);
  * shard_count > 1, out holds this shard's share (zero outside its window), so the shards'
  * outputs sum to the full result. */
 int dcb_apply(DcbModel *m, const float *mix, int B, int T, float *out, const DcbApplyOpts *o);
+/* dcb_apply on HOST buffers: mix_h [B][C][T] and out_h [B][S][C][T] in host memory (page-
+ * locked memory lets the copies overlap the compute; pageable memory works, serialised).
+ * Each segment batch's input span is copied in just before the batch, and each stretch of
+ * the output that no later batch touches is copied back while the next batches compute,
+ * on a second stream; returns when out_h holds the stems.  Whole track only (shard_count
+ * <= 1); the device buffers are kept by the model and reused.  Returns 0 or -1. */
+int dcb_apply_host(DcbModel *m, const float *mix_h, int B, int T, float *out_h,
+                   const DcbApplyOpts *o);
 /* Data-parallel form of dcb_apply.  The segments of all shift passes, ordered by output
  * position, are split into shard_count contiguous blocks; a shard's share of the output is
  * non-zero only on its window [lo, hi) along time (about 1 / shard_count of the track plus

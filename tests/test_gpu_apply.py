@@ -159,3 +159,25 @@ def test_layout_only_load_and_packed_image(tiny_apply, tmp_path):
     with pytest.raises(dcb.BackendError, match="checksum"):
         dcb.Model.from_packed(bad)
     del lay, pk
+
+
+def test_apply_host_buffers_match_device_apply(tiny_apply):
+    """dcb_apply_host (host input and output, copies overlapped with the batches on a second
+    stream) gives dcb_apply's result, with page-locked and with ordinary host tensors, and
+    leaves the rest of the output buffer's contents irrelevant (every sample is written)."""
+    import demucs_cuda_b200 as dcb
+    torch = tiny_apply["torch"]
+    model = tiny_apply["model"]
+    dcb.set_option("graphs", 1)
+    mix = tiny_apply["mix"]
+    want = model.apply(torch.from_numpy(mix).cuda(), shifts=1, batch_size=2).cpu().numpy()
+    for pinned in (True, False):
+        mh = torch.from_numpy(mix.copy())
+        oh = torch.full((1, model.n_sources, 2, mix.shape[-1]), float("nan"))
+        if pinned:
+            mh, oh = mh.pin_memory(), oh.pin_memory()
+        for _ in range(2):
+            model.apply_host(mh, oh, shifts=1, batch_size=2)
+            assert rel_l2(oh.numpy(), want) < 1e-6
+    dcb.set_option("graphs", 0)
+    assert dcb.device_fault() == 0
