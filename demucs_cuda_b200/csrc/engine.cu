@@ -398,8 +398,9 @@ struct DcbModel {
   std::vector<dcb::FwdGraph> graphs;
   cudaStream_t cap = nullptr;
   cudaEvent_t ev_in = nullptr, ev_out = nullptr;
-  // dcb_apply_host: copy stream, its two events and the device track / stems buffers
-  cudaStream_t hcp = nullptr;
+  // dcb_apply_host: upload (hcp) and download (hcd) streams, their events and the device
+  // track / stems buffers
+  cudaStream_t hcp = nullptr, hcd = nullptr;
   cudaEvent_t hev_in = nullptr, hev_out = nullptr;
   float *hmix = nullptr, *hout = nullptr;
   size_t hmix_cap = 0, hout_cap = 0;
@@ -1020,9 +1021,11 @@ void dcb_model_free(DcbModel *m) {
   if (m->cap) cudaStreamDestroy(m->cap);
   for (auto &kv : m->pos_cache) cudaFree(kv.second);
   if (m->hcp) cudaStreamSynchronize(m->hcp);
+  if (m->hcd) cudaStreamSynchronize(m->hcd);
   if (m->hev_in) cudaEventDestroy(m->hev_in);
   if (m->hev_out) cudaEventDestroy(m->hev_out);
   if (m->hcp) cudaStreamDestroy(m->hcp);
+  if (m->hcd) cudaStreamDestroy(m->hcd);
   cudaFree(m->hmix);
   cudaFree(m->hout);
   cudaFree(m->ola_w);

@@ -1311,11 +1311,11 @@ static int apply_window(DcbModel *m, const float *mix, int B, int T, const Sched
   return 0;
 }
 
-// dcb_apply_host's copy pipeline on a second stream: before batch k, the part of the track it
-// reads that is not on the device yet goes host -> device and the batch waits for it; after
-// batch k, the output samples that no later batch touches (those before the first output
-// position of batch k + 1; segments are in output order) go device -> host while the next
-// batches compute.
+// dcb_apply_host's copy pipeline on two copy streams (one per direction, so an upload never
+// queues behind a download): before batch k, the part of the track it reads that is not on
+// the device yet goes host -> device and the batch waits for it; after batch k, the output
+// samples that no later batch touches (those before the first output position of batch
+// k + 1; segments are in output order) go device -> host while the next batches compute.
 struct HostPipe : BatchHooks {
   DcbModel *m;
   const Sched *sc;
@@ -1344,10 +1344,10 @@ struct HostPipe : BatchHooks {
   }
   void flush(int64_t fin) {
     DCB_CUDA(cudaEventRecord(m->hev_out, stream()));
-    DCB_CUDA(cudaStreamWaitEvent(m->hcp, m->hev_out, 0));
+    DCB_CUDA(cudaStreamWaitEvent(m->hcd, m->hev_out, 0));
     DCB_CUDA(cudaMemcpy2DAsync(out_h + out_done, (size_t)T * 4, m->hout + out_done,
                                (size_t)T * 4, (size_t)(fin - out_done) * 4, (size_t)rows_out,
-                               cudaMemcpyDeviceToHost, m->hcp));
+                               cudaMemcpyDeviceToHost, m->hcd));
     out_done = fin;
   }
 };
@@ -1561,12 +1561,14 @@ int dcb_apply_host(DcbModel *m, const float *mix_h, int B, int T, float *out_h,
   const size_t nin = (size_t)B * C * T, nout = (size_t)rows * T;
   if (!m->hcp) {
     DCB_CUDA(cudaStreamCreateWithFlags(&m->hcp, cudaStreamNonBlocking));
+    DCB_CUDA(cudaStreamCreateWithFlags(&m->hcd, cudaStreamNonBlocking));
     DCB_CUDA(cudaEventCreateWithFlags(&m->hev_in, cudaEventDisableTiming));
     DCB_CUDA(cudaEventCreateWithFlags(&m->hev_out, cudaEventDisableTiming));
   }
   if (nin > m->hmix_cap || nout > m->hout_cap) {
     DCB_CUDA(cudaStreamSynchronize(stream()));
     DCB_CUDA(cudaStreamSynchronize(m->hcp));
+    DCB_CUDA(cudaStreamSynchronize(m->hcd));
     if (nin > m->hmix_cap) {
       cudaFree(m->hmix);
       m->hmix = nullptr;
@@ -1591,9 +1593,10 @@ int dcb_apply_host(DcbModel *m, const float *mix_h, int B, int T, float *out_h,
     }
   }
   if (failed()) return -1;
-  // the copy stream starts after everything already queued on the caller's stream
+  // the copy streams start after everything already queued on the caller's stream
   DCB_CUDA(cudaEventRecord(m->hev_out, stream()));
   DCB_CUDA(cudaStreamWaitEvent(m->hcp, m->hev_out, 0));
+  DCB_CUDA(cudaStreamWaitEvent(m->hcd, m->hev_out, 0));
   HostPipe hp;
   hp.m = m;
   hp.sc = &sc;
@@ -1606,6 +1609,7 @@ int dcb_apply_host(DcbModel *m, const float *mix_h, int B, int T, float *out_h,
   if (apply_window(m, m->hmix, B, T, sc, m->hout, T, o->transition_power, &hp) < 0) return -1;
   if (hp.out_done < T) hp.flush(T);
   DCB_CUDA(cudaStreamSynchronize(m->hcp));
+  DCB_CUDA(cudaStreamSynchronize(m->hcd));
   DCB_CUDA(cudaStreamSynchronize(stream()));
   return failed() ? -1 : 0;
 }

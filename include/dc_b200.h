@@ -281,7 +281,7 @@ int dcb_apply(DcbModel *m, const float *mix, int B, int T, float *out, const Dcb
  * locked memory lets the copies overlap the compute; pageable memory works, serialised).
  * Each segment batch's input span is copied in just before the batch, and each stretch of
  * the output that no later batch touches is copied back while the next batches compute,
- * on a second stream; returns when out_h holds the stems.  Whole track only (shard_count
+ * on two copy streams (one per direction); returns when out_h holds the stems.  Whole track only (shard_count
  * <= 1); the device buffers are kept by the model and reused.  Returns 0 or -1. */
 int dcb_apply_host(DcbModel *m, const float *mix_h, int B, int T, float *out_h,
                    const DcbApplyOpts *o);
