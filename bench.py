@@ -337,8 +337,10 @@ def b200_arm(args):
     value = audio / (ms / 1e3)
     e2e = audio / (ms_e2e / 1e3)
     hbm, tflops_burst, tflops_sus, pk_kind = peaks()
-    # dominant kernel class of the timed region (CUDA events around its launches)
-    kinds = {k: v for k, v in tr.items() if v["launches"]}
+    # dominant kernel class of the timed region (CUDA events around its launches); the
+    # memory-bound glue classes are reported separately (bytes only)
+    glue = {k: v for k, v in tr.items() if v["launches"] and k in dcb.GLUE_CLASSES}
+    kinds = {k: v for k, v in tr.items() if v["launches"] and k not in dcb.GLUE_CLASSES}
     dom = max(kinds, key=lambda k: kinds[k]["ms"])
     d = kinds[dom]
     per_launch_ms = d["ms"] / d["launches"]
@@ -370,6 +372,11 @@ def b200_arm(args):
                    "tflops": v["flops"] / (v["ms"] * 1e-3) / 1e12 if v["ms"] else 0.0,
                    "gbs": v["bytes"] / (v["ms"] * 1e-3) / 1e9 if v["ms"] else 0.0,
                    "launches_per_step": v["launches"] / args.steps} for k, v in kinds.items()}
+    glue_rep = {k: {"share_of_step": v["ms"] / args.steps / ms,
+                    "gbs": v["bytes"] / (v["ms"] * 1e-3) / 1e9 if v["ms"] else 0.0,
+                    "frac_of_hbm": (v["bytes"] / (v["ms"] * 1e-3) / 1e9) / hbm if v["ms"] else 0.0,
+                    "launches_per_step": v["launches"] / args.steps,
+                    "mb_per_step": v["bytes"] / args.steps / 1e6} for k, v in glue.items()}
     gemm_flops = sum(v["flops"] for v in kinds.values()) / args.steps
     gemm_ms = sum(v["ms"] for v in kinds.values()) / args.steps
 
@@ -417,6 +424,7 @@ def b200_arm(args):
                      if gemm_ms else None, "peak_tflops": tflops_sus,
                      "share_of_step": gemm_ms / ms, "traced_ms_per_step": ms_tr,
                      "classes": classes},
+            "glue": glue_rep,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "device_fault": fault,

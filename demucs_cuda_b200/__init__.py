@@ -470,10 +470,12 @@ def kernel_launches() -> int:
     return lib().dcb_kernel_launches()
 
 
-TRACE_CLASSES = ["conv", "conv_tr", "linear", "attention", "gemm_half"]
+TRACE_CLASSES = ["conv", "conv_tr", "linear", "attention", "gemm_half", "spectral", "dconv",
+                 "norm"]
+GLUE_CLASSES = ("spectral", "dconv", "norm")
 
 
-def trace_start(classes=("conv", "conv_tr", "linear", "attention", "gemm_half")):
+def trace_start(classes=tuple(TRACE_CLASSES)):
     mask = 0
     for c in classes:
         mask |= 1 << TRACE_CLASSES.index(c)

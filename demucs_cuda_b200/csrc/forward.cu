@@ -305,6 +305,10 @@ static void dconv_tail(const DConvW &dw, const float *h, float *y, int B, int C,
   const int64_t ysB = (int64_t)C * Fr * T, ysC = (int64_t)Fr * T;
   uint16_t *yhp = yh ? yh->p : nullptr;
   const int64_t pitch = yh ? yh->Wp : 0;
+  // minimum bytes: h read once, y read and rewritten, its fp16 companion written
+  TraceScope ts(TR_DCONV, 0.0,
+                (double)total * ((double)hid * 4.0 + (double)C * 8.0 + (yhp ? C * 2.0 : 0.0)),
+                total, C, hid);
 #define DCB_TAIL(P)                                                                            \
   k_dconv_tail<P><<<grid, 256, sm, stream()>>>(h, y, dw.c3.w, dw.c3.ld, dw.c3.bias, dw.gn4.w, \
                                               dw.gn4.b, dw.scale, zmean, zrstd, B, C, hid,   \
@@ -360,15 +364,24 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
         attr = sm;
       }
+      TraceScope ts(TR_DCONV, 0.0,
+                    (double)rows * T * ((double)hid * 8.0 + (h16.p ? hidp * 2.0 : 0.0)),
+                    rows, hid, T);
       k_gn_gelu_zstats<<<rows, kGnFusedThreads, sm, stream()>>>(
           rh, h, dw.gn1.w, dw.gn1.b, 1e-5f, dw.zc, C2, stat, stat + rows, h16.p, hidp);
       DCB_LAUNCHED();
     } else {
-      rowview_stats(rh, B, 1e-5f, stat, stat + rows, nullptr);
       const int64_t n = (int64_t)B * hid * Fr * T;
-      k_gn_gelu<<<grid_for(n, 256), 256, 0, stream()>>>(rh, h, stat, stat + rows, dw.gn1.w,
-                                                       dw.gn1.b, B);
-      DCB_LAUNCHED();
+      {
+        TraceScope ts(TR_DCONV, 0.0, (double)n * 4.0, rows, hid, T);
+        rowview_stats(rh, B, 1e-5f, stat, stat + rows, nullptr);
+      }
+      {
+        TraceScope ts(TR_DCONV, 0.0, (double)n * 8.0, rows, hid, T);
+        k_gn_gelu<<<grid_for(n, 256), 256, 0, stream()>>>(rh, h, stat, stat + rows, dw.gn1.w,
+                                                         dw.gn1.b, B);
+        DCB_LAUNCHED();
+      }
       if (h16.p) {
         const int64_t nh = (int64_t)B * Fr * T * (hidp / 8);
         k_to_half_cl<<<grid_for(nh, 256), 256, 0, stream()>>>(
@@ -382,8 +395,12 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
       DCB_CUDA(cudaMemsetAsync(acc, 0, (size_t)rows * (npair + hid) * sizeof(double), stream()));
       const dim3 gg((unsigned)((T + chunk - 1) / chunk), rows,
                     (unsigned)((npair + hid + kGramPairs - 1) / kGramPairs));
-      k_gram_chunk<<<gg, 256, (size_t)hid * chunk * sizeof(float), stream()>>>(rh, chunk, acc);
-      DCB_LAUNCHED();
+      {
+        TraceScope ts(TR_DCONV, 0.0, (double)n * 4.0, rows, hid, T);
+        k_gram_chunk<<<gg, 256, (size_t)hid * chunk * sizeof(float), stream()>>>(rh, chunk,
+                                                                                  acc);
+        DCB_LAUNCHED();
+      }
       k_zstats_final<<<(rows + 3) / 4, 128, 0, stream()>>>(acc, dw.zc, hid, T, C2, (int)rows,
                                                           1e-5f, stat, stat + rows);
       DCB_LAUNCHED();
@@ -718,9 +735,12 @@ static void tlayer_branch(DcbModel *m, const TLayerW &tl, float *x, int B, int T
   linear_rows(tl.lin2, b.hid, R, e3);
   // GroupNorm(1) over [Tq, D] per batch, affine on D (norm_out)
   float *st = dalloc((size_t)B * 2);
-  row_stats(x, B, (int64_t)Tq * D, st, st + B);
-  dk_norm_apply_last(x, x, st, st + B, tl.norm_out.w, tl.norm_out.b, B, (int64_t)Tq * D, D,
-                     1e-5f);
+  {
+    TraceScope ts(TR_NORM, 0.0, (double)B * Tq * D * 12.0, B, D, Tq);  // stats + apply
+    row_stats(x, B, (int64_t)Tq * D, st, st + B);
+    dk_norm_apply_last(x, x, st, st + B, tl.norm_out.w, tl.norm_out.b, B, (int64_t)Tq * D, D,
+                       1e-5f);
+  }
   dfree(st);
 }
 

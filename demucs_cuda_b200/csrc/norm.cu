@@ -519,6 +519,7 @@ __global__ void __launch_bounds__(128)
 void layernorm(const float *x, void *y, const float *w, const float *b, int64_t rows, int C,
                float eps, bool half_out, int ld_out) {
   if (rows <= 0) return;
+  TraceScope ts(TR_NORM, 0.0, (double)rows * C * (4.0 + (half_out ? 2.0 : 4.0)), rows, C, 0);
   // vector path: C = 128 * NV with aligned rows and parameters (and no output padding)
   const bool vec = C % 128 == 0 && C <= 1024 && ld_out == C && ((uintptr_t)x & 15) == 0 &&
                    ((uintptr_t)y & 15) == 0 && (!w || ((uintptr_t)w & 15) == 0) &&

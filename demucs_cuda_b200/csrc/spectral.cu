@@ -562,9 +562,12 @@ void ispec_fused(const float *x, float *out, const float *mean, const float *var
   float2 *z = nullptr;
   DCB_CUDA(cudaMallocAsync(&z, (size_t)R * N * F * sizeof(float2), stream()));
   dim3 tg((unsigned)((N + 31) / 32), (unsigned)((F + 31) / 32), (unsigned)R);
-  k_spec_frames_major<<<tg, dim3(32, 8), 0, stream()>>>(x, z, mean, var, rows_per_b, F, N,
-                                                         eps);
-  DCB_LAUNCHED();
+  {
+    TraceScope ts(TR_SPECTRAL, 0.0, 2.0 * R * N * F * 8.0, R, F, N);
+    k_spec_frames_major<<<tg, dim3(32, 8), 0, stream()>>>(x, z, mean, var, rows_per_b, F, N,
+                                                           eps);
+    DCB_LAUNCHED();
+  }
   const int j_first = (int)(start / hop);
   const int j_last = (int)((start + length - 1) / hop);
   const int groups = (j_last - j_first + 1 + kOlaHops - 1) / kOlaHops;
@@ -590,9 +593,13 @@ void ispec_fused(const float *x, float *out, const float *mean, const float *var
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
       attr = true;
     }
-    k_istft_stream4096<<<dim3((unsigned)runs, (unsigned)R), kFftThreads, sm, stream()>>>(
-        z, out, N, F, NF, window, twiddles4096(), start, length, g_first);
-    DCB_LAUNCHED();
+    {
+      TraceScope ts(TR_SPECTRAL, 0.0, (double)R * N * F * 8.0 + (double)R * length * 4.0, R,
+                    F, length);
+      k_istft_stream4096<<<dim3((unsigned)runs, (unsigned)R), kFftThreads, sm, stream()>>>(
+          z, out, N, F, NF, window, twiddles4096(), start, length, g_first);
+      DCB_LAUNCHED();
+    }
     DCB_CUDA(cudaFreeAsync(z, stream()));
     return;
   }
@@ -633,18 +640,30 @@ void spec_normalised(const float *xc, int B, int C, int64_t L, int n_fft, int ho
   DCB_REQUIRE(n_fft == kFftN && R <= 65535, "spec: n_fft %d (this path needs 4096)", n_fft);
   float2 *z = nullptr;
   DCB_CUDA(cudaMallocAsync(&z, (size_t)R * nframes * nbins * sizeof(float2), stream()));
-  k_stft_fm<<<dim3((unsigned)nframes, (unsigned)R), kFftThreads, 0, stream()>>>(
-      xc, z, L, hop, frame0, nframes, nbins, window, twiddles4096());
-  DCB_LAUNCHED();
-  // the statistics cover the same elements in any order
-  row_stats((const float *)z, B, (int64_t)C * nframes * nbins * 2, mean, var);
+  const double zb = (double)R * nframes * nbins * 8.0;
+  {
+    TraceScope ts(TR_SPECTRAL, 0.0, (double)R * L * 4.0 + zb, R, nbins, nframes);
+    k_stft_fm<<<dim3((unsigned)nframes, (unsigned)R), kFftThreads, 0, stream()>>>(
+        xc, z, L, hop, frame0, nframes, nbins, window, twiddles4096());
+    DCB_LAUNCHED();
+  }
+  {
+    // the statistics cover the same elements in any order
+    TraceScope ts(TR_SPECTRAL, 0.0, zb, R, nbins, nframes);
+    row_stats((const float *)z, B, (int64_t)C * nframes * nbins * 2, mean, var);
+  }
   dim3 tg((unsigned)((nframes + 31) / 32), (unsigned)((nbins + 31) / 32), (unsigned)R);
   if (mag) {
+    TraceScope ts(TR_SPECTRAL, 0.0, 2.0 * zb, R, nbins, nframes);
     k_fm_to_chw<<<tg, dim3(32, 8), 0, stream()>>>(z, mag, mean, var, C, nbins, nframes, 0.f, 0);
     DCB_LAUNCHED();
   }
-  k_fm_to_chw<<<tg, dim3(32, 8), 0, stream()>>>(z, x, mean, var, C, nbins, nframes, 1e-5f, 1);
-  DCB_LAUNCHED();
+  {
+    TraceScope ts(TR_SPECTRAL, 0.0, 2.0 * zb, R, nbins, nframes);
+    k_fm_to_chw<<<tg, dim3(32, 8), 0, stream()>>>(z, x, mean, var, C, nbins, nframes, 1e-5f,
+                                                  1);
+    DCB_LAUNCHED();
+  }
   DCB_CUDA(cudaFreeAsync(z, stream()));
 }
 

@@ -8,7 +8,14 @@
 
 namespace dcb {
 
-enum TraceClass : int { TR_CONV = 0, TR_CONVTR, TR_LINEAR, TR_ATTN, TR_GEMM, TR_NCLASS };
+// classes 0-4 are tensor-core kernels (FLOPs and minimum bytes), 5-7 the memory-bound glue
+// of the forward (minimum bytes: each input read once, each output written once): the STFT /
+// inverse STFT and their layout passes, the DConv GroupNorm statistics and CUDA-core tail,
+// and the transformer's LayerNorms / GroupNorm
+enum TraceClass : int {
+  TR_CONV = 0, TR_CONVTR, TR_LINEAR, TR_ATTN, TR_GEMM, TR_SPECTRAL, TR_DCONV, TR_NORM,
+  TR_NCLASS
+};
 
 struct TraceRec {
   int cls;

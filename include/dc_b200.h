@@ -206,7 +206,9 @@ uint64_t dcb_kernel_launches(void);
 /* Device-side fault word: bounded waits that expire set a bit here (0 = healthy). */
 uint32_t dcb_device_fault(int clear);
 /* Kernel-class trace: bit c of mask enables class c (0 implicit-GEMM conv, 1 stride-phase
- * transposed conv, 2 transformer linear, 3 flash attention, 4 dk_gemm_half).  Every
+ * transposed conv, 2 transformer linear, 3 flash attention, 4 dk_gemm_half, 5 STFT /
+ * inverse STFT and their layout passes, 6 DConv GroupNorm statistics and CUDA-core tail,
+ * 7 transformer LayerNorm / GroupNorm; 5-7 carry bytes only).  Every
  * launch of an enabled class is bracketed by CUDA events on the backend stream and tagged
  * with its algorithmic FLOPs and bytes; dcb_trace_stop synchronises and returns per-class
  * totals (milliseconds, FLOPs, bytes, launches) for classes < ncls. */
