@@ -401,8 +401,8 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
                                                                                   acc);
         DCB_LAUNCHED();
       }
-      k_zstats_final<<<(rows + 3) / 4, 128, 0, stream()>>>(acc, dw.zc, hid, T, C2, (int)rows,
-                                                          1e-5f, stat, stat + rows);
+      k_zstats_final<<<(unsigned)rows, 256, 0, stream()>>>(acc, dw.zc, hid, T, C2, (int)rows,
+                                                            1e-5f, stat, stat + rows);
       DCB_LAUNCHED();
       dfree(acc);
     }

@@ -141,6 +141,20 @@ __global__ void k_gn_gelu(RowView v, float *__restrict__ y, const float *__restr
 // threads of the one-CTA-per-row GroupNorm kernels
 constexpr int kGnFusedThreads = 256;
 
+// Upper-triangle entry p of a hid x hid Gram matrix -> (j, k), j <= k, in the order
+// (0,0), (0,1), .., (0,hid-1), (1,1), ..: entry (j, j) is at j hid - j (j - 1) / 2, so j is
+// the root of that quadratic (fp32 estimate, corrected by at most a step either way).
+static __device__ __forceinline__ void gram_pair(int p, int hid, int &j, int &k) {
+  const float b = 2.0f * (float)hid + 1.0f;
+  int jj = (int)((b - sqrtf(fmaxf(b * b - 8.0f * (float)p, 0.f))) * 0.5f);
+  if (jj < 0) jj = 0;
+  if (jj > hid - 1) jj = hid - 1;
+  while (jj > 0 && jj * hid - jj * (jj - 1) / 2 > p) jj--;
+  while (jj + 1 < hid && (jj + 1) * hid - (jj + 1) * jj / 2 <= p) jj++;
+  j = jj;
+  k = jj + (p - (jj * hid - jj * (jj - 1) / 2));
+}
+
 // DConv hidden rows (layers.c:24-53, the freq branch viewed as B*Fr rows [hid][T]):
 // GroupNorm(1) + GELU in place, one CTA per row, and the GroupNorm(1) statistics of the
 // row's next 1x1 conv output z = W16 . fp16(h) + b without forming z.  With S_j the sums
@@ -224,13 +238,7 @@ __global__ void __launch_bounds__(kGnFusedThreads)
   for (int p = wid; p < npair + hid; p += kGnFusedThreads / 32) {
     int j, k;
     if (p < npair) {
-      j = 0;
-      int q = p;
-      while (q >= hid - j) {
-        q -= hid - j;
-        j++;
-      }
-      k = j + q;
+      gram_pair(p, hid, j, k);
     } else {
       j = p - npair;
       k = -1;
@@ -298,13 +306,7 @@ __global__ void __launch_bounds__(256)
   for (int p = blockIdx.z * kGramPairs + wid; p < p_end; p += blockDim.x / 32) {
     int j, k;
     if (p < npair) {
-      j = 0;
-      int q = p;
-      while (q >= hid - j) {
-        q -= hid - j;
-        j++;
-      }
-      k = j + q;
+      gram_pair(p, hid, j, k);
     } else {
       j = p - npair;
       k = -1;
@@ -325,36 +327,49 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// GroupNorm statistics of z from the accumulated sums (see k_gn_gelu_zstats), one warp per
-// row: lanes split the Gram entries, fp64 shuffle reduction
-__global__ void k_zstats_final(const double *__restrict__ acc, const double *__restrict__ zc,
-                               int hid, int64_t T, int C2, int rows, float eps,
-                               float *__restrict__ zmean, float *__restrict__ zrstd) {
-  const int row = (int)(((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
-  const int lane = threadIdx.x & 31;
+// GroupNorm statistics of z from the accumulated sums (see k_gn_gelu_zstats), one CTA of
+// 256 threads per row: warp w takes the Gram rows j = w, w + 8, .., its lanes the entries
+// (j, k >= j) of each, addressed directly (entry (j, k) of the upper triangle sits at
+// j hid - j (j - 1) / 2 + k - j); fp64 shuffle and shared-memory reduction
+__global__ void __launch_bounds__(256)
+    k_zstats_final(const double *__restrict__ acc, const double *__restrict__ zc, int hid,
+                   int64_t T, int C2, int rows, float eps, float *__restrict__ zmean,
+                   float *__restrict__ zrstd) {
+  __shared__ double red[2][8];
+  const int row = blockIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   if (row >= rows) return;
   const int npair = hid * (hid + 1) / 2;
   const double *a = acc + (int64_t)row * (npair + hid);
   const double *G = zc, *u = zc + hid * hid, *vv = u + hid;
   double sz = 0.0, szz = 0.0;
-  for (int p = lane; p < npair; p += 32) {
-    int j = 0, q = p;
-    while (q >= hid - j) {
-      q -= hid - j;
-      j++;
-    }
-    const int k = j + q;
-    szz += (j == k ? 1.0 : 2.0) * G[j * hid + k] * a[p];
+  for (int j = wid; j < hid; j += 8) {
+    const int base = j * hid - j * (j - 1) / 2;
+    for (int k = j + lane; k < hid; k += 32)
+      szz += (k == j ? 1.0 : 2.0) * G[j * hid + k] * a[base + (k - j)];
   }
-  for (int j = lane; j < hid; j += 32) {
-    sz += u[j] * a[npair + j];
-    szz += 2.0 * vv[j] * a[npair + j];
+  if (wid == 0) {
+    for (int j = lane; j < hid; j += 32) {
+      sz += u[j] * a[npair + j];
+      szz += 2.0 * vv[j] * a[npair + j];
+    }
   }
   for (int o = 16; o > 0; o >>= 1) {
     sz += __shfl_xor_sync(0xffffffffu, sz, o);
     szz += __shfl_xor_sync(0xffffffffu, szz, o);
   }
   if (lane == 0) {
+    red[0][wid] = sz;
+    red[1][wid] = szz;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    sz = 0.0;
+    szz = 0.0;
+    for (int w = 0; w < 8; w++) {
+      sz += red[0][w];
+      szz += red[1][w];
+    }
     sz += (double)T * zc[hid * hid + 2 * hid];
     szz += (double)T * zc[hid * hid + 2 * hid + 1];
     const double nz = (double)C2 * T;

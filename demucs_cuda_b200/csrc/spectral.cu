@@ -267,7 +267,14 @@ static __device__ __forceinline__ void dft16(float2 (&v)[16]) {
 #pragma unroll
   for (int k1 = 0; k1 < 4; k1++) dft4(v[4 * k1], v[4 * k1 + 1], v[4 * k1 + 2], v[4 * k1 + 3]);
 }
-// forward DFT of buf (padded layout, natural order in and out); tw[e] = exp(-2 pi i e / 4096)
+// Pass twiddles of fft4096, laid out [pass][r][k] so that a warp's load of twiddle r for its
+// 32 consecutive k falls in one or two 128-byte lines: pass 1 (Ns = 16) holds
+// exp(-2 pi i k r / 256) at (r - 1) * 16 + k, pass 2 (Ns = 256) holds exp(-2 pi i k r / 4096)
+// at kTwPass2 + (r - 1) * 256 + k, for r = 1..15.
+constexpr int kTwPass2 = 15 * 16;
+constexpr int kTwEntries = kTwPass2 + 15 * 256;
+
+// forward DFT of buf (padded layout, natural order in and out); tw: the pass tables above
 static __device__ __forceinline__ void fft4096(float2 *buf, const float2 *__restrict__ tw) {
   const int j = threadIdx.x;
 #pragma unroll
@@ -278,8 +285,9 @@ static __device__ __forceinline__ void fft4096(float2 *buf, const float2 *__rest
     for (int r = 0; r < 16; r++) v[r] = buf[fpad(j + 256 * r)];
     const int k = j & (Ns - 1);
     if (pass > 0) {
+      const float2 *twp = tw + (pass == 1 ? 0 : kTwPass2) + k;
 #pragma unroll
-      for (int r = 1; r < 16; r++) v[r] = cmulf(v[r], __ldg(tw + ((k * r) << (8 - lg))));
+      for (int r = 1; r < 16; r++) v[r] = cmulf(v[r], __ldg(twp + (r - 1) * Ns));
     }
     dft16(v);
     __syncthreads();
@@ -293,15 +301,23 @@ static __device__ __forceinline__ void fft4096(float2 *buf, const float2 *__rest
 static float2 *g_tw_full = nullptr;
 
 // exp(-2 pi i e / 4096) for e < 4096, evaluated in double on the host
+// fft4096's pass tables, evaluated in double on the host (entry of pass p, r, k:
+// exp(-2 pi i e / 4096) with e = k r 4096 / (16 Ns), Ns = 16^p)
 static const float2 *twiddles4096() {
   if (g_tw_full) return g_tw_full;
-  std::vector<float2> h(kFftN);
-  for (int e = 0; e < kFftN; e++) {
-    const double a = -2.0 * 3.14159265358979323846 * (double)e / (double)kFftN;
-    h[e] = make_float2((float)cos(a), (float)sin(a));
+  std::vector<float2> h(kTwEntries);
+  for (int pass = 1; pass < 3; pass++) {
+    const int Ns = 1 << (4 * pass), base = pass == 1 ? 0 : kTwPass2;
+    for (int r = 1; r < 16; r++)
+      for (int k = 0; k < Ns; k++) {
+        const int e = (k * r) << (8 - 4 * pass);
+        const double a = -2.0 * 3.14159265358979323846 * (double)e / (double)kFftN;
+        h[base + (r - 1) * Ns + k] = make_float2((float)cos(a), (float)sin(a));
+      }
   }
-  DCB_CUDA(cudaMalloc(&g_tw_full, kFftN * sizeof(float2)));
-  DCB_CUDA(cudaMemcpy(g_tw_full, h.data(), kFftN * sizeof(float2), cudaMemcpyHostToDevice));
+  DCB_CUDA(cudaMalloc(&g_tw_full, kTwEntries * sizeof(float2)));
+  DCB_CUDA(cudaMemcpy(g_tw_full, h.data(), kTwEntries * sizeof(float2),
+                      cudaMemcpyHostToDevice));
   return g_tw_full;
 }
 

@@ -40,7 +40,7 @@ def _worker(rank, world, port, out_path):
     os.environ["MASTER_PORT"] = str(port)
     import datetime
     dist.init_process_group("gloo", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=60))
+                            timeout=datetime.timedelta(seconds=300))
     try:
         from demucs_cuda_b200 import synth
         import demucs_cuda_b200 as d
