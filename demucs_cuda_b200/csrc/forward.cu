@@ -31,6 +31,9 @@ static void dfree(void *p) {
 void ispec_fused(const float *x, float *out, const float *mean, const float *var, int B,
                  int rows_per_b, int F, int N, int n_fft, int hop, const float *window,
                  int64_t start, int64_t length, float eps);
+bool ispec_stream_ok(int n_fft, int hop, int N, int64_t start, int64_t length);
+void ispec_frames(const float2 *z, float *out, int64_t R, int F, int N, const float *window,
+                  int64_t start, int64_t length);
 void spec_normalised(const float *xc, int B, int C, int64_t L, int n_fft, int hop, int frame0,
                      int nframes, int nbins, const float *window, float *x, float *mean,
                      float *var, float *mag);
@@ -516,11 +519,22 @@ static float *enc_time(DcbModel *m, int idx, const float *x, const Half16 *xh, i
   return z;
 }
 
+// The last frequency decoder's output written straight as the inverse STFT's frame-major
+// spectrum (de-normalised), in place of the NCHW tensor: z [B * rows][frames][bins]
+struct SpecOut {
+  float2 *z = nullptr;
+  int rows = 0;  // complex rows per batch item (sources x audio channels)
+  const float *mean = nullptr, *var = nullptr;
+  float eps = 0.f;
+  bool done = false;  // the decoder wrote z (else it produced y as usual)
+};
+
 // transposed conv of a decoder from the fp16 companion zh of its input: y (fp32, optional)
-// and the fp16 companion of (y + skip_next) for the next decoder (optional)
+// and the fp16 companion of (y + skip_next) for the next decoder (optional), or the
+// spectrum of spec (y, skip_next and yh absent)
 static bool convtr_half(const ConvW &cw, const Half16 &zh, bool axis_h, int S, int crop,
                         int out_len, bool gelu, float *y, const Img &out, const float *skip_next,
-                        Half16 *yh) {
+                        Half16 *yh, const SpecOut *spec = nullptr) {
   Epi e;
   e.mode = EPI_CONVTR;
   e.bias = cw.bias;
@@ -539,6 +553,29 @@ static bool convtr_half(const ConvW &cw, const Half16 &zh, bool axis_h, int S, i
   e.axis_h = axis_h ? 1 : 0;
   e.hskip = skip_next;
   if (yh) epi_half(e, *yh);
+  if (spec) {
+    // the frequency transposed conv run along W over a view of zh with H and W swapped
+    // (lines = time frames, positions = bins), so that a lane's output bins are
+    // contiguous in the frame-major spectrum; one 64-channel block (the K blocks of the
+    // two axes are the same taps in the same order only then)
+    if (!axis_h || y || yh || skip_next || cw.ncb != 1) return false;
+    e.spec_z = spec->z;
+    e.spec_rows = spec->rows;
+    e.spec_frames = zh.W;
+    e.spec_bins = out_len;
+    e.spec_mean = spec->mean;
+    e.spec_var = spec->var;
+    e.spec_eps = spec->eps;
+    e.axis_h = 0;
+    e.Ho = zh.W;
+    e.Wo = zh.H + 1;
+    HalfAct v{zh.p, zh.images, zh.C, zh.W, zh.H, zh.H};
+    v.sW = zh.Wp;
+    v.sH = 1;
+    v.sN = (int64_t)zh.H * zh.Wp;
+    return conv_half(v, 1, 2, 1, 1, 0, 1, 1, 1, zh.W, zh.H + 1, cw.wt, cw.rows, cw.ldt, cw.ncb,
+                     e, 128);
+  }
   const int Ho = axis_h ? zh.H + 1 : 1, Wo = axis_h ? zh.W : zh.W + 1;
   e.Ho = Ho;
   e.Wo = Wo;
@@ -548,21 +585,32 @@ static bool convtr_half(const ConvW &cw, const Half16 &zh, bool axis_h, int S, i
 
 // freq decoder (dc_hdec, layers.c:143-220): input x + skip given as its fp16 companion xs
 // (x, skip fp32 for the fallback path) -> y [B, Cout, S*H, W] (fp32 when want_y) and, when
-// skip_next is given, the companion of y + skip_next for the next decoder
+// skip_next is given, the companion of y + skip_next for the next decoder.  With spec (the
+// last decoder), the output goes to spec's frame-major spectrum when the tensor-core path
+// takes it (spec->done; nullptr returned), else to y as usual.
 static float *dec_freq(DcbModel *m, int idx, const float *x, const float *skip, const Half16 *xs,
                        int B, int H, int W, bool last, bool want_y, const float *skip_next,
-                       Half16 *yh) {
+                       Half16 *yh, SpecOut *spec = nullptr) {
   const DecW &D = m->dec[idx];
   const int C = D.Cin, S = m->cfg.stride, c = m->cfg.context, pad = m->cfg.kernel_size / 4;
   const int out_len = (H - 1) * S + m->cfg.kernel_size - 2 * pad;
   const Img oimg = contiguous(B, D.Cout, out_len, W);
   const bool tma = xs && xs->p && D.rewrite.wt && D.convtr.wt;
-  float *y = want_y || !tma ? dalloc((size_t)B * D.Cout * out_len * W) : nullptr;
+  float *y = (want_y && !(spec && tma)) || !tma ? dalloc((size_t)B * D.Cout * out_len * W)
+                                               : nullptr;
   if (tma) {
     if (yh) *yh = half_alloc(B, D.Cout, out_len, W, false);
     Half16 zh = half_alloc(B, C, H, W, false);
     conv_any(D.rewrite, nullptr, xs, contiguous(B, C, H, W), 1, 1, c, c, 1, 1, H, W, nullptr,
              contiguous(B, C, H, W), 2, &zh, false);
+    if (spec && !skip_next && !yh &&
+        convtr_half(D.convtr, zh, true, S, pad, out_len, !last, nullptr, oimg, nullptr,
+                    nullptr, spec)) {
+      spec->done = true;
+      dfree(zh.p);
+      return nullptr;
+    }
+    if (!y) y = dalloc((size_t)B * D.Cout * out_len * W);
     if (!convtr_half(D.convtr, zh, true, S, pad, out_len, !last, y, oimg, skip_next, yh))
       fail("decoder %d: transposed conv not supported", idx);
     dfree(zh.p);
@@ -915,6 +963,7 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
   auto tma_dec = [&](const DecW &d) {
     return d.rewrite.wt && d.convtr.wt && d.Cin % 8 == 0;
   };
+  SpecOut spec;
   for (int i = 0; i < depth; i++) {
     const bool last = i == depth - 1;
     const bool want_y = last || sg.fn || !tma_dec(m->dec[i + 1]);
@@ -925,8 +974,19 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
     H = fr_len.back();
     fr_len.pop_back();
     Half16 ys;
+    if (last && !sg.fn && m->dec[i].Cout % 2 == 0 && H <= nfft / 2 + 1 &&
+        ispec_stream_ok(nfft, hop, W, (int64_t)nfft / 2 + pad, L)) {
+      // the inverse STFT reads the decoder's output as a frame-major spectrum, which the
+      // transposed conv's epilogue writes directly (de-normalised)
+      spec.rows = m->dec[i].Cout / 2;
+      spec.mean = mean;
+      spec.var = var;
+      spec.eps = 1e-5f;
+      spec.z = (float2 *)dalloc((size_t)2 * B * spec.rows * W * H);
+    }
     float *x2 = dec_freq(m, i, x, skip, &xs_f, B, Hin, W, last, want_y,
-                         last ? nullptr : saved.back(), last ? nullptr : &ys);
+                         last ? nullptr : saved.back(), last ? nullptr : &ys,
+                         spec.z ? &spec : nullptr);
     dfree(x);
     dfree(skip);
     dfree(xs_f.p);
@@ -960,8 +1020,12 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
   const int Ctot = m->dec[depth - 1].Cout;  // S * 2C
   const int64_t R = (int64_t)B * S * (Ctot / S / 2);
   float *xi = dalloc((size_t)R * L);
-  ispec_fused(x, xi, mean, var, B, Ctot / 2, H, W, nfft, hop, m->window,
-              (int64_t)nfft / 2 + pad, L, 1e-5f);
+  if (spec.done)
+    ispec_frames(spec.z, xi, R, H, W, m->window, (int64_t)nfft / 2 + pad, L);
+  else
+    ispec_fused(x, xi, mean, var, B, Ctot / 2, H, W, nfft, hop, m->window,
+                (int64_t)nfft / 2 + pad, L, 1e-5f);
+  dfree(spec.z);
   dfree(x);
   sg.emit("ispec", xi, {B, S, (int)(Ctot / S / 2), L});
   const int keep = T < L ? T : L;

@@ -1448,6 +1448,45 @@ static __device__ __forceinline__ void ch_epi_fast(const ConvH &c, const Epi &e,
     o0 = obase - s0 * O;
   }
   const float *cb = CT != 0 ? e.bias_x : e.bias;
+  if constexpr (CT == 2) {
+    if (e.spec_z) {
+      // the last frequency decoder run along its frequency axis (line = time frame ho,
+      // lane = input bin q): the de-normalised spectrum, frame-major.  Warp half h takes the
+      // channel pairs (re, im) of [h O/2, (h + 1) O/2); phases (0, 1), then (2, 3), give
+      // bins 4 q - crop + (0, 1), (2, 3): one 16-byte store per pair and phase pair, the
+      // lanes' stores filling each other's 32-byte sectors
+      const int Oh = O / 2, ob = half * Oh;
+      const float sd = sqrtf(e.spec_var[n]) + e.spec_eps, mu = e.spec_mean[n];
+      const int64_t rs = (int64_t)e.spec_frames * e.spec_bins;
+      float2 *zr = e.spec_z + (int64_t)n * e.spec_rows * rs + (int64_t)ho * e.spec_bins;
+#pragma unroll 1
+      for (int sp = 0; sp < 2; sp++) {
+        float a0[16], a1[16], b0[16], b1[16];
+        tmem_ld16(trow + (uint32_t)(2 * sp * O + ob), a0);
+        tmem_ld16(trow + (uint32_t)((2 * sp + 1) * O + ob), a1);
+#pragma unroll
+        for (int i = 0; i < 16; i++) {  // (the bias has O * 4 columns: read only Oh of 16)
+          b0[i] = i < Oh ? cb[2 * sp * O + ob + i] : 0.f;
+          b1[i] = i < Oh ? cb[(2 * sp + 1) * O + ob + i] : 0.f;
+        }
+        tmem_wait_ld();
+        const int f = q * e.stride + 2 * sp - e.crop;  // even: both bins in or both out
+        if (rv && f >= 0 && f + 1 < e.out_len) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            if (i < Oh) {
+              const float4 v4 = make_float4(fmaf(a0[i] + b0[i], sd, mu),
+                                            fmaf(a0[i + 1] + b0[i + 1], sd, mu),
+                                            fmaf(a1[i] + b1[i], sd, mu),
+                                            fmaf(a1[i + 1] + b1[i + 1], sd, mu));
+              *(float4 *)(zr + (int64_t)((ob + i) >> 1) * rs + f) = v4;
+            }
+          }
+        }
+      }
+      return;
+    }
+  }
   for (int c0 = 0; c0 < per; c0 += 16) {
     const int col0 = obase + c0;
     if (col0 >= ncol_total) break;
@@ -2116,8 +2155,11 @@ static void launch_conv_tma(const CUtensorMap &tx, const CUtensorMap &tx2, const
 // positions with the 128-byte swizzle of the UMMA operand
 static bool encode_half(CUtensorMap *map, const HalfAct &x, bool w4) {
   if (!get_encoder() || !x.p || ((uintptr_t)x.p & 15) || x.C % 8 || x.Wp < x.W) return false;
-  if (w4 && x.Wp % 4) return false;
+  if (w4 && (x.Wp % 4 || x.sW || x.sH || x.sN)) return false;
   const uint64_t rowb = (uint64_t)x.C * 2;  // bytes per position
+  // position strides along W, H and images (a strided view, else [images][H][Wp])
+  const uint64_t sw = x.sW ? (uint64_t)x.sW : 1, sh = x.sH ? (uint64_t)x.sH : (uint64_t)x.Wp;
+  const uint64_t sn = x.sN ? (uint64_t)x.sN : (uint64_t)x.Wp * x.H;
   cuuint64_t dims[5], strides[4];
   cuuint32_t box[5], es[5] = {1, 1, 1, 1, 1};
   int rank;
@@ -2127,9 +2169,9 @@ static bool encode_half(CUtensorMap *map, const HalfAct &x, bool w4) {
     dims[1] = (cuuint64_t)x.Wp;
     dims[2] = (cuuint64_t)x.H;
     dims[3] = (cuuint64_t)x.images;
-    strides[0] = rowb;
-    strides[1] = rowb * x.Wp;
-    strides[2] = rowb * x.Wp * x.H;
+    strides[0] = rowb * sw;
+    strides[1] = rowb * sh;
+    strides[2] = rowb * sn;
     box[0] = 64;
     box[1] = kBM;
     box[2] = 1;
@@ -2214,6 +2256,15 @@ static int conv_epi_kind(Epi &e, int bn) {
     e.y_al = 1;
   if (tr) {
     if (act > 1 || e.res || O < 16 || (O * e.stride) % 16 != 0) return 0;
+    if (e.spec_z) {
+      // the spectrum epilogue: whole 16-byte bin pairs, and 16 TMEM columns from each
+      // phase's channel half inside the accumulator
+      if (e.axis_h || act != 0 || e.y || e.yh || e.hskip || e.stride != 4 || O % 8 != 0 ||
+          O / 2 > 16 || 3 * O + O / 2 + 16 > bn || e.crop % 2 != 0 || e.spec_bins % 2 != 0 ||
+          !e.bias_x || !al16(e.spec_z))
+        return 0;
+      return 1 + 0 + 4 * 2;
+    }
     if (e.yh && O % 16 != 0) return 0;
     if (e.hskip && (!e.yh || O % 16 != 0)) return 0;  // skip rows are read 16 channels at a time
     if (e.bias && (!e.bias_x || !al16(e.bias_x))) return 0;
@@ -2270,6 +2321,8 @@ bool conv_half(const HalfAct &x, int KH, int KW, int SH, int SW, int PH, int PW,
   c.ntiles = (int)((N + bn - 1) / bn);
   Epi e2 = e;
   if (glu) e2.glu_half = bn / 2;
+  const int ek = g_opt_generic_epi ? 0 : conv_epi_kind(e2, bn);
+  if (ek == 0 && e2.spec_z) return false;  // only the specialised epilogue writes it
   {
     const int64_t M = x.images * Ho * Wo;
     const double n_alg = e.mode == EPI_CONVTR ? (double)e.O * e.stride : (glu ? 2.0 * e.O : e.O);
@@ -2277,11 +2330,11 @@ bool conv_half(const HalfAct &x, int KH, int KW, int SH, int SW, int PH, int PW,
     // minimum bytes: the fp16 input and weights once and the output once at its precision
     // (fp32 when the fp32 tensor is written, else the fp16 copy); the extra fp16
     // channels-last copy and the decoder skip read are the design's traffic, not counted
-    const double out_b = (double)M * n_alg / (glu ? 2 : 1) * (e.y ? 4.0 : (e.yh ? 2.0 : 0.0));
+    const double out_b =
+        (double)M * n_alg / (glu ? 2 : 1) * (e.y || e.spec_z ? 4.0 : (e.yh ? 2.0 : 0.0));
     TraceScope ts(e.mode == EPI_CONVTR ? TR_CONVTR : TR_CONV, 2.0 * M * n_alg * Kt,
                   (double)x.images * x.H * x.W * x.C * 2.0 + n_alg * Kt * 2.0 + out_b, M,
                   (int64_t)n_alg, Kt);
-    const int ek = g_opt_generic_epi ? 0 : conv_epi_kind(e2, bn);
     switch (bn) {
       case 32: launch_conv_h<32>(ta, tb, c, e2, ek); break;
       case 64: launch_conv_h<64>(ta, tb, c, e2, ek); break;

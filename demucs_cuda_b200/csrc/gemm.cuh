@@ -68,6 +68,16 @@ struct Epi {
   uint16_t *yh = nullptr;
   int yhH = 1, yhW = 1, yhC = 0;
   const float *hskip = nullptr;
+  // EPI_CONVTR along W over a view with the frequency axis as W (the last frequency
+  // decoder): instead of y, the de-normalised complex spectrum frame-major,
+  // spec_z[(n * spec_rows + o / 2) * spec_frames + h][w] = (v(o) sd + mean, v(o + 1) sd +
+  // mean) for even o, h the time frame and w the bin, sd = sqrt(spec_var[n]) + spec_eps,
+  // mean = spec_mean[n] (htdemucs.c:242-252) -- the inverse STFT's input, so the decoder
+  // output never goes through the NCHW layout
+  float2 *spec_z = nullptr;
+  int spec_rows = 0, spec_frames = 0, spec_bins = 0;
+  const float *spec_mean = nullptr, *spec_var = nullptr;
+  float spec_eps = 0.f;
   // frequency embedding added to the output (first frequency encoder, htdemucs.c:114-134):
   // value += emb_alpha * emb[h * emb_ld + o]
   const float *emb = nullptr;
@@ -102,6 +112,9 @@ struct HalfAct {
   const uint16_t *p = nullptr;
   int64_t images = 0;
   int C = 0, H = 1, W = 0, Wp = 0;
+  // position strides of a strided view along W, H and images (0: [images][H][Wp]
+  // contiguous); e.g. W and H swapped to run a conv along the stored H axis
+  int64_t sW = 0, sH = 0, sN = 0;
 };
 // conv / transposed conv over a HalfAct: taps (KH, KW), stride SH along H and SW (1 or 4)
 // along W, padding PH/PW, dilation DH/DW; B = weights in the TMA K order (ldt, ncb).

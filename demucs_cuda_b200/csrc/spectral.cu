@@ -566,6 +566,40 @@ static int log2i(int n) {
   return b;
 }
 
+// Whether the streamed inverse STFT (k_istft_stream4096) covers a call: n_fft 4096, hop
+// 1024, and output samples within the signal's hops
+bool ispec_stream_ok(int n_fft, int hop, int N, int64_t start, int64_t length) {
+  return n_fft == kFftN && hop == 1024 && g_stream_istft &&
+         (start + length - 1) / hop <= (int64_t)N + 6;
+}
+
+// Streamed inverse STFT + overlap-add of a frame-major spectrum z [R][N][F] (bins F <=
+// 2049; the decoder's F = 2048 leaves the Nyquist bin zero) -> out [R][length], samples
+// start .. start + length of the signal (ispec_stream_ok must hold)
+void ispec_frames(const float2 *z, float *out, int64_t R, int F, int N, const float *window,
+                  int64_t start, int64_t length) {
+  constexpr int hop = 1024;
+  DCB_REQUIRE(R <= 65535 && F <= kFftN / 2 + 1, "ispec: %lld rows, %d bins", (long long)R, F);
+  // output frames NF = N + 4 (two of padding on each side); hops covering the samples
+  // (the signal ends with hop NF + 2)
+  const int NF = N + 4;
+  const int g_first = (int)(start / hop);
+  const int g_last = (int)((start + length - 1) / hop);
+  const int runs = (g_last - g_first + kStreamHops) / kStreamHops;
+  const size_t sm = (size_t)kFftPadded * sizeof(float2) + 4 * 1024 * sizeof(float);
+  static bool attr = false;
+  if (!attr) {
+    DCB_CUDA(cudaFuncSetAttribute(k_istft_stream4096,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    attr = true;
+  }
+  TraceScope ts(TR_SPECTRAL, 0.0, (double)R * N * F * 8.0 + (double)R * length * 4.0, R, F,
+                length);
+  k_istft_stream4096<<<dim3((unsigned)runs, (unsigned)R), kFftThreads, sm, stream()>>>(
+      z, out, N, F, NF, window, twiddles4096(), start, length, g_first);
+  DCB_LAUNCHED();
+}
+
 // denormalise + inverse STFT + OLA of the decoder output (the engine's _ispec path):
 // x [B][2*rows_per_b][F][N] -> out [B*rows_per_b][length]
 void ispec_fused(const float *x, float *out, const float *mean, const float *var, int B,
@@ -594,28 +628,8 @@ void ispec_fused(const float *x, float *out, const float *mean, const float *var
                                   (int)smem));
     attr = smem;
   }
-  if (n_fft == kFftN && hop == 1024 && g_stream_istft &&
-      (start + length - 1) / hop <= (int64_t)N + 6) {
-    // output frames NF = N + 4 (two of padding on each side); hops covering the samples
-    // (the signal ends with hop NF + 2)
-    const int NF = N + 4;
-    const int g_first = (int)(start / hop);
-    const int g_last = (int)((start + length - 1) / hop);
-    const int runs = (g_last - g_first + kStreamHops) / kStreamHops;
-    const size_t sm = (size_t)kFftPadded * sizeof(float2) + 4 * 1024 * sizeof(float);
-    static bool attr = false;
-    if (!attr) {
-      DCB_CUDA(cudaFuncSetAttribute(k_istft_stream4096,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-      attr = true;
-    }
-    {
-      TraceScope ts(TR_SPECTRAL, 0.0, (double)R * N * F * 8.0 + (double)R * length * 4.0, R,
-                    F, length);
-      k_istft_stream4096<<<dim3((unsigned)runs, (unsigned)R), kFftThreads, sm, stream()>>>(
-          z, out, N, F, NF, window, twiddles4096(), start, length, g_first);
-      DCB_LAUNCHED();
-    }
+  if (ispec_stream_ok(n_fft, hop, N, start, length)) {
+    ispec_frames(z, out, R, F, N, window, start, length);
     DCB_CUDA(cudaFreeAsync(z, stream()));
     return;
   }

@@ -150,9 +150,10 @@ def test_short_specialised_epilogue_matches_generic(short):
 
 
 def test_short_streaming_istft_matches_two_pass(short):
-    """The fused streaming inverse STFT (frames inverted and overlap-added in shared
-    memory) gives the two-pass path's stems (windowed frames through HBM, then the
-    overlap-add with the window-sum division)."""
+    """The last decoder writing the de-normalised spectrum frame-major from its epilogue,
+    then the fused streaming inverse STFT (frames inverted and overlap-added in shared
+    memory), gives the two-pass path's stems (NCHW decoder output, a frame-major transpose,
+    windowed frames through HBM, then the overlap-add with the window-sum division)."""
     import demucs_cuda_b200 as dcb
     torch = short["torch"]
     x = _t(torch, short["mix"])
