@@ -3,27 +3,27 @@
 // [GEMM S = Q K^T -> dk_softmax_to_half -> GEMM O = P V] loop (ops.c:390-443,
 // attn.cu:26-89).
 //
-// CTA = 128 query rows of one head, 352 threads, key blocks of 64:
-//   warps 0-7  softmax: warp w serves TMEM lane quarter w & 3 (query rows 32 (w & 3) ..
-//              +31, one per lane) and column half w >> 2 (32 of the block's 64 keys), so
-//              eight warps share the exponentials; the two warps of a quarter exchange
-//              their half-block maxima through shared memory and an mbarrier.  Online
-//              softmax in fp32 (exp2 domain, running max; the O accumulator stays in TMEM
-//              and is rescaled there only when the maximum grows by more than
-//              2^kLazyLog2), P written as fp16 into shared memory in the UMMA A-operand
-//              layout;
-//   warp 8     TMA producer: Q once, then K blocks into a 4-stage ring (a stage is free
-//              once S of its block has completed);
-//   warp 10    TMA producer: V^T blocks into a 3-stage ring (free once P V of its block
-//              has completed);
-//   warp 9     TMEM owner; lane 0 issues S = Q K^T (M=128, N=64, K=hd) into one of two
-//              TMEM score buffers and O += P V (M=128, N=hd, K=64) from one of two P
-//              buffers.  S(j+2) is issued as soon as the softmax warps have read S(j) out
-//              of TMEM (s_empty), so it runs while they exponentiate block j.
-// TMEM: S0 | S1 | O | row sums (64 + 64 + 64 + 16 columns, 256 allocated); 107 KB of
-// shared memory: two CTAs share an SM.  Head dims up to 64 are zero-extended to a multiple of 16 (the MMA K of
-// S and N of P V) by TMA out-of-bounds fill; keys past Tk read as zero and are masked out
-// of the softmax.
+// CTA = 128 query rows of one head, 320 threads, key blocks of 64:
+//   warps 0-7  softmax: warp w serves TMEM lane quarter q = w & 3 (query rows 32 q .. +31,
+//              one per lane) and the key blocks of parity h = w >> 2: the two warps of a
+//              quarter take alternate blocks, each with its own running maximum, O
+//              accumulator O_h and row sums l_h in TMEM, so a warp has two block times for
+//              each of its blocks (all 64 keys of it per thread) and no per-block exchange.
+//              Online softmax in fp32 (exp2 domain; O_h is rescaled in TMEM only when the
+//              maximum grows by more than 2^kLazyLog2), P written as fp16 into its parity's
+//              shared-memory buffer in the UMMA A-operand layout.  At the end the pair
+//              exchanges maxima once and combines O = (O_0 a_0 + O_1 a_1) / (l_0 a_0 + l_1 a_1);
+//   warp 8     TMA producers: lane 0 Q once, then K blocks into a 4-stage ring (a stage is
+//              free once S of its block has completed); lane 1 V^T blocks into a 3-stage
+//              ring (free once P V of its block has completed);
+//   warp 9     TMEM owner; lane h issues, for the blocks j of parity h, S(j) = Q K(j)^T
+//              (M=128, N=64, K=hd) into score buffer h and O_h += P(j) V(j), l_h += P(j) 1
+//              (M=128, N=hd / 16, K=64).  S(j + 2) is issued as soon as the parity's warps
+//              have read S(j) out of TMEM, so it runs while they exponentiate block j.
+// TMEM: S_0 | S_1 | O_0 | O_1 | l_0 | l_1 (64 + 64 + 2 x 16 ceil(hd / 16) + 2 x 16 columns):
+// 256 for head dims up to 48 (two CTAs share an SM), 512 above; 109 KB of shared memory.
+// Head dims up to 64 are zero-extended to a multiple of 16 (the MMA K of S and N of P V) by
+// TMA out-of-bounds fill; keys past Tk read as zero and are masked out of the softmax.
 //
 // Inputs are fp16 exactly as the reference rounds them (split_heads of the fp32
 // projections): Q [BH][Tq][hd], K [BH][Tk][hd], V^T [BH][hd][Tkp].  The reference rounds
@@ -37,20 +37,21 @@
 
 namespace dcb {
 
-constexpr int kAttnThreads = 352;
-constexpr int kSoftWarps = 8, kKWarp = 8, kMmaWarpA = 9, kVWarp = 10;
+constexpr int kAttnThreads = 320;
+constexpr int kSoftWarps = 8, kLoadWarp = 8, kMmaWarpA = 9;
 constexpr int kQ = 128, kKV = 64, kHD = 64;
 constexpr uint32_t kQBytes = kQ * kHD * 2;      // 16 KB
 constexpr uint32_t kKBytes = kKV * kHD * 2;     // 8 KB
 constexpr uint32_t kVBytes = kHD * kKV * 2;     // 8 KB
-constexpr uint32_t kPBytes = kQ * kKV * 2;      // 16 KB per buffer
+constexpr uint32_t kPBytes = kQ * kKV * 2;      // 16 KB per buffer (one per block parity)
 constexpr int kKStages = 4, kVStages = 3;  // K is released after S, V only after P V
 constexpr uint32_t kOnesBytes = 16 * kKV * 2;  // 16 x 64 fp16 ones: the row-sum operand
-constexpr uint32_t kRedBytes = 2 * 2 * kQ * 4;  // half-block maxima [block parity][half][row]
-// + 512: the 32 mbarriers (256 B), the TMEM slot and the abort flag
+constexpr uint32_t kRedBytes = 2 * kQ * 4;     // final maxima [parity][row]
+// + 512: the mbarriers (<= 256 B), the TMEM slot and the abort flag
 constexpr size_t kAttnSmem = kQBytes + kKStages * kKBytes + kVStages * kVBytes + 2 * kPBytes +
                              kOnesBytes + kRedBytes + 512;
-constexpr int kSumCol = 64;       // TMEM column (after O) of the row sums of P
+// one CTA per SM when the accumulators take 512 TMEM columns (head dims above 48)
+constexpr size_t kAttnSmemWide = 120 * 1024;
 constexpr float kLazyLog2 = 2.0f; // rescale when a block maximum exceeds the running one by 4x
 
 struct AttnArgs {
@@ -97,7 +98,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   uint8_t *sQ = smem;
   uint8_t *sK = sQ + kQBytes;
   uint8_t *sV = sK + kKStages * kKBytes;
-  uint8_t *sP = sV + kVStages * kVBytes;
+  uint8_t *sP = sV + kVStages * kVBytes;  // [parity] P buffers
   uint8_t *sOnes = sP + 2 * kPBytes;
   float *sRed = (float *)(sOnes + kOnesBytes);
   uint64_t *bar = (uint64_t *)((uint8_t *)sRed + kRedBytes);
@@ -106,13 +107,13 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   uint64_t *k_empty = k_full + kKStages;   // [kKStages]
   uint64_t *v_full = k_empty + kKStages;   // [kVStages]
   uint64_t *v_empty = v_full + kVStages;   // [kVStages]
-  uint64_t *s_full = v_empty + kVStages;   // [2] score buffers computed
-  uint64_t *s_empty = s_full + 2;          // [2] score buffers read by the softmax warps
-  uint64_t *p_full = s_empty + 2;          // [2] P buffers written
-  uint64_t *p_empty = p_full + 2;          // [2] PV of a P buffer complete
-  uint64_t *o_full = p_empty + 2;
-  uint64_t *xch = o_full + 1;              // [4 quarters][2] half-block maxima written
-  uint32_t *tslot = (uint32_t *)(xch + 8);
+  uint64_t *s_full = v_empty + kVStages;   // [parity] score buffer computed
+  uint64_t *s_empty = s_full + 2;          // [parity] score buffer read by its 4 warps
+  uint64_t *p_full = s_empty + 2;          // [parity] P buffer written by its 4 warps
+  uint64_t *pv_done = p_full + 2;          // [parity] P V of the parity's latest block done
+  uint64_t *o_full = pv_done + 2;          // every MMA done
+  uint64_t *xch = o_full + 1;              // [quarter] final maxima written
+  uint32_t *tslot = (uint32_t *)(xch + 4);
   uint32_t *s_abort = tslot + 1;
 
   // a fault recorded by an earlier kernel, or a misaligned window: end this grid at once
@@ -130,6 +131,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   const int qt = blockIdx.x, bh = blockIdx.y;
   const int q0 = qt * kQ;
   const int nkv = (a.Tk + kKV - 1) / kKV;
+  // TMEM columns: S_0 | S_1 | O_0 | O_1 | l_0 | l_1
+  const int hd16 = (a.hd + 15) / 16;
+  const uint32_t ow = 16u * (uint32_t)hd16;
+  const uint32_t ncols = 2u * kKV + 2u * ow + 32u <= 256u ? 256u : 512u;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -143,16 +148,16 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kSoftWarps);
-      mbar_init(&p_full[i], kSoftWarps);
-      mbar_init(&p_empty[i], 1);
+      mbar_init(&s_empty[i], kSoftWarps / 2);
+      mbar_init(&p_full[i], kSoftWarps / 2);
+      mbar_init(&pv_done[i], 1);
     }
-    mbar_init(o_full, 1);
-    for (int i = 0; i < 8; i++) mbar_init(&xch[i], 2);
+    mbar_init(o_full, 2);
+    for (int i = 0; i < 4; i++) mbar_init(&xch[i], 2);
     fence_mbar_init();
   }
   if (warp == kMmaWarpA) {
-    tmem_alloc(tslot, 256);
+    tmem_alloc(tslot, ncols);
     tmem_relinquish();
   }
   if (threadIdx.x < kOnesBytes / 16) {
@@ -166,9 +171,11 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t tO = tmem + 2 * kKV;
+  const uint32_t tO = tmem + 2 * kKV;     // O_h at tO + h ow
+  const uint32_t tL = tO + 2 * ow;        // l_h at tL + 16 h
 
-  if (warp == kKWarp) {
+  if (warp == kLoadWarp) {
+    // two independent producer loops on two lanes of this warp
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -177,80 +184,77 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       for (int j = 0; j < nkv; j++) {
         const int st = j % kKStages;
         const uint32_t ph = (uint32_t)(j / kKStages) & 1u;
-        if (!mbar_wait_sleep(&k_empty[st], ph ^ 1u, kFaultAttn)) break;
+        if (!mbar_wait(&k_empty[st], ph ^ 1u, kFaultAttn)) break;
         mbar_expect_tx(&k_full[st], kKBytes);
         tma_load_3d(sK + st * kKBytes, &tmK, &k_full[st], 0, j * kKV, bh);
       }
-    }
-  } else if (warp == kVWarp) {
-    if (lane == 0) {
+    } else if (lane == 1) {
       tma_prefetch_desc(&tmV);
       for (int j = 0; j < nkv; j++) {
         const int st = j % kVStages;
         const uint32_t ph = (uint32_t)(j / kVStages) & 1u;
-        if (!mbar_wait_sleep(&v_empty[st], ph ^ 1u, kFaultAttn)) break;
+        if (!mbar_wait(&v_empty[st], ph ^ 1u, kFaultAttn)) break;
         mbar_expect_tx(&v_full[st], kVBytes);
         tma_load_3d(sV + st * kVBytes, &tmV, &v_full[st], j * kKV, 0, bh);
       }
     }
   } else if (warp == kMmaWarpA) {
-    if (lane == 0) {
-      // the head dim rounded up to the MMA granule: K steps of S, N of P V
-      const int hd16 = (a.hd + 15) / 16;
+    // two issuing lanes, one per block parity h, each on its own chain (S(j + 2) once the
+    // parity's warps have read S(j), P V(j) once they have written P(j)), so neither parity
+    // waits for the other's softmax
+    if (lane < 2) {
+      const int h = lane;
       const uint32_t id_s = idesc_f16_f32(kQ, kKV);
       const uint32_t id_o = idesc_f16_f32(kQ, 16 * hd16);
       const uint32_t id_l = idesc_f16_f32(kQ, 16);
       const uint64_t od = sw128_desc(smem_u32(sOnes));
-      bool ok = mbar_wait_sleep(q_full, 0, kFaultAttn);
+      bool ok = mbar_wait(q_full, 0, kFaultAttn);
       const uint64_t qd = sw128_desc(smem_u32(sQ));
-      // S(j) = Q K(j)^T into score buffer j & 1; K stage released when it completes
+      const uint32_t dS = tmem + (uint32_t)h * kKV;
+      // S(j) = Q K(j)^T into score buffer h; K stage released when it completes
       auto issue_s = [&](int j) -> bool {
         const int st = j % kKStages;
-        if (!mbar_wait_sleep(&k_full[st], (uint32_t)(j / kKStages) & 1u, kFaultAttn))
-          return false;
+        if (!mbar_wait(&k_full[st], (uint32_t)(j / kKStages) & 1u, kFaultAttn)) return false;
         tc_fence_after();
         const uint64_t kd = sw128_desc(smem_u32(sK + st * kKBytes));
-        const uint32_t dS = tmem + (uint32_t)(j & 1) * kKV;
         for (int k = 0; k < hd16; k++) umma_f16(dS, qd + 2u * k, kd + 2u * k, id_s, k > 0);
-        umma_commit(&s_full[j & 1]);
+        umma_commit(&s_full[h]);
         umma_commit(&k_empty[st]);
         return true;
       };
-      for (int j = 0; j < nkv && j < 2 && ok; j++) ok = issue_s(j);
-      for (int j = 0; j < nkv && ok; j++) {
-        // S(j + 2) into buffer j & 1 as soon as the softmax warps have read S(j)
+      if (ok && h < nkv) ok = issue_s(h);
+      uint32_t u = 0;  // this parity's blocks so far
+      for (int j = h; j < nkv && ok; j += 2, u++) {
         if (j + 2 < nkv) {
-          if (!mbar_wait_sleep(&s_empty[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn)) break;
+          if (!mbar_wait(&s_empty[h], u & 1u, kFaultAttn)) break;
           tc_fence_after();
           if (!(ok = issue_s(j + 2))) break;
         }
-        // O lives in TMEM across all key blocks
         const int sv = j % kVStages;
-        if (!mbar_wait_sleep(&p_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn)) break;
-        if (!mbar_wait_sleep(&v_full[sv], (uint32_t)(j / kVStages) & 1u, kFaultAttn)) break;
+        if (!mbar_wait(&p_full[h], u & 1u, kFaultAttn) ||
+            !mbar_wait(&v_full[sv], (uint32_t)(j / kVStages) & 1u, kFaultAttn))
+          break;
         tc_fence_after();
-        const uint64_t pd = sw128_desc(smem_u32(sP + (j & 1) * kPBytes));
+        const uint64_t pd = sw128_desc(smem_u32(sP + h * kPBytes));
         const uint64_t vd = sw128_desc(smem_u32(sV + sv * kVBytes));
-        // O += P(j) V(j); the row sums of the fp16 P accumulate in column kSumCol
+        // O_h += P(j) V(j); the row sums of the fp16 P accumulate in l_h
 #pragma unroll
         for (int k = 0; k < kKV / 16; k++) {
-          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
-          umma_f16(tO, pd + 2u * k, vd + 2u * k, id_o, acc);
-          umma_f16(tO + kSumCol, pd + 2u * k, od + 2u * k, id_l, acc);
+          const uint32_t acc = (u > 0 || k > 0) ? 1u : 0u;
+          umma_f16(tO + (uint32_t)h * ow, pd + 2u * k, vd + 2u * k, id_o, acc);
+          umma_f16(tL + 16u * (uint32_t)h, pd + 2u * k, od + 2u * k, id_l, acc);
         }
-        umma_commit(&p_empty[j & 1]);
+        umma_commit(&pv_done[h]);
         umma_commit(&v_empty[sv]);
       }
-      umma_commit(o_full);
+      umma_commit(o_full);  // (two arrivals: every MMA of both lanes)
     }
   } else {
     // softmax warps: warp w serves query rows 32 q .. 32 q + 31 (q = w & 3, the TMEM lane
-    // quarter it may access), one per lane, and columns 32 h .. 32 h + 31 (h = w >> 2) of
-    // each 64-key block; exp2 domain (scores scaled by scale * log2 e).  The running maximum
-    // m is only raised, and O (in TMEM) rescaled, when a block's maximum exceeds it by more
-    // than kLazyLog2: probabilities stay <= 4 and most blocks need no rescale.  The block
-    // maximum is the larger of the two warps' half-block maxima (exchanged through shared
-    // memory under an mbarrier of the warp pair), so both warps keep the same m.
+    // quarter it may access), one per lane, and the key blocks j with j & 1 = h = w >> 2,
+    // all 64 keys of each; exp2 domain (scores scaled by scale * log2 e).  The running
+    // maximum m is only raised, and O_h (in TMEM) rescaled, when a block's maximum exceeds
+    // it by more than kLazyLog2: probabilities stay <= 4 and most blocks need no rescale.
     // P = 2^(s - m) is evaluated two at a time in fp16 (packed fp32 FMA for the exponent,
     // ex2.approx.f16x2 of its fp16 rounding: at most 2^-11 * 2 error in the exponent of the
     // largest probabilities), the operand precision P V uses anyway; the row sums come from
@@ -261,125 +265,123 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const int r = q * 32 + lane;
     const uint32_t lrow = (uint32_t)(q * 32) << 16;
     const float sl2 = a.scale * 1.4426950408889634f;
+    const uint32_t tOh = tO + (uint32_t)h * ow, tLh = tL + 16u * (uint32_t)h;
+    const uint32_t prow = smem_u32(sP + h * kPBytes);
     float m_run = -INFINITY;
     bool ok = true;
-    for (int j = 0; j < nkv && ok; j++) {
-      if (!warp_all(mbar_wait_sleep(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, kFaultAttn))) {
+    uint32_t u = 0;  // this warp's blocks so far
+    for (int j = h; j < nkv && ok; j += 2, u++) {
+      if (!warp_all(mbar_wait(&s_full[h], u & 1u, kFaultAttn))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float v[32];
-      const uint32_t tS = tmem + (uint32_t)(j & 1) * kKV + (uint32_t)h * 32 + lrow;
-      tmem_ld16(tS, *(float(*)[16])v);
-      tmem_ld16(tS + 16, *(float(*)[16])(v + 16));
+      float v[64];
+      const uint32_t tS = tmem + (uint32_t)h * kKV + lrow;
+#pragma unroll
+      for (int c = 0; c < 4; c++) tmem_ld16(tS + 16u * c, *(float(*)[16])(v + 16 * c));
       tmem_wait_ld();
-      // score buffer j & 1 may take S(j + 2) once all eight warps have read it
+      // score buffer h may take S(j + 2) once the parity's four warps have read it
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[j & 1]);
-      const int kbase = j * kKV + h * 32;
-      if (kbase + 32 > a.Tk) {
+      if (lane == 0) mbar_arrive(&s_empty[h]);
+      const int kbase = j * kKV;
+      if (kbase + kKV > a.Tk) {
 #pragma unroll
-        for (int i = 0; i < 32; i++)
+        for (int i = 0; i < 64; i++)
           if (kbase + i >= a.Tk) v[i] = -INFINITY;
       }
-      // half-block maximum by three-input max, four independent chains
-      float m4[4];
+      // block maximum by three-input max, eight independent chains
+      float m8[8];
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
+      for (int c = 0; c < 8; c++) {
         const float *vc = v + 8 * c;
-        m4[c] = fmaxf(max3(max3(vc[0], vc[1], vc[2]), vc[3], vc[4]), max3(vc[5], vc[6], vc[7]));
+        m8[c] = fmaxf(max3(max3(vc[0], vc[1], vc[2]), vc[3], vc[4]), max3(vc[5], vc[6], vc[7]));
       }
-      const float mh = fmaxf(max3(m4[0], m4[1], m4[2]), m4[3]);
-      // exchange with the other warp of this quarter through shared memory; the pair's
-      // mbarrier (two arrivals, alternating buffers: block j + 2 reuses this one) orders the
-      // writes before the reads, and its wait is bounded like every other
-      float *rb = sRed + (j & 1) * 2 * kQ;
-      rb[h * kQ + r] = mh;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&xch[q * 2 + (j & 1)]);
-      if (!warp_all(mbar_wait(&xch[q * 2 + (j & 1)], (uint32_t)(j >> 1) & 1u, kFaultAttn))) {
-        ok = false;
-        break;
-      }
-      const float ms = fmaxf(mh, rb[(1 - h) * kQ + r]) * sl2;
+      const float ms =
+          fmaxf(max3(max3(m8[0], m8[1], m8[2]), m8[3], m8[4]), max3(m8[5], m8[6], m8[7])) * sl2;
       // raise this row's maximum when its block maximum exceeds it by more than kLazyLog2;
-      // the warp rescales when any of its rows does (rows that keep their maximum scale by 1)
+      // the warp rescales O_h when any of its rows does (rows that keep their maximum scale
+      // by 1)
       const bool raise = ms > m_run + kLazyLog2;
-      if (__any_sync(0xffffffffu, raise)) {
-        if (j > 0) {
-          // rescale this warp's half of the accumulated O rows (and, for h = 0, the running
-          // sums) to the new maxima once PV(j-1) has completed
-          if (!warp_all(mbar_wait(&p_empty[(j - 1) & 1], (uint32_t)((j - 1) >> 1) & 1u,
-                                  kFaultAttn))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const float alpha = raise ? exp2f(m_run - ms) : 1.0f;
-#pragma unroll
-          for (int c = 0; c < 48; c += 16) {
-            // h = 0: O columns 0..31 and the sums; h = 1: O columns 32..63
-            if (c == 32 && h == 1) break;
-            const uint32_t col = c < 32 ? (uint32_t)(h * 32 + c) : (uint32_t)kSumCol;
-            float ov[16];
-            tmem_ld16(tO + lrow + col, ov);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; i++) ov[i] *= alpha;
-            tmem_st16(tO + lrow + col, ov);
-          }
-          tmem_wait_st();
-        }
-        if (raise) m_run = ms;
-      }
-      // P buffer j & 1 is free once PV(j-2) has completed
-      if (j >= 2 && !warp_all(mbar_wait(&p_empty[j & 1], (uint32_t)((j - 2) >> 1) & 1u,
-                                        kFaultAttn))) {
-        ok = false;
-        break;
-      }
-      uint32_t w[16];
+      const bool any_raise = __any_sync(0xffffffffu, raise);
+      const float alpha = raise && u > 0 ? exp2f(m_run - ms) : 1.0f;
+      if (raise) m_run = ms;
+      // P = 2^(s sl2 - m) into registers (packed fp16 pairs): the exponentials run while P V
+      // of this warp's previous block may still be in flight
+      uint32_t w[32];
       const float nm = -m_run;
 #pragma unroll
-      for (int i = 0; i < 32; i += 2) {
+      for (int i = 0; i < 32; i++) {
         float x0, x1;
-        fma2(x0, x1, v[i], v[i + 1], sl2, nm);
-        w[i >> 1] = ex2_h2(pack_h2(x0, x1));
+        fma2(x0, x1, v[2 * i], v[2 * i + 1], sl2, nm);
+        w[i] = ex2_h2(pack_h2(x0, x1));
       }
-      // this half's four 16-byte chunks (8 keys each) of row r, SW128 A-operand layout
-      const uint32_t prow = smem_u32(sP + (j & 1) * kPBytes);
+      // P buffer h and O_h are free once that P V has completed
+      if (u > 0 && !warp_all(mbar_wait(&pv_done[h], (u - 1) & 1u, kFaultAttn))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (any_raise && u > 0) {
+        // O_h columns, then the row sums l_h (column tLh), 4 columns at a time
+#pragma unroll 1
+        for (uint32_t c = 0; c < ow + 4u; c += 4u) {
+          const uint32_t col = c < ow ? tOh + c : tLh;
+          float ov[4];
+          tmem_ld4(col + lrow, ov);
+          tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 4; c++)
-        st_shared_v4(prow + sw128_off(r, 4 * h + c), w[4 * c], w[4 * c + 1], w[4 * c + 2],
+          for (int i = 0; i < 4; i++) ov[i] *= alpha;
+          tmem_st4(col + lrow, ov);
+        }
+        tmem_wait_st();
+      }
+      // row r's eight 16-byte chunks (8 keys each), SW128 A-operand layout
+#pragma unroll
+      for (int c = 0; c < 8; c++)
+        st_shared_v4(prow + sw128_off(r, c), w[4 * c], w[4 * c + 1], w[4 * c + 2],
                      w[4 * c + 3]);
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[j & 1]);
+      if (lane == 0) mbar_arrive(&p_full[h]);
     }
-    // normalise and store this warp's half of the finished O row
-    if (warp_all(ok && mbar_wait(o_full, 0, kFaultAttn))) {
+    // combine the two parities: exchange the row maxima with the quarter's other warp, then
+    // O = (O_0 a_0 + O_1 a_1) / (l_0 a_0 + l_1 a_1) with a_h = 2^(m_h - max(m_0, m_1)); a
+    // parity with no blocks (nkv = 1) contributes nothing
+    sRed[h * kQ + r] = m_run;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&xch[q]);
+    const bool fin = warp_all(ok && mbar_wait(&xch[q], 0, kFaultAttn) &&
+                              mbar_wait(o_full, 0, kFaultAttn));
+    if (fin) {
       tc_fence_after();
-      const int t = q0 + r;
-      float lsum[16];
-      tmem_ld16(tO + lrow + kSumCol, lsum);
+      const float m_oth = sRed[(1 - h) * kQ + r];
+      const bool has0 = nkv >= 1, has1 = nkv >= 2;
+      const float m0 = h == 0 ? m_run : m_oth, m1 = h == 0 ? m_oth : m_run;
+      const float mm = has1 ? fmaxf(m0, m1) : m0;
+      const float a0 = has0 ? exp2f(m0 - mm) : 0.f, a1 = has1 ? exp2f(m1 - mm) : 0.f;
+      const float l0 = tmem_ld1(tL + lrow), l1 = tmem_ld1(tL + 16u + lrow);
       tmem_wait_ld();
-      const float inv = 1.0f / lsum[0];
+      const float inv = 1.0f / (l0 * a0 + (has1 ? l1 * a1 : 0.f));
+      const int t = q0 + r;
       const int b = bh / a.H, hh = bh - b * a.H;
       const int64_t D = (int64_t)a.H * a.hd;
       const int64_t off = ((int64_t)b * a.Tq + t) * D + (int64_t)hh * a.hd;
+      // this warp's half of the columns: h = 0 takes 0..31, h = 1 32..63 (those < hd)
 #pragma unroll
       for (int c = h * 32; c < h * 32 + 32; c += 16) {
-        float ov[16];
-        tmem_ld16(tO + lrow + c, ov);
+        if (c >= a.hd) break;
+        float o0[16], o1[16];
+        tmem_ld16(tO + (uint32_t)c + lrow, o0);
+        tmem_ld16(tO + ow + (uint32_t)c + lrow, o1);
         tmem_wait_ld();
         if (t < a.Tq) {
 #pragma unroll
           for (int i = 0; i < 16; i++) {
             if (c + i < a.hd) {
-              const float val = ov[i] * inv;
+              const float val = (o0[i] * a0 + (has1 ? o1[i] * a1 : 0.f)) * inv;
               if (a.o16) a.o16[off + c + i] = f2h_bits(val);
               if (a.o32) a.o32[off + c + i] = val;
             }
@@ -392,7 +394,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   __syncthreads();
   if (warp == kMmaWarpA) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, ncols);
   }
 }
 
@@ -487,11 +489,14 @@ void flash_attention(const uint16_t *q, const uint16_t *k, const uint16_t *vt, i
               map3(&mk, k, hd, Tk, (uint64_t)B * H, hd, (uint64_t)Tk * hd, 64, kKV) &&
               map3(&mv, vt, Tk, hd, (uint64_t)B * H, Tkp, (uint64_t)hd * Tkp, 64, 64);
     if (ok) {
-      const size_t smem = kAttnSmem;
+      // head dims above 48 take 512 TMEM columns: shared memory then holds one CTA per SM
+      const int hd16 = (hd + 15) / 16;
+      const size_t smem = 2 * kKV + 32 * hd16 + 32 <= 256 ? kAttnSmem : kAttnSmemWide;
       static bool attr = false;
       if (!attr) {
         DCB_CUDA(cudaFuncSetAttribute(k_flash_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)smem));
+                                      (int)(kAttnSmem > kAttnSmemWide ? kAttnSmem
+                                                                      : kAttnSmemWide)));
         attr = true;
       }
       DCB_REQUIRE(B * H <= 65535, "attention: too many heads");

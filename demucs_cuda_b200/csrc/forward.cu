@@ -33,7 +33,7 @@ void ispec_fused(const float *x, float *out, const float *mean, const float *var
                  int64_t start, int64_t length, float eps);
 bool ispec_stream_ok(int n_fft, int hop, int N, int64_t start, int64_t length);
 void ispec_frames(const float2 *z, float *out, int64_t R, int F, int N, const float *window,
-                  int64_t start, int64_t length);
+                  int64_t start, int64_t length, const StreamCombine &cb);
 void spec_normalised(const float *xc, int B, int C, int64_t L, int n_fft, int hop, int frame0,
                      int nframes, int nbins, const float *window, float *x, float *mean,
                      float *var, float *mag);
@@ -246,10 +246,13 @@ static void epi_half(Epi &e, const Half16 &h) {
 
 // conv through the fp16 companion when the TMA kernel covers it, else the gather kernel on
 // the fp32 tensor (then the companion, if wanted, is converted from the fp32 output)
-static void conv_any(const ConvW &cw, const float *x, const Half16 *xh, const Img &in, int SH,
+// Returns whether the channels-last tensor-core conv ran (only it sums row_stats: the
+// per-image output sums of a rows view, see Epi::row_stats; the caller falls back otherwise)
+static bool conv_any(const ConvW &cw, const float *x, const Half16 *xh, const Img &in, int SH,
                      int SW, int PH, int PW, int DH, int DW, int Ho, int Wo, float *y,
                      const Img &out, int act, Half16 *yh, bool rows_view,
-                     const float *emb = nullptr, float emb_alpha = 0.f, int emb_ld = 0) {
+                     const float *emb = nullptr, float emb_alpha = 0.f, int emb_ld = 0,
+                     double *row_stats = nullptr) {
   Epi e;
   e.mode = EPI_CONV;
   e.bias = cw.bias;
@@ -266,18 +269,29 @@ static void conv_any(const ConvW &cw, const float *x, const Half16 *xh, const Im
   e.emb = emb;
   e.emb_alpha = emb_alpha;
   e.emb_ld = emb_ld;
+  e.row_stats = rows_view ? row_stats : nullptr;
   if (yh && yh->p) epi_half(e, *yh);
   if (xh && xh->p && xh->im2col && cw.wi) {
     // the input is already im2col'd: a 1x1 conv with K = 8 taps x 8 channels
     if (conv_half(xh->act(), 1, 1, 1, 1, 0, 0, 1, 1, Ho, Wo, cw.wi, cw.rows, 64, 1, e, 0))
-      return;
+      return true;
   } else if (xh && xh->p && cw.wt) {
     const HalfAct a = rows_view ? xh->rows() : xh->act();
     if (conv_half(a, cw.KH, cw.KW, SH, SW, PH, PW, DH, DW, Ho, Wo, cw.wt, cw.rows, cw.ldt,
                   cw.ncb, e, act >= 2 ? cw.glu_bn : 0))
-      return;
+      return true;
+    if (e.row_stats) {
+      // an epilogue without the row sums: the conv alone (the caller forms the statistics)
+      e.row_stats = nullptr;
+      if (conv_half(a, cw.KH, cw.KW, SH, SW, PH, PW, DH, DW, Ho, Wo, cw.wt, cw.rows, cw.ldt,
+                    cw.ncb, e, act >= 2 ? cw.glu_bn : 0))
+        return false;
+    }
   }
-  DCB_REQUIRE(x != nullptr && y != nullptr, "conv: the gather kernel needs fp32 tensors");
+  if (x == nullptr || y == nullptr) {
+    fail("conv: the gather kernel needs fp32 tensors");
+    return false;
+  }
   conv(cw, x, nullptr, in, SH, SW, PH, PW, DH, DW, Ho, Wo, y, out, act);
   if (emb) {
     const int64_t n = (int64_t)out.N1 * e.O * Ho * Wo;
@@ -293,6 +307,7 @@ static void conv_any(const ConvW &cw, const float *x, const Half16 *xh, const Im
         rows_view ? (int64_t)yh->H * yh->W : out.sC, yh->W, yh->C);
     DCB_LAUNCHED();
   }
+  return false;
 }
 
 // ------------------------------------------------------------------ layers
@@ -347,10 +362,22 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
     const int dil = 1 << d;
     const int hid = dw.c0.O, C2 = dw.c3.O;
     DCB_REQUIRE(dw.zc != nullptr, "dconv: the 1x1 conv of layer %d is not 1x1", d);
-    // conv k3, dilation 2^d, padding 2^d -> h [B, hid, Fr, T]
+    // conv k3, dilation 2^d, padding 2^d -> h [B, hid, Fr, T]; its epilogue also sums each
+    // row's values and squares (the first GroupNorm's statistics) into hstat.  Row
+    // accumulators (zeroed): hstat [rows][2], the Gram sums acc [rows][npair + hid] and a
+    // block counter per row
+    const int npair = hid * (hid + 1) / 2;
+    const size_t nacc = (size_t)rows * (2 + npair + hid);
+    double *hstat = (double *)dalloc(nacc * 2 + rows);
+    double *gacc = hstat + 2 * (size_t)rows;
+    unsigned *gcnt = (unsigned *)(hstat + nacc);
+    DCB_CUDA(cudaMemsetAsync(hstat, 0, nacc * sizeof(double) + rows * sizeof(unsigned),
+                             stream()));
     float *h = dalloc((size_t)B * hid * Fr * T);
     const Img hv = freq_rows(B, hid, Fr, T);
-    conv_any(dw.c0, y, yh, v, 1, 1, 0, dil, 1, dil, 1, T, h, hv, 0, nullptr, true);
+    const bool hsums =
+        conv_any(dw.c0, y, yh, v, 1, 1, 0, dil, 1, dil, 1, T, h, hv, 0, nullptr, true, nullptr,
+                 0.f, 0, hstat);
     RowView rh{h, Fr, (int64_t)hid * Fr * T, T, (int64_t)Fr * T, hid, T};
     // hidden widths >= 24: the hidden rows as fp16 channels-last (channels padded to 8),
     // the A operand of a tensor-core 1x1 conv (narrower ones run on CUDA cores, where the
@@ -358,7 +385,34 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
     const int hidp = (hid + 7) / 8 * 8;
     Half16 h16 =
         hid >= 24 && dw.c3g.wt && yh && yh->p ? half_alloc(B, hidp, Fr, T, false) : Half16{};
-    if (fused) {
+    float *hg = nullptr;  // the GELU outputs (the new kernel does not work in place)
+    if (hsums) {
+      // GroupNorm(1) + GELU, the fp16 copy and the z statistics, by chunks of the rows and
+      // groups of Gram entries across CTAs (the last CTA of a row finishes its z statistics)
+      int chunk = 12288 / hid;
+      chunk = chunk > 1024 ? 1024 : chunk / 32 * 32;
+      if (chunk > T) chunk = T;
+      const int ntot = npair + hid, groups = (ntot + kDgThreads - 1) / kDgThreads;
+      const int egroup = (ntot + groups - 1) / groups;
+      const size_t sm = (size_t)hid * (chunk | 1) * sizeof(float);
+      static size_t attr = 0;
+      if (sm > 40 * 1024 && sm > attr) {
+        DCB_CUDA(cudaFuncSetAttribute(k_dconv_gn_gram,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        attr = sm;
+      }
+      TraceScope ts(TR_DCONV, 0.0,
+                    (double)rows * T * ((double)hid * 8.0 + (h16.p ? hidp * 2.0 : 0.0)),
+                    rows, hid, T);
+      hg = dalloc((size_t)B * hid * Fr * T);
+      const dim3 grid((unsigned)((T + chunk - 1) / chunk), rows, (unsigned)groups);
+      k_dconv_gn_gram<<<grid, kDgThreads, sm, stream()>>>(rh, hg, dw.gn1.w, dw.gn1.b, 1e-5f,
+                                                           hstat, gacc, gcnt, chunk, egroup,
+                                                           dw.zc, C2, stat, stat + rows, h16.p,
+                                                           hidp);
+      DCB_LAUNCHED();
+      std::swap(h, hg);  // h: the GELU outputs from here on
+    } else if (fused) {
       // GroupNorm(1) + GELU in place with the z statistics, one CTA per row
       const size_t sm = (size_t)hid * T * sizeof(float);
       static size_t attr = 0;
@@ -392,7 +446,6 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
         DCB_LAUNCHED();
       }
       // z statistics from the Gram matrix of fp16(h), accumulated over chunks of each row
-      const int npair = hid * (hid + 1) / 2;
       const int chunk = kGramChunk * 6 / hid >= kGramChunk ? kGramChunk : 12288 / hid;
       double *acc = (double *)dalloc((size_t)rows * (npair + hid) * 2);
       DCB_CUDA(cudaMemsetAsync(acc, 0, (size_t)rows * (npair + hid) * sizeof(double), stream()));
@@ -452,6 +505,8 @@ static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int
       }
     }
     dfree(h);
+    dfree(hg);
+    dfree(hstat);
   }
   dfree(stat);
 }
@@ -1019,23 +1074,39 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
   const int S = c.n_sources;
   const int Ctot = m->dec[depth - 1].Cout;  // S * 2C
   const int64_t R = (int64_t)B * S * (Ctot / S / 2);
-  float *xi = dalloc((size_t)R * L);
-  if (spec.done)
-    ispec_frames(spec.z, xi, R, H, W, m->window, (int64_t)nfft / 2 + pad, L);
-  else
-    ispec_fused(x, xi, mean, var, B, Ctot / 2, H, W, nfft, hop, m->window,
-                (int64_t)nfft / 2 + pad, L, 1e-5f);
-  dfree(spec.z);
-  dfree(x);
-  sg.emit("ispec", xi, {B, S, (int)(Ctot / S / 2), L});
   const int keep = T < L ? T : L;
-  {
-    const int64_t per = (int64_t)m->tdec[depth - 1].Cout * Lt;
+  const int64_t per = (int64_t)m->tdec[depth - 1].Cout * Lt;
+  float *xi = nullptr;
+  if (spec.done && !sg.fn) {
+    // the output stage (time branch + spectral branch, de-normalised) written by the
+    // streamed inverse STFT itself
+    StreamCombine cb;
+    cb.y = out;
+    cb.xt = xt;
+    cb.mean = meant;
+    cb.var = vart;
+    cb.rows = (int)(per / Lt);
+    cb.Lt = Lt;
+    cb.off = (L - Lt) / 2;
+    cb.keep = keep;
+    cb.eps = 1e-5f;
+    ispec_frames(spec.z, nullptr, R, H, W, m->window, (int64_t)nfft / 2 + pad, L, cb);
+  } else {
+    xi = dalloc((size_t)R * L);
+    if (spec.done)
+      ispec_frames(spec.z, xi, R, H, W, m->window, (int64_t)nfft / 2 + pad, L,
+                   StreamCombine{});
+    else
+      ispec_fused(x, xi, mean, var, B, Ctot / 2, H, W, nfft, hop, m->window,
+                  (int64_t)nfft / 2 + pad, L, 1e-5f);
+    sg.emit("ispec", xi, {B, S, (int)(Ctot / S / 2), L});
     const int64_t n = (int64_t)B * (per / Lt) * keep;
     k_final_combine<<<grid_for(n, 256), 256, 0, stream()>>>(xt, xi, out, meant, vart, B, per, Lt,
                                                            L, keep, 1e-5f);
     DCB_LAUNCHED();
   }
+  dfree(spec.z);
+  dfree(x);
   sg.emit("stems", out, {B, S, C, keep});
   dfree(xi);
   dfree(xt);

@@ -553,6 +553,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!GATHER) tma_prefetch_desc(&tmA);
       const uint32_t bytes = Cfg::kBTileBytes + (GATHER ? 0u : kATileBytes);
       uint32_t it = 0;
+      int st = 0;        // ring stage of K block `it` and its phase parity (kept
+      uint32_t ph = 0;   // incrementally: no division in the issue loop)
       bool ok = true;
       for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
         int bz, nt;
@@ -560,9 +562,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         tile_coords(s, tile, bz, m0, nt);
         const int cA = s.a_shared ? 0 : bz, cB = s.b_shared ? 0 : bz;
         for (int kb = 0; kb < s.nkb; kb++, it++) {
-          const int st = (int)(it % (uint32_t)stages);
-          const uint32_t ph = (it / (uint32_t)stages) & 1u;
-          if (!mbar_wait_sleep(&empty[st], ph ^ 1u, kFaultEmpty)) {
+          if (!mbar_wait(&empty[st], ph ^ 1u, kFaultEmpty)) {
             ok = false;
             break;
           }
@@ -570,6 +570,10 @@ __global__ void __launch_bounds__(kThreads, 2)
           tma_load_3d(sB + st * Cfg::kBTileBytes, &tmB, &full[st], kb * kBK, nt * BN, cB);
           if (!GATHER)
             tma_load_3d(sA + st * kATileBytes, &tmA, &full[st], kb * kBK, (int)m0, cA);
+          if (++st == stages) {
+            st = 0;
+            ph ^= 1u;
+          }
         }
       }
       if (!ok && !GATHER) {
@@ -585,17 +589,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       const uint32_t idesc = idesc_f16_f32(kBM, BN);
       uint32_t it = 0, local = 0;
+      int st = 0;
+      uint32_t ph = 0;
       bool ok = true;
       for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x, local++) {
         const uint32_t buf = local % (uint32_t)Cfg::kBufs;
         const uint32_t use = local / (uint32_t)Cfg::kBufs;
-        if (!mbar_wait_sleep(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * (uint32_t)Cfg::kAccCols;
         for (int kb = 0; kb < s.nkb; kb++, it++) {
-          const int st = (int)(it % (uint32_t)stages);
-          const uint32_t ph = (it / (uint32_t)stages) & 1u;
-          if (!mbar_wait_sleep(&full[st], ph, kFaultFull)) {
+          if (!mbar_wait(&full[st], ph, kFaultFull)) {
             ok = false;
             break;
           }
@@ -612,6 +616,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             // test hook (option "test_withhold_arrive"): stage 0 is never released
           } else {
             umma_commit(&empty[st]);
+          }
+          if (++st == stages) {
+            st = 0;
+            ph ^= 1u;
           }
         }
         if (ok) umma_commit(&acc_full[buf]);
@@ -646,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int kb = 0; kb < s.nkb; kb++, it++) {
         const int st = (int)(it % (uint32_t)stages);
         const uint32_t ph = (it / (uint32_t)stages) & 1u;
-        if (!mbar_wait_sleep(&empty[st], ph ^ 1u, kFaultEmpty)) {
+        if (!mbar_wait(&empty[st], ph ^ 1u, kFaultEmpty)) {
           ok = false;
           break;
         }
@@ -693,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       tile_coords(s, tile, bz, m0, nt);
       const uint32_t buf = local % (uint32_t)Cfg::kBufs;
       const uint32_t use = local / (uint32_t)Cfg::kBufs;
-      if (!warp_all(mbar_wait_sleep(&acc_full[buf], use & 1u, kFaultDone))) break;
+      if (!warp_all(mbar_wait(&acc_full[buf], use & 1u, kFaultDone))) break;
       tc_fence_after();
       const int64_t left = (int64_t)s.M - m0;
       epilogue_tile<BN, Cfg::kEpiWarps, 32, EK>(s, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp,
@@ -1118,6 +1126,10 @@ struct ConvH {
   int64_t lines;  // output lines (images * Ho)
   int tpl;        // tiles of 128 positions per line
   int N, nkb, ntiles, stages;
+  int kst_last;   // MMA K steps (16 channels each) of the last 64-channel block: the rest
+                  // of that block is the tensor's zero fill, and its products are skipped
+  int blocked;    // 1: each CTA takes one contiguous range of tiles (row statistics over
+                  // few rows: a CTA's tiles then mostly share their row), else cyclically
 };
 
 constexpr int kChEpiWarps = 8;  // warp & 3: TMEM lane quarter, warp >> 2: column half
@@ -1159,10 +1171,25 @@ static __device__ __forceinline__ void ch_tile(const ConvH &c, int64_t tile, int
 // transpose buffer to the fp32 NCHW output, 4 consecutive positions per 16-byte store.
 // Transposed-conv columns are (phase s, channel o), channels fastest; (s, o) of the
 // chunk start advance incrementally (no divisions in the loop).
+// e.row_stats: add a warp's share of an image's output sum and sum of squares (the
+// GroupNorm(1) statistics of a DConv hidden row, Ho = 1: image = row), fp64 atomics
+static __device__ __forceinline__ void row_stats_add(const Epi &e, int64_t n, int lane,
+                                                     double s, double q) {
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    q += __shfl_xor_sync(0xffffffffu, q, o);
+  }
+  if (lane == 0 && q > 0.0) {
+    atomicAdd(&e.row_stats[2 * n], s);
+    atomicAdd(&e.row_stats[2 * n + 1], q);
+  }
+}
+
 template <int BN>
 static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e, uint32_t tacc,
                                                    int warp, int lane, int64_t line, int wo0,
-                                                   int nt, float *wst) {
+                                                   int nt, float *wst, double &rsum,
+                                                   double &rsq) {
   const int quarter = warp & 3, half = warp >> 2;
   const uint32_t trow = tacc + ((uint32_t)(quarter * 32) << 16);
   const int ln = (int)line;
@@ -1272,6 +1299,20 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
       const float ex = okc ? e.emb_alpha * e.emb[(int64_t)ho * e.emb_ld + oxl] : 0.f;
 #pragma unroll
       for (int i = 0; i < 16; i++) val[i] += __shfl_sync(0xffffffffu, ex, i);
+    }
+    if (e.row_stats && rv) {
+      // (e.row_stats: this lane's sum and sum of squares of the row's outputs; the chunk's
+      // 16 in fp32, the running totals in fp64)
+      float s16 = 0.f, q16 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        if (col0 + i < ncol_total) {
+          s16 += val[i];
+          q16 = fmaf(val[i], val[i], q16);
+        }
+      }
+      rsum += (double)s16;
+      rsq += (double)q16;
     }
     // ---- (1) fp16 channels-last copy: value + skip, or res + scale[o] * value
     float mul[16];
@@ -1415,7 +1456,8 @@ static __device__ __forceinline__ void ch_epilogue(const ConvH &c, const Epi &e,
 template <int BN, int ACT, int CT>
 static __device__ __forceinline__ void ch_epi_fast(const ConvH &c, const Epi &e, uint32_t tacc,
                                                    int warp, int lane, int64_t line, int wo0,
-                                                   int nt, float *wst) {
+                                                   int nt, float *wst, double &rsum,
+                                                   double &rsq) {
   constexpr bool GLU = ACT >= 2;
   const int quarter = warp & 3, half = warp >> 2;
   const uint32_t trow = tacc + ((uint32_t)(quarter * 32) << 16);
@@ -1571,6 +1613,18 @@ static __device__ __forceinline__ void ch_epi_fast(const ConvH &c, const Epi &e,
         for (int i = 0; i < 16; i++) v[i] = fmaf(e.emb_alpha, em[i], v[i]);
       }
     }
+    if constexpr (CT == 0 && ACT == 0) {
+      if (e.row_stats && rv) {
+        float s16 = 0.f, q16 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          s16 += v[i];
+          q16 = fmaf(v[i], v[i], q16);
+        }
+        rsum += (double)s16;
+        rsq += (double)q16;
+      }
+    }
     // output value: res + scale * value (ACT 3); the fp16 copy adds the skip
     if constexpr (ACT == 3) {
       float sc[16];
@@ -1686,6 +1740,14 @@ __global__ void __launch_bounds__(kChThreads, 2)
   if (s_abort) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t ntiles_total = c.lines * c.tpl * c.ntiles;
+  // this CTA's tiles: t_beg, t_beg + t_step, .. < t_end (the same sequence for every role)
+  int64_t t_beg = blockIdx.x, t_end = ntiles_total, t_step = gridDim.x;
+  if (c.blocked) {
+    const int64_t per = (ntiles_total + gridDim.x - 1) / gridDim.x;
+    t_beg = (int64_t)blockIdx.x * per;
+    t_end = t_beg + per < ntiles_total ? t_beg + per : ntiles_total;
+    t_step = 1;
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; i++) {
@@ -1713,22 +1775,21 @@ __global__ void __launch_bounds__(kChThreads, 2)
     if (lane == 0) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
-      uint32_t it = 0;
+      int st = 0;       // ring stage and its phase parity, and the K block's (kh, cb, kw),
+      uint32_t ph = 0;  // all kept incrementally (no division in the issue loop)
       bool ok = true;
-      for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
+      for (int64_t tile = t_beg; ok && tile < t_end; tile += t_step) {
         int64_t line;
         int wo0, nt;
         ch_tile(c, tile, line, wo0, nt);
         const int64_t n = line / c.Ho;
         const int ho = (int)(line - n * c.Ho);
-        for (int kb = 0; kb < c.nkb; kb++, it++) {
-          const int st = (int)(it % (uint32_t)stages);
-          if (!mbar_wait_sleep(&empty[st], ((it / (uint32_t)stages) & 1u) ^ 1u, kFaultEmpty)) {
+        int kh = 0, cb = 0, kw = 0;
+        for (int kb = 0; kb < c.nkb; kb++) {
+          if (!mbar_wait(&empty[st], ph ^ 1u, kFaultEmpty)) {
             ok = false;
             break;
           }
-          const int grp = kb / c.KW, kw = kb - grp * c.KW;
-          const int kh = grp / c.ncb, cb = grp - kh * c.ncb;
           const int h = ho * c.SH - c.PH + kh * c.DH;
           const int d = kw * c.DW - c.PW;  // tap offset along W
           uint8_t *sb = smem + (size_t)st * Cfg::kStage;
@@ -1741,6 +1802,18 @@ __global__ void __launch_bounds__(kChThreads, 2)
             tma_load_5d(sb, &tmA, &full[st], cb * 64, phase, q0, h, (int)n);
           }
           tma_load_3d(sb + kATileBytes, &tmB, &full[st], kb * kBK, nt * BN, 0);
+          // K blocks run (kh, cb, kw) with kw fastest
+          if (++kw == c.KW) {
+            kw = 0;
+            if (++cb == c.ncb) {
+              cb = 0;
+              kh++;
+            }
+          }
+          if (++st == stages) {
+            st = 0;
+            ph ^= 1u;
+          }
         }
       }
     }
@@ -1748,16 +1821,18 @@ __global__ void __launch_bounds__(kChThreads, 2)
     // ---- MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_f16_f32(kBM, BN);
-      uint32_t it = 0, local = 0;
+      uint32_t local = 0;
+      int st = 0;
+      uint32_t ph = 0;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x, local++) {
+      for (int64_t tile = t_beg; ok && tile < t_end; tile += t_step, local++) {
         const uint32_t buf = local & 1u, use = local >> 1;
-        if (!mbar_wait_sleep(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
+        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, kFaultDone)) break;
         tc_fence_after();
         const uint32_t d = tmem + buf * (uint32_t)Cfg::kAccCols;
-        for (int kb = 0; kb < c.nkb; kb++, it++) {
-          const int st = (int)(it % (uint32_t)stages);
-          if (!mbar_wait_sleep(&full[st], (it / (uint32_t)stages) & 1u, kFaultFull)) {
+        int cb = 0, kw = 0;  // channel block and W tap of the K block (kw fastest)
+        for (int kb = 0; kb < c.nkb; kb++) {
+          if (!mbar_wait(&full[st], ph, kFaultFull)) {
             ok = false;
             break;
           }
@@ -1765,10 +1840,20 @@ __global__ void __launch_bounds__(kChThreads, 2)
           uint8_t *sb = smem + (size_t)st * Cfg::kStage;
           const uint64_t ad = sw128_desc(smem_u32(sb));
           const uint64_t bd = sw128_desc(smem_u32(sb + kATileBytes));
+          // the last channel block may hold fewer than 64 channels
+          const int kst = cb == c.ncb - 1 ? c.kst_last : kBK / 16;
 #pragma unroll
           for (int k = 0; k < kBK / 16; k++)
-            umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            if (k < kst) umma_f16(d, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0 ? 1u : 0u);
           umma_commit(&empty[st]);
+          if (++kw == c.KW) {
+            kw = 0;
+            if (++cb == c.ncb) cb = 0;
+          }
+          if (++st == stages) {
+            st = 0;
+            ph ^= 1u;
+          }
         }
         if (ok) umma_commit(&acc_full[buf]);
       }
@@ -1779,25 +1864,40 @@ __global__ void __launch_bounds__(kChThreads, 2)
     // ---- epilogue warps 0-3
     float *wst = stg + warp * (8 * 32);
     uint32_t local = 0;
-    for (int64_t tile = blockIdx.x; tile < ntiles_total; tile += gridDim.x, local++) {
+    // e.row_stats: this warp's running sums of its current row, added to the row's totals
+    // when the row changes and at the end (few atomics per row)
+    double rsum = 0.0, rsq = 0.0;
+    int64_t rrow = -1;
+    for (int64_t tile = t_beg; tile < t_end; tile += t_step, local++) {
       int64_t line;
       int wo0, nt;
       ch_tile(c, tile, line, wo0, nt);
+      if (e.row_stats) {
+        const int64_t rn = line / c.Ho;
+        if (rn != rrow) {
+          if (rrow >= 0) row_stats_add(e, rrow, lane, rsum, rsq);
+          rsum = 0.0;
+          rsq = 0.0;
+          rrow = rn;
+        }
+      }
       const uint32_t buf = local & 1u, use = local >> 1;
-      if (!warp_all(mbar_wait_sleep(&acc_full[buf], use & 1u, kFaultDone))) break;
+      if (!warp_all(mbar_wait(&acc_full[buf], use & 1u, kFaultDone))) break;
       tc_fence_after();
       // EK 0: generic epilogue; else the specialised one for ACT = (EK - 1) % 4 and
       // output geometry CT = (EK - 1) / 4
       if constexpr (EK == 0)
         ch_epilogue<BN>(c, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp, lane, line, wo0, nt,
-                        wst);
+                        wst, rsum, rsq);
       else
-        ch_epi_fast<BN, (EK - 1) % 4, (EK - 1) / 4>(
-            c, e, tmem + buf * (uint32_t)Cfg::kAccCols, warp, lane, line, wo0, nt, wst);
+        ch_epi_fast<BN, (EK - 1) % 4, (EK - 1) / 4>(c, e,
+                                                    tmem + buf * (uint32_t)Cfg::kAccCols, warp,
+                                                    lane, line, wo0, nt, wst, rsum, rsq);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    if (e.row_stats && rrow >= 0) row_stats_add(e, rrow, lane, rsum, rsq);
   }
 
   tc_fence_before();
@@ -2318,11 +2418,19 @@ bool conv_half(const HalfAct &x, int KH, int KW, int SH, int SW, int PH, int PW,
   c.tpl = (Wo + kBM - 1) / kBM;
   c.N = (int)N;
   c.nkb = KH * KW * ncb;
+  c.kst_last = (x.C - (ncb - 1) * 64 + 15) / 16;
+  // row statistics over few long rows: contiguous tile ranges (each CTA then adds a row's
+  // sums a few times instead of every CTA adding to every row); many rows keep the cyclic
+  // order (neighbouring tiles run together, sharing their input halo in L2)
+  c.blocked = e.row_stats != nullptr && x.images * Ho < 2LL * 2 * sm_count();
+  if (c.kst_last > kBK / 16) c.kst_last = kBK / 16;
   c.ntiles = (int)((N + bn - 1) / bn);
   Epi e2 = e;
   if (glu) e2.glu_half = bn / 2;
   const int ek = g_opt_generic_epi ? 0 : conv_epi_kind(e2, bn);
   if (ek == 0 && e2.spec_z) return false;  // only the specialised epilogue writes it
+  // row statistics: the generic and the plain (ACT 0) conv epilogues, one row per image
+  if (e2.row_stats && (e.mode != EPI_CONV || ek > 1 || Ho != 1)) return false;
   {
     const int64_t M = x.images * Ho * Wo;
     const double n_alg = e.mode == EPI_CONVTR ? (double)e.O * e.stride : (glu ? 2.0 * e.O : e.O);

@@ -68,6 +68,10 @@ struct Epi {
   uint16_t *yh = nullptr;
   int yhH = 1, yhW = 1, yhC = 0;
   const float *hskip = nullptr;
+  // EPI_CONV with Ho = 1 (images are rows): per image, the sum and the sum of squares of the
+  // output values, added in fp64 to row_stats[2 n], [2 n + 1] (the GroupNorm(1)
+  // statistics of a DConv hidden row, formed while the conv writes it)
+  double *row_stats = nullptr;
   // EPI_CONVTR along W over a view with the frequency axis as W (the last frequency
   // decoder): instead of y, the de-normalised complex spectrum frame-major,
   // spec_z[(n * spec_rows + o / 2) * spec_frames + h][w] = (v(o) sd + mean, v(o + 1) sd +

@@ -327,31 +327,29 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// GroupNorm statistics of z from the accumulated sums (see k_gn_gelu_zstats), one CTA of
-// 256 threads per row: warp w takes the Gram rows j = w, w + 8, .., its lanes the entries
-// (j, k >= j) of each, addressed directly (entry (j, k) of the upper triangle sits at
-// j hid - j (j - 1) / 2 + k - j); fp64 shuffle and shared-memory reduction
-__global__ void __launch_bounds__(256)
-    k_zstats_final(const double *__restrict__ acc, const double *__restrict__ zc, int hid,
-                   int64_t T, int C2, int rows, float eps, float *__restrict__ zmean,
-                   float *__restrict__ zrstd) {
-  __shared__ double red[2][8];
-  const int row = blockIdx.x;
+// z statistics of one DConv row (see k_gn_gelu_zstats) from its accumulated sums and upper
+// Gram entries a[npair + hid], by all 256 threads of a CTA: warp w takes the Gram rows j =
+// w, w + 8, .., its lanes the entries (j, k >= j), addressed directly (entry (j, k) of the
+// upper triangle sits at j hid - j (j - 1) / 2 + k - j); fp64 shuffle and shared-memory
+// reduction, thread 0 writes the mean and 1 / sqrt(var + eps) of z over its C2 T values
+static __device__ __forceinline__ void zstats_row(const double *__restrict__ a,
+                                                  const double *__restrict__ zc, int hid,
+                                                  int64_t T, int C2, float eps, float *zmean,
+                                                  float *zrstd, double (*red)[8]) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  if (row >= rows) return;
   const int npair = hid * (hid + 1) / 2;
-  const double *a = acc + (int64_t)row * (npair + hid);
   const double *G = zc, *u = zc + hid * hid, *vv = u + hid;
   double sz = 0.0, szz = 0.0;
   for (int j = wid; j < hid; j += 8) {
     const int base = j * hid - j * (j - 1) / 2;
     for (int k = j + lane; k < hid; k += 32)
-      szz += (k == j ? 1.0 : 2.0) * G[j * hid + k] * a[base + (k - j)];
+      szz += (k == j ? 1.0 : 2.0) * G[j * hid + k] * __ldcg(a + base + (k - j));
   }
   if (wid == 0) {
     for (int j = lane; j < hid; j += 32) {
-      sz += u[j] * a[npair + j];
-      szz += 2.0 * vv[j] * a[npair + j];
+      const double sj = __ldcg(a + npair + j);
+      sz += u[j] * sj;
+      szz += 2.0 * vv[j] * sj;
     }
   }
   for (int o = 16; o > 0; o >>= 1) {
@@ -376,8 +374,144 @@ __global__ void __launch_bounds__(256)
     const double mz = sz / nz;
     double vz = szz / nz - mz * mz;
     if (vz < 0.0) vz = 0.0;
-    zmean[row] = (float)mz;
-    zrstd[row] = 1.0f / sqrtf((float)vz + eps);
+    *zmean = (float)mz;
+    *zrstd = 1.0f / sqrtf((float)vz + eps);
+  }
+}
+
+// GroupNorm statistics of z from the accumulated sums, one CTA of 256 threads per row
+__global__ void __launch_bounds__(256)
+    k_zstats_final(const double *__restrict__ acc, const double *__restrict__ zc, int hid,
+                   int64_t T, int C2, int rows, float eps, float *__restrict__ zmean,
+                   float *__restrict__ zrstd) {
+  __shared__ double red[2][8];
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  const int npair = hid * (hid + 1) / 2;
+  zstats_row(acc + (int64_t)row * (npair + hid), zc, hid, T, C2, eps, zmean + row,
+             zrstd + row, red);
+}
+
+// DConv hidden rows [hid][T] after the k3 conv, whose epilogue summed each row's values and
+// squares into hstat (layers.c:24-53): GroupNorm(1) + GELU into hg (same layout as the
+// input), the fp16 channels-last copy (the 1x1 conv's A operand), and the sums S_j and
+// upper Gram entries Q_jk of fp16(h) (the z statistics, see k_gn_gelu_zstats) added into
+// acc[row] in fp64.  Block = (chunk of `chunk` positions, row, group of `egroup` Gram
+// entries): every block of a chunk forms its GELU outputs in shared memory, the group-0
+// block writes them out; a thread sums one entry over a slice of the positions (products of
+// fp16 values are exact in fp32, 32 of them are summed in fp32, the rest in fp64).  The
+// last block of a row to finish (a counter per row) turns acc[row] into zmean / zrstd.
+// hstat, acc and cnt start at zero.
+constexpr int kDgThreads = 256;
+__global__ void __launch_bounds__(kDgThreads)
+    k_dconv_gn_gram(RowView v, float *__restrict__ hg, const float *__restrict__ w,
+                    const float *__restrict__ bb, float eps, const double *__restrict__ hstat,
+                    double *__restrict__ acc, unsigned *__restrict__ cnt, int chunk, int egroup,
+                    const double *__restrict__ zc, int C2, float *__restrict__ zmean,
+                    float *__restrict__ zrstd, uint16_t *__restrict__ h16, int hidp) {
+  extern __shared__ float hs[];  // [hid][ld]: fp16-rounded GELU outputs of the chunk
+  __shared__ double red[2][8];
+  __shared__ unsigned s_last;
+  const int64_t row = blockIdx.y;
+  const int64_t b = row / v.Fr, f = row - b * v.Fr;
+  const int hid = v.C, T = v.T;
+  const int t0 = blockIdx.x * chunk;
+  const int len = T - t0 < chunk ? T - t0 : chunk;
+  const int ld = len | 1;  // odd row pitch: threads on consecutive channels hit distinct banks
+  const bool writer = blockIdx.z == 0;
+  // the row's GroupNorm statistics (same formulas as k_gn_gelu_zstats)
+  const double n = (double)hid * T;
+  const double md = __ldcg(hstat + 2 * row) / n;
+  double vd = __ldcg(hstat + 2 * row + 1) / n - md * md;
+  if (vd < 0.0) vd = 0.0;
+  const float m = (float)md;
+  const float rs = 1.0f / sqrtf((float)vd + eps);
+  const int64_t off = b * v.sB + f * v.sF + t0;
+  const float *__restrict__ xr = v.x + off;
+  float *__restrict__ yr = hg + off;
+  // eight elements per thread at a time: their loads are all in flight before the first
+  // result is stored (the input and the output are distinct buffers)
+  const int nel = hid * len;
+  for (int i0 = 0; i0 < nel; i0 += 8 * kDgThreads) {
+    float xv[8];
+    int cc[8], tt[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int i = i0 + k * kDgThreads + (int)threadIdx.x;
+      cc[k] = i / len;
+      tt[k] = i - cc[k] * len;
+      xv[k] = i < nel ? xr[(int64_t)cc[k] * v.sC + tt[k]] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int i = i0 + k * kDgThreads + (int)threadIdx.x;
+      if (i < nel) {
+        const int c = cc[k];
+        const float h = gelu_f((xv[k] - m) * rs * w[c] + bb[c]);
+        if (writer) yr[(int64_t)c * v.sC + tt[k]] = h;
+        hs[c * ld + tt[k]] = __half2float(__float2half_rn(h));
+      }
+    }
+  }
+  __syncthreads();
+  if (writer && h16) {
+    for (int t = threadIdx.x; t < len; t += kDgThreads) {
+      uint16_t *dst = h16 + (row * T + t0 + t) * hidp;
+      for (int c8 = 0; c8 < hidp; c8 += 8) {
+        float q[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) q[k] = c8 + k < hid ? hs[(c8 + k) * ld + t] : 0.f;
+        *(uint4 *)(dst + c8) = make_uint4(pack_h2(q[0], q[1]), pack_h2(q[2], q[3]),
+                                          pack_h2(q[4], q[5]), pack_h2(q[6], q[7]));
+      }
+    }
+  }
+  // this block's Gram entries [e0, e1), `slices` threads per entry
+  const int npair = hid * (hid + 1) / 2, ntot = npair + hid;
+  const int e0 = blockIdx.z * egroup;
+  const int e1 = e0 + egroup < ntot ? e0 + egroup : ntot;
+  const int ne = e1 - e0;
+  const int slices = ne >= kDgThreads ? 1 : kDgThreads / ne;
+  double *ar = acc + row * ntot;
+  if (threadIdx.x < ne * slices) {
+    const int p = e0 + (int)threadIdx.x % ne, sl = (int)threadIdx.x / ne;
+    int j, k;
+    if (p < npair) {
+      gram_pair(p, hid, j, k);
+    } else {
+      j = p - npair;
+      k = -1;
+    }
+    const float *hj = hs + j * ld;
+    const float *hk = hs + (k >= 0 ? k : j) * ld;
+    const float one = k >= 0 ? 0.f : 1.f;  // sums: hj[t] * 1 (hk = hj, weight 0)
+    double a = 0.0;
+    for (int tb = sl; tb < len; tb += 32 * slices) {
+      // 32 terms of this slice in fp32, four independent chains
+      float a4[4] = {0.f, 0.f, 0.f, 0.f};
+      const int te = tb + 32 * slices < len ? tb + 32 * slices : len;
+      int t = tb;
+      for (; t + 3 * slices < te; t += 4 * slices) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float x = hj[t + q * slices];
+          a4[q] = fmaf(x, fmaf(hk[t + q * slices], 1.f - one, one), a4[q]);
+        }
+      }
+      for (; t < te; t += slices) a4[0] = fmaf(hj[t], fmaf(hk[t], 1.f - one, one), a4[0]);
+      a += (double)((a4[0] + a4[1]) + (a4[2] + a4[3]));
+    }
+    atomicAdd(ar + p, a);
+  }
+  // the row's last block: every block's atomics are visible once its count is
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0)
+    s_last = atomicAdd(cnt + row, 1u) == gridDim.x * gridDim.z - 1 ? 1u : 0u;
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    zstats_row(ar, zc, hid, T, C2, eps, zmean + row, zrstd + row, red);
   }
 }
 

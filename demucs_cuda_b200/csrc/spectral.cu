@@ -466,13 +466,25 @@ __global__ void k_ola_frames4096(const float *__restrict__ fw, float *__restrict
 // contributor) is in; the three frames before the run are recomputed by the CTA (3 of
 // kStreamHops + 3 frames), so no frame buffer goes through HBM.
 constexpr int kStreamHops = 32;
+
+// The output stage (htdemucs.c:262-279) fused into the streamed inverse STFT: with y set,
+// sample t of row r goes to y[r][t - off] (t - off in [0, keep)) as the time branch's
+// de-normalised output plus the spectral branch's, xt[r][t - off] (sqrt(var[b]) + eps) +
+// mean[b] + istft, b = r / rows; nothing else is written
+struct StreamCombine {
+  float *y = nullptr;
+  const float *xt = nullptr, *mean = nullptr, *var = nullptr;
+  int rows = 1;
+  int64_t Lt = 0, off = 0, keep = 0;
+  float eps = 0.f;
+};
 int g_stream_istft = 1;  // 0: the two-pass inverse STFT (frames through HBM), for A/B checks
 
-__global__ void __launch_bounds__(kFftThreads)
+__global__ void __launch_bounds__(kFftThreads, 4)
     k_istft_stream4096(const float2 *__restrict__ z, float *__restrict__ out, int N, int F,
                        int NF, const float *__restrict__ window,
                        const float2 *__restrict__ tw, int64_t start, int64_t length,
-                       int g_first) {
+                       int g_first, const StreamCombine cb) {
   extern __shared__ float2 sbuf[];  // [kFftPadded] FFT buffer, then the ring [4][1024]
   float2 *buf = sbuf;
   float *ring = (float *)(sbuf + kFftPadded);
@@ -546,7 +558,17 @@ __global__ void __launch_bounds__(kFftThreads)
                 den += wv * wv;
               }
             }
-            out[r * length + t] = den > 0.f ? slot[w] / den : 0.f;
+            const float val = den > 0.f ? slot[w] / den : 0.f;
+            if (cb.y) {
+              const int64_t tt = t - cb.off;
+              if (tt >= 0 && tt < cb.keep) {
+                const int64_t b = r / cb.rows;
+                cb.y[r * cb.keep + tt] =
+                    fmaf(cb.xt[r * cb.Lt + tt], sqrtf(cb.var[b]) + cb.eps, cb.mean[b]) + val;
+              }
+            } else {
+              out[r * length + t] = val;
+            }
           }
           slot[w] = 0.f;
         }
@@ -577,7 +599,7 @@ bool ispec_stream_ok(int n_fft, int hop, int N, int64_t start, int64_t length) {
 // 2049; the decoder's F = 2048 leaves the Nyquist bin zero) -> out [R][length], samples
 // start .. start + length of the signal (ispec_stream_ok must hold)
 void ispec_frames(const float2 *z, float *out, int64_t R, int F, int N, const float *window,
-                  int64_t start, int64_t length) {
+                  int64_t start, int64_t length, const StreamCombine &cb) {
   constexpr int hop = 1024;
   DCB_REQUIRE(R <= 65535 && F <= kFftN / 2 + 1, "ispec: %lld rows, %d bins", (long long)R, F);
   // output frames NF = N + 4 (two of padding on each side); hops covering the samples
@@ -593,10 +615,11 @@ void ispec_frames(const float2 *z, float *out, int64_t R, int F, int N, const fl
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
     attr = true;
   }
-  TraceScope ts(TR_SPECTRAL, 0.0, (double)R * N * F * 8.0 + (double)R * length * 4.0, R, F,
-                length);
+  TraceScope ts(TR_SPECTRAL, 0.0,
+                (double)R * N * F * 8.0 + (cb.y ? (double)R * cb.keep * 8.0 : (double)R * length * 4.0),
+                R, F, length);
   k_istft_stream4096<<<dim3((unsigned)runs, (unsigned)R), kFftThreads, sm, stream()>>>(
-      z, out, N, F, NF, window, twiddles4096(), start, length, g_first);
+      z, out, N, F, NF, window, twiddles4096(), start, length, g_first, cb);
   DCB_LAUNCHED();
 }
 
@@ -629,7 +652,7 @@ void ispec_fused(const float *x, float *out, const float *mean, const float *var
     attr = smem;
   }
   if (ispec_stream_ok(n_fft, hop, N, start, length)) {
-    ispec_frames(z, out, R, F, N, window, start, length);
+    ispec_frames(z, out, R, F, N, window, start, length, StreamCombine{});
     DCB_CUDA(cudaFreeAsync(z, stream()));
     return;
   }

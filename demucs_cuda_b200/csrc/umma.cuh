@@ -55,19 +55,6 @@ static __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) 
       : "memory");
   return ok != 0;
 }
-// try_wait with a suspend-time hint: a waiting thread sleeps (up to the hint, in ns) until
-// the phase completes instead of re-polling, leaving issue slots to the working warps
-static __device__ __forceinline__ bool mbar_try_sleep(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
-      : "memory");
-  return ok != 0;
-}
 static __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -105,23 +92,6 @@ static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
 // at the time limit while another saw the phase complete would otherwise leave the warp
 // divergent in front of a TMEM access.  Every lane of the warp must call it.
 static __device__ __forceinline__ bool warp_all(bool ok) { return __all_sync(0xffffffffu, ok); }
-
-// mbar_wait through mbar_try_sleep (same bound and fault protocol)
-static __device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity,
-                                                       uint32_t fault) {
-  if (mbar_try_sleep(bar, parity)) return true;
-  const uint64_t t0 = global_ns(), lim = wait_limit_ns();
-  for (uint32_t i = 1;; i++) {
-    if (mbar_try_sleep(bar, parity)) return true;
-    if ((i & 15u) == 0) {
-      if (fault_pending()) return false;
-      if (global_ns() - t0 > lim) {
-        atomicOr(&g_dev_fault, fault);
-        return false;
-      }
-    }
-  }
-}
 
 // Fault-path drain: wait (bounded by the same limit, but not cut short by the fault word)
 // for a phase that this CTA's own copies complete, so that no copy is still landing in
@@ -224,6 +194,31 @@ static __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v
       "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
       "r"(__float_as_uint(v[15]))
       : "memory");
+}
+// 32 lanes x 32-bit, 4 consecutive columns per thread (load and store)
+static __device__ __forceinline__ void tmem_ld4(uint32_t taddr, float (&v)[4]) {
+  uint32_t r0, r1, r2, r3;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(taddr)
+               : "memory");
+  v[0] = __uint_as_float(r0);
+  v[1] = __uint_as_float(r1);
+  v[2] = __uint_as_float(r2);
+  v[3] = __uint_as_float(r3);
+}
+static __device__ __forceinline__ void tmem_st4(uint32_t taddr, const float (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])),
+               "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3]))
+               : "memory");
+}
+// 32 lanes x 32-bit, one column per thread
+static __device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr)
+               : "memory");
+  return __uint_as_float(r);
 }
 static __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
