@@ -316,6 +316,7 @@ def b200_arm(args):
 
     # the segment forward runs as a replayed CUDA graph (captured during the warm-up)
     dcb.set_option("graphs", 0 if args.no_graphs else 1)
+    dcb.set_option("streams", 0 if args.one_stream else 1)
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
@@ -418,6 +419,7 @@ def b200_arm(args):
                     "d2h_bytes_per_step": int(out_host.numel() * 4)},
             "gpu_launches": int(launches),
             "cuda_graphs": not args.no_graphs,
+            "branch_streams": 1 if args.one_stream else 2,
             "roofline": roof,
             "gemm": {"tflops": gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms else None,
                      "frac_of_peak": (gemm_flops / (gemm_ms * 1e-3) / 1e12) / tflops_sus
@@ -447,6 +449,8 @@ def main():
     ap.add_argument("--shifts", type=int, default=1)
     ap.add_argument("--overlap", type=float, default=0.25)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--one-stream", action="store_true",
+                    help="issue the time branch on the same stream as the frequency branch")
     ap.add_argument("--no-graphs", action="store_true",
                     help="launch every kernel eagerly instead of replaying the captured "
                          "segment forward")

@@ -25,6 +25,7 @@ void count_launch();
 void add_launches(uint64_t n);
 uint64_t launches_now();
 void set_stream_override(cudaStream_t s);
+cudaStream_t stream_override_get();
 
 #define DCB_CUDA(call)                                                                   \
   do {                                                                                   \
@@ -52,6 +53,7 @@ void set_stream_override(cudaStream_t s);
 // option values (dcb_set_option)
 extern int g_opt_simt;
 extern int g_opt_graphs;
+extern int g_opt_streams;
 extern int g_opt_generic_epi;  // channels-last convs take the generic epilogue
 
 // device fault word written by bounded waits (see umma.cuh); the library is one

@@ -28,6 +28,40 @@ static void dfree(void *p) {
   if (p) DCB_CUDA(cudaFreeAsync(p, stream()));
 }
 
+// The frequency and time branches are independent from the spectrogram to the transformer,
+// inside each transformer layer, and through the decoders: the time branch's layers are
+// issued on a second stream (option "streams"), forked from and joined back to the current
+// one with events, so its kernels fill the GPU beside the frequency branch's (inside a CUDA
+// graph capture the second stream joins the capture through the fork).
+static cudaStream_t aux_stream() {
+  static cudaStream_t s = nullptr;
+  if (!s) DCB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  return s;
+}
+// `waiter` waits for everything issued so far on `on`
+static void stream_wait(cudaStream_t waiter, cudaStream_t on) {
+  static cudaEvent_t ev[16] = {};
+  static int next = 0;
+  cudaEvent_t &e = ev[next];
+  next = (next + 1) % 16;
+  if (!e) DCB_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  DCB_CUDA(cudaEventRecord(e, on));
+  DCB_CUDA(cudaStreamWaitEvent(waiter, e, 0));
+}
+// issue on `s` for the lifetime of the scope (when `on`), then back to the previous stream
+struct OnStream {
+  cudaStream_t prev = nullptr;
+  bool on;
+  OnStream(cudaStream_t s, bool on_) : on(on_) {
+    if (!on) return;
+    prev = stream_override_get();
+    set_stream_override(s);
+  }
+  ~OnStream() {
+    if (on) set_stream_override(prev);
+  }
+};
+
 void ispec_fused(const float *x, float *out, const float *mean, const float *var, int B,
                  int rows_per_b, int F, int N, int n_fft, int hop, const float *window,
                  int64_t start, int64_t length, float eps);
@@ -847,8 +881,11 @@ static void tlayer_branch(DcbModel *m, const TLayerW &tl, float *x, int B, int T
   dfree(st);
 }
 
-// dc_crosstransformer (transformer.c:160-216): x [B, C, Fr, T1], xt [B, C, T2] in place
-static void crosstransformer(DcbModel *m, float *x, float *xt, int B, int Fr, int T1, int T2) {
+// dc_crosstransformer (transformer.c:160-216): x [B, C, Fr, T1], xt [B, C, T2] in place.
+// With `aux`, each layer's time-branch half runs on that stream beside the frequency
+// branch's (forked and joined per layer: a cross layer reads both branches' tokens).
+static void crosstransformer(DcbModel *m, float *x, float *xt, int B, int Fr, int T1, int T2,
+                             cudaStream_t aux) {
   const int D = m->D, H = m->cfg.t_heads, hd = D / H;
   const int N1 = Fr * T1, N2 = T2;
   float *tx = dalloc((size_t)B * N1 * D), *tt = dalloc((size_t)B * N2 * D);
@@ -878,22 +915,32 @@ static void crosstransformer(DcbModel *m, float *x, float *xt, int B, int Fr, in
     b->att = halloc((size_t)R * D);
     b->hid = halloc((size_t)R * ldh);
   }
+  const cudaStream_t s_main = stream();
   for (int l = 0; l < m->cfg.t_layers; l++) {
     const TLayerW &lx = m->layers[0][l], &lt = m->layers[1][l];
     if (!lx.cross) {
+      if (aux) stream_wait(aux, s_main);
       layernorm(tx, bx.ln, lx.norm1.w, lx.norm1.b, R1, D, 1e-5f, true, ldl);
       tlayer_branch(m, lx, tx, B, N1, N1, bx);
-      layernorm(tt, bt.ln, lt.norm1.w, lt.norm1.b, R2, D, 1e-5f, true, ldl);
-      tlayer_branch(m, lt, tt, B, N2, N2, bt);
+      {
+        OnStream os(aux, aux != nullptr);
+        layernorm(tt, bt.ln, lt.norm1.w, lt.norm1.b, R2, D, 1e-5f, true, ldl);
+        tlayer_branch(m, lt, tt, B, N2, N2, bt);
+      }
     } else {
       // both branches read the previous layer's tokens: take every LN first
       layernorm(tx, bx.ln, lx.norm1.w, lx.norm1.b, R1, D, 1e-5f, true, ldl);
       layernorm(tt, bx.lnk, lx.norm2.w, lx.norm2.b, R2, D, 1e-5f, true, ldl);
       layernorm(tt, bt.ln, lt.norm1.w, lt.norm1.b, R2, D, 1e-5f, true, ldl);
       layernorm(tx, bt.lnk, lt.norm2.w, lt.norm2.b, R1, D, 1e-5f, true, ldl);
+      if (aux) stream_wait(aux, s_main);
       tlayer_branch(m, lx, tx, B, N1, N2, bx);
-      tlayer_branch(m, lt, tt, B, N2, N1, bt);
+      {
+        OnStream os(aux, aux != nullptr);
+        tlayer_branch(m, lt, tt, B, N2, N1, bt);
+      }
     }
+    if (aux) stream_wait(s_main, aux);
   }
   {
     const int64_t n1 = (int64_t)B * D * N1, n2 = (int64_t)B * D * N2;
@@ -955,55 +1002,69 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
     dfree(mag);
   }
   sg.emit("x_norm", x, {B, 2 * C, nb, le});
-  row_stats(mix, B, (int64_t)C * L, meant, vart);
-  float *xt = dalloc((size_t)B * C * L);
-  dk_affine_rows(mix, xt, meant, vart, B, (int64_t)C * L, 1e-5f, 0);
-  sg.emit("xt_norm", xt, {B, C, L});
-
-  // encoders
+  // from here to the transformer the time branch runs on the second stream (the stage
+  // callbacks of the tests keep one stream)
+  const bool two = g_opt_streams && !sg.fn;
+  const cudaStream_t s_main = stream();
+  const cudaStream_t s_aux = two ? aux_stream() : s_main;
+  if (two) stream_wait(s_aux, s_main);
   std::vector<float *> saved, saved_t;
   std::vector<int> fr_len, t_len;  // H of the freq input, length of the time input
   int H = nb, W = le, Lt = L;
   char name[32];
-  // fp16 channels-last companions of the encoder inputs (none for the first encoders,
-  // whose few input channels take the gather kernel)
-  // (the first ones: the normalised inputs with their few channels padded to 8)
-  Half16 xh_t = first_input(m, false, xt, B, C, 1, L);
-  Half16 xh_f = first_input(m, true, x, B, 2 * C, nb, le);
-  for (int i = 0; i < depth; i++) {
-    t_len.push_back(Lt);
-    int Lo;
-    Half16 zt;
-    float *xt2 = enc_time(m, i, xt, &xh_t, B, Lt, &Lo, &zt);
-    if (i == 0) dfree(xt);  // the normalised input; encoder outputs live on as skips
+  float *xt = nullptr;
+  {
+    // time branch: normalised input, then the encoders
+    OnStream os(s_aux, two);
+    row_stats(mix, B, (int64_t)C * L, meant, vart);
+    xt = dalloc((size_t)B * C * L);
+    dk_affine_rows(mix, xt, meant, vart, B, (int64_t)C * L, 1e-5f, 0);
+    sg.emit("xt_norm", xt, {B, C, L});
+    // fp16 channels-last companion of each encoder input (the first: the normalised input
+    // with its few channels padded to 8, or its im2col form)
+    Half16 xh_t = first_input(m, false, xt, B, C, 1, L);
+    for (int i = 0; i < depth; i++) {
+      t_len.push_back(Lt);
+      int Lo;
+      Half16 zt;
+      float *xt2 = enc_time(m, i, xt, &xh_t, B, Lt, &Lo, &zt);
+      if (i == 0) dfree(xt);  // the normalised input; encoder outputs live on as skips
+      dfree(xh_t.p);
+      xh_t = zt;
+      xt = xt2;
+      Lt = Lo;
+      saved_t.push_back(xt);
+      snprintf(name, sizeof(name), "tenc_%d", i);
+      sg.emit(name, xt, {B, m->tenc[i].Cout, Lt});
+    }
     dfree(xh_t.p);
-    xh_t = zt;
-    xt = xt2;
-    Lt = Lo;
-    saved_t.push_back(xt);
-    snprintf(name, sizeof(name), "tenc_%d", i);
-    sg.emit(name, xt, {B, m->tenc[i].Cout, Lt});
-    fr_len.push_back(H);
-    int Ho;
-    Half16 zf;
-    float *x2 = enc_freq(m, i, x, &xh_f, B, H, W, &Ho, &zf);
-    if (i == 0) dfree(x);
-    dfree(xh_f.p);
-    xh_f = zf;
-    x = x2;
-    H = Ho;
-    saved.push_back(x);
-    snprintf(name, sizeof(name), "enc_%d", i);
-    sg.emit(name, x, {B, m->enc[i].Cout, H, W});
   }
-  dfree(xh_t.p);
-  dfree(xh_f.p);
+  {
+    // frequency branch encoders
+    Half16 xh_f = first_input(m, true, x, B, 2 * C, nb, le);
+    for (int i = 0; i < depth; i++) {
+      fr_len.push_back(H);
+      int Ho;
+      Half16 zf;
+      float *x2 = enc_freq(m, i, x, &xh_f, B, H, W, &Ho, &zf);
+      if (i == 0) dfree(x);
+      dfree(xh_f.p);
+      xh_f = zf;
+      x = x2;
+      H = Ho;
+      saved.push_back(x);
+      snprintf(name, sizeof(name), "enc_%d", i);
+      sg.emit(name, x, {B, m->enc[i].Cout, H, W});
+    }
+    dfree(xh_f.p);
+  }
+  if (two) stream_wait(s_main, s_aux);
   // the encoder outputs are kept as skips; the transformer works on copies
   const int D = m->D;
   float *tx = dalloc((size_t)B * D * H * W), *txt = dalloc((size_t)B * D * Lt);
   DCB_CUDA(cudaMemcpyAsync(tx, x, (size_t)B * D * H * W * 4, cudaMemcpyDeviceToDevice, stream()));
   DCB_CUDA(cudaMemcpyAsync(txt, xt, (size_t)B * D * Lt * 4, cudaMemcpyDeviceToDevice, stream()));
-  if (c.t_layers > 0) crosstransformer(m, tx, txt, B, H, W, Lt);
+  if (c.t_layers > 0) crosstransformer(m, tx, txt, B, H, W, Lt, two ? s_aux : nullptr);
   sg.emit("transformer_x", tx, {B, D, H, W});
   sg.emit("transformer_xt", txt, {B, D, Lt});
   x = tx;
@@ -1011,18 +1072,42 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
   // decoders (htdemucs.c:198-237).  Each decoder reads x + skip as an fp16 companion, which
   // the previous decoder's transposed conv writes (the first: a conversion of the
   // transformer output); the fp32 outputs are formed only where something reads them.
-  Half16 xs_f = to_half(x, saved.back(), B, D, H, W, false);
-  Half16 xs_t = to_half(xt, saved_t.back(), B, D, 1, Lt, false);
   // a decoder also writes its fp32 output when the next one reads fp32 (its channel counts
   // take the gather kernel)
   auto tma_dec = [&](const DecW &d) {
     return d.rewrite.wt && d.convtr.wt && d.Cin % 8 == 0;
   };
+  // time branch decoders on the second stream
+  if (two) stream_wait(s_aux, s_main);
+  {
+    OnStream os(s_aux, two);
+    Half16 xs_t = to_half(xt, saved_t.back(), B, D, 1, Lt, false);
+    for (int i = 0; i < depth; i++) {
+      const bool last = i == depth - 1;
+      const bool want_yt = last || sg.fn || !tma_dec(m->tdec[i + 1]);
+      float *skip_t = saved_t.back();
+      saved_t.pop_back();
+      const int Lin = Lt;
+      Lt = t_len.back();
+      t_len.pop_back();
+      Half16 yt;
+      float *xt2 = dec_time(m, i, xt, skip_t, &xs_t, B, Lin, Lt, last, want_yt,
+                            last ? nullptr : saved_t.back(), last ? nullptr : &yt);
+      dfree(xt);
+      dfree(skip_t);
+      dfree(xs_t.p);
+      xs_t = yt;
+      xt = xt2;
+      snprintf(name, sizeof(name), "tdec_%d", i);
+      if (xt) sg.emit(name, xt, {B, m->tdec[i].Cout, Lt});
+    }
+    dfree(xs_t.p);
+  }
+  Half16 xs_f = to_half(x, saved.back(), B, D, H, W, false);
   SpecOut spec;
   for (int i = 0; i < depth; i++) {
     const bool last = i == depth - 1;
     const bool want_y = last || sg.fn || !tma_dec(m->dec[i + 1]);
-    const bool want_yt = last || sg.fn || !tma_dec(m->tdec[i + 1]);
     float *skip = saved.back();
     saved.pop_back();
     const int Hin = H;
@@ -1052,24 +1137,9 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
     }
     snprintf(name, sizeof(name), "dec_%d", i);
     if (x) sg.emit(name, x, {B, m->dec[i].Cout, H, W});
-    float *skip_t = saved_t.back();
-    saved_t.pop_back();
-    const int Lin = Lt;
-    Lt = t_len.back();
-    t_len.pop_back();
-    Half16 yt;
-    float *xt2 = dec_time(m, i, xt, skip_t, &xs_t, B, Lin, Lt, last, want_yt,
-                          last ? nullptr : saved_t.back(), last ? nullptr : &yt);
-    dfree(xt);
-    dfree(skip_t);
-    dfree(xs_t.p);
-    xs_t = yt;
-    xt = xt2;
-    snprintf(name, sizeof(name), "tdec_%d", i);
-    if (xt) sg.emit(name, xt, {B, m->tdec[i].Cout, Lt});
   }
   dfree(xs_f.p);
-  dfree(xs_t.p);
+  if (two) stream_wait(s_main, s_aux);
   // output (htdemucs.c:242-279)
   const int S = c.n_sources;
   const int Ctot = m->dec[depth - 1].Cout;  // S * 2C
@@ -1613,7 +1683,7 @@ int dcb_stage_decoder(DcbModel *m, int branch, int idx, const float *x, const fl
 int dcb_stage_transformer(DcbModel *m, float *x, float *xt, int B, int C, int Fr, int T1,
                           int T2) {
   if (!m || C != m->D) return -1;
-  crosstransformer(m, x, xt, B, Fr, T1, T2);
+  crosstransformer(m, x, xt, B, Fr, T1, T2, nullptr);
   DCB_CUDA(cudaStreamSynchronize(stream()));
   return failed() ? -1 : 0;
 }

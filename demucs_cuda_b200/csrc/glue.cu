@@ -95,31 +95,23 @@ __global__ void k_rowview_combine(const double *partial, int64_t rows, int nchun
   }
 }
 
-static double *g_part = nullptr;
-static size_t g_part_cap = 0;
-
-// statistics of B*Fr rows; mean/rstd/var are device arrays of rows entries (var optional)
+// statistics of B*Fr rows; mean/rstd/var are device arrays of rows entries (var optional);
+// the per-chunk partials live in stream-ordered memory of the call's stream
 void rowview_stats(const RowView &v, int B, float eps, float *mean, float *rstd, float *var) {
   const int64_t rows = (int64_t)B * v.Fr;
   const int64_t L = (int64_t)v.C * v.T;
   if (rows <= 0 || L <= 0) return;
   const int nchunks = (int)((L + kGnChunk - 1) / kGnChunk);
-  const size_t need = (size_t)rows * nchunks * 3 * sizeof(double);
-  if (need > g_part_cap) {
-    if (g_part) {
-      DCB_CUDA(cudaStreamSynchronize(stream()));
-      DCB_CUDA(cudaFree(g_part));
-    }
-    g_part_cap = need < ((size_t)4 << 20) ? ((size_t)4 << 20) : need * 2;
-    DCB_CUDA(cudaMalloc(&g_part, g_part_cap));
-  }
   DCB_REQUIRE(rows <= 65535, "group norm: %lld rows", (long long)rows);
+  double *part = nullptr;
+  DCB_CUDA(cudaMallocAsync(&part, (size_t)rows * nchunks * 3 * sizeof(double), stream()));
   dim3 grid(nchunks, (unsigned)rows);
-  k_rowview_stats<<<grid, kGnThreads, 0, stream()>>>(v, nchunks, g_part);
+  k_rowview_stats<<<grid, kGnThreads, 0, stream()>>>(v, nchunks, part);
   DCB_LAUNCHED();
-  k_rowview_combine<<<grid_for(rows * 32, 128, 1 << 30), 128, 0, stream()>>>(g_part, rows, nchunks,
+  k_rowview_combine<<<grid_for(rows * 32, 128, 1 << 30), 128, 0, stream()>>>(part, rows, nchunks,
                                                                        eps, mean, rstd, var);
   DCB_LAUNCHED();
+  DCB_CUDA(cudaFreeAsync(part, stream()));
 }
 
 // y = GELU(GN(x)) in the same strided layout (x and y share strides)

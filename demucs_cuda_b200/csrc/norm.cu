@@ -113,9 +113,8 @@ __global__ void k_combine_stats(const double *partial, int64_t rows, int nchunks
   }
 }
 
-static double *g_stat_scratch = nullptr;
-static size_t g_stat_cap = 0;
-
+// the per-chunk partials live in stream-ordered memory of the call's stream (calls on two
+// streams never share them)
 void row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var) {
   if (rows <= 0 || L <= 0) return;
   DCB_REQUIRE(L / kStatChunk < 0x7fffffff && rows < 0x7fffffff &&
@@ -123,22 +122,15 @@ void row_stats(const float *x, int64_t rows, int64_t L, float *mean, float *var)
               "row_stats: %lld rows of %lld elements exceed the launch limits",
               (long long)rows, (long long)L);
   int nchunks = (int)((L + kStatChunk - 1) / kStatChunk);
-  size_t need = (size_t)rows * nchunks * 3 * sizeof(double);
-  if (need > g_stat_cap) {
-    if (g_stat_scratch) {
-      DCB_CUDA(cudaStreamSynchronize(stream()));
-      DCB_CUDA(cudaFree(g_stat_scratch));
-    }
-    size_t cap = need < ((size_t)1 << 20) ? ((size_t)1 << 20) : need * 2;
-    DCB_CUDA(cudaMalloc(&g_stat_scratch, cap));
-    g_stat_cap = cap;
-  }
-  k_chunk_stats<<<(unsigned)(rows * nchunks), kStatThreads, 0, stream()>>>(x, L, nchunks,
-                                                                          g_stat_scratch);
+  const size_t need = (size_t)rows * nchunks * 3 * sizeof(double);
+  double *part = nullptr;
+  DCB_CUDA(cudaMallocAsync(&part, need, stream()));
+  k_chunk_stats<<<(unsigned)(rows * nchunks), kStatThreads, 0, stream()>>>(x, L, nchunks, part);
   DCB_LAUNCHED();
-  k_combine_stats<<<grid_for(rows * 32, 128, 1 << 30), 128, 0, stream()>>>(g_stat_scratch, rows,
-                                                                     nchunks, mean, var);
+  k_combine_stats<<<grid_for(rows * 32, 128, 1 << 30), 128, 0, stream()>>>(part, rows, nchunks,
+                                                                     mean, var);
   DCB_LAUNCHED();
+  DCB_CUDA(cudaFreeAsync(part, stream()));
 }
 
 // ---- allocation-free row statistics (dk_row_stats_noalloc)

@@ -24,6 +24,7 @@ static std::atomic<uint64_t> g_launches{0};
 int g_opt_simt = 0;
 int g_opt_graphs = 0;
 int g_opt_generic_epi = 0;
+int g_opt_streams = 1;
 extern int g_stream_istft;
 
 void fail(const char *fmt, ...) {
@@ -49,6 +50,7 @@ uint64_t error_count() { return g_err_count; }
 static cudaStream_t g_override = nullptr;  // capture stream while a CUDA graph is recorded
 
 void set_stream_override(cudaStream_t s) { g_override = s; }
+cudaStream_t stream_override_get() { return g_override; }
 
 cudaStream_t stream() {
   if (g_override) return g_override;
@@ -242,6 +244,10 @@ int dcb_set_option(const char *name, int value) {
   } else if (!strcmp(name, "stream_istft")) {
     old = g_stream_istft;
     g_stream_istft = value;
+  } else if (!strcmp(name, "streams")) {
+    // 1: the time branch's layers run on a second stream beside the frequency branch's
+    old = g_opt_streams;
+    g_opt_streams = value;
   } else if (!strcmp(name, "generic_epilogue")) {
     old = g_opt_generic_epi;
     g_opt_generic_epi = value;

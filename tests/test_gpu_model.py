@@ -224,3 +224,24 @@ def test_full_forward_vs_reference_digest(torch_cuda):
         print(f"  {k:16s} samples rel {e:.3e}  energy rel {s:.3e}")
     assert errs["stems"][0] < STEMS_GATE and errs["stems"][1] < 2 * STEMS_GATE
     del model
+
+
+def test_short_two_streams_match_one(short):
+    """The time branch issued on a second stream (forked from the first and joined back with
+    events around the encoders, each transformer layer and the decoders) gives the
+    one-stream result (the captured-graph form runs in the apply tests, where the option is
+    on by default)."""
+    import demucs_cuda_b200 as dcb
+    torch = short["torch"]
+    x = _t(torch, short["mix"])
+    outs = {}
+    for streams in (0, 1):
+        old = dcb.set_option("streams", streams)
+        try:
+            outs[streams] = short["model"].forward(x).cpu().numpy()
+        finally:
+            dcb.set_option("streams", old)
+    e = rel_l2(outs[1], outs[0])
+    print(f"two streams vs one: rel_l2 {e:.3e}")
+    assert e < 1e-6
+    assert dcb.device_fault() == 0
