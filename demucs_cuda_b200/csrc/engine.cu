@@ -364,6 +364,7 @@ struct TLayerW {
 // output buffers so the graph's pointers stay valid across replays.
 struct FwdGraph {
   int B = 0, T = 0;
+  int idx = 0;  // which of the two alternating slots of this shape (overlapped batches)
   float *in = nullptr, *out = nullptr;
   bool warmed = false;
   cudaGraphExec_t exec = nullptr;

@@ -38,6 +38,12 @@ static cudaStream_t aux_stream() {
   if (!s) DCB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
   return s;
 }
+// the second stream of overlapped forward batches (see apply_window)
+static cudaStream_t batch_stream() {
+  static cudaStream_t s = nullptr;
+  if (!s) DCB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  return s;
+}
 // `waiter` waits for everything issued so far on `on`
 static void stream_wait(cudaStream_t waiter, cudaStream_t on) {
   static cudaEvent_t ev[16] = {};
@@ -1186,14 +1192,16 @@ static int forward(DcbModel *m, const float *mix_in, int B, int T, float *out, S
 }
 
 // ------------------------------------------------------------------ graph replay
-// Persistent in/out buffers of the forward for a batch shape (allocated once).
-static FwdGraph *forward_slot(DcbModel *m, int B, int T) {
+// Persistent in/out buffers of the forward for a batch shape and slot (allocated once; two
+// slots per shape let consecutive batches overlap, each with its own graph).
+static FwdGraph *forward_slot(DcbModel *m, int B, int T, int idx) {
   for (auto &g : m->graphs)
-    if (g.B == B && g.T == T) return &g;
+    if (g.B == B && g.T == T && g.idx == idx) return &g;
   const Cfg &c = m->cfg;
   FwdGraph g;
   g.B = B;
   g.T = T;
+  g.idx = idx;
   if (cudaMalloc(&g.in, (size_t)B * c.audio_channels * T * 4) != cudaSuccess ||
       cudaMalloc(&g.out, (size_t)B * c.n_sources * c.audio_channels * T * 4) != cudaSuccess) {
     (void)cudaGetLastError();
@@ -1207,7 +1215,7 @@ static FwdGraph *forward_slot(DcbModel *m, int B, int T) {
 // Run the forward on slot->in -> slot->out.  With the "graphs" option the first call runs
 // eagerly (growing every lazily sized scratch buffer and cache), the second records the
 // whole forward into a CUDA graph on a private stream, and every call from then on replays
-// it behind the caller's stream; kernel tracing forces the eager path.
+// it on the caller's stream; kernel tracing forces the eager path.
 static int forward_slot_run(DcbModel *m, FwdGraph *g) {
   Stage none;
   if (!g_opt_graphs || g_trace_mask || !g->warmed) {
@@ -1223,6 +1231,10 @@ static int forward_slot_run(DcbModel *m, FwdGraph *g) {
   const cudaStream_t user = stream();
   if (!g->exec) {
     cudaGraph_t graph = nullptr;
+    const cudaStream_t prev = stream_override_get();
+    // the capture stream starts behind everything issued so far on the caller's stream
+    DCB_CUDA(cudaEventRecord(m->ev_in, user));
+    DCB_CUDA(cudaStreamWaitEvent(m->cap, m->ev_in, 0));
     set_stream_override(m->cap);
     const uint64_t n0 = launches_now();
     cudaError_t e = cudaStreamBeginCapture(m->cap, cudaStreamCaptureModeThreadLocal);
@@ -1231,7 +1243,7 @@ static int forward_slot_run(DcbModel *m, FwdGraph *g) {
       r = forward(m, g->in, g->B, g->T, g->out, none);
       e = cudaStreamEndCapture(m->cap, &graph);
     }
-    set_stream_override(nullptr);
+    set_stream_override(prev);
     if (e != cudaSuccess || r < 0 || !graph) {
       if (graph) cudaGraphDestroy(graph);
       (void)cudaGetLastError();
@@ -1248,11 +1260,7 @@ static int forward_slot_run(DcbModel *m, FwdGraph *g) {
       return -1;
     }
   }
-  DCB_CUDA(cudaEventRecord(m->ev_in, user));
-  DCB_CUDA(cudaStreamWaitEvent(m->cap, m->ev_in, 0));
-  DCB_CUDA(cudaGraphLaunch(g->exec, m->cap));
-  DCB_CUDA(cudaEventRecord(m->ev_out, m->cap));
-  DCB_CUDA(cudaStreamWaitEvent(user, m->ev_out, 0));
+  DCB_CUDA(cudaGraphLaunch(g->exec, user));
   add_launches(g->launches);
   return g->T;
 }
@@ -1491,10 +1499,21 @@ static int apply_window(DcbModel *m, const float *mix, int B, int T, const Sched
     m->ola_pow = power;
   }
   const int rows = B * S * C;
-  for (int kb = 0; kb < (int)sc.batches.size(); kb++) {
+  // consecutive batches alternate between the caller's stream and a second one (each with
+  // its own slot and graph), so one batch's forward overlaps the next one's; the
+  // accumulations into the shared window stay in batch order (each waits for the previous
+  // batch), and the caller's stream joins the second one at the end
+  const int nb = (int)sc.batches.size();
+  const bool ovl = g_opt_streams && nb > 1;
+  const cudaStream_t bs0 = stream();
+  const cudaStream_t bs1 = ovl ? batch_stream() : bs0;
+  if (ovl) stream_wait(bs1, bs0);
+  for (int kb = 0; kb < nb; kb++) {
     const auto &bt = sc.batches[kb];
     const int nbt = (int)bt.size();
-    FwdGraph *slot = forward_slot(m, nbt * B, Lv);
+    const cudaStream_t bsk = (kb & 1) ? bs1 : bs0;
+    OnStream os(bsk, ovl);
+    FwdGraph *slot = forward_slot(m, nbt * B, Lv, ovl ? (kb & 1) : 0);
     if (!slot) return -1;
     BatchItems bi{};
     bi.cnt = nbt;
@@ -1525,6 +1544,7 @@ static int apply_window(DcbModel *m, const float *mix, int B, int T, const Sched
         mix, slot->in, B, C, T, Lv, bi);
     DCB_LAUNCHED();
     if (forward_slot_run(m, slot) < 0) return -1;
+    if (ovl && kb > 0) stream_wait(bsk, (kb & 1) ? bs0 : bs1);  // batch kb - 1 accumulated
     if (t1 > t0) {
       k_accumulate_items<<<grid_for(t1 - t0, 256, 148 * 16), 256, 0, stream()>>>(
           win, ld, sc.lo, slot->out, m->ola_w, rows, Lv, t0, t1, sc.seg, sc.stride, sc.scale,
@@ -1533,6 +1553,7 @@ static int apply_window(DcbModel *m, const float *mix, int B, int T, const Sched
     }
     if (hooks) hooks->after(kb);
   }
+  if (ovl) stream_wait(bs0, bs1);
   return 0;
 }
 
