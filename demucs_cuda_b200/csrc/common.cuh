@@ -54,6 +54,7 @@ cudaStream_t stream_override_get();
 extern int g_opt_simt;
 extern int g_opt_graphs;
 extern int g_opt_streams;
+extern int g_opt_dconv_rows;
 extern int g_opt_generic_epi;  // channels-last convs take the generic epilogue
 
 // device fault word written by bounded waits (see umma.cuh); the library is one

@@ -390,7 +390,62 @@ static void dconv_tail(const DConvW &dw, const float *h, float *y, int B, int C,
 // matrix of the hidden rows (the 1x1 conv output is never formed), and the 1x1 conv runs
 // fused with everything after it: on CUDA cores for hidden widths <= 24, as a tensor-core
 // conv with a GroupNorm + GLU epilogue above.
+// Both DConv layers of a frequency-branch level in one kernel, one CTA per row (b, f), for
+// the first level (k_dconv_rows: C = 48, hid = 6, k3 convs of dilation 1 and 2, rows of at
+// most kDrMaxT positions).  Returns false (nothing launched) otherwise.  (At C = 96 the
+// same kernel is slower than the per-layer path: two CTAs of six warps per SM leave the
+// CUDA-core k3 conv latency-bound.)
+static bool dconv_rows(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int T) {
+  if (g_opt_simt || E.ndconv != 2 || Fr <= 1 || !yh || !yh->p || yh->Wp != T || yh->C != C ||
+      C != 48 || T > kDrMaxT)
+    return false;
+  DconvRowArgs a{};
+  for (int l = 0; l < 2; l++) {
+    const DConvW &dw = E.dconv[l];
+    if (!dw.c0.w || !dw.c3.w || !dw.zc || dw.c0.O != C / 8 || dw.c0.KW != 3 ||
+        dw.c0.KH != 1 || dw.c0.C != C || dw.c3.O != 2 * C)
+      return false;
+    DconvRowLayer &L = a.L[l];
+    L.w0 = dw.c0.w;
+    L.ld0 = dw.c0.ld;
+    L.b0 = dw.c0.bias;
+    L.g1w = dw.gn1.w;
+    L.g1b = dw.gn1.b;
+    L.zc = dw.zc;
+    L.w3 = dw.c3.w;
+    L.ld3 = dw.c3.ld;
+    L.b3 = dw.c3.bias;
+    L.g4w = dw.gn4.w;
+    L.g4b = dw.gn4.b;
+    L.scale = dw.scale;
+    L.dil = 1 << l;
+  }
+  a.y = y;
+  a.yh = yh->p;
+  a.Fr = Fr;
+  a.T = T;
+  a.ysB = (int64_t)C * Fr * T;
+  a.ysC = (int64_t)Fr * T;
+  const int hid = C / 8, hidp = (hid + 3) / 4 * 4;
+  const size_t sm = (size_t)T * (C + 8) * 2 + (size_t)hid * T * 4 +
+                    ((size_t)5 * C * hidp + 7 * (size_t)C) * 4;
+  if (sm > 200 * 1024) return false;
+  const unsigned rows = (unsigned)((int64_t)B * Fr);
+  // minimum bytes: the fp16 row read and written once, y read and written per layer
+  TraceScope ts(TR_DCONV, 0.0, (double)rows * T * C * (2.0 * 2 + 8.0 * 2), rows, C, T);
+  static size_t attr = 0;
+  if (sm > 48 * 1024 && sm > attr) {
+    DCB_CUDA(cudaFuncSetAttribute(k_dconv_rows<48, 6, 8>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    attr = sm;
+  }
+  k_dconv_rows<48, 6, 8><<<rows, kDrThreads, sm, stream()>>>(a);
+  DCB_LAUNCHED();
+  return true;
+}
+
 static void dconv(const EncW &E, float *y, Half16 *yh, int B, int C, int Fr, int T) {
+  if (g_opt_dconv_rows && dconv_rows(E, y, yh, B, C, Fr, T)) return;
   const Img v = freq_rows(B, C, Fr, T);
   const unsigned rows = (unsigned)((int64_t)B * Fr);
   // one CTA per row when there are many short rows (frequency branch); chunked statistics

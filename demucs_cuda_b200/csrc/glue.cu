@@ -507,6 +507,297 @@ __global__ void __launch_bounds__(kDgThreads)
   }
 }
 
+// Both layers of a frequency-branch DConv (layers.c:24-53) for one row (b, f) of T
+// positions per CTA, when the row fits in shared memory (C = 48 or 96, hid = C / 8): the
+// row's fp16 channels-last copy stays in shared memory from the first layer's k3 conv to
+// the second layer's, and per layer the CTA forms h = conv_k3(fp16 y) + b on CUDA cores
+// (products of fp16 values exact in fp32, summed in fp32 as the tensor core does), its
+// GroupNorm(1) statistics (fp64), GELU, fp16(h), the z statistics from the sums and Gram
+// matrix of fp16(h) (see k_gn_gelu_zstats), and the 1x1 conv + GroupNorm + GLU +
+// LayerScale + residual of k_dconv_tail, reading the residual from and writing the result
+// to y; the final fp16 copy goes to yh.  Nothing else touches HBM.
+struct DconvRowLayer {
+  const uint16_t *w0;  // k3 conv weights [hid][ld0], element (o, kw C + c)
+  int64_t ld0;
+  const float *b0, *g1w, *g1b;  // conv bias, first GroupNorm affine [hid]
+  const double *zc;             // z statistics constants (see k_gn_gelu_zstats)
+  const uint16_t *w3;           // 1x1 conv [2C][ld3]
+  int64_t ld3;
+  const float *b3, *g4w, *g4b, *scale;  // [2C], [2C], [2C], [C]
+  int dil;
+};
+struct DconvRowArgs {
+  float *y;      // [B][C][Fr][T]
+  uint16_t *yh;  // [B][Fr][T][C] fp16 (channels-last, T unpadded)
+  int Fr, T;
+  int64_t ysB, ysC;  // y strides of b and c
+  DconvRowLayer L[2];
+};
+// 192 threads, each with positions t and t + 192 of the row (rows up to 384 positions); the
+// row's fp16 copy in shared memory has a pitch of C + 8 halves (an odd number of 16-byte
+// units), so a warp's 16-byte loads of 32 consecutive positions hit distinct banks
+constexpr int kDrThreads = 192;
+constexpr int kDrMaxT = 2 * kDrThreads;
+
+template <int C, int HID, int HIDP>
+__global__ void __launch_bounds__(kDrThreads)
+    k_dconv_rows(const DconvRowArgs a) {
+  static_assert(HIDP % 4 == 0 && HIDP >= HID && C % 8 == 0, "k_dconv_rows shape");
+  constexpr int NPAIR = HID * (HID + 1) / 2, NTOT = NPAIR + HID;
+  constexpr int SP = C + 8;  // pitch of the fp16 row copy (halves)
+  extern __shared__ __align__(16) uint8_t dsm[];
+  const int T = a.T;
+  uint16_t *sy = (uint16_t *)dsm;                        // [T][SP] fp16 y of this row
+  float *sh = (float *)(dsm + (size_t)T * SP * 2);       // [HID][T] h, then fp16(GELU)
+  float *sw0 = sh + (size_t)HID * T;                     // [3][C][HIDP]
+  float *sw3 = sw0 + 3 * C * HIDP;                       // [2C][HIDP]
+  float *sb3 = sw3 + 2 * C * HIDP;                       // [2C]
+  float *sg4w = sb3 + 2 * C, *sg4b = sg4w + 2 * C;       // [2C] each
+  float *ssc = sg4b + 2 * C;                             // [C]
+  __shared__ double dred[2][kDrThreads / 32];
+  __shared__ double dent[kDrThreads];  // Gram partial sums, then the entry totals
+  __shared__ float s_par[4];           // GroupNorm mean / rstd, z mean / rstd
+  const int row = blockIdx.x;
+  const int b = row / a.Fr, f = row - b * a.Fr;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  float *yrow = a.y + (int64_t)b * a.ysB + (int64_t)f * T;  // element (c, t): yrow[c ysC + t]
+  uint16_t *yhrow = a.yh + (int64_t)row * T * C;
+  // the row's fp16 copy into shared memory (16-byte chunks)
+  for (int i = tid; i < T * C / 8; i += kDrThreads) {
+    const int t = i / (C / 8), c8 = i - t * (C / 8);
+    *(uint4 *)(sy + (size_t)t * SP + 8 * c8) = ((const uint4 *)yhrow)[i];
+  }
+  for (int l = 0; l < 2; l++) {
+    const DconvRowLayer &L = a.L[l];
+    // this layer's weights as fp32: k3 conv [kw][c][o], 1x1 conv [c'][j] (o, j padded with 0)
+    for (int i = tid; i < 3 * C * HIDP; i += kDrThreads) {
+      const int o = i % HIDP, c = (i / HIDP) % C, kw = i / (HIDP * C);
+      sw0[i] = o < HID ? h2f_bits(L.w0[(int64_t)o * L.ld0 + kw * C + c]) : 0.f;
+    }
+    for (int i = tid; i < 2 * C * HIDP; i += kDrThreads) {
+      const int j = i % HIDP, c = i / HIDP;
+      sw3[i] = j < HID ? h2f_bits(L.w3[(int64_t)c * L.ld3 + j]) : 0.f;
+    }
+    for (int i = tid; i < 2 * C; i += kDrThreads) {
+      sb3[i] = L.b3[i];
+      sg4w[i] = L.g4w[i];
+      sg4b[i] = L.g4b[i];
+      if (i < C) ssc[i] = L.scale[i];
+    }
+    __syncthreads();
+    // h[o][t] = b0[o] + sum over taps kw and channels c of w0[o][kw][c] y[t + (kw - 1) dil][c]
+    // for this thread's positions t0 = tid and t1 = tid + kDrThreads (every weight load serves
+    // both)
+    double s1 = 0.0, s2 = 0.0;
+    {
+      const int t0 = tid, t1 = tid + kDrThreads;
+      const bool v0 = t0 < T, v1 = t1 < T;
+      float acc0[HIDP], acc1[HIDP];
+#pragma unroll
+      for (int o = 0; o < HIDP; o++) {
+        const float bo = o < HID ? L.b0[o] : 0.f;
+        acc0[o] = bo;
+        acc1[o] = bo;
+      }
+#pragma unroll
+      for (int kw = 0; kw < 3; kw++) {
+        const int ta = t0 + (kw - 1) * L.dil, tb = t1 + (kw - 1) * L.dil;
+        const bool ia = v0 && ta >= 0 && ta < T, ib = v1 && tb >= 0 && tb < T;
+        const uint4 *ya = (const uint4 *)(sy + (size_t)(ia ? ta : 0) * SP);
+        const uint4 *yb = (const uint4 *)(sy + (size_t)(ib ? tb : 0) * SP);
+        const float4 *wp = (const float4 *)(sw0 + (kw * C) * HIDP);
+#pragma unroll 1
+        for (int c8 = 0; c8 < C / 8; c8++) {
+          const uint4 ua = ia ? ya[c8] : make_uint4(0u, 0u, 0u, 0u);
+          const uint4 ub = ib ? yb[c8] : make_uint4(0u, 0u, 0u, 0u);
+          const uint32_t wa[4] = {ua.x, ua.y, ua.z, ua.w}, wb[4] = {ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const float xa = __half2float(__ushort_as_half((uint16_t)(wa[k >> 1] >> (16 * (k & 1)))));
+            const float xb = __half2float(__ushort_as_half((uint16_t)(wb[k >> 1] >> (16 * (k & 1)))));
+#pragma unroll
+            for (int q = 0; q < HIDP / 4; q++) {
+              const float4 w = wp[(8 * c8 + k) * (HIDP / 4) + q];
+              acc0[4 * q] = fmaf(w.x, xa, acc0[4 * q]);
+              acc0[4 * q + 1] = fmaf(w.y, xa, acc0[4 * q + 1]);
+              acc0[4 * q + 2] = fmaf(w.z, xa, acc0[4 * q + 2]);
+              acc0[4 * q + 3] = fmaf(w.w, xa, acc0[4 * q + 3]);
+              acc1[4 * q] = fmaf(w.x, xb, acc1[4 * q]);
+              acc1[4 * q + 1] = fmaf(w.y, xb, acc1[4 * q + 1]);
+              acc1[4 * q + 2] = fmaf(w.z, xb, acc1[4 * q + 2]);
+              acc1[4 * q + 3] = fmaf(w.w, xb, acc1[4 * q + 3]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 0; o < HID; o++) {
+        if (v0) {
+          sh[o * T + t0] = acc0[o];
+          s1 += (double)acc0[o];
+          s2 += (double)acc0[o] * acc0[o];
+        }
+        if (v1) {
+          sh[o * T + t1] = acc1[o];
+          s1 += (double)acc1[o];
+          s2 += (double)acc1[o] * acc1[o];
+        }
+      }
+    }
+    // GroupNorm(1) statistics of h over hid x T (the formulas of k_gn_gelu_zstats)
+    for (int o = 16; o > 0; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    if (lane == 0) {
+      dred[0][wid] = s1;
+      dred[1][wid] = s2;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      double t1 = 0.0, t2 = 0.0;
+      for (int w = 0; w < kDrThreads / 32; w++) {
+        t1 += dred[0][w];
+        t2 += dred[1][w];
+      }
+      const double n = (double)HID * T;
+      const double md = t1 / n;
+      double vd = t2 / n - md * md;
+      if (vd < 0.0) vd = 0.0;
+      s_par[0] = (float)md;
+      s_par[1] = 1.0f / sqrtf((float)vd + 1e-5f);
+    }
+    __syncthreads();
+    {
+      const float m = s_par[0], rs = s_par[1];
+      for (int i = tid; i < HID * T; i += kDrThreads) {
+        const int o = i / T;
+        sh[i] = __half2float(__float2half_rn(gelu_f((sh[i] - m) * rs * L.g1w[o] + L.g1b[o])));
+      }
+    }
+    __syncthreads();
+    // sums S_j and upper Gram entries Q_jk of fp16(h): entry e = tid % NTOT over the
+    // positions t = slice, slice + slices, ..; 32 terms in fp32, the rest in fp64
+    {
+      constexpr int SL = kDrThreads / NTOT > 0 ? kDrThreads / NTOT : 1;
+      double acc = 0.0;
+      if (tid < NTOT * SL) {
+        const int e = tid % NTOT, sl = tid / NTOT;
+        int j, k;
+        if (e < NPAIR) {
+          gram_pair(e, HID, j, k);
+        } else {
+          j = e - NPAIR;
+          k = -1;
+        }
+        const float *hj = sh + j * T, *hk = sh + (k >= 0 ? k : j) * T;
+        const float one = k >= 0 ? 0.f : 1.f;
+        for (int tb = sl; tb < T; tb += 32 * SL) {
+          float a32 = 0.f;
+          const int te = tb + 32 * SL < T ? tb + 32 * SL : T;
+          for (int t = tb; t < te; t += SL) a32 = fmaf(hj[t], fmaf(hk[t], 1.f - one, one), a32);
+          acc += (double)a32;
+        }
+      }
+      dent[tid] = acc;
+      __syncthreads();
+      if (tid < NTOT) {
+        double tot = 0.0;
+        for (int sl = 0; sl < SL; sl++) tot += dent[sl * NTOT + tid];
+        dent[tid] = tot;  // (slice 0's own slot: only this thread reads and writes it)
+      }
+      __syncthreads();
+      // z statistics (zstats_row's sums, from shared memory)
+      const double *G = L.zc, *u = L.zc + HID * HID, *vv = u + HID;
+      double sz = 0.0, szz = 0.0;
+      for (int e = tid; e < NTOT; e += kDrThreads) {
+        if (e < NPAIR) {
+          int j, k;
+          gram_pair(e, HID, j, k);
+          szz += (k == j ? 1.0 : 2.0) * G[j * HID + k] * dent[e];
+        } else {
+          const int j = e - NPAIR;
+          sz += u[j] * dent[e];
+          szz += 2.0 * vv[j] * dent[e];
+        }
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        sz += __shfl_xor_sync(0xffffffffu, sz, o);
+        szz += __shfl_xor_sync(0xffffffffu, szz, o);
+      }
+      __syncthreads();  // (every thread has read dred from the previous use)
+      if (lane == 0) {
+        dred[0][wid] = sz;
+        dred[1][wid] = szz;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        double z1 = 0.0, z2 = 0.0;
+        for (int w = 0; w < kDrThreads / 32; w++) {
+          z1 += dred[0][w];
+          z2 += dred[1][w];
+        }
+        z1 += (double)T * L.zc[HID * HID + 2 * HID];
+        z2 += (double)T * L.zc[HID * HID + 2 * HID + 1];
+        const double nz = (double)(2 * C) * T;
+        const double mz = z1 / nz;
+        double vz = z2 / nz - mz * mz;
+        if (vz < 0.0) vz = 0.0;
+        s_par[2] = (float)mz;
+        s_par[3] = 1.0f / sqrtf((float)vz + 1e-5f);
+      }
+      __syncthreads();
+    }
+    // 1x1 conv + GroupNorm + GLU + LayerScale + residual (k_dconv_tail's arithmetic), one
+    // position per thread; the fp16 copy of the result into shared memory (the next
+    // layer's input) and, after the last layer, to yh
+    {
+      const float mu = s_par[2], rs = s_par[3];
+      for (int t = tid; t < T; t += kDrThreads) {
+        float hv[HIDP];
+#pragma unroll
+        for (int j = 0; j < HIDP; j++) hv[j] = j < HID ? sh[j * T + t] : 0.f;
+        float *yp = yrow + t;
+#pragma unroll 1
+        for (int c0 = 0; c0 < C; c0 += 8) {
+          float yv[8], nv[8];
+#pragma unroll
+          for (int k = 0; k < 8; k++) yv[k] = yp[(int64_t)(c0 + k) * a.ysC];
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const int c = c0 + k;
+            const float4 *wa = (const float4 *)(sw3 + c * HIDP);
+            const float4 *wb = (const float4 *)(sw3 + (C + c) * HIDP);
+            float x = 0.f, g = 0.f;
+#pragma unroll
+            for (int j = 0; j < HIDP / 4; j++) {
+              const float4 p = wa[j], z = wb[j];
+              x = fmaf(p.x, hv[4 * j], x);
+              x = fmaf(p.y, hv[4 * j + 1], x);
+              x = fmaf(p.z, hv[4 * j + 2], x);
+              x = fmaf(p.w, hv[4 * j + 3], x);
+              g = fmaf(z.x, hv[4 * j], g);
+              g = fmaf(z.y, hv[4 * j + 1], g);
+              g = fmaf(z.z, hv[4 * j + 2], g);
+              g = fmaf(z.w, hv[4 * j + 3], g);
+            }
+            x = (x + sb3[c] - mu) * rs * sg4w[c] + sg4b[c];
+            g = (g + sb3[C + c] - mu) * rs * sg4w[C + c] + sg4b[C + c];
+            nv[k] = yv[k] + ssc[c] * (x * __fdividef(1.0f, 1.0f + __expf(-g)));
+          }
+#pragma unroll
+          for (int k = 0; k < 8; k++) yp[(int64_t)(c0 + k) * a.ysC] = nv[k];
+          const uint4 hv8 = make_uint4(pack_h2(nv[0], nv[1]), pack_h2(nv[2], nv[3]),
+                                       pack_h2(nv[4], nv[5]), pack_h2(nv[6], nv[7]));
+          *(uint4 *)(sy + (size_t)t * SP + c0) = hv8;
+          if (l == 1) *(uint4 *)(yhrow + (size_t)t * C + c0) = hv8;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 // DConv tail on CUDA cores for small hidden widths (layers.c:24-53, hid = C / 8 <= 24):
 // y[c] += scale[c] * GLU(GroupNorm(W16 . fp16(h) + b)) per position, with the GroupNorm
 // statistics of each row (b, f) precomputed.  A 1x1 conv of K = hid is a handful of MACs

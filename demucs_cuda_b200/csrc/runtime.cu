@@ -25,6 +25,7 @@ int g_opt_simt = 0;
 int g_opt_graphs = 0;
 int g_opt_generic_epi = 0;
 int g_opt_streams = 1;
+int g_opt_dconv_rows = 1;
 extern int g_stream_istft;
 
 void fail(const char *fmt, ...) {
@@ -248,6 +249,10 @@ int dcb_set_option(const char *name, int value) {
     // 1: the time branch's layers run on a second stream beside the frequency branch's
     old = g_opt_streams;
     g_opt_streams = value;
+  } else if (!strcmp(name, "dconv_rows")) {
+    // 1: frequency-branch DConv levels that fit take the fused one-CTA-per-row kernel
+    old = g_opt_dconv_rows;
+    g_opt_dconv_rows = value;
   } else if (!strcmp(name, "generic_epilogue")) {
     old = g_opt_generic_epi;
     g_opt_generic_epi = value;

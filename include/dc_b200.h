@@ -196,7 +196,11 @@ void *dcb_get_stream(void);
  * "graphs" (1 = replay captured CUDA graphs for repeated forwards), "generic_epilogue"
  * (1 = channels-last convs use their generic epilogue instead of the specialised ones, for
  * A/B checks), "stream_istft" (0 = the two-pass inverse STFT instead of the fused
- * streaming one, for A/B checks), "wait_limit_ms" (limit of every bounded device-side
+ * streaming one, for A/B checks), "streams" (1, the default = the time branch's layers on
+ * a second stream beside the frequency branch's, and consecutive dcb_apply batches on two
+ * alternating streams; 0 = one stream), "dconv_rows" (1, the default = both DConv layers of
+ * the first frequency level in one kernel, one CTA per row; 0 = the per-layer path),
+ * "wait_limit_ms" (limit of every bounded device-side
  * wait, default 2000; tests shorten it), "test_withhold_arrive" (1 = the next tensor-core
  * GEMM CTA does not release its first operand stage, so a bounded wait expires and sets
  * the device fault word: the failure-detection test).  Returns the old value. */

@@ -245,3 +245,36 @@ def test_short_two_streams_match_one(short):
     print(f"two streams vs one: rel_l2 {e:.3e}")
     assert e < 1e-6
     assert dcb.device_fault() == 0
+
+
+def test_short_fused_dconv_rows_match_per_layer(short):
+    """The fused frequency-branch DConv (both layers of a level in one kernel, one CTA per
+    row, k3 conv on CUDA cores, statistics in the CTA) gives the per-layer path's result
+    (tensor-core k3 conv, statistics across CTAs): the two sum the k3 conv's exact fp16
+    products in different orders, so a few fp16 roundings of h (the 1x1 conv's operand) and
+    of y's companion land on the other side of a tie; the teacher-forced encoder stages
+    agree to about 5e-5 and the stems well inside the path's fp16 noise (each path is
+    checked against the reference by the stage tests)."""
+    import demucs_cuda_b200 as dcb
+    torch = short["torch"]
+    m, R = short["model"], short["ref"]
+
+    def run():
+        out = {"stems": m.forward(_t(torch, short["mix"])).cpu().numpy()}
+        for i in range(4):
+            xin = R["x_norm"] if i == 0 else R[f"enc_{i - 1}"]
+            out[f"enc_{i}"] = m.stage_encoder(0, i, _t(torch, xin)).cpu().numpy()
+        return out
+
+    fused = run()
+    old = dcb.set_option("dconv_rows", 0)
+    try:
+        per_layer = run()
+    finally:
+        dcb.set_option("dconv_rows", old)
+    errs = {k: rel_l2(fused[k], per_layer[k]) for k in fused}
+    for k, v in errs.items():
+        print(f"  fused vs per-layer DConv {k:8s} {v:.3e}")
+    assert errs.pop("stems") < 2e-4
+    assert max(errs.values()) < 2e-4, errs
+    assert dcb.device_fault() == 0
