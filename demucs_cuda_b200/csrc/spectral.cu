@@ -485,15 +485,30 @@ __global__ void __launch_bounds__(kFftThreads, 4)
                        int NF, const float *__restrict__ window,
                        const float2 *__restrict__ tw, int64_t start, int64_t length,
                        int g_first, const StreamCombine cb) {
-  extern __shared__ float2 sbuf[];  // [kFftPadded] FFT buffer, then the ring [4][1024]
+  // [kFftPadded] FFT buffer, then the ring [4][1024], then 1 / (sum of the squared window
+  // over the four frames covering a sample) for the hops whose four frames all exist
+  extern __shared__ float2 sbuf[];
   float2 *buf = sbuf;
   float *ring = (float *)(sbuf + kFftPadded);
+  float *sinv = ring + 4 * 1024;
   constexpr int n = kFftN, hop = 1024;
   const int64_t r = blockIdx.y;
   const int k0 = g_first + blockIdx.x * kStreamHops;  // first output hop of this CTA
   const int k1 = min(k0 + kStreamHops, NF + 3);       // hops past NF + 2 hold no samples
   const float inv_n = 1.0f / (float)n;
   for (int i = threadIdx.x; i < 4 * hop; i += kFftThreads) ring[i] = 0.f;
+  for (int w = threadIdx.x; w < hop; w += kFftThreads) {
+    float den = 0.f;  // ascending frames (i = 3 .. 0), as below
+#pragma unroll
+    for (int i = 3; i >= 0; i--) {
+      const float wv = window[i * hop + w];
+      den += wv * wv;
+    }
+    sinv[w] = den > 0.f ? 1.0f / den : 0.f;
+  }
+  // the output stage's constants of this row
+  const float cb_sd = cb.y ? sqrtf(cb.var[r / cb.rows]) + cb.eps : 0.f;
+  const float cb_mu = cb.y ? cb.mean[r / cb.rows] : 0.f;
   int g = k0 - 3 < 0 ? 0 : k0 - 3;
   __syncthreads();
   for (; g < k1; g += 2) {
@@ -545,27 +560,30 @@ __global__ void __launch_bounds__(kFftThreads, 4)
       // every frame covering them
       if (ge >= k0) {
         float *slot = ring + ((ge & 3) << 10);
+        const bool inner = ge >= 3 && ge <= NF - 1;  // all four frames of the hop exist
         for (int w = threadIdx.x; w < hop; w += kFftThreads) {
           const int64_t idx = (int64_t)ge * hop + w;
           const int64_t t = idx - start;
           if (t >= 0 && t < length) {
-            float den = 0.f;  // ascending frames, as the two-pass overlap-add sums
+            float val;
+            if (inner) {
+              val = slot[w] * sinv[w];
+            } else {
+              float den = 0.f;  // ascending frames, as the two-pass overlap-add sums
 #pragma unroll
-            for (int i = 3; i >= 0; i--) {
-              const int gi = ge - i;
-              if (gi >= 0 && gi < NF) {
-                const float wv = window[i * hop + w];
-                den += wv * wv;
+              for (int i = 3; i >= 0; i--) {
+                const int gi = ge - i;
+                if (gi >= 0 && gi < NF) {
+                  const float wv = window[i * hop + w];
+                  den += wv * wv;
+                }
               }
+              val = den > 0.f ? slot[w] / den : 0.f;
             }
-            const float val = den > 0.f ? slot[w] / den : 0.f;
             if (cb.y) {
               const int64_t tt = t - cb.off;
-              if (tt >= 0 && tt < cb.keep) {
-                const int64_t b = r / cb.rows;
-                cb.y[r * cb.keep + tt] =
-                    fmaf(cb.xt[r * cb.Lt + tt], sqrtf(cb.var[b]) + cb.eps, cb.mean[b]) + val;
-              }
+              if (tt >= 0 && tt < cb.keep)
+                cb.y[r * cb.keep + tt] = fmaf(cb.xt[r * cb.Lt + tt], cb_sd, cb_mu) + val;
             } else {
               out[r * length + t] = val;
             }
@@ -608,7 +626,7 @@ void ispec_frames(const float2 *z, float *out, int64_t R, int F, int N, const fl
   const int g_first = (int)(start / hop);
   const int g_last = (int)((start + length - 1) / hop);
   const int runs = (g_last - g_first + kStreamHops) / kStreamHops;
-  const size_t sm = (size_t)kFftPadded * sizeof(float2) + 4 * 1024 * sizeof(float);
+  const size_t sm = (size_t)kFftPadded * sizeof(float2) + 5 * 1024 * sizeof(float);
   static bool attr = false;
   if (!attr) {
     DCB_CUDA(cudaFuncSetAttribute(k_istft_stream4096,
