@@ -3,7 +3,7 @@
 // [GEMM S = Q K^T -> dk_softmax_to_half -> GEMM O = P V] loop (ops.c:390-443,
 // attn.cu:26-89).
 //
-// CTA = 128 query rows of one head, 320 threads, key blocks of 64:
+// CTA = 128 query rows of one head, 384 threads, key blocks of 64:
 //   warps 0-7  softmax: warp w serves TMEM lane quarter q = w & 3 (query rows 32 q .. +31,
 //              one per lane) and the key blocks of parity h = w >> 2: the two warps of a
 //              quarter take alternate blocks, each with its own running maximum, O
@@ -13,13 +13,14 @@
 //              maximum grows by more than 2^kLazyLog2), P written as fp16 into its parity's
 //              shared-memory buffer in the UMMA A-operand layout.  At the end the pair
 //              exchanges maxima once and combines O = (O_0 a_0 + O_1 a_1) / (l_0 a_0 + l_1 a_1);
-//   warp 8     TMA producers: lane 0 Q once, then K blocks into a 4-stage ring (a stage is
-//              free once S of its block has completed); lane 1 V^T blocks into a 3-stage
-//              ring (free once P V of its block has completed);
-//   warp 9     TMEM owner; lane h issues, for the blocks j of parity h, S(j) = Q K(j)^T
-//              (M=128, N=64, K=hd) into score buffer h and O_h += P(j) V(j), l_h += P(j) 1
-//              (M=128, N=hd / 16, K=64).  S(j + 2) is issued as soon as the parity's warps
-//              have read S(j) out of TMEM, so it runs while they exponentiate block j.
+//   warp 8     TMA producer: Q once, then K blocks into a 4-stage ring (a stage is free
+//              once S of its block has completed); warp 11: V^T blocks into a 3-stage ring
+//              (free once P V of its block has completed);
+//   warps 9-10 MMA issue (warp 9 also owns the TMEM allocation): lane 0 of warp 9 + h
+//              issues, for the blocks j of parity h, S(j) = Q K(j)^T (M=128, N=64, K=hd)
+//              into score buffer h and O_h += P(j) V(j), l_h += P(j) 1 (M=128, N=hd / 16,
+//              K=64).  S(j + 2) is issued as soon as the parity's warps have read S(j) out
+//              of TMEM, so it runs while they exponentiate block j.
 // TMEM: S_0 | S_1 | O_0 | O_1 | l_0 | l_1 (64 + 64 + 2 x 16 ceil(hd / 16) + 2 x 16 columns):
 // 256 for head dims up to 48 (two CTAs share an SM), 512 above; 109 KB of shared memory.
 // Head dims up to 64 are zero-extended to a multiple of 16 (the MMA K of S and N of P V) by
@@ -37,8 +38,12 @@
 
 namespace dcb {
 
-constexpr int kAttnThreads = 320;
-constexpr int kSoftWarps = 8, kLoadWarp = 8, kMmaWarpA = 9;
+constexpr int kAttnThreads = 384;
+// one issuing thread per warp (lane 0) for each asynchronous role: warp 8 loads Q and K,
+// warp 11 loads V^T, warp 9 (also the TMEM owner) issues parity 0's MMAs and warp 10
+// parity 1's, so no two lanes of one warp ever issue a TMA copy, a tcgen05.mma or a
+// tcgen05.commit together
+constexpr int kSoftWarps = 8, kLoadWarp = 8, kMmaWarpA = 9, kMmaWarpB = 10, kVWarp = 11;
 constexpr int kQ = 128, kKV = 64, kHD = 64;
 constexpr uint32_t kQBytes = kQ * kHD * 2;      // 16 KB
 constexpr uint32_t kKBytes = kKV * kHD * 2;     // 8 KB
@@ -175,7 +180,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   const uint32_t tL = tO + 2 * ow;        // l_h at tL + 16 h
 
   if (warp == kLoadWarp) {
-    // two independent producer loops on two lanes of this warp
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -188,7 +192,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         mbar_expect_tx(&k_full[st], kKBytes);
         tma_load_3d(sK + st * kKBytes, &tmK, &k_full[st], 0, j * kKV, bh);
       }
-    } else if (lane == 1) {
+    }
+  } else if (warp == kVWarp) {
+    if (lane == 0) {
       tma_prefetch_desc(&tmV);
       for (int j = 0; j < nkv; j++) {
         const int st = j % kVStages;
@@ -198,12 +204,12 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         tma_load_3d(sV + st * kVBytes, &tmV, &v_full[st], j * kKV, 0, bh);
       }
     }
-  } else if (warp == kMmaWarpA) {
-    // two issuing lanes, one per block parity h, each on its own chain (S(j + 2) once the
+  } else if (warp == kMmaWarpA || warp == kMmaWarpB) {
+    // two issuing warps, one per block parity h, each on its own chain (S(j + 2) once the
     // parity's warps have read S(j), P V(j) once they have written P(j)), so neither parity
     // waits for the other's softmax
-    if (lane < 2) {
-      const int h = lane;
+    if (lane == 0) {
+      const int h = warp - kMmaWarpA;
       const uint32_t id_s = idesc_f16_f32(kQ, kKV);
       const uint32_t id_o = idesc_f16_f32(kQ, 16 * hd16);
       const uint32_t id_l = idesc_f16_f32(kQ, 16);
@@ -247,7 +253,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         umma_commit(&pv_done[h]);
         umma_commit(&v_empty[sv]);
       }
-      umma_commit(o_full);  // (two arrivals: every MMA of both lanes)
+      umma_commit(o_full);  // (two arrivals: every MMA of both issuing warps)
     }
   } else {
     // softmax warps: warp w serves query rows 32 q .. 32 q + 31 (q = w & 3, the TMEM lane

@@ -109,6 +109,19 @@ static __device__ __forceinline__ uint16_t f2h_bits(float v) {
 static __device__ __forceinline__ float h2f_bits(uint16_t h) {
   return __half2float(__ushort_as_half(h));
 }
+// (c0, c1) += (a0, a1) * (b0, b1) by one packed fp32 FMA (sm_100 fma.rn.f32x2; each lane
+// rounds as fmaf does)
+static __device__ __forceinline__ void ffma2(float &c0, float &c1, float a0, float a1, float b0,
+                                             float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%0, %1};\n\t"
+      "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
 // two floats -> packed fp16x2 (low = a)
 static __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   // one packed conversion (both halves round to nearest even): d = {hi: b, lo: a}

@@ -540,7 +540,7 @@ constexpr int kDrThreads = 192;
 constexpr int kDrMaxT = 2 * kDrThreads;
 
 template <int C, int HID, int HIDP>
-__global__ void __launch_bounds__(kDrThreads)
+__global__ void __launch_bounds__(kDrThreads, 4)
     k_dconv_rows(const DconvRowArgs a) {
   static_assert(HIDP % 4 == 0 && HIDP >= HID && C % 8 == 0, "k_dconv_rows shape");
   constexpr int NPAIR = HID * (HID + 1) / 2, NTOT = NPAIR + HID;
@@ -617,15 +617,12 @@ __global__ void __launch_bounds__(kDrThreads)
             const float xb = __half2float(__ushort_as_half((uint16_t)(wb[k >> 1] >> (16 * (k & 1)))));
 #pragma unroll
             for (int q = 0; q < HIDP / 4; q++) {
+              // both positions per instruction (packed FMA, each lane rounds as fmaf)
               const float4 w = wp[(8 * c8 + k) * (HIDP / 4) + q];
-              acc0[4 * q] = fmaf(w.x, xa, acc0[4 * q]);
-              acc0[4 * q + 1] = fmaf(w.y, xa, acc0[4 * q + 1]);
-              acc0[4 * q + 2] = fmaf(w.z, xa, acc0[4 * q + 2]);
-              acc0[4 * q + 3] = fmaf(w.w, xa, acc0[4 * q + 3]);
-              acc1[4 * q] = fmaf(w.x, xb, acc1[4 * q]);
-              acc1[4 * q + 1] = fmaf(w.y, xb, acc1[4 * q + 1]);
-              acc1[4 * q + 2] = fmaf(w.z, xb, acc1[4 * q + 2]);
-              acc1[4 * q + 3] = fmaf(w.w, xb, acc1[4 * q + 3]);
+              ffma2(acc0[4 * q], acc1[4 * q], w.x, w.x, xa, xb);
+              ffma2(acc0[4 * q + 1], acc1[4 * q + 1], w.y, w.y, xa, xb);
+              ffma2(acc0[4 * q + 2], acc1[4 * q + 2], w.z, w.z, xa, xb);
+              ffma2(acc0[4 * q + 3], acc1[4 * q + 3], w.w, w.w, xa, xb);
             }
           }
         }
@@ -748,49 +745,85 @@ __global__ void __launch_bounds__(kDrThreads)
       }
       __syncthreads();
     }
-    // 1x1 conv + GroupNorm + GLU + LayerScale + residual (k_dconv_tail's arithmetic), one
-    // position per thread; the fp16 copy of the result into shared memory (the next
-    // layer's input) and, after the last layer, to yh
+    // 1x1 conv + GroupNorm + GLU + LayerScale + residual (k_dconv_tail's arithmetic) for this
+    // thread's positions t0 and t1 = t0 + kDrThreads together, 8 channels at a time with the
+    // next 8 channels' residuals loaded ahead (the residual loads are the tail's latency);
+    // the fp16 copy of the result into shared memory (the next layer's input) and, after
+    // the last layer, to yh
     {
       const float mu = s_par[2], rs = s_par[3];
-      for (int t = tid; t < T; t += kDrThreads) {
-        float hv[HIDP];
+      const int t0 = tid, t1 = tid + kDrThreads;
+      const bool v0 = t0 < T, v1 = t1 < T;
+      float h0[HIDP], h1[HIDP];
 #pragma unroll
-        for (int j = 0; j < HIDP; j++) hv[j] = j < HID ? sh[j * T + t] : 0.f;
-        float *yp = yrow + t;
+      for (int j = 0; j < HIDP; j++) {
+        h0[j] = j < HID && v0 ? sh[j * T + t0] : 0.f;
+        h1[j] = j < HID && v1 ? sh[j * T + t1] : 0.f;
+      }
+      float *yp0 = yrow + (v0 ? t0 : 0), *yp1 = yrow + (v1 ? t1 : 0);
+      float yn0[8], yn1[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        yn0[k] = v0 ? yp0[(int64_t)k * a.ysC] : 0.f;
+        yn1[k] = v1 ? yp1[(int64_t)k * a.ysC] : 0.f;
+      }
 #pragma unroll 1
-        for (int c0 = 0; c0 < C; c0 += 8) {
-          float yv[8], nv[8];
+      for (int c0 = 0; c0 < C; c0 += 8) {
+        float y0[8], y1[8];
 #pragma unroll
-          for (int k = 0; k < 8; k++) yv[k] = yp[(int64_t)(c0 + k) * a.ysC];
+        for (int k = 0; k < 8; k++) {
+          y0[k] = yn0[k];
+          y1[k] = yn1[k];
+        }
+        if (c0 + 8 < C) {
 #pragma unroll
           for (int k = 0; k < 8; k++) {
-            const int c = c0 + k;
-            const float4 *wa = (const float4 *)(sw3 + c * HIDP);
-            const float4 *wb = (const float4 *)(sw3 + (C + c) * HIDP);
-            float x = 0.f, g = 0.f;
-#pragma unroll
-            for (int j = 0; j < HIDP / 4; j++) {
-              const float4 p = wa[j], z = wb[j];
-              x = fmaf(p.x, hv[4 * j], x);
-              x = fmaf(p.y, hv[4 * j + 1], x);
-              x = fmaf(p.z, hv[4 * j + 2], x);
-              x = fmaf(p.w, hv[4 * j + 3], x);
-              g = fmaf(z.x, hv[4 * j], g);
-              g = fmaf(z.y, hv[4 * j + 1], g);
-              g = fmaf(z.z, hv[4 * j + 2], g);
-              g = fmaf(z.w, hv[4 * j + 3], g);
-            }
-            x = (x + sb3[c] - mu) * rs * sg4w[c] + sg4b[c];
-            g = (g + sb3[C + c] - mu) * rs * sg4w[C + c] + sg4b[C + c];
-            nv[k] = yv[k] + ssc[c] * (x * __fdividef(1.0f, 1.0f + __expf(-g)));
+            yn0[k] = v0 ? yp0[(int64_t)(c0 + 8 + k) * a.ysC] : 0.f;
+            yn1[k] = v1 ? yp1[(int64_t)(c0 + 8 + k) * a.ysC] : 0.f;
           }
+        }
+        float n0[8], n1[8];
 #pragma unroll
-          for (int k = 0; k < 8; k++) yp[(int64_t)(c0 + k) * a.ysC] = nv[k];
-          const uint4 hv8 = make_uint4(pack_h2(nv[0], nv[1]), pack_h2(nv[2], nv[3]),
-                                       pack_h2(nv[4], nv[5]), pack_h2(nv[6], nv[7]));
-          *(uint4 *)(sy + (size_t)t * SP + c0) = hv8;
-          if (l == 1) *(uint4 *)(yhrow + (size_t)t * C + c0) = hv8;
+        for (int k = 0; k < 8; k++) {
+          const int c = c0 + k;
+          const float4 *wa = (const float4 *)(sw3 + c * HIDP);
+          const float4 *wb = (const float4 *)(sw3 + (C + c) * HIDP);
+          float x0 = 0.f, g0 = 0.f, x1 = 0.f, g1 = 0.f;
+#pragma unroll
+          for (int j = 0; j < HIDP / 4; j++) {
+            // the GLU's two halves per instruction (packed FMA, each lane rounds as fmaf)
+            const float4 p = wa[j], z = wb[j];
+            ffma2(x0, g0, p.x, z.x, h0[4 * j], h0[4 * j]);
+            ffma2(x0, g0, p.y, z.y, h0[4 * j + 1], h0[4 * j + 1]);
+            ffma2(x0, g0, p.z, z.z, h0[4 * j + 2], h0[4 * j + 2]);
+            ffma2(x0, g0, p.w, z.w, h0[4 * j + 3], h0[4 * j + 3]);
+            ffma2(x1, g1, p.x, z.x, h1[4 * j], h1[4 * j]);
+            ffma2(x1, g1, p.y, z.y, h1[4 * j + 1], h1[4 * j + 1]);
+            ffma2(x1, g1, p.z, z.z, h1[4 * j + 2], h1[4 * j + 2]);
+            ffma2(x1, g1, p.w, z.w, h1[4 * j + 3], h1[4 * j + 3]);
+          }
+          x0 = (x0 + sb3[c] - mu) * rs * sg4w[c] + sg4b[c];
+          g0 = (g0 + sb3[C + c] - mu) * rs * sg4w[C + c] + sg4b[C + c];
+          x1 = (x1 + sb3[c] - mu) * rs * sg4w[c] + sg4b[c];
+          g1 = (g1 + sb3[C + c] - mu) * rs * sg4w[C + c] + sg4b[C + c];
+          n0[k] = y0[k] + ssc[c] * (x0 * __fdividef(1.0f, 1.0f + __expf(-g0)));
+          n1[k] = y1[k] + ssc[c] * (x1 * __fdividef(1.0f, 1.0f + __expf(-g1)));
+        }
+        if (v0) {
+#pragma unroll
+          for (int k = 0; k < 8; k++) yp0[(int64_t)(c0 + k) * a.ysC] = n0[k];
+          const uint4 q0 = make_uint4(pack_h2(n0[0], n0[1]), pack_h2(n0[2], n0[3]),
+                                      pack_h2(n0[4], n0[5]), pack_h2(n0[6], n0[7]));
+          *(uint4 *)(sy + (size_t)t0 * SP + c0) = q0;
+          if (l == 1) *(uint4 *)(yhrow + (size_t)t0 * C + c0) = q0;
+        }
+        if (v1) {
+#pragma unroll
+          for (int k = 0; k < 8; k++) yp1[(int64_t)(c0 + k) * a.ysC] = n1[k];
+          const uint4 q1 = make_uint4(pack_h2(n1[0], n1[1]), pack_h2(n1[2], n1[3]),
+                                      pack_h2(n1[4], n1[5]), pack_h2(n1[6], n1[7]));
+          *(uint4 *)(sy + (size_t)t1 * SP + c0) = q1;
+          if (l == 1) *(uint4 *)(yhrow + (size_t)t1 * C + c0) = q1;
         }
       }
     }
