@@ -329,9 +329,12 @@ def b200_arm(args):
     step_e2e()
     ms_e2e, _, _ = timed(step_e2e, args.steps)
     # per-kernel-class CUDA events for the roofline: a separate eager pass (tracing
-    # bypasses the graph), so the headline numbers above carry no event overhead
+    # bypasses the graph), so the headline numbers above carry no event overhead; it runs
+    # on one stream, so no event pair also times a kernel of the other branch
+    dcb.set_option("streams", 0)
     step()
     ms_tr, _, tr = timed(step, args.steps, trace=True)
+    dcb.set_option("streams", 0 if args.one_stream else 1)
     fault = dcb.device_fault()
 
     audio = float(args.seconds) * max(1, 1)  # one track per step, whole job
@@ -367,7 +370,8 @@ def b200_arm(args):
                  "algorithmic_flops_per_launch": fl_launch,
                  "algorithmic_bytes_per_launch": by_launch})
     # shares: each class's kernel time per step (CUDA events around its launches in the
-    # traced eager pass) over the graph-replayed step time of the headline value; the traced
+    # traced one-stream eager pass) over the graph-replayed step time of the headline value,
+    # whose two branch streams overlap kernels (so the shares can sum above 1); the traced
     # pass itself runs host-bound (eager launches plus two events per traced launch)
     classes = {k: {"share_of_step": v["ms"] / args.steps / ms,
                    "tflops": v["flops"] / (v["ms"] * 1e-3) / 1e12 if v["ms"] else 0.0,
