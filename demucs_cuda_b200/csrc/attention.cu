@@ -67,10 +67,10 @@ struct AttnArgs {
 };
 
 
-// 2^x of two fp16 values (PTX ex2.approx.f16x2)
-static __device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+// 2^x in fp32 on the special-function unit (PTX ex2.approx.ftz.f32; 2^-inf = +0)
+static __device__ __forceinline__ float ex2_f32(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 // (x0, x1) = (a0, a1) * s + c by one packed fp32 FMA (sm_100 fma.rn.f32x2; each lane rounds
@@ -261,10 +261,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     // all 64 keys of each; exp2 domain (scores scaled by scale * log2 e).  The running
     // maximum m is only raised, and O_h (in TMEM) rescaled, when a block's maximum exceeds
     // it by more than kLazyLog2: probabilities stay <= 4 and most blocks need no rescale.
-    // P = 2^(s - m) is evaluated two at a time in fp16 (packed fp32 FMA for the exponent,
-    // ex2.approx.f16x2 of its fp16 rounding: at most 2^-11 * 2 error in the exponent of the
-    // largest probabilities), the operand precision P V uses anyway; the row sums come from
-    // the tensor core (P times a ones tile).  tcgen05.ld / st are warp-collective
+    // P = 2^(s - m) takes its exponent two at a time by packed fp32 FMA, is evaluated in
+    // fp32 (ex2.approx) and rounded to fp16, the operand precision P V uses anyway; the row
+    // sums come from the tensor core (P times a ones tile).  tcgen05.ld / st are warp-collective
     // (.sync.aligned): every decision in front of a TMEM access is warp-uniform (a wait's
     // outcome through warp_all, the rescale through __any_sync).
     const int q = warp & 3, h = warp >> 2;
@@ -321,7 +320,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       for (int i = 0; i < 32; i++) {
         float x0, x1;
         fma2(x0, x1, v[2 * i], v[2 * i + 1], sl2, nm);
-        w[i] = ex2_h2(pack_h2(x0, x1));
+        w[i] = pack_h2(ex2_f32(x0), ex2_f32(x1));
       }
       // P buffer h and O_h are free once that P V has completed
       if (u > 0 && !warp_all(mbar_wait(&pv_done[h], (u - 1) & 1u, kFaultAttn))) {

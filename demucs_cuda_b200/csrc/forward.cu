@@ -928,18 +928,22 @@ static void tlayer_branch(DcbModel *m, const TLayerW &tl, float *x, int B, int T
   eg.out = b.hid;
   eg.ldo = tl.lin2.ld;
   linear_rows(tl.lin1, b.ln, R, eg);
+  // GroupNorm(1) over [Tq, D] per batch, affine on D (norm_out): linear2's epilogue sums
+  // each batch item's Tq rows of the updated x (fp64 sums, zeroed here), the apply pass
+  // forms the mean and variance from them
+  static_assert(kStatSlots == kSumSlots, "row-group sums: slot counts of producer and consumer");
+  double *gs = (double *)dalloc((size_t)B * kStatSlots * 4);
+  DCB_CUDA(cudaMemsetAsync(gs, 0, (size_t)B * kStatSlots * 2 * sizeof(double), stream()));
   Epi e3 = er;
   e3.gamma = tl.gamma2;
+  e3.row_stats = gs;
+  e3.stat_rows = Tq;
   linear_rows(tl.lin2, b.hid, R, e3);
-  // GroupNorm(1) over [Tq, D] per batch, affine on D (norm_out)
-  float *st = dalloc((size_t)B * 2);
   {
-    TraceScope ts(TR_NORM, 0.0, (double)B * Tq * D * 12.0, B, D, Tq);  // stats + apply
-    row_stats(x, B, (int64_t)Tq * D, st, st + B);
-    dk_norm_apply_last(x, x, st, st + B, tl.norm_out.w, tl.norm_out.b, B, (int64_t)Tq * D, D,
-                       1e-5f);
+    TraceScope ts(TR_NORM, 0.0, (double)B * Tq * D * 8.0, B, D, Tq);  // apply
+    norm_apply_last_sums(x, x, gs, tl.norm_out.w, tl.norm_out.b, B, (int64_t)Tq * D, D, 1e-5f);
   }
-  dfree(st);
+  dfree(gs);
 }
 
 // dc_crosstransformer (transformer.c:160-216): x [B, C, Fr, T1], xt [B, C, T2] in place.

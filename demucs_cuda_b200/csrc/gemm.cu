@@ -273,6 +273,33 @@ static __device__ __forceinline__ void ld_cols16(const float *p, float (&d)[16])
 // Row-mode epilogue (EPI_ROWS_F32 / EPI_ROWS_F16 / EPI_HEADS) for 16-byte aligned outputs
 // and column constants (e.cvec, checked on the host): bias / gamma and the residual row
 // are loaded while the accumulator load is in flight.
+// e.row_stats in row mode: add a warp's output sums to their groups of e.stat_rows rows
+// (fp32 per lane over its columns, fp64 across lanes) in this CTA's slot; one atomic pair
+// per warp when all its valid rows share a group, per lane otherwise
+static __device__ __forceinline__ void rows_stats_add(const Epi &e, bool mv, int64_t m,
+                                                      float ls, float lq) {
+  const int lane = threadIdx.x & 31;
+  double *st = e.row_stats + 2 * (blockIdx.x % kStatSlots);
+  const unsigned valid = __ballot_sync(0xffffffffu, mv);
+  if (!valid) return;
+  const int64_t g = mv ? m / e.stat_rows : -1;
+  const int64_t g0 = __shfl_sync(0xffffffffu, g, __ffs(valid) - 1);
+  if (__all_sync(0xffffffffu, !mv || g == g0)) {
+    double s = mv ? (double)ls : 0.0, q = mv ? (double)lq : 0.0;
+    for (int o = 16; o > 0; o >>= 1) {
+      s += __shfl_xor_sync(0xffffffffu, s, o);
+      q += __shfl_xor_sync(0xffffffffu, q, o);
+    }
+    if (lane == 0) {
+      atomicAdd(&st[2 * kStatSlots * g0], s);
+      atomicAdd(&st[2 * kStatSlots * g0 + 1], q);
+    }
+  } else if (mv) {
+    atomicAdd(&st[2 * kStatSlots * g], (double)ls);
+    atomicAdd(&st[2 * kStatSlots * g + 1], (double)lq);
+  }
+}
+
 template <int BN, int NW>
 static __device__ __forceinline__ void rows_epi_fast(const Shape &s, const Epi &e,
                                                      uint32_t trow, int half, int r, int64_t m,
@@ -281,6 +308,7 @@ static __device__ __forceinline__ void rows_epi_fast(const Shape &s, const Epi &
   const RowInfo ri = mv ? decode_row(e, m) : RowInfo{0, 0, 0, 0, 0};
   constexpr int PER = NW == 8 ? (BN / 2 < 16 ? 16 : BN / 2) : BN;
   const int cbeg = NW == 8 ? half * PER : 0;
+  float ls = 0.f, lq = 0.f;  // e.row_stats: this lane's sums over its columns
   for (int c0 = cbeg; c0 < cbeg + PER && c0 < BN; c0 += 16) {
     const int64_t n = (int64_t)n0 + c0;
     if (n >= s.N) break;
@@ -324,6 +352,16 @@ static __device__ __forceinline__ void rows_epi_fast(const Shape &s, const Epi &
 #pragma unroll
         for (int j = 0; j < 4; j++)
           op[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        if (e.row_stats) {
+          const int nv = s.N - n < 16 ? (int)(s.N - n) : 16;
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            if (i < nv) {
+              ls += v[i];
+              lq = fmaf(v[i], v[i], lq);
+            }
+          }
+        }
       }
     } else {
       tmem_wait_ld();
@@ -363,6 +401,7 @@ static __device__ __forceinline__ void rows_epi_fast(const Shape &s, const Epi &
       }
     }
   }
+  if (e.mode == EPI_ROWS_F32 && e.row_stats) rows_stats_add(e, mv, m, ls, lq);
 }
 
 template <int BN, int NW, int CW, int EK>
@@ -2161,8 +2200,41 @@ void gemm_rows(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch,
   }
 }
 
+// e.row_stats of a row-mode output the specialised epilogue did not cover: one warp per
+// output row, fp32 over the row, fp64 atomics into its group's sums
+__global__ void k_rows_group_sums(const float *__restrict__ out, int64_t ldo, int64_t M,
+                                  int64_t N, int64_t grp, double *__restrict__ sums) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (r >= M) return;
+  float ls = 0.f, lq = 0.f;
+  for (int64_t c = lane; c < N; c += 32) {
+    const float v = out[r * ldo + c];
+    ls += v;
+    lq = fmaf(v, v, lq);
+  }
+  double s = ls, q = lq;
+  for (int o = 16; o > 0; o >>= 1) {
+    s += __shfl_xor_sync(0xffffffffu, s, o);
+    q += __shfl_xor_sync(0xffffffffu, q, o);
+  }
+  if (lane == 0) {
+    double *st = sums + 2 * (kStatSlots * (r / grp) + blockIdx.x % kStatSlots);
+    atomicAdd(&st[0], s);
+    atomicAdd(&st[1], q);
+  }
+}
+
+static void rows_group_sums(const Epi &e, int64_t M, int64_t N) {
+  k_rows_group_sums<<<grid_for(M * 32, 256, 1 << 30), 256, 0, stream()>>>(
+      (const float *)e.out, e.ldo, M, N, e.stat_rows, e.row_stats);
+  DCB_LAUNCHED();
+}
+
 void gemm_rows_launch(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t batch,
                       const Epi &e, Shape s, Gather g) {
+  DCB_REQUIRE(!e.row_stats || (e.mode == EPI_ROWS_F32 && e.stat_rows > 0 && batch == 1),
+              "gemm: row-group statistics need a single fp32 row-mode output");
   if (!g_opt_simt && K > 0 && batch <= 65535) {
     int bn = pick_bn(M, N, batch);
     // at most 128 columns: the accumulator is then double-buffered in TMEM, so a tile's
@@ -2186,10 +2258,12 @@ void gemm_rows_launch(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t
                     ? 1
                     : 0;
       dispatch_umma<false>(bn, ta, tb, s, g, ev, batch);
+      if (e.row_stats && !ev.cvec) rows_group_sums(e, M, N);
       return;
     }
   }
   launch_simt<false>(a, b, s, g, e, N, batch);
+  if (e.row_stats) rows_group_sums(e, M, N);
 }
 
 // fp32 activation view (W, H, C, N2, N1) as a 5-D tensor map with bw x 1 x 64 x 1 x 1

@@ -32,6 +32,8 @@ enum EpiMode : int {
   EPI_HEADS = 5,     // fp16 head-split sections [B][H][T][hd] / [B][H][hd][Tp]
 };
 
+constexpr int kStatSlots = 16;
+
 struct Epi {
   int mode = EPI_GEMM;
   int vec = 0;  // 16-column vector stores allowed (set by the launcher after checks)
@@ -71,7 +73,12 @@ struct Epi {
   // EPI_CONV with Ho = 1 (images are rows): per image, the sum and the sum of squares of the
   // output values, added in fp64 to row_stats[2 n], [2 n + 1] (the GroupNorm(1)
   // statistics of a DConv hidden row, formed while the conv writes it)
+  // EPI_ROWS_F32: the same sums per group of stat_rows consecutive output rows (group
+  // m / stat_rows; the GroupNorm(1) statistics of a transformer branch's [T, D] output),
+  // spread over kStatSlots slots per group (row_stats[(g * kStatSlots + slot) * 2 + 0/1],
+  // slot = CTA index % kStatSlots) so the atomics of many CTAs do not meet on one address
   double *row_stats = nullptr;
+  int64_t stat_rows = 0;
   // EPI_CONVTR along W over a view with the frequency axis as W (the last frequency
   // decoder): instead of y, the de-normalised complex spectrum frame-major,
   // spec_z[(n * spec_rows + o / 2) * spec_frames + h][w] = (v(o) sd + mean, v(o + 1) sd +

@@ -422,17 +422,29 @@ __global__ void __launch_bounds__(kDgThreads)
   const float *__restrict__ xr = v.x + off;
   float *__restrict__ yr = hg + off;
   // eight elements per thread at a time: their loads are all in flight before the first
-  // result is stored (the input and the output are distinct buffers)
+  // result is stored (the input and the output are distinct buffers).  Element i of the
+  // chunk is (channel i / len, position i % len); a thread steps i by kDgThreads, so its
+  // (channel, position) pair advances by subtraction (no division in the loop)
   const int nel = hid * len;
+  int cn = 0, tn = (int)threadIdx.x;
+  while (tn >= len) {
+    tn -= len;
+    cn++;
+  }
   for (int i0 = 0; i0 < nel; i0 += 8 * kDgThreads) {
     float xv[8];
     int cc[8], tt[8];
 #pragma unroll
     for (int k = 0; k < 8; k++) {
       const int i = i0 + k * kDgThreads + (int)threadIdx.x;
-      cc[k] = i / len;
-      tt[k] = i - cc[k] * len;
-      xv[k] = i < nel ? xr[(int64_t)cc[k] * v.sC + tt[k]] : 0.f;
+      cc[k] = cn;
+      tt[k] = tn;
+      xv[k] = i < nel ? xr[(int64_t)cn * v.sC + tn] : 0.f;
+      tn += kDgThreads;
+      while (tn >= len) {
+        tn -= len;
+        cn++;
+      }
     }
 #pragma unroll
     for (int k = 0; k < 8; k++) {
@@ -495,11 +507,14 @@ __global__ void __launch_bounds__(kDgThreads)
     }
     atomicAdd(ar + p, a);
   }
-  // the row's last block: every block's atomics are visible once its count is
-  __threadfence();
+  // the row's last block: every block's atomics are visible once its count is (the CTA
+  // barrier orders this block's atomics before thread 0's fence, which is cumulative, and
+  // the fence before the count)
   __syncthreads();
-  if (threadIdx.x == 0)
+  if (threadIdx.x == 0) {
+    __threadfence();
     s_last = atomicAdd(cnt + row, 1u) == gridDim.x * gridDim.z - 1 ? 1u : 0u;
+  }
   __syncthreads();
   if (s_last) {
     __threadfence();

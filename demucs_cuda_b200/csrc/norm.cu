@@ -317,12 +317,37 @@ __global__ void __launch_bounds__(256)
 // k_norm_last for rows of L = n * C floats with C % 4 == 0 (16-byte aligned): grid (blocks,
 // rows), float4 per thread step, the channel index advanced incrementally (no divisions in
 // the loop)
+// (sums: the row's statistics as fp64 sum and sum of squares of its L values, in place of
+// mean / var, split over kSumSlots slots [row][slot][2])
+constexpr int kSumSlots = 16;
+static __device__ __forceinline__ void stats_from_sums(const double *sums, int64_t r,
+                                                       double inv_n, float &m, float &v) {
+  double s = 0.0, q = 0.0;
+  const double *p = sums + 2 * kSumSlots * r;
+#pragma unroll
+  for (int i = 0; i < kSumSlots; i++) {
+    s += p[2 * i];
+    q += p[2 * i + 1];
+  }
+  const double md = s * inv_n;
+  const double vd = q * inv_n - md * md;
+  m = (float)md;
+  v = vd > 0.0 ? (float)vd : 0.f;
+}
+
 __global__ void k_norm_last4(const float4 *__restrict__ x, float4 *__restrict__ y,
                              const float *__restrict__ mean, const float *__restrict__ var,
                              const float *__restrict__ w, const float *__restrict__ b, int L4,
-                             int C4, float eps) {
+                             int C4, float eps, const double *__restrict__ sums, double inv_n) {
   const int r = blockIdx.y;
-  const float m = mean[r], rs = 1.0f / sqrtf(var[r] + eps);
+  float m, vr;
+  if (sums) {
+    stats_from_sums(sums, r, inv_n, m, vr);
+  } else {
+    m = mean[r];
+    vr = var[r];
+  }
+  const float rs = 1.0f / sqrtf(vr + eps);
   const float4 *xr = x + (int64_t)r * L4;
   float4 *yr = y + (int64_t)r * L4;
   const float4 *w4 = (const float4 *)w, *b4 = (const float4 *)b;
@@ -603,13 +628,45 @@ void dk_norm_apply_last(const float *x, float *y, const float *mean, const float
     const int L4 = (int)(L / 4), C4 = (int)(C / 4);
     const unsigned bx = grid_for(L4, 256, (148 * 8 + rows - 1) / rows);
     k_norm_last4<<<dim3(bx, (unsigned)rows), 256, 0, stream()>>>(
-        (const float4 *)x, (float4 *)y, mean, var, w, b, L4, C4, eps);
+        (const float4 *)x, (float4 *)y, mean, var, w, b, L4, C4, eps, nullptr, 0.0);
   } else {
     const int64_t nseg = (L + kSegFloats - 1) / kSegFloats;
     k_norm_last<<<seg_grid(rows * nseg), 256, 0, stream()>>>(x, y, mean, var, w, b, rows, L, C,
                                                              eps, nseg);
   }
   DCB_LAUNCHED();
+}
+
+__global__ void k_sums_to_stats(const double *__restrict__ sums, int64_t rows, double inv_n,
+                                float *__restrict__ mean, float *__restrict__ var) {
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < rows) stats_from_sums(sums, r, inv_n, mean[r], var[r]);
+}
+
+// dk_norm_apply_last with each row's statistics given as fp64 sums [rows][kSumSlots][2]
+// (partial sums and sums of squares of its L values, added over the slots), e.g. formed by
+// the producing GEMM's epilogue
+void norm_apply_last_sums(const float *x, float *y, const double *sums, const float *w,
+                          const float *b, int64_t rows, int64_t L, int64_t C, float eps) {
+  if (rows <= 0 || L <= 0) return;
+  DCB_REQUIRE(C > 0, "norm_apply_last: C %lld", (long long)C);
+  const double inv_n = 1.0 / (double)L;
+  const bool al = ((uintptr_t)x | (uintptr_t)y | (uintptr_t)w | (uintptr_t)b) % 16 == 0;
+  if (al && C % 4 == 0 && L % C == 0 && L / 4 < (1ll << 31) && rows <= 65535) {
+    const int L4 = (int)(L / 4), C4 = (int)(C / 4);
+    const unsigned bx = grid_for(L4, 256, (148 * 8 + rows - 1) / rows);
+    k_norm_last4<<<dim3(bx, (unsigned)rows), 256, 0, stream()>>>(
+        (const float4 *)x, (float4 *)y, nullptr, nullptr, w, b, L4, C4, eps, sums, inv_n);
+    DCB_LAUNCHED();
+    return;
+  }
+  float *st = nullptr;
+  DCB_CUDA(cudaMallocAsync(&st, (size_t)rows * 2 * sizeof(float), stream()));
+  k_sums_to_stats<<<grid_for(rows, 128, 1 << 30), 128, 0, stream()>>>(sums, rows, inv_n, st,
+                                                                      st + rows);
+  DCB_LAUNCHED();
+  dk_norm_apply_last(x, y, st, st + rows, w, b, rows, L, C, eps);
+  DCB_CUDA(cudaFreeAsync(st, stream()));
 }
 
 void dk_affine_rows(const float *x, float *y, const float *mean, const float *var,
