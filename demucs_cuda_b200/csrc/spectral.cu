@@ -459,13 +459,13 @@ __global__ void k_ola_frames4096(const float *__restrict__ fw, float *__restrict
 }
 
 // Fused inverse STFT + overlap-add for n = 4096, hop 1024 (the reference's istft with its
-// window-sum division): one CTA per (row, run of kStreamHops consecutive output hops).  The
+// window-sum division): one CTA per (row, run of `hops` consecutive output hops).  The
 // CTA inverts the frames covering its hops in ascending order, two real frames per complex
 // FFT (as k_ifft_frames4096), adds each windowed frame into a ring of four hop
 // accumulators in shared memory, and writes hop g as soon as frame g (its last
 // contributor) is in; the three frames before the run are recomputed by the CTA (3 of
-// kStreamHops + 3 frames), so no frame buffer goes through HBM.
-constexpr int kStreamHops = 32;
+// hops + 3 frames), so no frame buffer goes through HBM.  The run length is chosen per
+// call (stream_hops) so the CTAs fill whole waves of the GPU.
 
 // The output stage (htdemucs.c:262-279) fused into the streamed inverse STFT: with y set,
 // sample t of row r goes to y[r][t - off] (t - off in [0, keep)) as the time branch's
@@ -484,7 +484,7 @@ __global__ void __launch_bounds__(kFftThreads, 4)
     k_istft_stream4096(const float2 *__restrict__ z, float *__restrict__ out, int N, int F,
                        int NF, const float *__restrict__ window,
                        const float2 *__restrict__ tw, int64_t start, int64_t length,
-                       int g_first, const StreamCombine cb) {
+                       int g_first, int hops, const StreamCombine cb) {
   // [kFftPadded] FFT buffer, then the ring [4][1024], then 1 / (sum of the squared window
   // over the four frames covering a sample) for the hops whose four frames all exist
   extern __shared__ float2 sbuf[];
@@ -493,8 +493,8 @@ __global__ void __launch_bounds__(kFftThreads, 4)
   float *sinv = ring + 4 * 1024;
   constexpr int n = kFftN, hop = 1024;
   const int64_t r = blockIdx.y;
-  const int k0 = g_first + blockIdx.x * kStreamHops;  // first output hop of this CTA
-  const int k1 = min(k0 + kStreamHops, NF + 3);       // hops past NF + 2 hold no samples
+  const int k0 = g_first + blockIdx.x * hops;  // first output hop of this CTA
+  const int k1 = min(k0 + hops, NF + 3);       // hops past NF + 2 hold no samples
   const float inv_n = 1.0f / (float)n;
   for (int i = threadIdx.x; i < 4 * hop; i += kFftThreads) ring[i] = 0.f;
   for (int w = threadIdx.x; w < hop; w += kFftThreads) {
@@ -625,19 +625,40 @@ void ispec_frames(const float2 *z, float *out, int64_t R, int F, int N, const fl
   const int NF = N + 4;
   const int g_first = (int)(start / hop);
   const int g_last = (int)((start + length - 1) / hop);
-  const int runs = (g_last - g_first + kStreamHops) / kStreamHops;
   const size_t sm = (size_t)kFftPadded * sizeof(float2) + 5 * 1024 * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
+  static int slots = 0;  // resident CTAs of the whole GPU
+  if (!slots) {
     DCB_CUDA(cudaFuncSetAttribute(k_istft_stream4096,
                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    attr = true;
+    int per_sm = 0;
+    DCB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_istft_stream4096,
+                                                           kFftThreads, sm));
+    int dev = 0, nsm = 0;
+    DCB_CUDA(cudaGetDevice(&dev));
+    DCB_CUDA(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev));
+    slots = (per_sm > 0 ? per_sm : 1) * (nsm > 0 ? nsm : 1);
   }
+  // run length: the least waves x (hops + 3 frames) over the possible run counts (a CTA's
+  // time is about its frame count; every CTA of a wave runs at once)
+  const int total = g_last - g_first + 1;
+  int hops = total;
+  int64_t best = -1;
+  for (int runs = 1; runs <= total; runs++) {
+    const int hr = (total + runs - 1) / runs;
+    if ((total + hr - 1) / hr != runs) continue;  // same hop count as a smaller run count
+    const int64_t waves = ((int64_t)runs * R + slots - 1) / slots;
+    const int64_t cost = waves * (hr + 3);
+    if (best < 0 || cost < best) {
+      best = cost;
+      hops = hr;
+    }
+  }
+  const int runs = (total + hops - 1) / hops;
   TraceScope ts(TR_SPECTRAL, 0.0,
                 (double)R * N * F * 8.0 + (cb.y ? (double)R * cb.keep * 8.0 : (double)R * length * 4.0),
                 R, F, length);
   k_istft_stream4096<<<dim3((unsigned)runs, (unsigned)R), kFftThreads, sm, stream()>>>(
-      z, out, N, F, NF, window, twiddles4096(), start, length, g_first, cb);
+      z, out, N, F, NF, window, twiddles4096(), start, length, g_first, hops, cb);
   DCB_LAUNCHED();
 }
 
