@@ -954,14 +954,28 @@ static void crosstransformer(DcbModel *m, float *x, float *xt, int B, int Fr, in
   const int D = m->D, H = m->cfg.t_heads, hd = D / H;
   const int N1 = Fr * T1, N2 = T2;
   float *tx = dalloc((size_t)B * N1 * D), *tt = dalloc((size_t)B * N2 * D);
+  // token layout kernels: CTA = kTokT positions of one (b, f), a [D][kTokT + 1] fp32 tile
+  DCB_REQUIRE(D <= 1024 && B <= 65535 && Fr <= 65535, "transformer: D %d, B %d, Fr %d", D, B,
+              Fr);
+  const size_t tok_sm = (size_t)D * (kTokT + 1) * sizeof(float);
   {
-    const int64_t warps = (int64_t)B * N1;
-    k_tokens_ln_pos<<<(unsigned)((warps + 3) / 4), 128, 0, stream()>>>(
-        x, tx, m->norm_in.w, m->norm_in.b, pos_2d(m, D, Fr, T1), B, D, Fr, T1, 1e-5f);
+    static size_t attr = 0;
+    if (tok_sm > 48 * 1024 && tok_sm > attr) {
+      DCB_CUDA(cudaFuncSetAttribute(k_tokens_ln_pos,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tok_sm));
+      DCB_CUDA(cudaFuncSetAttribute(k_tokens_to_chw,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tok_sm));
+      attr = tok_sm;
+    }
+  }
+  {
+    k_tokens_ln_pos<<<dim3((unsigned)((T1 + kTokT - 1) / kTokT), (unsigned)Fr, (unsigned)B), 256,
+                      tok_sm, stream()>>>(x, tx, m->norm_in.w, m->norm_in.b,
+                                          pos_2d(m, D, Fr, T1), B, D, Fr, T1, 1e-5f);
     DCB_LAUNCHED();
-    const int64_t warps2 = (int64_t)B * N2;
-    k_tokens_ln_pos<<<(unsigned)((warps2 + 3) / 4), 128, 0, stream()>>>(
-        xt, tt, m->norm_in_t.w, m->norm_in_t.b, pos_1d(m, D, T2), B, D, 1, T2, 1e-5f);
+    k_tokens_ln_pos<<<dim3((unsigned)((T2 + kTokT - 1) / kTokT), 1u, (unsigned)B), 256, tok_sm,
+                      stream()>>>(xt, tt, m->norm_in_t.w, m->norm_in_t.b, pos_1d(m, D, T2), B, D,
+                                  1, T2, 1e-5f);
     DCB_LAUNCHED();
   }
   const int ldl = (D + 7) / 8 * 8;
@@ -1008,10 +1022,11 @@ static void crosstransformer(DcbModel *m, float *x, float *xt, int B, int Fr, in
     if (aux) stream_wait(s_main, aux);
   }
   {
-    const int64_t n1 = (int64_t)B * D * N1, n2 = (int64_t)B * D * N2;
-    k_tokens_to_chw<<<grid_for(n1, 256), 256, 0, stream()>>>(tx, x, B, D, Fr, T1);
+    k_tokens_to_chw<<<dim3((unsigned)((T1 + kTokT - 1) / kTokT), (unsigned)Fr, (unsigned)B), 256,
+                      tok_sm, stream()>>>(tx, x, B, D, Fr, T1);
     DCB_LAUNCHED();
-    k_tokens_to_chw<<<grid_for(n2, 256), 256, 0, stream()>>>(tt, xt, B, D, 1, T2);
+    k_tokens_to_chw<<<dim3((unsigned)((T2 + kTokT - 1) / kTokT), 1u, (unsigned)B), 256, tok_sm,
+                      stream()>>>(tt, xt, B, D, 1, T2);
     DCB_LAUNCHED();
   }
   for (TBuf *b : {&bx, &bt}) {

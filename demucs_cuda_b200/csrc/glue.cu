@@ -947,51 +947,75 @@ __global__ void k_add_freq_emb(float *x, const float *__restrict__ emb, float al
 }
 
 // tokens: x [B, C, Fr, T1] -> tok[b][t*Fr + f][c] = LN(x[b, :, f, t]) + pos[t*Fr + f][c]
-// (transformer.c:164-185); one warp per token, C <= 1024.  Fr = 1 gives the time branch
-// ([B, C, T2] -> [B, T2, C]).
-__global__ void k_tokens_ln_pos(const float *__restrict__ x, float *__restrict__ tok,
-                                const float *__restrict__ w, const float *__restrict__ bb,
-                                const float *__restrict__ pos, int B, int C, int Fr, int T1,
-                                float eps) {
-  const int64_t ntok = (int64_t)Fr * T1;
-  const int64_t gt = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (gt >= (int64_t)B * ntok) return;
-  const int64_t b = gt / ntok, tk = gt - b * ntok;
-  const int64_t t = tk / Fr, f = tk - t * Fr;
-  const float *xb = x + b * (int64_t)C * Fr * T1 + f * T1 + t;
+// (transformer.c:164-185), C <= 1024.  Fr = 1 gives the time branch ([B, C, T2] ->
+// [B, T2, C]).  CTA = kTokT consecutive t of one (b, f): its warps read the tile channel
+// by channel (128-byte rows along t) into shared memory [C][kTokT + 1] (odd pitch: both
+// the row writes and the per-token column reads are free of bank conflicts), then one warp
+// per token normalises it (lane sums over channels c = 32 i + lane, then a shuffle tree)
+// and writes the token's row contiguously.
+constexpr int kTokT = 32;
+__global__ void __launch_bounds__(256)
+    k_tokens_ln_pos(const float *__restrict__ x, float *__restrict__ tok,
+                    const float *__restrict__ w, const float *__restrict__ bb,
+                    const float *__restrict__ pos, int B, int C, int Fr, int T1, float eps) {
+  extern __shared__ float tile[];  // [C][kTokT + 1]
+  constexpr int P = kTokT + 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int t0 = blockIdx.x * kTokT, f = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int nt = T1 - t0 < kTokT ? T1 - t0 : kTokT;
   const int64_t sc = (int64_t)Fr * T1;
-  float v[32];
-  float s = 0.f;
+  const float *xb = x + b * (int64_t)C * sc + (int64_t)f * T1 + t0;
+  // eight channel rows per warp in flight before the first is stored
+  for (int c0 = warp; c0 < C; c0 += 8 * nw) {
+    float r[8];
 #pragma unroll
-  for (int i = 0; i < 32; i++) {
-    const int c = i * 32 + lane;
-    v[i] = c < C ? xb[c * sc] : 0.f;
-    s += v[i];
-  }
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  const double md = (double)s / (double)C;
-  const float m = (float)md;
-  float q = 0.f;
+    for (int k = 0; k < 8; k++) {
+      const int c = c0 + k * nw;
+      r[k] = c < C && lane < nt ? xb[c * sc + lane] : 0.f;
+    }
 #pragma unroll
-  for (int i = 0; i < 32; i++) {
-    const int c = i * 32 + lane;
-    if (c < C) {
-      const float d = v[i] - m;
-      q += d * d;
+    for (int k = 0; k < 8; k++) {
+      const int c = c0 + k * nw;
+      if (c < C) tile[c * P + lane] = r[k];
     }
   }
-  for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-  const double dm = md - (double)m;
-  double m2 = (double)q - (double)C * dm * dm;
-  const float var = (float)((m2 > 0 ? m2 : 0.0) / (double)C);
-  const float rs = 1.0f / sqrtf(var + eps);
-  float *o = tok + gt * C;
-  const float *pp = pos + tk * C;
+  __syncthreads();
+  const int64_t ntok = (int64_t)Fr * T1;
+  for (int j = warp; j < nt; j += nw) {
+    const int64_t tk = (int64_t)(t0 + j) * Fr + f;
+    float v[32];
+    float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; i++) {
-    const int c = i * 32 + lane;
-    if (c < C) o[c] = ((v[i] - m) * rs * w[c] + bb[c]) + pp[c];
+    for (int i = 0; i < 32; i++) {
+      const int c = i * 32 + lane;
+      v[i] = c < C ? tile[c * P + j] : 0.f;
+      s += v[i];
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const double md = (double)s / (double)C;
+    const float m = (float)md;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      const int c = i * 32 + lane;
+      if (c < C) {
+        const float d = v[i] - m;
+        q += d * d;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const double dm = md - (double)m;
+    double m2 = (double)q - (double)C * dm * dm;
+    const float var = (float)((m2 > 0 ? m2 : 0.0) / (double)C);
+    const float rs = 1.0f / sqrtf(var + eps);
+    float *o = tok + (b * ntok + tk) * C;
+    const float *pp = pos + tk * C;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+      const int c = i * 32 + lane;
+      if (c < C) o[c] = ((v[i] - m) * rs * w[c] + bb[c]) + pp[c];
+    }
   }
 }
 
@@ -1053,14 +1077,41 @@ __global__ void k_im2col8_half(const float *__restrict__ x, uint16_t *__restrict
   }
 }
 
-// tok [B, Fr*T1, C] (token t*Fr + f) -> x [B, C, Fr, T1]
-__global__ void k_tokens_to_chw(const float *__restrict__ tok, float *__restrict__ x, int B,
-                                int C, int Fr, int T1) {
-  const int64_t total = (int64_t)B * C * Fr * T1;
-  DCB_GRID_STRIDE(i, total) {
-    const int64_t t = i % T1, r = i / T1, f = r % Fr, r2 = r / Fr, c = r2 % C, b = r2 / C;
-    x[i] = tok[(b * (int64_t)Fr * T1 + t * Fr + f) * C + c];
+// tok [B, Fr*T1, C] (token t*Fr + f) -> x [B, C, Fr, T1]: CTA = kTokT consecutive t of one
+// (b, f); warps read token rows (contiguous channels) into shared memory [C][kTokT + 1],
+// then write channel rows (contiguous t)
+__global__ void __launch_bounds__(256)
+    k_tokens_to_chw(const float *__restrict__ tok, float *__restrict__ x, int B, int C, int Fr,
+                    int T1) {
+  extern __shared__ float tile[];  // [C][kTokT + 1]
+  constexpr int P = kTokT + 1;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int t0 = blockIdx.x * kTokT, f = blockIdx.y;
+  const int64_t b = blockIdx.z;
+  const int nt = T1 - t0 < kTokT ? T1 - t0 : kTokT;
+  const int64_t ntok = (int64_t)Fr * T1;
+  // eight loads per lane in flight before the first is stored
+  for (int j = warp; j < nt; j += nw) {
+    const float *row = tok + (b * ntok + (int64_t)(t0 + j) * Fr + f) * C;
+    for (int c0 = lane; c0 < C; c0 += 8 * 32) {
+      float r[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int c = c0 + 32 * k;
+        r[k] = c < C ? row[c] : 0.f;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const int c = c0 + 32 * k;
+        if (c < C) tile[c * P + j] = r[k];
+      }
+    }
   }
+  __syncthreads();
+  const int64_t sc = (int64_t)Fr * T1;
+  float *xb = x + b * (int64_t)C * sc + (int64_t)f * T1 + t0;
+  for (int c = warp; c < C; c += nw)
+    if (lane < nt) xb[c * sc + lane] = tile[c * P + lane];
 }
 
 // y[b][s][c][t] = xt_denorm + center_trim(xi) with denorm x * (sqrt(var) + eps) + mean per
