@@ -1007,12 +1007,20 @@ static void crosstransformer(DcbModel *m, float *x, float *xt, int B, int Fr, in
         tlayer_branch(m, lt, tt, B, N2, N2, bt);
       }
     } else {
-      // both branches read the previous layer's tokens: take every LN first
+      // both branches read the previous layer's tokens: every LN runs before either branch
+      // updates its tokens (two on each stream, then each stream waits for the other's)
+      if (aux) stream_wait(aux, s_main);
       layernorm(tx, bx.ln, lx.norm1.w, lx.norm1.b, R1, D, 1e-5f, true, ldl);
       layernorm(tt, bx.lnk, lx.norm2.w, lx.norm2.b, R2, D, 1e-5f, true, ldl);
-      layernorm(tt, bt.ln, lt.norm1.w, lt.norm1.b, R2, D, 1e-5f, true, ldl);
-      layernorm(tx, bt.lnk, lt.norm2.w, lt.norm2.b, R1, D, 1e-5f, true, ldl);
-      if (aux) stream_wait(aux, s_main);
+      {
+        OnStream os(aux, aux != nullptr);
+        layernorm(tt, bt.ln, lt.norm1.w, lt.norm1.b, R2, D, 1e-5f, true, ldl);
+        layernorm(tx, bt.lnk, lt.norm2.w, lt.norm2.b, R1, D, 1e-5f, true, ldl);
+      }
+      if (aux) {
+        stream_wait(s_main, aux);
+        stream_wait(aux, s_main);
+      }
       tlayer_branch(m, lx, tx, B, N1, N2, bx);
       {
         OnStream os(aux, aux != nullptr);
