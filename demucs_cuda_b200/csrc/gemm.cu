@@ -2238,12 +2238,11 @@ void gemm_rows_launch(int64_t M, int64_t N, int64_t K, RowsA a, RowsA b, int64_t
   if (!g_opt_simt && K > 0 && batch <= 65535) {
     int bn = pick_bn(M, N, batch);
     // at most 128 columns: the accumulator is then double-buffered in TMEM, so a tile's
-    // epilogue overlaps the next tile's MMAs
+    // epilogue overlaps the next tile's MMAs.  (Halving the tile for short GEMMs until every
+    // persistent CTA had two tiles made the transformer's linears no faster alone and the
+    // two-stream forward 0.9 % slower: the narrower tiles re-read A once per extra column
+    // tile while the other branch's kernels share the SMs.)
     if (bn > 128) bn = 128;
-    // short GEMMs (the transformer's): narrower N tiles until the persistent CTAs get two
-    // tiles each, so loads and epilogues of consecutive tiles overlap
-    const int64_t mt = (M + kBM - 1) / kBM;
-    while (bn > 64 && mt * ((N + bn - 1) / bn) * batch < 4ll * sm_count()) bn /= 2;
     CUtensorMap ta, tb;
     const bool ok =
         encode_map(&ta, a.p, (uint64_t)K, (uint64_t)M, s.a_shared ? 1 : (uint64_t)batch,
