@@ -953,6 +953,13 @@ static void crosstransformer(DcbModel *m, float *x, float *xt, int B, int Fr, in
                              cudaStream_t aux) {
   const int D = m->D, H = m->cfg.t_heads, hd = D / H;
   const int N1 = Fr * T1, N2 = T2;
+  // with the branches on two streams, each branch's linears take one persistent CTA per SM
+  // (the other branch's kernels run beside them); restored on return
+  struct UmmaCtas {
+    int prev;
+    explicit UmmaCtas(int n) : prev(g_umma_ctas_per_sm) { g_umma_ctas_per_sm = n; }
+    ~UmmaCtas() { g_umma_ctas_per_sm = prev; }
+  } umma_ctas(aux ? 1 : 2);
   float *tx = dalloc((size_t)B * N1 * D), *tt = dalloc((size_t)B * N2 * D);
   // token layout kernels: CTA = kTokT positions of one (b, f), a [D][kTokT + 1] fp32 tile
   DCB_REQUIRE(D <= 1024 && B <= 65535 && Fr <= 65535, "transformer: D %d, B %d, Fr %d", D, B,

@@ -2084,6 +2084,11 @@ int gather_bn(int64_t M, int64_t N, bool glu) {
   return bn;
 }
 
+// persistent CTAs of k_umma per SM: 2 (two fit), 1 while another stream's kernels share the
+// SMs (the cross transformer's two branches), where leaving room for them measured faster
+// than filling every SM with GEMM tiles
+int g_umma_ctas_per_sm = 2;
+
 static int sm_count() {
   static int n[64] = {0};
   int dev = 0;
@@ -2126,7 +2131,7 @@ static void launch_umma(const CUtensorMap &ta, const CUtensorMap &tb, Shape s, c
   s.ntiles = ntiles;
   s.batch = (int)batch;
   const int64_t tiles = mtiles * ntiles * batch;
-  const int64_t slots = 2ll * sm_count();
+  const int64_t slots = (int64_t)g_umma_ctas_per_sm * sm_count();
   const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
   k_umma<BN, GATHER, EK><<<grid, kThreads, smem, stream()>>>(ta, tb, s, g, e);
   DCB_LAUNCHED();
